@@ -1,0 +1,173 @@
+// matrix.cu — resident weight matrices and the q-row GEMM entry point (clm_b200_matmul_rows).
+#include <algorithm>
+#include <string>
+
+#include "codec.cuh"
+#include "gemv.cuh"
+#include "matrix.cuh"
+
+namespace clm {
+
+// f32 rows: one warp per output row, lanes stride the columns, positions in registers (q <= 16).
+__global__ void __launch_bounds__(256) gemv_f32_kernel(const float* __restrict__ w, uint32_t rows, uint32_t cols,
+                                                       const float* __restrict__ x, int q, float* __restrict__ y) {
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= rows) return;
+  const float* wr = w + (size_t)warp * cols;
+  float acc[16];
+#pragma unroll
+  for (int p = 0; p < 16; ++p) acc[p] = 0.0f;
+  for (uint32_t k = lane; k < cols; k += 32) {
+    const float wv = wr[k];
+#pragma unroll
+    for (int p = 0; p < 16; ++p)
+      if (p < q) acc[p] = fmaf(wv, x[(size_t)p * cols + k], acc[p]);
+  }
+#pragma unroll
+  for (int p = 0; p < 16; ++p) {
+    if (p >= q) break;
+    float v = acc[p];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) y[(size_t)p * rows + warp] = v;
+  }
+}
+
+int launch_gemv_f32(const float* d_w, uint32_t rows, uint32_t cols, const float* d_x, int q, float* d_y,
+                    cudaStream_t st) {
+  const uint64_t threads = (uint64_t)rows * 32;
+  gemv_f32_kernel<<<(unsigned)ceil_div(threads, 256), 256, 0, st>>>(d_w, rows, cols, d_x, q, d_y);
+  CLM_LAUNCHED("gemv_f32_kernel");
+  return CLM_OK;
+}
+
+int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_src, uint64_t nbytes, uint32_t rows,
+                  uint32_t cols, clm_b200_matrix** out) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(out != nullptr, CLM_INVALID_ARGUMENT, "null output");
+  *out = nullptr;
+  CLM_CHECK(rows > 0 && cols > 0, CLM_INVALID_ARGUMENT, "empty matrix");
+  const uint64_t want = clm_b200_tensor_bytes(quant, (uint64_t)rows * cols);
+  CLM_CHECK(want != 0, CLM_INVALID_ARGUMENT, "unsupported representation or partial block");
+  CLM_CHECK(nbytes == want, CLM_DATA_LOSS, "matrix byte size does not match rows x cols in its representation");
+  CLM_CHECK(bytes != nullptr, CLM_INVALID_ARGUMENT, "null bytes");
+  const bool tiled = quant == CLM_QUANT_Q4_K || quant == CLM_QUANT_Q8_0;
+  if (tiled) {
+    CLM_CHECK(rows % 16 == 0, CLM_INVALID_ARGUMENT, "Q4_K/Q8_0 matrices need rows % 16 == 0");
+    CLM_CHECK(cols % 256 == 0, CLM_INVALID_ARGUMENT, "Q4_K/Q8_0 matrices need cols % 256 == 0");
+  }
+  cudaStream_t st = ctx->stream;
+  auto* m = new clm_b200_matrix();
+  m->ctx = ctx;
+  m->quant = quant;
+  m->rows = rows;
+  m->cols = cols;
+  void* staging = nullptr;
+  int status = CLM_OK;
+  do {
+    const void* src = bytes;
+    if (!device_src) {
+      cudaError_t e = cudaMalloc(&staging, nbytes);
+      if (e != cudaSuccess) {
+        status = cuda_fail(e, "cudaMalloc(matrix staging)");
+        break;
+      }
+      e = cudaMemcpyAsync(staging, bytes, nbytes, cudaMemcpyHostToDevice, st);
+      if (e != cudaSuccess) {
+        status = cuda_fail(e, "cudaMemcpyAsync(matrix upload)");
+        break;
+      }
+      src = staging;
+    }
+    if (tiled) {
+      m->shape = gemv_shape(quant, rows, cols);
+      m->bytes = m->shape.bytes();
+      cudaError_t e = cudaMalloc(&m->data, m->bytes);
+      if (e != cudaSuccess) {
+        status = cuda_fail(e, "cudaMalloc(matrix tiles)");
+        break;
+      }
+      status = launch_repack(m->shape, static_cast<const uint8_t*>(src), static_cast<uint8_t*>(m->data), st);
+    } else {
+      m->bytes = (uint64_t)rows * cols * 4;
+      cudaError_t e = cudaMalloc(&m->data, m->bytes);
+      if (e != cudaSuccess) {
+        status = cuda_fail(e, "cudaMalloc(matrix f32)");
+        break;
+      }
+      status = launch_decode(quant, src, static_cast<float*>(m->data), (uint64_t)rows * cols, st);
+    }
+    if (status != CLM_OK) break;
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) status = cuda_fail(e, "matrix upload");
+  } while (false);
+  if (staging) cudaFree(staging);
+  if (status != CLM_OK) {
+    if (m->data) cudaFree(m->data);
+    delete m;
+    return status;
+  }
+  *out = m;
+  return CLM_OK;
+}
+
+int matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, int q, float* d_y, cudaStream_t st) {
+  if (w->quant == CLM_QUANT_F32 || w->quant == CLM_QUANT_Q8_FIXTURE)
+    return launch_gemv_f32(static_cast<const float*>(w->data), w->rows, w->cols, d_x, q, d_y, st);
+  const GemvPlan p = gemv_plan(w->shape, q, ctx->sm_count);
+  const uint64_t part_bytes = p.ksplit > 1 ? (uint64_t)p.ksplit * q * w->rows * 4 : 0;
+  void* scratch = nullptr;
+  CLM_TRY(ctx_scratch(ctx, p.xfrag_bytes + p.xs_bytes + part_bytes + 256, &scratch));
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  void* xfrag = base;
+  void* xs = base + p.xfrag_bytes;
+  float* part = reinterpret_cast<float*>(base + p.xfrag_bytes + p.xs_bytes);
+  CLM_TRY(launch_prep_x(w->shape, p, d_x, q, xfrag, xs, st));
+  CLM_TRY(launch_gemv(w->shape, p, static_cast<const uint8_t*>(w->data), xfrag, xs, q, p.ksplit > 1 ? part : d_y, st));
+  if (p.ksplit > 1) CLM_TRY(launch_reduce_splits(part, p.ksplit, q, w->rows, d_y, st));
+  return CLM_OK;
+}
+
+}  // namespace clm
+
+using namespace clm;
+
+extern "C" {
+
+int clm_b200_matrix_upload(clm_b200_ctx* ctx, int quant, const void* h_bytes, uint64_t nbytes, uint32_t rows,
+                           uint32_t cols, clm_b200_matrix** out) {
+  return matrix_create(ctx, quant, h_bytes, false, nbytes, rows, cols, out);
+}
+
+int clm_b200_matrix_upload_device(clm_b200_ctx* ctx, int quant, const void* d_bytes, uint64_t nbytes, uint32_t rows,
+                                  uint32_t cols, clm_b200_matrix** out) {
+  return matrix_create(ctx, quant, d_bytes, true, nbytes, rows, cols, out);
+}
+
+int clm_b200_matrix_free(clm_b200_matrix* m) {
+  if (m == nullptr) return CLM_OK;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
+  if (m->data) cudaFree(m->data);
+  delete m;
+  return CLM_OK;
+}
+
+int clm_b200_matrix_info(const clm_b200_matrix* m, int* quant, uint32_t* rows, uint32_t* cols, uint64_t* bytes) {
+  CLM_CHECK(m != nullptr, CLM_INVALID_ARGUMENT, "null matrix");
+  if (quant) *quant = m->quant;
+  if (rows) *rows = m->rows;
+  if (cols) *cols = m->cols;
+  if (bytes) *bytes = m->bytes;
+  return CLM_OK;
+}
+
+int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, uint32_t positions, float* d_y,
+                         void* stream) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(w != nullptr && d_x != nullptr && d_y != nullptr, CLM_INVALID_ARGUMENT, "null argument");
+  CLM_CHECK(w->ctx == ctx, CLM_INVALID_ARGUMENT, "matrix belongs to another context");
+  CLM_CHECK(positions >= 1 && positions <= 16, CLM_OUT_OF_RANGE, "positions must be in [1, 16]");
+  return matmul_rows(ctx, w, d_x, (int)positions, d_y, pick_stream(ctx, stream));
+}
+
+}  // extern "C"

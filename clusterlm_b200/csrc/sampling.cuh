@@ -1,0 +1,15 @@
+// sampling.cuh — internal launchers of sampling.cu shared with the engines.
+#pragma once
+#include "common.cuh"
+
+namespace clm {
+int launch_argmax(const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out, cudaStream_t st);
+// mx[r] = max of row r; kept[r] = sum exp(double(l - mx) / T)
+int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t vocab, float T, float* d_mx, double* d_kept,
+                     cudaStream_t st);
+// Stats layout: target row j of sequence b at b*(k+1)+j; draft row j at batch*(k+1) + b*k + j.
+int launch_accept_logits(const float* d_tl, const float* d_dl, const int32_t* d_drafts, uint32_t batch, uint32_t k,
+                         uint32_t vocab, float T, const float* d_mx, const double* d_kept, const double* d_uniforms,
+                         uint64_t seed, uint64_t counter_base, uint32_t* d_accepted, int32_t* d_next,
+                         cudaStream_t st);
+}  // namespace clm

@@ -1,0 +1,145 @@
+/*
+ * clm_b200.h — C ABI of the B200-native ClusterLM speculative-window backend (libclm_b200.so).
+ *
+ * Plain pointers and sizes only.  Every call returns an int status whose values equal
+ * clusterlm::ErrorCode (runtime/common/include/clusterlm/common/status.hpp:15-36); the message of the
+ * last failure on the calling thread is clm_b200_last_error().  No exception crosses this boundary.
+ *
+ * Pointer conventions: `d_` = device memory on the context's GPU, `h_` = host memory (pageable or pinned).
+ * `stream` is a cudaStream_t (NULL = the context's own stream).  Calls that take device pointers are
+ * asynchronous on that stream; calls that take host pointers synchronise before returning.
+ *
+ * Threading: a context, its matrices and engines are driven by one caller at a time
+ * (runtime/domain/include/clusterlm/domain/reference_domain.hpp:4 "Not thread-safe").
+ */
+#ifndef CLM_B200_H
+#define CLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLM_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define CLM_API __attribute__((visibility("default")))
+#else
+#define CLM_API
+#endif
+
+/* Status codes: the numeric values of clusterlm::ErrorCode (status.hpp:15-36). */
+enum {
+  CLM_OK = 0,
+  CLM_INVALID_ARGUMENT = 1,
+  CLM_OUT_OF_RANGE = 2,
+  CLM_NOT_FOUND = 3,
+  CLM_ALREADY_EXISTS = 4,
+  CLM_FAILED_PRECONDITION = 5,
+  CLM_RESOURCE_EXHAUSTED = 6,
+  CLM_DATA_LOSS = 7,
+  CLM_STALE_EPOCH = 10,
+  CLM_ABORTED = 11,
+  CLM_DEADLINE_EXCEEDED = 13,
+  CLM_VERSION_MISMATCH = 15,
+  CLM_INTERNAL = 17,
+  CLM_UNIMPLEMENTED = 18,
+  CLM_HARDWARE_UNAVAILABLE = 19
+};
+
+/* Tensor representations (runtime/objects/include/clusterlm/objects/tensor_codec.hpp:23-28 for the
+ * first three; Q4_K is the ggml 256-element / 144-byte superblock, ggml_types.cpp:26). */
+enum { CLM_QUANT_F32 = 0, CLM_QUANT_Q8_FIXTURE = 1, CLM_QUANT_Q8_0 = 2, CLM_QUANT_Q4_K = 3 };
+
+/* ---- library / context ------------------------------------------------------------------------ */
+CLM_API int clm_b200_abi_version(void);
+CLM_API const char* clm_b200_last_error(void);
+/* Number of visible CUDA devices (0 without a GPU: the backend's BackendInfo::hardware_available). */
+CLM_API int clm_b200_device_count(int* n);
+
+typedef struct clm_b200_ctx clm_b200_ctx;
+/* One context per (domain, GPU): owns a stream and every device allocation made through it
+ * (runtime/domain/include/clusterlm/domain/execution_domain.hpp:4-7: a domain never shares pointers,
+ * streams or allocators).  CLM_HARDWARE_UNAVAILABLE when the device is absent or not sm_100. */
+CLM_API int clm_b200_ctx_create(int device, clm_b200_ctx** out);
+CLM_API int clm_b200_ctx_destroy(clm_b200_ctx* ctx);
+CLM_API int clm_b200_ctx_stream(clm_b200_ctx* ctx, void** stream);
+CLM_API int clm_b200_ctx_synchronize(clm_b200_ctx* ctx);
+
+/* ---- codecs (replaces objects::tensor_bytes / decode_tensor, tensor_codec.cpp:9-99) ------------ */
+CLM_API uint64_t clm_b200_tensor_bytes(int quant, uint64_t n_elems);
+/* Exact dequantisation on the device: f32 copy, q8_0-fixture f32(scale)*q, q8_0 f32(half scale)*q, and
+ * Q4_K (d*sc)*q - (dmin*m) with each product and the difference rounded once in f32 (bit-identical to
+ * the reference decoder for the first three and to gguf-py for Q4_K).  CLM_DATA_LOSS on a byte-count
+ * mismatch, CLM_INVALID_ARGUMENT on an unknown type or a count that is not whole blocks. */
+CLM_API int clm_b200_decode_tensor(clm_b200_ctx* ctx, int quant, const void* d_bytes, uint64_t nbytes, float* d_out,
+                           uint64_t n_elems, void* stream);
+/* Deterministic Q4_K / Q8_0 encoders on the device (Q8_0 follows tensor_codec.cpp:127-141; Q4_K is this
+ * project's min/max quantiser).  n_elems must be whole blocks. */
+CLM_API int clm_b200_encode(clm_b200_ctx* ctx, int quant, const float* d_in, uint64_t n_elems, void* d_out, void* stream);
+/* Counter-based synthetic weights: out[i] = stddev * sqrt(3) * IH4(seed, tensor_id, first+i) / 2^22 where
+ * IH4 is the centred sum of four 22-bit Philox4x32-10 outputs (no reference counterpart). */
+CLM_API int clm_b200_generate_weights(clm_b200_ctx* ctx, uint64_t seed, uint32_t tensor_id, uint64_t first, uint64_t n,
+                              float stddev, float* d_out, void* stream);
+
+/* ---- resident q-row GEMM (replaces reference_matmul_rows, runtime/domain/src/reference_kernels.cpp:24-30) */
+typedef struct clm_b200_matrix clm_b200_matrix;
+/* Upload a rows x cols row-major tensor in its stored representation and repack it for the tiled
+ * kernels (lossless byte permutation for Q4_K / Q8_0; f32 / q8_0-fixture are decoded exactly to f32, as
+ * the reference does at prepare, reference_domain.cpp:222-231).  Q4_K and Q8_0 need rows % 16 == 0 and
+ * cols % 256 == 0.  `h_bytes` is host memory; `d_bytes` (the _device variant) is device memory. */
+CLM_API int clm_b200_matrix_upload(clm_b200_ctx* ctx, int quant, const void* h_bytes, uint64_t nbytes, uint32_t rows,
+                           uint32_t cols, clm_b200_matrix** out);
+CLM_API int clm_b200_matrix_upload_device(clm_b200_ctx* ctx, int quant, const void* d_bytes, uint64_t nbytes, uint32_t rows,
+                                  uint32_t cols, clm_b200_matrix** out);
+CLM_API int clm_b200_matrix_free(clm_b200_matrix* m);
+CLM_API int clm_b200_matrix_info(const clm_b200_matrix* m, int* quant, uint32_t* rows, uint32_t* cols, uint64_t* device_bytes);
+/* y[p][i] = W[i] . x[p] for p < positions (output position-major, as reference_matmul_rows).
+ * 1 <= positions <= 16.  fp16 tensor-core products with f32 accumulation for Q4_K / Q8_0; f32 for f32. */
+CLM_API int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, uint32_t positions,
+                         float* d_y, void* stream);
+
+/* ---- sampling and speculative acceptance (runtime/domain/src/sampling.cpp:44-131) --------------- */
+/* argmax per row, ties to the lowest index (sampling.cpp:44-49). */
+CLM_API int clm_b200_argmax_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out,
+                         void* stream);
+/* distribution() per row (sampling.cpp:51-86): temperature <= 0 gives one-hot argmax; otherwise
+ * exp(double(l - max)/T) normalised in double and rounded to f32.  top_k / top_p truncation is
+ * applied on the probability order (ties by lower index, as the stable sort). */
+CLM_API int clm_b200_distribution_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab,
+                               float temperature, uint32_t top_k, float top_p, float* d_probs, void* stream);
+/* sample_from() per row with one caller-supplied uniform per row (sampling.cpp:88-101).  The result is
+ * bit-identical to the serial double-precision reference: exact prefix sums locate the index and an
+ * error bound proves the serial rounding cannot change it; otherwise the row is re-walked serially. */
+CLM_API int clm_b200_sample_rows(clm_b200_ctx* ctx, const float* d_probs, uint32_t rows, uint32_t vocab,
+                         const double* d_uniforms, int32_t* d_out, void* stream);
+/* verify_speculative() for `batch` sequences (sampling.cpp:103-131).
+ *   d_target      [batch][k+1][vocab] target probabilities
+ *   d_drafts      [batch][k] drafted tokens
+ *   d_draft_probs [batch][k][vocab] drafter probabilities, or NULL for a deterministic (one-hot) drafter
+ *   d_uniforms    [batch][k+1] uniforms consumed in the reference's order (one per test with q > 0, then
+ *                 one for the final sample), or NULL to draw them from Philox4x32-10 keyed by `seed` with
+ *                 counter (draw, sequence, counter_base lo, counter_base hi)
+ * Outputs d_accepted[batch] (0..k) and d_next[batch] (resampled or bonus token). */
+CLM_API int clm_b200_verify_speculative(clm_b200_ctx* ctx, const float* d_target, const int32_t* d_drafts,
+                                const float* d_draft_probs, uint32_t batch, uint32_t k, uint32_t vocab,
+                                const double* d_uniforms, uint64_t seed, uint64_t counter_base, uint32_t* d_accepted,
+                                int32_t* d_next, void* stream);
+/* Fused acceptance straight from logits (no probability arrays written): P = distribution(target/T),
+ * Q = distribution(draft/T) computed on the fly, then verify_speculative as above.
+ *   d_target_logits [batch][k+1][vocab], d_draft_logits [batch][k][vocab] (NULL = one-hot drafter).
+ * temperature > 0, no top-k / top-p. */
+CLM_API int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_target_logits, const float* d_draft_logits,
+                           const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t vocab, float temperature,
+                           const double* d_uniforms, uint64_t seed, uint64_t counter_base, uint32_t* d_accepted,
+                           int32_t* d_next, void* stream);
+/* Philox4x32-10 uniforms: out[i] = top 53 bits of (o0:o1) * 2^-53 for counter (first+i lo, hi, c2, c3). */
+CLM_API int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,
+                             double* d_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
