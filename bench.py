@@ -1,0 +1,380 @@
+"""Benchmark: accepted tok/s of 8B-shape Q4_K speculative decoding (q = 4) on B200, plus verify-window HBM GB/s.
+
+Workload (one "step" = one speculative round): Llama-3-8B-shaped decoder (32 layers, d_model 4096, 32/8 heads x
+128, FFN 14336 SwiGLU, vocab 128,256, RoPE theta 5e5) with random-init weights N(0, 0.02) (counter-based
+generator) quantised to GGUF Q4_K, a one-layer MTP draft head, context filled with 4096 seeded random tokens
+(prefill), q = 4 linear windows, batch 1, stochastic acceptance at temperature 1 (Philox draws).  A round is:
+MTP draft of 3 tokens -> 4-row verify window over all 32 layers + LM head -> rejection-sampling acceptance ->
+commit of accepted + 1 positions, all device-resident in one CUDA graph.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+value        emitted tokens / device time of the K timed rounds (inputs resident in HBM)
+e2e          the same through clm_b200_spec_round (host API: round parameters host->device, emitted tokens
+             device->host, synchronised every round)
+roofline     the verify window (32 layers + head, q = 4): algorithmic bytes / event-timed window duration
+cpu_baseline the oracle's refmath-order CPU restatement on this host's cores, a bounded sample (one decoder
+             layer at context 4096 + the LM head + one MTP step, q = 4) extrapolated to a round
+With N > 1 (torchrun) every rank runs an independent replica on its own GPU (weak scaling); value is the sum.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+Q = 4
+CONTEXT = 4096
+TEMPERATURE = 1.0
+SEED = 0
+METRIC = "accepted tok/s, 8B-shape Q4_K spec decode q=4"
+
+# algorithmic bytes of one q = 4 verify window (weights of 32 layers + LM head, KV of 4096 positions)
+def window_bytes(geo, context):
+    H, qd, kvd, F, V = geo.hidden, geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim, geo.ffn, geo.vocab
+    per_layer = (qd * H + 2 * kvd * H + H * qd + 3 * F * H) * 144 // 256
+    head = V * H * 144 // 256
+    kv = geo.n_layers * 2 * context * kvd * 2
+    return geo.n_layers * per_layer + head + kv, geo.n_layers * per_layer + head, kv
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, value, device):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(world, value, device):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- CPU side (oracle)
+
+class CpuBaseline:
+    """The oracle's refmath-order CPU restatement of the round on this host, a bounded sample: one decoder
+    layer (q = 4 at context 4096, KV filled with random values), the LM head (q = 4) and one MTP step are
+    timed; a round is extrapolated as 32 layers + head + 3 MTP steps.  Weight bytes are random valid Q4_K
+    blocks (timing does not depend on their values)."""
+
+    def __init__(self, threads: int):
+        import numpy as np
+
+        from clusterlm_b200.engine import LLAMA3_8B
+        from oracle.oracle_py import LlamaDims, Oracle
+
+        self.np = np
+        self.o = Oracle()
+        self.g = g = LLAMA3_8B
+        self.threads = threads
+        rng = np.random.default_rng(0)
+
+        def q4k(rows, cols):
+            b = rng.integers(0, 256, (rows * cols // 256, 144), dtype=np.uint8)
+            b[:, 0:4] = np.frombuffer(np.array([0x1400, 0x1400], np.uint16).tobytes(), np.uint8)  # d, dmin ~ 2^-10
+            return b.reshape(-1)
+
+        H, qd, kvd, F, V = g.hidden, g.n_heads * g.head_dim, g.n_kv_heads * g.head_dim, g.ffn, g.vocab
+        self.wqkv, self.wo, self.wgu, self.wd = q4k(qd + 2 * kvd, H), q4k(H, qd), q4k(2 * F, H), q4k(H, F)
+        self.head = q4k(V, H)
+        self.ones = np.ones(H, np.float32)
+        self.kc = rng.standard_normal((CONTEXT + Q, kvd)).astype(np.float32)
+        self.vc = rng.standard_normal((CONTEXT + Q, kvd)).astype(np.float32)
+        self.dims = LlamaDims(H, g.n_heads, g.n_kv_heads, g.head_dim, F, g.rope_theta, g.rms_eps)
+        self.parts = {}
+
+    def round_s(self) -> float:
+        np, o, g = self.np, self.o, self.g
+        h = np.random.default_rng(1).standard_normal((Q, g.hidden)).astype(np.float32)
+        t0 = time.perf_counter()
+        o.llama_layer(self.dims, "q4_k", self.wqkv, self.wo, self.wgu, self.wd, self.ones, self.ones, self.kc,
+                      self.vc, CONTEXT, h, None, self.threads)
+        layer = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        o.matmul_rows_quant("q4_k", self.head, g.vocab, g.hidden, h, self.threads)
+        head = time.perf_counter() - t0
+        t0 = time.perf_counter()  # one MTP step: SwiGLU block over one row + the head over one row
+        x = h[:1]
+        y = o.matmul_rows_quant("q4_k", self.wgu, 2 * g.ffn, g.hidden, x, self.threads)
+        with np.errstate(over="ignore"):
+            a = (y[:, :g.ffn] / (1.0 + np.exp(-y[:, :g.ffn])) * y[:, g.ffn:]).astype(np.float32)
+        o.matmul_rows_quant("q4_k", self.wd, g.hidden, g.ffn, a, self.threads)
+        o.matmul_rows_quant("q4_k", self.head, g.vocab, g.hidden, x, self.threads)
+        mtp = time.perf_counter() - t0
+        self.parts = {"layer_s": layer, "head_s": head, "mtp_s": mtp}
+        return g.n_layers * layer + head + (Q - 1) * mtp
+
+    def sample_text(self, emitted_per_round: float) -> str:
+        p = self.parts
+        return (f"oracle (refmath-order f32 dot products over Q4_K rows decoded one at a time), {self.threads} "
+                f"threads: 1 decoder layer at context {CONTEXT} ({p['layer_s']:.3f} s), LM head q={Q} "
+                f"({p['head_s']:.3f} s), 1 MTP step ({p['mtp_s']:.3f} s) timed; round = {self.g.n_layers} layers + "
+                f"head + {Q - 1} MTP steps (extrapolated); {emitted_per_round:.3f} emitted tokens per round")
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the reference has no Llama-family code (its llama path is un-vendored llama.cpp),
+    so this times the oracle port of its refmath-order CPU math on all host threads, one bounded sample
+    (one layer + head + one MTP step, extrapolated to a round) per step."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cpu = CpuBaseline(threads)
+    for _ in range(min(args.warmup, 1)):
+        cpu.round_s()
+    steps = max(1, min(args.steps, 5))
+    per_step = [cpu.round_s() for _ in range(steps)]
+    ms = statistics.median(per_step)
+    value = 1.0 / ms  # one emitted token per round (acceptance of the device run is not known to this arm)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": ms * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama3-8b-shape q4_k spec decode q=4 ctx=4096 batch=1", "q": Q, "context": CONTEXT},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": cpu.sample_text(1.0)},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU side
+
+def run_b200(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+    from clusterlm_b200.runtime import Context
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    geo = LLAMA3_8B
+    ctx = Context(local)
+    max_ctx = CONTEXT + (args.warmup + args.steps + 8) * (Q + 1) + 64
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, 16, 1)
+    eng.generate_weights(seed=SEED, stddev=0.02)
+    eng.prepare()
+    eng.open_session(1)
+    rng = np.random.default_rng(1234 + rank)
+    prompt = rng.integers(0, geo.vocab, CONTEXT).astype(np.int32)
+    t0 = time.perf_counter()
+    eng.spec_begin(1, prompt, Q, temperature=TEMPERATURE, seed=SEED)
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    counts = torch.zeros(args.warmup + args.steps, dtype=torch.int32, device=dev)
+    toks = torch.zeros((args.warmup + args.steps, Q + 1), dtype=torch.int32, device=dev)
+    for i in range(args.warmup):
+        eng.spec_round_device(1, Q, TEMPERATURE, SEED, toks[i], counts[i], stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    start.record(stream)
+    for i in range(args.warmup, args.warmup + args.steps):
+        eng.spec_round_device(1, Q, TEMPERATURE, SEED, toks[i], counts[i], stream.cuda_stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    launches = eng.last_launches()
+    elapsed = start.elapsed_time(end) / 1e3
+    emitted = int(counts[args.warmup:].sum().item())
+    elapsed_max = max_over_ranks(world, elapsed, dev)
+    emitted_all = sum_over_ranks(world, emitted, dev)
+    value = emitted_all / elapsed_max
+
+    # e2e: host API, parameters in / tokens out every round
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    e2e_n = max(4, args.steps // 2)
+    t0 = time.perf_counter()
+    e_emitted = 0
+    for _ in range(e2e_n):
+        e_emitted += eng.spec_round(1, Q, TEMPERATURE, SEED).size
+    e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(world, e2e_s, dev)
+    e2e_value = sum_over_ranks(world, e_emitted, dev) / e2e_s
+
+    # verify-window roofline: one q = 4 window through the public window call, event-timed
+    total_b, weight_b, kv_b = window_bytes(geo, CONTEXT)
+    pos = eng.position(1)
+    wt = []
+    wtoks = torch.from_numpy(rng.integers(0, geo.vocab, Q).astype(np.int32)).to(dev)
+    wlogits = torch.empty((Q, geo.vocab), dtype=torch.float32, device=dev)
+    for i in range(8):
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        eng.run_window_device(1, pos, wtoks, wlogits, stream.cuda_stream)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        eng.abort(1)
+        if i >= 3:
+            wt.append(s0.elapsed_time(s1) / 1e3)
+    window_s = statistics.median(wt)
+    peak, peak_kind = load_peaks()
+    achieved = total_b / window_s / 1e9
+    eng.close_session(1)
+    eng.close()
+    ctx.close()
+
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cb = CpuBaseline(os.cpu_count() or 1)
+        r = cb.round_s()
+        cpu = {"value": (emitted / args.steps) / r, "cores": cb.threads, "sample": cb.sample_text(emitted / args.steps)}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
+        "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
+        "config": {"workload": "llama3-8b-shape q4_k spec decode q=4 ctx=4096 batch=1 mtp=1-layer T=1",
+                   "q": Q, "context": CONTEXT, "temperature": TEMPERATURE,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (4.8 GB weights streamed per round)",
+                   "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted / args.steps},
+        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": (Q + 1) * 4 + 4},
+        "gpu_launches": launches * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_kind": peak_kind, "kernel": "verify window q=4 (32 layers + head)",
+                     "algorithmic_bytes": total_b, "weight_bytes": weight_b, "kv_bytes": kv_b,
+                     "window_ms": window_s * 1e3},
+        "clocks": clk,
+    }
+    if cpu:
+        line["cpu_baseline"] = {"value": cpu["value"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
+                                "sample": cpu["sample"]}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_b200(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -58,6 +58,23 @@ _SIGS = {
     "clm_b200_verify_speculative": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _u64, _u64, _vp, _vp, _vp]),
     "clm_b200_accept_logits": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _f, _vp, _u64, _u64, _vp, _vp, _vp]),
     "clm_b200_philox_uniforms": (_i, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _vp]),
+    "clm_b200_llama_create": (_i, [_vp, _vp, _vp, C.POINTER(_vp)]),
+    "clm_b200_engine_destroy": (_i, [_vp]),
+    "clm_b200_engine_generate_weights": (_i, [_vp, _u64, _f]),
+    "clm_b200_engine_prepare": (_i, [_vp]),
+    "clm_b200_engine_info": (_i, [_vp, C.POINTER(_u64), C.POINTER(_u64), C.POINTER(_u32)]),
+    "clm_b200_session_open": (_i, [_vp, _u64]),
+    "clm_b200_session_close": (_i, [_vp, _u64]),
+    "clm_b200_run_window": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp]),
+    "clm_b200_run_window_device": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
+    "clm_b200_commit": (_i, [_vp, _u64, _u32]),
+    "clm_b200_abort": (_i, [_vp, _u64]),
+    "clm_b200_session_position": (_i, [_vp, _u64, C.POINTER(_u64)]),
+    "clm_b200_engine_last_launches": (_i, [_vp, C.POINTER(_u64)]),
+    "clm_b200_mtp_draft": (_i, [_vp, C.c_int32, _u32, _f, _u64, _u64, _vp, _vp]),
+    "clm_b200_spec_begin": (_i, [_vp, _u64, _vp, _u32, _vp]),
+    "clm_b200_spec_round": (_i, [_vp, _u64, _vp, _vp, _vp]),
+    "clm_b200_spec_round_device": (_i, [_vp, _u64, _vp, _vp, _vp, _vp]),
 }
 
 

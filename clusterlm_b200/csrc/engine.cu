@@ -1,0 +1,908 @@
+// engine.cu — the Llama-family execution engine: one stage (layer range) of a model on one GPU, its sessions,
+// window execution (CUDA graphs of PDL-chained kernels), commit/abort, the MTP draft head and the
+// device-resident speculative round.
+//
+// Window semantics follow ReferenceDomainImpl::execute / commit_window / abort_window
+// (runtime/domain/src/reference_domain.cpp:297-445): a window writes KV rows at positions base..base+q-1
+// tentatively; commit(n) advances the committed position by n (rows past it are rewritten before any later
+// read, as in the reference); abort drops the window.
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "codec.cuh"
+#include "gemv.cuh"
+#include "llama.cuh"
+#include "matrix.cuh"
+#include "pdl.cuh"
+#include "sampling.cuh"
+
+namespace clm {
+
+struct SessionState {  // device-resident, one per session
+  long long pos;               // committed position
+  unsigned long long round;    // speculative rounds completed (Philox counter)
+  int next_token;              // token to feed at `pos`
+  unsigned accepted;           // drafts accepted in the last round
+  int count;                   // tokens emitted by the last round
+  int pad;
+};
+
+struct Gemv {
+  clm_b200_matrix* m = nullptr;
+  GemvPlan plan[2];  // nt = 1, 2
+  const GemvPlan& for_q(int q) const { return plan[q <= 8 ? 0 : 1]; }
+};
+
+struct Session {
+  uint64_t id = 0;
+  std::vector<int32_t> pages;
+  int32_t* d_pages = nullptr;
+  SessionState* d_state = nullptr;
+  long long pos = 0;          // committed position as known to the host
+  long long pos_bound = 0;    // upper bound while device-driven rounds are in flight
+  bool pos_stale = false;     // device rounds ran since the last read of d_state->pos
+  uint32_t outstanding = 0;  // q of the outstanding window, 0 = none
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;  // (kind, q, flag) -> executable graph
+  std::map<std::tuple<int, int, int>, int> seen;
+  std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
+};
+
+__global__ void fill_kernel(float* p, float v, uint64_t n) {
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+__global__ void round_head_kernel(const SessionState* __restrict__ st, int32_t* __restrict__ win) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) win[0] = st->next_token;
+}
+
+__global__ void greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
+                                     const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
+                                     int32_t* __restrict__ nxt);
+
+// Emits win[1..a] and the next token, advances the session (commit of a+1 positions).
+__global__ void round_commit_kernel(SessionState* __restrict__ st, const int32_t* __restrict__ win,
+                                    const uint32_t* __restrict__ acc, const int32_t* __restrict__ nxt,
+                                    int32_t* __restrict__ emitted, uint32_t* __restrict__ count) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x != 0) return;
+  const uint32_t a = *acc;
+  for (uint32_t i = 0; i < a; ++i) emitted[i] = win[1 + i];
+  emitted[a] = *nxt;
+  *count = a + 1;
+  st->pos += a + 1;
+  st->next_token = *nxt;
+  st->accepted = a;
+  st->count = (int)(a + 1);
+  st->round += 1;
+}
+
+__global__ void set_next_kernel(SessionState* __restrict__ st, const int32_t* __restrict__ tok) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) st->next_token = *tok;
+}
+
+__global__ void embed_guard_kernel(const int32_t* __restrict__ tokens, int q, int vocab, int32_t* __restrict__ out,
+                                   int* __restrict__ bad) {
+  griddep_wait();
+  griddep_launch();
+  const int p = threadIdx.x;
+  if (p < q) {
+    const int32_t t = tokens[p];
+    const bool ok = t >= 0 && t < vocab;
+    out[p] = ok ? t : 0;
+    if (!ok) atomicExch(bad, 1);
+  }
+}
+
+}  // namespace clm
+
+using namespace clm;
+
+struct clm_b200_engine {
+  clm_b200_ctx* ctx = nullptr;
+  LlamaDims d;
+  clm_b200_llama_geometry geo{};
+  clm_b200_stage_spec spec{};
+  bool has_embd = false, has_head = false, has_mtp = false, has_tokens = false;
+  bool prepared = false, weights_ready = false;
+  int max_pages = 0;  // pages per session
+  int pages_total = 0;
+  std::vector<int32_t> free_pages;
+  // weights
+  struct Layer {
+    Gemv qkv, o, gu, down;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+  };
+  std::vector<Layer> layers;
+  uint8_t* embd = nullptr;
+  uint64_t embd_bytes = 0;
+  Gemv head, mtp_gu, mtp_down;
+  float *out_norm = nullptr, *mtp_ffn_norm = nullptr, *mtp_out_norm = nullptr;
+  // KV pools per layer
+  std::vector<__half*> kpool, vpool;
+  // window buffers
+  float* h = nullptr;
+  float* part = nullptr;
+  uint8_t* xfrag = nullptr;
+  uint8_t* xs = nullptr;
+  __half* q16 = nullptr;
+  float* attn_part = nullptr;
+  float* logits = nullptr;
+  int32_t* tokens = nullptr;
+  float* bin = nullptr;
+  float* bout = nullptr;
+  float* h_mtp = nullptr;
+  float* draft_logits = nullptr;
+  int32_t* win = nullptr;
+  float* stats_mx = nullptr;
+  double* stats_kept = nullptr;
+  uint32_t* acc = nullptr;
+  int32_t* nxt = nullptr;
+  int32_t* emitted = nullptr;
+  uint32_t* count = nullptr;
+  int* bad = nullptr;
+  unsigned long long* zero_counter = nullptr;
+  RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
+  unsigned long long last_launches = 0;  // kernels in the last window / round
+  std::map<uint64_t, std::unique_ptr<Session>> sessions;
+  std::vector<void*> allocations;
+  uint64_t weight_bytes = 0;
+
+  int floats_per_position() const { return 2 * d.H + 1; }
+  float hi_scale() const { return d.quant == CLM_QUANT_Q4_K ? 0.0625f : 1.0f; }
+  int wmax() const { return (int)spec.max_window; }
+
+  int alloc(void** p, size_t bytes) {
+    CLM_CUDA(cudaMalloc(p, bytes));
+    allocations.push_back(*p);
+    return CLM_OK;
+  }
+  template <typename T>
+  int alloc_t(T** p, size_t count) {
+    void* v = nullptr;
+    CLM_TRY(alloc(&v, count * sizeof(T)));
+    *p = static_cast<T*>(v);
+    return CLM_OK;
+  }
+
+  int make_gemv(Gemv& g, const void* d_src, uint64_t nbytes, uint32_t rows, uint32_t cols) {
+    CLM_TRY(matrix_create(ctx, d.quant, d_src, true, nbytes, rows, cols, &g.m));
+    g.plan[0] = gemv_plan(g.m->shape, 8, ctx->sm_count);
+    g.plan[1] = gemv_plan(g.m->shape, 16, ctx->sm_count);
+    weight_bytes += g.m->bytes;
+    return CLM_OK;
+  }
+
+  int ones(float** p, size_t n) {
+    CLM_TRY(alloc_t(p, n));
+    fill_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, ctx->stream>>>(*p, 1.0f, n);
+    CLM_LAUNCHED("fill_kernel");
+    return CLM_OK;
+  }
+
+  // ---- GEMV in the chain: returns the number of partial splits written to `part` (0: wrote `direct`)
+  int gemv(const Gemv& g, int q, float* direct, int* nsplit, cudaStream_t st) {
+    const GemvPlan& p = g.for_q(q);
+    const bool to_direct = direct != nullptr && p.ksplit == 1;
+    CLM_TRY(launch_gemv(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), xfrag, xs, q,
+                        to_direct ? direct : part, st));
+    *nsplit = to_direct ? 0 : p.ksplit;
+    if (direct != nullptr && !to_direct) {
+      CLM_TRY(launch_reduce_splits(part, p.ksplit, q, g.m->rows, direct, st));
+      *nsplit = 0;
+    }
+    return CLM_OK;
+  }
+
+  // ---- the layer range over q rows; input already in h (nsplit_in = 0)
+  int enqueue_layers(Session& s, int q, int* nsplit_out, cudaStream_t st) {
+    const int nt = q <= 8 ? 1 : 2;
+    int ns = 0;
+    const long long* pos = &s.d_state->pos;
+    for (size_t li = 0; li < layers.size(); ++li) {
+      Layer& L = layers[li];
+      const int lg = (int)(spec.layer_begin + li);
+      (void)lg;
+      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, L.attn_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
+      CLM_TRY(gemv(L.qkv, q, nullptr, &ns, st));
+      CLM_TRY(launch_rope_kv(part, ns, q, d, pos, nullptr, s.d_pages, kpool[li], vpool[li], q16, st));
+      CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, nullptr, q, d, max_pages, attn_part, st));
+      CLM_TRY(launch_attn_combine(attn_part, pos, q, d, max_pages, nt, hi_scale(), xfrag, xs, st));
+      CLM_TRY(gemv(L.o, q, nullptr, &ns, st));
+      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, L.ffn_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
+      CLM_TRY(gemv(L.gu, q, nullptr, &ns, st));
+      CLM_TRY(launch_swiglu(part, ns, q, d.F, nt, hi_scale(), xfrag, xs, st));
+      CLM_TRY(gemv(L.down, q, nullptr, &ns, st));
+    }
+    *nsplit_out = ns;
+    return CLM_OK;
+  }
+
+  // ---- a full window: input (tokens or records) -> layers -> logits or records
+  int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st) {
+    if (has_tokens) {
+      CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(64), 0, st, d_tok, q, (int)d.V, tokens, bad));
+      CLM_TRY(launch_embed(embd, d.quant, tokens, q, d.H, h, st));
+    } else {
+      CLM_TRY(launch_unpack_boundary(bin, q, d.H, h, st));
+    }
+    int ns = 0;
+    CLM_TRY(enqueue_layers(s, q, &ns, st));
+    if (has_head) {
+      const int nt = q <= 8 ? 1 : 2;
+      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, out_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
+      int dummy = 0;
+      CLM_TRY(gemv(head, q, logits, &dummy, st));
+    } else {
+      CLM_TRY(launch_pack_boundary(h, part, ns, q, d.H, bout, st));
+    }
+    return CLM_OK;
+  }
+
+  // ---- one MTP step: prev token (device) -> draft logits row
+  int enqueue_mtp_step(const int32_t* d_prev, float* d_logits_row, cudaStream_t st) {
+    CLM_TRY(launch_embed(embd, d.quant, d_prev, 1, d.H, h_mtp, st));
+    CLM_TRY(launch_norm(part, 0, d.H, 1, d.H, mtp_ffn_norm, d.eps, h_mtp, 1, hi_scale(), xfrag, xs, st));
+    int ns = 0;
+    CLM_TRY(gemv(mtp_gu, 1, nullptr, &ns, st));
+    CLM_TRY(launch_swiglu(part, ns, 1, d.F, 1, hi_scale(), xfrag, xs, st));
+    CLM_TRY(gemv(mtp_down, 1, nullptr, &ns, st));
+    CLM_TRY(launch_norm(part, ns, d.H, 1, d.H, mtp_out_norm, d.eps, h_mtp, 1, hi_scale(), xfrag, xs, st));
+    int dummy = 0;
+    CLM_TRY(gemv(head, 1, d_logits_row, &dummy, st));
+    return CLM_OK;
+  }
+
+  // ---- one speculative round on a WHOLE engine
+  // Temperature and seed are read from `ctl` (device); `stochastic` selects the acceptance kernels.
+  int enqueue_round(Session& s, int q, bool stochastic, cudaStream_t st) {
+    const unsigned long long* ctr = &s.d_state->round;
+    CLM_TRY(launch_pdl(round_head_kernel, dim3(1), dim3(32), 0, st, (const SessionState*)s.d_state, win));
+    for (int j = 0; j + 1 < q; ++j) {
+      CLM_TRY(enqueue_mtp_step(win + j, draft_logits + (size_t)j * d.V, st));
+      CLM_TRY(launch_sample_logits(draft_logits + (size_t)j * d.V, d.V, 0.0f, 0, (uint32_t)j, 1u, ctr, win + j + 1, st,
+                                   ctl));
+    }
+    CLM_TRY(enqueue_window(s, q, win, st));
+    if (stochastic) {
+      CLM_TRY(launch_row_stats(logits, q, d.V, 1.0f, stats_mx, stats_kept, st, ctl));
+      if (q > 1) CLM_TRY(launch_row_stats(draft_logits, q - 1, d.V, 1.0f, stats_mx + q, stats_kept + q, st, ctl));
+      CLM_TRY(launch_accept_logits(logits, q > 1 ? draft_logits : nullptr, win + 1, 1, q - 1, d.V, 1.0f, stats_mx,
+                                   stats_kept, nullptr, 0, 0, ctr, acc, nxt, st, ctl));
+    } else {
+      CLM_TRY(launch_pdl(greedy_accept_kernel, dim3(1), dim3(1024), 0, st, (const float*)logits, (uint32_t)d.V, q,
+                         (const int32_t*)win, acc, nxt));
+    }
+    CLM_TRY(launch_pdl(round_commit_kernel, dim3(1), dim3(32), 0, st, s.d_state, (const int32_t*)win,
+                       (const uint32_t*)acc, (const int32_t*)nxt, emitted, count));
+    return CLM_OK;
+  }
+
+  // Runs `enq` for (kind, q, flag) as a CUDA graph: eager on first use, captured on the second, replayed after.
+  template <typename F>
+  int run_graph(Session& s, int kind, int q, int flag, cudaStream_t st, F&& enq) {
+    const auto key = std::make_tuple(kind, q, flag);
+    auto it = s.graphs.find(key);
+    if (it != s.graphs.end()) {
+      CLM_CUDA(cudaGraphLaunch(it->second, st));
+      last_launches = s.launches[key];
+      return CLM_OK;
+    }
+    const unsigned long long l0 = t_kernel_launches;
+    if (s.seen[key]++ == 0) {
+      const int rc0 = enq(st);
+      last_launches = t_kernel_launches - l0;
+      return rc0;
+    }
+    cudaGraph_t g = nullptr;
+    CLM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const int rc = enq(st);
+    s.launches[key] = t_kernel_launches - l0;
+    last_launches = s.launches[key];
+    cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc != CLM_OK) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+    s.graphs[key] = ex;
+    CLM_CUDA(cudaGraphLaunch(ex, st));
+    return CLM_OK;
+  }
+
+  int check_bad(cudaStream_t st) {
+    int b = 0;
+    CLM_CUDA(cudaMemcpyAsync(&b, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CLM_CUDA(cudaStreamSynchronize(st));
+    if (b) {
+      CLM_CUDA(cudaMemset(bad, 0, sizeof(int)));
+      return fail(CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+    }
+    return CLM_OK;
+  }
+
+  void release_session(Session& s) {
+    for (auto& kv : s.graphs) cudaGraphExecDestroy(kv.second);
+    s.graphs.clear();
+    if (s.d_pages) cudaFree(s.d_pages);
+    if (s.d_state) cudaFree(s.d_state);
+    for (int32_t p : s.pages) free_pages.push_back(p);
+    s.pages.clear();
+    s.d_pages = nullptr;
+    s.d_state = nullptr;
+  }
+
+  ~clm_b200_engine() {
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto& kv : sessions) release_session(*kv.second);
+    sessions.clear();
+    auto free_m = [](Gemv& g) {
+      if (g.m) clm_b200_matrix_free(g.m);
+      g.m = nullptr;
+    };
+    for (auto& L : layers) {
+      free_m(L.qkv);
+      free_m(L.o);
+      free_m(L.gu);
+      free_m(L.down);
+    }
+    free_m(head);
+    free_m(mtp_gu);
+    free_m(mtp_down);
+    for (void* p : allocations) cudaFree(p);
+  }
+};
+
+namespace clm {
+
+__global__ void greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
+                                     const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
+                                     int32_t* __restrict__ nxt);
+
+}  // namespace clm
+
+// greedy acceptance (coordinator.cpp:1295-1298): longest prefix with argmax(logits[i]) == window[i+1]
+__device__ int32_t engine_block_argmax(const float* __restrict__ l, uint32_t vocab) {
+  __shared__ float sv[32];
+  __shared__ int32_t si[32];
+  __shared__ int32_t s_res;
+  float best = -INFINITY;
+  int32_t bi = INT32_MAX;
+  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = l[i];
+    if (v > best || (v == best && (int32_t)i < bi)) {
+      best = v;
+      bi = (int32_t)i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
+    bi = lane < (int)(blockDim.x / 32) ? si[lane] : INT32_MAX;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) s_res = (isnan(l[0]) || bi == INT32_MAX) ? 0 : bi;
+  }
+  __syncthreads();
+  const int32_t r = s_res;
+  __syncthreads();
+  return r;
+}
+
+__global__ void clm::greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
+                                          const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
+                                          int32_t* __restrict__ nxt) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ int32_t am[64];
+  for (int i = 0; i < q; ++i) {
+    const int32_t a = engine_block_argmax(logits + (size_t)i * vocab, vocab);
+    if (threadIdx.x == 0) am[i] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t a = 0;
+    while ((int)a + 1 < q && am[a] == win[a + 1]) ++a;
+    *acc = a;
+    *nxt = am[a];
+  }
+}
+
+namespace {
+
+int engine_enter(clm_b200_engine* e) {
+  CLM_CHECK(e != nullptr, CLM_INVALID_ARGUMENT, "null engine");
+  return ctx_enter(e->ctx);
+}
+
+Session* find_session(clm_b200_engine* e, uint64_t id) {
+  auto it = e->sessions.find(id);
+  return it == e->sessions.end() ? nullptr : it->second.get();
+}
+
+}  // namespace
+
+extern "C" {
+
+int clm_b200_llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_b200_stage_spec* spec,
+                          clm_b200_engine** out) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(g && spec && out, CLM_INVALID_ARGUMENT, "null argument");
+  *out = nullptr;
+  CLM_CHECK(g->n_layers > 0 && g->hidden > 0 && g->n_heads > 0 && g->n_kv_heads > 0 && g->vocab > 0 && g->ffn > 0,
+            CLM_INVALID_ARGUMENT, "geometry has a zero dimension");
+  CLM_CHECK(g->n_heads % g->n_kv_heads == 0, CLM_INVALID_ARGUMENT, "n_heads must be a multiple of n_kv_heads");
+  CLM_CHECK(g->head_dim == 128, CLM_UNIMPLEMENTED, "head_dim must be 128");
+  CLM_CHECK(g->quant == CLM_QUANT_Q4_K || g->quant == CLM_QUANT_Q8_0, CLM_INVALID_ARGUMENT, "quant must be Q4_K or Q8_0");
+  CLM_CHECK(g->hidden % 256 == 0 && g->ffn % 256 == 0 && (g->n_heads * g->head_dim) % 256 == 0, CLM_INVALID_ARGUMENT,
+            "hidden, ffn and n_heads*head_dim must be multiples of 256");
+  CLM_CHECK(g->vocab % 16 == 0 && (g->n_kv_heads * g->head_dim) % 16 == 0, CLM_INVALID_ARGUMENT,
+            "vocab and kv width must be multiples of 16");
+  CLM_CHECK(spec->layer_end <= g->n_layers && spec->layer_begin <= spec->layer_end, CLM_INVALID_ARGUMENT,
+            "layer range outside the model");
+  CLM_CHECK(spec->role >= CLM_ROLE_PREFIX && spec->role <= CLM_ROLE_WHOLE, CLM_INVALID_ARGUMENT, "unknown role");
+  CLM_CHECK(spec->max_context > 0 && spec->max_window > 0 && spec->max_sessions > 0 &&
+                spec->max_window <= spec->max_context,
+            CLM_INVALID_ARGUMENT, "domain spec needs max_context >= max_window >= 1 and max_sessions >= 1");
+  CLM_CHECK(spec->max_window <= 16, CLM_OUT_OF_RANGE, "max_window must be <= 16");
+  if (spec->role == CLM_ROLE_PREFIX || spec->role == CLM_ROLE_WHOLE)
+    CLM_CHECK(spec->layer_begin == 0, CLM_INVALID_ARGUMENT, "prefix domain must start at layer 0");
+  if (spec->role == CLM_ROLE_TAIL || spec->role == CLM_ROLE_WHOLE)
+    CLM_CHECK(spec->layer_end == g->n_layers, CLM_INVALID_ARGUMENT, "tail domain must end at the last layer");
+  if (spec->role == CLM_ROLE_MIDDLE)
+    CLM_CHECK(spec->layer_end > spec->layer_begin, CLM_INVALID_ARGUMENT, "middle domain needs at least one layer");
+  auto* e = new clm_b200_engine();
+  e->ctx = ctx;
+  e->geo = *g;
+  e->spec = *spec;
+  e->d.H = (int)g->hidden;
+  e->d.nh = (int)g->n_heads;
+  e->d.nkv = (int)g->n_kv_heads;
+  e->d.hd = (int)g->head_dim;
+  e->d.F = (int)g->ffn;
+  e->d.V = (int)g->vocab;
+  e->d.theta = g->rope_theta;
+  e->d.eps = g->rms_eps;
+  e->d.quant = g->quant;
+  e->has_tokens = spec->role == CLM_ROLE_PREFIX || spec->role == CLM_ROLE_WHOLE;
+  e->has_head = spec->role == CLM_ROLE_TAIL || spec->role == CLM_ROLE_WHOLE;
+  e->has_mtp = e->has_head && g->mtp != 0;
+  e->has_embd = e->has_tokens || e->has_mtp;
+  e->max_pages = (int)ceil_div(spec->max_context, kPageTokens);
+  *out = e;
+  return CLM_OK;
+}
+
+int clm_b200_engine_destroy(clm_b200_engine* e) {
+  if (!e) return CLM_OK;
+  delete e;
+  return CLM_OK;
+}
+
+int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float stddev) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(!e->weights_ready, CLM_FAILED_PRECONDITION, "weights already bound");
+  const LlamaDims& d = e->d;
+  cudaStream_t st = e->ctx->stream;
+  auto tbytes = [&](uint64_t n) { return clm_b200_tensor_bytes(d.quant, n); };
+  uint64_t biggest = std::max<uint64_t>(tbytes((uint64_t)(d.qd() + 2 * d.kvd()) * d.H), tbytes((uint64_t)2 * d.F * d.H));
+  biggest = std::max<uint64_t>(biggest, tbytes((uint64_t)d.H * d.F));
+  if (e->has_head || e->has_embd) biggest = std::max<uint64_t>(biggest, tbytes((uint64_t)d.V * d.H));
+  uint8_t* tmp = nullptr;
+  CLM_CUDA(cudaMalloc(&tmp, biggest));
+  int rc = CLM_OK;
+  auto gen = [&](uint32_t id, uint64_t n, uint8_t* dst) { return launch_gen_encode(d.quant, seed, id, n, stddev, dst, st); };
+  do {
+    for (uint32_t L = e->spec.layer_begin; L < e->spec.layer_end && rc == CLM_OK; ++L) {
+      clm_b200_engine::Layer lay;
+      const uint64_t H = d.H, qd = d.qd(), kvd = d.kvd(), F = d.F;
+      const uint32_t id = 16 * L;
+      if ((rc = gen(id + 0, qd * H, tmp)) || (rc = gen(id + 1, kvd * H, tmp + tbytes(qd * H))) ||
+          (rc = gen(id + 2, kvd * H, tmp + tbytes((qd + kvd) * H))))
+        break;
+      if ((rc = e->make_gemv(lay.qkv, tmp, tbytes((qd + 2 * kvd) * H), (uint32_t)(qd + 2 * kvd), (uint32_t)H))) break;
+      if ((rc = gen(id + 3, H * qd, tmp)) || (rc = e->make_gemv(lay.o, tmp, tbytes(H * qd), (uint32_t)H, (uint32_t)qd)))
+        break;
+      if ((rc = gen(id + 4, F * H, tmp)) || (rc = gen(id + 5, F * H, tmp + tbytes(F * H))) ||
+          (rc = e->make_gemv(lay.gu, tmp, tbytes(2 * F * H), (uint32_t)(2 * F), (uint32_t)H)))
+        break;
+      if ((rc = gen(id + 6, H * F, tmp)) || (rc = e->make_gemv(lay.down, tmp, tbytes(H * F), (uint32_t)H, (uint32_t)F)))
+        break;
+      if ((rc = e->ones(&lay.attn_norm, H)) || (rc = e->ones(&lay.ffn_norm, H))) break;
+      e->layers.push_back(lay);
+    }
+    if (rc) break;
+    const uint64_t VH = (uint64_t)d.V * d.H;
+    if (e->has_embd) {
+      e->embd_bytes = tbytes(VH);
+      if ((rc = e->alloc((void**)&e->embd, e->embd_bytes)) || (rc = gen(1000, VH, e->embd))) break;
+      e->weight_bytes += e->embd_bytes;
+    }
+    if (e->has_head) {
+      if ((rc = gen(1001, VH, tmp)) || (rc = e->make_gemv(e->head, tmp, tbytes(VH), (uint32_t)d.V, (uint32_t)d.H))) break;
+      if ((rc = e->ones(&e->out_norm, d.H))) break;
+    }
+    if (e->has_mtp) {
+      const uint64_t FH = (uint64_t)d.F * d.H;
+      if ((rc = gen(1002, FH, tmp)) || (rc = gen(1003, FH, tmp + tbytes(FH))) ||
+          (rc = e->make_gemv(e->mtp_gu, tmp, tbytes(2 * FH), (uint32_t)(2 * d.F), (uint32_t)d.H)))
+        break;
+      if ((rc = gen(1004, FH, tmp)) || (rc = e->make_gemv(e->mtp_down, tmp, tbytes(FH), (uint32_t)d.H, (uint32_t)d.F)))
+        break;
+      if ((rc = e->ones(&e->mtp_ffn_norm, d.H)) || (rc = e->ones(&e->mtp_out_norm, d.H))) break;
+    }
+  } while (false);
+  cudaStreamSynchronize(st);
+  cudaFree(tmp);
+  if (rc == CLM_OK) e->weights_ready = true;
+  return rc;
+}
+
+int clm_b200_engine_prepare(clm_b200_engine* e) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->weights_ready, CLM_FAILED_PRECONDITION, "weights are not bound");
+  CLM_CHECK(!e->prepared, CLM_FAILED_PRECONDITION, "engine already prepared");
+  const LlamaDims& d = e->d;
+  const int W = e->wmax();
+  // largest partial / fragment buffers over every GEMV of this stage at nt = 1 and 2
+  uint64_t part_floats = (uint64_t)W * std::max(d.H, 2 * d.F), xfrag = 0, xs = 0;
+  auto account = [&](const Gemv& g) {
+    if (!g.m) return;
+    for (int i = 0; i < 2; ++i) {
+      const GemvPlan& p = g.plan[i];
+      part_floats = std::max<uint64_t>(part_floats, (uint64_t)p.ksplit * W * g.m->rows);
+      xfrag = std::max<uint64_t>(xfrag, p.xfrag_bytes);
+      xs = std::max<uint64_t>(xs, p.xs_bytes);
+    }
+  };
+  for (auto& L : e->layers) {
+    account(L.qkv);
+    account(L.o);
+    account(L.gu);
+    account(L.down);
+  }
+  account(e->head);
+  account(e->mtp_gu);
+  account(e->mtp_down);
+  part_floats = std::max<uint64_t>(part_floats, (uint64_t)W * (d.qd() + 2 * d.kvd()));
+  e->pages_total = (int)e->spec.max_sessions * e->max_pages;
+  const size_t page_bytes = (size_t)d.nkv * kPageTokens * d.hd * sizeof(__half);
+  const int mtiles = (W * (d.nh / d.nkv) + 15) / 16;
+  CLM_TRY(e->alloc_t(&e->h, (size_t)W * d.H));
+  CLM_TRY(e->alloc_t(&e->part, part_floats));
+  CLM_TRY(e->alloc_t(&e->xfrag, xfrag));
+  CLM_TRY(e->alloc_t(&e->xs, xs));
+  CLM_TRY(e->alloc_t(&e->q16, (size_t)W * d.qd()));
+  CLM_TRY(e->alloc_t(&e->attn_part, (size_t)mtiles * d.nkv * e->max_pages * attn_partial_floats(d.hd)));
+  CLM_TRY(e->alloc_t(&e->tokens, (size_t)W));
+  CLM_TRY(e->alloc_t(&e->bin, (size_t)W * e->floats_per_position()));
+  CLM_TRY(e->alloc_t(&e->bout, (size_t)W * e->floats_per_position()));
+  CLM_TRY(e->alloc_t(&e->bad, 1));
+  CLM_CUDA(cudaMemset(e->bad, 0, sizeof(int)));
+  if (e->has_head) CLM_TRY(e->alloc_t(&e->logits, (size_t)W * d.V));
+  if (e->has_mtp) {
+    CLM_TRY(e->alloc_t(&e->h_mtp, (size_t)d.H));
+    CLM_TRY(e->alloc_t(&e->draft_logits, (size_t)W * d.V));
+  }
+  CLM_TRY(e->alloc_t(&e->win, (size_t)W + 1));
+  CLM_TRY(e->alloc_t(&e->stats_mx, (size_t)2 * W));
+  CLM_TRY(e->alloc_t(&e->stats_kept, (size_t)2 * W));
+  CLM_TRY(e->alloc_t(&e->acc, 1));
+  CLM_TRY(e->alloc_t(&e->nxt, 1));
+  CLM_TRY(e->alloc_t(&e->emitted, (size_t)W + 1));
+  CLM_TRY(e->alloc_t(&e->count, 1));
+  CLM_TRY(e->alloc_t(&e->zero_counter, 1));
+  CLM_TRY(e->alloc_t(&e->ctl, 1));
+  CLM_CUDA(cudaMemset(e->ctl, 0, sizeof(RoundCtl)));
+  CLM_CUDA(cudaMemset(e->zero_counter, 0, sizeof(unsigned long long)));
+  for (size_t li = 0; li < e->layers.size(); ++li) {
+    __half *k = nullptr, *v = nullptr;
+    CLM_TRY(e->alloc_t(&k, page_bytes / sizeof(__half) * e->pages_total));
+    CLM_TRY(e->alloc_t(&v, page_bytes / sizeof(__half) * e->pages_total));
+    CLM_CUDA(cudaMemset(k, 0, page_bytes * e->pages_total));
+    CLM_CUDA(cudaMemset(v, 0, page_bytes * e->pages_total));
+    e->kpool.push_back(k);
+    e->vpool.push_back(v);
+  }
+  for (int p = e->pages_total - 1; p >= 0; --p) e->free_pages.push_back(p);
+  CLM_CUDA(cudaStreamSynchronize(e->ctx->stream));
+  e->prepared = true;
+  return CLM_OK;
+}
+
+int clm_b200_engine_info(const clm_b200_engine* e, uint64_t* weight_bytes, uint64_t* state_bytes, uint32_t* fpp) {
+  CLM_CHECK(e != nullptr, CLM_INVALID_ARGUMENT, "null engine");
+  if (weight_bytes) *weight_bytes = e->weight_bytes;
+  if (state_bytes)
+    *state_bytes = (uint64_t)e->layers.size() * 2 * e->max_pages * e->d.nkv * kPageTokens * e->d.hd * sizeof(__half);
+  if (fpp) *fpp = (uint32_t)e->floats_per_position();
+  return CLM_OK;
+}
+
+int clm_b200_session_open(clm_b200_engine* e, uint64_t id) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(find_session(e, id) == nullptr, CLM_ALREADY_EXISTS, "session already open");
+  CLM_CHECK((int)e->free_pages.size() >= e->max_pages, CLM_RESOURCE_EXHAUSTED, "max_sessions reached");
+  auto s = std::make_unique<Session>();
+  s->id = id;
+  for (int i = 0; i < e->max_pages; ++i) {
+    s->pages.push_back(e->free_pages.back());
+    e->free_pages.pop_back();
+  }
+  cudaError_t err = cudaMalloc(&s->d_pages, s->pages.size() * sizeof(int32_t));
+  if (err == cudaSuccess) err = cudaMalloc(&s->d_state, sizeof(SessionState));
+  if (err == cudaSuccess)
+    err = cudaMemcpy(s->d_pages, s->pages.data(), s->pages.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMemset(s->d_state, 0, sizeof(SessionState));
+  if (err != cudaSuccess) {
+    e->release_session(*s);
+    return cuda_fail(err, "session_open");
+  }
+  e->sessions[id] = std::move(s);
+  return CLM_OK;
+}
+
+int clm_b200_session_close(clm_b200_engine* e, uint64_t id) {
+  CLM_TRY(engine_enter(e));
+  Session* s = find_session(e, id);
+  if (!s) return CLM_OK;  // idempotent cleanup (WindowLedger::abort_session)
+  CLM_CUDA(cudaStreamSynchronize(e->ctx->stream));
+  e->release_session(*s);
+  e->sessions.erase(id);
+  return CLM_OK;
+}
+
+// Re-reads the committed position after device-driven rounds.
+static int sync_pos(clm_b200_engine* e, Session* s) {
+  if (!s->pos_stale) return CLM_OK;
+  long long p = 0;
+  CLM_CUDA(cudaMemcpyAsync(&p, &s->d_state->pos, sizeof(p), cudaMemcpyDeviceToHost, e->ctx->stream));
+  CLM_CUDA(cudaStreamSynchronize(e->ctx->stream));
+  s->pos = s->pos_bound = p;
+  s->pos_stale = false;
+  return CLM_OK;
+}
+
+static int run_window_common(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, cudaStream_t st,
+                             Session** out) {
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_TRY(sync_pos(e, s));
+  CLM_CHECK(s->outstanding == 0, CLM_FAILED_PRECONDITION, "a window is already outstanding for this session");
+  CLM_CHECK(q >= 1, CLM_INVALID_ARGUMENT, "window must have at least one position");
+  CLM_CHECK(q <= e->spec.max_window, CLM_RESOURCE_EXHAUSTED, "window exceeds max_window");
+  CLM_CHECK(base + q <= e->spec.max_context, CLM_RESOURCE_EXHAUSTED, "window exceeds max_context");
+  CLM_CHECK((long long)base == s->pos, CLM_FAILED_PRECONDITION, "window base position != committed position");
+  (void)st;
+  *out = s;
+  return CLM_OK;
+}
+
+int clm_b200_run_window_device(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* d_tokens,
+                               const float* d_in, float* d_out, float* d_logits, void* stream) {
+  CLM_TRY(engine_enter(e));
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  Session* s = nullptr;
+  CLM_TRY(run_window_common(e, id, base, q, st, &s));
+  const size_t rec = (size_t)q * e->floats_per_position() * sizeof(float);
+  if (e->has_tokens) {
+    CLM_CHECK(d_tokens != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes tokens");
+  } else {
+    CLM_CHECK(d_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
+    CLM_CUDA(cudaMemcpyAsync(e->bin, d_in, rec, cudaMemcpyDeviceToDevice, st));
+  }
+  if (e->has_tokens) CLM_CUDA(cudaMemcpyAsync(e->win, d_tokens, q * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  CLM_TRY(e->run_graph(*s, 0, (int)q, 0, st, [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs); }));
+  if (e->has_head) {
+    if (d_logits)
+      CLM_CUDA(cudaMemcpyAsync(d_logits, e->logits, (size_t)q * e->d.V * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  } else if (d_out) {
+    CLM_CUDA(cudaMemcpyAsync(d_out, e->bout, rec, cudaMemcpyDeviceToDevice, st));
+  }
+  s->outstanding = q;  // out-of-range device tokens embed as zeros and are reported by clm_b200_commit
+  return CLM_OK;
+}
+
+int clm_b200_run_window(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens,
+                        const float* h_in, float* h_out, float* h_logits) {
+  CLM_TRY(engine_enter(e));
+  cudaStream_t st = e->ctx->stream;
+  Session* s = nullptr;
+  CLM_TRY(run_window_common(e, id, base, q, st, &s));
+  const size_t rec = (size_t)q * e->floats_per_position() * sizeof(float);
+  if (e->has_tokens) {
+    CLM_CHECK(h_tokens != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes tokens");
+    for (uint32_t i = 0; i < q; ++i)
+      CLM_CHECK(h_tokens[i] >= 0 && h_tokens[i] < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+    CLM_CUDA(cudaMemcpyAsync(e->win, h_tokens, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  } else {
+    CLM_CHECK(h_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
+    CLM_CUDA(cudaMemcpyAsync(e->bin, h_in, rec, cudaMemcpyHostToDevice, st));
+  }
+  CLM_TRY(e->run_graph(*s, 0, (int)q, 0, st, [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs); }));
+  if (e->has_head) {
+    if (h_logits)
+      CLM_CUDA(cudaMemcpyAsync(h_logits, e->logits, (size_t)q * e->d.V * sizeof(float), cudaMemcpyDeviceToHost, st));
+  } else if (h_out) {
+    CLM_CUDA(cudaMemcpyAsync(h_out, e->bout, rec, cudaMemcpyDeviceToHost, st));
+  }
+  CLM_CUDA(cudaStreamSynchronize(st));
+  s->outstanding = q;
+  return CLM_OK;
+}
+
+int clm_b200_commit(clm_b200_engine* e, uint64_t id, uint32_t accepted) {
+  CLM_TRY(engine_enter(e));
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_CHECK(s->outstanding > 0, CLM_FAILED_PRECONDITION, "no outstanding window");
+  CLM_CHECK(accepted >= 1 && accepted <= s->outstanding, CLM_INVALID_ARGUMENT, "accepted must be in [1, q]");
+  if (e->has_tokens) {
+    const int rc = e->check_bad(e->ctx->stream);
+    if (rc != CLM_OK) {
+      s->outstanding = 0;  // the window is dropped, as the ledger's fail_window does
+      return rc;
+    }
+  }
+  s->pos += accepted;
+  s->pos_bound = s->pos;
+  s->outstanding = 0;
+  // the device copy of the committed position is read by the next window's kernels (stream-ordered)
+  CLM_CUDA(cudaMemcpyAsync(&s->d_state->pos, &s->pos, sizeof(long long), cudaMemcpyHostToDevice, e->ctx->stream));
+  CLM_CUDA(cudaStreamSynchronize(e->ctx->stream));
+  return CLM_OK;
+}
+
+int clm_b200_abort(clm_b200_engine* e, uint64_t id) {
+  CLM_TRY(engine_enter(e));
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  s->outstanding = 0;  // KV rows past the committed position are rewritten before any read
+  return CLM_OK;
+}
+
+int clm_b200_engine_last_launches(const clm_b200_engine* e, uint64_t* launches) {
+  CLM_CHECK(e != nullptr && launches != nullptr, CLM_INVALID_ARGUMENT, "null argument");
+  *launches = e->last_launches;
+  return CLM_OK;
+}
+
+int clm_b200_session_position(const clm_b200_engine* e, uint64_t id, uint64_t* committed) {
+  CLM_CHECK(e != nullptr && committed != nullptr, CLM_INVALID_ARGUMENT, "null argument");
+  auto it = e->sessions.find(id);
+  CLM_CHECK(it != e->sessions.end(), CLM_NOT_FOUND, "session not open");
+  *committed = (uint64_t)it->second->pos;
+  return CLM_OK;
+}
+
+int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,
+                       int32_t* h_tokens, float* h_logits) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared && e->has_mtp, CLM_FAILED_PRECONDITION, "engine has no MTP head");
+  CLM_CHECK(count >= 1 && count < e->spec.max_window, CLM_OUT_OF_RANGE, "count must be in [1, max_window)");
+  CLM_CHECK(prev >= 0 && prev < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+  CLM_CHECK(h_tokens != nullptr, CLM_INVALID_ARGUMENT, "null output");
+  cudaStream_t st = e->ctx->stream;
+  unsigned long long ctr = counter;
+  CLM_CUDA(cudaMemcpyAsync(e->zero_counter, &ctr, sizeof(ctr), cudaMemcpyHostToDevice, st));
+  CLM_CUDA(cudaMemcpyAsync(e->win, &prev, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  for (uint32_t j = 0; j < count; ++j) {
+    CLM_TRY(e->enqueue_mtp_step(e->win + j, e->draft_logits + (size_t)j * e->d.V, st));
+    CLM_TRY(launch_sample_logits(e->draft_logits + (size_t)j * e->d.V, e->d.V, T, seed, j, 1u, e->zero_counter,
+                                 e->win + j + 1, st, nullptr));
+  }
+  CLM_CUDA(cudaMemcpyAsync(h_tokens, e->win + 1, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  if (h_logits)
+    CLM_CUDA(cudaMemcpyAsync(h_logits, e->draft_logits, (size_t)count * e->d.V * sizeof(float), cudaMemcpyDeviceToHost,
+                             st));
+  ctr = 0;
+  CLM_CUDA(cudaMemcpyAsync(e->zero_counter, &ctr, sizeof(ctr), cudaMemcpyHostToDevice, st));
+  CLM_CUDA(cudaStreamSynchronize(st));
+  return CLM_OK;
+}
+
+int clm_b200_spec_begin(clm_b200_engine* e, uint64_t id, const int32_t* h_prompt, uint32_t n,
+                        const clm_b200_spec_params* p) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->spec.role == CLM_ROLE_WHOLE, CLM_FAILED_PRECONDITION, "speculative rounds need a whole-model engine");
+  CLM_CHECK(h_prompt != nullptr && n >= 1 && p != nullptr, CLM_INVALID_ARGUMENT, "empty prompt");
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_TRY(sync_pos(e, s));
+  uint32_t off = 0;
+  while (off < n) {
+    const uint32_t q = std::min<uint32_t>(e->spec.max_window, n - off);
+    CLM_TRY(clm_b200_run_window(e, id, (uint64_t)s->pos, q, h_prompt + off, nullptr, nullptr, nullptr));
+    CLM_TRY(clm_b200_commit(e, id, q));
+    off += q;
+  }
+  // first token from the last prompt position (argmax, or a sample with Philox draw (0, stream 2, 0))
+  cudaStream_t st = e->ctx->stream;
+  const uint32_t last = (n - 1) % e->spec.max_window;
+  CLM_TRY(launch_sample_logits(e->logits + (size_t)last * e->d.V, e->d.V, p->temperature, p->seed, 0u, 2u,
+                               e->zero_counter, e->nxt, st, nullptr));
+  CLM_TRY(launch_pdl(set_next_kernel, dim3(1), dim3(32), 0, st, s->d_state, (const int32_t*)e->nxt));
+  CLM_CUDA(cudaStreamSynchronize(st));
+  return CLM_OK;
+}
+
+int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
+                               uint32_t* d_count, void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(p != nullptr, CLM_INVALID_ARGUMENT, "null params");
+  CLM_CHECK(e->spec.role == CLM_ROLE_WHOLE && e->has_mtp, CLM_FAILED_PRECONDITION,
+            "speculative rounds need a whole-model engine with an MTP head");
+  CLM_CHECK(p->q >= 1 && p->q <= e->spec.max_window, CLM_OUT_OF_RANGE, "q must be in [1, max_window]");
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_CHECK(s->outstanding == 0, CLM_FAILED_PRECONDITION, "a window is outstanding");
+  if ((uint64_t)s->pos_bound + p->q > e->spec.max_context) CLM_TRY(sync_pos(e, s));
+  CLM_CHECK((uint64_t)s->pos_bound + p->q <= e->spec.max_context, CLM_RESOURCE_EXHAUSTED,
+            "speculative round would exceed max_context");
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  const bool stochastic = p->temperature > 0.0f;
+  // the round's inputs (temperature, seed) go host -> device each round; the graph reads them there
+  RoundCtl c{p->temperature, 0u, (unsigned long long)p->seed};
+  CLM_CUDA(cudaMemcpyAsync(e->ctl, &c, sizeof(c), cudaMemcpyHostToDevice, st));
+  CLM_TRY(e->run_graph(*s, 1, (int)p->q, stochastic ? 1 : 0, st,
+                       [&](cudaStream_t cs) { return e->enqueue_round(*s, (int)p->q, stochastic, cs); }));
+  if (d_tokens) CLM_CUDA(cudaMemcpyAsync(d_tokens, e->emitted, (p->q + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  if (d_count) CLM_CUDA(cudaMemcpyAsync(d_count, e->count, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+  s->pos_bound += p->q;
+  s->pos_stale = true;
+  return CLM_OK;
+}
+
+int clm_b200_spec_round(clm_b200_engine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,
+                        uint32_t* h_count) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(h_tokens != nullptr && h_count != nullptr, CLM_INVALID_ARGUMENT, "null output");
+  cudaStream_t st = e->ctx->stream;
+  CLM_TRY(clm_b200_spec_round_device(e, id, p, nullptr, nullptr, st));
+  CLM_CUDA(cudaMemcpyAsync(h_count, e->count, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  CLM_CUDA(cudaMemcpyAsync(h_tokens, e->emitted, (p->q + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  CLM_CUDA(cudaStreamSynchronize(st));
+  Session* s = find_session(e, id);
+  s->pos += *h_count;
+  s->pos_bound = s->pos;
+  s->pos_stale = false;
+  return CLM_OK;
+}
+
+}  // extern "C"

@@ -2,6 +2,7 @@
 #include <algorithm>
 
 #include "gemv.cuh"
+#include "pdl.cuh"
 
 namespace clm {
 
@@ -27,9 +28,6 @@ __device__ __forceinline__ void mma16816(float c[4], uint32_t a0, uint32_t a1, u
 }
 __device__ __forceinline__ uint32_t lo_bcast(uint32_t x) { return __byte_perm(x, x, 0x1010); }
 __device__ __forceinline__ uint32_t hi_bcast(uint32_t x) { return __byte_perm(x, x, 0x3232); }
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
-}
 
 constexpr uint32_t kHalfNeg1024x2 = 0xE400E400u;
 constexpr uint32_t kHalfNeg128x2 = 0xD800D800u;
@@ -147,6 +145,8 @@ __global__ void prep_x_kernel(const float* __restrict__ x, int q, uint32_t cols,
   const uint32_t pairs = (sb_per_row + 1) / 2;
   const uint32_t n_xs = (uint32_t)nt_count * pairs * 32;
   const uint32_t gid = blockIdx.x * blockDim.x + threadIdx.x;
+  griddep_wait();
+  griddep_launch();
   if (gid < n_frag) {
     const uint32_t lane = gid % 32, s = (gid / 32) % 16, nt = (gid / 512) % nt_count, sb = gid / (512 * nt_count);
     const int p = (int)nt * 8 + (int)(lane / 4);
@@ -341,9 +341,11 @@ __global__ void __launch_bounds__(256) gemv_tiled_kernel(const uint8_t* __restri
   const uint8_t* tile0 = tiles + ((size_t)(grp * sb_per_row + sb0) * kGemvWarps + warp) * tile_bytes;
   const size_t sb_stride = (size_t)kGemvWarps * tile_bytes;
 
-  // Issue the first weight loads before staging activations (they do not depend on them).
+  // Issue the first weight loads before waiting for the producer of the activations (weights are immutable).
   Raw cur, nxt;
   load_raw(cur, tile0, lane);
+  griddep_wait();
+  griddep_launch();
 
   // Stage this CTA's activation fragments (one contiguous span each; sb0 is even).
   {
@@ -390,6 +392,8 @@ __global__ void __launch_bounds__(256) gemv_tiled_kernel(const uint8_t* __restri
 }
 
 __global__ void reduce_splits_kernel(const float* __restrict__ part, int ksplit, uint64_t n, float* __restrict__ y) {
+  griddep_wait();
+  griddep_launch();
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
     float a = 0.0f;
     for (int k = 0; k < ksplit; ++k) a += part[(uint64_t)k * n + i];
@@ -454,22 +458,18 @@ int launch_prep_x(const GemvShape& s, const GemvPlan& p, const float* d_x, int q
                   cudaStream_t st) {
   const uint32_t n = (uint32_t)p.nt * s.sb * 512 + (uint32_t)p.nt * ((s.sb + 1) / 2) * 32;
   const float hi_scale = s.quant == CLM_QUANT_Q4_K ? 0.0625f : 1.0f;
-  prep_x_kernel<<<(n + 255) / 256, 256, 0, st>>>(d_x, q, s.cols, s.sb, p.nt, hi_scale, static_cast<uint2*>(d_xfrag),
-                                                 static_cast<uint4*>(d_xs));
-  CLM_LAUNCHED("prep_x_kernel");
-  return CLM_OK;
+  return launch_pdl(prep_x_kernel, dim3((n + 255) / 256), dim3(256), 0, st, d_x, q, s.cols, s.sb, p.nt, hi_scale,
+                    static_cast<uint2*>(d_xfrag), static_cast<uint4*>(d_xs));
 }
 
 template <typename Raw, int NT>
 static int launch_gemv_t(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const void* d_xfrag,
                          const void* d_xs, int q, float* d_out, cudaStream_t st) {
   auto kern = gemv_tiled_kernel<Raw, NT>;
-  CLM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+  CLM_TRY(ensure_smem(kern, p.smem));
   const unsigned blocks = s.ng * (unsigned)p.ksplit;
-  kern<<<blocks, 256, p.smem, st>>>(d_tiles, s.rows, s.sb, s.tile_bytes, p.ksplit, p.sbps,
-                                    static_cast<const uint2*>(d_xfrag), static_cast<const uint4*>(d_xs), q, d_out);
-  CLM_LAUNCHED("gemv_tiled_kernel");
-  return CLM_OK;
+  return launch_pdl(kern, dim3(blocks), dim3(256), p.smem, st, d_tiles, s.rows, s.sb, s.tile_bytes, p.ksplit, p.sbps,
+                    static_cast<const uint2*>(d_xfrag), static_cast<const uint4*>(d_xs), q, d_out);
 }
 
 int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const void* d_xfrag, const void* d_xs,
@@ -484,9 +484,7 @@ int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, c
 int launch_reduce_splits(const float* d_part, int ksplit, int q, uint32_t rows, float* d_y, cudaStream_t st) {
   const uint64_t n = (uint64_t)q * rows;
   const uint64_t blocks = std::min<uint64_t>(ceil_div(n, 256), 4096);
-  reduce_splits_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_part, ksplit, n, d_y);
-  CLM_LAUNCHED("reduce_splits_kernel");
-  return CLM_OK;
+  return launch_pdl(reduce_splits_kernel, dim3((unsigned)blocks), dim3(256), 0, st, d_part, ksplit, n, d_y);
 }
 
 }  // namespace clm

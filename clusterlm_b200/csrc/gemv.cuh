@@ -45,6 +45,55 @@ struct GemvPlan {
   uint64_t xfrag_bytes = 0, xs_bytes = 0;
 };
 
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+}
+
+// Writes activation row p (x[cols] in shared memory, fp32) in the GEMV's fragment order:
+//   xfrag[sb][nt][s][lane], lane = (p%8)*4 + t: {half2(x[k0], x[k0+1]), half2(x[k1], x[k1+1]) * hi_scale}
+//   xs[pair][nt][lane]: fp16 hi/lo split of the 32-element sub-block sums
+// hi_scale is 1/16 for Q4_K (high-nibble sub-blocks) and 1 for Q8_0.  `sums` is shared scratch of cols/32
+// floats.  x == nullptr writes zeros (rows beyond the window).  All threads of the block must call.
+__device__ inline void write_xfrag_row(const float* x, int p, uint32_t cols, int nt_count, float hi_scale,
+                                       uint2* __restrict__ xfrag, uint4* __restrict__ xs, float* sums) {
+  const uint32_t sb_count = cols / 256, nt = (uint32_t)p / 8, g = (uint32_t)p % 8;
+  for (uint32_t it = threadIdx.x; it < sb_count * 64; it += blockDim.x) {
+    const uint32_t sb = it / 64, s = (it / 4) % 16, t = it % 4;
+    uint2 v = make_uint2(0, 0);
+    if (x) {
+      const uint32_t k0 = sb * 256 + 64 * t + 2 * s, k1 = k0 + 32;
+      v.x = pack_half2(x[k0], x[k0 + 1]);
+      v.y = pack_half2(x[k1] * hi_scale, x[k1 + 1] * hi_scale);
+    }
+    xfrag[((size_t)sb * nt_count + nt) * 512 + s * 32 + g * 4 + t] = v;
+  }
+  for (uint32_t j = threadIdx.x; j < cols / 32; j += blockDim.x) {
+    float a = 0.0f;
+    if (x)
+      for (int l = 0; l < 32; ++l) a += x[32 * j + l];
+    sums[j] = a;
+  }
+  __syncthreads();
+  const uint32_t pairs = (sb_count + 1) / 2;
+  for (uint32_t it = threadIdx.x; it < pairs * 4; it += blockDim.x) {
+    const uint32_t pr = it / 4, t = it % 4;
+    float v[4];
+    for (int h = 0; h < 2; ++h)
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t sb = 2 * pr + h;
+        v[2 * h + e] = sb < sb_count ? sums[sb * 8 + 2 * t + e] : 0.0f;
+      }
+    float hi[4], lo[4];
+    for (int i = 0; i < 4; ++i) {
+      hi[i] = __half2float(__float2half_rn(v[i]));
+      lo[i] = v[i] - hi[i];
+    }
+    xs[((size_t)pr * nt_count + nt) * 32 + g * 4 + t] =
+        make_uint4(pack_half2(hi[0], hi[1]), pack_half2(hi[2], hi[3]), pack_half2(lo[0], lo[1]), pack_half2(lo[2], lo[3]));
+  }
+  __syncthreads();
+}
+
 GemvShape gemv_shape(int quant, uint32_t rows, uint32_t cols);
 GemvPlan gemv_plan(const GemvShape& s, int q, int sm_count);
 

@@ -1,0 +1,46 @@
+// llama.cuh — kernels of the Llama-shaped decoder family (dense GQA attention with RoPE, SwiGLU FFN,
+// GGUF Q4_K / Q8_0 weights, paged fp16 KV cache).  The reference has no implementation of this family
+// (its llama path is the un-vendored llama.cpp); the per-layer math is the oracle's orc_llama_layer.
+#pragma once
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace clm {
+
+constexpr int kPageTokens = 64;  // KV page: 64 positions of one KV head
+constexpr int kAttnWarps = 4;    // pages per attention CTA (one per warp)
+
+struct LlamaDims {
+  int H = 0, nh = 0, nkv = 0, hd = 0, F = 0, V = 0;
+  float theta = 500000.0f, eps = 1e-5f;
+  int quant = CLM_QUANT_Q4_K;
+  int qd() const { return nh * hd; }
+  int kvd() const { return nkv * hd; }
+};
+
+// Attention partials of one (m-tile, kv head, page): 16 rows x (hd values + m + l).
+inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 2); }
+
+int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int q, int H, float* d_h, cudaStream_t st);
+// h[p] += sum_s part[s][p] (nsplit may be 0); x = rmsnorm(h) * w -> fragments for a GEMV over H columns.
+// Launches 8*nt CTAs (rows >= q write zeros).
+int launch_norm(const float* d_part, int nsplit, int part_rows, int q, int H, const float* d_w, float eps, float* d_h,
+                int nt, float hi_scale, void* d_xfrag, void* d_xs, cudaStream_t st);
+int launch_rope_kv(const float* d_part, int nsplit, int q, const LlamaDims& d, const long long* d_pos,
+                   const int32_t* d_parent, const int32_t* d_pages, __half* d_k, __half* d_v, __half* d_q,
+                   cudaStream_t st);
+int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
+                     const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
+                     float* d_part, cudaStream_t st);
+int launch_attn_combine(const float* d_part, const long long* d_pos, int q, const LlamaDims& d, int max_pages, int nt,
+                        float hi_scale, void* d_xfrag, void* d_xs, cudaStream_t st);
+// a = silu(gate) * up from the gate|up GEMV partials (rows 2F) -> fragments for the down GEMV.
+int launch_swiglu(const float* d_part, int nsplit, int q, int F, int nt, float hi_scale, void* d_xfrag, void* d_xs,
+                  cudaStream_t st);
+// Copies h[p][0:H] of rows into the boundary records out[p] = {S = h, P = 0, g = 1} (hc = 1).
+int launch_pack_boundary(const float* d_h, const float* d_part, int nsplit, int q, int H, float* d_out,
+                         cudaStream_t st);
+// Folds boundary records (S + g*P) into h (hc = 1).
+int launch_unpack_boundary(const float* d_in, int q, int H, float* d_h, cudaStream_t st);
+
+}  // namespace clm

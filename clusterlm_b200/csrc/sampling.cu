@@ -16,6 +16,7 @@
 #include <cfloat>
 
 #include "common.cuh"
+#include "pdl.cuh"
 #include "sampling.cuh"
 
 namespace clm {
@@ -362,10 +363,12 @@ __device__ double block_sum_d(double v) {
 // ---------------------------------------------------------------------------------------------------
 // kernels
 // ---------------------------------------------------------------------------------------------------
-// argmax per row: first index of the maximum; a NaN at index 0 pins the answer to 0 and NaNs elsewhere
-// are never chosen (the reference's `logits[i] > logits[best]` scan).
-__global__ void argmax_rows_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
-  const float* l = logits + (size_t)blockIdx.x * vocab;
+// First index of the maximum of l[0..vocab); a NaN at index 0 pins the answer to 0 and NaNs elsewhere are never
+// chosen (the reference's `logits[i] > logits[best]` scan).  All threads get the result.
+__device__ int32_t block_argmax(const float* __restrict__ l, uint32_t vocab) {
+  __shared__ float sv[32];
+  __shared__ int32_t si[32];
+  __shared__ int32_t s_res;
   float best = -INFINITY;
   int32_t bi = INT32_MAX;
   for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
@@ -375,8 +378,6 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, uint32_t vo
       bi = (int32_t)i;
     }
   }
-  __shared__ float sv[32];
-  __shared__ int32_t si[32];
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best, o);
     const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
@@ -402,13 +403,27 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, uint32_t vo
         bi = oi;
       }
     }
-    if (lane == 0) out[blockIdx.x] = (isnan(l[0]) || bi == INT32_MAX) ? 0 : bi;
+    if (lane == 0) s_res = (isnan(l[0]) || bi == INT32_MAX) ? 0 : bi;
   }
+  __syncthreads();
+  const int32_t r = s_res;
+  __syncthreads();
+  return r;
+}
+
+__global__ void argmax_rows_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  const int32_t r = block_argmax(logits + (size_t)blockIdx.x * vocab, vocab);
+  if (threadIdx.x == 0) out[blockIdx.x] = r;
 }
 
 // Row statistics for distribution(): max and kept = sum exp(double(l - max)/T).
 __global__ void row_stats_kernel(const float* __restrict__ logits, uint32_t vocab, float T, float* __restrict__ mx_out,
-                                 double* __restrict__ kept_out) {
+                                 double* __restrict__ kept_out, const RoundCtl* __restrict__ ctl) {
+  griddep_wait();
+  griddep_launch();
+  if (ctl) T = ctl->temperature;
   const float* l = logits + (size_t)blockIdx.x * vocab;
   float m = -FLT_MAX;
   for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, l[i]);
@@ -450,6 +465,7 @@ __global__ void __launch_bounds__(1024) sample_rows_kernel(const float* __restri
 
 __device__ __forceinline__ double draw_uniform(const double* uniforms, uint64_t seed, uint64_t counter_base,
                                                uint32_t seq, uint32_t k, uint32_t n) {
+  // Philox counter (draw, sequence, counter_base lo, counter_base hi) under key `seed`.
   if (uniforms) return uniforms[(size_t)seq * (k + 1) + n];
   return philox_uniform(seed, n, seq, (uint32_t)counter_base, (uint32_t)(counter_base >> 32));
 }
@@ -509,8 +525,16 @@ __global__ void __launch_bounds__(1024) verify_kernel(const float* __restrict__ 
 __global__ void __launch_bounds__(1024) accept_logits_kernel(
     const float* __restrict__ tl, const float* __restrict__ dl, const int32_t* __restrict__ drafts, uint32_t k,
     uint32_t vocab, float T, const float* __restrict__ mx, const double* __restrict__ kept,
-    const double* __restrict__ uniforms, uint64_t seed, uint64_t counter_base, uint32_t* __restrict__ accepted,
-    int32_t* __restrict__ next) {
+    const double* __restrict__ uniforms, uint64_t seed, uint64_t counter_base,
+    const unsigned long long* __restrict__ d_counter, uint32_t* __restrict__ accepted, int32_t* __restrict__ next,
+    const RoundCtl* __restrict__ ctl) {
+  griddep_wait();
+  griddep_launch();
+  if (d_counter) counter_base = *d_counter;
+  if (ctl) {
+    T = ctl->temperature;
+    seed = ctl->seed;
+  }
   const uint32_t b = blockIdx.x;
   const float* tb = tl + (size_t)b * (k + 1) * vocab;
   const float* db = dl ? dl + (size_t)b * k * vocab : nullptr;
@@ -575,27 +599,57 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t first, uint32_t c
 // ---------------------------------------------------------------------------------------------------
 int launch_argmax(const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out, cudaStream_t st) {
   if (rows == 0) return CLM_OK;
-  argmax_rows_kernel<<<rows, 1024, 0, st>>>(d_logits, vocab, d_out);
-  CLM_LAUNCHED("argmax_rows_kernel");
-  return CLM_OK;
+  return launch_pdl(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, d_logits, vocab, d_out);
 }
 
 int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t vocab, float T, float* d_mx, double* d_kept,
-                     cudaStream_t st) {
+                     cudaStream_t st, const RoundCtl* ctl) {
   if (rows == 0) return CLM_OK;
-  row_stats_kernel<<<rows, 512, 0, st>>>(d_logits, vocab, T, d_mx, d_kept);
-  CLM_LAUNCHED("row_stats_kernel");
-  return CLM_OK;
+  return launch_pdl(row_stats_kernel, dim3(rows), dim3(512), 0, st, d_logits, vocab, T, d_mx, d_kept, ctl);
 }
 
 int launch_accept_logits(const float* d_tl, const float* d_dl, const int32_t* d_drafts, uint32_t batch, uint32_t k,
                          uint32_t vocab, float T, const float* d_mx, const double* d_kept, const double* d_uniforms,
-                         uint64_t seed, uint64_t counter_base, uint32_t* d_accepted, int32_t* d_next,
-                         cudaStream_t st) {
-  accept_logits_kernel<<<batch, 1024, 0, st>>>(d_tl, d_dl, d_drafts, k, vocab, T, d_mx, d_kept, d_uniforms, seed,
-                                               counter_base, d_accepted, d_next);
-  CLM_LAUNCHED("accept_logits_kernel");
-  return CLM_OK;
+                         uint64_t seed, uint64_t counter_base, const unsigned long long* d_counter,
+                         uint32_t* d_accepted, int32_t* d_next, cudaStream_t st, const RoundCtl* ctl) {
+  return launch_pdl(accept_logits_kernel, dim3(batch), dim3(1024), 0, st, d_tl, d_dl, d_drafts, k, vocab, T, d_mx,
+                    d_kept, d_uniforms, seed, counter_base, d_counter, d_accepted, d_next, ctl);
+}
+
+// One row of logits -> one token: argmax (T <= 0) or sample_from(distribution(row, T)) with the Philox
+// uniform (draw, stream, counter lo, counter hi), counter read from *d_counter.
+__global__ void __launch_bounds__(1024) sample_logits_kernel(const float* __restrict__ logits, uint32_t vocab, float T,
+                                                             uint64_t seed, uint32_t draw, uint32_t stream_id,
+                                                             const unsigned long long* __restrict__ d_counter,
+                                                             int32_t* __restrict__ out, const RoundCtl* __restrict__ ctl) {
+  griddep_wait();
+  griddep_launch();
+  if (ctl) {
+    T = ctl->temperature;
+    seed = ctl->seed;
+  }
+  if (T <= 0.0f) {
+    const int32_t r = block_argmax(logits, vocab);
+    if (threadIdx.x == 0) *out = r;
+    return;
+  }
+  float m = -FLT_MAX;
+  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, logits[i]);
+  m = block_max(m);
+  double s = 0.0;
+  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) s += exp((double)__fsub_rn(logits[i], m) / (double)T);
+  s = block_sum_d(s);
+  const unsigned long long c = d_counter ? *d_counter : 0ull;
+  const double u = philox_uniform(seed, draw, stream_id, (uint32_t)c, (uint32_t)(c >> 32));
+  const int32_t tok = exact_sample(LogitRow{logits, m, s, T}, vocab, u);
+  if (threadIdx.x == 0) *out = tok;
+}
+
+int launch_sample_logits(const float* d_logits, uint32_t vocab, float T, uint64_t seed, uint32_t draw,
+                         uint32_t stream_id, const unsigned long long* d_counter, int32_t* d_out, cudaStream_t st,
+                         const RoundCtl* ctl) {
+  return launch_pdl(sample_logits_kernel, dim3(1), dim3(1024), 0, st, d_logits, vocab, T, seed, draw, stream_id,
+                    d_counter, d_out, ctl);
 }
 
 }  // namespace clm
@@ -683,7 +737,7 @@ int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_
   CLM_TRY(launch_row_stats(d_tl, trows, vocab, temperature, mx, kept, st));
   if (drows) CLM_TRY(launch_row_stats(d_dl, drows, vocab, temperature, mx + trows, kept + trows, st));
   return launch_accept_logits(d_tl, d_dl, d_drafts, batch, k, vocab, temperature, mx, kept, d_uniforms, seed,
-                              counter_base, d_accepted, d_next, st);
+                              counter_base, nullptr, d_accepted, d_next, st);
 }
 
 int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,

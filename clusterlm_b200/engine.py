@@ -1,0 +1,179 @@
+"""Python face of the engine ABI (clm_b200_llama_create and friends) with host numpy buffers.
+
+Mirrors the ExecutionDomain flow of the reference (runtime/domain/include/clusterlm/domain/
+execution_domain.hpp:143-174): create -> (weights) -> prepare -> open_session -> run_window -> commit /
+abort.  Admission rules (epochs, window ids) belong to the caller's ledger; the engine checks positions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._native import QUANTS, call
+
+_vp = C.c_void_p
+
+ROLE_PREFIX, ROLE_MIDDLE, ROLE_TAIL, ROLE_WHOLE = 0, 1, 2, 3
+
+
+class _Geometry(C.Structure):
+    _fields_ = [("n_layers", C.c_uint32), ("hidden", C.c_uint32), ("n_heads", C.c_uint32),
+                ("n_kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("ffn", C.c_uint32), ("vocab", C.c_uint32),
+                ("rope_theta", C.c_float), ("rms_eps", C.c_float), ("quant", C.c_int), ("mtp", C.c_uint32)]
+
+
+class _Spec(C.Structure):
+    _fields_ = [("layer_begin", C.c_uint32), ("layer_end", C.c_uint32), ("role", C.c_int),
+                ("max_context", C.c_uint32), ("max_window", C.c_uint32), ("max_sessions", C.c_uint32)]
+
+
+class _SpecParams(C.Structure):
+    _fields_ = [("q", C.c_uint32), ("temperature", C.c_float), ("seed", C.c_uint64)]
+
+
+@dataclass
+class LlamaGeometry:
+    n_layers: int
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rope_theta: float = 500000.0
+    rms_eps: float = 1e-5
+    quant: str = "q4_k"
+    mtp: bool = True
+
+    def c(self) -> _Geometry:
+        return _Geometry(self.n_layers, self.hidden, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn,
+                         self.vocab, self.rope_theta, self.rms_eps, QUANTS[self.quant], int(self.mtp))
+
+
+LLAMA3_8B = LlamaGeometry(32, 4096, 32, 8, 128, 14336, 128256)
+LLAMA3_70B = LlamaGeometry(80, 8192, 64, 8, 128, 28672, 128256)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+class Engine:
+    def __init__(self, ctx, geometry: LlamaGeometry, layer_begin: int, layer_end: int, role: int,
+                 max_context: int, max_window: int, max_sessions: int = 1):
+        self.ctx, self.geo, self.role = ctx, geometry, role
+        self.max_window = max_window
+        self._g = geometry.c()
+        self._s = _Spec(layer_begin, layer_end, role, max_context, max_window, max_sessions)
+        h = _vp()
+        call("clm_b200_llama_create", ctx.h, C.byref(self._g), C.byref(self._s), C.byref(h))
+        self.h = h
+
+    def close(self):
+        if self.h:
+            call("clm_b200_engine_destroy", self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def generate_weights(self, seed: int = 0, stddev: float = 0.02):
+        call("clm_b200_engine_generate_weights", self.h, seed, stddev)
+
+    def prepare(self):
+        call("clm_b200_engine_prepare", self.h)
+
+    def info(self):
+        w, s, f = C.c_uint64(), C.c_uint64(), C.c_uint32()
+        call("clm_b200_engine_info", self.h, C.byref(w), C.byref(s), C.byref(f))
+        return {"weight_bytes": w.value, "state_bytes_per_session": s.value, "floats_per_position": f.value}
+
+    def open_session(self, session: int):
+        call("clm_b200_session_open", self.h, session)
+
+    def close_session(self, session: int):
+        call("clm_b200_session_close", self.h, session)
+
+    def last_launches(self) -> int:
+        v = C.c_uint64()
+        call("clm_b200_engine_last_launches", self.h, C.byref(v))
+        return v.value
+
+    def stream(self) -> int:
+        v = _vp()
+        call("clm_b200_ctx_stream", self.ctx.h, C.byref(v))
+        return v.value or 0
+
+    def position(self, session: int) -> int:
+        v = C.c_uint64()
+        call("clm_b200_session_position", self.h, session, C.byref(v))
+        return v.value
+
+    def run_window(self, session: int, base: int, tokens=None, records=None):
+        """Returns logits (q, vocab) for tail/whole stages, records (q, 2H+1) otherwise."""
+        fpp = 2 * self.geo.hidden + 1
+        if tokens is not None:
+            tokens = _i32(tokens)
+            q = tokens.size
+        else:
+            records = _f32(records)
+            q = records.shape[0]
+        has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
+        out = np.zeros((q, self.geo.vocab if has_head else fpp), np.float32)
+        call("clm_b200_run_window", self.h, session, base, q,
+             None if tokens is None else tokens.ctypes.data_as(_vp),
+             None if records is None else records.ctypes.data_as(_vp),
+             None if has_head else out.ctypes.data_as(_vp), out.ctypes.data_as(_vp) if has_head else None)
+        return out
+
+    def run_window_device(self, session: int, base: int, d_tokens=None, d_out=None, stream=None, d_records=None):
+        """Device-buffer window (torch CUDA tensors): tokens or records in; logits or records out."""
+        q = (d_tokens if d_tokens is not None else d_records).shape[0]
+        has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
+        call("clm_b200_run_window_device", self.h, session, base, q,
+             None if d_tokens is None else _vp(d_tokens.data_ptr()),
+             None if d_records is None else _vp(d_records.data_ptr()),
+             None if has_head else _vp(d_out.data_ptr()), _vp(d_out.data_ptr()) if has_head else None,
+             None if stream is None else _vp(stream))
+
+    def commit(self, session: int, accepted: int):
+        call("clm_b200_commit", self.h, session, accepted)
+
+    def abort(self, session: int):
+        call("clm_b200_abort", self.h, session)
+
+    def mtp_draft(self, prev: int, count: int, temperature: float = 0.0, seed: int = 0, counter: int = 0,
+                  want_logits: bool = False):
+        toks = np.zeros(count, np.int32)
+        logits = np.zeros((count, self.geo.vocab), np.float32) if want_logits else None
+        call("clm_b200_mtp_draft", self.h, prev, count, temperature, seed, counter, toks.ctypes.data_as(_vp),
+             None if logits is None else logits.ctypes.data_as(_vp))
+        return (toks, logits) if want_logits else toks
+
+    def spec_begin(self, session: int, prompt, q: int, temperature: float = 0.0, seed: int = 0):
+        prompt = _i32(prompt)
+        p = _SpecParams(q, temperature, seed)
+        call("clm_b200_spec_begin", self.h, session, prompt.ctypes.data_as(_vp), prompt.size, C.byref(p))
+
+    def spec_round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0) -> np.ndarray:
+        p = _SpecParams(q, temperature, seed)
+        toks = np.zeros(q + 1, np.int32)
+        n = C.c_uint32()
+        call("clm_b200_spec_round", self.h, session, C.byref(p), toks.ctypes.data_as(_vp), C.byref(n))
+        return toks[: n.value].copy()
+
+    def spec_round_device(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None,
+                          d_count=None, stream=None):
+        p = _SpecParams(q, temperature, seed)
+        call("clm_b200_spec_round_device", self.h, session, C.byref(p),
+             None if d_tokens is None else _vp(d_tokens.data_ptr()),
+             None if d_count is None else _vp(d_count.data_ptr()), stream)

