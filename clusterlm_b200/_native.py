@@ -59,6 +59,8 @@ _SIGS = {
     "clm_b200_accept_logits": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _f, _vp, _u64, _u64, _vp, _vp, _vp]),
     "clm_b200_philox_uniforms": (_i, [_vp, _u64, _u64, _u32, _u32, _u64, _vp, _vp]),
     "clm_b200_llama_create": (_i, [_vp, _vp, _vp, C.POINTER(_vp)]),
+    "clm_b200_fixture_create": (_i, [_vp, _vp, _vp, C.POINTER(_vp)]),
+    "clm_b200_engine_set_object": (_i, [_vp, C.c_char_p, _i, _vp, _u64]),
     "clm_b200_engine_destroy": (_i, [_vp]),
     "clm_b200_engine_generate_weights": (_i, [_vp, _u64, _f]),
     "clm_b200_engine_prepare": (_i, [_vp]),

@@ -102,15 +102,37 @@ __device__ void encode_q4k_block(const float* x, uint8_t* o) {
   }
 }
 
+// binary16 bits of f, round to nearest even, by integer arithmetic (the binary16 encoding rules; same
+// results as tensor_codec.cpp:42-64 float_to_half).
+__device__ __forceinline__ uint32_t f32_to_f16_bits(float f) {
+  const uint32_t bits = __float_as_uint(f);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const uint32_t a = bits & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return sign | 0x7E00u;
+  if (a >= 0x47800000u) return sign | 0x7C00u;
+  if (a < 0x38800000u) {
+    if (a < 0x33000000u) return sign;
+    const uint32_t e = a >> 23, m = (a & 0x7FFFFFu) | 0x800000u, sh = 126 - e;
+    uint32_t h = m >> sh;
+    const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+    if (rem > half || (rem == half && (h & 1u))) ++h;
+    return sign | h;
+  }
+  uint32_t h = (((a >> 23) - 127 + 15) << 10) | ((a >> 13) & 0x3FFu);
+  const uint32_t rem = a & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+  return sign | h;
+}
+
 // tensor_codec.cpp:127-141 (encode_q8_0_ggml).
 __device__ void encode_q8_0_block(const float* x, uint8_t* o) {
   float amax = 0.0f;
   for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
   const float d = __fdiv_rn(amax, 127.0f);
   const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-  const unsigned short h = __half_as_ushort(__float2half_rn(d));
-  o[0] = (uint8_t)(h & 0xFF);
-  o[1] = (uint8_t)(h >> 8);
+  const uint32_t h = f32_to_f16_bits(d);
+  o[0] = (uint8_t)(h & 0xFFu);
+  o[1] = (uint8_t)((h >> 8) & 0xFFu);
   for (int i = 0; i < 32; ++i) o[2 + i] = (uint8_t)(int8_t)roundf(__fmul_rn(x[i], id));
 }
 

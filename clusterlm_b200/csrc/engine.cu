@@ -14,7 +14,9 @@
 #include <vector>
 
 #include "codec.cuh"
+#include "engine.cuh"
 #include "gemv.cuh"
+#include "gemv2.cuh"
 #include "llama.cuh"
 #include "matrix.cuh"
 #include "pdl.cuh"
@@ -107,8 +109,7 @@ __global__ void embed_guard_kernel(const int32_t* __restrict__ tokens, int q, in
 
 using namespace clm;
 
-struct clm_b200_engine {
-  clm_b200_ctx* ctx = nullptr;
+struct LlamaEngine : clm_b200_engine {
   LlamaDims d;
   clm_b200_llama_geometry geo{};
   clm_b200_stage_spec spec{};
@@ -132,9 +133,11 @@ struct clm_b200_engine {
   std::vector<__half*> kpool, vpool;
   // window buffers
   float* h = nullptr;
-  float* part = nullptr;
-  uint8_t* xfrag = nullptr;
-  uint8_t* xs = nullptr;
+  float* part = nullptr;     // GEMV split partials (last-CTA reduction)
+  int* gcount = nullptr;     // GEMV row-group counters
+  int* acount = nullptr;     // attention (m-tile, kv head) counters
+  XBuf xa, xb;               // activation hand-offs, alternated along the chain
+  float* ones_h = nullptr;   // norm weight 1 for stage ends without a following norm
   __half* q16 = nullptr;
   float* attn_part = nullptr;
   float* logits = nullptr;
@@ -153,7 +156,6 @@ struct clm_b200_engine {
   int* bad = nullptr;
   unsigned long long* zero_counter = nullptr;
   RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
-  unsigned long long last_launches = 0;  // kernels in the last window / round
   std::map<uint64_t, std::unique_ptr<Session>> sessions;
   std::vector<void*> allocations;
   uint64_t weight_bytes = 0;
@@ -175,8 +177,8 @@ struct clm_b200_engine {
     return CLM_OK;
   }
 
-  int make_gemv(Gemv& g, const void* d_src, uint64_t nbytes, uint32_t rows, uint32_t cols) {
-    CLM_TRY(matrix_create(ctx, d.quant, d_src, true, nbytes, rows, cols, &g.m));
+  int make_gemv(Gemv& g, const void* d_src, uint64_t nbytes, uint32_t rows, uint32_t cols, uint32_t half_rows = 0) {
+    CLM_TRY(matrix_create(ctx, d.quant, d_src, true, nbytes, rows, cols, &g.m, half_rows));
     g.plan[0] = gemv_plan(g.m->shape, 8, ctx->sm_count);
     g.plan[1] = gemv_plan(g.m->shape, 16, ctx->sm_count);
     weight_bytes += g.m->bytes;
@@ -190,61 +192,87 @@ struct clm_b200_engine {
     return CLM_OK;
   }
 
-  // ---- GEMV in the chain: returns the number of partial splits written to `part` (0: wrote `direct`)
-  int gemv(const Gemv& g, int q, float* direct, int* nsplit, cudaStream_t st) {
+  // ---- one fused GEMV of the chain
+  int gemv(const Gemv& g, int q, const XBuf& in, const Epi& epi, cudaStream_t st) {
     const GemvPlan& p = g.for_q(q);
-    const bool to_direct = direct != nullptr && p.ksplit == 1;
-    CLM_TRY(launch_gemv(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), xfrag, xs, q,
-                        to_direct ? direct : part, st));
-    *nsplit = to_direct ? 0 : p.ksplit;
-    if (direct != nullptr && !to_direct) {
-      CLM_TRY(launch_reduce_splits(part, p.ksplit, q, g.m->rows, direct, st));
-      *nsplit = 0;
-    }
-    return CLM_OK;
+    return launch_gemv3(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), in, q, epi, part, gcount, st);
+  }
+  Epi epi_base(int kind) const {
+    Epi e;
+    e.kind = kind;
+    e.ss_n = (float)d.H;
+    e.eps = d.eps;
+    e.hi_scale = hi_scale();
+    e.err = bad;
+    return e;
+  }
+  Epi epi_resid(float* hbuf, const float* wnext, const XBuf& next) const {
+    Epi e = epi_base(EPI_RESID_PREP);
+    e.h = hbuf;
+    e.H = d.H;
+    e.wnext = wnext;
+    e.next = next;
+    return e;
   }
 
-  // ---- the layer range over q rows; input already in h (nsplit_in = 0)
-  int enqueue_layers(Session& s, int q, int* nsplit_out, cudaStream_t st) {
+  // ---- the layer range over q rows; h holds the stage input and xa its first norm's preparation
+  int enqueue_layers(Session& s, int q, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
-    int ns = 0;
     const long long* pos = &s.d_state->pos;
     for (size_t li = 0; li < layers.size(); ++li) {
       Layer& L = layers[li];
-      const int lg = (int)(spec.layer_begin + li);
-      (void)lg;
-      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, L.attn_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
-      CLM_TRY(gemv(L.qkv, q, nullptr, &ns, st));
-      CLM_TRY(launch_rope_kv(part, ns, q, d, pos, nullptr, s.d_pages, kpool[li], vpool[li], q16, st));
-      CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, nullptr, q, d, max_pages, attn_part, st));
-      CLM_TRY(launch_attn_combine(attn_part, pos, q, d, max_pages, nt, hi_scale(), xfrag, xs, st));
-      CLM_TRY(gemv(L.o, q, nullptr, &ns, st));
-      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, L.ffn_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
-      CLM_TRY(gemv(L.gu, q, nullptr, &ns, st));
-      CLM_TRY(launch_swiglu(part, ns, q, d.F, nt, hi_scale(), xfrag, xs, st));
-      CLM_TRY(gemv(L.down, q, nullptr, &ns, st));
+      // q, k, v with RoPE and the paged KV append fused into the epilogue (input: xa = h * attn_norm)
+      Epi ek = epi_base(EPI_ROPE_KV);
+      ek.nh = d.nh;
+      ek.nkv = d.nkv;
+      ek.hd = d.hd;
+      ek.theta = d.theta;
+      ek.pos = pos;
+      ek.pages = s.d_pages;
+      ek.kpool = kpool[li];
+      ek.vpool = vpool[li];
+      ek.q16 = q16;
+      CLM_TRY(gemv(L.qkv, q, xa, ek, st));
+      // attention -> xb (W_o input)
+      CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, nullptr, q, d, max_pages, attn_part, acount,
+                               nt, hi_scale(), xb.frag, xb.sum, st));
+      XBuf ob = xb;
+      ob.ss = nullptr;
+      // h += W_o o ; xa = h * ffn_norm (+ sum of squares)
+      CLM_TRY(gemv(L.o, q, ob, epi_resid(h, L.ffn_norm, xa), st));
+      // SwiGLU of the gate/up rows -> xb (W_down input)
+      Epi es = epi_base(EPI_SWIGLU_PREP);
+      es.ffn = d.F;
+      es.next = xb;
+      CLM_TRY(gemv(L.gu, q, xa, es, st));
+      // h += W_down a ; xa = h * (next layer's attn_norm | output norm | 1)
+      const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
+      XBuf db = xb;
+      db.ss = nullptr;
+      CLM_TRY(gemv(L.down, q, db, epi_resid(h, wnext, xa), st));
     }
-    *nsplit_out = ns;
     return CLM_OK;
   }
 
   // ---- a full window: input (tokens or records) -> layers -> logits or records
   int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st) {
+    const int nt = q <= 8 ? 1 : 2;
     if (has_tokens) {
       CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(64), 0, st, d_tok, q, (int)d.V, tokens, bad));
       CLM_TRY(launch_embed(embd, d.quant, tokens, q, d.H, h, st));
     } else {
       CLM_TRY(launch_unpack_boundary(bin, q, d.H, h, st));
     }
-    int ns = 0;
-    CLM_TRY(enqueue_layers(s, q, &ns, st));
+    const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
+    CLM_TRY(launch_prep_rows(h, d.H, q, d.H, w0, nt, hi_scale(), xa, true, st));
+    CLM_TRY(enqueue_layers(s, q, st));
     if (has_head) {
-      const int nt = q <= 8 ? 1 : 2;
-      CLM_TRY(launch_norm(part, ns, d.H, q, d.H, out_norm, d.eps, h, nt, hi_scale(), xfrag, xs, st));
-      int dummy = 0;
-      CLM_TRY(gemv(head, q, logits, &dummy, st));
+      Epi eo = epi_base(EPI_STORE);
+      eo.out = logits;
+      eo.out_ld = d.V;
+      CLM_TRY(gemv(head, q, xa, eo, st));
     } else {
-      CLM_TRY(launch_pack_boundary(h, part, ns, q, d.H, bout, st));
+      CLM_TRY(launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st));
     }
     return CLM_OK;
   }
@@ -252,14 +280,18 @@ struct clm_b200_engine {
   // ---- one MTP step: prev token (device) -> draft logits row
   int enqueue_mtp_step(const int32_t* d_prev, float* d_logits_row, cudaStream_t st) {
     CLM_TRY(launch_embed(embd, d.quant, d_prev, 1, d.H, h_mtp, st));
-    CLM_TRY(launch_norm(part, 0, d.H, 1, d.H, mtp_ffn_norm, d.eps, h_mtp, 1, hi_scale(), xfrag, xs, st));
-    int ns = 0;
-    CLM_TRY(gemv(mtp_gu, 1, nullptr, &ns, st));
-    CLM_TRY(launch_swiglu(part, ns, 1, d.F, 1, hi_scale(), xfrag, xs, st));
-    CLM_TRY(gemv(mtp_down, 1, nullptr, &ns, st));
-    CLM_TRY(launch_norm(part, ns, d.H, 1, d.H, mtp_out_norm, d.eps, h_mtp, 1, hi_scale(), xfrag, xs, st));
-    int dummy = 0;
-    CLM_TRY(gemv(head, 1, d_logits_row, &dummy, st));
+    CLM_TRY(launch_prep_rows(h_mtp, d.H, 1, d.H, mtp_ffn_norm, 1, hi_scale(), xa, true, st));
+    Epi es = epi_base(EPI_SWIGLU_PREP);
+    es.ffn = d.F;
+    es.next = xb;
+    CLM_TRY(gemv(mtp_gu, 1, xa, es, st));
+    XBuf db = xb;
+    db.ss = nullptr;
+    CLM_TRY(gemv(mtp_down, 1, db, epi_resid(h_mtp, mtp_out_norm, xa), st));
+    Epi eo = epi_base(EPI_STORE);
+    eo.out = d_logits_row;
+    eo.out_ld = d.V;
+    CLM_TRY(gemv(head, 1, xa, eo, st));
     return CLM_OK;
   }
 
@@ -346,7 +378,7 @@ struct clm_b200_engine {
     s.d_state = nullptr;
   }
 
-  ~clm_b200_engine() {
+  ~LlamaEngine() override {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     for (auto& kv : sessions) release_session(*kv.second);
@@ -444,21 +476,23 @@ __global__ void clm::greedy_accept_kernel(const float* __restrict__ logits, uint
 
 namespace {
 
-int engine_enter(clm_b200_engine* e) {
+int engine_enter(LlamaEngine* e) {
   CLM_CHECK(e != nullptr, CLM_INVALID_ARGUMENT, "null engine");
   return ctx_enter(e->ctx);
 }
 
-Session* find_session(clm_b200_engine* e, uint64_t id) {
+Session* find_session(LlamaEngine* e, uint64_t id) {
   auto it = e->sessions.find(id);
   return it == e->sessions.end() ? nullptr : it->second.get();
 }
 
 }  // namespace
 
-extern "C" {
+namespace clm {
 
-int clm_b200_llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_b200_stage_spec* spec,
+LlamaEngine* as_llama(clm_b200_engine* e) { return static_cast<LlamaEngine*>(e); }
+
+int llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_b200_stage_spec* spec,
                           clm_b200_engine** out) {
   CLM_TRY(ctx_enter(ctx));
   CLM_CHECK(g && spec && out, CLM_INVALID_ARGUMENT, "null argument");
@@ -485,8 +519,9 @@ int clm_b200_llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, c
     CLM_CHECK(spec->layer_end == g->n_layers, CLM_INVALID_ARGUMENT, "tail domain must end at the last layer");
   if (spec->role == CLM_ROLE_MIDDLE)
     CLM_CHECK(spec->layer_end > spec->layer_begin, CLM_INVALID_ARGUMENT, "middle domain needs at least one layer");
-  auto* e = new clm_b200_engine();
+  auto* e = new LlamaEngine();
   e->ctx = ctx;
+  e->family = CLM_FAMILY_LLAMA;
   e->geo = *g;
   e->spec = *spec;
   e->d.H = (int)g->hidden;
@@ -507,13 +542,8 @@ int clm_b200_llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, c
   return CLM_OK;
 }
 
-int clm_b200_engine_destroy(clm_b200_engine* e) {
-  if (!e) return CLM_OK;
-  delete e;
-  return CLM_OK;
-}
 
-int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float stddev) {
+int llama_generate_weights(LlamaEngine* e, uint64_t seed, float stddev) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(!e->weights_ready, CLM_FAILED_PRECONDITION, "weights already bound");
   const LlamaDims& d = e->d;
@@ -528,7 +558,7 @@ int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float st
   auto gen = [&](uint32_t id, uint64_t n, uint8_t* dst) { return launch_gen_encode(d.quant, seed, id, n, stddev, dst, st); };
   do {
     for (uint32_t L = e->spec.layer_begin; L < e->spec.layer_end && rc == CLM_OK; ++L) {
-      clm_b200_engine::Layer lay;
+      LlamaEngine::Layer lay;
       const uint64_t H = d.H, qd = d.qd(), kvd = d.kvd(), F = d.F;
       const uint32_t id = 16 * L;
       if ((rc = gen(id + 0, qd * H, tmp)) || (rc = gen(id + 1, kvd * H, tmp + tbytes(qd * H))) ||
@@ -538,7 +568,7 @@ int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float st
       if ((rc = gen(id + 3, H * qd, tmp)) || (rc = e->make_gemv(lay.o, tmp, tbytes(H * qd), (uint32_t)H, (uint32_t)qd)))
         break;
       if ((rc = gen(id + 4, F * H, tmp)) || (rc = gen(id + 5, F * H, tmp + tbytes(F * H))) ||
-          (rc = e->make_gemv(lay.gu, tmp, tbytes(2 * F * H), (uint32_t)(2 * F), (uint32_t)H)))
+          (rc = e->make_gemv(lay.gu, tmp, tbytes(2 * F * H), (uint32_t)(2 * F), (uint32_t)H, (uint32_t)F)))
         break;
       if ((rc = gen(id + 6, H * F, tmp)) || (rc = e->make_gemv(lay.down, tmp, tbytes(H * F), (uint32_t)H, (uint32_t)F)))
         break;
@@ -559,7 +589,7 @@ int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float st
     if (e->has_mtp) {
       const uint64_t FH = (uint64_t)d.F * d.H;
       if ((rc = gen(1002, FH, tmp)) || (rc = gen(1003, FH, tmp + tbytes(FH))) ||
-          (rc = e->make_gemv(e->mtp_gu, tmp, tbytes(2 * FH), (uint32_t)(2 * d.F), (uint32_t)d.H)))
+          (rc = e->make_gemv(e->mtp_gu, tmp, tbytes(2 * FH), (uint32_t)(2 * d.F), (uint32_t)d.H, (uint32_t)d.F)))
         break;
       if ((rc = gen(1004, FH, tmp)) || (rc = e->make_gemv(e->mtp_down, tmp, tbytes(FH), (uint32_t)d.H, (uint32_t)d.F)))
         break;
@@ -572,22 +602,19 @@ int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float st
   return rc;
 }
 
-int clm_b200_engine_prepare(clm_b200_engine* e) {
+int llama_prepare(LlamaEngine* e) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->weights_ready, CLM_FAILED_PRECONDITION, "weights are not bound");
   CLM_CHECK(!e->prepared, CLM_FAILED_PRECONDITION, "engine already prepared");
   const LlamaDims& d = e->d;
   const int W = e->wmax();
-  // largest partial / fragment buffers over every GEMV of this stage at nt = 1 and 2
-  uint64_t part_floats = (uint64_t)W * std::max(d.H, 2 * d.F), xfrag = 0, xs = 0;
+  // largest split-partial buffer over every GEMV of this stage at nt = 1 and 2
+  uint64_t part_floats = 1, max_ng = 1;
   auto account = [&](const Gemv& g) {
     if (!g.m) return;
-    for (int i = 0; i < 2; ++i) {
-      const GemvPlan& p = g.plan[i];
-      part_floats = std::max<uint64_t>(part_floats, (uint64_t)p.ksplit * W * g.m->rows);
-      xfrag = std::max<uint64_t>(xfrag, p.xfrag_bytes);
-      xs = std::max<uint64_t>(xs, p.xs_bytes);
-    }
+    for (int i = 0; i < 2; ++i)
+      part_floats = std::max<uint64_t>(part_floats, (uint64_t)g.m->shape.ng * g.plan[i].ksplit * W * 128);
+    max_ng = std::max<uint64_t>(max_ng, g.m->shape.ng);
   };
   for (auto& L : e->layers) {
     account(L.qkv);
@@ -598,14 +625,25 @@ int clm_b200_engine_prepare(clm_b200_engine* e) {
   account(e->head);
   account(e->mtp_gu);
   account(e->mtp_down);
-  part_floats = std::max<uint64_t>(part_floats, (uint64_t)W * (d.qd() + 2 * d.kvd()));
   e->pages_total = (int)e->spec.max_sessions * e->max_pages;
   const size_t page_bytes = (size_t)d.nkv * kPageTokens * d.hd * sizeof(__half);
   const int mtiles = (W * (d.nh / d.nkv) + 15) / 16;
+  const int maxcols = std::max(std::max(d.H, d.F), d.qd());
   CLM_TRY(e->alloc_t(&e->h, (size_t)W * d.H));
   CLM_TRY(e->alloc_t(&e->part, part_floats));
-  CLM_TRY(e->alloc_t(&e->xfrag, xfrag));
-  CLM_TRY(e->alloc_t(&e->xs, xs));
+  CLM_TRY(e->alloc_t(&e->gcount, max_ng));
+  CLM_CUDA(cudaMemset(e->gcount, 0, max_ng * sizeof(int)));
+  CLM_TRY(e->alloc_t(&e->acount, (size_t)mtiles * d.nkv));
+  CLM_CUDA(cudaMemset(e->acount, 0, (size_t)mtiles * d.nkv * sizeof(int)));
+  for (XBuf* x : {&e->xa, &e->xb}) {
+    CLM_TRY(e->alloc((void**)&x->frag, xfrag_bytes(maxcols, 2)));
+    CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));
+    CLM_TRY(e->alloc((void**)&x->sum, xsum_bytes(maxcols)));
+    CLM_CUDA(cudaMemset(x->sum, 0, xsum_bytes(maxcols)));
+    CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 16) * 16));
+    x->nss = d.H / 16;
+  }
+  CLM_TRY(e->ones(&e->ones_h, d.H));
   CLM_TRY(e->alloc_t(&e->q16, (size_t)W * d.qd()));
   CLM_TRY(e->alloc_t(&e->attn_part, (size_t)mtiles * d.nkv * e->max_pages * attn_partial_floats(d.hd)));
   CLM_TRY(e->alloc_t(&e->tokens, (size_t)W));
@@ -644,7 +682,7 @@ int clm_b200_engine_prepare(clm_b200_engine* e) {
   return CLM_OK;
 }
 
-int clm_b200_engine_info(const clm_b200_engine* e, uint64_t* weight_bytes, uint64_t* state_bytes, uint32_t* fpp) {
+int llama_info(const LlamaEngine* e, uint64_t* weight_bytes, uint64_t* state_bytes, uint32_t* fpp) {
   CLM_CHECK(e != nullptr, CLM_INVALID_ARGUMENT, "null engine");
   if (weight_bytes) *weight_bytes = e->weight_bytes;
   if (state_bytes)
@@ -653,7 +691,7 @@ int clm_b200_engine_info(const clm_b200_engine* e, uint64_t* weight_bytes, uint6
   return CLM_OK;
 }
 
-int clm_b200_session_open(clm_b200_engine* e, uint64_t id) {
+int llama_session_open(LlamaEngine* e, uint64_t id) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
   CLM_CHECK(find_session(e, id) == nullptr, CLM_ALREADY_EXISTS, "session already open");
@@ -677,7 +715,7 @@ int clm_b200_session_open(clm_b200_engine* e, uint64_t id) {
   return CLM_OK;
 }
 
-int clm_b200_session_close(clm_b200_engine* e, uint64_t id) {
+int llama_session_close(LlamaEngine* e, uint64_t id) {
   CLM_TRY(engine_enter(e));
   Session* s = find_session(e, id);
   if (!s) return CLM_OK;  // idempotent cleanup (WindowLedger::abort_session)
@@ -688,7 +726,7 @@ int clm_b200_session_close(clm_b200_engine* e, uint64_t id) {
 }
 
 // Re-reads the committed position after device-driven rounds.
-static int sync_pos(clm_b200_engine* e, Session* s) {
+static int sync_pos(LlamaEngine* e, Session* s) {
   if (!s->pos_stale) return CLM_OK;
   long long p = 0;
   CLM_CUDA(cudaMemcpyAsync(&p, &s->d_state->pos, sizeof(p), cudaMemcpyDeviceToHost, e->ctx->stream));
@@ -698,7 +736,7 @@ static int sync_pos(clm_b200_engine* e, Session* s) {
   return CLM_OK;
 }
 
-static int run_window_common(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, cudaStream_t st,
+static int run_window_common(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, cudaStream_t st,
                              Session** out) {
   CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
   Session* s = find_session(e, id);
@@ -714,7 +752,7 @@ static int run_window_common(clm_b200_engine* e, uint64_t id, uint64_t base, uin
   return CLM_OK;
 }
 
-int clm_b200_run_window_device(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* d_tokens,
+int llama_run_window_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* d_tokens,
                                const float* d_in, float* d_out, float* d_logits, void* stream) {
   CLM_TRY(engine_enter(e));
   cudaStream_t st = pick_stream(e->ctx, stream);
@@ -735,11 +773,11 @@ int clm_b200_run_window_device(clm_b200_engine* e, uint64_t id, uint64_t base, u
   } else if (d_out) {
     CLM_CUDA(cudaMemcpyAsync(d_out, e->bout, rec, cudaMemcpyDeviceToDevice, st));
   }
-  s->outstanding = q;  // out-of-range device tokens embed as zeros and are reported by clm_b200_commit
+  s->outstanding = q;  // out-of-range device tokens embed as zeros and are reported by llama_commit
   return CLM_OK;
 }
 
-int clm_b200_run_window(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens,
+int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens,
                         const float* h_in, float* h_out, float* h_logits) {
   CLM_TRY(engine_enter(e));
   cudaStream_t st = e->ctx->stream;
@@ -767,7 +805,7 @@ int clm_b200_run_window(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t
   return CLM_OK;
 }
 
-int clm_b200_commit(clm_b200_engine* e, uint64_t id, uint32_t accepted) {
+int llama_commit(LlamaEngine* e, uint64_t id, uint32_t accepted) {
   CLM_TRY(engine_enter(e));
   Session* s = find_session(e, id);
   CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
@@ -789,7 +827,7 @@ int clm_b200_commit(clm_b200_engine* e, uint64_t id, uint32_t accepted) {
   return CLM_OK;
 }
 
-int clm_b200_abort(clm_b200_engine* e, uint64_t id) {
+int llama_abort(LlamaEngine* e, uint64_t id) {
   CLM_TRY(engine_enter(e));
   Session* s = find_session(e, id);
   CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
@@ -797,13 +835,7 @@ int clm_b200_abort(clm_b200_engine* e, uint64_t id) {
   return CLM_OK;
 }
 
-int clm_b200_engine_last_launches(const clm_b200_engine* e, uint64_t* launches) {
-  CLM_CHECK(e != nullptr && launches != nullptr, CLM_INVALID_ARGUMENT, "null argument");
-  *launches = e->last_launches;
-  return CLM_OK;
-}
-
-int clm_b200_session_position(const clm_b200_engine* e, uint64_t id, uint64_t* committed) {
+int llama_session_position(const LlamaEngine* e, uint64_t id, uint64_t* committed) {
   CLM_CHECK(e != nullptr && committed != nullptr, CLM_INVALID_ARGUMENT, "null argument");
   auto it = e->sessions.find(id);
   CLM_CHECK(it != e->sessions.end(), CLM_NOT_FOUND, "session not open");
@@ -811,7 +843,7 @@ int clm_b200_session_position(const clm_b200_engine* e, uint64_t id, uint64_t* c
   return CLM_OK;
 }
 
-int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,
+int llama_mtp_draft(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,
                        int32_t* h_tokens, float* h_logits) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->prepared && e->has_mtp, CLM_FAILED_PRECONDITION, "engine has no MTP head");
@@ -837,7 +869,7 @@ int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float T
   return CLM_OK;
 }
 
-int clm_b200_spec_begin(clm_b200_engine* e, uint64_t id, const int32_t* h_prompt, uint32_t n,
+int llama_spec_begin(LlamaEngine* e, uint64_t id, const int32_t* h_prompt, uint32_t n,
                         const clm_b200_spec_params* p) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->spec.role == CLM_ROLE_WHOLE, CLM_FAILED_PRECONDITION, "speculative rounds need a whole-model engine");
@@ -848,8 +880,8 @@ int clm_b200_spec_begin(clm_b200_engine* e, uint64_t id, const int32_t* h_prompt
   uint32_t off = 0;
   while (off < n) {
     const uint32_t q = std::min<uint32_t>(e->spec.max_window, n - off);
-    CLM_TRY(clm_b200_run_window(e, id, (uint64_t)s->pos, q, h_prompt + off, nullptr, nullptr, nullptr));
-    CLM_TRY(clm_b200_commit(e, id, q));
+    CLM_TRY(llama_run_window(e, id, (uint64_t)s->pos, q, h_prompt + off, nullptr, nullptr, nullptr));
+    CLM_TRY(llama_commit(e, id, q));
     off += q;
   }
   // first token from the last prompt position (argmax, or a sample with Philox draw (0, stream 2, 0))
@@ -862,7 +894,7 @@ int clm_b200_spec_begin(clm_b200_engine* e, uint64_t id, const int32_t* h_prompt
   return CLM_OK;
 }
 
-int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
+int llama_spec_round_device(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
                                uint32_t* d_count, void* stream) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(p != nullptr, CLM_INVALID_ARGUMENT, "null params");
@@ -889,12 +921,12 @@ int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t id, const clm_b200_s
   return CLM_OK;
 }
 
-int clm_b200_spec_round(clm_b200_engine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,
+int llama_spec_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,
                         uint32_t* h_count) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(h_tokens != nullptr && h_count != nullptr, CLM_INVALID_ARGUMENT, "null output");
   cudaStream_t st = e->ctx->stream;
-  CLM_TRY(clm_b200_spec_round_device(e, id, p, nullptr, nullptr, st));
+  CLM_TRY(llama_spec_round_device(e, id, p, nullptr, nullptr, st));
   CLM_CUDA(cudaMemcpyAsync(h_count, e->count, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
   CLM_CUDA(cudaMemcpyAsync(h_tokens, e->emitted, (p->q + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   CLM_CUDA(cudaStreamSynchronize(st));
@@ -905,4 +937,4 @@ int clm_b200_spec_round(clm_b200_engine* e, uint64_t id, const clm_b200_spec_par
   return CLM_OK;
 }
 
-}  // extern "C"
+}  // namespace clm

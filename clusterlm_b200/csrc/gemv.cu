@@ -2,43 +2,26 @@
 #include <algorithm>
 
 #include "gemv.cuh"
+#include "gemv_tile.cuh"
 #include "pdl.cuh"
 
 namespace clm {
 
 // ---------------------------------------------------------------------------------------------------
-// small device helpers
-// ---------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ void mma16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t lo_bcast(uint32_t x) { return __byte_perm(x, x, 0x1010); }
-__device__ __forceinline__ uint32_t hi_bcast(uint32_t x) { return __byte_perm(x, x, 0x3232); }
-
-constexpr uint32_t kHalfNeg1024x2 = 0xE400E400u;
-constexpr uint32_t kHalfNeg128x2 = 0xD800D800u;
-constexpr uint32_t kMagic = 0x64006400u;  // fp16 pair (1024, 1024)
-
-// ---------------------------------------------------------------------------------------------------
 // repack: GGUF row-major blocks -> fragment-ordered tiles
 // ---------------------------------------------------------------------------------------------------
+// Tiled row r -> source row.  half_rows = 0: identity.  half_rows = F > 0 (a stacked [gate; up] tensor of 2F
+// rows): each 128-row group g holds gate rows 64g..64g+63 then up rows F+64g..F+64g+63, so one group carries
+// both operands of SwiGLU for 64 consecutive ffn indices.
+__device__ __forceinline__ uint32_t interleaved_row(uint32_t r, uint32_t half_rows) {
+  if (half_rows == 0) return r;
+  const uint32_t grp = r / 128, k = r % 128;
+  return k < 64 ? grp * 64 + k : half_rows + grp * 64 + (k - 64);
+}
+
 // One thread per output 32-bit word of a tile's quant region, plus the scale records.
 __global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint32_t rows,
-                                  uint32_t sb_per_row, uint32_t ng) {
+                                  uint32_t sb_per_row, uint32_t ng, uint32_t half_rows) {
   const uint64_t tiles = (uint64_t)ng * sb_per_row * kGemvWarps;
   const uint64_t per_tile = 512 + 16;  // 512 qs words + 16 scale records
   const uint64_t gid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
@@ -51,6 +34,7 @@ __global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __re
   const uint32_t rt = grp * kGemvWarps + r8;
   uint8_t* t = dst + tile * kQ4kTileBytes;
   auto block_of = [&](uint32_t row) -> const uint8_t* {
+    row = interleaved_row(row, half_rows);
     return row < rows ? src + ((uint64_t)row * sb_per_row + sb) * 144 : nullptr;
   };
   if (item < 512) {
@@ -98,7 +82,7 @@ __global__ void repack_q4k_kernel(const uint8_t* __restrict__ src, uint8_t* __re
 }
 
 __global__ void repack_q80_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint32_t rows,
-                                  uint32_t sb_per_row, uint32_t ng) {
+                                  uint32_t sb_per_row, uint32_t ng, uint32_t half_rows) {
   const uint64_t tiles = (uint64_t)ng * sb_per_row * kGemvWarps;
   const uint64_t per_tile = 1024 + 16 * 8;  // 1024 q words + 16 rows x 8 half scales
   const uint64_t gid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
@@ -112,6 +96,7 @@ __global__ void repack_q80_kernel(const uint8_t* __restrict__ src, uint8_t* __re
   const uint32_t blocks_per_row = sb_per_row * 8;
   uint8_t* t = dst + tile * kQ80TileBytes;
   auto block_of = [&](uint32_t row, uint32_t j) -> const uint8_t* {
+    row = interleaved_row(row, half_rows);
     return row < rows ? src + ((uint64_t)row * blocks_per_row + (uint64_t)sb * 8 + j) * 34 : nullptr;
   };
   if (item < 1024) {
@@ -189,136 +174,6 @@ __global__ void prep_x_kernel(const float* __restrict__ x, int q, uint32_t cols,
     v.z = pack_half2(lo[0], lo[1]);
     v.w = pack_half2(lo[2], lo[3]);
     xs[i] = v;
-  }
-}
-
-// ---------------------------------------------------------------------------------------------------
-// the GEMV kernel
-// ---------------------------------------------------------------------------------------------------
-struct RawQ4k {
-  uint4 q[4];
-  uint4 rg, rg8;
-};
-struct RawQ80 {
-  uint4 q[8];
-  uint32_t sg, sg8;
-};
-
-__device__ __forceinline__ void load_raw(RawQ4k& r, const uint8_t* tile, int lane) {
-  const uint4* p = reinterpret_cast<const uint4*>(tile);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) r.q[j] = __ldg(p + j * 32 + lane);
-  const int g = lane / 4;
-  r.rg = __ldg(reinterpret_cast<const uint4*>(tile + 2048 + 16 * g));
-  r.rg8 = __ldg(reinterpret_cast<const uint4*>(tile + 2048 + 16 * (g + 8)));
-}
-__device__ __forceinline__ void load_raw(RawQ80& r, const uint8_t* tile, int lane) {
-  const uint4* p = reinterpret_cast<const uint4*>(tile);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    r.q[2 * j] = __ldg(p + j * 64 + lane * 2);
-    r.q[2 * j + 1] = __ldg(p + j * 64 + lane * 2 + 1);
-  }
-  const int g = lane / 4, t = lane % 4;
-  r.sg = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * g + 4 * t));
-  r.sg8 = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * t));
-}
-
-__device__ __forceinline__ uint32_t q4k_entries(const uint4& r, int t) {
-  const uint32_t a = t < 2 ? r.y : (t == 2 ? r.z : r.w);
-  const uint32_t b = t < 2 ? r.z : (t == 2 ? r.w : 0u);
-  return __funnelshift_r(a, b, (24 * t) & 31) & 0xFFFFFFu;
-}
-
-// Per-row dequant constants: sA/sB = scale broadcast for sub-blocks 2t / 2t+1, nA/nB = -1024 * scale,
-// negm = (-m(2t), -m(2t+1)) for the min mma.
-struct RowDq {
-  uint32_t sA, sB, nA, nB, negm;
-};
-
-__device__ __forceinline__ RowDq q4k_row(const uint4& r, int t) {
-  const uint32_t v = q4k_entries(r, t);
-  const uint32_t e0 = v & 0xFFFu, e1 = v >> 12;
-  const uint32_t scw = kMagic | (e0 & 63u) | ((e1 & 63u) << 16);
-  const uint32_t mw = kMagic | (e0 >> 6) | ((e1 >> 6) << 16);
-  const uint32_t d2 = lo_bcast(r.x), dm2 = hi_bcast(r.x);
-  const uint32_t S = hfma2u(scw, d2, hmul2u(d2, kHalfNeg1024x2));            // (d*sc_a, d*sc_b)
-  const uint32_t negdm2 = dm2 ^ 0x80008000u;
-  const uint32_t negM = hfma2u(mw, negdm2, hmul2u(negdm2, kHalfNeg1024x2));  // -(dmin*m_a), -(dmin*m_b)
-  RowDq o;
-  o.sA = lo_bcast(S);
-  o.sB = hi_bcast(S);
-  o.nA = hmul2u(o.sA, kHalfNeg1024x2);
-  o.nB = hmul2u(o.sB, kHalfNeg1024x2);
-  o.negm = negM;
-  return o;
-}
-
-__device__ __forceinline__ RowDq q80_row(uint32_t S) {
-  RowDq o;
-  o.sA = lo_bcast(S);
-  o.sB = hi_bcast(S);
-  o.nA = hmul2u(o.sA, kHalfNeg1024x2);
-  o.nB = hmul2u(o.sB, kHalfNeg1024x2);
-  o.negm = hmul2u(S, kHalfNeg128x2);  // the unsigned view adds 128 per byte: subtract 128*s*sum(x)
-  return o;
-}
-
-template <int NT>
-__device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const uint2* __restrict__ xf, int lane,
-                                          float (&acc)[NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
-  const RowDq dg = q4k_row(r.rg, t), dg8 = q4k_row(r.rg8, t);
-  negm_g = dg.negm;
-  negm_g8 = dg8.negm;
-#pragma unroll
-  for (int s = 0; s < 16; ++s) {
-    const uint4& qq = r.q[s / 4];
-    const uint32_t w = (s % 4 == 0) ? qq.x : (s % 4 == 1) ? qq.y : (s % 4 == 2) ? qq.z : qq.w;
-    const uint32_t w8 = w >> 8;
-    const uint32_t a0 = hfma2u((w & 0x000F000Fu) | kMagic, dg.sA, dg.nA);
-    const uint32_t a1 = hfma2u((w8 & 0x000F000Fu) | kMagic, dg8.sA, dg8.nA);
-    const uint32_t a2 = hfma2u((w & 0x00F000F0u) | kMagic, dg.sB, dg.nB);
-    const uint32_t a3 = hfma2u((w8 & 0x00F000F0u) | kMagic, dg8.sB, dg8.nB);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[nt], a0, a1, a2, a3, b.x, b.y);
-    }
-  }
-}
-
-template <int NT>
-__device__ __forceinline__ void tile_mmas(const RawQ80& r, int t, const uint2* __restrict__ xf, int lane,
-                                          float (&acc)[NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
-  const RowDq dg = q80_row(r.sg), dg8 = q80_row(r.sg8);
-  negm_g = dg.negm;
-  negm_g8 = dg8.negm;
-#pragma unroll
-  for (int s = 0; s < 16; ++s) {
-    const uint4& qq = r.q[2 * (s / 4) + (s % 4) / 2];
-    const uint32_t w0 = ((s % 2) == 0 ? qq.x : qq.z) ^ 0x80808080u;
-    const uint32_t w1 = ((s % 2) == 0 ? qq.y : qq.w) ^ 0x80808080u;
-    const uint32_t a0 = hfma2u(__byte_perm(w0, 0x64646464u, 0x4140), dg.sA, dg.nA);
-    const uint32_t a1 = hfma2u(__byte_perm(w0, 0x64646464u, 0x4342), dg8.sA, dg8.nA);
-    const uint32_t a2 = hfma2u(__byte_perm(w1, 0x64646464u, 0x4140), dg.sB, dg.nB);
-    const uint32_t a3 = hfma2u(__byte_perm(w1, 0x64646464u, 0x4342), dg8.sB, dg8.nB);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[nt], a0, a1, a2, a3, b.x, b.y);
-    }
-  }
-}
-
-// xs points at the CTA's staged sub-block sums, layout [pair][nt][lane].
-template <int NT>
-__device__ __forceinline__ void min_mma(float (&acc)[NT][4], uint32_t m0g, uint32_t m0g8, uint32_t m1g, uint32_t m1g8,
-                                        const uint4* __restrict__ xs, int pl, int lane) {
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint4 v = xs[(pl * NT + nt) * 32 + lane];
-    mma16816(acc[nt], m0g, m0g8, m1g, m1g8, v.x, v.y);
-    mma16816(acc[nt], m0g, m0g8, m1g, m1g8, v.z, v.w);
   }
 }
 
@@ -441,15 +296,15 @@ GemvPlan gemv_plan(const GemvShape& s, int q, int sm_count) {
   return p;
 }
 
-int launch_repack(const GemvShape& s, const uint8_t* d_src, uint8_t* d_tiles, cudaStream_t st) {
+int launch_repack(const GemvShape& s, const uint8_t* d_src, uint8_t* d_tiles, cudaStream_t st, uint32_t half_rows) {
   const uint64_t tiles = (uint64_t)s.ng * s.sb * kGemvWarps;
   const uint64_t items = tiles * (s.quant == CLM_QUANT_Q4_K ? 528 : 1152);
   const uint64_t blocks = ceil_div(items, 256);
   CLM_CHECK(blocks < (1ull << 31), CLM_RESOURCE_EXHAUSTED, "matrix too large to repack");
   if (s.quant == CLM_QUANT_Q4_K)
-    repack_q4k_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_src, d_tiles, s.rows, s.sb, s.ng);
+    repack_q4k_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_src, d_tiles, s.rows, s.sb, s.ng, half_rows);
   else
-    repack_q80_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_src, d_tiles, s.rows, s.sb, s.ng);
+    repack_q80_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_src, d_tiles, s.rows, s.sb, s.ng, half_rows);
   CLM_LAUNCHED("repack");
   return CLM_OK;
 }

@@ -98,7 +98,8 @@ GemvShape gemv_shape(int quant, uint32_t rows, uint32_t cols);
 GemvPlan gemv_plan(const GemvShape& s, int q, int sm_count);
 
 // Repack a GGUF-layout tensor (device memory) into the tiled layout (device memory, s.bytes()).
-int launch_repack(const GemvShape& s, const uint8_t* d_src, uint8_t* d_tiles, cudaStream_t st);
+// half_rows > 0 interleaves a stacked [gate; up] tensor of 2*half_rows rows in 64-row halves per 128-row group.
+int launch_repack(const GemvShape& s, const uint8_t* d_src, uint8_t* d_tiles, cudaStream_t st, uint32_t half_rows = 0);
 // fp32 activations x[q][cols] -> fragment-ordered fp16 (xfrag) and sub-block sums (xs).
 int launch_prep_x(const GemvShape& s, const GemvPlan& p, const float* d_x, int q, void* d_xfrag, void* d_xs,
                   cudaStream_t st);

@@ -1,0 +1,102 @@
+// gemv2.cuh — row-tile GEMV with bulk-copy weight streaming and fused epilogues (sm_100a).
+//
+// y[p][row] = W[row] . x[p] for q <= 16 window rows, W in GGUF Q4_K / Q8_0 repacked into 16-row x 256-column
+// tiles (the fragment-ordered tile format of gemv.cuh, stored row-tile-major: tile (rt, sb) at (rt*SB+sb)*TB).
+//
+//  * One CTA owns RPC (1 or 2) row tiles over the full K, so no split-K partials leave the CTA; its 8 consumer
+//    warps split the superblock pairs and reduce through shared memory in a fixed order (deterministic).
+//  * Each warp streams its tiles through a private ring of `nsw` shared-memory slots with cp.async.bulk
+//    (no multicast) completing on an mbarrier; the first `nsw` copies are issued before griddepcontrol.wait,
+//    so under programmatic dependent launch the weights of this layer stream in while the previous kernel
+//    finishes.  Every mbarrier wait is bounded; a timeout raises the engine's error flag.
+//  * Activations come from the producer kernel as fp16 fragments xfrag[sb][nt][16 s][32 lanes] (uint2) and
+//    f32 sub-block sums xsum[2 halves][sb*8 + j][16 p] (the Q4_K min / Q8_0 bias term).
+//  * Optional row scale 1/sqrt(mean(h^2) + eps) from per-CTA sum-of-squares partials: rmsnorm(h) * w is folded
+//    as (W . (h * w)) / denom, so no separate normalisation kernel runs between layers.
+//  * Epilogues: store; residual add + next-norm preparation; RoPE + paged KV append; SwiGLU + down preparation.
+#pragma once
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace clm {
+
+enum { EPI_STORE = 0, EPI_RESID_PREP = 1, EPI_ROPE_KV = 2, EPI_SWIGLU_PREP = 3 };
+
+// Activation hand-off between a producer and a consuming GEMV.
+struct XBuf {
+  uint2* frag = nullptr;   // [SB][nt][16 s][32 lanes]
+  float* sum = nullptr;    // [2][SB*8][16 p]
+  float* ss = nullptr;     // [nss][16 p] sum-of-squares partials (row scale), or null
+  int nss = 0;
+};
+
+struct Epi {
+  int kind = EPI_STORE;
+  // row scale: 1 / sqrtf(sum(ss) / ss_n + eps), from the input XBuf's ss partials
+  float ss_n = 0.0f, eps = 0.0f;
+  // EPI_STORE: out[p * out_ld + row]
+  float* out = nullptr;
+  long long out_ld = 0;
+  // EPI_RESID_PREP: h[p * H + row] += y; next input = h * wnext (fragments for a consumer with hi_scale)
+  float* h = nullptr;
+  int H = 0;
+  const float* wnext = nullptr;
+  XBuf next;
+  float hi_scale = 1.0f;
+  // EPI_ROPE_KV
+  int nh = 0, nkv = 0, hd = 0;
+  float theta = 0.0f;
+  const long long* pos = nullptr;
+  const int32_t* parent = nullptr;
+  const int32_t* pages = nullptr;
+  __half* kpool = nullptr;
+  __half* vpool = nullptr;
+  __half* q16 = nullptr;
+  // EPI_SWIGLU_PREP: rows of the CTA's first tile are gate rows, second tile the matching up rows
+  int ffn = 0;
+  int* err = nullptr;  // set to 1 if a bounded wait gave up
+};
+
+// The fused GEMV (gemv3.cu) over the group-major tile layout of gemv.cuh.  `part` holds ng*ksplit*q*128 f32
+// split partials and `counters` ng zero-initialised ints (left zero after every launch).
+size_t gemv3_smem(const GemvPlan& p);
+int launch_gemv3(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q, const Epi& epi,
+                 float* part, int* counters, cudaStream_t st);
+
+// Producer helpers.
+// x[q][cols] fp32 (row stride ld) times optional w[cols] -> fragments + sums (+ ss partials over 16-column
+// groups when with_ss).  Rows p in [q, 8*nt) are written as zeros.
+int launch_prep_rows(const float* d_x, long long ld, int q, int cols, const float* d_w, int nt, float hi_scale,
+                     const XBuf& out, bool with_ss, cudaStream_t st);
+// Bytes of the fragment / sum buffers for `cols` columns.
+inline size_t xfrag_bytes(int cols, int nt) { return (size_t)(cols / 256) * nt * 32 * 16 * sizeof(uint2); }
+inline size_t xsum_bytes(int cols) { return (size_t)2 * (cols / 32) * 16 * sizeof(float); }
+
+// Device helper shared by producers: writes the fragments / half sums of one 16-column group [16c, 16c+16)
+// of activation row p from `vals` (16 floats, already multiplied by the next norm's weight if any) and, when
+// ss_out is set, the sum of squares of `raw` (the values being normalised).  p >= q writes zeros.  One
+// thread per (group, p).
+__device__ __forceinline__ void prep16(const float* vals, const float* raw, int p, int q, int c, int nt,
+                                       float hi_scale, uint2* __restrict__ frag, float* __restrict__ xsum,
+                                       float* ss_out, int total_cols) {
+  const int k = 16 * c, sb = k / 256, o = k % 256, t = o / 64, part = (o % 64) / 32, s0 = (o % 32) / 2;
+  const int ntile = p / 8, g = p % 8;
+  // fragment layout [sb][nt][s][lane] (gemv.cuh): word (s, lane) at ((sb*nt + ntile)*16 + s)*32 + lane
+  uint32_t* w = reinterpret_cast<uint32_t*>(frag + ((size_t)sb * nt + ntile) * 512 + g * 4 + t);
+  float sum = 0.0f, ss = 0.0f;
+  const bool live = p < q;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = live ? vals[2 * i] : 0.0f, b = live ? vals[2 * i + 1] : 0.0f;
+    sum += a + b;
+    if (raw && live) ss += raw[2 * i] * raw[2 * i] + raw[2 * i + 1] * raw[2 * i + 1];
+    const float sa = part ? a * hi_scale : a, sbv = part ? b * hi_scale : b;
+    w[(s0 + i) * 64 + part] =
+        (uint32_t)__half_as_ushort(__float2half_rn(sa)) | ((uint32_t)__half_as_ushort(__float2half_rn(sbv)) << 16);
+  }
+  const int j = o / 32, half = (o % 32) / 16;
+  if (p < 16) xsum[((size_t)half * (total_cols / 32) + sb * 8 + j) * 16 + p] = sum;
+  if (ss_out && p < 16) ss_out[(size_t)c * 16 + p] = ss;
+}
+
+}  // namespace clm

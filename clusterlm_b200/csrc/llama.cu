@@ -1,6 +1,7 @@
 // llama.cu — per-layer kernels of the Llama-shaped decoder family (see llama.cuh).
 #include <cfloat>
 
+#include "gemv2.cuh"
 #include "llama.cuh"
 #include "pdl.cuh"
 
@@ -201,8 +202,12 @@ template <int HD>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const __half* __restrict__ q16, const __half* __restrict__ kpool, const __half* __restrict__ vpool,
     const int32_t* __restrict__ pages, const long long* __restrict__ d_pos, const int32_t* __restrict__ parent, int q,
-    int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part) {
+    int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
+    float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum) {
   static_assert(HD == 128, "head_dim 128 layout");
+  constexpr int RW = HD + 2;  // one partial row: O[HD], m, l
+  __shared__ float sp[kAttnWarps][16][RW];
+  __shared__ int s_last;
   griddep_wait();
   griddep_launch();
   const int kvh = blockIdx.x, mt = blockIdx.z;
@@ -212,113 +217,180 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
   const long long base = *d_pos;
   const long long nvis = base + q;
   const int npages = (int)((nvis + kPageTokens - 1) / kPageTokens);
-  if (pg >= npages || pg >= max_pages) return;
-  const int32_t page = pages[pg];
+  const int ngroups = (npages + kAttnWarps - 1) / kAttnWarps;
   const int r0 = mt * 16 + g, r1 = r0 + 8;
   const int i0 = r0 / group, i1 = r1 / group;
   const bool v0 = i0 < q, v1 = i1 < q;
+  const bool active = pg < npages && pg < max_pages;
 
-  // Q fragments: thread t holds head dims [32t, 32t+32) of rows r0 and r1.
-  uint4 qw0[4], qw1[4];
-  {
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    const uint4* a = reinterpret_cast<const uint4*>(q16 + ((size_t)i0 * nh + kvh * group + r0 % group) * HD + 32 * t);
-    const uint4* b = reinterpret_cast<const uint4*>(q16 + ((size_t)i1 * nh + kvh * group + r1 % group) * HD + 32 * t);
+  if (active) {
+    const int32_t page = pages[pg];
+    // Q fragments: thread t holds head dims [32t, 32t+32) of rows r0 and r1.
+    uint4 qw0[4], qw1[4];
+    {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      const uint4* a = reinterpret_cast<const uint4*>(q16 + ((size_t)i0 * nh + kvh * group + r0 % group) * HD + 32 * t);
+      const uint4* b = reinterpret_cast<const uint4*>(q16 + ((size_t)i1 * nh + kvh * group + r1 % group) * HD + 32 * t);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      qw0[j] = v0 ? a[j] : z;
-      qw1[j] = v1 ? b[j] : z;
+      for (int j = 0; j < 4; ++j) {
+        qw0[j] = v0 ? a[j] : z;
+        qw1[j] = v1 ? b[j] : z;
+      }
     }
-  }
-
-  // S = Q K^T over the 64 positions of the page; n-tile j column c <-> position 16*(c/2) + 2j + c%2.
-  const __half* kpage = kpool + ((size_t)page * nkv + kvh) * kPageTokens * HD;
-  float S[8][4];
+    // S = Q K^T over the 64 positions of the page; n-tile j column c <-> position 16*(c/2) + 2j + c%2.
+    const __half* kpage = kpool + ((size_t)page * nkv + kvh) * kPageTokens * HD;
+    float S[8][4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
-    const int pos = 16 * (g / 2) + 2 * j + (g % 2);
-    const uint4* kr = reinterpret_cast<const uint4*>(kpage + (size_t)pos * HD + 32 * t);
-    uint4 kw[4];
+    for (int j = 0; j < 8; ++j) {
+      S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+      const int pos = 16 * (g / 2) + 2 * j + (g % 2);
+      const uint4* kr = reinterpret_cast<const uint4*>(kpage + (size_t)pos * HD + 32 * t);
+      uint4 kw[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) kw[u] = kr[u];
+      for (int u = 0; u < 4; ++u) kw[u] = kr[u];
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks)
-      mma_f16(S[j], word_of(qw0, 2 * ks), word_of(qw1, 2 * ks), word_of(qw0, 2 * ks + 1), word_of(qw1, 2 * ks + 1),
-              word_of(kw, 2 * ks), word_of(kw, 2 * ks + 1));
-  }
-
-  // masked row maxima (log2 domain)
-  float m0 = -INFINITY, m1 = -INFINITY;
+      for (int ks = 0; ks < 8; ++ks)
+        mma_f16(S[j], word_of(qw0, 2 * ks), word_of(qw1, 2 * ks), word_of(qw0, 2 * ks + 1), word_of(qw1, 2 * ks + 1),
+                word_of(kw, 2 * ks), word_of(kw, 2 * ks + 1));
+    }
+    float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 8; ++j)
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const long long pos = (long long)pg * kPageTokens + 16 * t + 2 * j + e;
-      S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
-      S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
-      m0 = fmaxf(m0, S[j][e]);
-      m1 = fmaxf(m1, S[j][2 + e]);
+      for (int e = 0; e < 2; ++e) {
+        const long long pos = (long long)pg * kPageTokens + 16 * t + 2 * j + e;
+        S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
+        S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
+        m0 = fmaxf(m0, S[j][e]);
+        m1 = fmaxf(m1, S[j][2 + e]);
+      }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    float l0 = 0.0f, l1 = 0.0f;
+    uint32_t pa[8][2];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float p00 = m0 == -INFINITY ? 0.0f : exp2f(S[j][0] - m0);
+      const float p01 = m0 == -INFINITY ? 0.0f : exp2f(S[j][1] - m0);
+      const float p10 = m1 == -INFINITY ? 0.0f : exp2f(S[j][2] - m1);
+      const float p11 = m1 == -INFINITY ? 0.0f : exp2f(S[j][3] - m1);
+      l0 += p00 + p01;
+      l1 += p10 + p11;
+      pa[j][0] = pack_half2(p00, p01);
+      pa[j][1] = pack_half2(p10, p11);
     }
 #pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
-  }
-  float l0 = 0.0f, l1 = 0.0f;
-  uint32_t pa[8][2];  // P as fp16 pairs: [n-tile][row r0 / r1]
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float p00 = m0 == -INFINITY ? 0.0f : exp2f(S[j][0] - m0);
-    const float p01 = m0 == -INFINITY ? 0.0f : exp2f(S[j][1] - m0);
-    const float p10 = m1 == -INFINITY ? 0.0f : exp2f(S[j][2] - m1);
-    const float p11 = m1 == -INFINITY ? 0.0f : exp2f(S[j][3] - m1);
-    l0 += p00 + p01;
-    l1 += p10 + p11;
-    pa[j][0] = pack_half2(p00, p01);
-    pa[j][1] = pack_half2(p10, p11);
-  }
-#pragma unroll
-  for (int o = 1; o <= 2; o <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-  }
-
-  // O = P V; V^T page rows are head dims, n-tile jn covers dims 8jn..8jn+7, k-step kk positions 16t+4kk+{0..3}.
-  const __half* vpage = vpool + ((size_t)page * nkv + kvh) * HD * kPageTokens;
-  float* out = part + (((size_t)mt * nkv + kvh) * max_pages + pg) * 16 * (HD + 2);
+    for (int o = 1; o <= 2; o <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    const __half* vpage = vpool + ((size_t)page * nkv + kvh) * HD * kPageTokens;
 #pragma unroll 4
-  for (int jn = 0; jn < HD / 8; ++jn) {
-    float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    const uint4* vr = reinterpret_cast<const uint4*>(vpage + (size_t)(8 * jn + g) * kPageTokens + 16 * t);
-    const uint4 va = vr[0], vb = vr[1];
-    const uint32_t vw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
+    for (int jn = 0; jn < HD / 8; ++jn) {
+      float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint4* vr = reinterpret_cast<const uint4*>(vpage + (size_t)(8 * jn + g) * kPageTokens + 16 * t);
+      const uint4 va = vr[0], vb = vr[1];
+      const uint32_t vw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      mma_f16(O, pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1], vw[2 * kk], vw[2 * kk + 1]);
-    out[(size_t)g * (HD + 2) + 8 * jn + 2 * t] = O[0];
-    out[(size_t)g * (HD + 2) + 8 * jn + 2 * t + 1] = O[1];
-    out[(size_t)(g + 8) * (HD + 2) + 8 * jn + 2 * t] = O[2];
-    out[(size_t)(g + 8) * (HD + 2) + 8 * jn + 2 * t + 1] = O[3];
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16(O, pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1], vw[2 * kk], vw[2 * kk + 1]);
+      sp[warp][g][8 * jn + 2 * t] = O[0];
+      sp[warp][g][8 * jn + 2 * t + 1] = O[1];
+      sp[warp][g + 8][8 * jn + 2 * t] = O[2];
+      sp[warp][g + 8][8 * jn + 2 * t + 1] = O[3];
+    }
+    if (t == 0) {
+      sp[warp][g][HD] = m0;
+      sp[warp][g][HD + 1] = l0;
+      sp[warp][g + 8][HD] = m1;
+      sp[warp][g + 8][HD + 1] = l1;
+    }
+  } else {
+    for (int i = lane; i < 16; i += 32) {
+      sp[warp][i][HD] = -INFINITY;
+      sp[warp][i][HD + 1] = 0.0f;
+    }
   }
-  if (t == 0) {
-    out[(size_t)g * (HD + 2) + HD] = m0;
-    out[(size_t)g * (HD + 2) + HD + 1] = l0;
-    out[(size_t)(g + 8) * (HD + 2) + HD] = m1;
-    out[(size_t)(g + 8) * (HD + 2) + HD + 1] = l1;
+  __syncthreads();
+  // combine the CTA's pages into one partial per (m-tile, kv head, page group)
+  float* mine = part + (((size_t)mt * nkv + kvh) * max_pages + blockIdx.y) * 16 * RW;
+  if ((int)blockIdx.y < ngroups) {
+    for (int i = threadIdx.x; i < 16 * RW; i += blockDim.x) {
+      const int r = i / RW, c = i % RW;
+      float M = -INFINITY;
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sp[w][r][HD]);
+      float a = 0.0f;
+      if (c == HD) {
+        a = M;
+      } else {
+        for (int w = 0; w < kAttnWarps; ++w) {
+          const float m = sp[w][r][HD];
+          if (m == -INFINITY) continue;
+          a += sp[w][r][c] * exp2f(m - M);
+        }
+      }
+      mine[i] = a;
+    }
+  }
+  // the last CTA of this (m-tile, kv head) combines the page groups and writes W_o's input fragments
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&counters[mt * nkv + kvh], 1) == (int)gridDim.y - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* allp = part + ((size_t)mt * nkv + kvh) * max_pages * 16 * RW;
+  __shared__ float o_s[16][HD];
+  __shared__ float wmax[16], wsum[16];
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x;
+    float M = -INFINITY;
+    for (int gi = 0; gi < ngroups; ++gi) M = fmaxf(M, __ldcg(allp + ((size_t)gi * 16 + r) * RW + HD));
+    float L = 0.0f;
+    for (int gi = 0; gi < ngroups; ++gi) {
+      const float m = __ldcg(allp + ((size_t)gi * 16 + r) * RW + HD);
+      if (m != -INFINITY) L += __ldcg(allp + ((size_t)gi * 16 + r) * RW + HD + 1) * exp2f(m - M);
+    }
+    wmax[r] = M;
+    wsum[r] = L > 0.0f ? 1.0f / L : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    float a = 0.0f;
+    for (int gi = 0; gi < ngroups; ++gi) {
+      const float m = __ldcg(allp + ((size_t)gi * 16 + r) * RW + HD);
+      if (m != -INFINITY) a += __ldcg(allp + ((size_t)gi * 16 + r) * RW + c) * exp2f(m - wmax[r]);
+    }
+    o_s[r][c] = a * wsum[r];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) counters[mt * nkv + kvh] = 0;
+  // fragments: query vector r = window row i, head kvh*group + r%group; 8 column groups of 16 per head
+  const int qd = nh * HD;
+  for (int it = threadIdx.x; it < 16 * (HD / 16); it += blockDim.x) {
+    const int r = it / (HD / 16), gg = it % (HD / 16);
+    const int i = (mt * 16 + r) / group, head = kvh * group + (mt * 16 + r) % group;
+    if (i >= q) continue;
+    prep16(&o_s[r][16 * gg], nullptr, i, q, (head * HD + 16 * gg) / 16, nt_out, hi_scale, out_frag, out_sum, nullptr,
+           qd);
   }
 }
 
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
-                     float* d_part, cudaStream_t st) {
+                     float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
+                     cudaStream_t st) {
   CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
   const int group = d.nh / d.nkv;
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
   return launch_pdl(attention_kernel<128>, dim3(d.nkv, (max_pages + kAttnWarps - 1) / kAttnWarps, mtiles),
                     dim3(32 * kAttnWarps), 0, st, d_q, d_k, d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2,
-                    max_pages, d_part);
+                    max_pages, d_part, d_counters, nt_out, hi_scale, static_cast<uint2*>(d_frag), d_sum);
 }
 
 // ---------------------------------------------------------------------------------------------------

@@ -29,9 +29,13 @@ int launch_norm(const float* d_part, int nsplit, int part_rows, int q, int H, co
 int launch_rope_kv(const float* d_part, int nsplit, int q, const LlamaDims& d, const long long* d_pos,
                    const int32_t* d_parent, const int32_t* d_pages, __half* d_k, __half* d_v, __half* d_q,
                    cudaStream_t st);
+// Paged split-KV attention for q window rows; CTAs combine their 4 pages, and the last CTA of each
+// (m-tile, kv head) combines all page groups and writes W_o's input fragments (out_frag / out_sum, qd columns).
+// d_part holds mtiles*nkv*max_pages*16*(hd+2) floats; d_counters mtiles*nkv zeroed ints.
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
-                     float* d_part, cudaStream_t st);
+                     float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
+                     cudaStream_t st);
 int launch_attn_combine(const float* d_part, const long long* d_pos, int q, const LlamaDims& d, int max_pages, int nt,
                         float hi_scale, void* d_xfrag, void* d_xs, cudaStream_t st);
 // a = silu(gate) * up from the gate|up GEMV partials (rows 2F) -> fragments for the down GEMV.

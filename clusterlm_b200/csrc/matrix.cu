@@ -4,6 +4,7 @@
 
 #include "codec.cuh"
 #include "gemv.cuh"
+#include "gemv2.cuh"
 #include "matrix.cuh"
 
 namespace clm {
@@ -41,7 +42,7 @@ int launch_gemv_f32(const float* d_w, uint32_t rows, uint32_t cols, const float*
 }
 
 int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_src, uint64_t nbytes, uint32_t rows,
-                  uint32_t cols, clm_b200_matrix** out) {
+                  uint32_t cols, clm_b200_matrix** out, uint32_t half_rows) {
   CLM_TRY(ctx_enter(ctx));
   CLM_CHECK(out != nullptr, CLM_INVALID_ARGUMENT, "null output");
   *out = nullptr;
@@ -86,7 +87,7 @@ int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_s
         status = cuda_fail(e, "cudaMalloc(matrix tiles)");
         break;
       }
-      status = launch_repack(m->shape, static_cast<const uint8_t*>(src), static_cast<uint8_t*>(m->data), st);
+      status = launch_repack(m->shape, static_cast<const uint8_t*>(src), static_cast<uint8_t*>(m->data), st, half_rows);
     } else {
       m->bytes = (uint64_t)rows * cols * 4;
       cudaError_t e = cudaMalloc(&m->data, m->bytes);
@@ -113,18 +114,26 @@ int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_s
 int matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, int q, float* d_y, cudaStream_t st) {
   if (w->quant == CLM_QUANT_F32 || w->quant == CLM_QUANT_Q8_FIXTURE)
     return launch_gemv_f32(static_cast<const float*>(w->data), w->rows, w->cols, d_x, q, d_y, st);
-  const GemvPlan p = gemv_plan(w->shape, q, ctx->sm_count);
-  const uint64_t part_bytes = p.ksplit > 1 ? (uint64_t)p.ksplit * q * w->rows * 4 : 0;
+  const GemvShape& s = w->shape;
+  const GemvPlan p = gemv_plan(s, q, ctx->sm_count);
+  const size_t fb = xfrag_bytes((int)s.cols, p.nt), sb = xsum_bytes((int)s.cols);
+  const size_t pb = (size_t)s.ng * p.ksplit * q * 128 * sizeof(float), cb = (size_t)s.ng * sizeof(int);
   void* scratch = nullptr;
-  CLM_TRY(ctx_scratch(ctx, p.xfrag_bytes + p.xs_bytes + part_bytes + 256, &scratch));
+  CLM_TRY(ctx_scratch(ctx, fb + sb + pb + cb + 1024, &scratch));
   uint8_t* base = static_cast<uint8_t*>(scratch);
-  void* xfrag = base;
-  void* xs = base + p.xfrag_bytes;
-  float* part = reinterpret_cast<float*>(base + p.xfrag_bytes + p.xs_bytes);
-  CLM_TRY(launch_prep_x(w->shape, p, d_x, q, xfrag, xs, st));
-  CLM_TRY(launch_gemv(w->shape, p, static_cast<const uint8_t*>(w->data), xfrag, xs, q, p.ksplit > 1 ? part : d_y, st));
-  if (p.ksplit > 1) CLM_TRY(launch_reduce_splits(part, p.ksplit, q, w->rows, d_y, st));
-  return CLM_OK;
+  XBuf in;
+  in.frag = reinterpret_cast<uint2*>(base);
+  in.sum = reinterpret_cast<float*>(base + fb);
+  float* part = reinterpret_cast<float*>(base + fb + sb);
+  int* counters = reinterpret_cast<int*>(base + fb + sb + pb);
+  CLM_CUDA(cudaMemsetAsync(counters, 0, cb, st));
+  const float hi = w->quant == CLM_QUANT_Q4_K ? 0.0625f : 1.0f;
+  CLM_TRY(launch_prep_rows(d_x, s.cols, q, (int)s.cols, nullptr, p.nt, hi, in, false, st));
+  Epi e;
+  e.kind = EPI_STORE;
+  e.out = d_y;
+  e.out_ld = s.rows;
+  return launch_gemv3(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
 }
 
 }  // namespace clm

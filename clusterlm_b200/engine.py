@@ -64,6 +64,36 @@ def _f32(a):
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+class _FixGeometry(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("n_layers", "hidden", "residual_streams", "n_experts", "n_active_experts",
+                                          "expert_ff", "shared_expert_ff", "n_heads", "n_kv_heads", "head_dim",
+                                          "vocab", "ple_layer", "ple_ngram", "ple_rows")] + [("layer_kinds", _vp)]
+
+
+@dataclass
+class FixtureGeometry:
+    """ModelGeometry of the clusterlm-fixture family (runtime/objects/include/clusterlm/objects/geometry.hpp)."""
+    n_layers: int
+    hidden: int
+    residual_streams: int
+    n_experts: int
+    n_active_experts: int
+    expert_ff: int
+    shared_expert_ff: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    ple_layer: int
+    ple_ngram: int
+    ple_rows: int
+    layer_kinds: tuple
+
+    @property
+    def floats_per_position(self) -> int:
+        return self.residual_streams * self.hidden + self.hidden + self.residual_streams
+
+
 class Engine:
     def __init__(self, ctx, geometry: LlamaGeometry, layer_begin: int, layer_end: int, role: int,
                  max_context: int, max_window: int, max_sessions: int = 1):
@@ -74,6 +104,8 @@ class Engine:
         h = _vp()
         call("clm_b200_llama_create", ctx.h, C.byref(self._g), C.byref(self._s), C.byref(h))
         self.h = h
+        self.fpp = 2 * geometry.hidden + 1
+        self.vocab = geometry.vocab
 
     def close(self):
         if self.h:
@@ -119,8 +151,8 @@ class Engine:
         return v.value
 
     def run_window(self, session: int, base: int, tokens=None, records=None):
-        """Returns logits (q, vocab) for tail/whole stages, records (q, 2H+1) otherwise."""
-        fpp = 2 * self.geo.hidden + 1
+        """Returns logits (q, vocab) for tail/whole stages, records (q, floats_per_position) otherwise."""
+        fpp = self.fpp
         if tokens is not None:
             tokens = _i32(tokens)
             q = tokens.size
@@ -128,7 +160,7 @@ class Engine:
             records = _f32(records)
             q = records.shape[0]
         has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
-        out = np.zeros((q, self.geo.vocab if has_head else fpp), np.float32)
+        out = np.zeros((q, self.vocab if has_head else fpp), np.float32)
         call("clm_b200_run_window", self.h, session, base, q,
              None if tokens is None else tokens.ctypes.data_as(_vp),
              None if records is None else records.ctypes.data_as(_vp),
@@ -154,7 +186,7 @@ class Engine:
     def mtp_draft(self, prev: int, count: int, temperature: float = 0.0, seed: int = 0, counter: int = 0,
                   want_logits: bool = False):
         toks = np.zeros(count, np.int32)
-        logits = np.zeros((count, self.geo.vocab), np.float32) if want_logits else None
+        logits = np.zeros((count, self.vocab), np.float32) if want_logits else None
         call("clm_b200_mtp_draft", self.h, prev, count, temperature, seed, counter, toks.ctypes.data_as(_vp),
              None if logits is None else logits.ctypes.data_as(_vp))
         return (toks, logits) if want_logits else toks
@@ -177,3 +209,27 @@ class Engine:
         call("clm_b200_spec_round_device", self.h, session, C.byref(p),
              None if d_tokens is None else _vp(d_tokens.data_ptr()),
              None if d_count is None else _vp(d_count.data_ptr()), stream)
+
+
+class FixtureEngine(Engine):
+    """A stage of the clusterlm-fixture family (the reference's own model) on the device."""
+
+    def __init__(self, ctx, geometry: FixtureGeometry, layer_begin: int, layer_end: int, role: int,
+                 max_context: int, max_window: int, max_sessions: int = 1):
+        self.ctx, self.geo, self.role = ctx, geometry, role
+        self.max_window = max_window
+        self._kinds = np.ascontiguousarray(np.asarray(geometry.layer_kinds, np.uint8))
+        g = geometry
+        self._g = _FixGeometry(g.n_layers, g.hidden, g.residual_streams, g.n_experts, g.n_active_experts,
+                               g.expert_ff, g.shared_expert_ff, g.n_heads, g.n_kv_heads, g.head_dim, g.vocab,
+                               g.ple_layer, g.ple_ngram, g.ple_rows, self._kinds.ctypes.data_as(_vp))
+        self._s = _Spec(layer_begin, layer_end, role, max_context, max_window, max_sessions)
+        h = _vp()
+        call("clm_b200_fixture_create", ctx.h, C.byref(self._g), C.byref(self._s), C.byref(h))
+        self.h = h
+        self.fpp = geometry.floats_per_position
+        self.vocab = geometry.vocab
+
+    def set_object(self, name: str, quant: str, data) -> None:
+        buf = np.ascontiguousarray(data, np.uint8)
+        call("clm_b200_engine_set_object", self.h, name.encode(), QUANTS[quant], buf.ctypes.data_as(_vp), buf.nbytes)

@@ -227,6 +227,25 @@ CLM_API int clm_b200_spec_round(clm_b200_engine* e, uint64_t session, const clm_
 CLM_API int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
                                        int32_t* d_tokens, uint32_t* d_count, void* stream);
 
+/* ---- clusterlm-fixture family: the reference's own model (hc gated residual streams, 3:1 recurrent /
+ * attention layers without RoPE, top-K MoE with a shared SwiGLU expert, PLE n-gram lookup, injection gates;
+ * runtime/domain/src/reference_domain.cpp:452-585).  Computed in f32 with the reference's ascending
+ * reduction order and no FMA contraction. */
+typedef struct {
+  uint32_t n_layers, hidden, residual_streams, n_experts, n_active_experts, expert_ff, shared_expert_ff;
+  uint32_t n_heads, n_kv_heads, head_dim, vocab, ple_layer, ple_ngram, ple_rows;
+  const uint8_t* layer_kinds; /* n_layers entries: 0 recurrent, 1 full attention (geometry.hpp:16-19) */
+} clm_b200_fixture_geometry;
+
+CLM_API int clm_b200_fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* geometry,
+                                    const clm_b200_stage_spec* spec, clm_b200_engine** out);
+/* Binds one provisioned object by its manifest name ("blk.L.dense", "blk.L.shared", "blk.L.exp.E",
+ * "token_embd", "ple_lookup", "output_head", "mtp_drafter"; runtime/objects/src/manifest.cpp:214-218) in its
+ * stored representation (f32 or q8_0-fixture), decoded exactly on the device as the reference does at
+ * prepare (reference_domain.cpp:191-245).  CLM_DATA_LOSS when the size does not match the geometry. */
+CLM_API int clm_b200_engine_set_object(clm_b200_engine* e, const char* name, int quant, const void* h_bytes,
+                                       uint64_t nbytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -239,6 +239,14 @@ class Reference:
                                          C.c_uint32, _i32p]
         L.ref_write_fixture.restype = C.c_int
         L.ref_write_fixture.argtypes = [C.c_char_p, C.c_int, C.c_uint32, C.c_uint64]
+        L.ref_store_open.restype = C.c_void_p
+        L.ref_store_open.argtypes = [C.c_char_p]
+        L.ref_store_close.argtypes = [C.c_void_p]
+        L.ref_store_object.restype = C.c_int
+        L.ref_store_object.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_uint64, C.POINTER(C.c_int),
+                                       C.POINTER(C.c_uint64)]
+        L.ref_store_geometry.restype = C.c_int
+        L.ref_store_geometry.argtypes = [C.c_void_p, _u32p, _u8p, C.c_uint32]
         L.ref_pipeline_create.restype = C.c_void_p
         L.ref_pipeline_create.argtypes = [C.c_char_p, _u32p, C.c_uint32, C.c_uint32, C.c_uint32]
         L.ref_pipeline_destroy.argtypes = [C.c_void_p]
@@ -312,6 +320,40 @@ class Reference:
     def write_fixture(self, d: str, tiny: bool = False, layers: int = 0, seed: int = 0x434C4D31) -> None:
         if self.L.ref_write_fixture(d.encode(), int(tiny), layers, seed):
             raise RuntimeError(self.err())
+
+
+class ModelStore:
+    """The reference's CanonicalModelStore over a fixture model directory: geometry and object bytes."""
+
+    NAMES = {0: "f32", 1: "q8_0-fixture", 2: "q8_0"}
+
+    def __init__(self, ref: Reference, model_dir: str):
+        self.ref = ref
+        self.h = ref.L.ref_store_open(model_dir.encode())
+        if not self.h:
+            raise RuntimeError(ref.err())
+        dims = np.zeros(15, np.uint32)
+        kinds = np.zeros(1024, np.uint8)
+        ref.L.ref_store_geometry(self.h, dims, kinds, kinds.size)
+        keys = ["n_layers", "hidden", "residual_streams", "n_experts", "n_active_experts", "expert_ff",
+                "shared_expert_ff", "n_heads", "n_kv_heads", "head_dim", "vocab", "ple_layer", "ple_ngram",
+                "ple_rows", "mtp_layers"]
+        self.geometry = {k: int(v) for k, v in zip(keys, dims)}
+        self.layer_kinds = kinds[: self.geometry["n_layers"]].copy()
+
+    def object(self, name: str):
+        """(quant name, bytes) of a provisioned object."""
+        q, n = C.c_int(), C.c_uint64()
+        if self.ref.L.ref_store_object(self.h, name.encode(), None, 0, C.byref(q), C.byref(n)):
+            raise KeyError(self.ref.err())
+        buf = np.zeros(n.value, np.uint8)
+        self.ref.L.ref_store_object(self.h, name.encode(), buf.ctypes.data, buf.size, C.byref(q), C.byref(n))
+        return self.NAMES[q.value], buf
+
+    def close(self):
+        if self.h:
+            self.ref.L.ref_store_close(self.h)
+            self.h = None
 
 
 class RefPipeline:

@@ -132,6 +132,40 @@ int ref_write_fixture(const char* dir, int tiny, std::uint32_t layers, std::uint
   return m.is_ok() ? 0 : fail(m.status());
 }
 
+// ---- canonical model store: object bytes by manifest name (runtime/objects/src/canonical_store.cpp)
+void* ref_store_open(const char* dir) {
+  auto st = objects::CanonicalModelStore::open(dir);
+  if (!st.is_ok()) {
+    fail(st.status());
+    return nullptr;
+  }
+  return std::move(st).value().release();
+}
+void ref_store_close(void* h) { delete static_cast<objects::CanonicalModelStore*>(h); }
+// quant: 0 f32, 1 q8_0-fixture, 2 q8_0, -1 other.  Returns 0 and the byte count; copies when cap suffices.
+int ref_store_object(void* h, const char* name, std::uint8_t* buf, std::uint64_t cap, int* quant,
+                     std::uint64_t* nbytes) {
+  auto* s = static_cast<objects::CanonicalModelStore*>(h);
+  auto p = s->resolve(name);
+  if (!p.is_ok()) return fail(p.status());
+  const std::string& qt = p->entry->representation.quant_type;
+  *quant = qt == "f32" ? 0 : qt == "q8_0-fixture" ? 1 : qt == "q8_0" ? 2 : -1;
+  *nbytes = p->bytes.size();
+  if (buf && cap >= p->bytes.size()) std::memcpy(buf, p->bytes.data(), p->bytes.size());
+  return 0;
+}
+// geometry: 15 u32 fields then layer kinds (n_layers bytes)
+int ref_store_geometry(void* h, std::uint32_t* dims, std::uint8_t* kinds, std::uint32_t kinds_cap) {
+  auto* s = static_cast<objects::CanonicalModelStore*>(h);
+  const auto& g = s->manifest().geometry;
+  const std::uint32_t v[15] = {g.n_layers, g.hidden_size, g.residual_streams, g.n_experts, g.n_active_experts,
+                               g.expert_ff, g.shared_expert_ff, g.n_heads, g.n_kv_heads, g.head_dim,
+                               g.vocab_size, g.ple_layer, g.ple_ngram, g.ple_rows, g.mtp_layers};
+  std::memcpy(dims, v, sizeof v);
+  for (std::uint32_t i = 0; i < g.n_layers && i < kinds_cap; ++i) kinds[i] = static_cast<std::uint8_t>(g.layer_kinds[i]);
+  return 0;
+}
+
 // ---- in-process pipeline over ReferenceDomain (the pattern of tests/domain/pipeline_harness.hpp) ----
 struct RefPipeline {
   std::unique_ptr<objects::CanonicalModelStore> store;
