@@ -20,6 +20,7 @@ With N > 1 (torchrun) every rank runs an independent replica on its own GPU (wea
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -252,15 +253,16 @@ def run_b200(args, world, rank, local):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
-    geo = LLAMA3_8B
+    geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
+    context = args.context
     ctx = Context(local)
-    max_ctx = CONTEXT + (args.warmup + args.steps + 8) * (Q + 1) + 64
+    max_ctx = context + (args.warmup + args.steps + 8) * (Q + 1) + 64
     eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, 16, 1)
     eng.generate_weights(seed=SEED, stddev=0.02)
     eng.prepare()
     eng.open_session(1)
     rng = np.random.default_rng(1234 + rank)
-    prompt = rng.integers(0, geo.vocab, CONTEXT).astype(np.int32)
+    prompt = rng.integers(0, geo.vocab, context).astype(np.int32)
     t0 = time.perf_counter()
     eng.spec_begin(1, prompt, Q, temperature=TEMPERATURE, seed=SEED)
     prefill_s = time.perf_counter() - t0
@@ -301,7 +303,7 @@ def run_b200(args, world, rank, local):
     e2e_value = sum_over_ranks(world, e_emitted, dev) / e2e_s
 
     # verify-window roofline: one q = 4 window through the public window call, event-timed
-    total_b, weight_b, kv_b = window_bytes(geo, CONTEXT)
+    total_b, weight_b, kv_b = window_bytes(geo, context)
     pos = eng.position(1)
     wt = []
     wtoks = torch.from_numpy(rng.integers(0, geo.vocab, Q).astype(np.int32)).to(dev)
@@ -326,7 +328,8 @@ def run_b200(args, world, rank, local):
     if rank != 0:
         return
     cpu = None
-    if world == 1 and not args.no_cpu:
+    profile = args.layers != LLAMA3_8B.n_layers or context != CONTEXT
+    if world == 1 and not args.no_cpu and not profile:
         cb = CpuBaseline(os.cpu_count() or 1)
         r = cb.round_s()
         cpu = {"value": (emitted / args.steps) / r, "cores": cb.threads, "sample": cb.sample_text(emitted / args.steps)}
@@ -335,15 +338,17 @@ def run_b200(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
         "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
-        "config": {"workload": "llama3-8b-shape q4_k spec decode q=4 ctx=4096 batch=1 mtp=1-layer T=1",
-                   "q": Q, "context": CONTEXT, "temperature": TEMPERATURE,
+        "config": {"workload": (f"llama3-8b-shape q4_k spec decode q=4 ctx={context} batch=1 mtp=1-layer T=1"
+                                + (f" PROFILE CASE ({geo.n_layers} layers)" if profile else "")),
+                   "q": Q, "context": context, "temperature": TEMPERATURE,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2 (4.8 GB weights streamed per round)",
                    "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted / args.steps},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": (Q + 1) * 4 + 4},
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_kind": peak_kind, "kernel": "verify window q=4 (32 layers + head)",
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"verify window q=4 ({geo.n_layers} layers + head)",
                      "algorithmic_bytes": total_b, "weight_bytes": weight_b, "kv_bytes": kv_b,
                      "window_ms": window_s * 1e3},
         "clocks": clk,
@@ -361,6 +366,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    # smaller cases for profiler captures (the line is then marked PROFILE CASE and is not a bench result)
+    ap.add_argument("--context", type=int, default=CONTEXT, help="prefilled context (profiling)")
+    ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()

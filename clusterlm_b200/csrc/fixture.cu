@@ -38,6 +38,7 @@ struct FixLayerS {  // sequence state of one local layer for one session (device
 struct FixParams {
   int H, hc, E, K, ff, sff, nh, nkv, hd, V, ple_layer, ngram, ple_rows;
   int nlayers, layer_begin, max_context;
+  int score_ld;  // max_context + 1: a row of attention scores plus the stashed softmax sum
   int q;
   long long base;
   int has_tokens, has_head;
@@ -65,7 +66,7 @@ __device__ __forceinline__ uint64_t mix64d(uint64_t z) {
 }
 
 // One stage window.  `rec_io` holds the q boundary records (in: from the previous stage or zero + embedding;
-// out: this stage's records).  scratch: [q][nh][max_context] attention scores.
+// out: this stage's records).  scratch: [q][nh][max_context + 1] attention scores (+ softmax sum).
 __global__ void __launch_bounds__(256) fixture_window_kernel(FixParams P, const FixLayerW* __restrict__ W,
                                                              const FixLayerS* __restrict__ S,
                                                              const float* __restrict__ embd,
@@ -198,14 +199,14 @@ __global__ void __launch_bounds__(256) fixture_window_kernel(FixParams P, const 
           const int head = (int)(i / npos);
           const long long tt = i % npos;
           const float* kt = ls.kc + (size_t)tt * kvd + (head / group) * P.hd;
-          scores[((size_t)p * P.nh + head) * P.max_context + tt] = dotf(t + p * qd + head * P.hd, kt, P.hd) * scale;
+          scores[((size_t)p * P.nh + head) * P.score_ld + tt] = dotf(t + p * qd + head * P.hd, kt, P.hd) * scale;
         }
       }
       __syncthreads();
       // per (p, head): max, exp, ascending sum (one thread each)
       for (int i = tid; i < q * P.nh; i += nt) {
         const int p = i / P.nh;
-        float* sc = scores + (size_t)i * P.max_context;
+        float* sc = scores + (size_t)i * P.score_ld;
         const long long npos = P.base + p + 1;
         float mx = 0.0f;
         for (long long tt = 0; tt < npos; ++tt)
@@ -215,14 +216,13 @@ __global__ void __launch_bounds__(256) fixture_window_kernel(FixParams P, const 
           sc[tt] = fexp(sc[tt] - mx);
           sum += sc[tt];
         }
-        denom[0] = 0.0f;  // (unused slot; keeps the compiler from hoisting)
-        sc[P.max_context - 1] = sum;  // stash the sum in the last slot (npos <= max_context - 1 guaranteed)
+        sc[P.score_ld - 1] = sum;  // stash the sum past the row (npos <= max_context)
       }
       __syncthreads();
       for (int i = tid; i < q * qd; i += nt) {
         const int p = i / qd, hd_i = i % qd, head = hd_i / P.hd, dd = hd_i % P.hd;
-        const float* sc = scores + ((size_t)p * P.nh + head) * P.max_context;
-        const float sum = sc[P.max_context - 1];
+        const float* sc = scores + ((size_t)p * P.nh + head) * P.score_ld;
+        const float sum = sc[P.score_ld - 1];
         const long long npos = P.base + p + 1;
         float acc = 0.0f;
         for (long long tt = 0; tt < npos; ++tt) {
@@ -309,6 +309,8 @@ __global__ void __launch_bounds__(256) fixture_window_kernel(FixParams P, const 
     __syncthreads();
   }
 
+  // this stage's output records (a tail's run_window returns them too, reference_domain.cpp:408-427)
+  for (int i = tid; i < q * fpp; i += nt) rec_io[i] = rec[i];
   if (P.has_head) {
     // head_position (reference_domain.cpp:577-585): fold a copy of the streams, mean, rmsnorm(head_norm), logits
     for (int i = tid; i < q * H; i += nt) {
@@ -328,8 +330,6 @@ __global__ void __launch_bounds__(256) fixture_window_kernel(FixParams P, const 
     for (int i = tid; i < q * H; i += nt) x[i] = u[i] * head_norm[i % H] / denom[i / H];
     __syncthreads();
     for (int i = tid; i < q * P.V; i += nt) logits[i] = dotf(head_w + (size_t)(i % P.V) * H, x + (i / P.V) * H, H);
-  } else {
-    for (int i = tid; i < q * fpp; i += nt) rec_io[i] = rec[i];
   }
 }
 
@@ -448,7 +448,7 @@ int fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* g, const 
             "fixture engine supports E <= 64, H <= 1024, K <= 16");
   CLM_CHECK(spec->layer_end <= g->n_layers && spec->layer_begin <= spec->layer_end, CLM_INVALID_ARGUMENT,
             "layer range outside the model");
-  CLM_CHECK(spec->max_context >= 2 && spec->max_window >= 1 && spec->max_sessions >= 1 &&
+  CLM_CHECK(spec->max_context >= 1 && spec->max_window >= 1 && spec->max_sessions >= 1 &&
                 spec->max_window <= spec->max_context && spec->max_window <= 16,
             CLM_INVALID_ARGUMENT, "domain spec needs max_context >= max_window >= 1, max_window <= 16");
   // role rules (reference_domain.cpp:67-85)
@@ -502,6 +502,7 @@ int fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* g, const 
   P.nlayers = (int)(spec->layer_end - spec->layer_begin);
   P.layer_begin = (int)spec->layer_begin;
   P.max_context = (int)spec->max_context;
+  P.score_ld = P.max_context + 1;
   P.has_tokens = e->has_tokens();
   P.has_head = e->has_head();
   const int H = P.H, qd = P.nh * P.hd, kvd = P.nkv * P.hd;
@@ -602,7 +603,7 @@ int fixture_prepare(FixtureEngine* e) {
   CLM_TRY(e->alloc((void**)&e->rec_io, (size_t)W * fpp * sizeof(float)));
   CLM_TRY(e->alloc((void**)&e->tokens, (size_t)(W + 1) * sizeof(int32_t)));
   CLM_TRY(e->alloc((void**)&e->prev, sizeof(int32_t)));
-  CLM_TRY(e->alloc((void**)&e->scores, (size_t)W * P.nh * P.max_context * sizeof(float)));
+  CLM_TRY(e->alloc((void**)&e->scores, (size_t)W * P.nh * P.score_ld * sizeof(float)));
   if (e->has_head()) CLM_TRY(e->alloc((void**)&e->logits, (size_t)W * P.V * sizeof(float)));
   if (e->obj("mtp_drafter")) CLM_TRY(e->alloc((void**)&e->mtp_logits, (size_t)W * P.V * sizeof(float)));
   const int qd = P.nh * P.hd, kvd = P.nkv * P.hd, ffmax = std::max(P.ff, P.sff);
@@ -690,7 +691,7 @@ int fixture_run_window(FixtureEngine* e, uint64_t id, uint64_t base, uint32_t q,
   CLM_CHECK(s.outstanding == 0, CLM_FAILED_PRECONDITION, "a window is already outstanding for this session");
   CLM_CHECK(q >= 1, CLM_INVALID_ARGUMENT, "window must have at least one position");
   CLM_CHECK(q <= e->spec.max_window, CLM_RESOURCE_EXHAUSTED, "window exceeds max_window");
-  CLM_CHECK(base + q + 1 <= e->spec.max_context, CLM_RESOURCE_EXHAUSTED, "window exceeds max_context");
+  CLM_CHECK(base + q <= e->spec.max_context, CLM_RESOURCE_EXHAUSTED, "window exceeds max_context");
   CLM_CHECK((long long)base == s.pos, CLM_FAILED_PRECONDITION, "window base position != committed position");
   cudaStream_t st = device ? pick_stream(e->ctx, stream) : e->ctx->stream;
   const cudaMemcpyKind h2d = device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -709,6 +710,7 @@ int fixture_run_window(FixtureEngine* e, uint64_t id, uint64_t base, uint32_t q,
   FixParams P = e->P;
   P.q = (int)q;
   P.base = (long long)base;
+  P.has_head = e->has_head() && logits != nullptr;  // a tail's run_window without the head returns records only
   const unsigned long long l0 = t_kernel_launches;
   CLM_TRY(launch_pdl(fixture_window_kernel, dim3(1), dim3(256), e->smem, st, P, (const FixLayerW*)e->d_w,
                      (const FixLayerS*)s.d_layers, (const float*)e->obj("token_embd"),
@@ -717,11 +719,8 @@ int fixture_run_window(FixtureEngine* e, uint64_t id, uint64_t base, uint32_t q,
                      e->has_head() ? (const float*)e->obj("output_head") + P.H : nullptr, (const int32_t*)e->tokens,
                      (const int32_t*)s.history, e->rec_io, e->logits, e->scores));
   e->last_launches = t_kernel_launches - l0;
-  if (e->has_head()) {
-    if (logits) CLM_CUDA(cudaMemcpyAsync(logits, e->logits, (size_t)q * P.V * sizeof(float), d2h, st));
-  } else if (out) {
-    CLM_CUDA(cudaMemcpyAsync(out, e->rec_io, rec, d2h, st));
-  }
+  if (P.has_head) CLM_CUDA(cudaMemcpyAsync(logits, e->logits, (size_t)q * P.V * sizeof(float), d2h, st));
+  if (out) CLM_CUDA(cudaMemcpyAsync(out, e->rec_io, rec, d2h, st));
   if (!device) CLM_CUDA(cudaStreamSynchronize(st));
   s.outstanding = q;
   return CLM_OK;

@@ -28,11 +28,12 @@ QUANTS = {"f32": 0, "q8_0-fixture": 1, "q8_0": 2, "q4_k": 3}
 
 
 def build(reference_root: str | None = None) -> None:
-    """Compile liboracle.so, and _ref/libclm_ref.so when the reference sources are present."""
+    """Compile liboracle.so, and (when the reference sources are present) _ref/libclm_ref.so and the
+    drop-in parity driver _ref/backend_parity (needs libclm_b200.so built first)."""
     targets = ["oracle"]
     root = reference_root or os.environ.get("CLM_REFERENCE_ROOT", "/root/reference")
     if os.path.isdir(os.path.join(root, "runtime", "domain")):
-        targets.append("ref")
+        targets += ["ref", "parity"]
     subprocess.run(["make", "-s", "-C", HERE, f"REFERENCE_ROOT={root}", "-j8", *targets], check=True)
 
 
