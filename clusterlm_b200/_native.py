@@ -52,6 +52,7 @@ _SIGS = {
     "clm_b200_matrix_free": (_i, [_vp]),
     "clm_b200_matrix_info": (_i, [_vp, C.POINTER(_i), C.POINTER(_u32), C.POINTER(_u32), C.POINTER(_u64)]),
     "clm_b200_matmul_rows": (_i, [_vp, _vp, _vp, _u32, _vp, _vp]),
+    "clm_b200_matmul_rows_static": (_i, [_vp, _vp, _vp, _u32, _vp, _vp]),
     "clm_b200_argmax_rows": (_i, [_vp, _vp, _u32, _u32, _vp, _vp]),
     "clm_b200_distribution_rows": (_i, [_vp, _vp, _u32, _u32, _f, _u32, _f, _vp, _vp]),
     "clm_b200_sample_rows": (_i, [_vp, _vp, _u32, _u32, _vp, _vp, _vp]),

@@ -100,6 +100,17 @@ CLM_API int clm_b200_matrix_info(const clm_b200_matrix* m, int* quant, uint32_t*
  * 1 <= positions <= 16.  fp16 tensor-core products with f32 accumulation for Q4_K / Q8_0; f32 for f32. */
 CLM_API int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, uint32_t positions,
                          float* d_y, void* stream);
+/* The same product with all of its scratch in a fixed CLM_B200_STATIC_SCRATCH_BYTES device array compiled into
+ * the library: the call allocates no device memory (clm_b200_matmul_rows may grow the context's scratch with
+ * cudaMalloc).  No reference counterpart: the reference's CPU matmul needs no device scratch.  For callers
+ * that must not allocate once admitted, e.g. a domain whose device memory is fully leased at prepare.
+ * CLM_RESOURCE_EXHAUSTED when the matrix/positions need more scratch than the array holds (then use
+ * clm_b200_matmul_rows); CLM_OUT_OF_RANGE for more than 524,288 rows.  One array per device: calls whose kernels
+ * overlap on one device race on it, so serialise them per device.  The first call on a device resolves the
+ * array's address (set-up); make it before any stream capture meant to contain later calls. */
+#define CLM_B200_STATIC_SCRATCH_BYTES (8u << 20)
+CLM_API int clm_b200_matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x,
+                                        uint32_t positions, float* d_y, void* stream);
 
 /* ---- sampling and speculative acceptance (runtime/domain/src/sampling.cpp:44-131) --------------- */
 /* argmax per row, ties to the lowest index (sampling.cpp:44-49). */
