@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "codec.cuh"
+#include "bulk.cuh"
 #include "engine.cuh"
 #include "gemv.cuh"
 #include "gemv2.cuh"
@@ -64,9 +65,18 @@ __global__ void round_head_kernel(const SessionState* __restrict__ st, int32_t* 
   if (threadIdx.x == 0) win[0] = st->next_token;
 }
 
-__global__ void greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
-                                     const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
-                                     int32_t* __restrict__ nxt);
+// Greedy acceptance (coordinator.cpp:1295-1298) from the window's row argmaxes: accepted = longest prefix with
+// argmax(logits[i]) == window[i+1]; next = argmax(logits[accepted]).
+__global__ void greedy_decide_kernel(const int32_t* __restrict__ am, int q, const int32_t* __restrict__ win,
+                                     uint32_t* __restrict__ acc, int32_t* __restrict__ nxt) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x != 0) return;
+  uint32_t a = 0;
+  while ((int)a + 1 < q && am[a] == win[a + 1]) ++a;
+  *acc = a;
+  *nxt = am[a];
+}
 
 // Emits win[1..a] and the next token, advances the session (commit of a+1 positions).
 __global__ void round_commit_kernel(SessionState* __restrict__ st, const int32_t* __restrict__ win,
@@ -147,8 +157,10 @@ struct LlamaEngine : clm_b200_engine {
   float* h_mtp = nullptr;
   float* draft_logits = nullptr;
   int32_t* win = nullptr;
-  float* stats_mx = nullptr;
-  double* stats_kept = nullptr;
+  float* tprobs = nullptr;    // distribution rows of the window's logits [W][V]
+  float* dprobs = nullptr;    // distribution rows of the MTP drafts [W][V]
+  int32_t* am = nullptr;      // row argmaxes [W]
+  SampleScratch samp;         // chunked sampling scratch (2W rows, 1 sequence)
   uint32_t* acc = nullptr;
   int32_t* nxt = nullptr;
   int32_t* emitted = nullptr;
@@ -195,7 +207,7 @@ struct LlamaEngine : clm_b200_engine {
   // ---- one fused GEMV of the chain
   int gemv(const Gemv& g, int q, const XBuf& in, const Epi& epi, cudaStream_t st) {
     const GemvPlan& p = g.for_q(q);
-    return launch_gemv3(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), in, q, epi, part, gcount, st);
+    return launch_gemv(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), in, q, epi, part, gcount, st);
   }
   Epi epi_base(int kind) const {
     Epi e;
@@ -235,7 +247,7 @@ struct LlamaEngine : clm_b200_engine {
       CLM_TRY(gemv(L.qkv, q, xa, ek, st));
       // attention -> xb (W_o input)
       CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, nullptr, q, d, max_pages, attn_part, acount,
-                               nt, hi_scale(), xb.frag, xb.sum, st));
+                               nt, hi_scale(), xb.frag, xb.sum, bad, st));
       XBuf ob = xb;
       ob.ss = nullptr;
       // h += W_o o ; xa = h * ffn_norm (+ sum of squares)
@@ -302,22 +314,32 @@ struct LlamaEngine : clm_b200_engine {
     CLM_TRY(launch_pdl(round_head_kernel, dim3(1), dim3(32), 0, st, (const SessionState*)s.d_state, win));
     for (int j = 0; j + 1 < q; ++j) {
       CLM_TRY(enqueue_mtp_step(win + j, draft_logits + (size_t)j * d.V, st));
-      CLM_TRY(launch_sample_logits(draft_logits + (size_t)j * d.V, d.V, 0.0f, 0, (uint32_t)j, 1u, ctr, win + j + 1, st,
-                                   ctl));
+      CLM_TRY(sample_token(draft_logits + (size_t)j * d.V, stochastic, 1.0f, 0, (uint32_t)j, 1u, ctr, ctl,
+                           dprobs + (size_t)j * d.V, win + j + 1, st));
     }
     CLM_TRY(enqueue_window(s, q, win, st));
     if (stochastic) {
-      CLM_TRY(launch_row_stats(logits, q, d.V, 1.0f, stats_mx, stats_kept, st, ctl));
-      if (q > 1) CLM_TRY(launch_row_stats(draft_logits, q - 1, d.V, 1.0f, stats_mx + q, stats_kept + q, st, ctl));
-      CLM_TRY(launch_accept_logits(logits, q > 1 ? draft_logits : nullptr, win + 1, 1, q - 1, d.V, 1.0f, stats_mx,
-                                   stats_kept, nullptr, 0, 0, ctr, acc, nxt, st, ctl));
+      CLM_TRY(launch_probs(logits, q, d.V, 1.0f, ctl, tprobs, samp, st));
+      CLM_TRY(launch_accept(tprobs, q > 1 ? dprobs : nullptr, win + 1, 1, q - 1, d.V, nullptr, 0, 0, ctr, ctl, acc,
+                            nxt, samp, st));
     } else {
-      CLM_TRY(launch_pdl(greedy_accept_kernel, dim3(1), dim3(1024), 0, st, (const float*)logits, (uint32_t)d.V, q,
-                         (const int32_t*)win, acc, nxt));
+      CLM_TRY(launch_argmax_rows(logits, q, d.V, am, samp, st));
+      CLM_TRY(launch_pdl(greedy_decide_kernel, dim3(1), dim3(32), 0, st, (const int32_t*)am, q, (const int32_t*)win,
+                         acc, nxt));
     }
     CLM_TRY(launch_pdl(round_commit_kernel, dim3(1), dim3(32), 0, st, s.d_state, (const int32_t*)win,
                        (const uint32_t*)acc, (const int32_t*)nxt, emitted, count));
     return CLM_OK;
+  }
+
+  // One token from one logits row: argmax, or sample_from(distribution(row, T)) with the Philox uniform
+  // (draw, stream, *ctr) under the seed (ctl's when given); the distribution row goes to probs_row.
+  int sample_token(const float* row, bool stochastic, float T, uint64_t seed, uint32_t draw, uint32_t stream,
+                   const unsigned long long* ctr, const RoundCtl* rctl, float* probs_row, int32_t* out,
+                   cudaStream_t st) {
+    if (!stochastic) return launch_argmax_rows(row, 1, d.V, out, samp, st);
+    CLM_TRY(launch_probs(row, 1, d.V, T, rctl, probs_row, samp, st));
+    return launch_sample_rows(probs_row, 1, d.V, d.V, nullptr, seed, draw, stream, ctr, rctl, out, samp, st);
   }
 
   // Runs `enq` for (kind, q, flag) as a CUDA graph: eager on first use, captured on the second, replayed after.
@@ -362,6 +384,7 @@ struct LlamaEngine : clm_b200_engine {
     CLM_CUDA(cudaStreamSynchronize(st));
     if (b) {
       CLM_CUDA(cudaMemset(bad, 0, sizeof(int)));
+      if (b == kErrWaitTimeout) return fail(CLM_DEADLINE_EXCEEDED, "a bounded device wait gave up (copy never completed)");
       return fail(CLM_INVALID_ARGUMENT, "token outside the vocabulary");
     }
     return CLM_OK;
@@ -399,80 +422,6 @@ struct LlamaEngine : clm_b200_engine {
     for (void* p : allocations) cudaFree(p);
   }
 };
-
-namespace clm {
-
-__global__ void greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
-                                     const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
-                                     int32_t* __restrict__ nxt);
-
-}  // namespace clm
-
-// greedy acceptance (coordinator.cpp:1295-1298): longest prefix with argmax(logits[i]) == window[i+1]
-__device__ int32_t engine_block_argmax(const float* __restrict__ l, uint32_t vocab) {
-  __shared__ float sv[32];
-  __shared__ int32_t si[32];
-  __shared__ int32_t s_res;
-  float best = -INFINITY;
-  int32_t bi = INT32_MAX;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = l[i];
-    if (v > best || (v == best && (int32_t)i < bi)) {
-      best = v;
-      bi = (int32_t)i;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
-  }
-  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-  if (lane == 0) {
-    sv[warp] = best;
-    si[warp] = bi;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
-    bi = lane < (int)(blockDim.x / 32) ? si[lane] : INT32_MAX;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) {
-        best = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) s_res = (isnan(l[0]) || bi == INT32_MAX) ? 0 : bi;
-  }
-  __syncthreads();
-  const int32_t r = s_res;
-  __syncthreads();
-  return r;
-}
-
-__global__ void clm::greedy_accept_kernel(const float* __restrict__ logits, uint32_t vocab, int q,
-                                          const int32_t* __restrict__ win, uint32_t* __restrict__ acc,
-                                          int32_t* __restrict__ nxt) {
-  griddep_wait();
-  griddep_launch();
-  __shared__ int32_t am[64];
-  for (int i = 0; i < q; ++i) {
-    const int32_t a = engine_block_argmax(logits + (size_t)i * vocab, vocab);
-    if (threadIdx.x == 0) am[i] = a;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t a = 0;
-    while ((int)a + 1 < q && am[a] == win[a + 1]) ++a;
-    *acc = a;
-    *nxt = am[a];
-  }
-}
 
 namespace {
 
@@ -657,8 +606,16 @@ int llama_prepare(LlamaEngine* e) {
     CLM_TRY(e->alloc_t(&e->draft_logits, (size_t)W * d.V));
   }
   CLM_TRY(e->alloc_t(&e->win, (size_t)W + 1));
-  CLM_TRY(e->alloc_t(&e->stats_mx, (size_t)2 * W));
-  CLM_TRY(e->alloc_t(&e->stats_kept, (size_t)2 * W));
+  if (e->has_head) {
+    CLM_TRY(e->alloc_t(&e->tprobs, (size_t)W * d.V));
+    CLM_TRY(e->alloc_t(&e->dprobs, (size_t)W * d.V));
+    CLM_TRY(e->alloc_t(&e->am, (size_t)W));
+    void* sbase = nullptr;
+    const size_t sbytes = SampleScratch::bytes(2 * W, 1, d.V);
+    CLM_TRY(e->alloc(&sbase, sbytes));
+    e->samp = SampleScratch::carve(sbase, 2 * W, 1, d.V);
+    CLM_CUDA(cudaMemset(sbase, 0, e->samp.counter_bytes));
+  }
   CLM_TRY(e->alloc_t(&e->acc, 1));
   CLM_TRY(e->alloc_t(&e->nxt, 1));
   CLM_TRY(e->alloc_t(&e->emitted, (size_t)W + 1));
@@ -811,7 +768,7 @@ int llama_commit(LlamaEngine* e, uint64_t id, uint32_t accepted) {
   CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
   CLM_CHECK(s->outstanding > 0, CLM_FAILED_PRECONDITION, "no outstanding window");
   CLM_CHECK(accepted >= 1 && accepted <= s->outstanding, CLM_INVALID_ARGUMENT, "accepted must be in [1, q]");
-  if (e->has_tokens) {
+  {
     const int rc = e->check_bad(e->ctx->stream);
     if (rc != CLM_OK) {
       s->outstanding = 0;  // the window is dropped, as the ledger's fail_window does
@@ -856,8 +813,8 @@ int llama_mtp_draft(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint6
   CLM_CUDA(cudaMemcpyAsync(e->win, &prev, sizeof(int32_t), cudaMemcpyHostToDevice, st));
   for (uint32_t j = 0; j < count; ++j) {
     CLM_TRY(e->enqueue_mtp_step(e->win + j, e->draft_logits + (size_t)j * e->d.V, st));
-    CLM_TRY(launch_sample_logits(e->draft_logits + (size_t)j * e->d.V, e->d.V, T, seed, j, 1u, e->zero_counter,
-                                 e->win + j + 1, st, nullptr));
+    CLM_TRY(e->sample_token(e->draft_logits + (size_t)j * e->d.V, T > 0.0f, T, seed, j, 1u, e->zero_counter, nullptr,
+                            e->dprobs + (size_t)j * e->d.V, e->win + j + 1, st));
   }
   CLM_CUDA(cudaMemcpyAsync(h_tokens, e->win + 1, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   if (h_logits)
@@ -887,8 +844,8 @@ int llama_spec_begin(LlamaEngine* e, uint64_t id, const int32_t* h_prompt, uint3
   // first token from the last prompt position (argmax, or a sample with Philox draw (0, stream 2, 0))
   cudaStream_t st = e->ctx->stream;
   const uint32_t last = (n - 1) % e->spec.max_window;
-  CLM_TRY(launch_sample_logits(e->logits + (size_t)last * e->d.V, e->d.V, p->temperature, p->seed, 0u, 2u,
-                               e->zero_counter, e->nxt, st, nullptr));
+  CLM_TRY(e->sample_token(e->logits + (size_t)last * e->d.V, p->temperature > 0.0f, p->temperature, p->seed, 0u, 2u,
+                          e->zero_counter, nullptr, e->tprobs, e->nxt, st));
   CLM_TRY(launch_pdl(set_next_kernel, dim3(1), dim3(32), 0, st, s->d_state, (const int32_t*)e->nxt));
   CLM_CUDA(cudaStreamSynchronize(st));
   return CLM_OK;

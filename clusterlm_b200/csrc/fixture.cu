@@ -381,7 +381,8 @@ struct FixtureEngine : clm_b200_engine {
   std::vector<void*> allocations;
   uint64_t weight_bytes = 0;
   FixLayerW* d_w = nullptr;
-  float *rec_io = nullptr, *logits = nullptr, *scores = nullptr, *mtp_logits = nullptr;
+  float *rec_io = nullptr, *logits = nullptr, *scores = nullptr, *mtp_logits = nullptr, *mtp_probs = nullptr;
+  SampleScratch samp;  // chunked sampling scratch of the MTP drafter (1 row, 1 sequence)
   int32_t *tokens = nullptr, *prev = nullptr;
   std::map<uint64_t, std::unique_ptr<FixSession>> sessions;
   size_t smem = 0;
@@ -605,7 +606,14 @@ int fixture_prepare(FixtureEngine* e) {
   CLM_TRY(e->alloc((void**)&e->prev, sizeof(int32_t)));
   CLM_TRY(e->alloc((void**)&e->scores, (size_t)W * P.nh * P.score_ld * sizeof(float)));
   if (e->has_head()) CLM_TRY(e->alloc((void**)&e->logits, (size_t)W * P.V * sizeof(float)));
-  if (e->obj("mtp_drafter")) CLM_TRY(e->alloc((void**)&e->mtp_logits, (size_t)W * P.V * sizeof(float)));
+  if (e->obj("mtp_drafter")) {
+    CLM_TRY(e->alloc((void**)&e->mtp_logits, (size_t)W * P.V * sizeof(float)));
+    CLM_TRY(e->alloc((void**)&e->mtp_probs, (size_t)P.V * sizeof(float)));
+    void* sbase = nullptr;
+    CLM_TRY(e->alloc(&sbase, SampleScratch::bytes(1, 1, (uint32_t)P.V)));
+    e->samp = SampleScratch::carve(sbase, 1, 1, (uint32_t)P.V);
+    CLM_CUDA(cudaMemset(sbase, 0, e->samp.counter_bytes));
+  }
   const int qd = P.nh * P.hd, kvd = P.nkv * P.hd, ffmax = std::max(P.ff, P.sff);
   const size_t floats = (size_t)W * fpp + (size_t)W * P.H * 7 + (size_t)W * std::max(P.H, qd) + (size_t)W * 2 * kvd +
                         (size_t)W * qd + (size_t)W * 3 * ffmax + (size_t)W * P.E + (size_t)W * P.K + W;
@@ -782,8 +790,17 @@ int fixture_mtp_draft(FixtureEngine* e, int32_t prev, uint32_t count, float T, u
   for (uint32_t j = 0; j < count && rc == CLM_OK; ++j) {
     rc = launch_pdl(fixture_mtp_kernel, dim3(1), dim3(256), 0, st, (const float*)e->obj("token_embd"), mtp, mtp + P.H,
                     P.H, P.V, (const int32_t*)(e->tokens + j), e->mtp_logits + (size_t)j * P.V);
-    if (rc == CLM_OK)
-      rc = launch_sample_logits(e->mtp_logits + (size_t)j * P.V, P.V, T, seed, j, 1u, ctr, e->tokens + j + 1, st, nullptr);
+    if (rc == CLM_OK) {
+      const float* row = e->mtp_logits + (size_t)j * P.V;
+      if (T > 0.0f) {
+        rc = launch_probs(row, 1, (uint32_t)P.V, T, nullptr, e->mtp_probs, e->samp, st);
+        if (rc == CLM_OK)
+          rc = launch_sample_rows(e->mtp_probs, 1, (uint64_t)P.V, (uint32_t)P.V, nullptr, seed, j, 1u, ctr, nullptr,
+                                  e->tokens + j + 1, e->samp, st);
+      } else {
+        rc = launch_argmax_rows(row, 1, (uint32_t)P.V, e->tokens + j + 1, e->samp, st);
+      }
+    }
   }
   if (rc == CLM_OK) {
     cudaMemcpyAsync(h_tokens, e->tokens + 1, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st);

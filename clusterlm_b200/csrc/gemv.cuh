@@ -15,7 +15,7 @@
 //    fragments of those k are pre-scaled by 1/16, so no extra shift is needed.
 //  * The Q4_K min (and the +128 bias of the unsigned Q8_0 view) is one extra mma per tile pair:
 //    A = -m[row][sub-block], B = per-sub-block activation sums split into fp16 hi + lo.
-//  * Activations are staged once per CTA in shared memory in fragment order (one LDS.64 per mma).
+//  * Activations reach the consumer warps through shared memory in fragment order (one LDS.64 per mma).
 #pragma once
 #include "common.cuh"
 
@@ -26,6 +26,7 @@ constexpr int kQ80TileBytes = 4352;  // 4096 B int8 + 16 rows x 8 half scales
 constexpr int kGemvWarps = 8;        // row tiles per row group / warps per CTA
 constexpr int kXfragSbBytes = 16 * 32 * 8;  // one superblock of B fragments for one n8 column tile
 constexpr int kXsPairBytes = 32 * 16;       // one superblock pair of sub-block sums (hi, lo) per column tile
+constexpr size_t kGemvSmemBudget = 210 * 1024;  // dynamic shared memory of one persistent GEMV CTA
 
 struct GemvShape {
   int quant = 0;
@@ -39,14 +40,16 @@ struct GemvShape {
 
 struct GemvPlan {
   int nt = 1;        // n8 column tiles (1: q <= 8, 2: q <= 16)
-  int ksplit = 1;    // CTAs along k per row group
-  int sbps = 0;      // superblocks per split (even)
+  int grid = 0;      // persistent CTAs (one per SM)
+  int stages = 0;    // shared-memory ring stages per CTA
+  int ksplit = 1;    // partial slots per row group (the most CTA ranges one group can span)
   size_t smem = 0;   // dynamic shared memory bytes
   uint64_t xfrag_bytes = 0, xs_bytes = 0;
 };
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  return (uint32_t)__half_as_ushort(__float2half_rn(lo)) | ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+  const __half2 h = __floats2half2_rn(lo, hi);  // one paired conversion, lo in the low half
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 // Writes activation row p (x[cols] in shared memory, fp32) in the GEMV's fragment order:
@@ -100,13 +103,4 @@ GemvPlan gemv_plan(const GemvShape& s, int q, int sm_count);
 // Repack a GGUF-layout tensor (device memory) into the tiled layout (device memory, s.bytes()).
 // half_rows > 0 interleaves a stacked [gate; up] tensor of 2*half_rows rows in 64-row halves per 128-row group.
 int launch_repack(const GemvShape& s, const uint8_t* d_src, uint8_t* d_tiles, cudaStream_t st, uint32_t half_rows = 0);
-// fp32 activations x[q][cols] -> fragment-ordered fp16 (xfrag) and sub-block sums (xs).
-int launch_prep_x(const GemvShape& s, const GemvPlan& p, const float* d_x, int q, void* d_xfrag, void* d_xs,
-                  cudaStream_t st);
-// Partial (ksplit > 1) or final (ksplit == 1) outputs: out[ks][q][rows].
-int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const void* d_xfrag, const void* d_xs,
-                int q, float* d_out, cudaStream_t st);
-// y[p][i] = sum over ks of part[ks][p][i] (fixed order).
-int launch_reduce_splits(const float* d_part, int ksplit, int q, uint32_t rows, float* d_y, cudaStream_t st);
-
 }  // namespace clm

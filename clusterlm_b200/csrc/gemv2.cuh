@@ -1,18 +1,12 @@
-// gemv2.cuh — row-tile GEMV with bulk-copy weight streaming and fused epilogues (sm_100a).
+// gemv2.cuh — activation hand-off and fused epilogues of the q-row GEMV chain (kernel in gemv4.cu).
 //
-// y[p][row] = W[row] . x[p] for q <= 16 window rows, W in GGUF Q4_K / Q8_0 repacked into 16-row x 256-column
-// tiles (the fragment-ordered tile format of gemv.cuh, stored row-tile-major: tile (rt, sb) at (rt*SB+sb)*TB).
+// y[p][row] = W[row] . x[p] for q <= 16 window rows, W in GGUF Q4_K / Q8_0 repacked into the group-major tile
+// layout of gemv.cuh.
 //
-//  * One CTA owns RPC (1 or 2) row tiles over the full K, so no split-K partials leave the CTA; its 8 consumer
-//    warps split the superblock pairs and reduce through shared memory in a fixed order (deterministic).
-//  * Each warp streams its tiles through a private ring of `nsw` shared-memory slots with cp.async.bulk
-//    (no multicast) completing on an mbarrier; the first `nsw` copies are issued before griddepcontrol.wait,
-//    so under programmatic dependent launch the weights of this layer stream in while the previous kernel
-//    finishes.  Every mbarrier wait is bounded; a timeout raises the engine's error flag.
-//  * Activations come from the producer kernel as fp16 fragments xfrag[sb][nt][16 s][32 lanes] (uint2) and
-//    f32 sub-block sums xsum[2 halves][sb*8 + j][16 p] (the Q4_K min / Q8_0 bias term).
-//  * Optional row scale 1/sqrt(mean(h^2) + eps) from per-CTA sum-of-squares partials: rmsnorm(h) * w is folded
-//    as (W . (h * w)) / denom, so no separate normalisation kernel runs between layers.
+//  * Activations come from the producer kernel as fp16 fragments xfrag[sb][nt][16 s][32 lanes] (uint2) and f32
+//    sub-block sums xsum[2 halves][sb*8 + j][16 p] (the Q4_K min / Q8_0 bias term), written by prep16 below.
+//  * Optional row scale 1/sqrt(mean(h^2) + eps) from sum-of-squares partials: rmsnorm(h) * w is folded as
+//    (W . (h * w)) / denom, so no separate normalisation kernel runs between layers.
 //  * Epilogues: store; residual add + next-norm preparation; RoPE + paged KV append; SwiGLU + down preparation.
 #pragma once
 #include "common.cuh"
@@ -57,11 +51,10 @@ struct Epi {
   int* err = nullptr;  // set to 1 if a bounded wait gave up
 };
 
-// The fused GEMV (gemv3.cu) over the group-major tile layout of gemv.cuh.  `part` holds ng*ksplit*q*128 f32
-// split partials and `counters` ng zero-initialised ints (left zero after every launch).
-size_t gemv3_smem(const GemvPlan& p);
-int launch_gemv3(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q, const Epi& epi,
-                 float* part, int* counters, cudaStream_t st);
+// The fused GEMV (gemv4.cu) over the group-major tile layout of gemv.cuh.  `part` holds ng*p.ksplit*q*128 f32
+// segment partials and `counters` ng zero-initialised ints (left zero after every launch).
+int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q, const Epi& epi,
+                float* part, int* counters, cudaStream_t st);
 
 // Producer helpers.
 // x[q][cols] fp32 (row stride ld) times optional w[cols] -> fragments + sums (+ ss partials over 16-column

@@ -64,6 +64,27 @@ static __device__ __forceinline__ void load_raw(RawQ80& r, const uint8_t* tile, 
   r.sg8 = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * t));
 }
 
+// Raw tile image from shared memory (the bulk-copied k-chunk); same lane mapping as load_raw.
+static __device__ __forceinline__ void load_raw_s(RawQ4k& r, const uint8_t* tile, int lane) {
+  const uint4* p = reinterpret_cast<const uint4*>(tile);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) r.q[j] = p[j * 32 + lane];
+  const int g = lane / 4;
+  r.rg = *reinterpret_cast<const uint4*>(tile + 2048 + 16 * g);
+  r.rg8 = *reinterpret_cast<const uint4*>(tile + 2048 + 16 * (g + 8));
+}
+static __device__ __forceinline__ void load_raw_s(RawQ80& r, const uint8_t* tile, int lane) {
+  const uint4* p = reinterpret_cast<const uint4*>(tile);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    r.q[2 * j] = p[j * 64 + lane * 2];
+    r.q[2 * j + 1] = p[j * 64 + lane * 2 + 1];
+  }
+  const int g = lane / 4, t = lane % 4;
+  r.sg = *reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * g + 4 * t);
+  r.sg8 = *reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * t);
+}
+
 static __device__ __forceinline__ uint32_t q4k_entries(const uint4& r, int t) {
   const uint32_t a = t < 2 ? r.y : (t == 2 ? r.z : r.w);
   const uint32_t b = t < 2 ? r.z : (t == 2 ? r.w : 0u);
@@ -104,9 +125,10 @@ static __device__ __forceinline__ RowDq q80_row(uint32_t S) {
   return o;
 }
 
+// acc[s & 1]: even and odd k-steps accumulate into separate registers, two independent mma chains.
 template <int NT>
 static __device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const uint2* __restrict__ xf, int lane,
-                                          float (&acc)[NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
+                                          float (&acc)[2][NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
   const RowDq dg = q4k_row(r.rg, t), dg8 = q4k_row(r.rg8, t);
   negm_g = dg.negm;
   negm_g8 = dg8.negm;
@@ -122,14 +144,14 @@ static __device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const u
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[nt], a0, a1, a2, a3, b.x, b.y);
+      mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
     }
   }
 }
 
 template <int NT>
 static __device__ __forceinline__ void tile_mmas(const RawQ80& r, int t, const uint2* __restrict__ xf, int lane,
-                                          float (&acc)[NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
+                                          float (&acc)[2][NT][4], uint32_t& negm_g, uint32_t& negm_g8) {
   const RowDq dg = q80_row(r.sg), dg8 = q80_row(r.sg8);
   negm_g = dg.negm;
   negm_g8 = dg8.negm;
@@ -145,20 +167,8 @@ static __device__ __forceinline__ void tile_mmas(const RawQ80& r, int t, const u
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[nt], a0, a1, a2, a3, b.x, b.y);
+      mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
     }
-  }
-}
-
-// xs points at the CTA's staged sub-block sums, layout [pair][nt][lane].
-template <int NT>
-static __device__ __forceinline__ void min_mma(float (&acc)[NT][4], uint32_t m0g, uint32_t m0g8, uint32_t m1g, uint32_t m1g8,
-                                        const uint4* __restrict__ xs, int pl, int lane) {
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint4 v = xs[(pl * NT + nt) * 32 + lane];
-    mma16816(acc[nt], m0g, m0g8, m1g, m1g8, v.x, v.y);
-    mma16816(acc[nt], m0g, m0g8, m1g, m1g8, v.z, v.w);
   }
 }
 

@@ -22,25 +22,15 @@ struct LlamaDims {
 inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 2); }
 
 int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int q, int H, float* d_h, cudaStream_t st);
-// h[p] += sum_s part[s][p] (nsplit may be 0); x = rmsnorm(h) * w -> fragments for a GEMV over H columns.
-// Launches 8*nt CTAs (rows >= q write zeros).
-int launch_norm(const float* d_part, int nsplit, int part_rows, int q, int H, const float* d_w, float eps, float* d_h,
-                int nt, float hi_scale, void* d_xfrag, void* d_xs, cudaStream_t st);
-int launch_rope_kv(const float* d_part, int nsplit, int q, const LlamaDims& d, const long long* d_pos,
-                   const int32_t* d_parent, const int32_t* d_pages, __half* d_k, __half* d_v, __half* d_q,
-                   cudaStream_t st);
-// Paged split-KV attention for q window rows; CTAs combine their 4 pages, and the last CTA of each
-// (m-tile, kv head) combines all page groups and writes W_o's input fragments (out_frag / out_sum, qd columns).
-// d_part holds mtiles*nkv*max_pages*16*(hd+2) floats; d_counters mtiles*nkv zeroed ints.
+// Paged split-KV attention for q window rows: pages staged in shared memory by bulk copies (committed pages
+// before griddepcontrol.wait), CTAs combine their 4 pages, and the last CTA of each (m-tile, kv head) combines
+// all page groups and writes W_o's input fragments (out_frag / out_sum, qd columns).
+// d_part holds mtiles*nkv*max_pages*16*(hd+2) floats; d_counters mtiles*nkv zeroed ints; a bounded wait that
+// gives up stores kErrWaitTimeout in *d_err.
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
-                     cudaStream_t st);
-int launch_attn_combine(const float* d_part, const long long* d_pos, int q, const LlamaDims& d, int max_pages, int nt,
-                        float hi_scale, void* d_xfrag, void* d_xs, cudaStream_t st);
-// a = silu(gate) * up from the gate|up GEMV partials (rows 2F) -> fragments for the down GEMV.
-int launch_swiglu(const float* d_part, int nsplit, int q, int F, int nt, float hi_scale, void* d_xfrag, void* d_xs,
-                  cudaStream_t st);
+                     int* d_err, cudaStream_t st);
 // Copies h[p][0:H] of rows into the boundary records out[p] = {S = h, P = 0, g = 1} (hc = 1).
 int launch_pack_boundary(const float* d_h, const float* d_part, int nsplit, int q, int H, float* d_out,
                          cudaStream_t st);

@@ -133,7 +133,7 @@ int matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, i
   e.kind = EPI_STORE;
   e.out = d_y;
   e.out_ld = s.rows;
-  return launch_gemv3(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
+  return launch_gemv(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
 }
 
 }  // namespace clm

@@ -74,7 +74,7 @@ int matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float*
   e.kind = EPI_STORE;
   e.out = d_y;
   e.out_ld = s.rows;
-  return launch_gemv3(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
+  return launch_gemv(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
 }
 
 }  // namespace

@@ -9,10 +9,14 @@
 //    sample float(max(0, P - Q)) (or P when that mass is zero); if all are accepted sample the bonus row.
 //
 // sample_from is reproduced bit for bit without a serial walk.  Every positive f32 value is an integer
-// multiple of 2^-149, so prefix sums are computed EXACTLY in 192-bit fixed point with a block scan.  The
-// serial double sums differ from the exact ones by at most g*S (recursive summation bound, g ~ V*2^-53), and
-// r likewise.  The index is taken from the exact prefixes only when that bound proves the serial comparisons
-// give the same index; otherwise (probability ~V*g per draw) one thread re-walks the row serially.
+// multiple of 2^-149, so prefix sums are computed EXACTLY in 192-bit fixed point.  The serial double sums
+// differ from the exact ones by at most g*S (recursive summation bound, g ~ V*2^-53), and r likewise.  The
+// index is taken from the exact prefixes only when that bound proves the serial comparisons give the same
+// index; otherwise (probability ~V*g per draw) one thread re-walks the row serially.
+//
+// Every row operation is spread over ceil(V / kSampleChunk) CTAs per row ("chunks"): per-chunk partial results
+// go to scratch, and the last CTA of a row (atomic counter, left at zero afterwards) combines them in chunk
+// order, so results are deterministic and independent of scheduling.
 #include <cfloat>
 
 #include "common.cuh"
@@ -177,155 +181,56 @@ __device__ int32_t serial_sample(const F& fx, uint32_t n, double u) {
   return last;
 }
 
-// Block-cooperative exact sample_from.  All threads must call; all threads get the result.
-// *fell_back (optional) reports whether the serial walk was needed.
-template <typename F>
-__device__ int32_t exact_sample(const F& fx, uint32_t n, double u, bool* fell_back = nullptr) {
-  __shared__ int32_t s_result;
-  __shared__ int s_state;  // 0 undecided, 1 decided, 2 fallback
-  __shared__ U192 s_th_true, s_th_false;
-  const uint32_t nt = blockDim.x, tid = threadIdx.x;
-  const uint32_t chunk = (n + nt - 1) / nt;
-  const uint32_t c0 = min(n, tid * chunk), c1 = min(n, c0 + chunk);
-  U192 sum = u192_zero();
-  int32_t last_nz = -1;
-  bool bad = false;
-  for (uint32_t i = c0; i < c1; ++i) {
-    const float x = fx(i);
-    if (!fast_ok(x)) {
-      bad = true;
-      continue;
-    }
-    if (x > 0.0f) {
-      u192_add(sum, u192_from_float(x));
-      last_nz = (int32_t)i;
-    }
-  }
-  if (tid == 0) s_state = 0;
-  bad = __syncthreads_or(bad);
-  U192 total;
-  const U192 prefix = block_exclusive_scan(sum, &total);
-  // last nonzero index strictly before this chunk (chunks are ordered, so a max-scan), and overall
-  int32_t overall_last;
-  const int32_t prev_before_chunk = block_exclusive_max(last_nz, &overall_last);
-  if (bad) {
-    if (tid == 0) {
-      s_state = 2;
-    }
-  } else if (overall_last < 0) {
-    if (tid == 0) {
-      s_result = 0;
-      s_state = 1;
-    }
-  } else if (tid == 0) {
-    const double S = u192_to_double(total);
-    const double g = ((double)n + 8.0) * 0x1.0p-52 + 16.0 * 0x1.0p-53;
-    const double r_lo = u * S * (1.0 - g), r_hi = u * S * (1.0 + g);
-    bool ok = u192_from_double(r_hi * (1.0 + 2.0 * g), true, &s_th_true);
-    ok = ok && u192_from_double(r_lo * (1.0 - 2.0 * g), false, &s_th_false);
-    if (!ok) {
-      s_state = 2;
-    } else if (!u192_gt(total, s_th_true)) {
-      // no certainly-true index: answer the last nonzero if every prefix is certainly false
-      if (!u192_gt(total, s_th_false)) {
-        s_result = overall_last;
-        s_state = 1;
-      } else {
-        s_state = 2;
-      }
-    }
-  }
-  __syncthreads();
-  if (s_state == 0) {
-    // the chunk whose exact prefix crosses th_true holds the first certainly-true index
-    U192 end = prefix;
-    u192_add(end, sum);
-    if (!u192_gt(prefix, s_th_true) && u192_gt(end, s_th_true)) {
-      U192 run = prefix;
-      int32_t prev_nz = prev_before_chunk;
-      U192 prev_prefix = prefix;
-      for (uint32_t i = c0; i < c1; ++i) {
-        const float x = fx(i);
-        if (!(x > 0.0f)) continue;
-        u192_add(run, u192_from_float(x));
-        if (u192_gt(run, s_th_true)) {
-          const bool prev_false = prev_nz < 0 || !u192_gt(prev_prefix, s_th_false);
-          if (prev_false) {
-            s_result = (int32_t)i;
-            s_state = 1;
-          } else {
-            s_state = 2;
-          }
-          break;
-        }
-        prev_nz = (int32_t)i;
-        prev_prefix = run;
-      }
-    }
-  }
-  __syncthreads();
-  if (s_state != 1) {
-    if (tid == 0) s_result = serial_sample(fx, n, u);
-    __syncthreads();
-  }
-  if (fell_back) *fell_back = s_state != 1;
-  const int32_t r = s_result;
-  __syncthreads();
-  return r;
-}
 
 // ---------------------------------------------------------------------------------------------------
-// value providers
+// scratch
 // ---------------------------------------------------------------------------------------------------
-struct RowValues {
-  const float* p;
-  __device__ float operator()(uint32_t i) const { return p[i]; }
-};
+namespace {
+size_t al(size_t n) { return (n + 255) & ~size_t{255}; }
+}  // namespace
 
-// float(max(0, double(P_i) - Q_i)), Q one-hot at d when q == nullptr (sampling.cpp:117-123)
-struct ResidualArrays {
-  const float* P;
-  const float* Q;
-  int32_t d;
-  __device__ float operator()(uint32_t i) const {
-    const double qi = Q ? (double)Q[i] : ((int32_t)i == d ? 1.0 : 0.0);
-    const double r = (double)P[i] - qi;
-    return (float)(r > 0.0 ? r : 0.0);
-  }
-};
-
-// distribution() value of one logit row: float(exp(double(l - mx)/T) / kept)
-__device__ __forceinline__ float dist_value(float l, float mx, double inv_t_div, double kept, float T) {
-  (void)inv_t_div;
-  const double e = exp((double)__fsub_rn(l, mx) / (double)T);
-  return (float)(e / kept);
+size_t SampleScratch::bytes(uint32_t rows, uint32_t seqs, uint32_t V) {
+  const size_t C = sample_chunks(V);
+  return al((rows + seqs) * sizeof(int)) + al(rows * C * 4) + al(rows * C * 8) + al(rows * 4) + al(rows * 8) +
+         al(rows * C * 4) + al(rows * C * 4) + al(seqs * 2 * C * 24) + al(seqs * 2 * C * 4) + al(seqs * C * 4) +
+         al(seqs * 8) + al(seqs * 4);
 }
 
-struct LogitRow {
-  const float* l;
-  float mx;
-  double kept;
-  float T;
-  __device__ float operator()(uint32_t i) const { return dist_value(l[i], mx, 0.0, kept, T); }
-};
-
-struct ResidualLogits {
-  LogitRow P;
-  const float* ql;  // draft logits row or nullptr (one-hot)
-  float qmx;
-  double qkept;
-  int32_t d;
-  __device__ float operator()(uint32_t i) const {
-    const double pi = (double)P(i);
-    const double qi = ql ? (double)dist_value(ql[i], qmx, 0.0, qkept, P.T) : ((int32_t)i == d ? 1.0 : 0.0);
-    const double r = pi - qi;
-    return (float)(r > 0.0 ? r : 0.0);
-  }
-};
+SampleScratch SampleScratch::carve(void* base, uint32_t rows, uint32_t seqs, uint32_t V) {
+  const size_t C = sample_chunks(V);
+  uint8_t* p = static_cast<uint8_t*>(base);
+  SampleScratch s;
+  s.rows = rows;
+  s.seqs = seqs;
+  s.chunks = (uint32_t)C;
+  auto take = [&](size_t n) {
+    uint8_t* r = p;
+    p += al(n);
+    return r;
+  };
+  s.rcnt = reinterpret_cast<int*>(take((rows + seqs) * sizeof(int)));
+  s.scnt = s.rcnt + rows;
+  s.counter_bytes = al((rows + seqs) * sizeof(int));
+  s.cmax = reinterpret_cast<float*>(take(rows * C * 4));
+  s.csum = reinterpret_cast<double*>(take(rows * C * 8));
+  s.mx = reinterpret_cast<float*>(take(rows * 4));
+  s.kept = reinterpret_cast<double*>(take(rows * 8));
+  s.cval = reinterpret_cast<float*>(take(rows * C * 4));
+  s.cidx = reinterpret_cast<int32_t*>(take(rows * C * 4));
+  s.c192 = reinterpret_cast<unsigned long long*>(take(seqs * 2 * C * 24));
+  s.clast = reinterpret_cast<int32_t*>(take(seqs * 2 * C * 4));
+  s.cflag = reinterpret_cast<int*>(take(seqs * C * 4));
+  s.u = reinterpret_cast<double*>(take(seqs * 8));
+  s.sel = reinterpret_cast<int32_t*>(take(seqs * 4));
+  return s;
+}
 
 // ---------------------------------------------------------------------------------------------------
 // block reductions
 // ---------------------------------------------------------------------------------------------------
+constexpr int kSampleThreads = 256;
+constexpr int kPerThread = kSampleChunk / kSampleThreads;  // 8 contiguous entries per thread
+
 __device__ float block_max(float v) {
   __shared__ float sm[32];
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -360,93 +265,150 @@ __device__ double block_sum_d(double v) {
   return v;
 }
 
-// ---------------------------------------------------------------------------------------------------
-// kernels
-// ---------------------------------------------------------------------------------------------------
-// First index of the maximum of l[0..vocab); a NaN at index 0 pins the answer to 0 and NaNs elsewhere are never
-// chosen (the reference's `logits[i] > logits[best]` scan).  All threads get the result.
-__device__ int32_t block_argmax(const float* __restrict__ l, uint32_t vocab) {
+// (value, index) maximum with ties to the lower index; NaN values never win.
+__device__ __forceinline__ void argmax_merge(float& bv, int32_t& bi, float v, int32_t i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__device__ void block_argmax_pair(float& bv, int32_t& bi) {
   __shared__ float sv[32];
   __shared__ int32_t si[32];
-  __shared__ int32_t s_res;
-  float best = -INFINITY;
-  int32_t bi = INT32_MAX;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = l[i];
-    if (v > best || (v == best && (int32_t)i < bi)) {
-      best = v;
-      bi = (int32_t)i;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-    const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
-  }
+  for (int o = 16; o > 0; o >>= 1) argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   if (lane == 0) {
-    sv[warp] = best;
+    sv[warp] = bv;
     si[warp] = bi;
   }
   __syncthreads();
   if (warp == 0) {
-    best = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
+    bv = lane < (int)(blockDim.x / 32) ? sv[lane] : -INFINITY;
     bi = lane < (int)(blockDim.x / 32) ? si[lane] : INT32_MAX;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > best || (ov == best && oi < bi)) {
-        best = ov;
-        bi = oi;
-      }
+    for (int o = 16; o > 0; o >>= 1)
+      argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    if (lane == 0) {
+      sv[0] = bv;
+      si[0] = bi;
     }
-    if (lane == 0) s_res = (isnan(l[0]) || bi == INT32_MAX) ? 0 : bi;
   }
   __syncthreads();
-  const int32_t r = s_res;
+  bv = sv[0];
+  bi = si[0];
   __syncthreads();
+}
+
+// The last CTA of row r (of `total` CTAs) gets true; the counter is left at zero.
+__device__ bool last_of(int* cnt, int total) {
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_last = atomicAdd(cnt, 1) == total - 1;
+    if (s_last) *cnt = 0;
+  }
+  __syncthreads();
+  const bool r = s_last;
+  if (r) __threadfence();
   return r;
 }
 
-__global__ void argmax_rows_kernel(const float* __restrict__ logits, uint32_t vocab, int32_t* __restrict__ out) {
-  griddep_wait();
-  griddep_launch();
-  const int32_t r = block_argmax(logits + (size_t)blockIdx.x * vocab, vocab);
-  if (threadIdx.x == 0) out[blockIdx.x] = r;
-}
+__device__ __forceinline__ float read_temperature(float T, const RoundCtl* ctl) { return ctl ? ctl->temperature : T; }
 
-// Row statistics for distribution(): max and kept = sum exp(double(l - max)/T).
-__global__ void row_stats_kernel(const float* __restrict__ logits, uint32_t vocab, float T, float* __restrict__ mx_out,
-                                 double* __restrict__ kept_out, const RoundCtl* __restrict__ ctl) {
+// ---------------------------------------------------------------------------------------------------
+// argmax rows (sampling.cpp:44-49): first index of the maximum; a NaN at index 0 pins the answer to 0 and
+// NaNs elsewhere are never chosen (the reference's `logits[i] > logits[best]` scan)
+// ---------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSampleThreads) argmax_chunks_kernel(const float* __restrict__ logits, uint32_t V,
+                                                                       float* __restrict__ cval,
+                                                                       int32_t* __restrict__ cidx, int* __restrict__ cnt,
+                                                                       int32_t* __restrict__ out) {
   griddep_wait();
   griddep_launch();
-  if (ctl) T = ctl->temperature;
-  const float* l = logits + (size_t)blockIdx.x * vocab;
-  float m = -FLT_MAX;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, l[i]);
-  m = block_max(m);
-  double s = 0.0;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) s += exp((double)__fsub_rn(l[i], m) / (double)T);
-  s = block_sum_d(s);
+  const uint32_t c = blockIdx.x, r = blockIdx.y, C = gridDim.x;
+  const float* l = logits + (size_t)r * V;
+  const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
+  float bv = -INFINITY;
+  int32_t bi = INT32_MAX;
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) argmax_merge(bv, bi, l[i], (int32_t)i);
+  block_argmax_pair(bv, bi);
   if (threadIdx.x == 0) {
-    mx_out[blockIdx.x] = m;
-    kept_out[blockIdx.x] = s;
+    cval[(size_t)r * C + c] = bv;
+    cidx[(size_t)r * C + c] = bi;
+  }
+  if (!last_of(&cnt[r], (int)C)) return;
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    int32_t ix = INT32_MAX;
+    for (uint32_t k = 0; k < C; ++k) argmax_merge(v, ix, __ldcg(cval + (size_t)r * C + k), __ldcg(cidx + (size_t)r * C + k));
+    out[r] = (isnan(l[0]) || ix == INT32_MAX) ? 0 : ix;
   }
 }
 
-__global__ void distribution_kernel(const float* __restrict__ logits, uint32_t vocab, float T,
-                                    const float* __restrict__ mx, const double* __restrict__ kept,
-                                    float* __restrict__ probs) {
-  const size_t row = blockIdx.y;
-  const float* l = logits + row * vocab;
-  float* o = probs + row * vocab;
-  const float m = mx[row];
-  const double k = kept[row];
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < vocab; i += gridDim.x * blockDim.x)
-    o[i] = dist_value(l[i], m, 0.0, k, T);
+// ---------------------------------------------------------------------------------------------------
+// distribution rows (sampling.cpp:51-86, temperature only): P_i = float(exp(double(l_i - max) / T) / kept)
+// ---------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* __restrict__ logits, uint32_t V,
+                                                                   float* __restrict__ cmax, float* __restrict__ mx,
+                                                                   int* __restrict__ cnt) {
+  griddep_wait();
+  griddep_launch();
+  const uint32_t c = blockIdx.x, r = blockIdx.y, C = gridDim.x;
+  const float* l = logits + (size_t)r * V;
+  const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
+  float m = -FLT_MAX;
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) m = fmaxf(m, l[i]);
+  m = block_max(m);
+  if (threadIdx.x == 0) cmax[(size_t)r * C + c] = m;
+  if (!last_of(&cnt[r], (int)C)) return;
+  if (threadIdx.x == 0) {
+    float a = -FLT_MAX;
+    for (uint32_t k = 0; k < C; ++k) a = fmaxf(a, __ldcg(cmax + (size_t)r * C + k));
+    mx[r] = a;
+  }
+}
+
+__global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* __restrict__ logits, uint32_t V,
+                                                                   float T, const RoundCtl* __restrict__ ctl,
+                                                                   const float* __restrict__ mx,
+                                                                   double* __restrict__ csum, double* __restrict__ kept,
+                                                                   int* __restrict__ cnt) {
+  griddep_wait();
+  griddep_launch();
+  T = read_temperature(T, ctl);
+  const uint32_t c = blockIdx.x, r = blockIdx.y, C = gridDim.x;
+  const float* l = logits + (size_t)r * V;
+  const float m = mx[r];
+  const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
+  double acc = 0.0;
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) acc += exp((double)__fsub_rn(l[i], m) / (double)T);
+  acc = block_sum_d(acc);
+  if (threadIdx.x == 0) csum[(size_t)r * C + c] = acc;
+  if (!last_of(&cnt[r], (int)C)) return;
+  if (threadIdx.x == 0) {
+    double a = 0.0;
+    for (uint32_t k = 0; k < C; ++k) a += __ldcg(csum + (size_t)r * C + k);
+    kept[r] = a;
+  }
+}
+
+__global__ void __launch_bounds__(kSampleThreads) probs_kernel(const float* __restrict__ logits, uint32_t V, float T,
+                                                               const RoundCtl* __restrict__ ctl,
+                                                               const float* __restrict__ mx,
+                                                               const double* __restrict__ kept,
+                                                               float* __restrict__ probs) {
+  griddep_wait();
+  griddep_launch();
+  T = read_temperature(T, ctl);
+  const uint32_t c = blockIdx.x, r = blockIdx.y;
+  const float* l = logits + (size_t)r * V;
+  float* o = probs + (size_t)r * V;
+  const float m = mx[r];
+  const double k = kept[r];
+  const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads)
+    o[i] = (float)(exp((double)__fsub_rn(l[i], m) / (double)T) / k);
 }
 
 __global__ void onehot_kernel(const int32_t* __restrict__ idx, uint32_t vocab, float* __restrict__ probs) {
@@ -455,14 +417,228 @@ __global__ void onehot_kernel(const int32_t* __restrict__ idx, uint32_t vocab, f
     probs[row * vocab + i] = (int32_t)i == idx[row] ? 1.0f : 0.0f;
 }
 
-__global__ void __launch_bounds__(1024) sample_rows_kernel(const float* __restrict__ probs, uint32_t vocab,
-                                                           const double* __restrict__ uniforms,
-                                                           int32_t* __restrict__ out) {
-  RowValues f{probs + (size_t)blockIdx.x * vocab};
-  const int32_t r = exact_sample(f, vocab, uniforms[blockIdx.x]);
-  if (threadIdx.x == 0) out[blockIdx.x] = r;
+// ---------------------------------------------------------------------------------------------------
+// exact sample_from over chunks
+// ---------------------------------------------------------------------------------------------------
+// What sequence b samples from.  Plain jobs: row P + b*row_stride.  Acceptance jobs (sel[b] = j written by
+// accept_decide_kernel): j == k -> the bonus row P[b][k]; else the residual float(max(0, P[b][j] - Q[b][j]))
+// (Q one-hot at the draft when Q is null), or P[b][j] when no residual is positive (sampling.cpp:117-126).
+struct SampleJob {
+  const float* P = nullptr;
+  const float* Q = nullptr;
+  const int32_t* drafts = nullptr;
+  uint64_t row_stride = 0;  // plain jobs
+  uint32_t k = 0;
+  bool accept = false;
+  const int32_t* sel = nullptr;
+  // the uniform of sequence b: uniforms[b] (or u_dev[b]) else Philox(seed, draw, stream, *d_counter) under ctl's seed
+  const double* uniforms = nullptr;
+  uint64_t seed = 0;
+  uint32_t draw = 0, stream = 0;
+  const unsigned long long* d_counter = nullptr;
+  const RoundCtl* ctl = nullptr;
+};
+
+struct RowFx {
+  const float* P;
+  const float* Q;  // residual against Q, or one-hot at d when Q is null and residual is set
+  int32_t d;
+  bool residual;
+  __device__ float operator()(uint32_t i) const {
+    if (!residual) return P[i];
+    const double qi = Q ? (double)Q[i] : ((int32_t)i == d ? 1.0 : 0.0);
+    const double r = (double)P[i] - qi;
+    return (float)(r > 0.0 ? r : 0.0);
+  }
+};
+
+// fx of sequence b: variant 0 = main (bonus / residual / plain row), 1 = fallback P[b][j] (acceptance, j < k)
+__device__ __forceinline__ RowFx job_fx(const SampleJob& job, uint32_t b, uint32_t V, int variant) {
+  if (!job.accept) return RowFx{job.P + (size_t)b * job.row_stride, nullptr, 0, false};
+  const uint32_t j = (uint32_t)job.sel[b];
+  const float* Pj = job.P + ((size_t)b * (job.k + 1) + j) * V;
+  if (j >= job.k || variant == 1) return RowFx{Pj, nullptr, 0, false};
+  return RowFx{Pj, job.Q ? job.Q + ((size_t)b * job.k + j) * V : nullptr, job.drafts[(size_t)b * job.k + j], true};
 }
 
+__device__ __forceinline__ double job_uniform(const SampleJob& job, const double* u_dev, uint32_t b) {
+  if (u_dev) return u_dev[b];
+  if (job.uniforms) return job.uniforms[b];
+  const uint64_t seed = job.ctl ? job.ctl->seed : job.seed;
+  const unsigned long long c = job.d_counter ? *job.d_counter : 0ull;
+  return philox_uniform(seed, job.draw, job.stream, (uint32_t)c, (uint32_t)(c >> 32));
+}
+
+// Per-chunk exact sums of fx over this thread's kPerThread contiguous entries.
+template <typename F>
+__device__ __forceinline__ void thread_sums(const F& fx, uint32_t lo, uint32_t hi, U192& sum, int32_t& last, bool& bad) {
+  sum = u192_zero();
+  last = -1;
+  bad = false;
+  for (uint32_t i = lo; i < hi; ++i) {
+    const float x = fx(i);
+    if (!fast_ok(x)) {
+      bad = true;
+      continue;
+    }
+    if (x > 0.0f) {
+      u192_add(sum, u192_from_float(x));
+      last = (int32_t)i;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kSampleThreads) sample_chunks_kernel(SampleJob job, uint32_t V,
+                                                                       unsigned long long* __restrict__ c192,
+                                                                       int32_t* __restrict__ clast,
+                                                                       int* __restrict__ cflag, int* __restrict__ cnt,
+                                                                       const double* __restrict__ u_dev,
+                                                                       int32_t* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  const uint32_t c = blockIdx.x, b = blockIdx.y, C = gridDim.x, tid = threadIdx.x;
+  const uint32_t clo = c * kSampleChunk, chi = min(V, clo + kSampleChunk);
+  const bool two = job.accept && (uint32_t)job.sel[b] < job.k;  // residual with a P fallback
+  __shared__ int s_flags;
+  if (tid == 0) s_flags = 0;
+  __syncthreads();
+  const uint32_t lo = min(chi, clo + tid * kPerThread), hi = min(chi, lo + kPerThread);
+  for (int variant = 0; variant < (two ? 2 : 1); ++variant) {
+    const RowFx fx = job_fx(job, b, V, variant);
+    U192 sum;
+    int32_t last;
+    bool bad;
+    thread_sums(fx, lo, hi, sum, last, bad);
+    bool anypos = false;
+    if (variant == 0 && two)
+      for (uint32_t i = lo; i < hi; ++i) {  // residual mass test in double (sampling.cpp:121-123)
+        const double qi = fx.Q ? (double)fx.Q[i] : ((int32_t)i == fx.d ? 1.0 : 0.0);
+        anypos |= ((double)fx.P[i] - qi) > 0.0;
+      }
+    U192 total;
+    (void)block_exclusive_scan(sum, &total);
+    int32_t lmax;
+    (void)block_exclusive_max(last, &lmax);
+    if (bad) atomicOr(&s_flags, variant == 0 ? 1 : 4);
+    if (anypos) atomicOr(&s_flags, 2);
+    __syncthreads();
+    if (tid == 0) {
+      unsigned long long* o = c192 + (((size_t)b * 2 + variant) * C + c) * 3;
+      o[0] = total.w[0];
+      o[1] = total.w[1];
+      o[2] = total.w[2];
+      clast[((size_t)b * 2 + variant) * C + c] = lmax;
+    }
+  }
+  if (tid == 0) cflag[(size_t)b * C + c] = s_flags;
+  if (!last_of(&cnt[b], (int)C)) return;
+
+  // ---- last CTA of sequence b: pick the row variant, locate the chunk, then the entry ----
+  __shared__ int s_variant, s_state, s_chunk;
+  __shared__ int32_t s_result, s_prev_nz;
+  __shared__ U192 s_th_true, s_th_false, s_prefix;
+  if (tid == 0) {
+    int fl = 0;
+    for (uint32_t k = 0; k < C; ++k) fl |= __ldcg(cflag + (size_t)b * C + k);
+    s_variant = (two && !(fl & 2)) ? 1 : 0;
+    s_state = (fl & (s_variant == 0 ? 1 : 4)) ? 2 : 0;  // a non-finite or huge value: serial walk
+  }
+  __syncthreads();
+  const int variant = s_variant;
+  const RowFx fx = job_fx(job, b, V, variant);
+  const double u = job_uniform(job, u_dev, b);
+  // chunk prefix sums (C <= kSampleThreads chunks per row)
+  U192 csum = u192_zero();
+  int32_t cl = -1;
+  if (tid < C) {
+    const unsigned long long* o = c192 + (((size_t)b * 2 + variant) * C + tid) * 3;
+    csum.w[0] = __ldcg(o);
+    csum.w[1] = __ldcg(o + 1);
+    csum.w[2] = __ldcg(o + 2);
+    cl = __ldcg(clast + ((size_t)b * 2 + variant) * C + tid);
+  }
+  U192 total;
+  const U192 cprefix = block_exclusive_scan(csum, &total);
+  int32_t overall_last;
+  const int32_t cprev = block_exclusive_max(cl, &overall_last);
+  if (tid == 0 && s_state == 0) {
+    if (overall_last < 0) {
+      s_result = 0;
+      s_state = 1;
+    } else {
+      const double S = u192_to_double(total);
+      const double g = ((double)V + 8.0) * 0x1.0p-52 + 16.0 * 0x1.0p-53;
+      const double r_lo = u * S * (1.0 - g), r_hi = u * S * (1.0 + g);
+      bool ok = u192_from_double(r_hi * (1.0 + 2.0 * g), true, &s_th_true);
+      ok = ok && u192_from_double(r_lo * (1.0 - 2.0 * g), false, &s_th_false);
+      if (!ok) {
+        s_state = 2;
+      } else if (!u192_gt(total, s_th_true)) {
+        // no certainly-true index: answer the last nonzero if every prefix is certainly false
+        if (!u192_gt(total, s_th_false)) {
+          s_result = overall_last;
+          s_state = 1;
+        } else {
+          s_state = 2;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (s_state == 0 && tid < C) {
+    U192 end = cprefix;
+    u192_add(end, csum);
+    if (!u192_gt(cprefix, s_th_true) && u192_gt(end, s_th_true)) {
+      s_chunk = (int)tid;
+      s_prefix = cprefix;
+      s_prev_nz = cprev;
+    }
+  }
+  __syncthreads();
+  const int state = s_state;  // every thread branches on the same value
+  __syncthreads();
+  if (state == 0) {
+    // entry level inside the crossing chunk
+    const uint32_t xlo = (uint32_t)s_chunk * kSampleChunk, xhi = min(V, xlo + kSampleChunk);
+    const uint32_t lo2 = min(xhi, xlo + tid * kPerThread), hi2 = min(xhi, lo2 + kPerThread);
+    U192 sum;
+    int32_t last;
+    bool bad;
+    thread_sums(fx, lo2, hi2, sum, last, bad);
+    U192 ctot;
+    U192 prefix = block_exclusive_scan(sum, &ctot);
+    u192_add(prefix, s_prefix);
+    int32_t lm;
+    int32_t prev = block_exclusive_max(last, &lm);
+    if (prev < 0) prev = s_prev_nz;
+    U192 end = prefix;
+    u192_add(end, sum);
+    if (!u192_gt(prefix, s_th_true) && u192_gt(end, s_th_true)) {
+      U192 run = prefix;
+      int32_t prev_nz = prev;
+      U192 prev_prefix = prefix;
+      for (uint32_t i = lo2; i < hi2; ++i) {
+        const float x = fx(i);
+        if (!(x > 0.0f)) continue;
+        u192_add(run, u192_from_float(x));
+        if (u192_gt(run, s_th_true)) {
+          const bool prev_false = prev_nz < 0 || !u192_gt(prev_prefix, s_th_false);
+          s_result = (int32_t)i;
+          s_state = prev_false ? 1 : 2;
+          break;
+        }
+        prev_nz = (int32_t)i;
+        prev_prefix = run;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) out[b] = s_state == 1 ? s_result : serial_sample(fx, V, u);
+}
+
+// ---------------------------------------------------------------------------------------------------
+// speculative acceptance decisions (sampling.cpp:103-116): one thread per sequence
+// ---------------------------------------------------------------------------------------------------
 __device__ __forceinline__ double draw_uniform(const double* uniforms, uint64_t seed, uint64_t counter_base,
                                                uint32_t seq, uint32_t k, uint32_t n) {
   // Philox counter (draw, sequence, counter_base lo, counter_base hi) under key `seed`.
@@ -470,120 +646,36 @@ __device__ __forceinline__ double draw_uniform(const double* uniforms, uint64_t 
   return philox_uniform(seed, n, seq, (uint32_t)counter_base, (uint32_t)(counter_base >> 32));
 }
 
-// One CTA per sequence: sequential acceptance tests, then a block-cooperative exact resample.
-__global__ void __launch_bounds__(1024) verify_kernel(const float* __restrict__ target, const int32_t* __restrict__ drafts,
-                                                      const float* __restrict__ draft_probs, uint32_t k, uint32_t vocab,
-                                                      const double* __restrict__ uniforms, uint64_t seed,
-                                                      uint64_t counter_base, uint32_t* __restrict__ accepted,
-                                                      int32_t* __restrict__ next) {
-  const uint32_t b = blockIdx.x;
-  const float* T = target + (size_t)b * (k + 1) * vocab;
-  const int32_t* d = drafts + (size_t)b * k;
-  const float* Q = draft_probs ? draft_probs + (size_t)b * k * vocab : nullptr;
-  __shared__ uint32_t s_j, s_used;
-  if (threadIdx.x == 0) {
-    uint32_t used = 0, j = 0;
-    for (; j < k; ++j) {
-      const uint32_t dj = (uint32_t)d[j];
-      const double p = dj < vocab ? (double)T[(size_t)j * vocab + dj] : 0.0;
-      const double q = Q ? (dj < vocab ? (double)Q[(size_t)j * vocab + dj] : 0.0) : 1.0;
-      if (q > 0.0) {
-        const double ratio = p / q;
-        const double lim = ratio < 1.0 ? ratio : 1.0;
-        if (draw_uniform(uniforms, seed, counter_base, b, k, used++) < lim) continue;
-      }
-      break;
-    }
-    s_j = j;
-    s_used = used;
-  }
-  __syncthreads();
-  const uint32_t j = s_j;
-  const double u = draw_uniform(uniforms, seed, counter_base, b, k, s_used);
-  int32_t tok;
-  if (j == k) {
-    tok = exact_sample(RowValues{T + (size_t)k * vocab}, vocab, u);
-  } else {
-    ResidualArrays res{T + (size_t)j * vocab, Q ? Q + (size_t)j * vocab : nullptr, d[j]};
-    // mass > 0 iff some residual (in double) is positive
-    bool any = false;
-    for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-      const double qi = res.Q ? (double)res.Q[i] : ((int32_t)i == res.d ? 1.0 : 0.0);
-      any |= ((double)res.P[i] - qi) > 0.0;
-    }
-    any = __syncthreads_or(any);
-    tok = any ? exact_sample(res, vocab, u) : exact_sample(RowValues{res.P}, vocab, u);
-  }
-  if (threadIdx.x == 0) {
-    accepted[b] = j;
-    next[b] = tok;
-  }
-}
-
-// Fused acceptance from logits (row statistics precomputed by row_stats_kernel).
-// Stats layout: target row j of sequence b at b*(k+1) + j; draft row j at batch*(k+1) + b*k + j.
-__global__ void __launch_bounds__(1024) accept_logits_kernel(
-    const float* __restrict__ tl, const float* __restrict__ dl, const int32_t* __restrict__ drafts, uint32_t k,
-    uint32_t vocab, float T, const float* __restrict__ mx, const double* __restrict__ kept,
-    const double* __restrict__ uniforms, uint64_t seed, uint64_t counter_base,
-    const unsigned long long* __restrict__ d_counter, uint32_t* __restrict__ accepted, int32_t* __restrict__ next,
-    const RoundCtl* __restrict__ ctl) {
+__global__ void accept_decide_kernel(const float* __restrict__ P, const float* __restrict__ Q,
+                                     const int32_t* __restrict__ drafts, uint32_t batch, uint32_t k, uint32_t V,
+                                     const double* __restrict__ uniforms, uint64_t seed, uint64_t counter_base,
+                                     const unsigned long long* __restrict__ d_counter, const RoundCtl* __restrict__ ctl,
+                                     int32_t* __restrict__ sel, double* __restrict__ u_out,
+                                     uint32_t* __restrict__ accepted) {
   griddep_wait();
   griddep_launch();
+  const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
   if (d_counter) counter_base = *d_counter;
-  if (ctl) {
-    T = ctl->temperature;
-    seed = ctl->seed;
-  }
-  const uint32_t b = blockIdx.x;
-  const float* tb = tl + (size_t)b * (k + 1) * vocab;
-  const float* db = dl ? dl + (size_t)b * k * vocab : nullptr;
+  if (ctl) seed = ctl->seed;
+  const float* Pb = P + (size_t)b * (k + 1) * V;
+  const float* Qb = Q ? Q + (size_t)b * k * V : nullptr;
   const int32_t* d = drafts + (size_t)b * k;
-  const float* smx = mx + (size_t)b * (k + 1);  // target row j: smx[j]
-  const double* skept = kept + (size_t)b * (k + 1);
-  const float* qmx = mx + (size_t)gridDim.x * (k + 1) + (size_t)b * k;  // draft row j: qmx[j]
-  const double* qkept = kept + (size_t)gridDim.x * (k + 1) + (size_t)b * k;
-  __shared__ uint32_t s_j, s_used;
-  if (threadIdx.x == 0) {
-    uint32_t used = 0, j = 0;
-    for (; j < k; ++j) {
-      const uint32_t dj = (uint32_t)d[j];
-      const double p = dj < vocab ? (double)dist_value(tb[(size_t)j * vocab + dj], smx[j], 0.0, skept[j], T) : 0.0;
-      const double q =
-          db ? (dj < vocab ? (double)dist_value(db[(size_t)j * vocab + dj], qmx[j], 0.0, qkept[j], T) : 0.0) : 1.0;
-      if (q > 0.0) {
-        const double ratio = p / q;
-        const double lim = ratio < 1.0 ? ratio : 1.0;
-        if (draw_uniform(uniforms, seed, counter_base, b, k, used++) < lim) continue;
-      }
-      break;
+  uint32_t used = 0, j = 0;
+  for (; j < k; ++j) {
+    const uint32_t dj = (uint32_t)d[j];
+    const double p = dj < V ? (double)Pb[(size_t)j * V + dj] : 0.0;
+    const double q = Qb ? (dj < V ? (double)Qb[(size_t)j * V + dj] : 0.0) : 1.0;
+    if (q > 0.0) {
+      const double ratio = p / q;
+      const double lim = ratio < 1.0 ? ratio : 1.0;
+      if (draw_uniform(uniforms, seed, counter_base, b, k, used++) < lim) continue;
     }
-    s_j = j;
-    s_used = used;
+    break;
   }
-  __syncthreads();
-  const uint32_t j = s_j;
-  const double u = draw_uniform(uniforms, seed, counter_base, b, k, s_used);
-  int32_t tok;
-  if (j == k) {
-    tok = exact_sample(LogitRow{tb + (size_t)k * vocab, smx[k], skept[k], T}, vocab, u);
-  } else {
-    ResidualLogits res{LogitRow{tb + (size_t)j * vocab, smx[j], skept[j], T},
-                       db ? db + (size_t)j * vocab : nullptr, db ? qmx[j] : 0.0f, db ? qkept[j] : 1.0, d[j]};
-    bool any = false;
-    for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-      const double pi = (double)res.P(i);
-      const double qi = res.ql ? (double)dist_value(res.ql[i], res.qmx, 0.0, res.qkept, T)
-                               : ((int32_t)i == res.d ? 1.0 : 0.0);
-      any |= (pi - qi) > 0.0;
-    }
-    any = __syncthreads_or(any);
-    tok = any ? exact_sample(res, vocab, u) : exact_sample(res.P, vocab, u);
-  }
-  if (threadIdx.x == 0) {
-    accepted[b] = j;
-    next[b] = tok;
-  }
+  sel[b] = (int32_t)j;
+  accepted[b] = j;
+  u_out[b] = draw_uniform(uniforms, seed, counter_base, b, k, used);
 }
 
 __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,
@@ -597,64 +689,87 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t first, uint32_t c
 // ---------------------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------------------
-int launch_argmax(const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out, cudaStream_t st) {
+int launch_argmax_rows(const float* d_logits, uint32_t rows, uint32_t V, int32_t* d_out, const SampleScratch& s,
+                       cudaStream_t st) {
   if (rows == 0) return CLM_OK;
-  return launch_pdl(argmax_rows_kernel, dim3(rows), dim3(1024), 0, st, d_logits, vocab, d_out);
+  CLM_CHECK(rows <= s.rows, CLM_INTERNAL, "sampling scratch too small");
+  return launch_pdl(argmax_chunks_kernel, dim3(sample_chunks(V), rows), dim3(kSampleThreads), 0, st, d_logits, V,
+                    s.cval, s.cidx, s.rcnt, d_out);
 }
 
-int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t vocab, float T, float* d_mx, double* d_kept,
-                     cudaStream_t st, const RoundCtl* ctl) {
+int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, float* d_probs,
+                 const SampleScratch& s, cudaStream_t st) {
   if (rows == 0) return CLM_OK;
-  return launch_pdl(row_stats_kernel, dim3(rows), dim3(512), 0, st, d_logits, vocab, T, d_mx, d_kept, ctl);
+  CLM_CHECK(rows <= s.rows, CLM_INTERNAL, "sampling scratch too small");
+  const dim3 grid(sample_chunks(V), rows);
+  CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, s.cmax, s.mx, s.rcnt));
+  CLM_TRY(launch_pdl(stats_sum_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, T, ctl,
+                     (const float*)s.mx, s.csum, s.kept, s.rcnt));
+  return launch_pdl(probs_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, T, ctl, (const float*)s.mx,
+                    (const double*)s.kept, d_probs);
 }
 
-int launch_accept_logits(const float* d_tl, const float* d_dl, const int32_t* d_drafts, uint32_t batch, uint32_t k,
-                         uint32_t vocab, float T, const float* d_mx, const double* d_kept, const double* d_uniforms,
-                         uint64_t seed, uint64_t counter_base, const unsigned long long* d_counter,
-                         uint32_t* d_accepted, int32_t* d_next, cudaStream_t st, const RoundCtl* ctl) {
-  return launch_pdl(accept_logits_kernel, dim3(batch), dim3(1024), 0, st, d_tl, d_dl, d_drafts, k, vocab, T, d_mx,
-                    d_kept, d_uniforms, seed, counter_base, d_counter, d_accepted, d_next, ctl);
+static int launch_sample_job(const SampleJob& job, uint32_t seqs, uint32_t V, const double* u_dev, int32_t* d_out,
+                             const SampleScratch& s, cudaStream_t st) {
+  CLM_CHECK(seqs <= s.seqs, CLM_INTERNAL, "sampling scratch too small");
+  CLM_CHECK(sample_chunks(V) <= (uint32_t)kSampleThreads, CLM_OUT_OF_RANGE, "vocabulary too large for sampling");
+  return launch_pdl(sample_chunks_kernel, dim3(sample_chunks(V), seqs), dim3(kSampleThreads), 0, st, job, V, s.c192,
+                    s.clast, s.cflag, s.scnt, u_dev, d_out);
 }
 
-// One row of logits -> one token: argmax (T <= 0) or sample_from(distribution(row, T)) with the Philox
-// uniform (draw, stream, counter lo, counter hi), counter read from *d_counter.
-__global__ void __launch_bounds__(1024) sample_logits_kernel(const float* __restrict__ logits, uint32_t vocab, float T,
-                                                             uint64_t seed, uint32_t draw, uint32_t stream_id,
-                                                             const unsigned long long* __restrict__ d_counter,
-                                                             int32_t* __restrict__ out, const RoundCtl* __restrict__ ctl) {
-  griddep_wait();
-  griddep_launch();
-  if (ctl) {
-    T = ctl->temperature;
-    seed = ctl->seed;
-  }
-  if (T <= 0.0f) {
-    const int32_t r = block_argmax(logits, vocab);
-    if (threadIdx.x == 0) *out = r;
-    return;
-  }
-  float m = -FLT_MAX;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, logits[i]);
-  m = block_max(m);
-  double s = 0.0;
-  for (uint32_t i = threadIdx.x; i < vocab; i += blockDim.x) s += exp((double)__fsub_rn(logits[i], m) / (double)T);
-  s = block_sum_d(s);
-  const unsigned long long c = d_counter ? *d_counter : 0ull;
-  const double u = philox_uniform(seed, draw, stream_id, (uint32_t)c, (uint32_t)(c >> 32));
-  const int32_t tok = exact_sample(LogitRow{logits, m, s, T}, vocab, u);
-  if (threadIdx.x == 0) *out = tok;
+int launch_sample_rows(const float* d_probs, uint32_t rows, uint64_t row_stride, uint32_t V, const double* d_uniforms,
+                       uint64_t seed, uint32_t draw, uint32_t stream_id, const unsigned long long* d_counter,
+                       const RoundCtl* ctl, int32_t* d_out, const SampleScratch& s, cudaStream_t st) {
+  if (rows == 0) return CLM_OK;
+  SampleJob job;
+  job.P = d_probs;
+  job.row_stride = row_stride;
+  job.uniforms = d_uniforms;
+  job.seed = seed;
+  job.draw = draw;
+  job.stream = stream_id;
+  job.d_counter = d_counter;
+  job.ctl = ctl;
+  return launch_sample_job(job, rows, V, nullptr, d_out, s, st);
 }
 
-int launch_sample_logits(const float* d_logits, uint32_t vocab, float T, uint64_t seed, uint32_t draw,
-                         uint32_t stream_id, const unsigned long long* d_counter, int32_t* d_out, cudaStream_t st,
-                         const RoundCtl* ctl) {
-  return launch_pdl(sample_logits_kernel, dim3(1), dim3(1024), 0, st, d_logits, vocab, T, seed, draw, stream_id,
-                    d_counter, d_out, ctl);
+int launch_accept(const float* d_P, const float* d_Q, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
+                  const double* d_uniforms, uint64_t seed, uint64_t counter_base,
+                  const unsigned long long* d_counter, const RoundCtl* ctl, uint32_t* d_accepted, int32_t* d_next,
+                  const SampleScratch& s, cudaStream_t st) {
+  if (batch == 0) return CLM_OK;
+  CLM_CHECK(batch <= s.seqs, CLM_INTERNAL, "sampling scratch too small");
+  CLM_TRY(launch_pdl(accept_decide_kernel, dim3((batch + 127) / 128), dim3(128), 0, st, d_P, d_Q, d_drafts, batch, k,
+                     V, d_uniforms, seed, counter_base, d_counter, ctl, s.sel, s.u, d_accepted));
+  SampleJob job;
+  job.P = d_P;
+  job.Q = d_Q;
+  job.drafts = d_drafts;
+  job.k = k;
+  job.accept = true;
+  job.sel = s.sel;
+  return launch_sample_job(job, batch, V, s.u, d_next, s, st);
 }
 
 }  // namespace clm
 
 using namespace clm;
+
+namespace {
+
+// Scratch for a C-ABI call from the context's scratch buffer, counters zeroed on the call's stream.
+int abi_scratch(clm_b200_ctx* ctx, uint32_t rows, uint32_t seqs, uint32_t V, size_t extra, cudaStream_t st,
+                SampleScratch* out, void** extra_ptr) {
+  const size_t sb = SampleScratch::bytes(rows, seqs, V);
+  void* base = nullptr;
+  CLM_TRY(ctx_scratch(ctx, sb + extra + 256, &base));
+  *out = SampleScratch::carve(base, rows, seqs, V);
+  CLM_CUDA(cudaMemsetAsync(base, 0, out->counter_bytes, st));
+  if (extra_ptr) *extra_ptr = static_cast<uint8_t*>(base) + ((sb + 255) & ~size_t{255});
+  return CLM_OK;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -662,8 +777,12 @@ int clm_b200_argmax_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows
                          void* stream) {
   CLM_TRY(ctx_enter(ctx));
   CLM_CHECK(vocab > 0, CLM_INVALID_ARGUMENT, "empty vocabulary");
-  CLM_CHECK(rows == 0 || (d_logits && d_out), CLM_INVALID_ARGUMENT, "null buffer");
-  return launch_argmax(d_logits, rows, vocab, d_out, pick_stream(ctx, stream));
+  if (rows == 0) return CLM_OK;
+  CLM_CHECK(d_logits && d_out, CLM_INVALID_ARGUMENT, "null buffer");
+  cudaStream_t st = pick_stream(ctx, stream);
+  SampleScratch s;
+  CLM_TRY(abi_scratch(ctx, rows, 0, vocab, 0, st, &s, nullptr));
+  return launch_argmax_rows(d_logits, rows, vocab, d_out, s, st);
 }
 
 int clm_b200_distribution_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab,
@@ -673,26 +792,21 @@ int clm_b200_distribution_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_
   if (rows == 0) return CLM_OK;
   CLM_CHECK(d_logits && d_probs, CLM_INVALID_ARGUMENT, "null buffer");
   cudaStream_t st = pick_stream(ctx, stream);
-  const unsigned gx = (unsigned)std::min<uint64_t>(ceil_div(vocab, 256), 64);
   if (temperature <= 0.0f) {
-    void* scr = nullptr;
-    CLM_TRY(ctx_scratch(ctx, (size_t)rows * 4, &scr));
-    int32_t* idx = static_cast<int32_t*>(scr);
-    CLM_TRY(launch_argmax(d_logits, rows, vocab, idx, st));
-    onehot_kernel<<<dim3(gx, rows), 256, 0, st>>>(idx, vocab, d_probs);
+    SampleScratch s;
+    void* idx = nullptr;
+    CLM_TRY(abi_scratch(ctx, rows, 0, vocab, (size_t)rows * 4, st, &s, &idx));
+    CLM_TRY(launch_argmax_rows(d_logits, rows, vocab, static_cast<int32_t*>(idx), s, st));
+    const unsigned gx = (unsigned)std::min<uint64_t>(ceil_div(vocab, 256), 64);
+    onehot_kernel<<<dim3(gx, rows), 256, 0, st>>>(static_cast<const int32_t*>(idx), vocab, d_probs);
     CLM_LAUNCHED("onehot_kernel");
     return CLM_OK;
   }
   CLM_CHECK(top_k == 0 && top_p >= 1.0f, CLM_UNIMPLEMENTED,
             "top-k / top-p truncation is not implemented on the device yet (temperature-only distributions)");
-  void* scr = nullptr;
-  CLM_TRY(ctx_scratch(ctx, (size_t)rows * 16, &scr));
-  double* kept = static_cast<double*>(scr);
-  float* mx = reinterpret_cast<float*>(kept + rows);
-  CLM_TRY(launch_row_stats(d_logits, rows, vocab, temperature, mx, kept, st));
-  distribution_kernel<<<dim3(gx, rows), 256, 0, st>>>(d_logits, vocab, temperature, mx, kept, d_probs);
-  CLM_LAUNCHED("distribution_kernel");
-  return CLM_OK;
+  SampleScratch s;
+  CLM_TRY(abi_scratch(ctx, rows, 0, vocab, 0, st, &s, nullptr));
+  return launch_probs(d_logits, rows, vocab, temperature, nullptr, d_probs, s, st);
 }
 
 int clm_b200_sample_rows(clm_b200_ctx* ctx, const float* d_probs, uint32_t rows, uint32_t vocab,
@@ -701,9 +815,10 @@ int clm_b200_sample_rows(clm_b200_ctx* ctx, const float* d_probs, uint32_t rows,
   CLM_CHECK(vocab > 0, CLM_INVALID_ARGUMENT, "empty vocabulary");
   if (rows == 0) return CLM_OK;
   CLM_CHECK(d_probs && d_uniforms && d_out, CLM_INVALID_ARGUMENT, "null buffer");
-  sample_rows_kernel<<<rows, 1024, 0, pick_stream(ctx, stream)>>>(d_probs, vocab, d_uniforms, d_out);
-  CLM_LAUNCHED("sample_rows_kernel");
-  return CLM_OK;
+  cudaStream_t st = pick_stream(ctx, stream);
+  SampleScratch s;
+  CLM_TRY(abi_scratch(ctx, 0, rows, vocab, 0, st, &s, nullptr));
+  return launch_sample_rows(d_probs, rows, vocab, vocab, d_uniforms, 0, 0, 0, nullptr, nullptr, d_out, s, st);
 }
 
 int clm_b200_verify_speculative(clm_b200_ctx* ctx, const float* d_target, const int32_t* d_drafts,
@@ -714,10 +829,11 @@ int clm_b200_verify_speculative(clm_b200_ctx* ctx, const float* d_target, const 
   CLM_CHECK(vocab > 0, CLM_INVALID_ARGUMENT, "empty vocabulary");
   if (batch == 0) return CLM_OK;
   CLM_CHECK(d_target && (k == 0 || d_drafts) && d_accepted && d_next, CLM_INVALID_ARGUMENT, "null buffer");
-  verify_kernel<<<batch, 1024, 0, pick_stream(ctx, stream)>>>(d_target, d_drafts, d_draft_probs, k, vocab, d_uniforms,
-                                                              seed, counter_base, d_accepted, d_next);
-  CLM_LAUNCHED("verify_kernel");
-  return CLM_OK;
+  cudaStream_t st = pick_stream(ctx, stream);
+  SampleScratch s;
+  CLM_TRY(abi_scratch(ctx, 0, batch, vocab, 0, st, &s, nullptr));
+  return launch_accept(d_target, d_draft_probs, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr,
+                       nullptr, d_accepted, d_next, s, st);
 }
 
 int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_dl, const int32_t* d_drafts,
@@ -730,14 +846,15 @@ int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_
   CLM_CHECK(d_tl && (k == 0 || d_drafts) && d_accepted && d_next, CLM_INVALID_ARGUMENT, "null buffer");
   cudaStream_t st = pick_stream(ctx, stream);
   const uint32_t trows = batch * (k + 1), drows = d_dl ? batch * k : 0, rows = trows + drows;
-  void* scr = nullptr;
-  CLM_TRY(ctx_scratch(ctx, (size_t)rows * 16, &scr));
-  double* kept = static_cast<double*>(scr);
-  float* mx = reinterpret_cast<float*>(kept + rows);
-  CLM_TRY(launch_row_stats(d_tl, trows, vocab, temperature, mx, kept, st));
-  if (drows) CLM_TRY(launch_row_stats(d_dl, drows, vocab, temperature, mx + trows, kept + trows, st));
-  return launch_accept_logits(d_tl, d_dl, d_drafts, batch, k, vocab, temperature, mx, kept, d_uniforms, seed,
-                              counter_base, nullptr, d_accepted, d_next, st);
+  SampleScratch s;
+  void* probs = nullptr;
+  CLM_TRY(abi_scratch(ctx, rows, batch, vocab, (size_t)rows * vocab * sizeof(float), st, &s, &probs));
+  float* P = static_cast<float*>(probs);
+  float* Q = drows ? P + (size_t)trows * vocab : nullptr;
+  CLM_TRY(launch_probs(d_tl, trows, vocab, temperature, nullptr, P, s, st));
+  if (drows) CLM_TRY(launch_probs(d_dl, drows, vocab, temperature, nullptr, Q, s, st));
+  return launch_accept(P, Q, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr, nullptr, d_accepted,
+                       d_next, s, st);
 }
 
 int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,

@@ -12,19 +12,48 @@ struct RoundCtl {
   unsigned long long seed;
 };
 
-int launch_argmax(const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out, cudaStream_t st);
-// mx[r] = max of row r; kept[r] = sum exp(double(l - mx) / T)
-int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t vocab, float T, float* d_mx, double* d_kept,
-                     cudaStream_t st, const RoundCtl* ctl = nullptr);
-// Stats layout: target row j of sequence b at b*(k+1)+j; draft row j at batch*(k+1) + b*k + j.
-// counter_base is read from *d_counter when d_counter is not null.
-int launch_accept_logits(const float* d_tl, const float* d_dl, const int32_t* d_drafts, uint32_t batch, uint32_t k,
-                         uint32_t vocab, float T, const float* d_mx, const double* d_kept, const double* d_uniforms,
-                         uint64_t seed, uint64_t counter_base, const unsigned long long* d_counter,
-                         uint32_t* d_accepted, int32_t* d_next, cudaStream_t st, const RoundCtl* ctl = nullptr);
-// One logits row -> token: argmax for T <= 0, else an exact sample of distribution(row, T) with the Philox
-// uniform (draw, stream_id, *d_counter lo, hi) under key `seed`.
-int launch_sample_logits(const float* d_logits, uint32_t vocab, float T, uint64_t seed, uint32_t draw,
-                         uint32_t stream_id, const unsigned long long* d_counter, int32_t* d_out, cudaStream_t st,
-                         const RoundCtl* ctl = nullptr);
+constexpr uint32_t kSampleChunk = 2048;  // vocabulary entries per CTA
+inline uint32_t sample_chunks(uint32_t V) { return (V + kSampleChunk - 1) / kSampleChunk; }
+
+// Device scratch of the chunked row kernels for up to `rows` statistic rows and `seqs` sampled sequences.
+// The first counter_bytes hold counters that must be zero before the first launch (every kernel leaves them
+// zero).  One scratch must not be used by two launches that can run concurrently.
+struct SampleScratch {
+  uint32_t rows = 0, seqs = 0, chunks = 0;
+  size_t counter_bytes = 0;
+  int* rcnt = nullptr;               // [rows]
+  int* scnt = nullptr;               // [seqs]
+  float* cmax = nullptr;             // [rows][C]
+  double* csum = nullptr;            // [rows][C]
+  float* mx = nullptr;               // [rows]
+  double* kept = nullptr;            // [rows]
+  float* cval = nullptr;             // [rows][C] argmax chunks
+  int32_t* cidx = nullptr;           // [rows][C]
+  unsigned long long* c192 = nullptr;  // [seqs][2][C][3] exact chunk sums
+  int32_t* clast = nullptr;          // [seqs][2][C]
+  int* cflag = nullptr;              // [seqs][C]
+  double* u = nullptr;               // [seqs]
+  int32_t* sel = nullptr;            // [seqs]
+  static size_t bytes(uint32_t rows, uint32_t seqs, uint32_t V);
+  static SampleScratch carve(void* base, uint32_t rows, uint32_t seqs, uint32_t V);
+};
+
+// out[r] = argmax of row r (ties to the lowest index).
+int launch_argmax_rows(const float* d_logits, uint32_t rows, uint32_t V, int32_t* d_out, const SampleScratch& s,
+                       cudaStream_t st);
+// probs[r] = distribution(logits[r], T) (temperature from ctl when given).
+int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, float* d_probs,
+                 const SampleScratch& s, cudaStream_t st);
+// out[b] = sample_from(probs + b*row_stride, u_b): u_b = d_uniforms[b], or Philox(seed | ctl->seed, draw,
+// stream_id, *d_counter) when d_uniforms is null.
+int launch_sample_rows(const float* d_probs, uint32_t rows, uint64_t row_stride, uint32_t V, const double* d_uniforms,
+                       uint64_t seed, uint32_t draw, uint32_t stream_id, const unsigned long long* d_counter,
+                       const RoundCtl* ctl, int32_t* d_out, const SampleScratch& s, cudaStream_t st);
+// verify_speculative for `batch` sequences over probability rows P [batch][k+1][V] and Q [batch][k][V] (null:
+// one-hot drafts).  Uniforms from d_uniforms [batch][k+1], else Philox(seed | ctl->seed, draw, sequence,
+// counter_base | *d_counter).
+int launch_accept(const float* d_P, const float* d_Q, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
+                  const double* d_uniforms, uint64_t seed, uint64_t counter_base,
+                  const unsigned long long* d_counter, const RoundCtl* ctl, uint32_t* d_accepted, int32_t* d_next,
+                  const SampleScratch& s, cudaStream_t st);
 }  // namespace clm

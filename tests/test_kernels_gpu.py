@@ -144,6 +144,29 @@ def test_argmax_matches_reference(ctx):
     assert np.array_equal(host(argmax_token(ctx, dev(g["logits"]))), g["argmax"])
 
 
+def test_argmax_multichunk_ties_and_nans(ctx):
+    """Rows spanning many CTAs: ties across chunks go to the lowest index, a NaN at index 0 pins 0, NaNs
+    elsewhere never win (the reference's `logits[i] > logits[best]` scan)."""
+    from clusterlm_b200.runtime import argmax_token
+
+    V = 128256
+    rows = []
+    r = np.zeros(V, np.float32); r[5000] = 3; r[100000] = 3; rows.append(r)
+    r = np.zeros(V, np.float32); r[0] = np.nan; r[7] = 5; rows.append(r)
+    r = np.ones(V, np.float32); r[9] = np.nan; r[V - 1] = 2; rows.append(r)
+    rows.append(np.full(V, -np.inf, np.float32))
+    r = np.random.default_rng(3).standard_normal(V).astype(np.float32); rows.append(r)
+
+    def ref(l):
+        if np.isnan(l[0]):
+            return 0
+        m = np.where(np.isnan(l), -np.inf, l)
+        return int(np.argmax(m)) if np.any(m > l[0]) else 0
+
+    got = host(argmax_token(ctx, dev(np.stack(rows))))
+    assert list(got) == [ref(x) for x in rows]
+
+
 def test_distribution_matches_reference(ctx):
     from clusterlm_b200.runtime import distribution
 
