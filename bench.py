@@ -72,13 +72,18 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        # nvidia-smi needs a moment before its first line: start timing only once it is sampling
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.lines.clear()
 
     def _read(self):
         for line in self.proc.stdout:

@@ -21,6 +21,7 @@
 #include "bulk.cuh"
 #include "gemv2.cuh"
 #include "gemv_tile.cuh"
+#include "llama.cuh"
 #include "pdl.cuh"
 
 namespace clm {
@@ -119,16 +120,20 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
         const float c = (float)cs, s = (float)sn;
         const float ra = a * c - b * s, rb = a * s + b * c;
         __half* dst;
-        if (head < epi.nh)
+        if (head < epi.nh) {
           dst = epi.q16 + ((size_t)p * epi.nh + head) * hd + 2 * pr;
-        else
-          dst = epi.kpool + (((size_t)page * epi.nkv + (head - epi.nh)) * 64 + slot % 64) * hd + 2 * pr;
+        } else {
+          const int pos = (int)(slot % 64), d0 = 2 * pr;
+          dst = epi.kpool + (((size_t)page * epi.nkv + (head - epi.nh)) * 64 + pos) * hd +
+                8 * kv_k_chunk(d0 >> 3, pos) + (d0 & 7);
+        }
         dst[0] = __float2half_rn(ra);
         dst[1] = __float2half_rn(rb);
       } else {
-        __half* vt = epi.vpool + (((size_t)page * epi.nkv + (head - epi.nh - epi.nkv)) * hd + 2 * pr) * 64 + slot % 64;
-        vt[0] = __float2half_rn(a);
-        vt[64] = __float2half_rn(b);
+        const int pos = (int)(slot % 64), d0 = 2 * pr;
+        __half* vt = epi.vpool + (((size_t)page * epi.nkv + (head - epi.nh - epi.nkv)) * hd + d0) * 64;
+        vt[8 * kv_v_chunk(pos >> 3, d0) + (pos & 7)] = __float2half_rn(a);
+        vt[64 + 8 * kv_v_chunk(pos >> 3, d0 + 1) + (pos & 7)] = __float2half_rn(b);
       }
     }
   } else if (EPI == EPI_SWIGLU_PREP) {

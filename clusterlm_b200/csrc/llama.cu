@@ -158,26 +158,38 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
       for (int j = 0; j < 8; ++j) {
         S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
         const int pos = 16 * (g / 2) + 2 * j + (g % 2);
-        const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)pos * HD + 32 * t);
+        const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)pos * HD);
         uint4 kw[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) kw[u] = kr[u];
+        for (int u = 0; u < 4; ++u) kw[u] = kr[kv_k_chunk(4 * t + u, pos)];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_f16(S[j], word_of(qw0, 2 * kk), word_of(qw1, 2 * kk), word_of(qw0, 2 * kk + 1), word_of(qw1, 2 * kk + 1),
                   word_of(kw, 2 * kk), word_of(kw, 2 * kk + 1));
       }
       float m0 = -INFINITY, m1 = -INFINITY;
+      if (committed_page) {  // every position is visible to every window row
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 8; ++j)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const long long pos = (long long)pg * kPageTokens + 16 * t + 2 * j + e;
-          S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
-          S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
-          m0 = fmaxf(m0, S[j][e]);
-          m1 = fmaxf(m1, S[j][2 + e]);
-        }
+          for (int e = 0; e < 2; ++e) {
+            S[j][e] = v0 ? S[j][e] * scale_log2 : -INFINITY;
+            S[j][2 + e] = v1 ? S[j][2 + e] * scale_log2 : -INFINITY;
+            m0 = fmaxf(m0, S[j][e]);
+            m1 = fmaxf(m1, S[j][2 + e]);
+          }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const long long pos = (long long)pg * kPageTokens + 16 * t + 2 * j + e;
+            S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
+            S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
+            m0 = fmaxf(m0, S[j][e]);
+            m1 = fmaxf(m1, S[j][2 + e]);
+          }
+      }
 #pragma unroll
       for (int o = 1; o <= 2; o <<= 1) {
         m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
@@ -205,8 +217,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
 #pragma unroll 4
       for (int jn = 0; jn < HD / 8; ++jn) {
         float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const uint4* vr = reinterpret_cast<const uint4*>(vs + (size_t)(8 * jn + g) * kPageTokens + 16 * t);
-        const uint4 va = vr[0], vb = vr[1];
+        const int vrow = 8 * jn + g;
+        const uint4* vr = reinterpret_cast<const uint4*>(vs + (size_t)vrow * kPageTokens);
+        const uint4 va = vr[kv_v_chunk(2 * t, vrow)], vb = vr[kv_v_chunk(2 * t + 1, vrow)];
         const uint32_t vw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -266,7 +279,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
   // combine weights w[gi][r] = exp2(m_gi - M) / L, staged in shared memory (after o_s)
   float* o_s = reinterpret_cast<float*>(attn_smem);  // [16][HD], reusing the page buffers
   float* wgt = o_s + 16 * HD;                         // [ngroups][16]
-  for (int i = threadIdx.x; i < ngroups * 16; i += blockDim.x) wgt[i] = __ldcg(allp + (size_t)i * RW + HD);
+  float* lsum = wgt + ngroups * 16;                    // [ngroups][16]
+  for (int i = threadIdx.x; i < ngroups * 16; i += blockDim.x) {
+    wgt[i] = __ldcg(allp + (size_t)i * RW + HD);
+    lsum[i] = __ldcg(allp + (size_t)i * RW + HD + 1);
+  }
   __syncthreads();
   if (threadIdx.x < 16) {
     const int r = threadIdx.x;
@@ -276,7 +293,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     for (int gi = 0; gi < ngroups; ++gi) {
       const float m = wgt[gi * 16 + r];
       const float e = m == -INFINITY ? 0.0f : exp2f(m - M);
-      L += __ldcg(allp + ((size_t)gi * 16 + r) * RW + HD + 1) * e;
+      L += lsum[gi * 16 + r] * e;
       wgt[gi * 16 + r] = e;
     }
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
@@ -331,7 +348,7 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
   const size_t smem = attn_smem_bytes(128);
-  CLM_CHECK((size_t)16 * 128 * 4 + (size_t)((max_pages + kAttnWarps - 1) / kAttnWarps) * 16 * 4 <= smem,
+  CLM_CHECK((size_t)16 * 128 * 4 + (size_t)((max_pages + kAttnWarps - 1) / kAttnWarps) * 32 * 4 <= smem,
             CLM_RESOURCE_EXHAUSTED, "attention: max_context too large for the page-group combine");
   CLM_TRY(ensure_smem(attention_kernel<128>, smem));
   return launch_pdl(attention_kernel<128>, dim3(d.nkv, (max_pages + kAttnWarps - 1) / kAttnWarps, mtiles),

@@ -18,6 +18,14 @@ struct LlamaDims {
   int kvd() const { return nkv * hd; }
 };
 
+// Swizzled 16-byte chunks of a KV page (bank-conflict-free shared-memory reads of the attention kernel):
+//   K page [64 positions][128 head dims] fp16: head-dim chunk c (8 dims) of position pos is stored at chunk
+//     kv_k_chunk(c, pos) of that position's row;
+//   V^T page [128 head dims][64 positions] fp16: position chunk c (8 positions) of head dim d is stored at chunk
+//     kv_v_chunk(c, d) of that dim's row.
+__host__ __device__ __forceinline__ int kv_k_chunk(int c, int pos) { return c ^ (((c >> 3) & 1) << 1) ^ (pos & 1); }
+__host__ __device__ __forceinline__ int kv_v_chunk(int c, int d) { return c ^ (d & 1); }
+
 // Attention partials of one (m-tile, kv head, page): 16 rows x (hd values + m + l).
 inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 2); }
 
