@@ -10,6 +10,7 @@ namespace clm {
 
 constexpr uint32_t kSpinLimit = 1u << 20;  // polls of mbarrier.try_wait (each suspends the thread briefly)
 constexpr int kErrWaitTimeout = 2;         // error-flag value: a bounded wait gave up
+constexpr int kErrPartialSlots = 3;        // error-flag value: a split reduction had more segments than slots
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

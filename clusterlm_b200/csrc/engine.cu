@@ -6,6 +6,7 @@
 // (runtime/domain/src/reference_domain.cpp:297-445): a window writes KV rows at positions base..base+q-1
 // tentatively; commit(n) advances the committed position by n (rows past it are rewritten before any later
 // read, as in the reference); abort drops the window.
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -16,6 +17,7 @@
 #include "codec.cuh"
 #include "bulk.cuh"
 #include "engine.cuh"
+#include "window.cuh"
 #include "gemv.cuh"
 #include "gemv2.cuh"
 #include "llama.cuh"
@@ -52,11 +54,25 @@ struct Session {
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;  // (kind, q, flag) -> executable graph
   std::map<std::tuple<int, int, int>, int> seen;
   std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
+  std::map<int, MkPhase*> mk_phases;  // window megakernel phase tables by q (device arrays)
 };
 
 __global__ void fill_kernel(float* p, float v, uint64_t n) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
     p[i] = v;
+}
+
+// rope[pos][i] = (cos, sin)(pos * theta^(-2i/hd)), evaluated in double and rounded to f32.
+__global__ void rope_table_kernel(float2* __restrict__ out, uint32_t npos, int hd, float theta) {
+  const uint64_t n = (uint64_t)npos * (hd / 2);
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t pos = k / (hd / 2);
+    const int i = (int)(k % (hd / 2));
+    const double inv = exp2(-(double)(2 * i) / (double)hd * log2((double)theta));
+    double sn, cs;
+    sincos((double)pos * inv, &sn, &cs);
+    out[k] = make_float2((float)cs, (float)sn);
+  }
 }
 
 __global__ void round_head_kernel(const SessionState* __restrict__ st, int32_t* __restrict__ win) {
@@ -150,6 +166,13 @@ struct LlamaEngine : clm_b200_engine {
   float* ones_h = nullptr;   // norm weight 1 for stage ends without a following norm
   __half* q16 = nullptr;
   float* attn_part = nullptr;
+  float2* rope = nullptr;    // RoPE (cos, sin) table [max_context][hd/2]
+  // verify-window megakernel (window.cu): grid / ring stages per column-tile count (index nt - 1), barrier counter,
+  // attention segment partials
+  int mk_grid[2] = {0, 0}, mk_stage_count[2] = {0, 0}, mk_stage_bytes[2] = {0, 0};
+  int mk_attn_maxseg = 0;
+  unsigned* mk_bar = nullptr;
+  float* mk_attn_part = nullptr;
   float* logits = nullptr;
   int32_t* tokens = nullptr;
   float* bin = nullptr;
@@ -238,7 +261,7 @@ struct LlamaEngine : clm_b200_engine {
       ek.nh = d.nh;
       ek.nkv = d.nkv;
       ek.hd = d.hd;
-      ek.theta = d.theta;
+      ek.rope = rope;
       ek.pos = pos;
       ek.pages = s.d_pages;
       ek.kpool = kpool[li];
@@ -266,6 +289,114 @@ struct LlamaEngine : clm_b200_engine {
     return CLM_OK;
   }
 
+  // ---- the layers (+ head) of a window as megakernel phases: the same chain as enqueue_layers
+  MkGemv mk_gemv(const Gemv& g, int nt, const XBuf& in, const Epi& epi) const {
+    MkGemv m;
+    m.tiles = static_cast<const uint8_t*>(g.m->data);
+    m.rows = g.m->shape.rows;
+    m.ng = (int)g.m->shape.ng;
+    m.geo = g4_geom(g.m->shape, nt);
+    m.maxseg = g.plan[nt - 1].ksplit;
+    m.in = in;
+    m.epi = epi;
+    m.epi_kind = epi.kind;
+    return m;
+  }
+
+  int enqueue_window_mk(Session& s, int q, cudaStream_t st) {
+    const int nt = q <= 8 ? 1 : 2;
+    auto it = s.mk_phases.find(q);
+    MkPhase* d_ph = nullptr;
+    const int nph = (int)layers.size() * 5 + (has_head ? 1 : 0);
+    if (it != s.mk_phases.end()) {
+      d_ph = it->second;
+    } else {
+      std::vector<MkPhase> ph;
+      const long long* pos = &s.d_state->pos;
+      const int group = d.nh / d.nkv;
+      for (size_t li = 0; li < layers.size(); ++li) {
+        const Layer& L = layers[li];
+        Epi ek = epi_base(EPI_ROPE_KV);
+        ek.nh = d.nh;
+        ek.nkv = d.nkv;
+        ek.hd = d.hd;
+        ek.rope = rope;
+        ek.pos = pos;
+        ek.pages = s.d_pages;
+        ek.kpool = kpool[li];
+        ek.vpool = vpool[li];
+        ek.q16 = q16;
+        MkPhase p0;
+        p0.kind = MK_GEMV;
+        p0.g = mk_gemv(L.qkv, nt, xa, ek);
+        ph.push_back(p0);
+        MkPhase pa;
+        pa.kind = MK_ATTN;
+        pa.a.q16 = q16;
+        pa.a.kpool = kpool[li];
+        pa.a.vpool = vpool[li];
+        pa.a.pages = s.d_pages;
+        pa.a.nh = d.nh;
+        pa.a.nkv = d.nkv;
+        pa.a.mtiles = (q * group + 15) / 16;
+        pa.a.maxseg = mk_attn_maxseg;
+        pa.a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
+        pa.a.part = mk_attn_part;
+        pa.a.counters = acount;
+        pa.a.out = xb;
+        pa.a.out.ss = nullptr;
+        pa.a.hi_scale = hi_scale();
+        pa.a.nt_out = nt;
+        ph.push_back(pa);
+        XBuf ob = xb;
+        ob.ss = nullptr;
+        MkPhase po;
+        po.kind = MK_GEMV;
+        po.g = mk_gemv(L.o, nt, ob, epi_resid(h, L.ffn_norm, xa));
+        ph.push_back(po);
+        Epi es = epi_base(EPI_SWIGLU_PREP);
+        es.ffn = d.F;
+        es.next = xb;
+        MkPhase pg;
+        pg.kind = MK_GEMV;
+        pg.g = mk_gemv(L.gu, nt, xa, es);
+        ph.push_back(pg);
+        const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
+        XBuf db = xb;
+        db.ss = nullptr;
+        MkPhase pd;
+        pd.kind = MK_GEMV;
+        pd.g = mk_gemv(L.down, nt, db, epi_resid(h, wnext, xa));
+        ph.push_back(pd);
+      }
+      if (has_head) {
+        Epi eo = epi_base(EPI_STORE);
+        eo.out = logits;
+        eo.out_ld = d.V;
+        MkPhase pho;
+        pho.kind = MK_GEMV;
+        pho.g = mk_gemv(head, nt, xa, eo);
+        ph.push_back(pho);
+      }
+      CLM_CHECK((int)ph.size() == nph, CLM_INTERNAL, "megakernel phase count");
+      CLM_CUDA(cudaMalloc(&d_ph, ph.size() * sizeof(MkPhase)));
+      CLM_CUDA(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
+      s.mk_phases[q] = d_ph;
+    }
+    MkParams P;
+    P.phases = d_ph;
+    P.nphases = nph;
+    P.q = q;
+    P.pos = &s.d_state->pos;
+    P.part = part;
+    P.counters = gcount;
+    P.barrier = mk_bar;
+    P.err = bad;
+    P.stages = mk_stage_count[nt - 1];
+    P.stage_bytes = mk_stage_bytes[nt - 1];
+    return launch_window_mk(P, d.quant, nt, mk_grid[nt - 1], st);
+  }
+
   // ---- a full window: input (tokens or records) -> layers -> logits or records
   int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
@@ -277,6 +408,12 @@ struct LlamaEngine : clm_b200_engine {
     }
     const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
     CLM_TRY(launch_prep_rows(h, d.H, q, d.H, w0, nt, hi_scale(), xa, true, st));
+    if (mk_grid[nt - 1] > 0 && !layers.empty()) {
+      // layers (and the head) in one cooperative launch
+      CLM_TRY(enqueue_window_mk(s, q, st));
+      if (!has_head) CLM_TRY(launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st));
+      return CLM_OK;
+    }
     CLM_TRY(enqueue_layers(s, q, st));
     if (has_head) {
       Epi eo = epi_base(EPI_STORE);
@@ -385,6 +522,7 @@ struct LlamaEngine : clm_b200_engine {
     if (b) {
       CLM_CUDA(cudaMemset(bad, 0, sizeof(int)));
       if (b == kErrWaitTimeout) return fail(CLM_DEADLINE_EXCEEDED, "a bounded device wait gave up (copy never completed)");
+      if (b == kErrPartialSlots) return fail(CLM_INTERNAL, "a split reduction needed more partial slots than planned");
       return fail(CLM_INVALID_ARGUMENT, "token outside the vocabulary");
     }
     return CLM_OK;
@@ -393,6 +531,8 @@ struct LlamaEngine : clm_b200_engine {
   void release_session(Session& s) {
     for (auto& kv : s.graphs) cudaGraphExecDestroy(kv.second);
     s.graphs.clear();
+    for (auto& kv : s.mk_phases) cudaFree(kv.second);
+    s.mk_phases.clear();
     if (s.d_pages) cudaFree(s.d_pages);
     if (s.d_state) cudaFree(s.d_state);
     for (int32_t p : s.pages) free_pages.push_back(p);
@@ -589,12 +729,41 @@ int llama_prepare(LlamaEngine* e) {
     CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));
     CLM_TRY(e->alloc((void**)&x->sum, xsum_bytes(maxcols)));
     CLM_CUDA(cudaMemset(x->sum, 0, xsum_bytes(maxcols)));
-    CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 16) * 16));
-    x->nss = d.H / 16;
+    CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 128) * 16));
+    x->nss = d.H / 128;
   }
   CLM_TRY(e->ones(&e->ones_h, d.H));
   CLM_TRY(e->alloc_t(&e->q16, (size_t)W * d.qd()));
   CLM_TRY(e->alloc_t(&e->attn_part, (size_t)mtiles * d.nkv * e->max_pages * attn_partial_floats(d.hd)));
+  {
+    const size_t n = (size_t)e->spec.max_context * (d.hd / 2);
+    CLM_TRY(e->alloc_t(&e->rope, n));
+    rope_table_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, e->ctx->stream>>>(e->rope, e->spec.max_context, d.hd,
+                                                                               d.theta);
+    CLM_LAUNCHED("rope_table_kernel");
+  }
+  // window megakernel: one cooperative grid per column-tile count, opt-in with CLM_B200_WINDOW_MK=1 (the
+  // per-kernel chain with programmatic dependent launch is faster on the measured shapes: it overlaps each
+  // kernel's tail with the next kernel's start, which the megakernel's grid barriers cannot)
+  {
+    const char* env = getenv("CLM_B200_WINDOW_MK");
+    const bool want = env && env[0] == '1' && d.hd == 128;
+    const int G = e->ctx->sm_count;
+    e->mk_attn_maxseg = (G + d.nkv - 1) / d.nkv + 1;  // bound for one m-tile (more m-tiles: fewer segments)
+    if (want && !e->layers.empty() && e->mk_attn_maxseg <= 64) {
+      for (int nt = 1; nt <= 2; ++nt) {
+        const GemvShape sh = e->layers[0].qkv.m->shape;
+        const int sbytes = g4_geom(sh, nt).stage_bytes;
+        const int stages = mk_stages(sbytes);
+        e->mk_stage_bytes[nt - 1] = sbytes;
+        e->mk_stage_count[nt - 1] = stages;
+        e->mk_grid[nt - 1] = stages ? mk_grid(e->ctx->device, stages, sbytes, d.quant, nt) : 0;
+        if (e->mk_grid[nt - 1] != G) e->mk_grid[nt - 1] = 0;  // the stream-K bounds assume one CTA per SM
+      }
+      CLM_TRY(e->alloc_t(&e->mk_bar, 1));
+      CLM_TRY(e->alloc_t(&e->mk_attn_part, (size_t)mtiles * d.nkv * e->mk_attn_maxseg * 16 * kMkAttnRowFloats));
+    }
+  }
   CLM_TRY(e->alloc_t(&e->tokens, (size_t)W));
   CLM_TRY(e->alloc_t(&e->bin, (size_t)W * e->floats_per_position()));
   CLM_TRY(e->alloc_t(&e->bout, (size_t)W * e->floats_per_position()));

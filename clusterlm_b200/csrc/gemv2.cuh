@@ -20,7 +20,7 @@ enum { EPI_STORE = 0, EPI_RESID_PREP = 1, EPI_ROPE_KV = 2, EPI_SWIGLU_PREP = 3 }
 struct XBuf {
   uint2* frag = nullptr;   // [SB][nt][16 s][32 lanes]
   float* sum = nullptr;    // [2][SB*8][16 p]
-  float* ss = nullptr;     // [nss][16 p] sum-of-squares partials (row scale), or null
+  float* ss = nullptr;     // [nss][16 p] sum-of-squares partials, one per 128 columns (row scale), or null
   int nss = 0;
 };
 
@@ -39,7 +39,7 @@ struct Epi {
   float hi_scale = 1.0f;
   // EPI_ROPE_KV
   int nh = 0, nkv = 0, hd = 0;
-  float theta = 0.0f;
+  const float2* rope = nullptr;  // [position][hd/2] (cos, sin) of position * theta^(-2i/hd)
   const long long* pos = nullptr;
   const int32_t* parent = nullptr;
   const int32_t* pages = nullptr;

@@ -1,0 +1,353 @@
+// gemv_core.cuh — building blocks of the persistent q-row GEMV shared by the single-matrix kernel (gemv4.cu)
+// and the verify-window megakernel (window.cu): consumer warp roles, the per-unit tensor-core step, row-group
+// flush (segment partials + last-arriver reduction) and the fused epilogues.
+#pragma once
+#include "bulk.cuh"
+#include "gemv2.cuh"
+#include "gemv_tile.cuh"
+#include "llama.cuh"
+
+namespace clm {
+
+constexpr int kG4Consumers = 512;              // 16 consumer warps: 8 row tiles x 2 superblocks
+constexpr int kG4Threads = kG4Consumers + 32;  // + the producer warp
+constexpr int kG4MaxStages = 4;
+constexpr int kG4SumBytes = 16 * 16 * 4;       // one half of a unit's sub-block sums: [16 sub-blocks][16 p] f32
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+__device__ __forceinline__ long long tree_depth4(const int32_t* parent, int i) {
+  long long d = 0;
+  for (int a = parent[i]; a >= 0 && d < 64; a = parent[a]) ++d;
+  return d;
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// CTA whose stream-K range holds unit x.
+__device__ __forceinline__ int cta_of_unit(long long x, long long U, int G) { return (int)(((x + 1) * G - 1) / U); }
+
+// Segments of the group of units [x, y] (the CTA ranges that hold any of them) and this CTA's ordinal among them;
+// u0 = first unit of this CTA's range.  With U >= G every CTA owns at least one unit, so consecutive CTAs are
+// consecutive segments; with U < G every CTA owns at most one unit and CTAs without units sit between them.
+__device__ __forceinline__ void group_segments(long long x, long long y, long long U, int G, long long u0, int* seg,
+                                               int* nseg) {
+  if (U >= G) {
+    const int c_first = cta_of_unit(x, U, G);
+    *seg = (int)blockIdx.x - c_first;
+    *nseg = cta_of_unit(y, U, G) - c_first + 1;
+  } else {
+    *seg = (int)((u0 > x ? u0 : x) - x);
+    *nseg = (int)(y - x + 1);
+  }
+}
+
+struct G4Geom {
+  int sb;          // superblocks per row
+  int ppr;         // units (superblock pairs) per row group
+  int tile_bytes;  // one 16-row x 256-column tile
+  int sb_bytes;    // 8 tiles of one superblock
+  int stage_bytes;
+  int frag_off, sum_off;  // offsets inside a stage: [weights 2 sb][fragments 2 sb x NT][sums half 0][half 1]
+};
+
+// Position in a CTA's unit range without divisions in the loops: (row group, superblock pair) of the unit and
+// (ring slot, phase parity) of its stage.
+struct UnitCursor {
+  int grp = 0, pr = 0, slot = 0;
+  uint32_t phase = 0;
+  __device__ __forceinline__ void next(int ppr, int stages) {
+    if (++pr == ppr) {
+      pr = 0;
+      ++grp;
+    }
+    if (++slot == stages) {
+      slot = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Epilogue over y[p][r] (128 rows of group grp) in shared memory; consumer threads only.
+template <int EPI>
+__device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t rows, int q, const Epi& epi,
+                            float* s_ss) {
+  const int tid = threadIdx.x;
+  const int row0 = grp * 128;
+  if (EPI == EPI_STORE) {
+    for (int i = tid; i < q * 128; i += kG4Consumers) {
+      const int p = i / 128, r = i % 128;
+      if (row0 + r < (int)rows) epi.out[(size_t)p * epi.out_ld + row0 + r] = y[i] * s_scale[p];
+    }
+  } else if (EPI == EPI_RESID_PREP) {
+    for (int i = tid; i < q * 128; i += kG4Consumers) {
+      const int p = i / 128, r = i % 128;
+      if (row0 + r >= (int)rows) continue;
+      float* hp = epi.h + (size_t)p * epi.H + row0 + r;
+      const float hn = *hp + y[i] * s_scale[p];
+      *hp = hn;
+      y[i] = hn;
+    }
+    consumer_sync();
+    const int nt_out = q <= 8 ? 1 : 2;
+    for (int i = tid; i < 8 * 8 * nt_out; i += kG4Consumers) {
+      const int gg = i % 8, p = i / 8;
+      float vals[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const int r = 16 * gg + k;
+        vals[k] = p < q ? y[p * 128 + r] * epi.wnext[row0 + r] : 0.0f;
+      }
+      prep16(vals, nullptr, p, q, (row0 + 16 * gg) / 16, nt_out, epi.hi_scale, epi.next.frag, epi.next.sum, nullptr,
+             epi.H);
+    }
+    // the next consumer's row scale: sum of squares of this group's 128 new residual values, per row
+    if (epi.next.ss) {
+      const int p = tid / 32, ln = tid % 32;  // 16 rows, one warp each
+      float a = 0.0f;
+      if (p < q && row0 + ln < (int)rows) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float v = y[p * 128 + ln + 32 * k];
+          a += v * v;
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (ln == 0) epi.next.ss[(size_t)grp * 16 + p] = a;
+    }
+  } else if (EPI == EPI_ROPE_KV) {
+    const int head = grp, hd = epi.hd;
+    const long long base = *epi.pos;
+    for (int i = tid; i < q * (hd / 2); i += kG4Consumers) {
+      const int p = i / (hd / 2), pr = i % (hd / 2);
+      const float a = y[p * 128 + 2 * pr] * s_scale[p], b = y[p * 128 + 2 * pr + 1] * s_scale[p];
+      const long long slot = base + p;
+      const long long rope_pos = epi.parent ? base + tree_depth4(epi.parent, p) : slot;
+      const int32_t page = epi.pages[slot / 64];
+      if (head < epi.nh + epi.nkv) {
+        const float2 cs = epi.rope[(size_t)rope_pos * (hd / 2) + pr];
+        const float c = cs.x, s = cs.y;
+        const float ra = a * c - b * s, rb = a * s + b * c;
+        __half* dst;
+        if (head < epi.nh) {
+          dst = epi.q16 + ((size_t)p * epi.nh + head) * hd + 2 * pr;
+        } else {
+          const int pos = (int)(slot % 64), d0 = 2 * pr;
+          dst = epi.kpool + (((size_t)page * epi.nkv + (head - epi.nh)) * 64 + pos) * hd +
+                8 * kv_k_chunk(d0 >> 3, pos) + (d0 & 7);
+        }
+        dst[0] = __float2half_rn(ra);
+        dst[1] = __float2half_rn(rb);
+      } else {
+        const int pos = (int)(slot % 64), d0 = 2 * pr;
+        __half* vt = epi.vpool + (((size_t)page * epi.nkv + (head - epi.nh - epi.nkv)) * hd + d0) * 64;
+        vt[8 * kv_v_chunk(pos >> 3, d0) + (pos & 7)] = __float2half_rn(a);
+        vt[64 + 8 * kv_v_chunk(pos >> 3, d0 + 1) + (pos & 7)] = __float2half_rn(b);
+      }
+    }
+  } else if (EPI == EPI_SWIGLU_PREP) {
+    // rows [0, 64) gate, [64, 128) up of ffn indices grp*64 + [0, 64)
+    for (int i = tid; i < q * 64; i += kG4Consumers) {
+      const int p = i / 64, k = i % 64;
+      const float gv = y[p * 128 + k] * s_scale[p], uv = y[p * 128 + 64 + k] * s_scale[p];
+      y[p * 128 + k] = gv / (1.0f + expf(-gv)) * uv;
+    }
+    consumer_sync();
+    const int nt_out = q <= 8 ? 1 : 2;
+    for (int i = tid; i < 4 * 8 * nt_out; i += kG4Consumers) {
+      const int gg = i % 4, p = i / 4;
+      float vals[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) vals[k] = p < q ? y[p * 128 + 16 * gg + k] : 0.0f;
+      prep16(vals, nullptr, p, q, (grp * 64 + 16 * gg) / 16, nt_out, epi.hi_scale, epi.next.frag, epi.next.sum,
+             nullptr, epi.ffn);
+    }
+  }
+  (void)s_ss;
+  consumer_sync();  // y is reused by the next group
+}
+
+
+// Epilogue kind chosen at run time (the megakernel's phases).
+__device__ __forceinline__ void g4_epilogue_rt(int kind, float* y, const float* s_scale, int grp, uint32_t rows,
+                                               int q, const Epi& epi) {
+  switch (kind) {
+    case EPI_STORE: g4_epilogue<EPI_STORE>(y, s_scale, grp, rows, q, epi, nullptr); break;
+    case EPI_RESID_PREP: g4_epilogue<EPI_RESID_PREP>(y, s_scale, grp, rows, q, epi, nullptr); break;
+    case EPI_ROPE_KV: g4_epilogue<EPI_ROPE_KV>(y, s_scale, grp, rows, q, epi, nullptr); break;
+    default: g4_epilogue<EPI_SWIGLU_PREP>(y, s_scale, grp, rows, q, epi, nullptr); break;
+  }
+}
+
+// Row scale (folded rmsnorm) 1/sqrt(sum(ss)/ss_n + eps) per window row from the input's sum-of-squares partials
+// (1 without partials), in two steps so that the partials' load latency overlaps the first units: g4_ss_load at
+// the start of a GEMV (registers only), g4_ss_finish before the first flush.  Consumer threads only; s_red holds
+// kG4Consumers floats; at most 2 * kG4Consumers / 16 partials per row.
+struct G4SsPre {
+  float a = 0.0f, b = 0.0f;
+};
+__device__ __forceinline__ G4SsPre g4_ss_load(const XBuf& in) {
+  G4SsPre r;
+  const int tid = threadIdx.x, p = tid % 16, c = tid / 16;
+  constexpr int kStride = kG4Consumers / 16;
+  if (in.ss) {
+    if (c < in.nss) r.a = in.ss[(size_t)c * 16 + p];
+    if (c + kStride < in.nss) r.b = in.ss[(size_t)(c + kStride) * 16 + p];
+  }
+  return r;
+}
+__device__ __forceinline__ void g4_ss_finish(const G4SsPre& pre, const XBuf& in, const Epi& epi, int q, float* s_red,
+                                             float* s_scale) {
+  const int tid = threadIdx.x;
+  s_red[tid] = pre.a + pre.b;
+  consumer_sync();
+  if (tid < 16) {
+    float sc = 1.0f;
+    if (in.ss && tid < q) {
+      float tot = 0.0f;
+      for (int c = 0; c < kG4Consumers / 16; ++c) tot += s_red[c * 16 + tid];
+      sc = 1.0f / sqrtf(tot / epi.ss_n + epi.eps);
+    }
+    s_scale[tid] = sc;
+  }
+  consumer_sync();
+}
+
+// Accumulators of one consumer warp: row tile rt = warp % 8, superblock hh = warp / 8 of each unit, even and
+// odd k-steps in separate registers.
+template <int NT>
+struct G4Acc {
+  float v[2][NT][4];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[a][nt][i] = 0.0f;
+  }
+  // dst[p][r] (+)= this warp's sums for its rows
+  __device__ __forceinline__ void put(float* dst, bool add, int q, int rt, int lane) const {
+    const int t = lane % 4, g = lane / 4, r0 = rt * 16 + g, r1 = r0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int p0 = nt * 8 + 2 * t;
+      const float v0 = v[0][nt][0] + v[1][nt][0], v1 = v[0][nt][1] + v[1][nt][1];
+      const float v2 = v[0][nt][2] + v[1][nt][2], v3 = v[0][nt][3] + v[1][nt][3];
+      if (p0 < q) {
+        dst[p0 * 128 + r0] = add ? dst[p0 * 128 + r0] + v0 : v0;
+        dst[p0 * 128 + r1] = add ? dst[p0 * 128 + r1] + v2 : v2;
+      }
+      if (p0 + 1 < q) {
+        dst[(p0 + 1) * 128 + r0] = add ? dst[(p0 + 1) * 128 + r0] + v1 : v1;
+        dst[(p0 + 1) * 128 + r1] = add ? dst[(p0 + 1) * 128 + r1] + v3 : v3;
+      }
+    }
+  }
+};
+
+// One unit (superblock pair of a row group) staged at `st`: this warp's tile of superblock hh.
+template <typename Raw, int NT>
+__device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom& geo, int nsb, int warp, int lane,
+                                                G4Acc<NT>& acc) {
+  const int rt = warp % kGemvWarps, hh = warp / kGemvWarps, t = lane % 4, g = lane / 4;
+  if (hh >= nsb) return;
+  const uint2* xf = reinterpret_cast<const uint2*>(st + geo.frag_off) + hh * NT * 512;
+  const float* s0 = reinterpret_cast<const float*>(st + geo.sum_off);
+  const float* s1 = s0 + kG4SumBytes / 4;
+  uint32_t mg, mg8;
+  Raw r;
+  load_raw_s(r, st + (size_t)hh * geo.sb_bytes + (size_t)rt * geo.tile_bytes, lane);
+  tile_mmas<NT>(r, t, xf, lane, acc.v, mg, mg8);
+  // min / bias term of this superblock: A = -m per (row, sub-block) in this warp's k-half of the pair,
+  // B = fp16 hi + lo of the pair's sub-block sums
+  const uint32_t a0 = hh == 0 ? mg : 0u, a1 = hh == 0 ? mg8 : 0u, a2 = hh == 1 ? mg : 0u, a3 = hh == 1 ? mg8 : 0u;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int p = nt * 8 + g;
+    float v[4];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int sub = h2 * 8 + 2 * t + e;
+        v[2 * h2 + e] = h2 < nsb ? s0[sub * 16 + p] + s1[sub * 16 + p] : 0.0f;
+      }
+    // fp16 hi + lo split of each sum (paired conversions)
+    const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v[0] - f01.x, v[1] - f01.y);
+    const __half2 l23 = __floats2half2_rn(v[2] - f23.x, v[3] - f23.y);
+    mma16816(acc.v[0][nt], a0, a1, a2, a3, h2u(h01), h2u(h23));
+    mma16816(acc.v[1][nt], a0, a1, a2, a3, h2u(l01), h2u(l23));
+  }
+}
+
+// Flush row group `grp` of a stream-K range: fold the two superblock warps into y (fixed order); a group owned by
+// this CTA alone goes to the epilogue, otherwise the segment partial is published and the last CTA to arrive sums
+// the segments in index order and runs the epilogue.  Consumer threads only.
+template <int NT>
+__device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
+                         long long U, int G, long long u0, int ppr, int q, uint32_t rows, int epi_kind, const Epi& epi,
+                         float* s_scale, int* s_last, const G4SsPre& ss_pre, const XBuf& in, bool& scale_ready,
+                         float* s_red) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
+  if (!scale_ready) {
+    g4_ss_finish(ss_pre, in, epi, q, s_red, s_scale);
+    scale_ready = true;
+  }
+  const int rt = warp % kGemvWarps, hh = warp / kGemvWarps;
+  if (hh == 1) acc.put(y, false, q, rt, lane);
+  consumer_sync();
+  if (hh == 0) acc.put(y, true, q, rt, lane);
+  consumer_sync();
+  int seg = 0, nseg = 1;
+  group_segments((long long)grp * ppr, (long long)grp * ppr + ppr - 1, U, G, u0, &seg, &nseg);
+  if (nseg > maxseg) {  // partial slots too few for this launch shape: never write past them
+    if (tid == 0 && epi.err) atomicExch(epi.err, kErrPartialSlots);
+    return;
+  }
+  if (nseg > 1) {
+    float* mine = part + ((size_t)grp * maxseg + seg) * q * 128;
+    for (int i = tid; i < q * 128; i += kG4Consumers) mine[i] = y[i];
+    __threadfence();
+    consumer_sync();
+    if (tid == 0) *s_last = atomicAdd(&counters[grp], 1) == nseg - 1;
+    consumer_sync();
+    if (!*s_last) return;
+    __threadfence();
+    const float* all = part + (size_t)grp * maxseg * q * 128;
+    for (int i = tid; i < q * 128; i += kG4Consumers) {
+      float a = 0.0f;
+      int k = 0;
+      for (; k + 4 <= nseg; k += 4) {
+        const float v0 = __ldcg(all + (size_t)k * q * 128 + i), v1 = __ldcg(all + (size_t)(k + 1) * q * 128 + i);
+        const float v2 = __ldcg(all + (size_t)(k + 2) * q * 128 + i), v3 = __ldcg(all + (size_t)(k + 3) * q * 128 + i);
+        a += v0;
+        a += v1;
+        a += v2;
+        a += v3;
+      }
+      for (; k < nseg; ++k) a += __ldcg(all + (size_t)k * q * 128 + i);
+      y[i] = a;
+    }
+    if (tid == 0) counters[grp] = 0;
+    consumer_sync();
+  }
+  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi);
+}
+
+// Geometry of a tiled matrix in the persistent GEMV for `nt` column tiles.
+inline G4Geom g4_geom(const GemvShape& s, int nt) {
+  G4Geom geo;
+  geo.sb = (int)s.sb;
+  geo.ppr = (int)(s.sb + 1) / 2;
+  geo.tile_bytes = s.tile_bytes;
+  geo.sb_bytes = kGemvWarps * s.tile_bytes;
+  geo.frag_off = 2 * geo.sb_bytes;
+  geo.sum_off = geo.frag_off + 2 * nt * kXfragSbBytes;
+  geo.stage_bytes = geo.sum_off + 2 * kG4SumBytes;
+  return geo;
+}
+
+}  // namespace clm

@@ -22,9 +22,10 @@ int ensure_smem(void (*kernel)(KArgs...), size_t bytes) {
   static thread_local size_t last_bytes[64];
   const size_t slot = (reinterpret_cast<uintptr_t>(reinterpret_cast<const void*>(kernel)) / 16 + dev) % 64;
   if (last_kernel[slot] == reinterpret_cast<const void*>(kernel) && last_bytes[slot] >= bytes) return CLM_OK;
-  CLM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  const size_t want = bytes > 200 * 1024 ? bytes : 200 * 1024;
+  CLM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want));
   last_kernel[slot] = reinterpret_cast<const void*>(kernel);
-  last_bytes[slot] = 200 * 1024;
+  last_bytes[slot] = want;
   return CLM_OK;
 }
 
