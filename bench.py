@@ -249,6 +249,66 @@ def run_reference(args, world, rank):
 
 # --------------------------------------------------------------------------- GPU side
 
+def profile_case(args) -> bool:
+    return args.layers != 32 or args.context != CONTEXT
+
+
+# acceptance micro-workload: 64 sequences x q = 8 (k = 7 drafts) x vocab 151,936, target logits ~ N(0, 3^2), draft
+# logits = target + N(0, 0.5^2), drafts sampled from the draft distribution, Philox seed 0, T = 1
+C2_B, C2_Q, C2_V = 64, 8, 151936
+
+
+def acceptance_micro(ctx, dev, peak, with_cpu):
+    """clm_b200_accept_logits on the acceptance micro-workload, device-resident inputs, event-timed."""
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.runtime import accept_logits
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    k = C2_Q - 1
+    tl = torch.randn((C2_B, C2_Q, C2_V), generator=g, device=dev) * 3.0
+    dl = tl[:, :k] + torch.randn((C2_B, k, C2_V), generator=g, device=dev) * 0.5
+    drafts = torch.multinomial(torch.softmax(dl.reshape(-1, C2_V), dim=-1), 1, generator=g).reshape(C2_B, k)
+    drafts = drafts.to(torch.int32).contiguous()
+    for _ in range(3):
+        accept_logits(ctx, tl, dl, drafts, 1.0, seed=0, counter_base=0)
+    torch.cuda.synchronize(dev)
+    n = 10
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for i in range(n):
+        acc, nxt = accept_logits(ctx, tl, dl, drafts, 1.0, seed=0, counter_base=i)
+    s1.record()
+    torch.cuda.synchronize(dev)
+    sec = s0.elapsed_time(s1) / 1e3 / n
+    # logits read once plus the residual sample's two rows per sequence
+    algo = (C2_B * (C2_Q + k) + 2 * C2_B) * C2_V * 4
+    out = {"config": f"{C2_B} sequences x q={C2_Q} (k={k}) x vocab {C2_V}, logits N(0,3^2), drafts +N(0,0.5^2), "
+                     "Philox seed 0, T=1",
+           "ms_per_call": sec * 1e3, "sequences_per_s": C2_B / sec,
+           "accepted_mean": float(acc.float().mean().item()),
+           "roofline": {"bound": "hbm", "algorithmic_bytes": algo, "achieved": algo / sec / 1e9, "peak": peak,
+                        "unit": "GB/s", "frac": algo / sec / 1e9 / peak}}
+    if with_cpu:
+        from oracle.oracle_py import Oracle
+
+        orc = Oracle()
+        t0 = time.perf_counter()
+        t = tl[0].cpu().numpy()
+        d = dl[0].cpu().numpy()
+        P = np.stack([orc.distribution(r, 1.0) for r in t])
+        Q = np.stack([orc.distribution(r, 1.0) for r in d])
+        us = np.array([orc.philox_uniform(0, j, 0, 0, 0) for j in range(k + 1)])
+        orc.verify(P, drafts[0].cpu().numpy(), Q, us)
+        one = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": 1.0 / one, "unit": "sequences/s", "cores": 1, "kind": "port",
+                               "sample": "oracle distribution (stable sort, double) + verify_speculative, one "
+                                         f"sequence ({C2_Q + k} rows) timed ({one:.2f} s)"}
+    del tl, dl
+    return out
+
+
 def run_b200(args, world, rank, local):
     import numpy as np
     import torch
@@ -328,12 +388,13 @@ def run_b200(args, world, rank, local):
     achieved = total_b / window_s / 1e9
     eng.close_session(1)
     eng.close()
+    micro = acceptance_micro(ctx, dev, peak, not args.no_cpu) if (world == 1 and not profile_case(args)) else None
     ctx.close()
 
     if rank != 0:
         return
     cpu = None
-    profile = args.layers != LLAMA3_8B.n_layers or context != CONTEXT
+    profile = profile_case(args)
     if world == 1 and not args.no_cpu and not profile:
         cb = CpuBaseline(os.cpu_count() or 1)
         r = cb.round_s()
@@ -361,6 +422,8 @@ def run_b200(args, world, rank, local):
     if cpu:
         line["cpu_baseline"] = {"value": cpu["value"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
                                 "sample": cpu["sample"]}
+    if micro:
+        line["acceptance_micro"] = micro
     print(json.dumps(line), flush=True)
 
 

@@ -51,6 +51,7 @@ struct Session {
   long long pos_bound = 0;    // upper bound while device-driven rounds are in flight
   bool pos_stale = false;     // device rounds ran since the last read of d_state->pos
   uint32_t outstanding = 0;  // q of the outstanding window, 0 = none
+  bool tree = false;         // the outstanding window is a tree (commit with clm_b200_commit_path)
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;  // (kind, q, flag) -> executable graph
   std::map<std::tuple<int, int, int>, int> seen;
   std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
@@ -72,6 +73,41 @@ __global__ void rope_table_kernel(float2* __restrict__ out, uint32_t npos, int h
     double sn, cs;
     sincos((double)pos * inv, &sn, &cs);
     out[k] = make_float2((float)cs, (float)sn);
+  }
+}
+
+// Keeps the accepted tree path: the KV rows of window nodes path[i] move to window slot i (base + i), in every
+// layer and kv head.  One CTA per (layer, kv head); all sources are read before any row is written (a path is
+// increasing, but a destination can be a later move's source).  K rows are swizzled by position parity and V^T
+// columns by head-dim parity (llama.cuh), so elements are moved one by one with both layouts' index maps.
+__global__ void kv_compact_kernel(__half* const* __restrict__ kpools, __half* const* __restrict__ vpools,
+                                  const int32_t* __restrict__ pages, const long long* __restrict__ d_pos,
+                                  const int32_t* __restrict__ path, int n, int nkv, int hd) {
+  extern __shared__ __half kv_rows[];  // [n][2][hd]
+  const int layer = blockIdx.x, kvh = blockIdx.y;
+  __half* K = kpools[layer];
+  __half* Vt = vpools[layer];
+  const long long base = *d_pos;
+  auto k_at = [&](long long slot, int dd) -> __half* {
+    const int pos = (int)(slot % 64);
+    return K + (((size_t)pages[slot / 64] * nkv + kvh) * 64 + pos) * hd + 8 * kv_k_chunk(dd >> 3, pos) + (dd & 7);
+  };
+  auto v_at = [&](long long slot, int dd) -> __half* {
+    const int pos = (int)(slot % 64);
+    return Vt + (((size_t)pages[slot / 64] * nkv + kvh) * hd + dd) * 64 + 8 * kv_v_chunk(pos >> 3, dd) + (pos & 7);
+  };
+  for (int j = threadIdx.x; j < n * hd; j += blockDim.x) {
+    const int i = j / hd, dd = j % hd;
+    const long long src = base + path[i];
+    kv_rows[(2 * i) * hd + dd] = *k_at(src, dd);
+    kv_rows[(2 * i + 1) * hd + dd] = *v_at(src, dd);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < n * hd; j += blockDim.x) {
+    const int i = j / hd, dd = j % hd;
+    if (path[i] == i) continue;
+    *k_at(base + i, dd) = kv_rows[(2 * i) * hd + dd];
+    *v_at(base + i, dd) = kv_rows[(2 * i + 1) * hd + dd];
   }
 }
 
@@ -157,6 +193,8 @@ struct LlamaEngine : clm_b200_engine {
   float *out_norm = nullptr, *mtp_ffn_norm = nullptr, *mtp_out_norm = nullptr;
   // KV pools per layer
   std::vector<__half*> kpool, vpool;
+  __half** d_kpools = nullptr;  // device copies of the pool pointers (tree-path KV compaction)
+  __half** d_vpools = nullptr;
   // window buffers
   float* h = nullptr;
   float* part = nullptr;     // GEMV split partials (last-CTA reduction)
@@ -180,6 +218,7 @@ struct LlamaEngine : clm_b200_engine {
   float* h_mtp = nullptr;
   float* draft_logits = nullptr;
   int32_t* win = nullptr;
+  int32_t* parents = nullptr;  // tree window: parent node of each window row (-1: the committed context)
   float* tprobs = nullptr;    // distribution rows of the window's logits [W][V]
   float* dprobs = nullptr;    // distribution rows of the MTP drafts [W][V]
   int32_t* am = nullptr;      // row argmaxes [W]
@@ -251,7 +290,7 @@ struct LlamaEngine : clm_b200_engine {
   }
 
   // ---- the layer range over q rows; h holds the stage input and xa its first norm's preparation
-  int enqueue_layers(Session& s, int q, cudaStream_t st) {
+  int enqueue_layers(Session& s, int q, const int32_t* parent, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
     const long long* pos = &s.d_state->pos;
     for (size_t li = 0; li < layers.size(); ++li) {
@@ -267,9 +306,10 @@ struct LlamaEngine : clm_b200_engine {
       ek.kpool = kpool[li];
       ek.vpool = vpool[li];
       ek.q16 = q16;
+      ek.parent = parent;
       CLM_TRY(gemv(L.qkv, q, xa, ek, st));
       // attention -> xb (W_o input)
-      CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, nullptr, q, d, max_pages, attn_part, acount,
+      CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, parent, q, d, max_pages, attn_part, acount,
                                nt, hi_scale(), xb.frag, xb.sum, bad, st));
       XBuf ob = xb;
       ob.ss = nullptr;
@@ -398,7 +438,7 @@ struct LlamaEngine : clm_b200_engine {
   }
 
   // ---- a full window: input (tokens or records) -> layers -> logits or records
-  int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st) {
+  int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st, const int32_t* parent = nullptr) {
     const int nt = q <= 8 ? 1 : 2;
     if (has_tokens) {
       CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(64), 0, st, d_tok, q, (int)d.V, tokens, bad));
@@ -408,13 +448,13 @@ struct LlamaEngine : clm_b200_engine {
     }
     const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
     CLM_TRY(launch_prep_rows(h, d.H, q, d.H, w0, nt, hi_scale(), xa, true, st));
-    if (mk_grid[nt - 1] > 0 && !layers.empty()) {
+    if (mk_grid[nt - 1] > 0 && !layers.empty() && parent == nullptr) {
       // layers (and the head) in one cooperative launch
       CLM_TRY(enqueue_window_mk(s, q, st));
       if (!has_head) CLM_TRY(launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st));
       return CLM_OK;
     }
-    CLM_TRY(enqueue_layers(s, q, st));
+    CLM_TRY(enqueue_layers(s, q, parent, st));
     if (has_head) {
       Epi eo = epi_base(EPI_STORE);
       eo.out = logits;
@@ -775,6 +815,7 @@ int llama_prepare(LlamaEngine* e) {
     CLM_TRY(e->alloc_t(&e->draft_logits, (size_t)W * d.V));
   }
   CLM_TRY(e->alloc_t(&e->win, (size_t)W + 1));
+  CLM_TRY(e->alloc_t(&e->parents, (size_t)W));
   if (e->has_head) {
     CLM_TRY(e->alloc_t(&e->tprobs, (size_t)W * d.V));
     CLM_TRY(e->alloc_t(&e->dprobs, (size_t)W * d.V));
@@ -903,11 +944,17 @@ int llama_run_window_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t
   return CLM_OK;
 }
 
-int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens,
-                        const float* h_in, float* h_out, float* h_logits) {
+static int run_window_host(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_parents,
+                           const int32_t* h_tokens, const float* h_in, float* h_out, float* h_logits) {
   CLM_TRY(engine_enter(e));
   cudaStream_t st = e->ctx->stream;
   Session* s = nullptr;
+  if (h_parents != nullptr) {
+    // a tree: every node's parent is an earlier node or -1 (the committed context)
+    for (uint32_t i = 0; i < q; ++i)
+      CLM_CHECK(h_parents[i] >= -1 && h_parents[i] < (int32_t)i, CLM_INVALID_ARGUMENT,
+                "tree window: parent[i] must be -1 or an earlier node");
+  }
   CLM_TRY(run_window_common(e, id, base, q, st, &s));
   const size_t rec = (size_t)q * e->floats_per_position() * sizeof(float);
   if (e->has_tokens) {
@@ -919,7 +966,14 @@ int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, con
     CLM_CHECK(h_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
     CLM_CUDA(cudaMemcpyAsync(e->bin, h_in, rec, cudaMemcpyHostToDevice, st));
   }
-  CLM_TRY(e->run_graph(*s, 0, (int)q, 0, st, [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs); }));
+  if (h_parents != nullptr) {
+    CLM_CUDA(cudaMemcpyAsync(e->parents, h_parents, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    CLM_TRY(e->run_graph(*s, 4, (int)q, 0, st,
+                         [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs, e->parents); }));
+  } else {
+    CLM_TRY(e->run_graph(*s, 0, (int)q, 0, st,
+                         [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs); }));
+  }
   if (e->has_head) {
     if (h_logits)
       CLM_CUDA(cudaMemcpyAsync(h_logits, e->logits, (size_t)q * e->d.V * sizeof(float), cudaMemcpyDeviceToHost, st));
@@ -928,6 +982,66 @@ int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, con
   }
   CLM_CUDA(cudaStreamSynchronize(st));
   s->outstanding = q;
+  s->tree = h_parents != nullptr;
+  return CLM_OK;
+}
+
+int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens,
+                     const float* h_in, float* h_out, float* h_logits) {
+  return run_window_host(e, id, base, q, nullptr, h_tokens, h_in, h_out, h_logits);
+}
+
+int llama_run_tree(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_parents,
+                   const int32_t* h_tokens, const float* h_in, float* h_out, float* h_logits) {
+  CLM_CHECK(h_parents != nullptr, CLM_INVALID_ARGUMENT, "null parents");
+  return run_window_host(e, id, base, q, h_parents, h_tokens, h_in, h_out, h_logits);
+}
+
+int llama_commit_path(LlamaEngine* e, uint64_t id, const int32_t* h_path, uint32_t n) {
+  CLM_TRY(engine_enter(e));
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_CHECK(s->outstanding > 0, CLM_FAILED_PRECONDITION, "no outstanding window");
+  CLM_CHECK(h_path != nullptr && n >= 1 && n <= s->outstanding, CLM_INVALID_ARGUMENT, "path must hold 1..q nodes");
+  std::vector<int32_t> parents(s->outstanding, -1);
+  if (s->tree)
+    CLM_CUDA(cudaMemcpy(parents.data(), e->parents, s->outstanding * sizeof(int32_t), cudaMemcpyDeviceToHost));
+  else
+    for (uint32_t i = 0; i < s->outstanding; ++i) parents[i] = (int32_t)i - 1;
+  for (uint32_t i = 0; i < n; ++i) {
+    CLM_CHECK(h_path[i] >= 0 && (uint32_t)h_path[i] < s->outstanding, CLM_INVALID_ARGUMENT, "path node out of range");
+    CLM_CHECK(parents[h_path[i]] == (i == 0 ? -1 : h_path[i - 1]), CLM_INVALID_ARGUMENT,
+              "path must run from a root (parent -1) along parent links");
+  }
+  {
+    const int rc = e->check_bad(e->ctx->stream);
+    if (rc != CLM_OK) {
+      s->outstanding = 0;
+      return rc;
+    }
+  }
+  cudaStream_t st = e->ctx->stream;
+  bool moved = false;
+  for (uint32_t i = 0; i < n; ++i) moved |= h_path[i] != (int32_t)i;
+  if (moved && !e->layers.empty()) {
+    if (e->d_kpools == nullptr) {
+      CLM_TRY(e->alloc_t(&e->d_kpools, e->layers.size()));
+      CLM_TRY(e->alloc_t(&e->d_vpools, e->layers.size()));
+      CLM_CUDA(cudaMemcpy(e->d_kpools, e->kpool.data(), e->layers.size() * sizeof(__half*), cudaMemcpyHostToDevice));
+      CLM_CUDA(cudaMemcpy(e->d_vpools, e->vpool.data(), e->layers.size() * sizeof(__half*), cudaMemcpyHostToDevice));
+    }
+    CLM_CUDA(cudaMemcpyAsync(e->parents, h_path, n * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const size_t smem = (size_t)n * 2 * e->d.hd * sizeof(__half);
+    kv_compact_kernel<<<dim3((unsigned)e->layers.size(), (unsigned)e->d.nkv), 256, smem, st>>>(
+        e->d_kpools, e->d_vpools, s->d_pages, &s->d_state->pos, e->parents, (int)n, e->d.nkv, e->d.hd);
+    CLM_LAUNCHED("kv_compact_kernel");
+  }
+  s->pos += n;
+  s->pos_bound = s->pos;
+  s->outstanding = 0;
+  s->tree = false;
+  CLM_CUDA(cudaMemcpyAsync(&s->d_state->pos, &s->pos, sizeof(long long), cudaMemcpyHostToDevice, st));
+  CLM_CUDA(cudaStreamSynchronize(st));
   return CLM_OK;
 }
 
@@ -944,6 +1058,7 @@ int llama_commit(LlamaEngine* e, uint64_t id, uint32_t accepted) {
       return rc;
     }
   }
+  CLM_CHECK(!s->tree, CLM_FAILED_PRECONDITION, "a tree window is committed with clm_b200_commit_path");
   s->pos += accepted;
   s->pos_bound = s->pos;
   s->outstanding = 0;

@@ -31,6 +31,9 @@ int llama_run_window_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t
 int llama_run_window(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_tokens, const float* h_in,
                      float* h_out, float* h_logits);
 int llama_commit(LlamaEngine* e, uint64_t id, uint32_t accepted);
+int llama_run_tree(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_parents,
+                   const int32_t* h_tokens, const float* h_in, float* h_out, float* h_logits);
+int llama_commit_path(LlamaEngine* e, uint64_t id, const int32_t* h_path, uint32_t n);
 int llama_abort(LlamaEngine* e, uint64_t id);
 int llama_session_position(const LlamaEngine* e, uint64_t id, uint64_t* committed);
 int llama_mtp_draft(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,

@@ -87,6 +87,19 @@ int clm_b200_commit(clm_b200_engine* e, uint64_t id, uint32_t accepted) {
   return e->family == CLM_FAMILY_LLAMA ? llama_commit(llama(e), id, accepted) : fixture_commit(fixture(e), id, accepted);
 }
 
+int clm_b200_run_tree_window(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* h_parents,
+                             const int32_t* h_tokens, const float* h_in, float* h_out, float* h_logits) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "tree windows are served by the Llama-family engine");
+  return llama_run_tree(llama(e), id, base, q, h_parents, h_tokens, h_in, h_out, h_logits);
+}
+
+int clm_b200_commit_path(clm_b200_engine* e, uint64_t id, const int32_t* h_path, uint32_t n) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "tree windows are served by the Llama-family engine");
+  return llama_commit_path(llama(e), id, h_path, n);
+}
+
 int clm_b200_abort(clm_b200_engine* e, uint64_t id) {
   CLM_TRY(enter(e));
   return e->family == CLM_FAMILY_LLAMA ? llama_abort(llama(e), id) : fixture_abort(fixture(e), id);

@@ -687,6 +687,128 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t first, uint32_t c
 }
 
 // ---------------------------------------------------------------------------------------------------
+// distribution() with top-k / top-p (sampling.cpp:51-86) exactly as the reference orders it: the sum of e in
+// index order, a stable descending sort of e, the top-p cumulative and the kept sum in sorted order.  One CTA per
+// row; the sort is a stable LSD radix sort on 4-bit digits of ~bits(e) (descending e, ties by ascending index).
+// ---------------------------------------------------------------------------------------------------
+constexpr int kTruncThreads = 512;
+
+// Block-wide exclusive sum of one uint32 per thread.
+__device__ uint32_t block_exclusive_sum_u32(uint32_t v) {
+  __shared__ uint32_t ws[32];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  uint32_t inc = v;
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t o = __shfl_up_sync(0xffffffffu, inc, d);
+    if (lane >= d) inc += o;
+  }
+  if (lane == 31) ws[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < nw ? ws[lane] : 0u;
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t o = __shfl_up_sync(0xffffffffu, w, d);
+      if (lane >= d) w += o;
+    }
+    if (lane < nw) ws[lane] = w;  // inclusive warp prefix
+  }
+  __syncthreads();
+  const uint32_t r = (warp > 0 ? ws[warp - 1] : 0u) + inc - v;
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kTruncThreads) truncated_distribution_kernel(
+    const float* __restrict__ logits, uint32_t V, float T, uint32_t top_k, float top_p, double* __restrict__ e_all,
+    unsigned long long* __restrict__ key_a, unsigned long long* __restrict__ key_b, uint32_t* __restrict__ idx_a,
+    uint32_t* __restrict__ idx_b, float* __restrict__ probs) {
+  __shared__ uint32_t cnt[16][kTruncThreads];  // per-thread digit counts, then scatter offsets
+  __shared__ uint32_t s_keep;
+  __shared__ double s_sum, s_kept;
+  const uint32_t row = blockIdx.x, tid = threadIdx.x;
+  const float* l = logits + (size_t)row * V;
+  double* e = e_all + (size_t)row * V;
+  unsigned long long* ka = key_a + (size_t)row * V;
+  unsigned long long* kb = key_b + (size_t)row * V;
+  uint32_t* ia = idx_a + (size_t)row * V;
+  uint32_t* ib = idx_b + (size_t)row * V;
+  float* out = probs + (size_t)row * V;
+  // max (std::max_element: NaNs never win unless first; finite logits expected)
+  float m = -FLT_MAX;
+  for (uint32_t i = tid; i < V; i += kTruncThreads) m = fmaxf(m, l[i]);
+  m = block_max(m);
+  for (uint32_t i = tid; i < V; i += kTruncThreads) {
+    const double v = exp((double)__fsub_rn(l[i], m) / (double)T);
+    e[i] = v;
+    ka[i] = ~(unsigned long long)__double_as_longlong(v);  // ascending ~bits = descending e (e >= 0)
+    ia[i] = i;
+    out[i] = 0.0f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double sum = 0.0;
+    for (uint32_t i = 0; i < V; ++i) sum += e[i];
+    s_sum = sum;
+  }
+  // stable LSD radix sort: each thread owns a contiguous chunk, so equal digits keep their order
+  const uint32_t chunk = (V + kTruncThreads - 1) / kTruncThreads;
+  const uint32_t c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
+  for (int pass = 0; pass < 16; ++pass) {
+    const int shift = 4 * pass;
+    for (int d = 0; d < 16; ++d) cnt[d][tid] = 0;
+    for (uint32_t i = c0; i < c1; ++i) ++cnt[(ka[i] >> shift) & 15][tid];
+    __syncthreads();
+    {  // exclusive scan in (digit, thread) order: thread t scans linear entries [16t, 16t + 16)
+      uint32_t* lin = &cnt[0][0];
+      uint32_t local = 0;
+      for (int j = 0; j < 16; ++j) local += lin[16 * tid + j];
+      const uint32_t before = block_exclusive_sum_u32(local);
+      uint32_t run = before;
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t c = lin[16 * tid + j];
+        lin[16 * tid + j] = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    for (uint32_t i = c0; i < c1; ++i) {
+      const unsigned long long k = ka[i];
+      const uint32_t dst = cnt[(k >> shift) & 15][tid]++;
+      kb[dst] = k;
+      ib[dst] = ia[i];
+    }
+    __syncthreads();
+    unsigned long long* tk = ka;
+    ka = kb;
+    kb = tk;
+    uint32_t* ti = ia;
+    ia = ib;
+    ib = ti;
+  }
+  // ia is the stable descending order
+  if (tid == 0) {
+    uint32_t keep = V;
+    if (top_k > 0 && top_k < keep) keep = top_k;
+    if (top_p < 1.0f) {
+      double acc = 0.0;
+      for (uint32_t i = 0; i < keep; ++i) {
+        acc += e[ia[i]] / s_sum;
+        if (acc >= (double)top_p) {
+          keep = i + 1;
+          break;
+        }
+      }
+    }
+    double kept = 0.0;
+    for (uint32_t i = 0; i < keep; ++i) kept += e[ia[i]];
+    s_keep = keep;
+    s_kept = kept;
+  }
+  __syncthreads();
+  for (uint32_t i = tid; i < s_keep; i += kTruncThreads) out[ia[i]] = (float)(e[ia[i]] / s_kept);
+}
+
+// ---------------------------------------------------------------------------------------------------
 // host launchers
 // ---------------------------------------------------------------------------------------------------
 int launch_argmax_rows(const float* d_logits, uint32_t rows, uint32_t V, int32_t* d_out, const SampleScratch& s,
@@ -802,8 +924,21 @@ int clm_b200_distribution_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_
     CLM_LAUNCHED("onehot_kernel");
     return CLM_OK;
   }
-  CLM_CHECK(top_k == 0 && top_p >= 1.0f, CLM_UNIMPLEMENTED,
-            "top-k / top-p truncation is not implemented on the device yet (temperature-only distributions)");
+  if (top_k > 0 || top_p < 1.0f) {
+    // exact reference ordering (sort + serial sums): one CTA per row, scratch 28 bytes per entry
+    void* scr = nullptr;
+    const size_t n = (size_t)rows * vocab;
+    CLM_TRY(ctx_scratch(ctx, n * (8 + 8 + 8 + 4 + 4) + 1024, &scr));
+    double* e = static_cast<double*>(scr);
+    unsigned long long* ka = reinterpret_cast<unsigned long long*>(e + n);
+    unsigned long long* kb = ka + n;
+    uint32_t* ia = reinterpret_cast<uint32_t*>(kb + n);
+    uint32_t* ib = ia + n;
+    truncated_distribution_kernel<<<rows, kTruncThreads, 0, st>>>(d_logits, vocab, temperature, top_k, top_p, e, ka,
+                                                                   kb, ia, ib, d_probs);
+    CLM_LAUNCHED("truncated_distribution_kernel");
+    return CLM_OK;
+  }
   SampleScratch s;
   CLM_TRY(abi_scratch(ctx, rows, 0, vocab, 0, st, &s, nullptr));
   return launch_probs(d_logits, rows, vocab, temperature, nullptr, d_probs, s, st);

@@ -177,6 +177,28 @@ class Engine:
              None if has_head else _vp(d_out.data_ptr()), _vp(d_out.data_ptr()) if has_head else None,
              None if stream is None else _vp(stream))
 
+    def run_tree_window(self, session: int, base: int, parents, tokens=None, records=None):
+        """Tree window: node i's parent is parents[i] (an earlier node or -1); logits or records per node."""
+        parents = _i32(parents)
+        fpp = self.fpp
+        if tokens is not None:
+            tokens = _i32(tokens)
+        else:
+            records = _f32(records)
+        q = parents.size
+        has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
+        out = np.zeros((q, self.vocab if has_head else fpp), np.float32)
+        call("clm_b200_run_tree_window", self.h, session, base, q, parents.ctypes.data_as(_vp),
+             None if tokens is None else tokens.ctypes.data_as(_vp),
+             None if records is None else records.ctypes.data_as(_vp),
+             None if has_head else out.ctypes.data_as(_vp), out.ctypes.data_as(_vp) if has_head else None)
+        return out
+
+    def commit_path(self, session: int, path):
+        """Keeps the root-to-node path (node indices) of the outstanding window."""
+        path = _i32(path)
+        call("clm_b200_commit_path", self.h, session, path.ctypes.data_as(_vp), path.size)
+
     def commit(self, session: int, accepted: int):
         call("clm_b200_commit", self.h, session, accepted)
 

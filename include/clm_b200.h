@@ -117,8 +117,9 @@ CLM_API int clm_b200_matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix
 CLM_API int clm_b200_argmax_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab, int32_t* d_out,
                          void* stream);
 /* distribution() per row (sampling.cpp:51-86): temperature <= 0 gives one-hot argmax; otherwise
- * exp(double(l - max)/T) normalised in double and rounded to f32.  top_k / top_p truncation is
- * applied on the probability order (ties by lower index, as the stable sort). */
+ * exp(double(l - max)/T) normalised in double and rounded to f32.  With top_k > 0 or top_p < 1 the rows are
+ * truncated exactly as the reference orders them (stable descending sort, ties by lower index; top-p
+ * cumulative and kept sum in sorted order). */
 CLM_API int clm_b200_distribution_rows(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab,
                                float temperature, uint32_t top_k, float top_p, float* d_probs, void* stream);
 /* sample_from() per row with one caller-supplied uniform per row (sampling.cpp:88-101).  The result is
@@ -204,6 +205,17 @@ CLM_API int clm_b200_run_window_device(clm_b200_engine* e, uint64_t session, uin
                                        void* stream);
 /* Keeps the first `accepted` positions of the outstanding window (1..q): commit_window, reference_domain.cpp:297-317. */
 CLM_API int clm_b200_commit(clm_b200_engine* e, uint64_t session, uint32_t accepted);
+/* Tree verification window (no reference counterpart: the reference's windows are linear,
+ * coordinator.cpp:1244-1255).  Node i has parent h_parents[i] (an earlier node, or -1 for the committed
+ * context); it is placed at KV slot base + i, rotated (RoPE) at position base + depth(i), and attends to the
+ * committed context and its own ancestors.  Llama-family engines. */
+CLM_API int clm_b200_run_tree_window(clm_b200_engine* e, uint64_t session, uint64_t base, uint32_t positions,
+                                     const int32_t* h_parents, const int32_t* h_tokens, const float* h_in,
+                                     float* h_out, float* h_logits);
+/* Commits the accepted root-to-node path h_path[0..n) of the outstanding (tree or linear) window: the path's KV
+ * rows move to slots base..base+n-1 and the committed position advances by n (commit_window's keep-prefix rule
+ * for a tree). */
+CLM_API int clm_b200_commit_path(clm_b200_engine* e, uint64_t session, const int32_t* h_path, uint32_t n);
 /* Drops the outstanding window (abort_window, reference_domain.cpp:319-329). */
 CLM_API int clm_b200_abort(clm_b200_engine* e, uint64_t session);
 CLM_API int clm_b200_session_position(const clm_b200_engine* e, uint64_t session, uint64_t* committed);

@@ -172,13 +172,28 @@ def test_distribution_matches_reference(ctx):
 
     g = load("sampling.npz")
     for pi, p in enumerate(g["dist_params"]):
-        if p[1] != 0 or p[2] < 1.0:
-            continue  # top-k / top-p are not on the device yet
-        got = host(distribution(ctx, dev(g["logits"]), float(p[0])))
+        got = host(distribution(ctx, dev(g["logits"]), float(p[0]), int(p[1]), float(p[2])))
         want = g["dist"][pi]
         ulps = np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
         assert ulps.max() <= 1, (p, ulps.max())
         assert (ulps == 0).mean() > 0.99
+
+
+def test_truncated_distribution_large_vocab_matches_oracle(ctx, oracle):
+    """top-k / top-p at a 128K vocabulary with ties: same kept set and values as the reference ordering."""
+    from clusterlm_b200.runtime import distribution
+
+    V = 128256
+    rng = np.random.default_rng(11)
+    logits = (rng.standard_normal((3, V)) * 2).astype(np.float32)
+    logits[1, 1000:1100] = logits[1].max()  # a block of tied maxima
+    for T, k, pp in [(1.0, 50, 1.0), (0.7, 0, 0.9), (1.3, 2000, 0.5), (1.0, 120, 0.95)]:
+        got = host(distribution(ctx, dev(logits), T, k, pp))
+        for r in range(3):
+            want = oracle.distribution(logits[r], T, k, pp)
+            assert np.array_equal(got[r] > 0, want > 0), (T, k, pp, r)
+            ulps = np.abs(got[r].view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+            assert ulps.max() <= 1, (T, k, pp, r, ulps.max())
 
 
 def test_sample_from_bit_exact(ctx):

@@ -252,3 +252,60 @@ def test_window_megakernel_matches_chain_and_oracle(ctx, oracle, monkeypatch):
         mk.commit(1, keep)
         ch.commit(1, keep)
         pos += keep
+
+
+def _tree16():
+    # root 0; children 1..4 of 0; two children each of 1..4 (5..12); one child each of 5, 6, 7 (13, 14, 15)
+    parents = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 6, 7]
+    return np.array(parents, np.int32)
+
+
+@pytest.mark.parametrize("quant", ["q4_k", "q8_0"])
+def test_tree_window_matches_oracle_and_path_commit(ctx, oracle, quant):
+    """A 16-node draft tree (4, 2, 1 branching): every node attends to the committed context and its ancestors and
+    is rotated at base + depth; committing a root-to-leaf path compacts its KV rows, so the next linear window sees
+    exactly the context a linear run of that path would have produced."""
+    from llama_oracle import LlamaOracle
+
+    geo = small_geo(quant)
+    e = make_engine(ctx, geo, max_context=256, max_window=16)
+    m = LlamaOracle(oracle, geo)
+    e.open_session(1)
+    rng = np.random.default_rng(3)
+    pos = 0
+    pre = rng.integers(0, geo.vocab, 12).astype(np.int32)
+    assert rel(e.run_window(1, pos, tokens=pre), m.window(pre, pos)) < 2e-2
+    e.commit(1, 12)
+    pos = 12
+    parents = _tree16()
+    toks = rng.integers(0, geo.vocab, 16).astype(np.int32)
+    got = e.run_tree_window(1, pos, parents, tokens=toks)
+    want = m.logits(m.run_layers(m.embed(toks), pos, parent=parents))
+    assert rel(got, want) < 2e-2, rel(got, want)
+    path = [0, 2, 7, 15]
+    e.commit_path(1, path)
+    for L in m.layers:  # the oracle keeps the same rows
+        m.kc[L][pos:pos + 4] = m.kc[L][[pos + i for i in path]]
+        m.vc[L][pos:pos + 4] = m.vc[L][[pos + i for i in path]]
+    pos += 4
+    assert e.position(1) == pos
+    nxt = rng.integers(0, geo.vocab, 4).astype(np.int32)
+    assert rel(e.run_window(1, pos, tokens=nxt), m.window(nxt, pos)) < 2e-2
+
+
+def test_tree_window_refusals(ctx):
+    from clusterlm_b200 import ClmError
+
+    geo = small_geo()
+    e = make_engine(ctx, geo, max_context=64, max_window=16)
+    e.open_session(1)
+    toks = np.zeros(4, np.int32)
+    with pytest.raises(ClmError):
+        e.run_tree_window(1, 0, [-1, 0, 3, 1], tokens=toks)  # parent after the node
+    e.run_tree_window(1, 0, [-1, 0, 0, 1], tokens=toks)
+    with pytest.raises(ClmError):
+        e.commit(1, 2)  # a tree is committed by path
+    with pytest.raises(ClmError):
+        e.commit_path(1, [0, 2, 3])  # 3's parent is 1, not 2
+    e.commit_path(1, [0, 1, 3])
+    assert e.position(1) == 3
