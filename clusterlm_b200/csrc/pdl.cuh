@@ -43,7 +43,8 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // The implicit default streams keep plain serialisation (griddepcontrol.wait then returns at once).
+  cfg.numAttrs = (st == nullptr || st == cudaStreamLegacy || st == cudaStreamPerThread) ? 0 : 1;
   CLM_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
   ++t_kernel_launches;
   return CLM_OK;

@@ -28,8 +28,15 @@ def _ptr(t: torch.Tensor | None):
     return _vp(t.data_ptr())
 
 
+# cudaStreamLegacy: the legacy default stream named explicitly (a NULL stream argument selects the context's own
+# non-blocking stream in the C ABI, which is not ordered with torch's default stream).
+_LEGACY_STREAM = 0x1
+
+
 def _stream() -> _vp:
-    return _vp(torch.cuda.current_stream().cuda_stream)
+    """The stream the C ABI call runs on: torch's current stream, so torch work before and after is ordered."""
+    h = torch.cuda.current_stream().cuda_stream
+    return _vp(h if h else _LEGACY_STREAM)
 
 
 def device_count() -> int:
