@@ -15,7 +15,11 @@ e2e          the same through clm_b200_spec_round (host API: round parameters ho
 roofline     the verify window (32 layers + head, q = 4): algorithmic bytes / event-timed window duration
 cpu_baseline the oracle's refmath-order CPU restatement on this host's cores, a bounded sample (one decoder
              layer at context 4096 + the LM head + one MTP step, q = 4) extrapolated to a round
-With N > 1 (torchrun) every rank runs an independent replica on its own GPU (weak scaling); value is the sum.
+With N > 1 (torchrun, one process per GPU) the model is split into N pipeline stages (layer ranges balanced by
+the bytes each stage streams per round; the tail holds the LM head and the MTP drafter), joined by device links
+over NVLink, with N sequences in flight (--inflight) so that every stage is busy: weak scaling (each GPU streams
+about one model's worth of bytes per N rounds).  value = emitted tokens of all sequences / max-over-ranks device
+time; the roofline is the per-GPU HBM stream of the timed rounds.
 """
 from __future__ import annotations
 
@@ -39,6 +43,13 @@ SEED = 0
 METRIC = "accepted tok/s, 8B-shape Q4_K spec decode q=4"
 
 # algorithmic bytes of one q = 4 verify window (weights of 32 layers + LM head, KV of 4096 positions)
+def round_bytes(geo, context, q=Q):
+    """Algorithmic bytes of one speculative round: the verify window plus q-1 MTP draft steps (MTP block + head)."""
+    total, _, _ = window_bytes(geo, context)
+    H, F, V = geo.hidden, geo.ffn, geo.vocab
+    return total + (q - 1) * (3 * F * H + V * H) * 144 // 256
+
+
 def window_bytes(geo, context):
     H, qd, kvd, F, V = geo.hidden, geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim, geo.ffn, geo.vocab
     per_layer = (qd * H + 2 * kvd * H + H * qd + 3 * F * H) * 144 // 256
@@ -123,8 +134,10 @@ def dist_setup():
     if world > 1:
         import datetime
 
+        import torch
         import torch.distributed as dist
 
+        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     return world, rank, local
 
@@ -407,7 +420,7 @@ def run_b200(args, world, rank, local):
         "config": {"workload": (f"llama3-8b-shape q4_k spec decode q=4 ctx={context} batch=1 mtp=1-layer T=1"
                                 + (f" PROFILE CASE ({geo.n_layers} layers)" if profile else "")),
                    "q": Q, "context": context, "temperature": TEMPERATURE,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": "single",
                    "l2": "inputs larger than L2 (4.8 GB weights streamed per round)",
                    "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted / args.steps},
         "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": (Q + 1) * 4 + 4},
@@ -427,6 +440,118 @@ def run_b200(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_pipeline(args, world, rank, local):
+    """N > 1: the stage pipeline (clusterlm_b200.pipeline) with `inflight` sequences."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from clusterlm_b200.engine import LLAMA3_8B
+    from clusterlm_b200.pipeline import StagePipeline, format_plan, parse_plan, plan_stages
+    from clusterlm_b200.runtime import Context
+
+    dev = torch.device(f"cuda:{local}")
+    geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
+    context = args.context
+    S = args.inflight or world
+    plan = parse_plan(args.plan, geo.n_layers) if args.plan else plan_stages(geo, world, Q, context)
+    e2e_n = max(4, args.steps // 2)
+    max_ctx = context + (args.warmup + args.steps + e2e_n + 8) * (Q + 1) + 64
+    ctx = Context(local)
+
+    def gather(obj):
+        res = [None] * world
+        dist.all_gather_object(res, obj)
+        return res
+
+    pipe = StagePipeline(ctx, geo, plan, rank, max_ctx, S, gather, max_window=16, timeout_s=60.0, weight_seed=SEED)
+    stream = torch.cuda.ExternalStream(pipe.engine.stream(), device=dev)
+    t0 = time.perf_counter()
+    for s in range(S):
+        prompt = np.random.default_rng(1234 + s).integers(0, geo.vocab, context).astype(np.int32)
+        pipe.open_session(s + 1)
+        row = pipe.prefill(s + 1, prompt)
+        pipe.begin(s + 1, row, Q, TEMPERATURE, SEED)
+    pipe.status()
+    barrier(world)
+    prefill_s = max_over_ranks(world, time.perf_counter() - t0, dev)
+    n_rounds = args.warmup + args.steps
+    toks = torch.zeros((n_rounds, S, Q + 1), dtype=torch.int32, device=dev)
+    cnt = torch.zeros((n_rounds, S), dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    for k in range(args.warmup):
+        for s in range(S):
+            pipe.round(s + 1, Q, TEMPERATURE, SEED, toks[k, s], cnt[k, s])
+    pipe.status()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(args.warmup, n_rounds):
+        for s in range(S):
+            pipe.round(s + 1, Q, TEMPERATURE, SEED, toks[k, s], cnt[k, s])
+    end.record(stream)
+    pipe.status()
+    clk = clocks.stop()
+    launches = pipe.engine.last_launches() * args.steps * S
+    elapsed = start.elapsed_time(end) / 1e3
+    emitted = int(cnt[args.warmup:].sum().item()) if pipe.is_tail else 0
+    elapsed_max = max_over_ranks(world, elapsed, dev)
+    emitted_all = sum_over_ranks(world, emitted, dev)
+    launches_all = sum_over_ranks(world, launches, dev)
+    value = emitted_all / elapsed_max
+
+    # e2e: the same rounds with the emitted tokens read back to pinned host memory every round (the tail) and the
+    # round parameters copied host -> device every round (every stage), timed on the host, max over ranks
+    host = torch.zeros((e2e_n, S, Q + 1), dtype=torch.int32).pin_memory()
+    hcnt = torch.zeros((e2e_n, S), dtype=torch.int32).pin_memory()
+    e_toks = torch.zeros((S, Q + 1), dtype=torch.int32, device=dev)
+    e_cnt = torch.zeros(S, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for k in range(e2e_n):
+            for s in range(S):
+                pipe.round(s + 1, Q, TEMPERATURE, SEED, e_toks[s], e_cnt[s], stream.cuda_stream)
+                if pipe.is_tail:
+                    host[k, s].copy_(e_toks[s], non_blocking=True)
+                    hcnt[k, s].copy_(e_cnt[s], non_blocking=True)
+    stream.synchronize()
+    e2e_s = max_over_ranks(world, time.perf_counter() - t0, dev)
+    e2e_emitted = sum_over_ranks(world, int(hcnt.sum().item()) if pipe.is_tail else 0, dev)
+    pipe.status()
+    pipe.close(lambda: barrier(world))
+    ctx.close()
+    if rank != 0:
+        return
+    peak, peak_kind = load_peaks()
+    per_gpu = S * args.steps * round_bytes(geo, context) / world / elapsed_max / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
+        "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
+        "config": {"workload": (f"llama3-8b-shape q4_k spec decode q=4 ctx={context} mtp=1-layer T=1, "
+                                f"{world}-stage pipeline, {S} sequences in flight"
+                                + (f" PROFILE CASE ({geo.n_layers} layers)" if profile_case(args) else "")),
+                   "q": Q, "context": context, "temperature": TEMPERATURE, "parallelism": f"pp{world}",
+                   "plan": format_plan(plan), "inflight": S, "step": f"one round of each of the {S} sequences",
+                   "l2": "inputs larger than L2 (each stage streams its weights every round)",
+                   "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted_all / (args.steps * S)},
+        "e2e": {"value": e2e_emitted / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16 * S * world,
+                "d2h_bytes_per_step": ((Q + 1) * 4 + 4) * S},
+        "gpu_launches": int(launches_all),
+        "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "pipeline rounds, per GPU (all stages' weights + KV + MTP drafts / N / device time)",
+                     "algorithmic_bytes_per_round": round_bytes(geo, context)},
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -437,12 +562,16 @@ def main():
     # smaller cases for profiler captures (the line is then marked PROFILE CASE and is not a bench result)
     ap.add_argument("--context", type=int, default=CONTEXT, help="prefilled context (profiling)")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
+    ap.add_argument("--inflight", type=int, default=0, help="sequences in flight with N > 1 (default N)")
+    ap.add_argument("--plan", default="", help="stage plan BEGIN-END@gK,... with N > 1 (default: byte-balanced)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif world > 1:
+            run_pipeline(args, world, rank, local)
         else:
             run_b200(args, world, rank, local)
     finally:

@@ -80,7 +80,17 @@ _SIGS = {
     "clm_b200_spec_begin": (_i, [_vp, _u64, _vp, _u32, _vp]),
     "clm_b200_spec_round": (_i, [_vp, _u64, _vp, _vp, _vp]),
     "clm_b200_spec_round_device": (_i, [_vp, _u64, _vp, _vp, _vp, _vp]),
+    "clm_b200_link_create": (_i, [_vp, _i, _u32, _u64, C.c_double, C.POINTER(_vp)]),
+    "clm_b200_link_export": (_i, [_vp, _vp]),
+    "clm_b200_link_connect": (_i, [_vp, _vp]),
+    "clm_b200_link_destroy": (_i, [_vp]),
+    "clm_b200_pipe_attach": (_i, [_vp, _vp, _vp]),
+    "clm_b200_pipe_prefill": (_i, [_vp, _u64, _vp, _u32, _vp]),
+    "clm_b200_pipe_begin": (_i, [_vp, _u64, _u32, _vp, _vp]),
+    "clm_b200_pipe_round": (_i, [_vp, _u64, _vp, _vp, _vp, _vp]),
+    "clm_b200_pipe_status": (_i, [_vp, _vp]),
 }
+LINK_HANDLE_BYTES = 128  # CLM_B200_LINK_HANDLE_BYTES
 
 
 def _bind():

@@ -17,6 +17,7 @@
 #include "codec.cuh"
 #include "bulk.cuh"
 #include "engine.cuh"
+#include "link.cuh"
 #include "window.cuh"
 #include "gemv.cuh"
 #include "gemv2.cuh"
@@ -33,7 +34,7 @@ struct SessionState {  // device-resident, one per session
   int next_token;              // token to feed at `pos`
   unsigned accepted;           // drafts accepted in the last round
   int count;                   // tokens emitted by the last round
-  int pad;
+  unsigned commit_in;          // pipeline: positions committed at the start of the current round (from the link)
 };
 
 struct Gemv {
@@ -56,6 +57,8 @@ struct Session {
   std::map<std::tuple<int, int, int>, int> seen;
   std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
   std::map<int, MkPhase*> mk_phases;  // window megakernel phase tables by q (device arrays)
+  int32_t* d_win = nullptr;    // pipeline tail: this session's current window tokens [W + 1]
+  float* d_dprobs = nullptr;   // pipeline tail: draft distributions of the current window [W][V]
 };
 
 __global__ void fill_kernel(float* p, float v, uint64_t n) {
@@ -148,6 +151,13 @@ __global__ void round_commit_kernel(SessionState* __restrict__ st, const int32_t
   st->round += 1;
 }
 
+// Commits a prefill chunk of q positions (auto_commit).
+__global__ void pos_advance_kernel(SessionState* __restrict__ st, int q) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) st->pos += q;
+}
+
 __global__ void set_next_kernel(SessionState* __restrict__ st, const int32_t* __restrict__ tok) {
   griddep_wait();
   griddep_launch();
@@ -230,6 +240,10 @@ struct LlamaEngine : clm_b200_engine {
   int* bad = nullptr;
   unsigned long long* zero_counter = nullptr;
   RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
+  // stage pipeline (link.cuh): input and output links and their device views
+  clm_b200_link* pipe_in = nullptr;
+  clm_b200_link* pipe_out = nullptr;
+  LinkDev lin, lout;
   std::map<uint64_t, std::unique_ptr<Session>> sessions;
   std::vector<void*> allocations;
   uint64_t weight_bytes = 0;
@@ -487,26 +501,75 @@ struct LlamaEngine : clm_b200_engine {
   // ---- one speculative round on a WHOLE engine
   // Temperature and seed are read from `ctl` (device); `stochastic` selects the acceptance kernels.
   int enqueue_round(Session& s, int q, bool stochastic, cudaStream_t st) {
-    const unsigned long long* ctr = &s.d_state->round;
-    CLM_TRY(launch_pdl(round_head_kernel, dim3(1), dim3(32), 0, st, (const SessionState*)s.d_state, win));
-    for (int j = 0; j + 1 < q; ++j) {
-      CLM_TRY(enqueue_mtp_step(win + j, draft_logits + (size_t)j * d.V, st));
-      CLM_TRY(sample_token(draft_logits + (size_t)j * d.V, stochastic, 1.0f, 0, (uint32_t)j, 1u, ctr, ctl,
-                           dprobs + (size_t)j * d.V, win + j + 1, st));
-    }
+    CLM_TRY(enqueue_drafts(s, q, stochastic, win, dprobs, st));
     CLM_TRY(enqueue_window(s, q, win, st));
+    return enqueue_accept(s, q, stochastic, win, dprobs, st);
+  }
+
+  // The window's tokens: w[0] = the session's next token, w[1..q-1] = MTP drafts chained from it (greedy, or
+  // sampled with Philox draws (draw j, stream 1, session round) from distribution rows kept in dp[j]).
+  int enqueue_drafts(Session& s, int q, bool stochastic, int32_t* w, float* dp, cudaStream_t st) {
+    const unsigned long long* ctr = &s.d_state->round;
+    CLM_TRY(launch_pdl(round_head_kernel, dim3(1), dim3(32), 0, st, (const SessionState*)s.d_state, w));
+    for (int j = 0; j + 1 < q; ++j) {
+      CLM_TRY(enqueue_mtp_step(w + j, draft_logits + (size_t)j * d.V, st));
+      CLM_TRY(sample_token(draft_logits + (size_t)j * d.V, stochastic, 1.0f, 0, (uint32_t)j, 1u, ctr, ctl,
+                           dp + (size_t)j * d.V, w + j + 1, st));
+    }
+    return CLM_OK;
+  }
+
+  // Acceptance of the window w (logits in `logits`, draft distributions dp) and the round's commit.
+  int enqueue_accept(Session& s, int q, bool stochastic, const int32_t* w, const float* dp, cudaStream_t st) {
+    const unsigned long long* ctr = &s.d_state->round;
     if (stochastic) {
-      CLM_TRY(launch_probs(logits, q, d.V, 1.0f, ctl, tprobs, samp, st));
-      CLM_TRY(launch_accept(tprobs, q > 1 ? dprobs : nullptr, win + 1, 1, q - 1, d.V, nullptr, 0, 0, ctr, ctl, acc,
-                            nxt, samp, st));
+      // the window's distributions are evaluated from its logits where acceptance reads them
+      CLM_TRY(launch_row_stats(logits, q, d.V, 1.0f, ctl, 0, samp, st));
+      AcceptRows src;
+      src.LP = logits;
+      src.Q = q > 1 ? dp : nullptr;
+      CLM_TRY(launch_accept(src, w + 1, 1, q - 1, d.V, nullptr, 0, 0, ctr, ctl, acc, nxt, samp, st));
     } else {
       CLM_TRY(launch_argmax_rows(logits, q, d.V, am, samp, st));
-      CLM_TRY(launch_pdl(greedy_decide_kernel, dim3(1), dim3(32), 0, st, (const int32_t*)am, q, (const int32_t*)win,
-                         acc, nxt));
+      CLM_TRY(launch_pdl(greedy_decide_kernel, dim3(1), dim3(32), 0, st, (const int32_t*)am, q, w, acc, nxt));
     }
-    CLM_TRY(launch_pdl(round_commit_kernel, dim3(1), dim3(32), 0, st, s.d_state, (const int32_t*)win,
-                       (const uint32_t*)acc, (const int32_t*)nxt, emitted, count));
-    return CLM_OK;
+    return launch_pdl(round_commit_kernel, dim3(1), dim3(32), 0, st, s.d_state, w, (const uint32_t*)acc,
+                      (const int32_t*)nxt, emitted, count);
+  }
+
+  // ---- stage pipeline (clm_b200_pipe_*)
+  uint32_t record_bytes(int q) const { return (uint32_t)(((size_t)q * floats_per_position() * 4 + 15) / 16 * 16); }
+  static uint32_t token_bytes(int q) { return (uint32_t)((q * 4 + 15) / 16 * 16); }
+
+  // One round of session s on this stage (see clm_b200_pipe_round).
+  int enqueue_pipe_round(Session& s, int q, bool stochastic, cudaStream_t st) {
+    long long* pos = &s.d_state->pos;
+    unsigned* cin = &s.d_state->commit_in;
+    if (spec.role == CLM_ROLE_PREFIX) {
+      CLM_TRY(launch_link_recv(lin, win, (uint32_t)((wmax() + 1) * 4), (uint32_t)q, pos, cin, bad, st));
+    } else {
+      // the tail committed its own previous round at acceptance
+      CLM_TRY(launch_link_recv(lin, bin, record_bytes(wmax()), (uint32_t)q,
+                               spec.role == CLM_ROLE_TAIL ? nullptr : pos, cin, bad, st));
+    }
+    if (spec.role != CLM_ROLE_TAIL) {
+      CLM_TRY(enqueue_window(s, q, win, st));
+      return launch_link_send(lout, bout, record_bytes(q), cin, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
+    }
+    CLM_TRY(enqueue_window(s, q, s.d_win, st));
+    CLM_TRY(enqueue_accept(s, q, stochastic, s.d_win, s.d_dprobs, st));
+    CLM_TRY(enqueue_drafts(s, q, stochastic, s.d_win, s.d_dprobs, st));
+    return launch_link_send(lout, s.d_win, token_bytes(q), count, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
+  }
+
+  // One prompt chunk of session s on this stage, committed at once (the prefix's tokens are already in win).
+  int enqueue_pipe_prefill(Session& s, int q, cudaStream_t st) {
+    if (spec.role != CLM_ROLE_PREFIX)
+      CLM_TRY(launch_link_recv(lin, bin, record_bytes(wmax()), (uint32_t)q, nullptr, nullptr, bad, st));
+    CLM_TRY(enqueue_window(s, q, win, st));
+    if (spec.role != CLM_ROLE_TAIL)
+      CLM_TRY(launch_link_send(lout, bout, record_bytes(q), nullptr, (uint32_t)q, LINK_MSG_PREFILL, bad, st));
+    return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, st, s.d_state, q);
   }
 
   // One token from one logits row: argmax, or sample_from(distribution(row, T)) with the Philox uniform
@@ -563,6 +626,9 @@ struct LlamaEngine : clm_b200_engine {
       CLM_CUDA(cudaMemset(bad, 0, sizeof(int)));
       if (b == kErrWaitTimeout) return fail(CLM_DEADLINE_EXCEEDED, "a bounded device wait gave up (copy never completed)");
       if (b == kErrPartialSlots) return fail(CLM_INTERNAL, "a split reduction needed more partial slots than planned");
+      if (b == kErrLinkTimeout)
+        return fail(CLM_DEADLINE_EXCEEDED, "a stage link wait gave up (the peer stage stopped or fell behind)");
+      if (b == kErrLinkMismatch) return fail(CLM_VERSION_MISMATCH, "a stage link message has another window width");
       return fail(CLM_INVALID_ARGUMENT, "token outside the vocabulary");
     }
     return CLM_OK;
@@ -575,6 +641,10 @@ struct LlamaEngine : clm_b200_engine {
     s.mk_phases.clear();
     if (s.d_pages) cudaFree(s.d_pages);
     if (s.d_state) cudaFree(s.d_state);
+    if (s.d_win) cudaFree(s.d_win);
+    if (s.d_dprobs) cudaFree(s.d_dprobs);
+    s.d_win = nullptr;
+    s.d_dprobs = nullptr;
     for (int32_t p : s.pages) free_pages.push_back(p);
     s.pages.clear();
     s.d_pages = nullptr;
@@ -805,8 +875,11 @@ int llama_prepare(LlamaEngine* e) {
     }
   }
   CLM_TRY(e->alloc_t(&e->tokens, (size_t)W));
-  CLM_TRY(e->alloc_t(&e->bin, (size_t)W * e->floats_per_position()));
-  CLM_TRY(e->alloc_t(&e->bout, (size_t)W * e->floats_per_position()));
+  // (+4 floats: link messages are whole 16-byte units)
+  CLM_TRY(e->alloc_t(&e->bin, (size_t)W * e->floats_per_position() + 4));
+  CLM_TRY(e->alloc_t(&e->bout, (size_t)W * e->floats_per_position() + 4));
+  CLM_CUDA(cudaMemset(e->bin, 0, ((size_t)W * e->floats_per_position() + 4) * sizeof(float)));
+  CLM_CUDA(cudaMemset(e->bout, 0, ((size_t)W * e->floats_per_position() + 4) * sizeof(float)));
   CLM_TRY(e->alloc_t(&e->bad, 1));
   CLM_CUDA(cudaMemset(e->bad, 0, sizeof(int)));
   if (e->has_head) CLM_TRY(e->alloc_t(&e->logits, (size_t)W * d.V));
@@ -874,6 +947,12 @@ int llama_session_open(LlamaEngine* e, uint64_t id) {
   if (err == cudaSuccess)
     err = cudaMemcpy(s->d_pages, s->pages.data(), s->pages.size() * sizeof(int32_t), cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = cudaMemset(s->d_state, 0, sizeof(SessionState));
+  if (err == cudaSuccess && e->spec.role == CLM_ROLE_TAIL && e->has_mtp) {
+    // a pipeline tail keeps each session's window and draft distributions across rounds
+    err = cudaMalloc(&s->d_win, (size_t)(e->wmax() + 1) * sizeof(int32_t));
+    if (err == cudaSuccess) err = cudaMemset(s->d_win, 0, (size_t)(e->wmax() + 1) * sizeof(int32_t));
+    if (err == cudaSuccess) err = cudaMalloc(&s->d_dprobs, (size_t)e->wmax() * e->d.V * sizeof(float));
+  }
   if (err != cudaSuccess) {
     e->release_session(*s);
     return cuda_fail(err, "session_open");
@@ -1160,6 +1239,106 @@ int llama_spec_round_device(LlamaEngine* e, uint64_t id, const clm_b200_spec_par
   s->pos_bound += p->q;
   s->pos_stale = true;
   return CLM_OK;
+}
+
+// ---- stage pipeline ------------------------------------------------------------------------------
+
+int llama_pipe_attach(LlamaEngine* e, clm_b200_link* in, clm_b200_link* out) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(e->spec.role != CLM_ROLE_WHOLE, CLM_FAILED_PRECONDITION, "a whole-model engine is not a pipeline stage");
+  CLM_CHECK(e->spec.role != CLM_ROLE_TAIL || e->has_mtp, CLM_FAILED_PRECONDITION,
+            "a pipeline tail drafts the next window: it needs an MTP head");
+  LinkDev li, lo;
+  CLM_TRY(link_dev(in, false, &li));
+  CLM_TRY(link_dev(out, true, &lo));
+  const uint32_t need_in = e->spec.role == CLM_ROLE_PREFIX ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
+  const uint32_t need_out = e->spec.role == CLM_ROLE_TAIL ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
+  CLM_CHECK(li.slot_bytes >= need_in + kLinkHeaderBytes && lo.slot_bytes >= need_out + kLinkHeaderBytes,
+            CLM_RESOURCE_EXHAUSTED, "link slots are smaller than a max_window message");
+  e->pipe_in = in;
+  e->pipe_out = out;
+  e->lin = li;
+  e->lout = lo;
+  return CLM_OK;
+}
+
+static int pipe_session(LlamaEngine* e, uint64_t id, uint32_t q, Session** out) {
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(e->pipe_in != nullptr, CLM_FAILED_PRECONDITION, "engine is not attached to a pipeline");
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_CHECK(s->outstanding == 0, CLM_FAILED_PRECONDITION, "a window is outstanding");
+  CLM_CHECK(q >= 1 && q <= e->spec.max_window, CLM_OUT_OF_RANGE, "window must be in [1, max_window]");
+  CLM_CHECK((uint64_t)s->pos_bound + q <= e->spec.max_context, CLM_RESOURCE_EXHAUSTED,
+            "pipeline round would exceed max_context");
+  *out = s;
+  return CLM_OK;
+}
+
+int llama_pipe_prefill(LlamaEngine* e, uint64_t id, const int32_t* h_tokens, uint32_t q, void* stream) {
+  CLM_TRY(engine_enter(e));
+  Session* s = nullptr;
+  CLM_TRY(pipe_session(e, id, q, &s));
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  if (e->spec.role == CLM_ROLE_PREFIX) {
+    CLM_CHECK(h_tokens != nullptr, CLM_INVALID_ARGUMENT, "the prefix consumes tokens");
+    for (uint32_t i = 0; i < q; ++i)
+      CLM_CHECK(h_tokens[i] >= 0 && h_tokens[i] < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+    CLM_CUDA(cudaMemcpyAsync(e->win, h_tokens, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  }
+  CLM_TRY(e->run_graph(*s, 6, (int)q, 0, st, [&](cudaStream_t cs) { return e->enqueue_pipe_prefill(*s, (int)q, cs); }));
+  s->pos_bound += q;
+  s->pos_stale = true;
+  return CLM_OK;
+}
+
+int llama_pipe_begin(LlamaEngine* e, uint64_t id, uint32_t row, const clm_b200_spec_params* p, void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(p != nullptr, CLM_INVALID_ARGUMENT, "null params");
+  CLM_CHECK(e->spec.role == CLM_ROLE_TAIL, CLM_FAILED_PRECONDITION, "only the pipeline tail begins the rounds");
+  Session* s = nullptr;
+  CLM_TRY(pipe_session(e, id, p->q, &s));
+  CLM_CHECK(row < e->spec.max_window, CLM_OUT_OF_RANGE, "row outside the last window");
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  const bool stochastic = p->temperature > 0.0f;
+  RoundCtl c{p->temperature, 0u, (unsigned long long)p->seed};
+  CLM_CUDA(cudaMemcpyAsync(e->ctl, &c, sizeof(c), cudaMemcpyHostToDevice, st));
+  CLM_TRY(e->sample_token(e->logits + (size_t)row * e->d.V, stochastic, p->temperature, p->seed, 0u, 2u,
+                          e->zero_counter, nullptr, e->tprobs, e->nxt, st));
+  CLM_TRY(launch_pdl(set_next_kernel, dim3(1), dim3(32), 0, st, s->d_state, (const int32_t*)e->nxt));
+  CLM_TRY(e->enqueue_drafts(*s, (int)p->q, stochastic, s->d_win, s->d_dprobs, st));
+  return launch_link_send(e->lout, s->d_win, LlamaEngine::token_bytes((int)p->q), nullptr, p->q, LINK_MSG_WINDOW,
+                          e->bad, st);
+}
+
+int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens, uint32_t* d_count,
+                     void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(p != nullptr, CLM_INVALID_ARGUMENT, "null params");
+  Session* s = nullptr;
+  CLM_TRY(pipe_session(e, id, p->q, &s));
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  const bool stochastic = p->temperature > 0.0f;
+  if (e->spec.role == CLM_ROLE_TAIL) {
+    RoundCtl c{p->temperature, 0u, (unsigned long long)p->seed};
+    CLM_CUDA(cudaMemcpyAsync(e->ctl, &c, sizeof(c), cudaMemcpyHostToDevice, st));
+  }
+  CLM_TRY(e->run_graph(*s, 5, (int)p->q, stochastic ? 1 : 0, st,
+                       [&](cudaStream_t cs) { return e->enqueue_pipe_round(*s, (int)p->q, stochastic, cs); }));
+  if (e->spec.role == CLM_ROLE_TAIL) {
+    if (d_tokens)
+      CLM_CUDA(cudaMemcpyAsync(d_tokens, e->emitted, (p->q + 1) * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    if (d_count) CLM_CUDA(cudaMemcpyAsync(d_count, e->count, sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+  }
+  s->pos_bound += p->q;
+  s->pos_stale = true;
+  return CLM_OK;
+}
+
+int llama_pipe_status(LlamaEngine* e, void* stream) {
+  CLM_TRY(engine_enter(e));
+  return e->check_bad(pick_stream(e->ctx, stream));
 }
 
 int llama_spec_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,

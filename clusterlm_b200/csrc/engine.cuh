@@ -42,6 +42,12 @@ int llama_spec_begin(LlamaEngine* e, uint64_t id, const int32_t* h_prompt, uint3
 int llama_spec_round_device(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
                             uint32_t* d_count, void* stream);
 int llama_spec_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens, uint32_t* h_count);
+int llama_pipe_attach(LlamaEngine* e, clm_b200_link* in, clm_b200_link* out);
+int llama_pipe_prefill(LlamaEngine* e, uint64_t id, const int32_t* h_tokens, uint32_t q, void* stream);
+int llama_pipe_begin(LlamaEngine* e, uint64_t id, uint32_t row, const clm_b200_spec_params* p, void* stream);
+int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens, uint32_t* d_count,
+                     void* stream);
+int llama_pipe_status(LlamaEngine* e, void* stream);
 // fixture family (fixture.cu)
 int fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* g, const clm_b200_stage_spec* spec,
                    clm_b200_engine** out);

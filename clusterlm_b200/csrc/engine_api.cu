@@ -145,4 +145,36 @@ int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t id, const clm_b200_s
   return llama_spec_round_device(llama(e), id, p, d_tokens, d_count, stream);
 }
 
+static int llama_only(clm_b200_engine* e) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "stage pipelines are implemented for the Llama family");
+  return CLM_OK;
+}
+
+int clm_b200_pipe_attach(clm_b200_engine* e, clm_b200_link* in, clm_b200_link* out) {
+  CLM_TRY(llama_only(e));
+  return llama_pipe_attach(llama(e), in, out);
+}
+
+int clm_b200_pipe_prefill(clm_b200_engine* e, uint64_t id, const int32_t* h_tokens, uint32_t positions, void* stream) {
+  CLM_TRY(llama_only(e));
+  return llama_pipe_prefill(llama(e), id, h_tokens, positions, stream);
+}
+
+int clm_b200_pipe_begin(clm_b200_engine* e, uint64_t id, uint32_t row, const clm_b200_spec_params* p, void* stream) {
+  CLM_TRY(llama_only(e));
+  return llama_pipe_begin(llama(e), id, row, p, stream);
+}
+
+int clm_b200_pipe_round(clm_b200_engine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
+                        uint32_t* d_count, void* stream) {
+  CLM_TRY(llama_only(e));
+  return llama_pipe_round(llama(e), id, p, d_tokens, d_count, stream);
+}
+
+int clm_b200_pipe_status(clm_b200_engine* e, void* stream) {
+  CLM_TRY(llama_only(e));
+  return llama_pipe_status(llama(e), stream);
+}
+
 }  // extern "C"

@@ -316,6 +316,13 @@ __device__ bool last_of(int* cnt, int total) {
 
 __device__ __forceinline__ float read_temperature(float T, const RoundCtl* ctl) { return ctl ? ctl->temperature : T; }
 
+// e = exp(double(l - m) / T), the reference's softmax term (sampling.cpp:64); at T = 1 the division is the
+// identity and is skipped (same value, no double division).
+__device__ __forceinline__ double soft_term(float l, float m, float T) {
+  const double x = (double)__fsub_rn(l, m);
+  return exp(T == 1.0f ? x : x / (double)T);
+}
+
 // ---------------------------------------------------------------------------------------------------
 // argmax rows (sampling.cpp:44-49): first index of the maximum; a NaN at index 0 pins the answer to 0 and
 // NaNs elsewhere are never chosen (the reference's `logits[i] > logits[best]` scan)
@@ -350,12 +357,13 @@ __global__ void __launch_bounds__(kSampleThreads) argmax_chunks_kernel(const flo
 // distribution rows (sampling.cpp:51-86, temperature only): P_i = float(exp(double(l_i - max) / T) / kept)
 // ---------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* __restrict__ logits, uint32_t V,
-                                                                   float* __restrict__ cmax, float* __restrict__ mx,
-                                                                   int* __restrict__ cnt) {
+                                                                   uint32_t off, float* __restrict__ cmax,
+                                                                   float* __restrict__ mx, int* __restrict__ cnt) {
   griddep_wait();
   griddep_launch();
-  const uint32_t c = blockIdx.x, r = blockIdx.y, C = gridDim.x;
-  const float* l = logits + (size_t)r * V;
+  const uint32_t c = blockIdx.x, C = gridDim.x;
+  const float* l = logits + (size_t)blockIdx.y * V;
+  const uint32_t r = blockIdx.y + off;  // statistics row
   const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
   float m = -FLT_MAX;
   for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) m = fmaxf(m, l[i]);
@@ -370,19 +378,21 @@ __global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* 
 }
 
 __global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* __restrict__ logits, uint32_t V,
-                                                                   float T, const RoundCtl* __restrict__ ctl,
+                                                                   uint32_t off, float T,
+                                                                   const RoundCtl* __restrict__ ctl,
                                                                    const float* __restrict__ mx,
                                                                    double* __restrict__ csum, double* __restrict__ kept,
                                                                    int* __restrict__ cnt) {
   griddep_wait();
   griddep_launch();
   T = read_temperature(T, ctl);
-  const uint32_t c = blockIdx.x, r = blockIdx.y, C = gridDim.x;
-  const float* l = logits + (size_t)r * V;
+  const uint32_t c = blockIdx.x, C = gridDim.x;
+  const float* l = logits + (size_t)blockIdx.y * V;
+  const uint32_t r = blockIdx.y + off;
   const float m = mx[r];
   const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
   double acc = 0.0;
-  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) acc += exp((double)__fsub_rn(l[i], m) / (double)T);
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) acc += soft_term(l[i], m, T);
   acc = block_sum_d(acc);
   if (threadIdx.x == 0) csum[(size_t)r * C + c] = acc;
   if (!last_of(&cnt[r], (int)C)) return;
@@ -408,7 +418,7 @@ __global__ void __launch_bounds__(kSampleThreads) probs_kernel(const float* __re
   const double k = kept[r];
   const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
   for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads)
-    o[i] = (float)(exp((double)__fsub_rn(l[i], m) / (double)T) / k);
+    o[i] = (float)(soft_term(l[i], m, T) / k);
 }
 
 __global__ void onehot_kernel(const int32_t* __restrict__ idx, uint32_t vocab, float* __restrict__ probs) {
@@ -424,8 +434,16 @@ __global__ void onehot_kernel(const int32_t* __restrict__ idx, uint32_t vocab, f
 // accept_decide_kernel): j == k -> the bonus row P[b][k]; else the residual float(max(0, P[b][j] - Q[b][j]))
 // (Q one-hot at the draft when Q is null), or P[b][j] when no residual is positive (sampling.cpp:117-126).
 struct SampleJob {
+  // target rows P [seq][k+1][V] and draft rows Q [seq][k][V]: materialised probabilities, or (P / Q null) logits
+  // LP / LQ whose statistics (launch_row_stats) are at scratch rows 0.. and qoff..; no Q and no LQ: one-hot drafts
   const float* P = nullptr;
   const float* Q = nullptr;
+  const float* LP = nullptr;
+  const float* LQ = nullptr;
+  const float* mx = nullptr;
+  const double* kept = nullptr;
+  uint32_t qoff = 0;
+  float T = 1.0f;  // logits-mode temperature (ctl's when given)
   const int32_t* drafts = nullptr;
   uint64_t row_stride = 0;  // plain jobs
   uint32_t k = 0;
@@ -439,26 +457,55 @@ struct SampleJob {
   const RoundCtl* ctl = nullptr;
 };
 
+// One probability row: materialised (p), or distribution(logits row, T) evaluated per entry from the row's
+// (max, kept) exactly as probs_kernel writes it.
+struct ProbRow {
+  const float* p = nullptr;
+  const float* l = nullptr;
+  float m = 0.0f;
+  double kept = 1.0;
+  float T = 1.0f;
+  __device__ __forceinline__ float operator()(uint32_t i) const {
+    return p ? p[i] : (float)(soft_term(l[i], m, T) / kept);
+  }
+};
+
 struct RowFx {
-  const float* P;
-  const float* Q;  // residual against Q, or one-hot at d when Q is null and residual is set
+  ProbRow P;
+  ProbRow Q;  // residual against Q, or one-hot at d when hasQ is false and residual is set
+  bool hasQ;
   int32_t d;
   bool residual;
+  __device__ __forceinline__ double q_at(uint32_t i) const { return hasQ ? (double)Q(i) : ((int32_t)i == d ? 1.0 : 0.0); }
   __device__ float operator()(uint32_t i) const {
-    if (!residual) return P[i];
-    const double qi = Q ? (double)Q[i] : ((int32_t)i == d ? 1.0 : 0.0);
-    const double r = (double)P[i] - qi;
+    if (!residual) return P(i);
+    const double r = (double)P(i) - q_at(i);
     return (float)(r > 0.0 ? r : 0.0);
   }
 };
 
+__device__ __forceinline__ float job_temperature(const SampleJob& job) { return job.ctl ? job.ctl->temperature : job.T; }
+
+// Target row `row` ([seq][k+1] numbering) and draft row `row` ([seq][k]) of an acceptance job.
+__device__ __forceinline__ ProbRow target_row(const SampleJob& job, size_t row, uint32_t V, float T) {
+  if (job.P) return ProbRow{job.P + row * V};
+  return ProbRow{nullptr, job.LP + row * V, job.mx[row], job.kept[row], T};
+}
+__device__ __forceinline__ ProbRow draft_row(const SampleJob& job, size_t row, uint32_t V, float T) {
+  if (job.Q) return ProbRow{job.Q + row * V};
+  if (job.LQ) return ProbRow{nullptr, job.LQ + row * V, job.mx[job.qoff + row], job.kept[job.qoff + row], T};
+  return ProbRow{};
+}
+
 // fx of sequence b: variant 0 = main (bonus / residual / plain row), 1 = fallback P[b][j] (acceptance, j < k)
-__device__ __forceinline__ RowFx job_fx(const SampleJob& job, uint32_t b, uint32_t V, int variant) {
-  if (!job.accept) return RowFx{job.P + (size_t)b * job.row_stride, nullptr, 0, false};
+__device__ __forceinline__ RowFx job_fx(const SampleJob& job, uint32_t b, uint32_t V, int variant, float T) {
+  if (!job.accept) return RowFx{ProbRow{job.P + (size_t)b * job.row_stride}, ProbRow{}, false, 0, false};
   const uint32_t j = (uint32_t)job.sel[b];
-  const float* Pj = job.P + ((size_t)b * (job.k + 1) + j) * V;
-  if (j >= job.k || variant == 1) return RowFx{Pj, nullptr, 0, false};
-  return RowFx{Pj, job.Q ? job.Q + ((size_t)b * job.k + j) * V : nullptr, job.drafts[(size_t)b * job.k + j], true};
+  const ProbRow Pj = target_row(job, (size_t)b * (job.k + 1) + j, V, T);
+  if (j >= job.k || variant == 1) return RowFx{Pj, ProbRow{}, false, 0, false};
+  const bool hasQ = job.Q != nullptr || job.LQ != nullptr;
+  return RowFx{Pj, hasQ ? draft_row(job, (size_t)b * job.k + j, V, T) : ProbRow{}, hasQ,
+               job.drafts[(size_t)b * job.k + j], true};
 }
 
 __device__ __forceinline__ double job_uniform(const SampleJob& job, const double* u_dev, uint32_t b) {
@@ -499,22 +546,21 @@ __global__ void __launch_bounds__(kSampleThreads) sample_chunks_kernel(SampleJob
   const uint32_t c = blockIdx.x, b = blockIdx.y, C = gridDim.x, tid = threadIdx.x;
   const uint32_t clo = c * kSampleChunk, chi = min(V, clo + kSampleChunk);
   const bool two = job.accept && (uint32_t)job.sel[b] < job.k;  // residual with a P fallback
+  const float T = job_temperature(job);
   __shared__ int s_flags;
   if (tid == 0) s_flags = 0;
   __syncthreads();
   const uint32_t lo = min(chi, clo + tid * kPerThread), hi = min(chi, lo + kPerThread);
   for (int variant = 0; variant < (two ? 2 : 1); ++variant) {
-    const RowFx fx = job_fx(job, b, V, variant);
+    const RowFx fx = job_fx(job, b, V, variant, T);
     U192 sum;
     int32_t last;
     bool bad;
     thread_sums(fx, lo, hi, sum, last, bad);
     bool anypos = false;
     if (variant == 0 && two)
-      for (uint32_t i = lo; i < hi; ++i) {  // residual mass test in double (sampling.cpp:121-123)
-        const double qi = fx.Q ? (double)fx.Q[i] : ((int32_t)i == fx.d ? 1.0 : 0.0);
-        anypos |= ((double)fx.P[i] - qi) > 0.0;
-      }
+      for (uint32_t i = lo; i < hi; ++i)  // residual mass test in double (sampling.cpp:121-123)
+        anypos |= ((double)fx.P(i) - fx.q_at(i)) > 0.0;
     U192 total;
     (void)block_exclusive_scan(sum, &total);
     int32_t lmax;
@@ -545,7 +591,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_chunks_kernel(SampleJob
   }
   __syncthreads();
   const int variant = s_variant;
-  const RowFx fx = job_fx(job, b, V, variant);
+  const RowFx fx = job_fx(job, b, V, variant, T);
   const double u = job_uniform(job, u_dev, b);
   // chunk prefix sums (C <= kSampleThreads chunks per row)
   U192 csum = u192_zero();
@@ -646,26 +692,24 @@ __device__ __forceinline__ double draw_uniform(const double* uniforms, uint64_t 
   return philox_uniform(seed, n, seq, (uint32_t)counter_base, (uint32_t)(counter_base >> 32));
 }
 
-__global__ void accept_decide_kernel(const float* __restrict__ P, const float* __restrict__ Q,
-                                     const int32_t* __restrict__ drafts, uint32_t batch, uint32_t k, uint32_t V,
-                                     const double* __restrict__ uniforms, uint64_t seed, uint64_t counter_base,
-                                     const unsigned long long* __restrict__ d_counter, const RoundCtl* __restrict__ ctl,
-                                     int32_t* __restrict__ sel, double* __restrict__ u_out,
-                                     uint32_t* __restrict__ accepted) {
+__global__ void accept_decide_kernel(SampleJob job, uint32_t batch, uint32_t V, const double* __restrict__ uniforms,
+                                     uint64_t seed, uint64_t counter_base, int32_t* __restrict__ sel,
+                                     double* __restrict__ u_out, uint32_t* __restrict__ accepted) {
   griddep_wait();
   griddep_launch();
   const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
-  if (d_counter) counter_base = *d_counter;
-  if (ctl) seed = ctl->seed;
-  const float* Pb = P + (size_t)b * (k + 1) * V;
-  const float* Qb = Q ? Q + (size_t)b * k * V : nullptr;
-  const int32_t* d = drafts + (size_t)b * k;
+  const uint32_t k = job.k;
+  if (job.d_counter) counter_base = *job.d_counter;
+  if (job.ctl) seed = job.ctl->seed;
+  const float T = job_temperature(job);
+  const bool hasQ = job.Q != nullptr || job.LQ != nullptr;
+  const int32_t* d = job.drafts + (size_t)b * k;
   uint32_t used = 0, j = 0;
   for (; j < k; ++j) {
     const uint32_t dj = (uint32_t)d[j];
-    const double p = dj < V ? (double)Pb[(size_t)j * V + dj] : 0.0;
-    const double q = Qb ? (dj < V ? (double)Qb[(size_t)j * V + dj] : 0.0) : 1.0;
+    const double p = dj < V ? (double)target_row(job, (size_t)b * (k + 1) + j, V, T)(dj) : 0.0;
+    const double q = hasQ ? (dj < V ? (double)draft_row(job, (size_t)b * k + j, V, T)(dj) : 0.0) : 1.0;
     if (q > 0.0) {
       const double ratio = p / q;
       const double lim = ratio < 1.0 ? ratio : 1.0;
@@ -738,7 +782,7 @@ __global__ void __launch_bounds__(kTruncThreads) truncated_distribution_kernel(
   for (uint32_t i = tid; i < V; i += kTruncThreads) m = fmaxf(m, l[i]);
   m = block_max(m);
   for (uint32_t i = tid; i < V; i += kTruncThreads) {
-    const double v = exp((double)__fsub_rn(l[i], m) / (double)T);
+    const double v = soft_term(l[i], m, T);
     e[i] = v;
     ka[i] = ~(unsigned long long)__double_as_longlong(v);  // ascending ~bits = descending e (e >= 0)
     ia[i] = i;
@@ -819,14 +863,21 @@ int launch_argmax_rows(const float* d_logits, uint32_t rows, uint32_t V, int32_t
                     s.cval, s.cidx, s.rcnt, d_out);
 }
 
+int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, uint32_t off,
+                     const SampleScratch& s, cudaStream_t st) {
+  if (rows == 0) return CLM_OK;
+  CLM_CHECK(off + rows <= s.rows, CLM_INTERNAL, "sampling scratch too small");
+  const dim3 grid(sample_chunks(V), rows);
+  CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, off, s.cmax, s.mx, s.rcnt));
+  return launch_pdl(stats_sum_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, off, T, ctl,
+                    (const float*)s.mx, s.csum, s.kept, s.rcnt);
+}
+
 int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, float* d_probs,
                  const SampleScratch& s, cudaStream_t st) {
   if (rows == 0) return CLM_OK;
-  CLM_CHECK(rows <= s.rows, CLM_INTERNAL, "sampling scratch too small");
+  CLM_TRY(launch_row_stats(d_logits, rows, V, T, ctl, 0, s, st));
   const dim3 grid(sample_chunks(V), rows);
-  CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, s.cmax, s.mx, s.rcnt));
-  CLM_TRY(launch_pdl(stats_sum_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, T, ctl,
-                     (const float*)s.mx, s.csum, s.kept, s.rcnt));
   return launch_pdl(probs_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, T, ctl, (const float*)s.mx,
                     (const double*)s.kept, d_probs);
 }
@@ -855,21 +906,31 @@ int launch_sample_rows(const float* d_probs, uint32_t rows, uint64_t row_stride,
   return launch_sample_job(job, rows, V, nullptr, d_out, s, st);
 }
 
-int launch_accept(const float* d_P, const float* d_Q, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
+int launch_accept(const AcceptRows& rows, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
                   const double* d_uniforms, uint64_t seed, uint64_t counter_base,
                   const unsigned long long* d_counter, const RoundCtl* ctl, uint32_t* d_accepted, int32_t* d_next,
                   const SampleScratch& s, cudaStream_t st) {
   if (batch == 0) return CLM_OK;
   CLM_CHECK(batch <= s.seqs, CLM_INTERNAL, "sampling scratch too small");
-  CLM_TRY(launch_pdl(accept_decide_kernel, dim3((batch + 127) / 128), dim3(128), 0, st, d_P, d_Q, d_drafts, batch, k,
-                     V, d_uniforms, seed, counter_base, d_counter, ctl, s.sel, s.u, d_accepted));
+  CLM_CHECK((rows.P != nullptr) != (rows.LP != nullptr), CLM_INTERNAL, "acceptance needs one target row source");
   SampleJob job;
-  job.P = d_P;
-  job.Q = d_Q;
+  job.P = rows.P;
+  job.Q = rows.Q;
+  job.LP = rows.LP;
+  job.LQ = rows.Q ? nullptr : rows.LQ;
+  job.mx = s.mx;
+  job.kept = s.kept;
+  job.qoff = rows.q_stats_off;
+  job.T = rows.T;
+  job.ctl = ctl;
+  job.d_counter = d_counter;
   job.drafts = d_drafts;
   job.k = k;
   job.accept = true;
   job.sel = s.sel;
+  CLM_TRY(launch_pdl(accept_decide_kernel, dim3((batch + 127) / 128), dim3(128), 0, st, job, batch, V, d_uniforms,
+                     seed, counter_base, s.sel, s.u, d_accepted));
+  job.d_counter = nullptr;  // the sample kernel takes the uniforms accept_decide_kernel stored
   return launch_sample_job(job, batch, V, s.u, d_next, s, st);
 }
 
@@ -967,8 +1028,11 @@ int clm_b200_verify_speculative(clm_b200_ctx* ctx, const float* d_target, const 
   cudaStream_t st = pick_stream(ctx, stream);
   SampleScratch s;
   CLM_TRY(abi_scratch(ctx, 0, batch, vocab, 0, st, &s, nullptr));
-  return launch_accept(d_target, d_draft_probs, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr,
-                       nullptr, d_accepted, d_next, s, st);
+  AcceptRows src;
+  src.P = d_target;
+  src.Q = d_draft_probs;
+  return launch_accept(src, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr, nullptr, d_accepted,
+                       d_next, s, st);
 }
 
 int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_dl, const int32_t* d_drafts,
@@ -982,13 +1046,16 @@ int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_
   cudaStream_t st = pick_stream(ctx, stream);
   const uint32_t trows = batch * (k + 1), drows = d_dl ? batch * k : 0, rows = trows + drows;
   SampleScratch s;
-  void* probs = nullptr;
-  CLM_TRY(abi_scratch(ctx, rows, batch, vocab, (size_t)rows * vocab * sizeof(float), st, &s, &probs));
-  float* P = static_cast<float*>(probs);
-  float* Q = drows ? P + (size_t)trows * vocab : nullptr;
-  CLM_TRY(launch_probs(d_tl, trows, vocab, temperature, nullptr, P, s, st));
-  if (drows) CLM_TRY(launch_probs(d_dl, drows, vocab, temperature, nullptr, Q, s, st));
-  return launch_accept(P, Q, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr, nullptr, d_accepted,
+  CLM_TRY(abi_scratch(ctx, rows, batch, vocab, 0, st, &s, nullptr));
+  // row statistics only (target rows at 0.., draft rows at trows..); probabilities are evaluated where used
+  CLM_TRY(launch_row_stats(d_tl, trows, vocab, temperature, nullptr, 0, s, st));
+  if (drows) CLM_TRY(launch_row_stats(d_dl, drows, vocab, temperature, nullptr, trows, s, st));
+  AcceptRows src;
+  src.LP = d_tl;
+  src.LQ = d_dl;
+  src.q_stats_off = trows;
+  src.T = temperature;
+  return launch_accept(src, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr, nullptr, d_accepted,
                        d_next, s, st);
 }
 

@@ -41,6 +41,9 @@ struct SampleScratch {
 // out[r] = argmax of row r (ties to the lowest index).
 int launch_argmax_rows(const float* d_logits, uint32_t rows, uint32_t V, int32_t* d_out, const SampleScratch& s,
                        cudaStream_t st);
+// Row statistics of distribution(logits[r], T) (max and kept) into scratch rows off + r.
+int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, uint32_t off,
+                     const SampleScratch& s, cudaStream_t st);
 // probs[r] = distribution(logits[r], T) (temperature from ctl when given).
 int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, float* d_probs,
                  const SampleScratch& s, cudaStream_t st);
@@ -49,10 +52,21 @@ int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, cons
 int launch_sample_rows(const float* d_probs, uint32_t rows, uint64_t row_stride, uint32_t V, const double* d_uniforms,
                        uint64_t seed, uint32_t draw, uint32_t stream_id, const unsigned long long* d_counter,
                        const RoundCtl* ctl, int32_t* d_out, const SampleScratch& s, cudaStream_t st);
-// verify_speculative for `batch` sequences over probability rows P [batch][k+1][V] and Q [batch][k][V] (null:
-// one-hot drafts).  Uniforms from d_uniforms [batch][k+1], else Philox(seed | ctl->seed, draw, sequence,
-// counter_base | *d_counter).
-int launch_accept(const float* d_P, const float* d_Q, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
+// The rows verify_speculative reads: target P [batch][k+1][V] and draft Q [batch][k][V] as probabilities, or as
+// logits (LP / LQ) whose launch_row_stats statistics are at scratch rows 0.. (target) and q_stats_off.. (draft);
+// the probabilities are then evaluated where they are used, bit-identical to launch_probs' output.  No Q and
+// no LQ: one-hot drafts.
+struct AcceptRows {
+  const float* P = nullptr;
+  const float* LP = nullptr;
+  const float* Q = nullptr;
+  const float* LQ = nullptr;
+  uint32_t q_stats_off = 0;
+  float T = 1.0f;  // logits-mode temperature (ctl's when given)
+};
+// verify_speculative for `batch` sequences.  Uniforms from d_uniforms [batch][k+1], else Philox(seed | ctl->seed,
+// draw, sequence, counter_base | *d_counter).
+int launch_accept(const AcceptRows& rows, const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t V,
                   const double* d_uniforms, uint64_t seed, uint64_t counter_base,
                   const unsigned long long* d_counter, const RoundCtl* ctl, uint32_t* d_accepted, int32_t* d_next,
                   const SampleScratch& s, cudaStream_t st);

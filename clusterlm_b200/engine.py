@@ -11,7 +11,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._native import QUANTS, call
+from ._native import LINK_HANDLE_BYTES, QUANTS, call
 
 _vp = C.c_void_p
 
@@ -231,6 +231,66 @@ class Engine:
         call("clm_b200_spec_round_device", self.h, session, C.byref(p),
              None if d_tokens is None else _vp(d_tokens.data_ptr()),
              None if d_count is None else _vp(d_count.data_ptr()), stream)
+
+
+    # ---- stage pipeline (clm_b200_pipe_*)
+    def pipe_attach(self, link_in: "Link", link_out: "Link"):
+        call("clm_b200_pipe_attach", self.h, link_in.h, link_out.h)
+        self._links = (link_in, link_out)  # the links must outlive the engine's use of them
+
+    def pipe_prefill(self, session: int, q: int, tokens=None, stream=None):
+        """One prompt chunk of q positions through this stage, committed at once (the prefix takes tokens)."""
+        t = None if tokens is None else _i32(tokens)
+        call("clm_b200_pipe_prefill", self.h, session, None if t is None else t.ctypes.data_as(_vp), q,
+             None if stream is None else _vp(stream))
+
+    def pipe_begin(self, session: int, row: int, q: int, temperature: float = 0.0, seed: int = 0, stream=None):
+        p = _SpecParams(q, temperature, seed)
+        call("clm_b200_pipe_begin", self.h, session, row, C.byref(p), None if stream is None else _vp(stream))
+
+    def pipe_round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None, d_count=None,
+                   stream=None):
+        p = _SpecParams(q, temperature, seed)
+        call("clm_b200_pipe_round", self.h, session, C.byref(p),
+             None if d_tokens is None else _vp(d_tokens.data_ptr()),
+             None if d_count is None else _vp(d_count.data_ptr()), None if stream is None else _vp(stream))
+
+    def pipe_status(self, stream=None):
+        call("clm_b200_pipe_status", self.h, None if stream is None else _vp(stream))
+
+
+LINK_SEND, LINK_RECV = 0, 1
+
+
+class Link:
+    """One end of a one-way stage link between two GPUs (clm_b200_link_*)."""
+
+    def __init__(self, ctx, end: int, slots: int, payload_bytes: int, timeout_s: float = 30.0):
+        h = _vp()
+        call("clm_b200_link_create", ctx.h, end, slots, payload_bytes, timeout_s, C.byref(h))
+        self.h, self.end, self.ctx = h, end, ctx
+
+    def export(self) -> bytes:
+        buf = C.create_string_buffer(LINK_HANDLE_BYTES)
+        call("clm_b200_link_export", self.h, buf)
+        return buf.raw
+
+    def connect(self, peer_handle: bytes):
+        if len(peer_handle) != LINK_HANDLE_BYTES:
+            raise ValueError("link handle has the wrong size")
+        buf = C.create_string_buffer(peer_handle, LINK_HANDLE_BYTES)
+        call("clm_b200_link_connect", self.h, buf)
+
+    def close(self):
+        if self.h:
+            call("clm_b200_link_destroy", self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class FixtureEngine(Engine):

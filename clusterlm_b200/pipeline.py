@@ -1,0 +1,200 @@
+"""Speculative stage pipeline across the GPUs of one node (one process per GPU).
+
+The reference runs a speculative round stage by stage: the Father's prefix, the Nodes' middle stages and the
+Father's tail, joined by RunWindow / StageResult messages over TCP (orchestrator/coordinator/src/
+coordinator.cpp:736-832), with the drafter on the tail and a CommitWindow fan-out after acceptance
+(coordinator.cpp:836-892).  Here every stage is a b200 engine on its own GPU and the hops are device links
+(clm_b200_link_*): records go stage to stage, the tail accepts, commits, drafts the next window with its MTP head
+and sends the window's tokens back to the prefix; each message carries the commit count of the session's previous
+round, so no stage needs a host round trip.  Several sequences are in flight so that every stage is busy.
+
+Plans use the reference's text form (ClusterPlan::parse, coordinator.cpp:54-95): "BEGIN-END@OWNER,...", in pipeline
+order, contiguous, ending at the last layer, only the tail may be empty; an owner here is a GPU of the node
+("g3" or "3") rather than a Node index or "father".
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Callable, Sequence
+
+from .engine import LINK_RECV, LINK_SEND, ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL, Engine, LlamaGeometry, Link
+
+BYTES_PER_WEIGHT = {"q4_k": 144 / 256, "q8_0": 34 / 32}
+
+
+@dataclasses.dataclass(frozen=True)
+class StagePlan:
+    begin: int
+    end: int
+    gpu: int
+
+    def describe(self) -> str:
+        return f"{self.begin}-{self.end}@g{self.gpu}"
+
+
+def parse_plan(text: str, n_layers: int) -> list[StagePlan]:
+    """ClusterPlan::parse + validate (coordinator.cpp:54-110) for GPU owners."""
+    stages = []
+    for item in text.split(","):
+        at, dash = item.find("@"), item.find("-")
+        if at < 0 or dash < 0 or dash > at:
+            raise ValueError(f"plan item '{item}' is not BEGIN-END@OWNER")
+        try:
+            begin, end = int(item[:dash]), int(item[dash + 1:at])
+        except ValueError:
+            raise ValueError(f"bad layer range in '{item}'") from None
+        owner = item[at + 1:]
+        try:
+            gpu = int(owner[1:] if owner.startswith("g") else owner)
+        except ValueError:
+            raise ValueError(f"bad owner in '{item}' (a GPU of this node: gK)") from None
+        stages.append(StagePlan(begin, end, gpu))
+    if len(stages) < 2:
+        raise ValueError("a plan needs at least a prefix and a tail")
+    if stages[-1].end != n_layers:
+        raise ValueError(f"plan must end at layer {n_layers}")
+    expect = 0
+    for i, s in enumerate(stages):
+        if s.begin != expect or (s.end <= s.begin and i + 1 != len(stages)):
+            raise ValueError("stage ranges must be contiguous and non-empty")
+        expect = s.end
+    if len({s.gpu for s in stages}) != len(stages):
+        raise ValueError("every stage needs its own GPU")
+    return stages
+
+
+def format_plan(stages: Sequence[StagePlan]) -> str:
+    return ",".join(s.describe() for s in stages)
+
+
+def stage_costs(geo: LlamaGeometry, q: int, context: int) -> tuple[float, float]:
+    """(bytes one layer streams per round, extra bytes of the tail per round): layer weights plus the layer's KV
+    of every session's context; the tail adds the LM head and q-1 MTP draft steps (MTP block + LM head each)."""
+    bw = BYTES_PER_WEIGHT[geo.quant]
+    H, F, V = geo.hidden, geo.ffn, geo.vocab
+    qd, kvd = geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim
+    layer = (H * (qd + 2 * kvd) + qd * H + 3 * F * H) * bw + 2 * context * kvd * 2
+    head = V * H * bw
+    mtp = 3 * F * H * bw if geo.mtp else 0.0
+    tail = head + (q - 1) * (mtp + head)
+    return layer, tail
+
+
+def plan_stages(geo: LlamaGeometry, world: int, q: int, context: int) -> list[StagePlan]:
+    """Contiguous layer ranges for `world` GPUs minimising the largest per-round byte stream of a stage (every
+    stage but the tail holds at least one layer)."""
+    L = geo.n_layers
+    if world < 2:
+        raise ValueError("a pipeline needs at least two stages")
+    if world - 1 > L:
+        raise ValueError("more stages than layers")
+    layer, tail = stage_costs(geo, q, context)
+    INF = float("inf")
+    # best[i][k]: smallest max cost placing layers [0, k) on stages [0, i) (all non-empty)
+    best = [[INF] * (L + 1) for _ in range(world)]
+    cut = [[0] * (L + 1) for _ in range(world)]
+    best[0][0] = 0.0
+    for i in range(1, world):
+        for k in range(i, L + 1):
+            for j in range(i - 1, k):
+                c = max(best[i - 1][j], (k - j) * layer)
+                if c < best[i][k]:
+                    best[i][k], cut[i][k] = c, j
+    # the tail takes the rest (possibly nothing)
+    end, top = None, INF
+    for k in range(world - 1, L + 1):
+        c = max(best[world - 1][k], (L - k) * layer + tail)
+        if c < top:
+            top, end = c, k
+    bounds = [end]
+    for i in range(world - 1, 0, -1):
+        bounds.append(cut[i][bounds[-1]])
+    bounds = bounds[::-1] + [L]
+    return [StagePlan(bounds[i], bounds[i + 1], i) for i in range(world)]
+
+
+def role_of(rank: int, world: int) -> int:
+    return ROLE_PREFIX if rank == 0 else ROLE_TAIL if rank == world - 1 else ROLE_MIDDLE
+
+
+def link_peers(rank: int, world: int) -> tuple[int, int]:
+    """(rank whose output this rank receives, rank this rank sends to): the ring prefix -> ... -> tail -> prefix."""
+    return (rank - 1) % world, (rank + 1) % world
+
+
+def wire(rank: int, world: int, gathered: Sequence[tuple[bytes, bytes]]) -> tuple[bytes, bytes]:
+    """Given every rank's (input-link handle, output-link handle), the handles this rank's input and output links
+    connect to: the input (receiving end) maps its sender's output end and vice versa."""
+    src, dst = link_peers(rank, world)
+    return gathered[src][1], gathered[dst][0]
+
+
+class StagePipeline:
+    """This rank's stage of a speculative pipeline: engine, links and the per-round calls.
+
+    Every rank must make the same calls (prefill chunks, rounds) for the same sessions in the same order.
+    `all_gather` exchanges one picklable object per rank (torch.distributed.all_gather_object in practice);
+    `engine_factory` / `link_factory` default to the device classes (host-logic tests pass stand-ins)."""
+
+    def __init__(self, ctx, geo: LlamaGeometry, plan: Sequence[StagePlan], rank: int, max_context: int,
+                 sessions: int, all_gather: Callable[[object], list], max_window: int = 16, slots: int = 0,
+                 timeout_s: float = 30.0, weight_seed: int = 0, stddev: float = 0.02,
+                 engine_factory=Engine, link_factory=Link):
+        self.rank, self.world = rank, len(plan)
+        self.role = role_of(rank, self.world)
+        self.max_window = max_window
+        self.ctx = ctx
+        st = plan[rank]
+        self.engine = engine_factory(ctx, geo, st.begin, st.end, self.role, max_context, max_window, sessions)
+        self.engine.generate_weights(seed=weight_seed, stddev=stddev)
+        self.engine.prepare()
+        fpp = 2 * geo.hidden + 1
+        rec = max_window * fpp * 4
+        tok = (max_window + 1) * 4
+        # a slot per sequence in flight (plus one), so no sender ever waits on a credit in steady state
+        slots = slots or sessions + 1
+        self.link_in = link_factory(ctx, LINK_RECV, slots, tok if self.role == ROLE_PREFIX else rec, timeout_s)
+        self.link_out = link_factory(ctx, LINK_SEND, slots, tok if self.role == ROLE_TAIL else rec, timeout_s)
+        gathered = all_gather((self.link_in.export(), self.link_out.export()))
+        peer_in, peer_out = wire(rank, self.world, gathered)
+        self.link_in.connect(peer_in)
+        self.link_out.connect(peer_out)
+        self.engine.pipe_attach(self.link_in, self.link_out)
+
+    @property
+    def is_tail(self) -> bool:
+        return self.role == ROLE_TAIL
+
+    def open_session(self, session: int):
+        self.engine.open_session(session)
+
+    def prefill(self, session: int, prompt: Sequence[int], stream=None) -> int:
+        """Runs the prompt through this stage in chunks of max_window; returns the last chunk's final row."""
+        n = len(prompt)
+        off = 0
+        while off < n:
+            q = min(self.max_window, n - off)
+            self.engine.pipe_prefill(session, q, prompt[off:off + q] if self.role == ROLE_PREFIX else None, stream)
+            off += q
+        return (n - 1) % self.max_window
+
+    def begin(self, session: int, row: int, q: int, temperature: float = 0.0, seed: int = 0, stream=None):
+        if self.is_tail:
+            self.engine.pipe_begin(session, row, q, temperature, seed, stream)
+
+    def round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None, d_count=None,
+              stream=None):
+        self.engine.pipe_round(session, q, temperature, seed, d_tokens, d_count, stream)
+
+    def status(self, stream=None):
+        self.engine.pipe_status(stream)
+
+    def close(self, barrier: Callable[[], None]):
+        """Waits for this stage's work, then for every rank (`barrier`), before any link memory is released: a
+        peer may still be storing into this rank's inbox until its own stream has drained."""
+        self.ctx.synchronize()
+        barrier()
+        self.engine.close()
+        self.link_in.close()
+        self.link_out.close()
+        barrier()

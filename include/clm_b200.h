@@ -250,6 +250,48 @@ CLM_API int clm_b200_spec_round(clm_b200_engine* e, uint64_t session, const clm_
 CLM_API int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
                                        int32_t* d_tokens, uint32_t* d_count, void* stream);
 
+/* ---- stage pipeline across the GPUs of one node ----------------------------------------------------
+ * Replaces the Father -> Node -> ... -> Father hops of a speculative window (RunWindow / StageResult over
+ * TCP: orchestrator/coordinator/src/coordinator.cpp:736-832, runtime/transport) for stages placed on GPUs of
+ * one box, one process (or context) per GPU.  A link is a one-way FIFO of `slots` messages of at most
+ * `payload_bytes` between two GPUs: the sender's kernel stores each message into the receiver's memory over
+ * NVLink and publishes it with a system-scope flag; the receiver's kernel waits for the flag (bounded by
+ * `timeout_s`), copies the message out and returns a credit.  The two ends must be on different GPUs. */
+typedef struct clm_b200_link clm_b200_link;
+enum { CLM_LINK_SEND = 0, CLM_LINK_RECV = 1 };
+#define CLM_B200_LINK_HANDLE_BYTES 128
+CLM_API int clm_b200_link_create(clm_b200_ctx* ctx, int end, uint32_t slots, uint64_t payload_bytes, double timeout_s,
+                                 clm_b200_link** out);
+/* Writes this end's handle (CLM_B200_LINK_HANDLE_BYTES bytes) for the other end's process. */
+CLM_API int clm_b200_link_export(const clm_b200_link* link, void* handle);
+/* Maps the other end from its handle (a CUDA IPC mapping, or a peer pointer when both ends are in one process). */
+CLM_API int clm_b200_link_connect(clm_b200_link* link, const void* peer_handle);
+CLM_API int clm_b200_link_destroy(clm_b200_link* link);
+
+/* Binds a stage engine into a speculative pipeline (Llama family, max_sessions sequences in flight):
+ *   prefix: `in` receives window tokens from the tail, `out` sends boundary records to the next stage;
+ *   middle: `in` receives records, `out` sends records;
+ *   tail (with an MTP head): `in` receives records, `out` sends the next window's tokens to the prefix.
+ * Every message carries the count of positions the receiver commits for the session before the window (the
+ * tail's acceptance of the session's previous window: commit_window fan-out, coordinator.cpp:836-892). */
+CLM_API int clm_b200_pipe_attach(clm_b200_engine* e, clm_b200_link* in, clm_b200_link* out);
+/* One prompt chunk of `positions` (<= max_window) through this stage, committed at once (prefill with
+ * auto_commit, coordinator.cpp:896-959).  The prefix takes h_tokens; the other stages receive records. */
+CLM_API int clm_b200_pipe_prefill(clm_b200_engine* e, uint64_t session, const int32_t* h_tokens, uint32_t positions,
+                                  void* stream);
+/* Tail, after the prompt: the first next token from row `row` of the last prefill chunk's logits (argmax, or
+ * a sample with Philox draw (0, stream 2, 0)), the first window's q-1 MTP drafts, sent to the prefix. */
+CLM_API int clm_b200_pipe_begin(clm_b200_engine* e, uint64_t session, uint32_t row, const clm_b200_spec_params* params,
+                                void* stream);
+/* One speculative round of `session` on this stage, device-resident: wait for the input, commit the previous
+ * round, run the window, forward.  The tail also accepts (as clm_b200_spec_round_device), commits, drafts the
+ * next window and sends it to the prefix; its emitted tokens / count go to d_tokens / d_count (optional).
+ * Every stage runs the same rounds of the same sessions in the same order. */
+CLM_API int clm_b200_pipe_round(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
+                                int32_t* d_tokens, uint32_t* d_count, void* stream);
+/* Synchronises the engine's stream; CLM_DEADLINE_EXCEEDED if a link wait gave up (a peer stage stopped). */
+CLM_API int clm_b200_pipe_status(clm_b200_engine* e, void* stream);
+
 /* ---- clusterlm-fixture family: the reference's own model (hc gated residual streams, 3:1 recurrent /
  * attention layers without RoPE, top-K MoE with a shared SwiGLU expert, PLE n-gram lookup, injection gates;
  * runtime/domain/src/reference_domain.cpp:452-585).  Computed in f32 with the reference's ascending

@@ -281,3 +281,29 @@ def test_accept_logits_philox_matches_oracle(ctx, oracle):
         us = np.array([oracle.philox_uniform(seed, n, b, base, 0) for n in range(k + 1)])
         a, n, _ = oracle.verify(P[b], drafts[b], Q[b], us)
         assert (a, n) == (acc[b], nxt[b]), b
+
+
+def test_accept_logits_equals_materialised_at_acceptance_micro_size(ctx):
+    """The acceptance micro-workload at full size (64 sequences x q = 8 x vocab 151,936): acceptance evaluated from
+    logits gives the same accepted counts and tokens as verify_speculative over the materialised distributions
+    (same Philox counters), for several counter bases."""
+    import torch
+
+    from clusterlm_b200.runtime import accept_logits, distribution, verify_speculative
+
+    B, q, V = 64, 8, 151936
+    k = q - 1
+    dev_ = torch.device("cuda:0")
+    g = torch.Generator(device=dev_).manual_seed(0)
+    tl = torch.randn((B, q, V), generator=g, device=dev_) * 3.0
+    dl = tl[:, :k] + torch.randn((B, k, V), generator=g, device=dev_) * 0.5
+    drafts = torch.multinomial(torch.softmax(dl.reshape(-1, V), dim=-1), 1, generator=g).reshape(B, k)
+    drafts = drafts.to(torch.int32).contiguous()
+    P = distribution(ctx, tl.reshape(-1, V), 1.0).reshape(B, q, V)
+    Q = distribution(ctx, dl.reshape(-1, V), 1.0).reshape(B, k, V)
+    for base in (0, 1, 977):
+        a1, n1 = accept_logits(ctx, tl, dl, drafts, 1.0, seed=0, counter_base=base)
+        a2, n2 = verify_speculative(ctx, P, drafts, Q, seed=0, counter_base=base)
+        assert torch.equal(a1, a2) and torch.equal(n1, n2), base
+    # a spread of outcomes (not all accepted / all rejected)
+    assert 0 < int(a1.sum()) < B * k
