@@ -322,6 +322,57 @@ def acceptance_micro(ctx, dev, peak, with_cpu):
     return out
 
 
+# tree-window micro-workload: the 8B shape in Q8_0 with a 16-node draft tree (root; 4 children; 2 children each;
+# 3 nodes at depth 3, so 16 = max_window nodes), context 4096, batch 1 (one sequence per window)
+C4_PARENTS = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 6, 7]
+
+
+def tree_micro(ctx, dev, peak, context):
+    """One 16-node tree verification window (Q8_0 8B shape) through clm_b200_run_tree_window_device, event-timed on
+    the engine's stream; batch 8 is 8 such windows (the weights are streamed once per sequence)."""
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+
+    geo = dataclasses.replace(LLAMA3_8B, quant="q8_0")
+    q = len(C4_PARENTS)
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, context + 64, 16, 1)
+    eng.generate_weights(seed=SEED, stddev=0.02)
+    eng.prepare()
+    eng.open_session(1)
+    rng = np.random.default_rng(77)
+    eng.spec_begin(1, rng.integers(0, geo.vocab, context).astype(np.int32), 4)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    parents = torch.tensor(C4_PARENTS, dtype=torch.int32, device=dev)
+    toks = torch.from_numpy(rng.integers(0, geo.vocab, q).astype(np.int32)).to(dev)
+    logits = torch.empty((q, geo.vocab), dtype=torch.float32, device=dev)
+    pos = eng.position(1)
+    times = []
+    for i in range(8):
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        eng.run_tree_window_device(1, pos, parents, toks, logits, stream.cuda_stream)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        eng.abort(1)
+        if i >= 3:
+            times.append(s0.elapsed_time(s1) / 1e3)
+    sec = statistics.median(times)
+    eng.close_session(1)
+    eng.close()
+    H, qd, kvd, F, V = geo.hidden, geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim, geo.ffn, geo.vocab
+    weights = (geo.n_layers * (qd * H + 2 * kvd * H + H * qd + 3 * F * H) + V * H) * 34 // 32
+    kv = geo.n_layers * 2 * context * kvd * 2
+    algo = weights + kv
+    return {"config": f"8B-shape Q8_0, 16-node draft tree (parents {C4_PARENTS}), context {context}, batch 1",
+            "ms_per_window": sec * 1e3, "windows_per_s": 1.0 / sec,
+            "batch8_ms": 8 * sec * 1e3,
+            "roofline": {"bound": "hbm", "algorithmic_bytes": algo, "weight_bytes": weights, "kv_bytes": kv,
+                         "achieved": algo / sec / 1e9, "peak": peak, "unit": "GB/s", "frac": algo / sec / 1e9 / peak}}
+
+
 def run_b200(args, world, rank, local):
     import numpy as np
     import torch
@@ -402,6 +453,7 @@ def run_b200(args, world, rank, local):
     eng.close_session(1)
     eng.close()
     micro = acceptance_micro(ctx, dev, peak, not args.no_cpu) if (world == 1 and not profile_case(args)) else None
+    tree = tree_micro(ctx, dev, peak, context) if (world == 1 and not profile_case(args)) else None
     ctx.close()
 
     if rank != 0:
@@ -437,6 +489,8 @@ def run_b200(args, world, rank, local):
                                 "sample": cpu["sample"]}
     if micro:
         line["acceptance_micro"] = micro
+    if tree:
+        line["tree_window"] = tree
     print(json.dumps(line), flush=True)
 
 

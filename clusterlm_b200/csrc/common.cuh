@@ -46,6 +46,10 @@ struct clm_b200_ctx {
   // Grow-only device scratch for temporaries of a single call (row statistics, partial sums).
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
+  // Objects created on this context (engines, matrices, links) that are still alive.  clm_b200_ctx_destroy
+  // while some are alive only marks the context closed; the last object's destruction frees it.
+  int refs = 0;
+  bool closed = false;
 };
 
 namespace clm {
@@ -54,6 +58,9 @@ namespace clm {
 int ctx_scratch(clm_b200_ctx* ctx, size_t bytes, void** out);
 // Makes ctx->device current for the calling thread.
 int ctx_enter(clm_b200_ctx* ctx);
+// An object created on ctx holds it (retain) until it is destroyed (release frees a closed, unused context).
+void ctx_retain(clm_b200_ctx* ctx);
+void ctx_release(clm_b200_ctx* ctx);
 inline cudaStream_t pick_stream(clm_b200_ctx* ctx, void* s) { return s ? static_cast<cudaStream_t>(s) : ctx->stream; }
 
 // ---- device helpers ----

@@ -32,6 +32,22 @@ int ctx_enter(clm_b200_ctx* ctx) {
   return CLM_OK;
 }
 
+void ctx_retain(clm_b200_ctx* ctx) {
+  if (ctx) ++ctx->refs;
+}
+
+static void ctx_free(clm_b200_ctx* ctx) {
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+void ctx_release(clm_b200_ctx* ctx) {
+  if (ctx && --ctx->refs <= 0 && ctx->closed) ctx_free(ctx);
+}
+
 int ctx_scratch(clm_b200_ctx* ctx, size_t bytes, void** out) {
   if (bytes > ctx->scratch_bytes) {
     CLM_CUDA(cudaStreamSynchronize(ctx->stream));
@@ -98,12 +114,9 @@ int clm_b200_ctx_create(int device, clm_b200_ctx** out) {
 }
 
 int clm_b200_ctx_destroy(clm_b200_ctx* ctx) {
-  if (ctx == nullptr) return CLM_OK;
-  cudaSetDevice(ctx->device);
-  cudaStreamSynchronize(ctx->stream);
-  if (ctx->scratch) cudaFree(ctx->scratch);
-  cudaStreamDestroy(ctx->stream);
-  delete ctx;
+  if (ctx == nullptr || ctx->closed) return CLM_OK;
+  ctx->closed = true;
+  if (ctx->refs <= 0) ctx_free(ctx);  // else the last object created on it frees it
   return CLM_OK;
 }
 

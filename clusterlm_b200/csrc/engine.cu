@@ -164,6 +164,19 @@ __global__ void set_next_kernel(SessionState* __restrict__ st, const int32_t* __
   if (threadIdx.x == 0) st->next_token = *tok;
 }
 
+// Copies a device tree's parent array, replacing any entry that is not -1 or an earlier node by -1 and flagging
+// the window (kErrBadTree), so no ancestor walk can leave the window.
+constexpr int kErrBadTree = 6;
+__global__ void tree_guard_kernel(const int32_t* __restrict__ in, int q, int32_t* __restrict__ out, int* __restrict__ bad) {
+  const int i = threadIdx.x;
+  if (i < q) {
+    const int32_t p = in[i];
+    const bool ok = p >= -1 && p < i;
+    out[i] = ok ? p : -1;
+    if (!ok) atomicExch(bad, kErrBadTree);
+  }
+}
+
 __global__ void embed_guard_kernel(const int32_t* __restrict__ tokens, int q, int vocab, int32_t* __restrict__ out,
                                    int* __restrict__ bad) {
   griddep_wait();
@@ -629,6 +642,8 @@ struct LlamaEngine : clm_b200_engine {
       if (b == kErrLinkTimeout)
         return fail(CLM_DEADLINE_EXCEEDED, "a stage link wait gave up (the peer stage stopped or fell behind)");
       if (b == kErrLinkMismatch) return fail(CLM_VERSION_MISMATCH, "a stage link message has another window width");
+      if (b == kErrBadTree)
+        return fail(CLM_INVALID_ARGUMENT, "tree window: parent[i] must be -1 or an earlier node");
       return fail(CLM_INVALID_ARGUMENT, "token outside the vocabulary");
     }
     return CLM_OK;
@@ -720,6 +735,7 @@ int llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_
     CLM_CHECK(spec->layer_end > spec->layer_begin, CLM_INVALID_ARGUMENT, "middle domain needs at least one layer");
   auto* e = new LlamaEngine();
   e->ctx = ctx;
+  ctx_retain(ctx);
   e->family = CLM_FAMILY_LLAMA;
   e->geo = *g;
   e->spec = *spec;
@@ -1020,6 +1036,37 @@ int llama_run_window_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t
     CLM_CUDA(cudaMemcpyAsync(d_out, e->bout, rec, cudaMemcpyDeviceToDevice, st));
   }
   s->outstanding = q;  // out-of-range device tokens embed as zeros and are reported by llama_commit
+  return CLM_OK;
+}
+
+int llama_run_tree_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* d_parents,
+                          const int32_t* d_tokens, const float* d_in, float* d_out, float* d_logits, void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(d_parents != nullptr, CLM_INVALID_ARGUMENT, "null parents");
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  Session* s = nullptr;
+  CLM_TRY(run_window_common(e, id, base, q, st, &s));
+  const size_t rec = (size_t)q * e->floats_per_position() * sizeof(float);
+  if (e->has_tokens) {
+    CLM_CHECK(d_tokens != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes tokens");
+    CLM_CUDA(cudaMemcpyAsync(e->win, d_tokens, q * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  } else {
+    CLM_CHECK(d_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
+    CLM_CUDA(cudaMemcpyAsync(e->bin, d_in, rec, cudaMemcpyDeviceToDevice, st));
+  }
+  // device parents are validated on the device (a bad entry becomes -1 and the window reports an error at commit)
+  tree_guard_kernel<<<1, 32 * ((q + 31) / 32), 0, st>>>(d_parents, (int)q, e->parents, e->bad);
+  CLM_LAUNCHED("tree_guard_kernel");
+  CLM_TRY(e->run_graph(*s, 4, (int)q, 0, st,
+                       [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs, e->parents); }));
+  if (e->has_head) {
+    if (d_logits)
+      CLM_CUDA(cudaMemcpyAsync(d_logits, e->logits, (size_t)q * e->d.V * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  } else if (d_out) {
+    CLM_CUDA(cudaMemcpyAsync(d_out, e->bout, rec, cudaMemcpyDeviceToDevice, st));
+  }
+  s->outstanding = q;
+  s->tree = true;
   return CLM_OK;
 }
 

@@ -29,7 +29,10 @@ int clm_b200_fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* 
 }
 
 int clm_b200_engine_destroy(clm_b200_engine* e) {
+  if (e == nullptr) return CLM_OK;
+  clm_b200_ctx* ctx = e->ctx;
   delete e;
+  ctx_release(ctx);
   return CLM_OK;
 }
 
@@ -143,6 +146,14 @@ int clm_b200_spec_round_device(clm_b200_engine* e, uint64_t id, const clm_b200_s
   CLM_TRY(enter(e));
   CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "device-resident rounds are implemented for the Llama family");
   return llama_spec_round_device(llama(e), id, p, d_tokens, d_count, stream);
+}
+
+int clm_b200_run_tree_window_device(clm_b200_engine* e, uint64_t id, uint64_t base, uint32_t positions,
+                                    const int32_t* d_parents, const int32_t* d_tokens, const float* d_in, float* d_out,
+                                    float* d_logits, void* stream) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "tree windows are implemented for the Llama family");
+  return llama_run_tree_device(llama(e), id, base, positions, d_parents, d_tokens, d_in, d_out, d_logits, stream);
 }
 
 static int llama_only(clm_b200_engine* e) {

@@ -52,9 +52,31 @@ __device__ __forceinline__ float ftanh(float z) { return (float)tanh((double)z);
 __device__ __forceinline__ float fsilu(float z) { return z / (1.0f + fexp(-z)); }
 __device__ __forceinline__ float fsigmoid(float z) { return 1.0f / (1.0f + fexp(-z)); }
 
+// refmath::dot order (reference_math.hpp): acc += a[i] * b[i] for ascending i, each product and sum rounded
+// (this file is built without contraction).  The operands (global or shared) are fetched 16 at a time ahead of
+// the sums, so a row costs one memory latency per 16 elements instead of one per element; the arithmetic and its
+// order are unchanged.
 __device__ __forceinline__ float dotf(const float* a, const float* b, int n) {
   float acc = 0.0f;
-  for (int i = 0; i < n; ++i) acc += a[i] * b[i];
+  int i = 0;
+  if (((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0) {
+    for (; i + 16 <= n; i += 16) {
+      float4 wa[4], wb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        wa[j] = reinterpret_cast<const float4*>(a + i)[j];
+        wb[j] = reinterpret_cast<const float4*>(b + i)[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc += wa[j].x * wb[j].x;
+        acc += wa[j].y * wb[j].y;
+        acc += wa[j].z * wb[j].z;
+        acc += wa[j].w * wb[j].w;
+      }
+    }
+  }
+  for (; i < n; ++i) acc += a[i] * b[i];
   return acc;
 }
 
@@ -486,6 +508,7 @@ int fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* g, const 
       delete e;
       return fail(CLM_INVALID_ARGUMENT, "geometry: unknown layer kind");
     }
+  ctx_retain(ctx);
   FixParams& P = e->P;
   P.H = (int)g->hidden;
   P.hc = (int)g->residual_streams;

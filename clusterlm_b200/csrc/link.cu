@@ -221,6 +221,7 @@ int clm_b200_link_create(clm_b200_ctx* ctx, int end, uint32_t slots, uint64_t pa
     delete l;
     return cuda_fail(e, "link allocation");
   }
+  ctx_retain(ctx);
   *out = l;
   return CLM_OK;
 }
@@ -290,7 +291,9 @@ int clm_b200_link_destroy(clm_b200_link* link) {
   if (link->peer && link->peer_ipc) cudaIpcCloseMemHandle(link->peer);
   if (link->own) cudaFree(link->own);
   if (link->local) cudaFree(link->local);
+  clm_b200_ctx* ctx = link->ctx;
   delete link;
+  ctx_release(ctx);
   return CLM_OK;
 }
 

@@ -79,15 +79,21 @@ __device__ __forceinline__ bool visible(long long pos, long long base, int i, co
   return false;
 }
 
-// Shared memory of one attention CTA: kAttnWarps pages of K [64][HD] and V^T [HD][64] (fp16), staged by bulk copies.
+// Shared memory of one attention CTA: kAttnPages pages of K [64][HD] and V^T [HD][64] (fp16), staged by bulk copies.
 constexpr size_t attn_page_bytes(int hd) { return (size_t)kPageTokens * hd * sizeof(__half); }
-constexpr size_t attn_smem_bytes(int hd) { return (size_t)kAttnWarps * 2 * attn_page_bytes(hd); }
+constexpr size_t attn_smem_bytes(int hd) { return (size_t)kAttnPages * 2 * attn_page_bytes(hd); }
 
-// One CTA = kAttnWarps warps = kAttnWarps consecutive pages of one kv head for one m-tile of 16 query rows.
-// Each warp's page (K and V^T, 2 x 16 KB) is fetched with two cp.async.bulk copies into shared memory; pages
-// that hold only committed positions (all < base) are requested BEFORE griddepcontrol.wait, because the
-// preceding QKV GEMV writes only positions >= base, so under programmatic dependent launch the bulk of the KV
-// stream overlaps the previous kernel.  The page holding the window's own positions is requested after the wait.
+// One CTA = kAttnPages consecutive pages of one kv head for one m-tile of 16 query rows; two warps per page, warp
+// w taking positions [32*(w%2), 32*(w%2)+32) of page w/2.  Each page (K and V^T, 2 x 16 KB) is fetched with two
+// cp.async.bulk copies into shared memory; pages that hold only committed positions (all < base) are requested
+// BEFORE griddepcontrol.wait, because the preceding QKV GEMV writes only positions >= base, so under
+// programmatic dependent launch the bulk of the KV stream overlaps the previous kernel.  The page holding the
+// window's own positions is requested after the wait.
+//
+// Fragment mapping (mma m16n8k16, lane = 4g + t): in S = Q K^T, n-tile j column n is half-page position
+// p(j, n) = 8*(n/2) + 2j + n%2, so the C fragment of n-tile j holds positions 8t + 2j + {0, 1}; the P fragments
+// of S's n-tiles 2kk and 2kk+1 are then exactly the A fragment of the P.V k-step kk over positions
+// 8t + 4kk + {0..3}, whose B fragment is the lane's single V^T chunk (positions 8t..8t+7 of the half page).
 template <int HD>
 __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const __half* __restrict__ q16, const __half* __restrict__ kpool, const __half* __restrict__ vpool,
@@ -95,20 +101,22 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
     float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err) {
   static_assert(HD == 128, "head_dim 128 layout");
-  constexpr int RW = HD + 2;  // one partial row: O[HD], m, l
+  constexpr int RW = kAttnRowFloats;  // one partial row: O[HD], m, l, padding (16-byte aligned rows)
   constexpr uint32_t kPageBytes = (uint32_t)attn_page_bytes(HD);
   extern __shared__ __align__(128) uint8_t attn_smem[];
-  __shared__ __align__(8) uint64_t bar[kAttnWarps];
+  __shared__ __align__(8) uint64_t bar[kAttnPages];
   __shared__ int s_last;
   const int kvh = blockIdx.x, mt = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, g = lane / 4, t = lane % 4;
-  const int pg = blockIdx.y * kAttnWarps + warp;
-  __half* ks = reinterpret_cast<__half*>(attn_smem + (size_t)warp * 2 * kPageBytes);
+  const int wp = warp / 2, half = warp % 2;  // page within the CTA, half of that page
+  const int pg = blockIdx.y * kAttnPages + wp;
+  __half* ks = reinterpret_cast<__half*>(attn_smem + (size_t)wp * 2 * kPageBytes);
   __half* vs = ks + kPageTokens * HD;
-  float* sp = reinterpret_cast<float*>(ks);  // this warp's partial [16][RW], written over K once S is done
+  // this warp's partial [16][RW], written over its page once both warps of the page are done with it
+  float* sp = reinterpret_cast<float*>(attn_smem + (size_t)wp * 2 * kPageBytes) + half * 16 * RW;
 
   if (threadIdx.x == 0) {
-    for (int w = 0; w < kAttnWarps; ++w) mbar_init(&bar[w], 1);
+    for (int w = 0; w < kAttnPages; ++w) mbar_init(&bar[w], 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -116,27 +124,29 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
   const long long base = *d_pos;
   const long long nvis = base + q;
   const int npages = (int)((nvis + kPageTokens - 1) / kPageTokens);
-  const int ngroups = (npages + kAttnWarps - 1) / kAttnWarps;
+  const int ngroups = (npages + kAttnPages - 1) / kAttnPages;
   const bool active = pg < npages && pg < max_pages;
   const bool committed_page = (long long)(pg + 1) * kPageTokens <= base;
-  int32_t page = 0;
   auto request = [&]() {
-    page = pages[pg];
+    const int32_t page = pages[pg];
     const size_t off = ((size_t)page * nkv + kvh) * kPageTokens * HD;
-    mbar_expect_tx(&bar[warp], 2 * kPageBytes);
-    bulk_g2s(ks, kpool + off, kPageBytes, &bar[warp]);
-    bulk_g2s(vs, vpool + off, kPageBytes, &bar[warp]);
+    mbar_expect_tx(&bar[wp], 2 * kPageBytes);
+    bulk_g2s(ks, kpool + off, kPageBytes, &bar[wp]);
+    bulk_g2s(vs, vpool + off, kPageBytes, &bar[wp]);
   };
-  if (active && committed_page && lane == 0) request();
+  const bool requester = active && half == 0 && lane == 0;
+  if (requester && committed_page) request();
   griddep_wait();
   griddep_launch();
-  if (active && !committed_page && lane == 0) request();
+  if (requester && !committed_page) request();
 
   const int group = nh / nkv;
   const int r0 = mt * 16 + g, r1 = r0 + 8;
   const int i0 = r0 / group, i1 = r1 / group;
   const bool v0 = i0 < q, v1 = i1 < q;
   bool ok = active;
+  float O[HD / 8][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
   if (active) {
     // Q fragments: thread t holds head dims [32t, 32t+32) of rows r0 and r1 (the same k permutation as K below).
     uint4 qw0[4], qw1[4];
@@ -150,14 +160,13 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
         qw1[j] = v1 ? b[j] : z;
       }
     }
-    ok = mbar_wait(&bar[warp], 0, err);
+    ok = mbar_wait(&bar[wp], 0, err);
     if (ok) {
-      // S = Q K^T over the 64 positions of the page; n-tile j column c <-> position 16*(c/2) + 2j + c%2.
-      float S[8][4];
+      float S[4][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
-        const int pos = 16 * (g / 2) + 2 * j + (g % 2);
+        const int pos = 32 * half + 8 * (g / 2) + 2 * j + (g % 2);
         const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)pos * HD);
         uint4 kw[4];
 #pragma unroll
@@ -167,10 +176,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
           mma_f16(S[j], word_of(qw0, 2 * kk), word_of(qw1, 2 * kk), word_of(qw0, 2 * kk + 1), word_of(qw1, 2 * kk + 1),
                   word_of(kw, 2 * kk), word_of(kw, 2 * kk + 1));
       }
-      float m0 = -INFINITY, m1 = -INFINITY;
       if (committed_page) {  // every position is visible to every window row
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             S[j][e] = v0 ? S[j][e] * scale_log2 : -INFINITY;
@@ -180,10 +188,10 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
           }
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const long long pos = (long long)pg * kPageTokens + 16 * t + 2 * j + e;
+            const long long pos = (long long)pg * kPageTokens + 32 * half + 8 * t + 2 * j + e;
             S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
             S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
             m0 = fmaxf(m0, S[j][e]);
@@ -195,10 +203,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
         m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
         m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
       }
-      float l0 = 0.0f, l1 = 0.0f;
-      uint32_t pa[8][2];
+      uint32_t pa[4][2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 4; ++j) {
         const float p00 = m0 == -INFINITY ? 0.0f : exp2f(S[j][0] - m0);
         const float p01 = m0 == -INFINITY ? 0.0f : exp2f(S[j][1] - m0);
         const float p10 = m1 == -INFINITY ? 0.0f : exp2f(S[j][2] - m1);
@@ -213,59 +220,61 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
         l0 += __shfl_xor_sync(0xffffffffu, l0, o);
         l1 += __shfl_xor_sync(0xffffffffu, l1, o);
       }
-      __syncwarp();  // every lane is done with K: its space now takes the partial rows
-#pragma unroll 4
-      for (int jn = 0; jn < HD / 8; ++jn) {
-        float O[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const int vrow = 8 * jn + g;
-        const uint4* vr = reinterpret_cast<const uint4*>(vs + (size_t)vrow * kPageTokens);
-        const uint4 va = vr[kv_v_chunk(2 * t, vrow)], vb = vr[kv_v_chunk(2 * t + 1, vrow)];
-        const uint32_t vw[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_f16(O, pa[2 * kk][0], pa[2 * kk][1], pa[2 * kk + 1][0], pa[2 * kk + 1][1], vw[2 * kk], vw[2 * kk + 1]);
-        sp[g * RW + 8 * jn + 2 * t] = O[0];
-        sp[g * RW + 8 * jn + 2 * t + 1] = O[1];
-        sp[(g + 8) * RW + 8 * jn + 2 * t] = O[2];
-        sp[(g + 8) * RW + 8 * jn + 2 * t + 1] = O[3];
-      }
-      if (t == 0) {
-        sp[g * RW + HD] = m0;
-        sp[g * RW + HD + 1] = l0;
-        sp[(g + 8) * RW + HD] = m1;
-        sp[(g + 8) * RW + HD + 1] = l1;
+      for (int jn = 0; jn < HD / 8; ++jn) {
+        O[jn][0] = O[jn][1] = O[jn][2] = O[jn][3] = 0.0f;
+        const int vrow = 8 * jn + g;
+        const uint4 va = reinterpret_cast<const uint4*>(vs + (size_t)vrow * kPageTokens)[kv_v_chunk(4 * half + t, vrow)];
+        mma_f16(O[jn], pa[0][0], pa[0][1], pa[1][0], pa[1][1], va.x, va.y);
+        mma_f16(O[jn], pa[2][0], pa[2][1], pa[3][0], pa[3][1], va.z, va.w);
       }
     } else {
       // the copy never completed (error flag raised): give it one more bounded wait before the CTA can exit
-      mbar_wait(&bar[warp], 0, err);
+      mbar_wait(&bar[wp], 0, err);
     }
   }
-  if (!ok) {
-    for (int i = lane; i < 16; i += 32) {
-      sp[i * RW + HD] = -INFINITY;
-      sp[i * RW + HD + 1] = 0.0f;
+  // both warps of the page are done reading it: its space takes their partials
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + wp) : "memory");
+  if (active && ok) {
+#pragma unroll
+    for (int jn = 0; jn < HD / 8; ++jn) {
+      *reinterpret_cast<float2*>(sp + g * RW + 8 * jn + 2 * t) = make_float2(O[jn][0], O[jn][1]);
+      *reinterpret_cast<float2*>(sp + (g + 8) * RW + 8 * jn + 2 * t) = make_float2(O[jn][2], O[jn][3]);
     }
+    if (t == 0) {
+      sp[g * RW + HD] = m0;
+      sp[g * RW + HD + 1] = l0;
+      sp[(g + 8) * RW + HD] = m1;
+      sp[(g + 8) * RW + HD + 1] = l1;
+    }
+  } else if (lane < 16) {
+    sp[lane * RW + HD] = -INFINITY;
+    sp[lane * RW + HD + 1] = 0.0f;
   }
   __syncthreads();
-  auto spw = [&](int w) { return reinterpret_cast<const float*>(attn_smem + (size_t)w * 2 * kPageBytes); };
-  // combine the CTA's pages into one partial per (m-tile, kv head, page group)
+  auto spw = [&](int w) {
+    return reinterpret_cast<const float*>(attn_smem + (size_t)(w / 2) * 2 * kPageBytes) + (w % 2) * 16 * RW;
+  };
+  // combine the CTA's warps into one partial per (m-tile, kv head, page group)
   float* mine = part + (((size_t)mt * nkv + kvh) * max_pages + blockIdx.y) * 16 * RW;
   if ((int)blockIdx.y < ngroups) {
-    for (int i = threadIdx.x; i < 16 * RW; i += blockDim.x) {
-      const int r = i / RW, c = i % RW;
+    for (int i = threadIdx.x; i < 16 * (HD + 2); i += blockDim.x) {
+      const int r = i / (HD + 2), c = i % (HD + 2);
       float M = -INFINITY;
+#pragma unroll
       for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, spw(w)[r * RW + HD]);
       float a = 0.0f;
       if (c == HD) {
         a = M;
       } else {
+#pragma unroll
         for (int w = 0; w < kAttnWarps; ++w) {
           const float m = spw(w)[r * RW + HD];
           if (m == -INFINITY) continue;
           a += spw(w)[r * RW + c] * exp2f(m - M);
         }
       }
-      mine[i] = a;
+      mine[r * RW + c] = a;
     }
   }
   // the last CTA of this (m-tile, kv head) combines the page groups and writes W_o's input fragments
@@ -300,31 +309,50 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     for (int gi = 0; gi < ngroups; ++gi) wgt[gi * 16 + r] *= inv;
   }
   __syncthreads();
-  // one column per thread, the 16 rows in registers: 16 independent loads per page group
-  for (int c = threadIdx.x; c < HD; c += blockDim.x) {
-    float a[16];
+  {
+    // thread (row r, 8 columns c8): 16-byte loads, four page groups in flight
+    const int r = threadIdx.x / (HD / 8), c8 = threadIdx.x % (HD / 8);
+    float a[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) a[r] = 0.0f;
+    for (int k = 0; k < 8; ++k) a[k] = 0.0f;
+    const float* col = allp + (size_t)r * RW + 8 * c8;
     int gi = 0;
-    for (; gi + 2 <= ngroups; gi += 2) {
-      const float* p0 = allp + (size_t)gi * 16 * RW + c;
-      const float* p1 = p0 + 16 * RW;
-      float v0[16], v1[16];
+    for (; gi + 4 <= ngroups; gi += 4) {
+      float4 v[4][2];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        v0[r] = __ldcg(p0 + r * RW);
-        v1[r] = __ldcg(p1 + r * RW);
+      for (int u = 0; u < 4; ++u) {
+        const float4* p4 = reinterpret_cast<const float4*>(col + (size_t)(gi + u) * 16 * RW);
+        v[u][0] = __ldcg(p4);
+        v[u][1] = __ldcg(p4 + 1);
       }
 #pragma unroll
-      for (int r = 0; r < 16; ++r) a[r] += v0[r] * wgt[gi * 16 + r] + v1[r] * wgt[(gi + 1) * 16 + r];
+      for (int u = 0; u < 4; ++u) {
+        const float w = wgt[(gi + u) * 16 + r];
+        a[0] += v[u][0].x * w;
+        a[1] += v[u][0].y * w;
+        a[2] += v[u][0].z * w;
+        a[3] += v[u][0].w * w;
+        a[4] += v[u][1].x * w;
+        a[5] += v[u][1].y * w;
+        a[6] += v[u][1].z * w;
+        a[7] += v[u][1].w * w;
+      }
     }
     for (; gi < ngroups; ++gi) {
-      const float* p0 = allp + (size_t)gi * 16 * RW + c;
-#pragma unroll
-      for (int r = 0; r < 16; ++r) a[r] += __ldcg(p0 + r * RW) * wgt[gi * 16 + r];
+      const float4* p4 = reinterpret_cast<const float4*>(col + (size_t)gi * 16 * RW);
+      const float4 x0 = __ldcg(p4), x1 = __ldcg(p4 + 1);
+      const float w = wgt[gi * 16 + r];
+      a[0] += x0.x * w;
+      a[1] += x0.y * w;
+      a[2] += x0.z * w;
+      a[3] += x0.w * w;
+      a[4] += x1.x * w;
+      a[5] += x1.y * w;
+      a[6] += x1.z * w;
+      a[7] += x1.w * w;
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r) o_s[r * HD + c] = a[r];
+    for (int k = 0; k < 8; ++k) o_s[r * HD + 8 * c8 + k] = a[k];
   }
   __syncthreads();
   if (threadIdx.x == 0) counters[mt * nkv + kvh] = 0;
@@ -348,10 +376,10 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
   const size_t smem = attn_smem_bytes(128);
-  CLM_CHECK((size_t)16 * 128 * 4 + (size_t)((max_pages + kAttnWarps - 1) / kAttnWarps) * 32 * 4 <= smem,
+  CLM_CHECK((size_t)16 * 128 * 4 + (size_t)((max_pages + kAttnPages - 1) / kAttnPages) * 32 * 4 <= smem,
             CLM_RESOURCE_EXHAUSTED, "attention: max_context too large for the page-group combine");
   CLM_TRY(ensure_smem(attention_kernel<128>, smem));
-  return launch_pdl(attention_kernel<128>, dim3(d.nkv, (max_pages + kAttnWarps - 1) / kAttnWarps, mtiles),
+  return launch_pdl(attention_kernel<128>, dim3(d.nkv, (max_pages + kAttnPages - 1) / kAttnPages, mtiles),
                     dim3(32 * kAttnWarps), smem, st, d_q, d_k, d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv,
                     scale_log2, max_pages, d_part, d_counters, nt_out, hi_scale, static_cast<uint2*>(d_frag), d_sum,
                     d_err);

@@ -8,7 +8,9 @@
 namespace clm {
 
 constexpr int kPageTokens = 64;  // KV page: 64 positions of one KV head
-constexpr int kAttnWarps = 4;    // pages per attention CTA (one per warp)
+constexpr int kAttnPages = 4;    // pages per attention CTA
+constexpr int kAttnWarps = 8;    // warps per attention CTA (two per page, half a page each)
+constexpr int kAttnRowFloats = 132;  // one partial row: O[128], m, l, 2 floats of padding (16-byte aligned rows)
 
 struct LlamaDims {
   int H = 0, nh = 0, nkv = 0, hd = 0, F = 0, V = 0;
@@ -27,13 +29,13 @@ __host__ __device__ __forceinline__ int kv_k_chunk(int c, int pos) { return c ^ 
 __host__ __device__ __forceinline__ int kv_v_chunk(int c, int d) { return c ^ (d & 1); }
 
 // Attention partials of one (m-tile, kv head, page): 16 rows x (hd values + m + l).
-inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 2); }
+inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 4); }
 
 int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int q, int H, float* d_h, cudaStream_t st);
 // Paged split-KV attention for q window rows: pages staged in shared memory by bulk copies (committed pages
-// before griddepcontrol.wait), CTAs combine their 4 pages, and the last CTA of each (m-tile, kv head) combines
+// before griddepcontrol.wait), CTAs combine their 4 pages (8 warps), and the last CTA of each (m-tile, kv head) combines
 // all page groups and writes W_o's input fragments (out_frag / out_sum, qd columns).
-// d_part holds mtiles*nkv*max_pages*16*(hd+2) floats; d_counters mtiles*nkv zeroed ints; a bounded wait that
+// d_part holds mtiles*nkv*max_pages*attn_partial_floats(hd) floats; d_counters mtiles*nkv zeroed ints; a bounded wait that
 // gives up stores kErrWaitTimeout in *d_err.
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,

@@ -107,6 +107,7 @@ int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_s
     delete m;
     return status;
   }
+  ctx_retain(ctx);
   *out = m;
   return CLM_OK;
 }
@@ -157,7 +158,9 @@ int clm_b200_matrix_free(clm_b200_matrix* m) {
   cudaSetDevice(m->ctx->device);
   cudaStreamSynchronize(m->ctx->stream);
   if (m->data) cudaFree(m->data);
+  clm_b200_ctx* ctx = m->ctx;
   delete m;
+  ctx_release(ctx);
   return CLM_OK;
 }
 

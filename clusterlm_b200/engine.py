@@ -194,6 +194,17 @@ class Engine:
              None if has_head else out.ctypes.data_as(_vp), out.ctypes.data_as(_vp) if has_head else None)
         return out
 
+    def run_tree_window_device(self, session: int, base: int, d_parents, d_tokens=None, d_out=None, stream=None,
+                               d_records=None):
+        """Device-buffer tree window (torch CUDA tensors): parents, tokens or records in; logits or records out."""
+        q = d_parents.shape[0]
+        has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
+        call("clm_b200_run_tree_window_device", self.h, session, base, q, _vp(d_parents.data_ptr()),
+             None if d_tokens is None else _vp(d_tokens.data_ptr()),
+             None if d_records is None else _vp(d_records.data_ptr()),
+             None if has_head else _vp(d_out.data_ptr()), _vp(d_out.data_ptr()) if has_head else None,
+             None if stream is None else _vp(stream))
+
     def commit_path(self, session: int, path):
         """Keeps the root-to-node path (node indices) of the outstanding window."""
         path = _i32(path)

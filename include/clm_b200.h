@@ -212,6 +212,11 @@ CLM_API int clm_b200_commit(clm_b200_engine* e, uint64_t session, uint32_t accep
 CLM_API int clm_b200_run_tree_window(clm_b200_engine* e, uint64_t session, uint64_t base, uint32_t positions,
                                      const int32_t* h_parents, const int32_t* h_tokens, const float* h_in,
                                      float* h_out, float* h_logits);
+/* Same with device buffers; the parent array is validated on the device (an entry that is not -1 or an earlier
+ * node is replaced by -1 and the next commit reports CLM_INVALID_ARGUMENT). */
+CLM_API int clm_b200_run_tree_window_device(clm_b200_engine* e, uint64_t session, uint64_t base, uint32_t positions,
+                                            const int32_t* d_parents, const int32_t* d_tokens, const float* d_in,
+                                            float* d_out, float* d_logits, void* stream);
 /* Commits the accepted root-to-node path h_path[0..n) of the outstanding (tree or linear) window: the path's KV
  * rows move to slots base..base+n-1 and the committed position advances by n (commit_window's keep-prefix rule
  * for a tree). */

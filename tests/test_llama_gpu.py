@@ -309,3 +309,36 @@ def test_tree_window_refusals(ctx):
         e.commit_path(1, [0, 2, 3])  # 3's parent is 1, not 2
     e.commit_path(1, [0, 1, 3])
     assert e.position(1) == 3
+
+
+def test_tree_window_device_equals_host_and_guards_parents(ctx):
+    """The device-buffer tree window gives the host variant's logits bit for bit; a parent that is not -1 or an
+    earlier node is replaced on the device and the commit reports CLM_INVALID_ARGUMENT."""
+    import torch
+
+    from clusterlm_b200 import ClmError
+
+    geo = small_geo("q8_0")
+    e = make_engine(ctx, geo, max_context=256, max_window=16)
+    e.open_session(1)
+    rng = np.random.default_rng(9)
+    pre = rng.integers(0, geo.vocab, 16).astype(np.int32)
+    e.run_window(1, 0, tokens=pre)
+    e.commit(1, 16)
+    parents = np.array(_tree16(), np.int32)
+    toks = rng.integers(0, geo.vocab, 16).astype(np.int32)
+    want = e.run_tree_window(1, 16, parents, tokens=toks)
+    e.abort(1)
+    dev = torch.device("cuda:0")
+    out = torch.empty((16, geo.vocab), dtype=torch.float32, device=dev)
+    e.run_tree_window_device(1, 16, torch.from_numpy(parents).to(dev), torch.from_numpy(toks).to(dev), out)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), want)
+    e.commit_path(1, [0, 1])
+    bad = parents.copy()
+    bad[5] = 9  # a later node
+    e.run_tree_window_device(1, 18, torch.from_numpy(bad).to(dev), torch.from_numpy(toks).to(dev), out)
+    with pytest.raises(ClmError, match="earlier node"):
+        e.commit_path(1, [0])
+    assert e.position(1) == 18
+    e.close()
