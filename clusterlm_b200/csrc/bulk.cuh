@@ -74,4 +74,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// Release-add on a global counter (gpu scope): makes this thread's earlier writes, and those ordered before it by a
+// CTA barrier, visible to a reader that acquires the counter.
+__device__ __forceinline__ void red_release_add(int* ctr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ctr), "r"(v) : "memory");
+}
+
+// Waits until *ctr >= target with acquire loads (gpu scope); false (and *err = kErrWaitTimeout) after kSpinLimit
+// polls.
+__device__ __forceinline__ bool wait_count(const int* ctr, int target, int* err) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (i >= 64) __nanosleep(64);
+  }
+  if (err != nullptr) atomicExch(err, kErrWaitTimeout);
+  return false;
+}
+
 }  // namespace clm

@@ -15,8 +15,9 @@
 //    k-steps on separate accumulators), then releases the slot ("empty" mbarrier).  The two warps of a row
 //    tile fold their accumulators through shared memory when the CTA flushes a row group.
 //  * When a CTA's range leaves a row group it flushes the group: a group owned by one CTA goes straight to the
-//    epilogue; otherwise each CTA writes its segment's partial and the last one to arrive (atomic counter) sums
-//    the segments in index order (deterministic) and runs the epilogue.
+//    epilogue; otherwise the later segments publish their partials (release-add on the group's counter) and move
+//    on, and the group's first segment, which reaches the group at the end of its range, waits for them (bounded
+//    acquire spin), sums the segments in index order (deterministic) and runs the epilogue.
 //  * Every mbarrier wait is bounded (bulk.cuh); a timeout raises the epilogue's error flag.
 #include "gemv_core.cuh"
 #include "pdl.cuh"

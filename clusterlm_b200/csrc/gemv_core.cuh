@@ -1,6 +1,6 @@
 // gemv_core.cuh — building blocks of the persistent q-row GEMV shared by the single-matrix kernel (gemv4.cu)
 // and the verify-window megakernel (window.cu): consumer warp roles, the per-unit tensor-core step, row-group
-// flush (segment partials + last-arriver reduction) and the fused epilogues.
+// flush (segment partials reduced by the group's first segment) and the fused epilogues.
 #pragma once
 #include "bulk.cuh"
 #include "gemv2.cuh"
@@ -284,8 +284,11 @@ __device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom&
 }
 
 // Flush row group `grp` of a stream-K range: fold the two superblock warps into y (fixed order); a group owned by
-// this CTA alone goes to the epilogue, otherwise the segment partial is published and the last CTA to arrive sums
-// the segments in index order and runs the epilogue.  Consumer threads only.
+// this CTA alone goes to the epilogue.  Otherwise a later segment publishes its partial (release-add on the group's
+// counter by one thread after the consumer barrier) and continues without waiting, and the group's first segment
+// waits (bounded acquire spin) for the other nseg-1 partials, sums them in segment order, resets the counter and
+// runs the epilogue.  Every CTA of the grid is resident (one per SM), so the wait always ends.  Consumer threads
+// only.
 template <int NT>
 __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
                          long long U, int G, long long u0, int ppr, int q, uint32_t rows, int epi_kind, const Epi& epi,
@@ -308,18 +311,26 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     return;
   }
   if (nseg > 1) {
-    float* mine = part + ((size_t)grp * maxseg + seg) * q * 128;
-    for (int i = tid; i < q * 128; i += kG4Consumers) mine[i] = y[i];
-    __threadfence();
-    consumer_sync();
-    if (tid == 0) *s_last = atomicAdd(&counters[grp], 1) == nseg - 1;
+    if (seg > 0) {
+      // a later segment publishes its partial and moves on; the group's first segment (whose CTA reaches the
+      // group at the end of its range) reduces it
+      float* mine = part + ((size_t)grp * maxseg + seg) * q * 128;
+      for (int i = tid; i < q * 128; i += kG4Consumers) mine[i] = y[i];
+      consumer_sync();
+      if (tid == 0) red_release_add(&counters[grp], 1);
+      return;
+    }
+    if (tid == 0) {
+      const bool ok = wait_count(&counters[grp], nseg - 1, epi.err);
+      if (ok) counters[grp] = 0;  // every arrival of this launch is in: ready for the next launch
+      *s_last = ok;
+    }
     consumer_sync();
     if (!*s_last) return;
-    __threadfence();
     const float* all = part + (size_t)grp * maxseg * q * 128;
     for (int i = tid; i < q * 128; i += kG4Consumers) {
-      float a = 0.0f;
-      int k = 0;
+      float a = y[i];
+      int k = 1;
       for (; k + 4 <= nseg; k += 4) {
         const float v0 = __ldcg(all + (size_t)k * q * 128 + i), v1 = __ldcg(all + (size_t)(k + 1) * q * 128 + i);
         const float v2 = __ldcg(all + (size_t)(k + 2) * q * 128 + i), v3 = __ldcg(all + (size_t)(k + 3) * q * 128 + i);
@@ -331,7 +342,6 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
       for (; k < nseg; ++k) a += __ldcg(all + (size_t)k * q * 128 + i);
       y[i] = a;
     }
-    if (tid == 0) counters[grp] = 0;
     consumer_sync();
   }
   g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi);

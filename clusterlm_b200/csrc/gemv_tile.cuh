@@ -25,6 +25,13 @@ static __device__ __forceinline__ void mma16816(float c[4], uint32_t a0, uint32_
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// (a & MASK) | c in one LOP3 (c held in a register, so the mask can be the instruction's immediate).
+template <uint32_t MASK>
+static __device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(MASK), "r"(c));
+  return d;
+}
 static __device__ __forceinline__ uint32_t lo_bcast(uint32_t x) { return __byte_perm(x, x, 0x1010); }
 static __device__ __forceinline__ uint32_t hi_bcast(uint32_t x) { return __byte_perm(x, x, 0x3232); }
 
@@ -132,15 +139,17 @@ static __device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const u
   const RowDq dg = q4k_row(r.rg, t), dg8 = q4k_row(r.rg8, t);
   negm_g = dg.negm;
   negm_g8 = dg8.negm;
+  uint32_t magic;  // the exponent pattern in a register: each nibble pair is then one LOP3
+  asm volatile("mov.b32 %0, %1;" : "=r"(magic) : "n"(kMagic));
 #pragma unroll
   for (int s = 0; s < 16; ++s) {
     const uint4& qq = r.q[s / 4];
     const uint32_t w = (s % 4 == 0) ? qq.x : (s % 4 == 1) ? qq.y : (s % 4 == 2) ? qq.z : qq.w;
     const uint32_t w8 = w >> 8;
-    const uint32_t a0 = hfma2u((w & 0x000F000Fu) | kMagic, dg.sA, dg.nA);
-    const uint32_t a1 = hfma2u((w8 & 0x000F000Fu) | kMagic, dg8.sA, dg8.nA);
-    const uint32_t a2 = hfma2u((w & 0x00F000F0u) | kMagic, dg.sB, dg.nB);
-    const uint32_t a3 = hfma2u((w8 & 0x00F000F0u) | kMagic, dg8.sB, dg8.nB);
+    const uint32_t a0 = hfma2u(and_or<0x000F000Fu>(w, magic), dg.sA, dg.nA);
+    const uint32_t a1 = hfma2u(and_or<0x000F000Fu>(w8, magic), dg8.sA, dg8.nA);
+    const uint32_t a2 = hfma2u(and_or<0x00F000F0u>(w, magic), dg.sB, dg.nB);
+    const uint32_t a3 = hfma2u(and_or<0x00F000F0u>(w8, magic), dg8.sB, dg8.nB);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint2 b = xf[(nt * 16 + s) * 32 + lane];
