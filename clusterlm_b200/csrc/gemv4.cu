@@ -6,14 +6,18 @@
 // [c*U/G, (c+1)*U/G).  Every unit is ~37 KB (Q4_K) / ~70 KB (Q8_0) of weights, so every CTA streams the same
 // number of bytes whatever the matrix shape.
 //
-//  * Warp 8 is the producer: one lane keeps a ring of `stages` shared-memory slots full with cp.async.bulk
-//    copies (no multicast) of the unit's weights, activation fragments and sub-block sums, completing on the
-//    slot's "full" mbarrier.  The first `stages` weight copies are issued before griddepcontrol.wait (weights are
-//    immutable), so under programmatic dependent launch they stream in while the previous kernel finishes.
-//  * Warps 0..15 consume: warp w dequantises row tile w % 8 of superblock w / 8 of the unit in registers
-//    (gemv_tile.cuh) and issues m16n8k16 tensor-core products against the staged fragments (even and odd
-//    k-steps on separate accumulators), then releases the slot ("empty" mbarrier).  The two warps of a row
-//    tile fold their accumulators through shared memory when the CTA flushes a row group.
+//  * Warp 16 is the producer: one lane keeps a ring of `stages` shared-memory slots (one unit each) full with
+//    cp.async.bulk copies (no multicast) of the unit's weights, activation fragments and sub-block sums,
+//    completing on the slot's "full" mbarrier.  The first `stages` weight copies are issued before
+//    griddepcontrol.wait (weights are immutable), so under programmatic dependent launch they stream in while the
+//    previous kernel finishes.
+//  * Warps 0..15 consume in two groups of eight: group w / 8 takes the units at even / odd positions of the CTA's
+//    range, warp w the row tile w % 8 of both superblocks of each.  A warp dequantises its tiles in registers
+//    (gemv_tile.cuh), issues m16n8k16 tensor-core products against the staged fragments (even and odd k-steps on
+//    separate accumulators, one min / bias mma pair per unit) and releases the slot ("empty" mbarrier, one
+//    arrival per warp of the group).  The two groups run half a
+//    unit apart, so their dequantisation bursts interleave and a slot is refilled as soon as its group is done.
+//    The groups fold their accumulators through shared memory when the CTA flushes a row group.
 //  * When a CTA's range leaves a row group it flushes the group: a group owned by one CTA goes straight to the
 //    epilogue; otherwise the later segments publish their partials (release-add on the group's counter) and move
 //    on, and the group's first segment, which reaches the group at the end of its range, waits for them (bounded
@@ -48,7 +52,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kG4Consumers / 32);
+      mbar_init(&empty[s], kGemvWarps);  // the eight warps of the group that consumes the slot's unit
     }
     mbar_fence_init();
   }
@@ -63,7 +67,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         const int nsb = min(2, geo.sb - 2 * c.pr);
         uint8_t* st = smem + (size_t)c.slot * geo.stage_bytes;
         const uint32_t wb = (uint32_t)(nsb * geo.sb_bytes);
-        const uint32_t ab = (uint32_t)(nsb * NT * kXfragSbBytes + 2 * nsb * 512);
+        const uint32_t ab = (uint32_t)(nsb * NT * kXfragSbBytes + 2 * nsb * kG4SbSumBytes);
         mbar_expect_tx(&full[c.slot], wb + ab);
         bulk_g2s_stream(st, tiles + ((size_t)c.grp * geo.sb + 2 * c.pr) * geo.sb_bytes, wb, &full[c.slot], policy);
       };
@@ -73,8 +77,8 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         bulk_g2s(st + geo.frag_off, in.frag + (size_t)2 * c.pr * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
                  &full[c.slot]);
         for (int h = 0; h < 2; ++h)
-          bulk_g2s(st + geo.sum_off + h * kG4SumBytes, in.sum + ((size_t)h * nsub + 16 * c.pr) * 16,
-                   (uint32_t)(nsb * 512), &full[c.slot]);
+          bulk_g2s(st + geo.sum_off + h * geo.sum_half, in.sum + ((size_t)h * nsub + 16 * c.pr) * 16,
+                   (uint32_t)(nsb * kG4SbSumBytes), &full[c.slot]);
       };
       const int pre = min(n, stages);
       UnitCursor w = start, a = start;
@@ -97,12 +101,14 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
   // ---------------- consumers ----------------
   griddep_wait();
   griddep_launch();
+  const int grp_of_warp = warp / kGemvWarps, rt = warp % kGemvWarps;
   const G4SsPre ss_pre = g4_ss_load(in);
   bool scale_ready = false;
   G4Acc<NT> acc;
   acc.zero();
   int cur = n > 0 ? start.grp : -1;
   UnitCursor c = start;
+  // both groups walk every unit of the range, so they flush the same row groups at the same points
   for (int i = 0; i < n; ++i, c.next(geo.ppr, stages)) {
     if (c.grp != cur) {
       g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
@@ -110,9 +116,9 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
       cur = c.grp;
       acc.zero();
     }
-    const int nsb = min(2, geo.sb - 2 * c.pr);
+    if ((i & 1) != grp_of_warp) continue;
     mbar_wait(&full[c.slot], c.phase, epi.err);
-    g4_consume_unit<Raw, NT>(smem + (size_t)c.slot * geo.stage_bytes, geo, nsb, warp, lane, acc);
+    g4_consume_pair<Raw, NT>(smem + (size_t)c.slot * geo.stage_bytes, geo, min(2, geo.sb - 2 * c.pr), rt, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[c.slot]);
   }
@@ -168,7 +174,7 @@ static int launch4(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles
                    const Epi& epi, float* part, int* counters, cudaStream_t st) {
   auto kern = gemv4_kernel<Raw, NT, EPI>;
   CLM_TRY(ensure_smem(kern, p.smem));
-  const G4Geom geo = g4_geom(s, NT);
+  const G4Geom geo = g4_geom(s, NT, 2);
   return launch_pdl(kern, dim3((unsigned)p.grid), dim3(kG4Threads), p.smem, st, d_tiles, s.rows, (int)s.ng, geo,
                     p.stages, in, q, epi, part, counters, p.ksplit);
 }

@@ -11,8 +11,8 @@ namespace clm {
 
 constexpr int kG4Consumers = 512;              // 16 consumer warps: 8 row tiles x 2 superblocks
 constexpr int kG4Threads = kG4Consumers + 32;  // + the producer warp
-constexpr int kG4MaxStages = 4;
-constexpr int kG4SumBytes = 16 * 16 * 4;       // one half of a unit's sub-block sums: [16 sub-blocks][16 p] f32
+constexpr int kG4MaxStages = 10;
+constexpr int kG4SbSumBytes = 8 * 16 * 4;      // one half of one superblock's sub-block sums: [8 sub-blocks][16 p] f32
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
@@ -44,11 +44,13 @@ __device__ __forceinline__ void group_segments(long long x, long long y, long lo
 
 struct G4Geom {
   int sb;          // superblocks per row
-  int ppr;         // units (superblock pairs) per row group
+  int usb;         // superblocks per unit (1: the single-matrix GEMV, 2: the window megakernel)
+  int ppr;         // units per row group
   int tile_bytes;  // one 16-row x 256-column tile
   int sb_bytes;    // 8 tiles of one superblock
   int stage_bytes;
-  int frag_off, sum_off;  // offsets inside a stage: [weights 2 sb][fragments 2 sb x NT][sums half 0][half 1]
+  int sum_half;    // bytes of one half of a unit's sub-block sums (usb x kG4SbSumBytes)
+  int frag_off, sum_off;  // offsets inside a stage: [weights usb sb][fragments usb sb x NT][sums half 0][half 1]
 };
 
 // Position in a CTA's unit range without divisions in the loops: (row group, superblock pair) of the unit and
@@ -246,15 +248,15 @@ struct G4Acc {
   }
 };
 
-// One unit (superblock pair of a row group) staged at `st`: this warp's tile of superblock hh.
+// Row tile rt of superblock hh of the unit staged at `st` (nsb superblocks in the unit): dequantised tensor-core
+// products into acc, then the unit's min / bias term for this superblock.
 template <typename Raw, int NT>
-__device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom& geo, int nsb, int warp, int lane,
-                                                G4Acc<NT>& acc) {
-  const int rt = warp % kGemvWarps, hh = warp / kGemvWarps, t = lane % 4, g = lane / 4;
-  if (hh >= nsb) return;
+__device__ __forceinline__ void g4_consume_tile(const uint8_t* st, const G4Geom& geo, int hh, int nsb, int rt,
+                                                int lane, G4Acc<NT>& acc) {
+  const int t = lane % 4, g = lane / 4;
   const uint2* xf = reinterpret_cast<const uint2*>(st + geo.frag_off) + hh * NT * 512;
   const float* s0 = reinterpret_cast<const float*>(st + geo.sum_off);
-  const float* s1 = s0 + kG4SumBytes / 4;
+  const float* s1 = s0 + geo.sum_half / 4;
   uint32_t mg, mg8;
   Raw r;
   load_raw_s(r, st + (size_t)hh * geo.sb_bytes + (size_t)rt * geo.tile_bytes, lane);
@@ -281,6 +283,55 @@ __device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom&
     mma16816(acc.v[0][nt], a0, a1, a2, a3, h2u(h01), h2u(h23));
     mma16816(acc.v[1][nt], a0, a1, a2, a3, h2u(l01), h2u(l23));
   }
+}
+
+// Both superblocks of the unit staged at `st` (nsb of them) for row tile rt: one warp's whole share of the unit,
+// with one min / bias mma pair for the two superblocks together.
+template <typename Raw, int NT>
+__device__ __forceinline__ void g4_consume_pair(const uint8_t* st, const G4Geom& geo, int nsb, int rt, int lane,
+                                                G4Acc<NT>& acc) {
+  const int t = lane % 4, g = lane / 4;
+  const uint2* xf = reinterpret_cast<const uint2*>(st + geo.frag_off);
+  const float* s0 = reinterpret_cast<const float*>(st + geo.sum_off);
+  const float* s1 = s0 + geo.sum_half / 4;
+  uint32_t m0 = 0u, m08 = 0u, m1 = 0u, m18 = 0u;
+  {
+    Raw r;
+    load_raw_s(r, st + (size_t)rt * geo.tile_bytes, lane);
+    tile_mmas<NT>(r, t, xf, lane, acc.v, m0, m08);
+  }
+  if (nsb > 1) {
+    Raw r;
+    load_raw_s(r, st + (size_t)geo.sb_bytes + (size_t)rt * geo.tile_bytes, lane);
+    tile_mmas<NT>(r, t, xf + NT * 512, lane, acc.v, m1, m18);
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int p = nt * 8 + g;
+    float v[4];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int sub = h2 * 8 + 2 * t + e;
+        v[2 * h2 + e] = h2 < nsb ? s0[sub * 16 + p] + s1[sub * 16 + p] : 0.0f;
+      }
+    const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(v[0] - f01.x, v[1] - f01.y);
+    const __half2 l23 = __floats2half2_rn(v[2] - f23.x, v[3] - f23.y);
+    mma16816(acc.v[0][nt], m0, m08, m1, m18, h2u(h01), h2u(h23));
+    mma16816(acc.v[1][nt], m0, m08, m1, m18, h2u(l01), h2u(l23));
+  }
+}
+
+// One unit (superblock pair of a row group) staged at `st`: this warp's tile of superblock hh = warp / 8.
+template <typename Raw, int NT>
+__device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom& geo, int nsb, int warp, int lane,
+                                                G4Acc<NT>& acc) {
+  const int rt = warp % kGemvWarps, hh = warp / kGemvWarps;
+  if (hh >= nsb) return;
+  g4_consume_tile<Raw, NT>(st, geo, hh, nsb, rt, lane, acc);
 }
 
 // Flush row group `grp` of a stream-K range: fold the two superblock warps into y (fixed order); a group owned by
@@ -347,16 +398,18 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
   g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi);
 }
 
-// Geometry of a tiled matrix in the persistent GEMV for `nt` column tiles.
-inline G4Geom g4_geom(const GemvShape& s, int nt) {
+// Geometry of a tiled matrix in the persistent GEMV for `nt` column tiles and units of `usb` superblocks.
+inline G4Geom g4_geom(const GemvShape& s, int nt, int usb = 2) {
   G4Geom geo;
   geo.sb = (int)s.sb;
-  geo.ppr = (int)(s.sb + 1) / 2;
+  geo.usb = usb;
+  geo.ppr = (int)(s.sb + usb - 1) / usb;
   geo.tile_bytes = s.tile_bytes;
   geo.sb_bytes = kGemvWarps * s.tile_bytes;
-  geo.frag_off = 2 * geo.sb_bytes;
-  geo.sum_off = geo.frag_off + 2 * nt * kXfragSbBytes;
-  geo.stage_bytes = geo.sum_off + 2 * kG4SumBytes;
+  geo.sum_half = usb * kG4SbSumBytes;
+  geo.frag_off = usb * geo.sb_bytes;
+  geo.sum_off = geo.frag_off + usb * nt * kXfragSbBytes;
+  geo.stage_bytes = geo.sum_off + 2 * geo.sum_half;
   return geo;
 }
 

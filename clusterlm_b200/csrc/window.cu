@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) window_mk_kernel(MkParams P) {
           bulk_g2s(st + m.geo.frag_off, m.in.frag + (size_t)2 * pr2 * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
                    bar);
           for (int h = 0; h < 2; ++h)
-            bulk_g2s(st + m.geo.sum_off + h * kG4SumBytes, m.in.sum + ((size_t)h * nsub + 16 * pr2) * 16,
+            bulk_g2s(st + m.geo.sum_off + h * m.geo.sum_half, m.in.sum + ((size_t)h * nsub + 16 * pr2) * 16,
                      (uint32_t)(nsb * 512), bar);
         } else if ((long long)(pr2 + 1) * 64 > base) {
           const MkAttn& a = ph.a;
