@@ -74,6 +74,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   return false;
 }
 
+// L2 prefetch of global bytes (no shared memory, no completion to wait for): src 16-byte aligned, bytes a multiple
+// of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Prefetches into L2 the first `cap` bytes of share c of [base, base + total) split into G contiguous shares (the
+// way a G-CTA stream-K kernel splits its operand), in pieces of at most 32 KB.
+__device__ __forceinline__ void l2_prefetch_share(const uint8_t* base, unsigned long long total, int c, int G,
+                                                  unsigned long long cap) {
+  if (base == nullptr || G <= 0) return;
+  const unsigned long long lo = (total * (unsigned long long)c / G) & ~15ull;
+  unsigned long long hi = (total * (unsigned long long)(c + 1) / G) & ~15ull;
+  if (hi > lo + cap) hi = lo + (cap & ~15ull);
+  for (unsigned long long o = lo; o < hi; o += 32768ull) {
+    const unsigned long long n = hi - o < 32768ull ? hi - o : 32768ull;
+    bulk_prefetch_l2(base + o, (uint32_t)n);
+  }
+}
+
 // Release-add on a global counter (gpu scope): makes this thread's earlier writes, and those ordered before it by a
 // CTA barrier, visible to a reader that acquires the counter.
 __device__ __forceinline__ void red_release_add(int* ctr, int v) {

@@ -316,6 +316,14 @@ struct LlamaEngine : clm_b200_engine {
     return e;
   }
 
+  // L2 lookahead of the next GEMV of the chain: each CTA prefetches the first bytes of the matching CTA range of
+  // `next` (up to its ring's worth) once its own copies are issued
+  static void lookahead(Epi& e, const Gemv& next) {
+    e.pf = static_cast<const uint8_t*>(next.m->data);
+    e.pf_bytes = next.m->shape.bytes();
+    e.pf_cap = 256 * 1024;
+  }
+
   // ---- the layer range over q rows; h holds the stage input and xa its first norm's preparation
   int enqueue_layers(Session& s, int q, const int32_t* parent, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
@@ -334,24 +342,35 @@ struct LlamaEngine : clm_b200_engine {
       ek.vpool = vpool[li];
       ek.q16 = q16;
       ek.parent = parent;
+      ek.pf_kv = true;  // the attention's KV pages into L2 while the QKV GEMV drains
+      ek.pf_max_pages = max_pages;
       CLM_TRY(gemv(L.qkv, q, xa, ek, st));
-      // attention -> xb (W_o input)
+      // attention -> xb (W_o input); W_o into L2 meanwhile
       CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, parent, q, d, max_pages, attn_part, acount,
-                               nt, hi_scale(), xb.frag, xb.sum, bad, st));
+                               nt, hi_scale(), xb.frag, xb.sum, bad, static_cast<const uint8_t*>(L.o.m->data),
+                               L.o.m->shape.bytes(), ctx->sm_count, st));
       XBuf ob = xb;
       ob.ss = nullptr;
       // h += W_o o ; xa = h * ffn_norm (+ sum of squares)
-      CLM_TRY(gemv(L.o, q, ob, epi_resid(h, L.ffn_norm, xa), st));
+      Epi eo = epi_resid(h, L.ffn_norm, xa);
+      lookahead(eo, L.gu);
+      CLM_TRY(gemv(L.o, q, ob, eo, st));
       // SwiGLU of the gate/up rows -> xb (W_down input)
       Epi es = epi_base(EPI_SWIGLU_PREP);
       es.ffn = d.F;
       es.next = xb;
+      lookahead(es, L.down);
       CLM_TRY(gemv(L.gu, q, xa, es, st));
       // h += W_down a ; xa = h * (next layer's attn_norm | output norm | 1)
       const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
       XBuf db = xb;
       db.ss = nullptr;
-      CLM_TRY(gemv(L.down, q, db, epi_resid(h, wnext, xa), st));
+      Epi ed = epi_resid(h, wnext, xa);
+      if (li + 1 < layers.size())
+        lookahead(ed, layers[li + 1].qkv);
+      else if (has_head)
+        lookahead(ed, head);
+      CLM_TRY(gemv(L.down, q, db, ed, st));
     }
     return CLM_OK;
   }
@@ -848,8 +867,8 @@ int llama_prepare(LlamaEngine* e) {
   CLM_TRY(e->alloc_t(&e->part, part_floats));
   CLM_TRY(e->alloc_t(&e->gcount, max_ng));
   CLM_CUDA(cudaMemset(e->gcount, 0, max_ng * sizeof(int)));
-  CLM_TRY(e->alloc_t(&e->acount, (size_t)mtiles * d.nkv));
-  CLM_CUDA(cudaMemset(e->acount, 0, (size_t)mtiles * d.nkv * sizeof(int)));
+  CLM_TRY(e->alloc_t(&e->acount, (size_t)2 * mtiles * d.nkv));  // attention arrival + departure counters
+  CLM_CUDA(cudaMemset(e->acount, 0, (size_t)2 * mtiles * d.nkv * sizeof(int)));
   for (XBuf* x : {&e->xa, &e->xb}) {
     CLM_TRY(e->alloc((void**)&x->frag, xfrag_bytes(maxcols, 2)));
     CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));

@@ -49,6 +49,14 @@ struct Epi {
   // EPI_SWIGLU_PREP: rows of the CTA's first tile are gate rows, second tile the matching up rows
   int ffn = 0;
   int* err = nullptr;  // set to 1 if a bounded wait gave up
+  // L2 lookahead: once a CTA's producer has issued its own copies it prefetches into L2 the first pf_cap bytes of
+  // its share of the next kernel's weights [pf, pf + pf_bytes) (split like the next kernel's stream-K ranges), so
+  // the next kernel's first copies hit L2 while this kernel drains.  With EPI_ROPE_KV and pf_kv the prefetch is
+  // instead this layer's KV pages [0, ceil((pos + q) / 64)) for the attention that follows.
+  const uint8_t* pf = nullptr;
+  unsigned long long pf_bytes = 0, pf_cap = 0;
+  bool pf_kv = false;
+  int pf_max_pages = 0;
 };
 
 // The fused GEMV (gemv4.cu) over the group-major tile layout of gemv.cuh.  `part` holds ng*p.ksplit*q*128 f32

@@ -91,6 +91,20 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         issue_weights(w);
         issue_acts(w);
       }
+      // every copy of this CTA is issued: prefetch the next kernel's first bytes into L2 while this one drains
+      if (EPI == EPI_ROPE_KV && epi.pf_kv) {
+        const long long vis = *epi.pos + q;
+        const long long npl = (vis + 63) / 64;
+        const int np = (int)(npl < epi.pf_max_pages ? npl : epi.pf_max_pages);
+        const size_t page_bytes = (size_t)epi.nkv * 64 * epi.hd * sizeof(__half);  // all kv heads of one page
+        for (int item = blockIdx.x; item < 2 * np; item += G) {
+          const __half* pool = (item & 1) ? epi.vpool : epi.kpool;
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(pool) + (size_t)epi.pages[item >> 1] * page_bytes;
+          l2_prefetch_share(src, page_bytes, 0, 1, page_bytes);
+        }
+      } else {
+        l2_prefetch_share(epi.pf, epi.pf_bytes, blockIdx.x, G, epi.pf_cap);
+      }
     } else {
       griddep_wait();
       griddep_launch();
@@ -107,13 +121,16 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
   G4Acc<NT> acc;
   acc.zero();
   int cur = n > 0 ? start.grp : -1;
+  EpiPre pre;
+  if (cur >= 0) epi_preload<EPI>(pre, cur, rows, q, epi);
   UnitCursor c = start;
   // both groups walk every unit of the range, so they flush the same row groups at the same points
   for (int i = 0; i < n; ++i, c.next(geo.ppr, stages)) {
     if (c.grp != cur) {
       g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
-                   in, scale_ready, s_red);
+                   in, scale_ready, s_red, &pre);
       cur = c.grp;
+      epi_preload<EPI>(pre, cur, rows, q, epi);
       acc.zero();
     }
     if ((i & 1) != grp_of_warp) continue;
@@ -123,7 +140,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
     if (lane == 0) mbar_arrive(&empty[c.slot]);
   }
   if (cur >= 0) g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
-                   in, scale_ready, s_red);
+                   in, scale_ready, s_red, &pre);
 }
 
 // x[p][0:cols] (row stride ld) * w -> fragments / sums (+ sum-of-squares partials per 128 columns); one warp per

@@ -16,6 +16,7 @@ constexpr int kG4SbSumBytes = 8 * 16 * 4;      // one half of one superblock's s
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 
+template <int EPI = 0>
 __device__ __forceinline__ long long tree_depth4(const int32_t* parent, int i) {
   long long d = 0;
   for (int a = parent[i]; a >= 0 && d < 64; a = parent[a]) ++d;
@@ -70,10 +71,52 @@ struct UnitCursor {
   }
 };
 
-// Epilogue over y[p][r] (128 rows of group grp) in shared memory; consumer threads only.
+// Epilogue operands that do not depend on this kernel's products (the residual rows and the next norm's weights,
+// or the position, page and RoPE factors), loaded when a CTA starts a row group so that their latency overlaps the
+// group's tensor-core work and the segment exchange.  Element i = tid + kG4Consumers * k of the epilogue's loops.
+struct EpiPre {
+  float h[4];       // EPI_RESID_PREP: h[p][row0 + r], i = p * 128 + r
+  float w;          // EPI_RESID_PREP: wnext[row0 + tid] (tid < 128)
+  long long base;   // EPI_ROPE_KV: committed position
+  float2 cs[2];     // EPI_ROPE_KV: RoPE (cos, sin) of element i = p * (hd / 2) + pair
+  int32_t page[2];  // EPI_ROPE_KV: KV page of window row p
+};
+
+template <int EPI>
+__device__ __forceinline__ void epi_preload(EpiPre& pre, int grp, uint32_t rows, int q, const Epi& epi) {
+  const int tid = threadIdx.x, row0 = grp * 128;
+  if (EPI == EPI_RESID_PREP) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
+      pre.h[k] = (i < q * 128 && row0 + r < (int)rows) ? epi.h[(size_t)p * epi.H + row0 + r] : 0.0f;
+    }
+    pre.w = (tid < 128 && row0 + tid < (int)rows) ? epi.wnext[row0 + tid] : 0.0f;
+  } else if (EPI == EPI_ROPE_KV) {
+    const int hd = epi.hd, head = grp;
+    pre.base = *epi.pos;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + kG4Consumers * k, p = i / (hd / 2), pr = i % (hd / 2);
+      pre.cs[k] = make_float2(0.0f, 0.0f);
+      pre.page[k] = 0;
+      if (i < q * (hd / 2)) {
+        const long long slot = pre.base + p;
+        pre.page[k] = epi.pages[slot / 64];
+        if (head < epi.nh + epi.nkv) {
+          const long long rope_pos = epi.parent ? pre.base + tree_depth4<0>(epi.parent, p) : slot;
+          pre.cs[k] = epi.rope[(size_t)rope_pos * (hd / 2) + pr];
+        }
+      }
+    }
+  }
+}
+
+// Epilogue over y[p][r] (128 rows of group grp) in shared memory; consumer threads only.  `pre` holds the operands
+// preloaded by epi_preload (or null: they are read here); s_aux is shared scratch of at least 128 floats.
 template <int EPI>
 __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t rows, int q, const Epi& epi,
-                            float* s_ss) {
+                            float* s_aux, const EpiPre* pre) {
   const int tid = threadIdx.x;
   const int row0 = grp * 128;
   if (EPI == EPI_STORE) {
@@ -82,14 +125,16 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
       if (row0 + r < (int)rows) epi.out[(size_t)p * epi.out_ld + row0 + r] = y[i] * s_scale[p];
     }
   } else if (EPI == EPI_RESID_PREP) {
-    for (int i = tid; i < q * 128; i += kG4Consumers) {
-      const int p = i / 128, r = i % 128;
-      if (row0 + r >= (int)rows) continue;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
+      if (i >= q * 128 || row0 + r >= (int)rows) continue;
       float* hp = epi.h + (size_t)p * epi.H + row0 + r;
-      const float hn = *hp + y[i] * s_scale[p];
+      const float hn = (pre ? pre->h[k] : *hp) + y[i] * s_scale[p];
       *hp = hn;
       y[i] = hn;
     }
+    if (tid < 128) s_aux[tid] = pre ? pre->w : (row0 + tid < (int)rows ? epi.wnext[row0 + tid] : 0.0f);
     consumer_sync();
     const int nt_out = q <= 8 ? 1 : 2;
     for (int i = tid; i < 8 * 8 * nt_out; i += kG4Consumers) {
@@ -98,7 +143,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
 #pragma unroll
       for (int k = 0; k < 16; ++k) {
         const int r = 16 * gg + k;
-        vals[k] = p < q ? y[p * 128 + r] * epi.wnext[row0 + r] : 0.0f;
+        vals[k] = p < q ? y[p * 128 + r] * s_aux[r] : 0.0f;
       }
       prep16(vals, nullptr, p, q, (row0 + 16 * gg) / 16, nt_out, epi.hi_scale, epi.next.frag, epi.next.sum, nullptr,
              epi.H);
@@ -119,15 +164,23 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
     }
   } else if (EPI == EPI_ROPE_KV) {
     const int head = grp, hd = epi.hd;
-    const long long base = *epi.pos;
-    for (int i = tid; i < q * (hd / 2); i += kG4Consumers) {
+    const long long base = pre ? pre->base : *epi.pos;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + kG4Consumers * k;
+      if (i >= q * (hd / 2)) continue;
       const int p = i / (hd / 2), pr = i % (hd / 2);
       const float a = y[p * 128 + 2 * pr] * s_scale[p], b = y[p * 128 + 2 * pr + 1] * s_scale[p];
       const long long slot = base + p;
-      const long long rope_pos = epi.parent ? base + tree_depth4(epi.parent, p) : slot;
-      const int32_t page = epi.pages[slot / 64];
+      const int32_t page = pre ? pre->page[k] : epi.pages[slot / 64];
       if (head < epi.nh + epi.nkv) {
-        const float2 cs = epi.rope[(size_t)rope_pos * (hd / 2) + pr];
+        float2 cs;
+        if (pre) {
+          cs = pre->cs[k];
+        } else {
+          const long long rope_pos = epi.parent ? base + tree_depth4(epi.parent, p) : slot;
+          cs = epi.rope[(size_t)rope_pos * (hd / 2) + pr];
+        }
         const float c = cs.x, s = cs.y;
         const float ra = a * c - b * s, rb = a * s + b * c;
         __half* dst;
@@ -165,19 +218,18 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
              nullptr, epi.ffn);
     }
   }
-  (void)s_ss;
   consumer_sync();  // y is reused by the next group
 }
 
 
 // Epilogue kind chosen at run time (the megakernel's phases).
 __device__ __forceinline__ void g4_epilogue_rt(int kind, float* y, const float* s_scale, int grp, uint32_t rows,
-                                               int q, const Epi& epi) {
+                                               int q, const Epi& epi, float* s_aux, const EpiPre* pre) {
   switch (kind) {
-    case EPI_STORE: g4_epilogue<EPI_STORE>(y, s_scale, grp, rows, q, epi, nullptr); break;
-    case EPI_RESID_PREP: g4_epilogue<EPI_RESID_PREP>(y, s_scale, grp, rows, q, epi, nullptr); break;
-    case EPI_ROPE_KV: g4_epilogue<EPI_ROPE_KV>(y, s_scale, grp, rows, q, epi, nullptr); break;
-    default: g4_epilogue<EPI_SWIGLU_PREP>(y, s_scale, grp, rows, q, epi, nullptr); break;
+    case EPI_STORE: g4_epilogue<EPI_STORE>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    case EPI_RESID_PREP: g4_epilogue<EPI_RESID_PREP>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    case EPI_ROPE_KV: g4_epilogue<EPI_ROPE_KV>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    default: g4_epilogue<EPI_SWIGLU_PREP>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
   }
 }
 
@@ -344,7 +396,7 @@ template <int NT>
 __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
                          long long U, int G, long long u0, int ppr, int q, uint32_t rows, int epi_kind, const Epi& epi,
                          float* s_scale, int* s_last, const G4SsPre& ss_pre, const XBuf& in, bool& scale_ready,
-                         float* s_red) {
+                         float* s_red, const EpiPre* pre = nullptr) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
   if (!scale_ready) {
     g4_ss_finish(ss_pre, in, epi, q, s_red, s_scale);
@@ -395,7 +447,7 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     }
     consumer_sync();
   }
-  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi);
+  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);
 }
 
 // Geometry of a tiled matrix in the persistent GEMV for `nt` column tiles and units of `usb` superblocks.

@@ -79,16 +79,26 @@ __device__ __forceinline__ bool visible(long long pos, long long base, int i, co
   return false;
 }
 
-// Shared memory of one attention CTA: kAttnPages pages of K [64][HD] and V^T [HD][64] (fp16), staged by bulk copies.
+// Shared memory of one attention CTA: kAttnPages page buffers of K [64][HD] and V^T [HD][64] (fp16), staged by bulk
+// copies.
 constexpr size_t attn_page_bytes(int hd) { return (size_t)kPageTokens * hd * sizeof(__half); }
 constexpr size_t attn_smem_bytes(int hd) { return (size_t)kAttnPages * 2 * attn_page_bytes(hd); }
 
-// One CTA = kAttnPages consecutive pages of one kv head for one m-tile of 16 query rows; two warps per page, warp
-// w taking positions [32*(w%2), 32*(w%2)+32) of page w/2.  Each page (K and V^T, 2 x 16 KB) is fetched with two
-// cp.async.bulk copies into shared memory; pages that hold only committed positions (all < base) are requested
-// BEFORE griddepcontrol.wait, because the preceding QKV GEMV writes only positions >= base, so under
-// programmatic dependent launch the bulk of the KV stream overlaps the previous kernel.  The page holding the
-// window's own positions is requested after the wait.
+// Split-KV decode attention.  Grid (kv head, split, m-tile); the S = gridDim.y splits of a (kv head, m-tile) own
+// contiguous page ranges of the visible positions [0, pos + q).
+//
+//  * Page buffer b (of kAttnPages) serves the CTA's pages b, b + kAttnPages, ...; warps 2b and 2b+1 take
+//    positions [0, 32) and [32, 64) of each and keep a running (max, sum, O) per query row (online softmax), so a
+//    warp's state stays in registers however many pages the split holds.  Committed pages (every position
+//    < pos) are requested before griddepcontrol.wait: the preceding QKV GEMV writes only positions >= pos, so the
+//    bulk of the KV stream overlaps the previous kernel.  A buffer is refilled once both of its warps are done
+//    with it (named barrier of the pair).
+//  * The CTA folds its eight warps into one partial (per-row weights computed once), writes it, and publishes it
+//    with one release-add on the (m-tile, kv head) arrival counter.
+//  * Every split waits (bounded acquire spin) until all S partials are in, then combines a 1/S slice of the
+//    16 rows x HD/16 column groups over the S partials and writes W_o's input fragments for it.  All splits of
+//    the grid are resident together (at most one CTA per SM and the grid is no larger than the SM count), so
+//    the wait ends.  The last split to leave resets the counters for the next launch.
 //
 // Fragment mapping (mma m16n8k16, lane = 4g + t): in S = Q K^T, n-tile j column n is half-page position
 // p(j, n) = 8*(n/2) + 2j + n%2, so the C fragment of n-tile j holds positions 8t + 2j + {0, 1}; the P fragments
@@ -99,21 +109,23 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const __half* __restrict__ q16, const __half* __restrict__ kpool, const __half* __restrict__ vpool,
     const int32_t* __restrict__ pages, const long long* __restrict__ d_pos, const int32_t* __restrict__ parent, int q,
     int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
-    float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err) {
+    float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err,
+    const uint8_t* __restrict__ pf, unsigned long long pf_bytes) {
   static_assert(HD == 128, "head_dim 128 layout");
+  static_assert(kAttnWarps == 2 * kAttnPages, "two warps per page buffer");
   constexpr int RW = kAttnRowFloats;  // one partial row: O[HD], m, l, padding (16-byte aligned rows)
   constexpr uint32_t kPageBytes = (uint32_t)attn_page_bytes(HD);
+  constexpr int kItems = 16 * (HD / 16);  // (row, 16-column group) items of the final combine
   extern __shared__ __align__(128) uint8_t attn_smem[];
   __shared__ __align__(8) uint64_t bar[kAttnPages];
-  __shared__ int s_last;
-  const int kvh = blockIdx.x, mt = blockIdx.z;
+  __shared__ float s_wt[16][kAttnWarps];
+  __shared__ float s_ml[16][2];
+  __shared__ float s_out[kAttnWarps * 32 / 16][16];
+  const int kvh = blockIdx.x, split = blockIdx.y, S = gridDim.y, mt = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, g = lane / 4, t = lane % 4;
-  const int wp = warp / 2, half = warp % 2;  // page within the CTA, half of that page
-  const int pg = blockIdx.y * kAttnPages + wp;
+  const int wp = warp / 2, half = warp % 2;  // page buffer of this warp, half of each page
   __half* ks = reinterpret_cast<__half*>(attn_smem + (size_t)wp * 2 * kPageBytes);
   __half* vs = ks + kPageTokens * HD;
-  // this warp's partial [16][RW], written over its page once both warps of the page are done with it
-  float* sp = reinterpret_cast<float*>(attn_smem + (size_t)wp * 2 * kPageBytes) + half * 16 * RW;
 
   if (threadIdx.x == 0) {
     for (int w = 0; w < kAttnPages; ++w) mbar_init(&bar[w], 1);
@@ -123,49 +135,56 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
   // committed position and page table do not depend on the preceding kernel
   const long long base = *d_pos;
   const long long nvis = base + q;
-  const int npages = (int)((nvis + kPageTokens - 1) / kPageTokens);
-  const int ngroups = (npages + kAttnPages - 1) / kAttnPages;
-  const bool active = pg < npages && pg < max_pages;
-  const bool committed_page = (long long)(pg + 1) * kPageTokens <= base;
-  auto request = [&]() {
-    const int32_t page = pages[pg];
-    const size_t off = ((size_t)page * nkv + kvh) * kPageTokens * HD;
+  const long long np_l = (nvis + kPageTokens - 1) / kPageTokens;
+  const int npages = (int)(np_l < max_pages ? np_l : max_pages);
+  const int p_begin = (int)((long long)split * npages / S), p_end = (int)((long long)(split + 1) * npages / S);
+  const bool owner = half == 0 && lane == 0;  // requests the pages of buffer wp
+  auto request = [&](int pg) {
+    const size_t off = ((size_t)pages[pg] * nkv + kvh) * kPageTokens * HD;
     mbar_expect_tx(&bar[wp], 2 * kPageBytes);
     bulk_g2s(ks, kpool + off, kPageBytes, &bar[wp]);
     bulk_g2s(vs, vpool + off, kPageBytes, &bar[wp]);
   };
-  const bool requester = active && half == 0 && lane == 0;
-  if (requester && committed_page) request();
+  const int first = p_begin + wp;
+  const bool first_committed = (long long)(first + 1) * kPageTokens <= base;
+  if (owner && first < p_end && first_committed) request(first);
+  // L2 lookahead: this CTA's share of the next kernel's weights (W_o), read while the attention runs
+  if (threadIdx.x == 32 * (kAttnWarps - 1))
+    l2_prefetch_share(pf, pf_bytes, (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
+                      (int)(gridDim.x * gridDim.y * gridDim.z), ~0ull);
   griddep_wait();
   griddep_launch();
-  if (requester && !committed_page) request();
+  if (owner && first < p_end && !first_committed) request(first);
 
   const int group = nh / nkv;
   const int r0 = mt * 16 + g, r1 = r0 + 8;
   const int i0 = r0 / group, i1 = r1 / group;
   const bool v0 = i0 < q, v1 = i1 < q;
-  bool ok = active;
-  float O[HD / 8][4];
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-  if (active) {
-    // Q fragments: thread t holds head dims [32t, 32t+32) of rows r0 and r1 (the same k permutation as K below).
-    uint4 qw0[4], qw1[4];
-    {
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      const uint4* a = reinterpret_cast<const uint4*>(q16 + ((size_t)i0 * nh + kvh * group + r0 % group) * HD + 32 * t);
-      const uint4* b = reinterpret_cast<const uint4*>(q16 + ((size_t)i1 * nh + kvh * group + r1 % group) * HD + 32 * t);
+  // Q fragments: thread t holds head dims [32t, 32t+32) of rows r0 and r1 (the same k permutation as K below).
+  uint4 qw0[4], qw1[4];
+  {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    const uint4* a = reinterpret_cast<const uint4*>(q16 + ((size_t)i0 * nh + kvh * group + r0 % group) * HD + 32 * t);
+    const uint4* b = reinterpret_cast<const uint4*>(q16 + ((size_t)i1 * nh + kvh * group + r1 % group) * HD + 32 * t);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qw0[j] = v0 ? a[j] : z;
-        qw1[j] = v1 ? b[j] : z;
-      }
+    for (int j = 0; j < 4; ++j) {
+      qw0[j] = v0 ? a[j] : z;
+      qw1[j] = v1 ? b[j] : z;
     }
-    ok = mbar_wait(&bar[wp], 0, err);
+  }
+  float O[HD / 8][4];
+#pragma unroll
+  for (int jn = 0; jn < HD / 8; ++jn) O[jn][0] = O[jn][1] = O[jn][2] = O[jn][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  uint32_t phase = 0;
+  for (int pg = first; pg < p_end; pg += kAttnPages, phase ^= 1u) {
+    // every issued copy is waited for (bounded), so no copy is in flight when the CTA leaves
+    const bool ok = mbar_wait(&bar[wp], phase, err);
     if (ok) {
-      float S[4][4];
+      float Sx[4][4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.0f;
+        Sx[j][0] = Sx[j][1] = Sx[j][2] = Sx[j][3] = 0.0f;
         const int pos = 32 * half + 8 * (g / 2) + 2 * j + (g % 2);
         const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)pos * HD);
         uint4 kw[4];
@@ -173,18 +192,19 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
         for (int u = 0; u < 4; ++u) kw[u] = kr[kv_k_chunk(4 * t + u, pos)];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16(S[j], word_of(qw0, 2 * kk), word_of(qw1, 2 * kk), word_of(qw0, 2 * kk + 1), word_of(qw1, 2 * kk + 1),
+          mma_f16(Sx[j], word_of(qw0, 2 * kk), word_of(qw1, 2 * kk), word_of(qw0, 2 * kk + 1), word_of(qw1, 2 * kk + 1),
                   word_of(kw, 2 * kk), word_of(kw, 2 * kk + 1));
       }
-      if (committed_page) {  // every position is visible to every window row
+      float mx0 = m0, mx1 = m1;
+      if ((long long)(pg + 1) * kPageTokens <= base) {  // every position is visible to every window row
 #pragma unroll
         for (int j = 0; j < 4; ++j)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            S[j][e] = v0 ? S[j][e] * scale_log2 : -INFINITY;
-            S[j][2 + e] = v1 ? S[j][2 + e] * scale_log2 : -INFINITY;
-            m0 = fmaxf(m0, S[j][e]);
-            m1 = fmaxf(m1, S[j][2 + e]);
+            Sx[j][e] = v0 ? Sx[j][e] * scale_log2 : -INFINITY;
+            Sx[j][2 + e] = v1 ? Sx[j][2 + e] * scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, Sx[j][e]);
+            mx1 = fmaxf(mx1, Sx[j][2 + e]);
           }
       } else {
 #pragma unroll
@@ -192,197 +212,201 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const long long pos = (long long)pg * kPageTokens + 32 * half + 8 * t + 2 * j + e;
-            S[j][e] = (v0 && visible(pos, base, i0, parent)) ? S[j][e] * scale_log2 : -INFINITY;
-            S[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? S[j][2 + e] * scale_log2 : -INFINITY;
-            m0 = fmaxf(m0, S[j][e]);
-            m1 = fmaxf(m1, S[j][2 + e]);
+            Sx[j][e] = (v0 && visible(pos, base, i0, parent)) ? Sx[j][e] * scale_log2 : -INFINITY;
+            Sx[j][2 + e] = (v1 && visible(pos, base, i1, parent)) ? Sx[j][2 + e] * scale_log2 : -INFINITY;
+            mx0 = fmaxf(mx0, Sx[j][e]);
+            mx1 = fmaxf(mx1, Sx[j][2 + e]);
           }
       }
 #pragma unroll
       for (int o = 1; o <= 2; o <<= 1) {
-        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      // rescale the running state to the new maxima
+      const float c0 = mx0 == -INFINITY ? 1.0f : exp2f(m0 - mx0), c1 = mx1 == -INFINITY ? 1.0f : exp2f(m1 - mx1);
+      m0 = mx0;
+      m1 = mx1;
+      l0 *= c0;
+      l1 *= c1;
+#pragma unroll
+      for (int jn = 0; jn < HD / 8; ++jn) {
+        O[jn][0] *= c0;
+        O[jn][1] *= c0;
+        O[jn][2] *= c1;
+        O[jn][3] *= c1;
       }
       uint32_t pa[4][2];
+      float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float p00 = m0 == -INFINITY ? 0.0f : exp2f(S[j][0] - m0);
-        const float p01 = m0 == -INFINITY ? 0.0f : exp2f(S[j][1] - m0);
-        const float p10 = m1 == -INFINITY ? 0.0f : exp2f(S[j][2] - m1);
-        const float p11 = m1 == -INFINITY ? 0.0f : exp2f(S[j][3] - m1);
-        l0 += p00 + p01;
-        l1 += p10 + p11;
+        const float p00 = m0 == -INFINITY ? 0.0f : exp2f(Sx[j][0] - m0);
+        const float p01 = m0 == -INFINITY ? 0.0f : exp2f(Sx[j][1] - m0);
+        const float p10 = m1 == -INFINITY ? 0.0f : exp2f(Sx[j][2] - m1);
+        const float p11 = m1 == -INFINITY ? 0.0f : exp2f(Sx[j][3] - m1);
+        ps0 += p00 + p01;
+        ps1 += p10 + p11;
         pa[j][0] = pack_half2(p00, p01);
         pa[j][1] = pack_half2(p10, p11);
       }
 #pragma unroll
       for (int o = 1; o <= 2; o <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+        ps0 += __shfl_xor_sync(0xffffffffu, ps0, o);
+        ps1 += __shfl_xor_sync(0xffffffffu, ps1, o);
       }
+      l0 += ps0;
+      l1 += ps1;
 #pragma unroll
       for (int jn = 0; jn < HD / 8; ++jn) {
-        O[jn][0] = O[jn][1] = O[jn][2] = O[jn][3] = 0.0f;
         const int vrow = 8 * jn + g;
         const uint4 va = reinterpret_cast<const uint4*>(vs + (size_t)vrow * kPageTokens)[kv_v_chunk(4 * half + t, vrow)];
         mma_f16(O[jn], pa[0][0], pa[0][1], pa[1][0], pa[1][1], va.x, va.y);
         mma_f16(O[jn], pa[2][0], pa[2][1], pa[3][0], pa[3][1], va.z, va.w);
       }
-    } else {
-      // the copy never completed (error flag raised): give it one more bounded wait before the CTA can exit
-      mbar_wait(&bar[wp], 0, err);
     }
+    // both warps of the buffer are done with this page: refill it with the buffer's next page
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + wp) : "memory");
+    if (owner && pg + kAttnPages < p_end) request(pg + kAttnPages);
   }
-  // both warps of the page are done reading it: its space takes their partials
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + wp) : "memory");
-  if (active && ok) {
+
+  // this warp's partial [16][RW] over the first half of its buffer's space (its pages are all consumed)
+  float* sp = reinterpret_cast<float*>(attn_smem + (size_t)wp * 2 * kPageBytes) + half * 16 * RW;
 #pragma unroll
-    for (int jn = 0; jn < HD / 8; ++jn) {
-      *reinterpret_cast<float2*>(sp + g * RW + 8 * jn + 2 * t) = make_float2(O[jn][0], O[jn][1]);
-      *reinterpret_cast<float2*>(sp + (g + 8) * RW + 8 * jn + 2 * t) = make_float2(O[jn][2], O[jn][3]);
-    }
-    if (t == 0) {
-      sp[g * RW + HD] = m0;
-      sp[g * RW + HD + 1] = l0;
-      sp[(g + 8) * RW + HD] = m1;
-      sp[(g + 8) * RW + HD + 1] = l1;
-    }
-  } else if (lane < 16) {
-    sp[lane * RW + HD] = -INFINITY;
-    sp[lane * RW + HD + 1] = 0.0f;
+  for (int jn = 0; jn < HD / 8; ++jn) {
+    *reinterpret_cast<float2*>(sp + g * RW + 8 * jn + 2 * t) = make_float2(O[jn][0], O[jn][1]);
+    *reinterpret_cast<float2*>(sp + (g + 8) * RW + 8 * jn + 2 * t) = make_float2(O[jn][2], O[jn][3]);
+  }
+  if (t == 0) {
+    sp[g * RW + HD] = m0;
+    sp[g * RW + HD + 1] = l0;
+    sp[(g + 8) * RW + HD] = m1;
+    sp[(g + 8) * RW + HD + 1] = l1;
   }
   __syncthreads();
   auto spw = [&](int w) {
     return reinterpret_cast<const float*>(attn_smem + (size_t)(w / 2) * 2 * kPageBytes) + (w % 2) * 16 * RW;
   };
-  // combine the CTA's warps into one partial per (m-tile, kv head, page group)
-  float* mine = part + (((size_t)mt * nkv + kvh) * max_pages + blockIdx.y) * 16 * RW;
-  if ((int)blockIdx.y < ngroups) {
-    for (int i = threadIdx.x; i < 16 * (HD + 2); i += blockDim.x) {
-      const int r = i / (HD + 2), c = i % (HD + 2);
-      float M = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, spw(w)[r * RW + HD]);
-      float a = 0.0f;
-      if (c == HD) {
-        a = M;
-      } else {
-#pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) {
-          const float m = spw(w)[r * RW + HD];
-          if (m == -INFINITY) continue;
-          a += spw(w)[r * RW + c] * exp2f(m - M);
-        }
-      }
-      mine[r * RW + c] = a;
-    }
-  }
-  // the last CTA of this (m-tile, kv head) combines the page groups and writes W_o's input fragments
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&counters[mt * nkv + kvh], 1) == (int)gridDim.y - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const float* allp = part + ((size_t)mt * nkv + kvh) * max_pages * 16 * RW;
-  // combine weights w[gi][r] = exp2(m_gi - M) / L, staged in shared memory (after o_s)
-  float* o_s = reinterpret_cast<float*>(attn_smem);  // [16][HD], reusing the page buffers
-  float* wgt = o_s + 16 * HD;                         // [ngroups][16]
-  float* lsum = wgt + ngroups * 16;                    // [ngroups][16]
-  for (int i = threadIdx.x; i < ngroups * 16; i += blockDim.x) {
-    wgt[i] = __ldcg(allp + (size_t)i * RW + HD);
-    lsum[i] = __ldcg(allp + (size_t)i * RW + HD + 1);
-  }
-  __syncthreads();
+  // per-row weights of the eight warps, once
   if (threadIdx.x < 16) {
     const int r = threadIdx.x;
     float M = -INFINITY;
-    for (int gi = 0; gi < ngroups; ++gi) M = fmaxf(M, wgt[gi * 16 + r]);
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, spw(w)[r * RW + HD]);
     float L = 0.0f;
-    for (int gi = 0; gi < ngroups; ++gi) {
-      const float m = wgt[gi * 16 + r];
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float m = spw(w)[r * RW + HD];
       const float e = m == -INFINITY ? 0.0f : exp2f(m - M);
-      L += lsum[gi * 16 + r] * e;
-      wgt[gi * 16 + r] = e;
+      s_wt[r][w] = e;
+      L += spw(w)[r * RW + HD + 1] * e;
     }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    for (int gi = 0; gi < ngroups; ++gi) wgt[gi * 16 + r] *= inv;
+    s_ml[r][0] = M;
+    s_ml[r][1] = L;
   }
   __syncthreads();
-  {
-    // thread (row r, 8 columns c8): 16-byte loads, four page groups in flight
-    const int r = threadIdx.x / (HD / 8), c8 = threadIdx.x % (HD / 8);
-    float a[8];
+  // this split's partial, in global memory
+  const size_t head_slot = (size_t)mt * nkv + kvh;
+  float* allp = part + head_slot * S * 16 * RW;
+  float* mine = allp + (size_t)split * 16 * RW;
+  for (int i = threadIdx.x; i < 16 * (HD / 4); i += blockDim.x) {
+    const int r = i / (HD / 4), c4 = i % (HD / 4);
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) a[k] = 0.0f;
-    const float* col = allp + (size_t)r * RW + 8 * c8;
-    int gi = 0;
-    for (; gi + 4 <= ngroups; gi += 4) {
-      float4 v[4][2];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float4* p4 = reinterpret_cast<const float4*>(col + (size_t)(gi + u) * 16 * RW);
-        v[u][0] = __ldcg(p4);
-        v[u][1] = __ldcg(p4 + 1);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = wgt[(gi + u) * 16 + r];
-        a[0] += v[u][0].x * w;
-        a[1] += v[u][0].y * w;
-        a[2] += v[u][0].z * w;
-        a[3] += v[u][0].w * w;
-        a[4] += v[u][1].x * w;
-        a[5] += v[u][1].y * w;
-        a[6] += v[u][1].z * w;
-        a[7] += v[u][1].w * w;
-      }
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float e = s_wt[r][w];
+      const float4 v = *reinterpret_cast<const float4*>(spw(w) + r * RW + 4 * c4);
+      a.x += v.x * e;
+      a.y += v.y * e;
+      a.z += v.z * e;
+      a.w += v.w * e;
     }
-    for (; gi < ngroups; ++gi) {
-      const float4* p4 = reinterpret_cast<const float4*>(col + (size_t)gi * 16 * RW);
-      const float4 x0 = __ldcg(p4), x1 = __ldcg(p4 + 1);
-      const float w = wgt[gi * 16 + r];
-      a[0] += x0.x * w;
-      a[1] += x0.y * w;
-      a[2] += x0.z * w;
-      a[3] += x0.w * w;
-      a[4] += x1.x * w;
-      a[5] += x1.y * w;
-      a[6] += x1.z * w;
-      a[7] += x1.w * w;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) o_s[r * HD + 8 * c8 + k] = a[k];
+    *reinterpret_cast<float4*>(mine + r * RW + 4 * c4) = a;
+  }
+  if (threadIdx.x < 16) {
+    mine[threadIdx.x * RW + HD] = s_ml[threadIdx.x][0];
+    mine[threadIdx.x * RW + HD + 1] = s_ml[threadIdx.x][1];
   }
   __syncthreads();
-  if (threadIdx.x == 0) counters[mt * nkv + kvh] = 0;
-  // fragments: query vector r = window row i, head kvh*group + r%group; 8 column groups of 16 per head
+  int* arrive = counters + head_slot;
+  int* depart = counters + (size_t)gridDim.z * nkv + head_slot;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    red_release_add(arrive, 1);
+    s_ok = wait_count(arrive, S, err);
+    // every split has passed the wait once all have departed: the last one resets both counters
+    if (atomicAdd(depart, 1) == S - 1) {
+      *arrive = 0;
+      *depart = 0;
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;
+
+  // final combine of this split's slice of the (row, column group) items over the S partials
+  const int it_begin = split * kItems / S, it_end = (split + 1) * kItems / S;
+  const int lanes = blockDim.x / 16;  // items in flight per pass
   const int qd = nh * HD;
-  for (int it = threadIdx.x; it < 16 * (HD / 16); it += blockDim.x) {
-    const int r = it / (HD / 16), gg = it % (HD / 16);
-    const int i = (mt * 16 + r) / group, head = kvh * group + (mt * 16 + r) % group;
-    if (i >= q) continue;
-    prep16(&o_s[r * HD + 16 * gg], nullptr, i, q, (head * HD + 16 * gg) / 16, nt_out, hi_scale, out_frag, out_sum,
-           nullptr, qd);
+  for (int it0 = it_begin; it0 < it_end; it0 += lanes) {
+    const int li = threadIdx.x / 16, c = threadIdx.x % 16, it = it0 + li;
+    const bool live = it < it_end;
+    const int r = live ? it / (HD / 16) : 0, cg = live ? it % (HD / 16) : 0;
+    // all of a thread's loads are issued before any is used (kAttnMaxSplits at a time)
+    float M = -INFINITY, L = 0.0f, a = 0.0f;
+    for (int k0 = 0; k0 < S; k0 += kAttnMaxSplits) {
+      float mk[kAttnMaxSplits], lk[kAttnMaxSplits], vk[kAttnMaxSplits];
+#pragma unroll
+      for (int k = 0; k < kAttnMaxSplits; ++k) {
+        const float* row = allp + ((size_t)(k0 + k) * 16 + r) * RW;
+        const bool in = k0 + k < S;
+        mk[k] = in ? __ldcg(row + HD) : -INFINITY;
+        lk[k] = in ? __ldcg(row + HD + 1) : 0.0f;
+        vk[k] = in ? __ldcg(row + 16 * cg + c) : 0.0f;
+      }
+      float Mn = M;
+#pragma unroll
+      for (int k = 0; k < kAttnMaxSplits; ++k) Mn = fmaxf(Mn, mk[k]);
+      const float cr = Mn == -INFINITY ? 1.0f : exp2f(M - Mn);  // rescale what earlier batches summed
+      L *= cr;
+      a *= cr;
+      M = Mn;
+#pragma unroll
+      for (int k = 0; k < kAttnMaxSplits; ++k) {
+        const float e = mk[k] == -INFINITY ? 0.0f : exp2f(mk[k] - M);
+        L += lk[k] * e;
+        a += vk[k] * e;
+      }
+    }
+    s_out[li][c] = L > 0.0f ? a / L : 0.0f;
+    __syncthreads();
+    if (live && c == 0) {
+      // query vector r = window row i, head kvh*group + r%group; 16 columns 16cg.. of that head
+      const int i = (mt * 16 + r) / group, head = kvh * group + (mt * 16 + r) % group;
+      if (i < q)
+        prep16(s_out[li], nullptr, i, q, (head * HD + 16 * cg) / 16, nt_out, hi_scale, out_frag, out_sum, nullptr, qd);
+    }
+    __syncthreads();
   }
 }
 
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum, int* d_err,
-                     cudaStream_t st) {
+                     const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count, cudaStream_t st) {
   CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
   const int group = d.nh / d.nkv;
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
   const size_t smem = attn_smem_bytes(128);
-  CLM_CHECK((size_t)16 * 128 * 4 + (size_t)((max_pages + kAttnPages - 1) / kAttnPages) * 32 * 4 <= smem,
-            CLM_RESOURCE_EXHAUSTED, "attention: max_context too large for the page-group combine");
+  // splits per (kv head, m-tile): enough for the pages, no more CTAs than SMs (the splits wait for each other)
+  const int heads = d.nkv * mtiles;
+  CLM_CHECK(heads <= sm_count, CLM_RESOURCE_EXHAUSTED, "attention: more (kv head, m-tile) pairs than SMs");
+  int splits = (max_pages + kAttnPages - 1) / kAttnPages;
+  if (splits > sm_count / heads) splits = sm_count / heads;
+  if (splits < 1) splits = 1;
   CLM_TRY(ensure_smem(attention_kernel<128>, smem));
-  return launch_pdl(attention_kernel<128>, dim3(d.nkv, (max_pages + kAttnPages - 1) / kAttnPages, mtiles),
-                    dim3(32 * kAttnWarps), smem, st, d_q, d_k, d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv,
-                    scale_log2, max_pages, d_part, d_counters, nt_out, hi_scale, static_cast<uint2*>(d_frag), d_sum,
-                    d_err);
+  return launch_pdl(attention_kernel<128>, dim3(d.nkv, splits, mtiles), dim3(32 * kAttnWarps), smem, st, d_q, d_k,
+                    d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2, max_pages, d_part, d_counters, nt_out,
+                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes);
 }
 
 // ---------------------------------------------------------------------------------------------------

@@ -8,8 +8,9 @@
 namespace clm {
 
 constexpr int kPageTokens = 64;  // KV page: 64 positions of one KV head
-constexpr int kAttnPages = 4;    // pages per attention CTA
-constexpr int kAttnWarps = 8;    // warps per attention CTA (two per page, half a page each)
+constexpr int kAttnPages = 4;    // page buffers per attention CTA
+constexpr int kAttnWarps = 8;    // warps per attention CTA (two per page buffer, half a page each)
+constexpr int kAttnMaxSplits = 24;  // partials a thread of the final attention combine loads at once
 constexpr int kAttnRowFloats = 132;  // one partial row: O[128], m, l, 2 floats of padding (16-byte aligned rows)
 
 struct LlamaDims {
@@ -32,15 +33,18 @@ __host__ __device__ __forceinline__ int kv_v_chunk(int c, int d) { return c ^ (d
 inline size_t attn_partial_floats(int hd) { return (size_t)16 * (hd + 4); }
 
 int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int q, int H, float* d_h, cudaStream_t st);
-// Paged split-KV attention for q window rows: pages staged in shared memory by bulk copies (committed pages
-// before griddepcontrol.wait), CTAs combine their 4 pages (8 warps), and the last CTA of each (m-tile, kv head) combines
-// all page groups and writes W_o's input fragments (out_frag / out_sum, qd columns).
-// d_part holds mtiles*nkv*max_pages*attn_partial_floats(hd) floats; d_counters mtiles*nkv zeroed ints; a bounded wait that
-// gives up stores kErrWaitTimeout in *d_err.
+// Paged split-KV attention for q window rows: per (kv head, m-tile of 16 query rows) S splits own contiguous page
+// ranges (pages staged in shared memory by bulk copies, committed pages before griddepcontrol.wait, online softmax
+// per warp), write one partial each, and every split then combines a slice of the outputs over all partials and
+// writes W_o's input fragments (out_frag / out_sum, qd columns).  S is chosen so that the grid fits the SM count.
+// d_part holds mtiles*nkv*max_pages*attn_partial_floats(hd) floats; d_counters 2*mtiles*nkv zeroed ints (left zero);
+// a bounded wait that gives up stores kErrWaitTimeout in *d_err.  [d_prefetch, d_prefetch + prefetch_bytes) (the next
+// kernel's weights, or null) is prefetched into L2, split over the CTAs.
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
-                     int* d_err, cudaStream_t st);
+                     int* d_err, const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count,
+                     cudaStream_t st);
 // Copies h[p][0:H] of rows into the boundary records out[p] = {S = h, P = 0, g = 1} (hc = 1).
 int launch_pack_boundary(const float* d_h, const float* d_part, int nsplit, int q, int H, float* d_out,
                          cudaStream_t st);
