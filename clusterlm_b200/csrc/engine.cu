@@ -317,11 +317,11 @@ struct LlamaEngine : clm_b200_engine {
   }
 
   // L2 lookahead of the next GEMV of the chain: each CTA prefetches the first bytes of the matching CTA range of
-  // `next` (up to its ring's worth) once its own copies are issued
+  // `next` (its first units) once its own copies are issued
   static void lookahead(Epi& e, const Gemv& next) {
     e.pf = static_cast<const uint8_t*>(next.m->data);
     e.pf_bytes = next.m->shape.bytes();
-    e.pf_cap = 256 * 1024;
+    e.pf_cap = 64 * 1024;
   }
 
   // ---- the layer range over q rows; h holds the stage input and xa its first norm's preparation
