@@ -3,8 +3,11 @@
 // y[p][row] = W[row] . x[p] for q <= 16 window rows, W in GGUF Q4_K / Q8_0 repacked into the group-major tile
 // layout of gemv.cuh.
 //
-//  * Activations come from the producer kernel as fp16 fragments xfrag[sb][nt][16 s][32 lanes] (uint2) and f32
-//    sub-block sums xsum[2 halves][sb*8 + j][16 p] (the Q4_K min / Q8_0 bias term), written by prep16 below.
+//  * Activations come from the producer kernel as fp16 fragments xfrag[sb][nt][16 s][32 lanes] (uint2) and the
+//    sums of every 16-column half of every 32-column sub-block, split into fp16 hi + lo and stored directly as the
+//    B fragments of the Q4_K min / Q8_0 bias mma: xsum[sb][n-tile (2)][32 lanes] of four words {hi half 0,
+//    hi half 1, lo half 0, lo half 1}, each word the pair (sub-block 2t, 2t+1) of lane (g, t) = window row g of
+//    the n-tile.  Both written by prep16 below.
 //  * Optional row scale 1/sqrt(mean(h^2) + eps) from sum-of-squares partials: rmsnorm(h) * w is folded as
 //    (W . (h * w)) / denom, so no separate normalisation kernel runs between layers.
 //  * Epilogues: store; residual add + next-norm preparation; RoPE + paged KV append; SwiGLU + down preparation.
@@ -19,7 +22,7 @@ enum { EPI_STORE = 0, EPI_RESID_PREP = 1, EPI_ROPE_KV = 2, EPI_SWIGLU_PREP = 3 }
 // Activation hand-off between a producer and a consuming GEMV.
 struct XBuf {
   uint2* frag = nullptr;   // [SB][nt][16 s][32 lanes]
-  float* sum = nullptr;    // [2][SB*8][16 p]
+  float* sum = nullptr;    // [SB][2 n-tiles][32 lanes][4 words] min / bias mma B fragments (1 KB per superblock)
   float* ss = nullptr;     // [nss][16 p] sum-of-squares partials, one per 128 columns (row scale), or null
   int nss = 0;
 };
@@ -71,7 +74,7 @@ int launch_prep_rows(const float* d_x, long long ld, int q, int cols, const floa
                      const XBuf& out, bool with_ss, cudaStream_t st);
 // Bytes of the fragment / sum buffers for `cols` columns.
 inline size_t xfrag_bytes(int cols, int nt) { return (size_t)(cols / 256) * nt * 32 * 16 * sizeof(uint2); }
-inline size_t xsum_bytes(int cols) { return (size_t)2 * (cols / 32) * 16 * sizeof(float); }
+inline size_t xsum_bytes(int cols) { return (size_t)(cols / 256) * 1024; }
 
 // Device helper shared by producers: writes the fragments / half sums of one 16-column group [16c, 16c+16)
 // of activation row p from `vals` (16 floats, already multiplied by the next norm's weight if any) and, when
@@ -96,8 +99,16 @@ __device__ __forceinline__ void prep16(const float* vals, const float* raw, int 
         (uint32_t)__half_as_ushort(__float2half_rn(sa)) | ((uint32_t)__half_as_ushort(__float2half_rn(sbv)) << 16);
   }
   const int j = o / 32, half = (o % 32) / 16;
-  if (p < 16) xsum[((size_t)half * (total_cols / 32) + sb * 8 + j) * 16 + p] = sum;
+  if (p < 16) {
+    // B fragment words of the min / bias mma (k = half * 8 + sub-block): lane (p % 8, j / 2), element j % 2
+    const __half hi = __float2half_rn(sum);
+    const __half lo = __float2half_rn(sum - __half2float(hi));
+    __half* wq = reinterpret_cast<__half*>(xsum) + ((((size_t)sb * 2 + ntile) * 32 + g * 4 + (j >> 1)) * 4) * 2;
+    wq[half * 2 + (j & 1)] = hi;
+    wq[(2 + half) * 2 + (j & 1)] = lo;
+  }
   if (ss_out && p < 16) ss_out[(size_t)c * 16 + p] = ss;
+  (void)total_cols;
 }
 
 }  // namespace clm

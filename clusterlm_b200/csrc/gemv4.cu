@@ -62,7 +62,6 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t policy = evict_first_policy();
-      const int nsub = geo.sb * 8;
       auto issue_weights = [&](const UnitCursor& c) {
         const int nsb = min(2, geo.sb - 2 * c.pr);
         uint8_t* st = smem + (size_t)c.slot * geo.stage_bytes;
@@ -76,9 +75,8 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         uint8_t* st = smem + (size_t)c.slot * geo.stage_bytes;
         bulk_g2s(st + geo.frag_off, in.frag + (size_t)2 * c.pr * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
                  &full[c.slot]);
-        for (int h = 0; h < 2; ++h)
-          bulk_g2s(st + geo.sum_off + h * geo.sum_half, in.sum + ((size_t)h * nsub + 16 * c.pr) * 16,
-                   (uint32_t)(nsb * kG4SbSumBytes), &full[c.slot]);
+        bulk_g2s(st + geo.sum_off, reinterpret_cast<const uint8_t*>(in.sum) + (size_t)2 * c.pr * 1024,
+                 (uint32_t)(nsb * 1024), &full[c.slot]);
       };
       const int pre = min(n, stages);
       UnitCursor w = start, a = start;

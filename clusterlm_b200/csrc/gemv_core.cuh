@@ -305,47 +305,31 @@ struct G4Acc {
 template <typename Raw, int NT>
 __device__ __forceinline__ void g4_consume_tile(const uint8_t* st, const G4Geom& geo, int hh, int nsb, int rt,
                                                 int lane, G4Acc<NT>& acc) {
-  const int t = lane % 4, g = lane / 4;
+  const int t = lane % 4;
   const uint2* xf = reinterpret_cast<const uint2*>(st + geo.frag_off) + hh * NT * 512;
-  const float* s0 = reinterpret_cast<const float*>(st + geo.sum_off);
-  const float* s1 = s0 + geo.sum_half / 4;
   uint32_t mg, mg8;
   Raw r;
   load_raw_s(r, st + (size_t)hh * geo.sb_bytes + (size_t)rt * geo.tile_bytes, lane);
   tile_mmas<NT>(r, t, xf, lane, acc.v, mg, mg8);
-  // min / bias term of this superblock: A = -m per (row, sub-block) in this warp's k-half of the pair,
-  // B = fp16 hi + lo of the pair's sub-block sums
-  const uint32_t a0 = hh == 0 ? mg : 0u, a1 = hh == 0 ? mg8 : 0u, a2 = hh == 1 ? mg : 0u, a3 = hh == 1 ? mg8 : 0u;
+  // min / bias term of this superblock: A = -m per (row, sub-block) for both 16-column halves, B = the staged
+  // fp16 hi / lo half sums (prep16's fragment layout)
+  const uint4* sf = reinterpret_cast<const uint4*>(st + geo.sum_off) + hh * 64;
+  (void)nsb;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int p = nt * 8 + g;
-    float v[4];
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int sub = h2 * 8 + 2 * t + e;
-        v[2 * h2 + e] = h2 < nsb ? s0[sub * 16 + p] + s1[sub * 16 + p] : 0.0f;
-      }
-    // fp16 hi + lo split of each sum (paired conversions)
-    const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-    const __half2 l01 = __floats2half2_rn(v[0] - f01.x, v[1] - f01.y);
-    const __half2 l23 = __floats2half2_rn(v[2] - f23.x, v[3] - f23.y);
-    mma16816(acc.v[0][nt], a0, a1, a2, a3, h2u(h01), h2u(h23));
-    mma16816(acc.v[1][nt], a0, a1, a2, a3, h2u(l01), h2u(l23));
+    const uint4 b = sf[nt * 32 + lane];
+    mma16816(acc.v[0][nt], mg, mg8, mg, mg8, b.x, b.y);
+    mma16816(acc.v[1][nt], mg, mg8, mg, mg8, b.z, b.w);
   }
 }
 
-// Both superblocks of the unit staged at `st` (nsb of them) for row tile rt: one warp's whole share of the unit,
-// with one min / bias mma pair for the two superblocks together.
+// Both superblocks of the unit staged at `st` (nsb of them) for row tile rt: one warp's whole share of the unit.
 template <typename Raw, int NT>
 __device__ __forceinline__ void g4_consume_pair(const uint8_t* st, const G4Geom& geo, int nsb, int rt, int lane,
                                                 G4Acc<NT>& acc) {
-  const int t = lane % 4, g = lane / 4;
+  const int t = lane % 4;
   const uint2* xf = reinterpret_cast<const uint2*>(st + geo.frag_off);
-  const float* s0 = reinterpret_cast<const float*>(st + geo.sum_off);
-  const float* s1 = s0 + geo.sum_half / 4;
+  const uint4* sf = reinterpret_cast<const uint4*>(st + geo.sum_off);
   uint32_t m0 = 0u, m08 = 0u, m1 = 0u, m18 = 0u;
   {
     Raw r;
@@ -357,23 +341,17 @@ __device__ __forceinline__ void g4_consume_pair(const uint8_t* st, const G4Geom&
     load_raw_s(r, st + (size_t)geo.sb_bytes + (size_t)rt * geo.tile_bytes, lane);
     tile_mmas<NT>(r, t, xf + NT * 512, lane, acc.v, m1, m18);
   }
+  // min / bias terms: A = -m per (row, sub-block) for both 16-column halves, B = the staged hi / lo half sums
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int p = nt * 8 + g;
-    float v[4];
+  for (int hh = 0; hh < 2; ++hh) {
+    if (hh >= nsb) break;
+    const uint32_t a = hh ? m1 : m0, a8 = hh ? m18 : m08;
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int sub = h2 * 8 + 2 * t + e;
-        v[2 * h2 + e] = h2 < nsb ? s0[sub * 16 + p] + s1[sub * 16 + p] : 0.0f;
-      }
-    const __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-    const __half2 l01 = __floats2half2_rn(v[0] - f01.x, v[1] - f01.y);
-    const __half2 l23 = __floats2half2_rn(v[2] - f23.x, v[3] - f23.y);
-    mma16816(acc.v[0][nt], m0, m08, m1, m18, h2u(h01), h2u(h23));
-    mma16816(acc.v[1][nt], m0, m08, m1, m18, h2u(l01), h2u(l23));
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint4 b = sf[hh * 64 + nt * 32 + lane];
+      mma16816(acc.v[0][nt], a, a8, a, a8, b.x, b.y);
+      mma16816(acc.v[1][nt], a, a8, a, a8, b.z, b.w);
+    }
   }
 }
 
@@ -458,7 +436,7 @@ inline G4Geom g4_geom(const GemvShape& s, int nt, int usb = 2) {
   geo.ppr = (int)(s.sb + usb - 1) / usb;
   geo.tile_bytes = s.tile_bytes;
   geo.sb_bytes = kGemvWarps * s.tile_bytes;
-  geo.sum_half = usb * kG4SbSumBytes;
+  geo.sum_half = usb * kG4SbSumBytes;  // the stage's sum region is 2 * sum_half = usb x 1 KB
   geo.frag_off = usb * geo.sb_bytes;
   geo.sum_off = geo.frag_off + usb * nt * kXfragSbBytes;
   geo.stage_bytes = geo.sum_off + 2 * geo.sum_half;

@@ -161,12 +161,11 @@ __global__ void __launch_bounds__(kG4Threads, 1) window_mk_kernel(MkParams P) {
       auto late = [&](int g2, int pr2, uint8_t* st, uint64_t* bar) {
         if (ph.kind == MK_GEMV) {
           const MkGemv& m = ph.g;
-          const int nsb = min(2, m.geo.sb - 2 * pr2), nsub = m.geo.sb * 8;
+          const int nsb = min(2, m.geo.sb - 2 * pr2);
           bulk_g2s(st + m.geo.frag_off, m.in.frag + (size_t)2 * pr2 * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
                    bar);
-          for (int h = 0; h < 2; ++h)
-            bulk_g2s(st + m.geo.sum_off + h * m.geo.sum_half, m.in.sum + ((size_t)h * nsub + 16 * pr2) * 16,
-                     (uint32_t)(nsb * 512), bar);
+          bulk_g2s(st + m.geo.sum_off, reinterpret_cast<const uint8_t*>(m.in.sum) + (size_t)2 * pr2 * 1024,
+                   (uint32_t)(nsb * 1024), bar);
         } else if ((long long)(pr2 + 1) * 64 > base) {
           const MkAttn& a = ph.a;
           const int kvh = g2 % a.nkv;
