@@ -576,6 +576,10 @@ def run_pipeline(args, world, rank, local):
     e2e_s = max_over_ranks(world, time.perf_counter() - t0, dev)
     e2e_emitted = sum_over_ranks(world, int(hcnt.sum().item()) if pipe.is_tail else 0, dev)
     pipe.status()
+    # torch buffers used on the engine's stream are released while that stream still exists (the pinned host
+    # allocator records an event on it when a buffer is freed)
+    del host, hcnt, e_toks, e_cnt, toks, cnt
+    torch.cuda.synchronize(dev)
     pipe.close(lambda: barrier(world))
     ctx.close()
     if rank != 0:

@@ -94,6 +94,25 @@ __device__ __forceinline__ void l2_prefetch_share(const uint8_t* base, unsigned 
   }
 }
 
+// mbar_wait for a thread that can afford a little latency (a producer waiting for a ring slot): sleeps `ns`
+// nanoseconds between polls, so the spin does not take issue slots from the warps doing the work.  Bounded like
+// mbar_wait (kSpinLimit polls).
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err, uint32_t ns) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    __nanosleep(ns);
+  }
+  if (err != nullptr) atomicExch(err, kErrWaitTimeout);
+  return false;
+}
+
 // Release-add on a global counter (gpu scope): makes this thread's earlier writes, and those ordered before it by a
 // CTA barrier, visible to a reader that acquires the counter.
 __device__ __forceinline__ void red_release_add(int* ctr, int v) {

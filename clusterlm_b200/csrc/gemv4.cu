@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
       griddep_launch();
       for (int i = 0; i < pre; ++i, a.next(geo.ppr, stages)) issue_acts(a);
       for (int i = pre; i < n; ++i, w.next(geo.ppr, stages)) {
-        if (!mbar_wait(&empty[w.slot], w.phase ^ 1u, epi.err)) break;  // the slot's previous use is consumed
+        // the slot's previous use is consumed (sleeping between polls leaves the issue slots to the consumers)
+        if (!mbar_wait_backoff(&empty[w.slot], w.phase ^ 1u, epi.err, 128)) break;
         issue_weights(w);
         issue_acts(w);
       }
