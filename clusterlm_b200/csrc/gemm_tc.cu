@@ -1,0 +1,340 @@
+// gemm_tc.cu — wide-window dequantising GEMM on the 5th-generation tensor cores (tcgen05 / TMEM), sm_100a.
+//
+// Y[p][n] = W[n] . X[p] for p < P window rows (17 <= P <= 256: tree windows of several sequences, prefill chunks),
+// W in GGUF Q4_K / Q8_0, repacked in the group-major tile layout of gemv.cuh.  The q <= 16 windows use the
+// bandwidth-bound q-row GEMV (gemv4.cu); from P > 16 on the tensor-core work per weight byte grows with P and the
+// tcgen05 path takes over:
+//
+//  * Grid (row group of 128 weight rows, K split).  A CTA walks its K range in chunks of 64 columns.  For every
+//    chunk eight warps dequantise the group's 128 x 64 weights (row tile w of warp w) from the repacked tiles
+//    into fp16 in shared memory, and load the window's P x 64 activations (f32 -> fp16); both tiles are written in
+//    the K-major 128-byte-swizzle layout that tcgen05.mma reads (8-row atoms of 1024 B, 16-byte chunk c of row r
+//    stored at chunk c ^ (r % 8)).  A 4-stage ring of such tiles keeps the dequantisation ahead of the MMAs.
+//  * Warp 8 owns the accumulator: it allocates P (rounded up to a power of two, >= 32) TMEM columns, and one of
+//    its lanes issues the four K = 16 tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = P window
+//    rows, f32 accumulate in TMEM) per chunk once the stage's "full" mbarrier has all eight warps' arrivals, then
+//    tcgen05.commit releases the stage ("free" mbarrier) when those MMAs have read it.
+//  * After the last chunk a commit on the "done" mbarrier hands the accumulator to the epilogue: warp w reads TMEM
+//    lanes 32 (w % 4) .. +31 (its weight rows) and half of the columns with tcgen05.ld and stores the f32 partial
+//    of its K range; a second kernel sums the K splits in split order (deterministic) into Y.
+//  * Every mbarrier wait is bounded (bulk.cuh) and records an error instead of hanging; the TMEM columns are
+//    freed by the CTA that allocated them on every path.
+//
+// Weights are dequantised as GGUF decodes them (Q4_K: q * (d*sc) - dmin*m, Q8_0: q * d), rounded to fp16 once
+// (d*sc and dmin*m are themselves fp16); the activations are rounded to fp16; products accumulate in f32.
+#include "bulk.cuh"
+#include "gemm_tc.cuh"
+#include "gemv_tile.cuh"
+#include "pdl.cuh"
+
+namespace clm {
+
+namespace {
+
+constexpr int kTcWarps = 8;                   // dequant / load / epilogue warps
+constexpr int kTcThreads = 32 * (kTcWarps + 1);  // + the MMA warp
+constexpr int kTcStages = 4;
+constexpr int kTcKc = 64;                     // columns per chunk (one 128-byte swizzle row of fp16)
+constexpr uint32_t kATileBytes = 128 * kTcKc * 2;  // 16 KB
+
+// Byte offset of element chunk (row r, 16-byte chunk c) in a K-major SW128 tile.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart (SBO), LBO unused (1).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);        // start address
+  d |= (uint64_t)1u << 16;                          // leading byte offset (16-byte units), unused for SW128 K-major
+  d |= (uint64_t)(1024u >> 4) << 32;                // stride byte offset: next 8-row atom
+  d |= (uint64_t)1u << 46;                          // descriptor version (sm100)
+  d |= (uint64_t)2u << 61;                          // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor of kind::f16: A, B fp16 (K-major), D f32, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint4 ldg_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+constexpr uint32_t kMagic1152 = 0x64806480u;  // fp16 pair (1152, 1152) = 1024 + 128
+
+// fp16 pairs of 8 consecutive weights of one row, two sub-blocks: `lo` for columns [8q, 8q+8) of the chunk's
+// first sub-block, `hi` for the same columns of the second.
+struct Dq8 {
+  uint4 lo, hi;
+};
+
+// Q4_K: the thread's four nibble words (k-steps 4q..4q+3 of the quarter j of the superblock) for rows g and g+8.
+__device__ __forceinline__ void dq_q4k(const uint8_t* tile, int j, int g, int qq, Dq8& r0, Dq8& r8) {
+  const uint4 raw = ldg_nc(tile + (size_t)(qq * 32 + 4 * g + j) * 16);
+  const uint4 rg = ldg_nc(tile + 2048 + 16 * g), rg8 = ldg_nc(tile + 2048 + 16 * (g + 8));
+  const RowDq d = q4k_row(rg, j), d8 = q4k_row(rg8, j);
+  const uint32_t mA = lo_bcast(d.negm), mB = hi_bcast(d.negm), mA8 = lo_bcast(d8.negm), mB8 = hi_bcast(d8.negm);
+  uint32_t magic;
+  asm volatile("mov.b32 %0, %1;" : "=r"(magic) : "n"(kMagic));
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t o0[4], o1[4], o8[4], o9[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t x = w[s], x4 = x >> 4, x8 = x >> 8, x12 = x >> 12;
+    // q exactly (1024 + q - 1024), then q * (d*sc) - dmin*m with one rounding
+    o0[s] = hfma2u(hsub2u(and_or<0x000F000Fu>(x, magic), kMagic), d.sA, mA);
+    o1[s] = hfma2u(hsub2u(and_or<0x000F000Fu>(x4, magic), kMagic), d.sB, mB);
+    o8[s] = hfma2u(hsub2u(and_or<0x000F000Fu>(x8, magic), kMagic), d8.sA, mA8);
+    o9[s] = hfma2u(hsub2u(and_or<0x000F000Fu>(x12, magic), kMagic), d8.sB, mB8);
+  }
+  r0.lo = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+  r0.hi = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  r8.lo = make_uint4(o8[0], o8[1], o8[2], o8[3]);
+  r8.hi = make_uint4(o9[0], o9[1], o9[2], o9[3]);
+}
+
+// Q8_0: the thread's eight int8 words (k-steps 4q..4q+3, blocks 2j and 2j+1) for rows g and g+8.
+__device__ __forceinline__ void dq_q80(const uint8_t* tile, int j, int g, int qq, Dq8& r0, Dq8& r8) {
+  const uint8_t* base = tile + (size_t)(qq * 256 + (4 * g + j) * 8) * 4;
+  const uint4 a = ldg_nc(base), b = ldg_nc(base + 16);
+  const uint32_t sg = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * g + 4 * j));
+  const uint32_t sg8 = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * j));
+  const uint32_t sA = lo_bcast(sg), sB = hi_bcast(sg), sA8 = lo_bcast(sg8), sB8 = hi_bcast(sg8);
+  // words in order (s, e): a = {(0,0),(0,1),(1,0),(1,1)}, b = {(2,0),(2,1),(3,0),(3,1)}
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t o0[4], o1[4], o8[4], o9[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const uint32_t x0 = w[2 * s] ^ 0x80808080u, x1 = w[2 * s + 1] ^ 0x80808080u;
+    // the signed byte exactly (1024 + (b + 128) - 1152), then b * d with one rounding
+    o0[s] = hmul2u(hsub2u(__byte_perm(x0, 0x64646464u, 0x4140), kMagic1152), sA);
+    o8[s] = hmul2u(hsub2u(__byte_perm(x0, 0x64646464u, 0x4342), kMagic1152), sA8);
+    o1[s] = hmul2u(hsub2u(__byte_perm(x1, 0x64646464u, 0x4140), kMagic1152), sB);
+    o9[s] = hmul2u(hsub2u(__byte_perm(x1, 0x64646464u, 0x4342), kMagic1152), sB8);
+  }
+  r0.lo = make_uint4(o0[0], o0[1], o0[2], o0[3]);
+  r0.hi = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  r8.lo = make_uint4(o8[0], o8[1], o8[2], o8[3]);
+  r8.hi = make_uint4(o9[0], o9[1], o9[2], o9[3]);
+}
+
+template <int QUANT>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* __restrict__ tiles, int sb_count,
+                                                                 int tile_bytes, const float* __restrict__ x, int q,
+                                                                 int K, int P, int ksplit,
+                                                                 float* __restrict__ part, uint32_t rows_total,
+                                                                 int* __restrict__ err) {
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  __shared__ __align__(8) uint64_t full[kTcStages], freeb[kTcStages], done;
+  __shared__ uint32_t s_tmem;
+  // 1024-byte aligned tile area (the dynamic allocation carries 1 KB of slack)
+  uint8_t* tc_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
+  const uint32_t btile = (uint32_t)P * 128u;
+  const uint32_t stage_bytes = kATileBytes + btile;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int grp = blockIdx.x, split = blockIdx.y;
+  const int chunks = K / kTcKc;
+  const int c0 = split * chunks / ksplit, c1 = (split + 1) * chunks / ksplit;
+  const int ncols = P <= 32 ? 32 : (P <= 64 ? 64 : (P <= 128 ? 128 : 256));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], kTcWarps);
+      mbar_init(&freeb[s], 1);
+    }
+    mbar_init(&done, 1);
+    mbar_fence_init();
+  }
+  if (warp == kTcWarps) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  griddep_wait();
+  griddep_launch();
+
+  if (warp == kTcWarps) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(P);
+      const uint32_t sbase = smem_addr(tc_smem);
+      int slot = 0;
+      uint32_t phase = 0;
+      for (int c = c0; c < c1; ++c) {
+        mbar_wait(&full[slot], phase, err);
+        tc_fence_after();
+        const uint32_t a = sbase + (uint32_t)slot * stage_bytes, b = a + kATileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTcKc / 16; ++kk)
+          umma_f16(tmem, umma_desc_sw128(a + 32 * kk), umma_desc_sw128(b + 32 * kk), idesc,
+                   (c > c0 || kk > 0) ? 1u : 0u);
+        umma_commit(&freeb[slot]);  // the stage is free once these MMAs have read it
+        if (++slot == kTcStages) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      umma_commit(&done);  // all MMAs of the CTA complete: the accumulator is final
+    }
+    __syncwarp();
+  } else {
+    // ---------------- dequant / activation warps ----------------
+    const int rt = warp, g = lane / 4, qq = lane % 4;
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int c = c0; c < c1; ++c) {
+      // the slot's previous MMAs have read it (a fresh barrier passes the parity-1 wait at once)
+      mbar_wait(&freeb[slot], phase ^ 1u, err);
+      uint8_t* A = tc_smem + (size_t)slot * stage_bytes;
+      uint8_t* B = A + kATileBytes;
+      const int sb = c / 4, j = c % 4;
+      const uint8_t* tile = tiles + (((size_t)grp * sb_count + sb) * kGemvWarps + rt) * (size_t)tile_bytes;
+      Dq8 r0, r8;
+      if (QUANT == CLM_QUANT_Q4_K)
+        dq_q4k(tile, j, g, qq, r0, r8);
+      else
+        dq_q80(tile, j, g, qq, r0, r8);
+      const int row = rt * 16 + g;
+      *reinterpret_cast<uint4*>(A + sw128_off(row, qq)) = r0.lo;
+      *reinterpret_cast<uint4*>(A + sw128_off(row, 4 + qq)) = r0.hi;
+      *reinterpret_cast<uint4*>(A + sw128_off(row + 8, qq)) = r8.lo;
+      *reinterpret_cast<uint4*>(A + sw128_off(row + 8, 4 + qq)) = r8.hi;
+      // activations: P rows x 8 chunks of 8 columns, f32 -> fp16 (rows >= q are zero)
+      for (int i = threadIdx.x; i < P * 8; i += kTcWarps * 32) {
+        const int p = i / 8, ch = i % 8;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (p < q) {
+          const float4* src = reinterpret_cast<const float4*>(x + (size_t)p * K + (size_t)c * kTcKc + 8 * ch);
+          const float4 u0 = __ldg(src), u1 = __ldg(src + 1);
+          v = make_uint4(pack_half2(u0.x, u0.y), pack_half2(u0.z, u0.w), pack_half2(u1.x, u1.y),
+                         pack_half2(u1.z, u1.w));
+        }
+        *reinterpret_cast<uint4*>(B + sw128_off(p, ch)) = v;
+      }
+      fence_async_smem();  // generic-proxy writes -> visible to the tensor core's async reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[slot]);
+      if (++slot == kTcStages) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    // ---------------- epilogue: TMEM -> f32 partial ----------------
+    mbar_wait(&done, 0, err);
+    tc_fence_after();
+    const int quarter = warp % 4, colhalf = warp / 4;
+    const uint32_t row = (uint32_t)grp * 128 + 32 * quarter + lane;
+    float* out = part + (size_t)split * q * rows_total;
+    for (int cb = colhalf * 32; cb < P; cb += 64) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)cb, v);
+      if (row < rows_total) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (cb + i < q) out[(size_t)(cb + i) * rows_total + row] = v[i];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTcWarps) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols) : "memory");
+  }
+}
+
+__global__ void split_sum_kernel(const float* __restrict__ part, int ksplit, uint64_t n, float* __restrict__ y) {
+  griddep_wait();
+  griddep_launch();
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    float a = part[i];
+    for (int s = 1; s < ksplit; ++s) a += part[(uint64_t)s * n + i];
+    y[i] = a;
+  }
+}
+
+}  // namespace
+
+TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count) {
+  TcPlan p;
+  p.P = ((q + 15) / 16) * 16;
+  const int chunks = (int)s.cols / kTcKc;
+  // enough CTAs for the SMs, at least two chunks per CTA
+  int ks = (int)((sm_count + s.ng - 1) / s.ng);
+  if (ks > chunks / 2) ks = chunks / 2;
+  if (ks < 1) ks = 1;
+  p.ksplit = ks;
+  p.smem = 1024 + (size_t)kTcStages * (kATileBytes + (size_t)p.P * 128);
+  p.part_floats = (size_t)ks * q * s.rows;
+  return p;
+}
+
+int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
+                   float* d_part, int* d_err, cudaStream_t st) {
+  CLM_CHECK(q > 16 && q <= 256, CLM_OUT_OF_RANGE, "tensor-core GEMM covers 17..256 window rows");
+  CLM_CHECK(s.cols % kTcKc == 0 && s.cols % 256 == 0, CLM_INVALID_ARGUMENT, "columns must be a multiple of 256");
+  CLM_CHECK(s.quant == CLM_QUANT_Q4_K || s.quant == CLM_QUANT_Q8_0, CLM_UNIMPLEMENTED, "tensor-core GEMM: Q4_K / Q8_0");
+  CLM_CHECK(p.smem <= 227 * 1024, CLM_RESOURCE_EXHAUSTED, "tensor-core GEMM: shared memory");
+  const dim3 grid(s.ng, (unsigned)p.ksplit);
+  if (s.quant == CLM_QUANT_Q4_K) {
+    CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q4_K>, p.smem));
+    CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q4_K>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
+                       s.tile_bytes, d_x, q, (int)s.cols, p.P, p.ksplit, p.ksplit > 1 ? d_part : d_y, s.rows, d_err));
+  } else {
+    CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q8_0>, p.smem));
+    CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q8_0>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
+                       s.tile_bytes, d_x, q, (int)s.cols, p.P, p.ksplit, p.ksplit > 1 ? d_part : d_y, s.rows, d_err));
+  }
+  if (p.ksplit > 1) {
+    const uint64_t n = (uint64_t)q * s.rows;
+    CLM_TRY(launch_pdl(split_sum_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,
+                       (const float*)d_part, p.ksplit, n, d_y));
+  }
+  return CLM_OK;
+}
+
+}  // namespace clm

@@ -1,0 +1,23 @@
+// gemm_tc.cuh — wide-window (17..256 rows) dequantising GEMM on tcgen05 tensor cores (kernel in gemm_tc.cu).
+#pragma once
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace clm {
+
+struct TcPlan {
+  int P = 0;              // window rows rounded up to a multiple of 16 (the MMA's N)
+  int ksplit = 1;         // K splits (grid y); > 1 sums f32 partials in split order
+  size_t smem = 0;        // dynamic shared memory of one CTA
+  size_t part_floats = 0; // f32 partials needed when ksplit > 1
+};
+
+TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count);
+
+// y[p][n] = W[n] . x[p] (x: q x cols f32 row-major, 16-byte aligned; y: q x rows f32) for 17 <= q <= 256 with W
+// in the tile layout of gemv.cuh (Q4_K or Q8_0).  d_part holds p.part_floats floats when p.ksplit > 1; a bounded
+// wait that gives up stores kErrWaitTimeout in *d_err (if not null).
+int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
+                   float* d_part, int* d_err, cudaStream_t st);
+
+}  // namespace clm

@@ -5,6 +5,7 @@
 #include "codec.cuh"
 #include "gemv.cuh"
 #include "gemv2.cuh"
+#include "gemm_tc.cuh"
 #include "matrix.cuh"
 
 namespace clm {
@@ -116,6 +117,15 @@ int matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, i
   if (w->quant == CLM_QUANT_F32 || w->quant == CLM_QUANT_Q8_FIXTURE)
     return launch_gemv_f32(static_cast<const float*>(w->data), w->rows, w->cols, d_x, q, d_y, st);
   const GemvShape& s = w->shape;
+  if (q > 16) {
+    // wide windows: tcgen05 tensor-core GEMM (gemm_tc.cu)
+    CLM_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CLM_INVALID_ARGUMENT, "x must be 16-byte aligned");
+    const TcPlan tp = gemm_tc_plan(s, q, ctx->sm_count);
+    void* scratch = nullptr;
+    if (tp.ksplit > 1) CLM_TRY(ctx_scratch(ctx, tp.part_floats * sizeof(float), &scratch));
+    return launch_gemm_tc(s, tp, static_cast<const uint8_t*>(w->data), d_x, q, d_y, static_cast<float*>(scratch),
+                          nullptr, st);
+  }
   const GemvPlan p = gemv_plan(s, q, ctx->sm_count);
   const size_t fb = xfrag_bytes((int)s.cols, p.nt), sb = xsum_bytes((int)s.cols);
   const size_t pb = (size_t)s.ng * p.ksplit * q * 128 * sizeof(float), cb = (size_t)s.ng * sizeof(int);
@@ -178,7 +188,9 @@ int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const floa
   CLM_TRY(ctx_enter(ctx));
   CLM_CHECK(w != nullptr && d_x != nullptr && d_y != nullptr, CLM_INVALID_ARGUMENT, "null argument");
   CLM_CHECK(w->ctx == ctx, CLM_INVALID_ARGUMENT, "matrix belongs to another context");
-  CLM_CHECK(positions >= 1 && positions <= 16, CLM_OUT_OF_RANGE, "positions must be in [1, 16]");
+  CLM_CHECK(positions >= 1 && positions <= 256, CLM_OUT_OF_RANGE, "positions must be in [1, 256]");
+  CLM_CHECK(positions <= 16 || w->quant == CLM_QUANT_Q4_K || w->quant == CLM_QUANT_Q8_0, CLM_OUT_OF_RANGE,
+            "more than 16 positions need a Q4_K or Q8_0 matrix");
   return matmul_rows(ctx, w, d_x, (int)positions, d_y, pick_stream(ctx, stream));
 }
 

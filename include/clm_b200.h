@@ -97,7 +97,9 @@ CLM_API int clm_b200_matrix_upload_device(clm_b200_ctx* ctx, int quant, const vo
 CLM_API int clm_b200_matrix_free(clm_b200_matrix* m);
 CLM_API int clm_b200_matrix_info(const clm_b200_matrix* m, int* quant, uint32_t* rows, uint32_t* cols, uint64_t* device_bytes);
 /* y[p][i] = W[i] . x[p] for p < positions (output position-major, as reference_matmul_rows).
- * 1 <= positions <= 16.  fp16 tensor-core products with f32 accumulation for Q4_K / Q8_0; f32 for f32. */
+ * 1 <= positions <= 16: the bandwidth-bound q-row GEMV (fp16 tensor-core products, f32 accumulation) for Q4_K /
+ * Q8_0, f32 for f32.  17 <= positions <= 256 (Q4_K / Q8_0 only, d_x 16-byte aligned): a tcgen05 tensor-core GEMM
+ * with TMEM accumulators (weights dequantised to fp16 in shared memory, activations rounded to fp16). */
 CLM_API int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, uint32_t positions,
                          float* d_y, void* stream);
 /* The same product with all of its scratch in a fixed CLM_B200_STATIC_SCRATCH_BYTES device array compiled into

@@ -130,6 +130,19 @@ def test_matmul_rows_llama_shapes(ctx, oracle, quant, rows, cols):
     assert np.abs(y - want).max() / np.abs(want).max() < 2e-2
 
 
+@pytest.mark.parametrize("quant,rows,cols,q", [("q4_k", 256, 1024, 17), ("q8_0", 256, 1024, 17),
+                                               ("q4_k", 384, 2048, 64), ("q8_0", 208, 512, 40),
+                                               ("q8_0", 512, 1024, 128), ("q4_k", 128, 4096, 256),
+                                               ("q4_k", 4096, 4096, 128)])
+def test_matmul_rows_wide_tensor_cores(ctx, oracle, quant, rows, cols, q):
+    """17..256 positions run on the tcgen05 GEMM (weights dequantised to fp16 in shared memory, activations fp16,
+    f32 accumulation in tensor memory): the same product as reference_matmul_rows within fp16 rounding."""
+    y, want = _gemv_case(ctx, oracle, quant, rows, cols, q, seed=q)
+    rel = np.linalg.norm(y - want) / np.linalg.norm(want)
+    assert rel < 2e-3, rel
+    assert np.abs(y - want).max() / np.abs(want).max() < 1e-2
+
+
 def test_matmul_rows_f32(ctx, oracle):
     y, want = _gemv_case(ctx, oracle, "f32", 100, 70, 5)
     assert np.abs(y - want).max() < 1e-4
