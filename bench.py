@@ -15,6 +15,8 @@ e2e          the same through clm_b200_spec_round (host API: round parameters ho
 roofline     the verify window (32 layers + head, q = 4): algorithmic bytes / event-timed window duration
 cpu_baseline the oracle's refmath-order CPU restatement on this host's cores, a bounded sample (one decoder
              layer at context 4096 + the LM head + one MTP step, q = 4) extrapolated to a round
+wide_window  128 window rows (8 sequences x 16 tree nodes) through the tcgen05 tensor-core GEMM over one 8B layer's
+             Q8_0 matrices: TFLOP/s against the measured bf16 tensor peak
 With N > 1 (torchrun, one process per GPU) the model is split into N pipeline stages (layer ranges balanced by
 the bytes each stage streams per round; the tail holds the LM head and the MTP drafter), joined by device links
 over NVLink, with N sequences in flight (--inflight) so that every stage is busy: weak scaling (each GPU streams
@@ -373,6 +375,59 @@ def tree_micro(ctx, dev, peak, context):
                          "achieved": algo / sec / 1e9, "peak": peak, "unit": "GB/s", "frac": algo / sec / 1e9 / peak}}
 
 
+def load_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def wide_micro(ctx, dev):
+    """The C4 batch's weight stream as one wide window: 8 sequences x 16 tree nodes = 128 rows through the
+    tcgen05 GEMM (clm_b200_matmul_rows with 128 positions) over one 8B-shape decoder layer's matrices in Q8_0
+    (qkv, o, gate|up, down), event-timed back to back with device-resident inputs; 32 layers extrapolated."""
+    import torch
+
+    from clusterlm_b200.runtime import Matrix, generate_weights, encode
+
+    rows_q = 128
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate|up": (28672, 4096), "down": (4096, 14336)}
+    mats, xs, ys = [], [], []
+    for tid, (name, (r, c)) in enumerate(shapes.items()):
+        w = generate_weights(ctx, SEED, 900 + tid, 0, r * c, 0.02)
+        mats.append(Matrix(ctx, "q8_0", encode(ctx, "q8_0", w), r, c))
+        del w
+        xs.append(torch.randn((rows_q, c), device=dev, generator=torch.Generator(device=dev).manual_seed(tid)))
+        ys.append(torch.empty((rows_q, r), device=dev))
+    torch.cuda.synchronize(dev)
+    for _ in range(3):
+        for m, x, y in zip(mats, xs, ys):
+            m.matmul_rows(x, y)
+    torch.cuda.synchronize(dev)
+    n = 10
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(n):
+        for m, x, y in zip(mats, xs, ys):
+            m.matmul_rows(x, y)
+    s1.record()
+    torch.cuda.synchronize(dev)
+    sec = s0.elapsed_time(s1) / 1e3 / n
+    for m in mats:
+        m.close()
+    params = sum(r * c for r, c in shapes.values())
+    flops = 2.0 * rows_q * params
+    peak, kind = load_tensor_peak()
+    tf = flops / sec / 1e12
+    return {"config": "one 8B-shape decoder layer (qkv 6144x4096, o 4096^2, gate|up 28672x4096, down 4096x14336), "
+                      "Q8_0, 128 window rows (8 sequences x 16 tree nodes), x f32 in, y f32 out",
+            "ms_per_layer": sec * 1e3, "ms_per_32_layers": 32 * sec * 1e3,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_kind": kind, "flops_per_layer": flops,
+                         "weight_gbs": params * 34 / 32 / sec / 1e9}}
+
+
 def run_b200(args, world, rank, local):
     import numpy as np
     import torch
@@ -454,6 +509,7 @@ def run_b200(args, world, rank, local):
     eng.close()
     micro = acceptance_micro(ctx, dev, peak, not args.no_cpu) if (world == 1 and not profile_case(args)) else None
     tree = tree_micro(ctx, dev, peak, context) if (world == 1 and not profile_case(args)) else None
+    wide = wide_micro(ctx, dev) if (world == 1 and not profile_case(args)) else None
     ctx.close()
 
     if rank != 0:
@@ -491,6 +547,8 @@ def run_b200(args, world, rank, local):
         line["acceptance_micro"] = micro
     if tree:
         line["tree_window"] = tree
+    if wide:
+        line["wide_window"] = wide
     print(json.dumps(line), flush=True)
 
 

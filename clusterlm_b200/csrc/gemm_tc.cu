@@ -5,14 +5,19 @@
 // bandwidth-bound q-row GEMV (gemv4.cu); from P > 16 on the tensor-core work per weight byte grows with P and the
 // tcgen05 path takes over:
 //
-//  * Grid (row group of 128 weight rows, K split).  A CTA walks its K range in chunks of 64 columns.  For every
-//    chunk eight warps dequantise the group's 128 x 64 weights (row tile w of warp w) from the repacked tiles
-//    into fp16 in shared memory, and load the window's P x 64 activations (f32 -> fp16); both tiles are written in
-//    the K-major 128-byte-swizzle layout that tcgen05.mma reads (8-row atoms of 1024 B, 16-byte chunk c of row r
-//    stored at chunk c ^ (r % 8)).  A 4-stage ring of such tiles keeps the dequantisation ahead of the MMAs.
+//  * A first kernel converts the window's activations (f32) to fp16 tiles already in the MMA's layout (K-major,
+//    128-byte swizzle: 8-row atoms of 1024 B, 16-byte chunk c of row r stored at chunk c ^ (r % 8)), one
+//    P x 64 tile per 64-column chunk.
+//  * Grid (row group of 128 weight rows, K split).  A CTA walks its K range in chunks of 64 columns.  Warp 9
+//    bulk-copies (cp.async.bulk, no multicast) the group's raw superblocks (8 repacked tiles, issued before
+//    griddepcontrol.wait) into a 2-slot ring and each chunk's activation tile into the chunk's stage.  For every
+//    chunk eight warps dequantise the group's 128 x 64 weights (row tile w of warp w) from the staged superblock
+//    into the stage's fp16 A tile, in the same swizzled layout.  Up to four stages keep the copies and the
+//    dequantisation ahead of the MMAs.
 //  * Warp 8 owns the accumulator: it allocates P (rounded up to a power of two, >= 32) TMEM columns, and one of
 //    its lanes issues the four K = 16 tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = P window
-//    rows, f32 accumulate in TMEM) per chunk once the stage's "full" mbarrier has all eight warps' arrivals, then
+//    rows, f32 accumulate in TMEM) per chunk once the stage's "full" mbarrier has the eight warps' arrivals and
+//    the activation tile's bytes, then
 //    tcgen05.commit releases the stage ("free" mbarrier) when those MMAs have read it.
 //  * After the last chunk a commit on the "done" mbarrier hands the accumulator to the epilogue: warp w reads TMEM
 //    lanes 32 (w % 4) .. +31 (its weight rows) and half of the columns with tcgen05.ld and stores the f32 partial
@@ -31,9 +36,10 @@ namespace clm {
 
 namespace {
 
-constexpr int kTcWarps = 8;                   // dequant / load / epilogue warps
-constexpr int kTcThreads = 32 * (kTcWarps + 1);  // + the MMA warp
-constexpr int kTcStages = 4;
+constexpr int kTcWarps = 8;                      // dequant / epilogue warps
+constexpr int kTcThreads = 32 * (kTcWarps + 2);  // + the MMA warp + the copy warp
+constexpr int kTcMaxStages = 4;
+constexpr int kTcRawSlots = 2;                   // raw superblock stages (8 repacked tiles each)
 constexpr int kTcKc = 64;                     // columns per chunk (one 128-byte swizzle row of fp16)
 constexpr uint32_t kATileBytes = 128 * kTcKc * 2;  // 16 KB
 
@@ -92,7 +98,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ uint4 ldg_nc(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 
 __device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
   uint32_t d;
@@ -107,10 +113,11 @@ struct Dq8 {
   uint4 lo, hi;
 };
 
-// Q4_K: the thread's four nibble words (k-steps 4q..4q+3 of the quarter j of the superblock) for rows g and g+8.
+// Q4_K: the thread's four nibble words (k-steps 4q..4q+3 of the quarter j of the superblock) for rows g and g+8,
+// from the tile staged in shared memory.
 __device__ __forceinline__ void dq_q4k(const uint8_t* tile, int j, int g, int qq, Dq8& r0, Dq8& r8) {
-  const uint4 raw = ldg_nc(tile + (size_t)(qq * 32 + 4 * g + j) * 16);
-  const uint4 rg = ldg_nc(tile + 2048 + 16 * g), rg8 = ldg_nc(tile + 2048 + 16 * (g + 8));
+  const uint4 raw = lds128(tile + (size_t)(qq * 32 + 4 * g + j) * 16);
+  const uint4 rg = lds128(tile + 2048 + 16 * g), rg8 = lds128(tile + 2048 + 16 * (g + 8));
   const RowDq d = q4k_row(rg, j), d8 = q4k_row(rg8, j);
   const uint32_t mA = lo_bcast(d.negm), mB = hi_bcast(d.negm), mA8 = lo_bcast(d8.negm), mB8 = hi_bcast(d8.negm);
   uint32_t magic;
@@ -132,12 +139,13 @@ __device__ __forceinline__ void dq_q4k(const uint8_t* tile, int j, int g, int qq
   r8.hi = make_uint4(o9[0], o9[1], o9[2], o9[3]);
 }
 
-// Q8_0: the thread's eight int8 words (k-steps 4q..4q+3, blocks 2j and 2j+1) for rows g and g+8.
+// Q8_0: the thread's eight int8 words (k-steps 4q..4q+3, blocks 2j and 2j+1) for rows g and g+8, from shared
+// memory.
 __device__ __forceinline__ void dq_q80(const uint8_t* tile, int j, int g, int qq, Dq8& r0, Dq8& r8) {
   const uint8_t* base = tile + (size_t)(qq * 256 + (4 * g + j) * 8) * 4;
-  const uint4 a = ldg_nc(base), b = ldg_nc(base + 16);
-  const uint32_t sg = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * g + 4 * j));
-  const uint32_t sg8 = __ldg(reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * j));
+  const uint4 a = lds128(base), b = lds128(base + 16);
+  const uint32_t sg = *reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * g + 4 * j);
+  const uint32_t sg8 = *reinterpret_cast<const uint32_t*>(tile + 4096 + 16 * (g + 8) + 4 * j);
   const uint32_t sA = lo_bcast(sg), sB = hi_bcast(sg), sA8 = lo_bcast(sg8), sB8 = hi_bcast(sg8);
   // words in order (s, e): a = {(0,0),(0,1),(1,0),(1,1)}, b = {(2,0),(2,1),(3,0),(3,1)}
   const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -157,19 +165,40 @@ __device__ __forceinline__ void dq_q80(const uint8_t* tile, int j, int g, int qq
   r8.hi = make_uint4(o9[0], o9[1], o9[2], o9[3]);
 }
 
+// x (q x K f32) -> fp16 activation tiles in the MMA's layout: [K / 64 chunks][P rows, SW128 K-major], rows >= q zero,
+// so that each chunk's B tile is one contiguous bulk copy.
+__global__ void tc_xprep_kernel(const float* __restrict__ x, int q, int K, int P, uint8_t* __restrict__ xh) {
+  griddep_wait();
+  griddep_launch();
+  const uint64_t n = (uint64_t)(K / kTcKc) * P * 8;  // 16-byte chunks
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const int ch = (int)(i % 8), p = (int)((i / 8) % P), c = (int)(i / ((uint64_t)8 * P));
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (p < q) {
+      const float4* src = reinterpret_cast<const float4*>(x + (size_t)p * K + (size_t)c * kTcKc + 8 * ch);
+      const float4 u0 = __ldg(src), u1 = __ldg(src + 1);
+      v = make_uint4(pack_half2(u0.x, u0.y), pack_half2(u0.z, u0.w), pack_half2(u1.x, u1.y), pack_half2(u1.z, u1.w));
+    }
+    *reinterpret_cast<uint4*>(xh + (size_t)c * P * 128 + sw128_off(p, ch)) = v;
+  }
+}
+
 template <int QUANT>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* __restrict__ tiles, int sb_count,
-                                                                 int tile_bytes, const float* __restrict__ x, int q,
-                                                                 int K, int P, int ksplit,
+                                                                 int tile_bytes, const uint8_t* __restrict__ xh, int q,
+                                                                 int K, int P, int ksplit, int stages,
                                                                  float* __restrict__ part, uint32_t rows_total,
                                                                  int* __restrict__ err) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], freeb[kTcStages], done;
+  __shared__ __align__(8) uint64_t full[kTcMaxStages], freeb[kTcMaxStages], raw_full[kTcRawSlots],
+      raw_free[kTcRawSlots], done;
   __shared__ uint32_t s_tmem;
-  // 1024-byte aligned tile area (the dynamic allocation carries 1 KB of slack)
+  // 1024-byte aligned area (the dynamic allocation carries 1 KB of slack): [stages x (A tile, B tile)][raw slots]
   uint8_t* tc_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
   const uint32_t btile = (uint32_t)P * 128u;
   const uint32_t stage_bytes = kATileBytes + btile;
+  const uint32_t raw_bytes = (uint32_t)kGemvWarps * (uint32_t)tile_bytes;
+  uint8_t* raw_base = tc_smem + (size_t)stages * stage_bytes;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int grp = blockIdx.x, split = blockIdx.y;
   const int chunks = K / kTcKc;
@@ -177,9 +206,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
   const int ncols = P <= 32 ? 32 : (P <= 64 ? 64 : (P <= 128 ? 128 : 256));
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full[s], kTcWarps);
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], kTcWarps + 1);  // eight dequant warps + the copy warp's expect_tx of the B tile
       mbar_init(&freeb[s], 1);
+    }
+    for (int s = 0; s < kTcRawSlots; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_free[s], kTcWarps);
     }
     mbar_init(&done, 1);
     mbar_fence_init();
@@ -194,11 +227,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  griddep_wait();
-  griddep_launch();
 
-  if (warp == kTcWarps) {
+  if (warp == kTcWarps + 1) {
+    // ---------------- copy warp: raw superblocks (weights, before griddepcontrol.wait) and B tiles ----------------
+    if (lane == 0) {
+      const uint64_t policy = evict_first_policy();
+      int rslot = 0, slot = 0;
+      uint32_t rphase = 0, phase = 0;
+      bool waited = false;
+      for (int c = c0; c < c1; ++c) {
+        if (c == c0 || c % 4 == 0) {
+          if (!mbar_wait_backoff(&raw_free[rslot], rphase ^ 1u, err, 64)) break;
+          const int sb = c / 4;
+          mbar_expect_tx(&raw_full[rslot], raw_bytes);
+          bulk_g2s_stream(raw_base + (size_t)rslot * raw_bytes,
+                          tiles + ((size_t)grp * sb_count + sb) * (size_t)raw_bytes, raw_bytes, &raw_full[rslot],
+                          policy);
+          if (++rslot == kTcRawSlots) {
+            rslot = 0;
+            rphase ^= 1u;
+          }
+        }
+        if (!waited) {  // the activations are the previous kernel's output
+          griddep_wait();
+          griddep_launch();
+          waited = true;
+        }
+        if (!mbar_wait_backoff(&freeb[slot], phase ^ 1u, err, 64)) break;
+        mbar_expect_tx(&full[slot], btile);
+        bulk_g2s(tc_smem + (size_t)slot * stage_bytes + kATileBytes, xh + (size_t)c * btile, btile, &full[slot]);
+        if (++slot == stages) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!waited) {
+        griddep_wait();
+        griddep_launch();
+      }
+    } else {
+      griddep_wait();
+      griddep_launch();
+    }
+  } else if (warp == kTcWarps) {
     // ---------------- MMA issuer ----------------
+    griddep_wait();
+    griddep_launch();
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(P);
       const uint32_t sbase = smem_addr(tc_smem);
@@ -213,7 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
           umma_f16(tmem, umma_desc_sw128(a + 32 * kk), umma_desc_sw128(b + 32 * kk), idesc,
                    (c > c0 || kk > 0) ? 1u : 0u);
         umma_commit(&freeb[slot]);  // the stage is free once these MMAs have read it
-        if (++slot == kTcStages) {
+        if (++slot == stages) {
           slot = 0;
           phase ^= 1u;
         }
@@ -222,43 +296,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
     }
     __syncwarp();
   } else {
-    // ---------------- dequant / activation warps ----------------
+    // ---------------- dequant warps ----------------
+    griddep_wait();
+    griddep_launch();
     const int rt = warp, g = lane / 4, qq = lane % 4;
-    int slot = 0;
-    uint32_t phase = 0;
+    int slot = 0, rslot = 0;
+    uint32_t phase = 0, rphase = 0;
     for (int c = c0; c < c1; ++c) {
+      if (c == c0 || c % 4 == 0) mbar_wait(&raw_full[rslot], rphase, err);
       // the slot's previous MMAs have read it (a fresh barrier passes the parity-1 wait at once)
       mbar_wait(&freeb[slot], phase ^ 1u, err);
       uint8_t* A = tc_smem + (size_t)slot * stage_bytes;
-      uint8_t* B = A + kATileBytes;
-      const int sb = c / 4, j = c % 4;
-      const uint8_t* tile = tiles + (((size_t)grp * sb_count + sb) * kGemvWarps + rt) * (size_t)tile_bytes;
+      const uint8_t* tile = raw_base + (size_t)rslot * raw_bytes + (size_t)rt * tile_bytes;
       Dq8 r0, r8;
       if (QUANT == CLM_QUANT_Q4_K)
-        dq_q4k(tile, j, g, qq, r0, r8);
+        dq_q4k(tile, c % 4, g, qq, r0, r8);
       else
-        dq_q80(tile, j, g, qq, r0, r8);
+        dq_q80(tile, c % 4, g, qq, r0, r8);
       const int row = rt * 16 + g;
       *reinterpret_cast<uint4*>(A + sw128_off(row, qq)) = r0.lo;
       *reinterpret_cast<uint4*>(A + sw128_off(row, 4 + qq)) = r0.hi;
       *reinterpret_cast<uint4*>(A + sw128_off(row + 8, qq)) = r8.lo;
       *reinterpret_cast<uint4*>(A + sw128_off(row + 8, 4 + qq)) = r8.hi;
-      // activations: P rows x 8 chunks of 8 columns, f32 -> fp16 (rows >= q are zero)
-      for (int i = threadIdx.x; i < P * 8; i += kTcWarps * 32) {
-        const int p = i / 8, ch = i % 8;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (p < q) {
-          const float4* src = reinterpret_cast<const float4*>(x + (size_t)p * K + (size_t)c * kTcKc + 8 * ch);
-          const float4 u0 = __ldg(src), u1 = __ldg(src + 1);
-          v = make_uint4(pack_half2(u0.x, u0.y), pack_half2(u0.z, u0.w), pack_half2(u1.x, u1.y),
-                         pack_half2(u1.z, u1.w));
-        }
-        *reinterpret_cast<uint4*>(B + sw128_off(p, ch)) = v;
-      }
       fence_async_smem();  // generic-proxy writes -> visible to the tensor core's async reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[slot]);
-      if (++slot == kTcStages) {
+      if (c % 4 == 3 || c == c1 - 1) {  // done with this raw superblock
+        if (lane == 0) mbar_arrive(&raw_free[rslot]);
+        if (++rslot == kTcRawSlots) {
+          rslot = 0;
+          rphase ^= 1u;
+        }
+      }
+      if (++slot == stages) {
         slot = 0;
         phase ^= 1u;
       }
@@ -303,31 +373,45 @@ TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count) {
   TcPlan p;
   p.P = ((q + 15) / 16) * 16;
   const int chunks = (int)s.cols / kTcKc;
-  // enough CTAs for the SMs, at least two chunks per CTA
-  int ks = (int)((sm_count + s.ng - 1) / s.ng);
+  // K splits: as many as keep the grid within one wave of CTAs (one per SM), at least two chunks per CTA
+  const int sms = sm_count > 0 ? sm_count : 148;
+  int ks = (int)(s.ng < (uint32_t)sms ? sms / s.ng : 1);
   if (ks > chunks / 2) ks = chunks / 2;
   if (ks < 1) ks = 1;
   p.ksplit = ks;
-  p.smem = 1024 + (size_t)kTcStages * (kATileBytes + (size_t)p.P * 128);
+  const size_t raw = (size_t)kTcRawSlots * kGemvWarps * s.tile_bytes;
+  const size_t stage = kATileBytes + (size_t)p.P * 128;
+  p.stages = kTcMaxStages;
+  while (p.stages > 2 && 1024 + p.stages * stage + raw > 227 * 1024) --p.stages;
+  p.smem = 1024 + (size_t)p.stages * stage + raw;
   p.part_floats = (size_t)ks * q * s.rows;
+  p.xh_bytes = (size_t)p.P * s.cols * 2;
   return p;
 }
 
 int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
-                   float* d_part, int* d_err, cudaStream_t st) {
+                   uint8_t* d_xh, float* d_part, int* d_err, cudaStream_t st) {
   CLM_CHECK(q > 16 && q <= 256, CLM_OUT_OF_RANGE, "tensor-core GEMM covers 17..256 window rows");
-  CLM_CHECK(s.cols % kTcKc == 0 && s.cols % 256 == 0, CLM_INVALID_ARGUMENT, "columns must be a multiple of 256");
+  CLM_CHECK(s.cols % 256 == 0, CLM_INVALID_ARGUMENT, "columns must be a multiple of 256");
   CLM_CHECK(s.quant == CLM_QUANT_Q4_K || s.quant == CLM_QUANT_Q8_0, CLM_UNIMPLEMENTED, "tensor-core GEMM: Q4_K / Q8_0");
   CLM_CHECK(p.smem <= 227 * 1024, CLM_RESOURCE_EXHAUSTED, "tensor-core GEMM: shared memory");
+  CLM_CHECK((reinterpret_cast<uintptr_t>(d_xh) & 15) == 0, CLM_INTERNAL, "activation tiles must be 16-byte aligned");
+  {
+    const uint64_t n = (uint64_t)(s.cols / kTcKc) * p.P * 8;
+    CLM_TRY(launch_pdl(tc_xprep_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,
+                       d_x, q, (int)s.cols, p.P, d_xh));
+  }
   const dim3 grid(s.ng, (unsigned)p.ksplit);
+  float* out = p.ksplit > 1 ? d_part : d_y;
+  const uint8_t* xh = d_xh;
   if (s.quant == CLM_QUANT_Q4_K) {
     CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q4_K>, p.smem));
     CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q4_K>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, d_x, q, (int)s.cols, p.P, p.ksplit, p.ksplit > 1 ? d_part : d_y, s.rows, d_err));
+                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err));
   } else {
     CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q8_0>, p.smem));
     CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q8_0>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, d_x, q, (int)s.cols, p.P, p.ksplit, p.ksplit > 1 ? d_part : d_y, s.rows, d_err));
+                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err));
   }
   if (p.ksplit > 1) {
     const uint64_t n = (uint64_t)q * s.rows;

@@ -8,16 +8,19 @@ namespace clm {
 struct TcPlan {
   int P = 0;              // window rows rounded up to a multiple of 16 (the MMA's N)
   int ksplit = 1;         // K splits (grid y); > 1 sums f32 partials in split order
+  int stages = 0;         // (A tile, B tile) stages in shared memory
   size_t smem = 0;        // dynamic shared memory of one CTA
   size_t part_floats = 0; // f32 partials needed when ksplit > 1
+  size_t xh_bytes = 0;    // fp16 activation tiles (P x cols)
 };
 
 TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count);
 
 // y[p][n] = W[n] . x[p] (x: q x cols f32 row-major, 16-byte aligned; y: q x rows f32) for 17 <= q <= 256 with W
-// in the tile layout of gemv.cuh (Q4_K or Q8_0).  d_part holds p.part_floats floats when p.ksplit > 1; a bounded
-// wait that gives up stores kErrWaitTimeout in *d_err (if not null).
+// in the tile layout of gemv.cuh (Q4_K or Q8_0).  d_xh holds p.xh_bytes (16-byte aligned) for the fp16 activation
+// tiles, d_part p.part_floats floats when p.ksplit > 1; a bounded wait that gives up stores kErrWaitTimeout in
+// *d_err (if not null).
 int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
-                   float* d_part, int* d_err, cudaStream_t st);
+                   uint8_t* d_xh, float* d_part, int* d_err, cudaStream_t st);
 
 }  // namespace clm

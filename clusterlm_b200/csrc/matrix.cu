@@ -121,10 +121,12 @@ int matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x, i
     // wide windows: tcgen05 tensor-core GEMM (gemm_tc.cu)
     CLM_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0, CLM_INVALID_ARGUMENT, "x must be 16-byte aligned");
     const TcPlan tp = gemm_tc_plan(s, q, ctx->sm_count);
+    const size_t xb = (tp.xh_bytes + 255) / 256 * 256;
     void* scratch = nullptr;
-    if (tp.ksplit > 1) CLM_TRY(ctx_scratch(ctx, tp.part_floats * sizeof(float), &scratch));
-    return launch_gemm_tc(s, tp, static_cast<const uint8_t*>(w->data), d_x, q, d_y, static_cast<float*>(scratch),
-                          nullptr, st);
+    CLM_TRY(ctx_scratch(ctx, xb + tp.part_floats * sizeof(float), &scratch));
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    return launch_gemm_tc(s, tp, static_cast<const uint8_t*>(w->data), d_x, q, d_y, base,
+                          reinterpret_cast<float*>(base + xb), nullptr, st);
   }
   const GemvPlan p = gemv_plan(s, q, ctx->sm_count);
   const size_t fb = xfrag_bytes((int)s.cols, p.nt), sb = xsum_bytes((int)s.cols);
