@@ -668,6 +668,21 @@ def run_pipeline(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_micro(args):
+    """One micro-benchmark alone on cuda:0 (a small command for profiler captures); prints its JSON object."""
+    import torch
+
+    from clusterlm_b200.runtime import Context
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    ctx = Context(0)
+    peak, _ = load_peaks()
+    obj = wide_micro(ctx, dev) if args.micro == "wide" else acceptance_micro(ctx, dev, peak, False)
+    ctx.close()
+    print(json.dumps({"micro": args.micro, **obj}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -680,12 +695,16 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
     ap.add_argument("--inflight", type=int, default=0, help="sequences in flight with N > 1 (default N)")
     ap.add_argument("--plan", default="", help="stage plan BEGIN-END@gK,... with N > 1 (default: byte-balanced)")
+    ap.add_argument("--micro", default="", choices=["", "wide", "accept"],
+                    help="run one micro-benchmark alone and print its object (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.micro:
+            run_micro(args)
         elif world > 1:
             run_pipeline(args, world, rank, local)
         else:
