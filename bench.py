@@ -329,9 +329,15 @@ def acceptance_micro(ctx, dev, peak, with_cpu):
 C4_PARENTS = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 6, 7]
 
 
+C4_BATCH = 8
+
+
 def tree_micro(ctx, dev, peak, context):
-    """One 16-node tree verification window (Q8_0 8B shape) through clm_b200_run_tree_window_device, event-timed on
-    the engine's stream; batch 8 is 8 such windows (the weights are streamed once per sequence)."""
+    """C4: 16-node tree verification windows (Q8_0 8B shape, context `context` per sequence).
+    batch 1: one sequence's tree through clm_b200_run_tree_window_device (the GEMV chain), event-timed on the
+    engine's stream.  batch 8: eight sequences' trees in ONE window through clm_b200_run_batch_window (128 rows:
+    tcgen05 GEMMs, each weight matrix read once; per-sequence RoPE/KV and attention), timed by events on the engine
+    stream around the host call (its launches are issued directly, so the time includes their issue)."""
     import numpy as np
     import torch
 
@@ -339,7 +345,8 @@ def tree_micro(ctx, dev, peak, context):
 
     geo = dataclasses.replace(LLAMA3_8B, quant="q8_0")
     q = len(C4_PARENTS)
-    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, context + 64, 16, 1)
+    wmax = C4_BATCH * q
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, context + 64, wmax, C4_BATCH)
     eng.generate_weights(seed=SEED, stddev=0.02)
     eng.prepare()
     eng.open_session(1)
@@ -362,17 +369,57 @@ def tree_micro(ctx, dev, peak, context):
         if i >= 3:
             times.append(s0.elapsed_time(s1) / 1e3)
     sec = statistics.median(times)
-    eng.close_session(1)
+    # batch 8: sessions 2..8 prefilled in wmax-row windows (device tokens), then one 128-row window per call
+    pre_out = torch.empty((wmax, geo.vocab), dtype=torch.float32, device=dev)
+    for b in range(2, C4_BATCH + 1):
+        eng.open_session(b)
+        prompt = torch.from_numpy(rng.integers(0, geo.vocab, context).astype(np.int32)).to(dev)
+        for off in range(0, context, wmax):
+            n = min(wmax, context - off)
+            eng.run_window_device(b, off, prompt[off:off + n], pre_out[:n], stream.cuda_stream)
+            eng.commit(b, n)
+    ids = list(range(1, C4_BATCH + 1))
+    bases = [eng.position(b) for b in ids]
+    btoks = rng.integers(0, geo.vocab, (C4_BATCH, q)).astype(np.int32)
+    btimes, bwall = [], []
+    for i in range(6):
+        torch.cuda.synchronize(dev)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        s0.record(stream)
+        eng.run_batch_window(ids, bases, btoks, C4_PARENTS, logits=False)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        t1 = time.perf_counter()
+        for b in ids:
+            eng.abort(b)
+        if i >= 2:
+            btimes.append(s0.elapsed_time(s1) / 1e3)
+            bwall.append(t1 - t0)
+    bsec = statistics.median(btimes)
+    for b in ids:
+        eng.close_session(b)
     eng.close()
     H, qd, kvd, F, V = geo.hidden, geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim, geo.ffn, geo.vocab
-    weights = (geo.n_layers * (qd * H + 2 * kvd * H + H * qd + 3 * F * H) + V * H) * 34 // 32
+    params = geo.n_layers * (qd * H + 2 * kvd * H + H * qd + 3 * F * H) + V * H
+    weights = params * 34 // 32
     kv = geo.n_layers * 2 * context * kvd * 2
     algo = weights + kv
-    return {"config": f"8B-shape Q8_0, 16-node draft tree (parents {C4_PARENTS}), context {context}, batch 1",
+    balgo = weights + C4_BATCH * kv
+    bflops = 2.0 * C4_BATCH * q * params
+    tpeak, tkind = load_tensor_peak()
+    return {"config": f"8B-shape Q8_0, 16-node draft tree (parents {C4_PARENTS}), context {context}",
             "ms_per_window": sec * 1e3, "windows_per_s": 1.0 / sec,
-            "batch8_ms": 8 * sec * 1e3,
             "roofline": {"bound": "hbm", "algorithmic_bytes": algo, "weight_bytes": weights, "kv_bytes": kv,
-                         "achieved": algo / sec / 1e9, "peak": peak, "unit": "GB/s", "frac": algo / sec / 1e9 / peak}}
+                         "achieved": algo / sec / 1e9, "peak": peak, "unit": "GB/s", "frac": algo / sec / 1e9 / peak},
+            "batch8": {"config": f"{C4_BATCH} sequences x {q}-node trees = {C4_BATCH * q} rows in one window "
+                                 "(clm_b200_run_batch_window), no logits read back",
+                       "ms_per_window": bsec * 1e3, "host_ms_per_call": statistics.median(bwall) * 1e3,
+                       "tree_nodes_per_s": C4_BATCH * q / bsec,
+                       "roofline": {"bound": "hbm", "algorithmic_bytes": balgo, "achieved": balgo / bsec / 1e9,
+                                    "peak": peak, "unit": "GB/s", "frac": balgo / bsec / 1e9 / peak},
+                       "tensor": {"gemm_flops": bflops, "achieved": bflops / bsec / 1e12, "peak": tpeak,
+                                  "unit": "TFLOP/s", "frac": bflops / bsec / 1e12 / tpeak, "peak_kind": tkind}}}
 
 
 def load_tensor_peak():
@@ -428,6 +475,53 @@ def wide_micro(ctx, dev):
                          "weight_gbs": params * 34 / 32 / sec / 1e9}}
 
 
+PREFILL_CHUNK = 256
+
+
+def prefill_micro(eng, geo, dev, stream, context, rng):
+    """Prefill of a `context`-token prompt in 256-row windows (the tcgen05 GEMM path of the engine) on session 2 of
+    the bench engine: each window is event-timed on the engine stream and committed.  Tensor roofline over the
+    GEMM flops (every window row through every layer matrix and the head); the time also holds the attention and
+    the elementwise steps."""
+    import numpy as np
+    import torch
+
+    ch = PREFILL_CHUNK
+    n = context - context % ch
+    prompt = torch.from_numpy(rng.integers(0, geo.vocab, max(n, ch)).astype(np.int32)).to(dev)
+    out = torch.empty((ch, geo.vocab), dtype=torch.float32, device=dev)
+    eng.open_session(2)
+    for _ in range(3):  # eager, graph capture, replay
+        eng.run_window_device(2, 0, prompt[:ch], out, stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+        eng.abort(2)
+    times = []
+    for off in range(0, n, ch):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        eng.run_window_device(2, off, prompt[off:off + ch], out, stream.cuda_stream)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        eng.commit(2, ch)
+        times.append(s0.elapsed_time(s1) / 1e3)
+    eng.close_session(2)
+    if not times:
+        return None
+    sec = sum(times)
+    H, F, V = geo.hidden, geo.ffn, geo.vocab
+    qd, kvd = geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim
+    params = geo.n_layers * ((qd + 2 * kvd) * H + H * qd + 2 * F * H + H * F) + V * H
+    flops = 2.0 * n * params
+    peak, kind = load_tensor_peak()
+    tf = flops / sec / 1e12
+    return {"config": f"{n}-token prompt in {ch}-row windows through the engine (tcgen05 GEMMs, paged fp16 KV), "
+                      f"{geo.quant} {geo.n_layers}-layer 8B shape, logits for every row",
+            "tok_s": n / sec, "ms_per_window": 1e3 * sec / len(times),
+            "ms_first_window": 1e3 * times[0], "ms_last_window": 1e3 * times[-1],
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_kind": kind, "gemm_flops": flops}}
+
+
 def run_b200(args, world, rank, local):
     import numpy as np
     import torch
@@ -441,7 +535,10 @@ def run_b200(args, world, rank, local):
     context = args.context
     ctx = Context(local)
     max_ctx = context + (args.warmup + args.steps + 8) * (Q + 1) + 64
-    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, 16, 1)
+    # windows of up to 256 rows: the prompt is prefilled in 256-row windows on the tensor-core path (the profile
+    # case keeps 16-row prefill windows, so its launch list matches the recorded ncu skip counts)
+    wmax = 16 if profile_case(args) else PREFILL_CHUNK
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, wmax, 2)
     eng.generate_weights(seed=SEED, stddev=0.02)
     eng.prepare()
     eng.open_session(1)
@@ -506,6 +603,7 @@ def run_b200(args, world, rank, local):
     peak, peak_kind = load_peaks()
     achieved = total_b / window_s / 1e9
     eng.close_session(1)
+    prefill = prefill_micro(eng, geo, dev, stream, context, rng) if (world == 1 and wmax > 16) else None
     eng.close()
     micro = acceptance_micro(ctx, dev, peak, not args.no_cpu) if (world == 1 and not profile_case(args)) else None
     tree = tree_micro(ctx, dev, peak, context) if (world == 1 and not profile_case(args)) else None
@@ -549,6 +647,8 @@ def run_b200(args, world, rank, local):
         line["tree_window"] = tree
     if wide:
         line["wide_window"] = wide
+    if prefill:
+        line["prefill"] = prefill
     print(json.dumps(line), flush=True)
 
 

@@ -25,6 +25,8 @@
 #include "matrix.cuh"
 #include "pdl.cuh"
 #include "sampling.cuh"
+#include "gemm_tc.cuh"
+#include "wide.cuh"
 
 namespace clm {
 
@@ -53,6 +55,7 @@ struct Session {
   bool pos_stale = false;     // device rounds ran since the last read of d_state->pos
   uint32_t outstanding = 0;  // q of the outstanding window, 0 = none
   bool tree = false;         // the outstanding window is a tree (commit with clm_b200_commit_path)
+  std::vector<int32_t> tree_parents;  // the outstanding tree's parents when given by the host (else in e->parents)
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;  // (kind, q, flag) -> executable graph
   std::map<std::tuple<int, int, int>, int> seen;
   std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
@@ -234,6 +237,13 @@ struct LlamaEngine : clm_b200_engine {
   int mk_attn_maxseg = 0;
   unsigned* mk_bar = nullptr;
   float* mk_attn_part = nullptr;
+  // wide windows (17..max_window rows when max_window > 16): tensor-core GEMMs (gemm_tc.cu) between the elementwise
+  // steps of wide.cu
+  float* wy = nullptr;       // GEMM outputs [W][largest row count of a layer matrix]
+  float* wpart = nullptr;    // split-K partials of the tensor-core GEMMs
+  size_t wpart_floats = 0;
+  float* wattn = nullptr;    // attention outputs [W][qd]
+  uint8_t* wxh = nullptr;    // fp16 activation tiles of the next GEMM
   float* logits = nullptr;
   int32_t* tokens = nullptr;
   float* bin = nullptr;
@@ -483,8 +493,66 @@ struct LlamaEngine : clm_b200_engine {
     return launch_window_mk(P, d.quant, nt, mk_grid[nt - 1], st);
   }
 
+  // ---- one tensor-core GEMM of a wide window: y[p] = W . x[p] over the tiles in wxh
+  int gemm_wide(const Gemv& g, int q, float* y, cudaStream_t st) {
+    const TcPlan p = gemm_tc_plan(g.m->shape, q, ctx->sm_count);
+    CLM_CHECK(p.ksplit == 1 || p.part_floats <= wpart_floats, CLM_INTERNAL, "wide window: split-K partials");
+    return launch_gemm_tc_tiles(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), wxh, q, y, wpart, bad, st);
+  }
+
+  // ---- a wide window (17..256 rows: prefill chunks, large trees, or the windows of several sessions stacked):
+  // per layer the QKV, W_o, gate|up and down GEMMs on tensor cores over all rows, each followed by its
+  // elementwise step (RoPE + KV append, residual + rmsnorm, SwiGLU) that writes the next GEMM's fp16 tiles; the
+  // RoPE/KV step and the attention run per session segment (its own position, pages and cache rows)
+  struct WideSeg {
+    Session* s;
+    int row0, q;
+  };
+  int enqueue_window_wide(Session& s, int q, const int32_t* d_tok, const int32_t* parent, cudaStream_t st) {
+    const WideSeg seg{&s, 0, q};
+    return enqueue_window_wide(&seg, 1, q, d_tok, parent, st);
+  }
+  int enqueue_window_wide(const WideSeg* segs, int nseg, int q, const int32_t* d_tok, const int32_t* parent,
+                          cudaStream_t st) {
+    const int P = (q + 15) / 16 * 16;
+    const size_t qkv_rows = (size_t)d.qd() + 2 * d.kvd();
+    if (has_tokens) {
+      CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(256), 0, st, d_tok, q, (int)d.V, tokens, bad));
+      CLM_TRY(launch_embed(embd, d.quant, tokens, q, d.H, h, st));
+    } else {
+      CLM_TRY(launch_unpack_boundary(bin, q, d.H, h, st));
+    }
+    const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
+    CLM_TRY(launch_wide_norm_prep(nullptr, h, q, d.H, w0, d.eps, P, wxh, st));
+    for (size_t li = 0; li < layers.size(); ++li) {
+      const Layer& L = layers[li];
+      CLM_TRY(gemm_wide(L.qkv, q, wy, st));
+      for (int k = 0; k < nseg; ++k) {
+        const WideSeg& g = segs[k];
+        const long long* pos = &g.s->d_state->pos;
+        __half* qs = q16 + (size_t)g.row0 * d.qd();
+        CLM_TRY(launch_wide_rope_kv(wy + (size_t)g.row0 * qkv_rows, g.q, d, rope, pos, g.s->d_pages, parent, qs,
+                                    kpool[li], vpool[li], st));
+        CLM_TRY(launch_attention(qs, kpool[li], vpool[li], g.s->d_pages, pos, parent, g.q, d, max_pages, attn_part,
+                                 acount, 2, hi_scale(), xb.frag, xb.sum, bad, nullptr, 0, ctx->sm_count, st,
+                                 wattn + (size_t)g.row0 * d.qd()));
+      }
+      CLM_TRY(launch_tc_xprep(wattn, q, d.qd(), P, wxh, st));
+      CLM_TRY(gemm_wide(L.o, q, wy, st));
+      CLM_TRY(launch_wide_norm_prep(wy, h, q, d.H, L.ffn_norm, d.eps, P, wxh, st));
+      CLM_TRY(gemm_wide(L.gu, q, wy, st));
+      CLM_TRY(launch_wide_swiglu_prep(wy, q, d.F, P, wxh, st));
+      CLM_TRY(gemm_wide(L.down, q, wy, st));
+      const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
+      CLM_TRY(launch_wide_norm_prep(wy, h, q, d.H, wnext, d.eps, P, wxh, st));
+    }
+    if (has_head) return gemm_wide(head, q, logits, st);
+    return launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st);
+  }
+
   // ---- a full window: input (tokens or records) -> layers -> logits or records
   int enqueue_window(Session& s, int q, const int32_t* d_tok, cudaStream_t st, const int32_t* parent = nullptr) {
+    if (q > 16) return enqueue_window_wide(s, q, d_tok, parent, st);
     const int nt = q <= 8 ? 1 : 2;
     if (has_tokens) {
       CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(64), 0, st, d_tok, q, (int)d.V, tokens, bad));
@@ -745,7 +813,7 @@ int llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_
   CLM_CHECK(spec->max_context > 0 && spec->max_window > 0 && spec->max_sessions > 0 &&
                 spec->max_window <= spec->max_context,
             CLM_INVALID_ARGUMENT, "domain spec needs max_context >= max_window >= 1 and max_sessions >= 1");
-  CLM_CHECK(spec->max_window <= 16, CLM_OUT_OF_RANGE, "max_window must be <= 16");
+  CLM_CHECK(spec->max_window <= 256, CLM_OUT_OF_RANGE, "max_window must be <= 256");
   if (spec->role == CLM_ROLE_PREFIX || spec->role == CLM_ROLE_WHOLE)
     CLM_CHECK(spec->layer_begin == 0, CLM_INVALID_ARGUMENT, "prefix domain must start at layer 0");
   if (spec->role == CLM_ROLE_TAIL || spec->role == CLM_ROLE_WHOLE)
@@ -862,6 +930,7 @@ int llama_prepare(LlamaEngine* e) {
   e->pages_total = (int)e->spec.max_sessions * e->max_pages;
   const size_t page_bytes = (size_t)d.nkv * kPageTokens * d.hd * sizeof(__half);
   const int mtiles = (W * (d.nh / d.nkv) + 15) / 16;
+  const int mtiles_q16 = (std::min(W, 16) * (d.nh / d.nkv) + 15) / 16;  // windows on the GEMV chain
   const int maxcols = std::max(std::max(d.H, d.F), d.qd());
   CLM_TRY(e->alloc_t(&e->h, (size_t)W * d.H));
   CLM_TRY(e->alloc_t(&e->part, part_floats));
@@ -879,7 +948,35 @@ int llama_prepare(LlamaEngine* e) {
   }
   CLM_TRY(e->ones(&e->ones_h, d.H));
   CLM_TRY(e->alloc_t(&e->q16, (size_t)W * d.qd()));
-  CLM_TRY(e->alloc_t(&e->attn_part, (size_t)mtiles * d.nkv * e->max_pages * attn_partial_floats(d.hd)));
+  // split partials, one per CTA: a launch has (m-tiles x kv heads) x splits CTAs with splits <= max_pages, and
+  // more than one split only while that product stays within the SM count
+  {
+    const size_t narrow = (size_t)mtiles_q16 * d.nkv * e->max_pages;
+    const size_t wide = std::max((size_t)e->ctx->sm_count, (size_t)mtiles * d.nkv);
+    CLM_TRY(e->alloc_t(&e->attn_part, std::max(narrow, wide) * attn_partial_floats(d.hd)));
+  }
+  if (W > 16) {
+    size_t rows = (size_t)d.H, part_max = 0;
+    auto wide_account = [&](const Gemv& g) {
+      if (!g.m) return;
+      rows = std::max<size_t>(rows, g.m->shape.rows);
+      const TcPlan p = gemm_tc_plan(g.m->shape, W, e->ctx->sm_count);
+      if (p.ksplit > 1) part_max = std::max(part_max, p.part_floats);
+    };
+    for (auto& L : e->layers) {
+      wide_account(L.qkv);
+      wide_account(L.o);
+      wide_account(L.gu);
+      wide_account(L.down);
+    }
+    wide_account(e->head);
+    const size_t P = (size_t)(W + 15) / 16 * 16;
+    CLM_TRY(e->alloc_t(&e->wy, (size_t)W * rows));
+    e->wpart_floats = part_max;
+    if (part_max) CLM_TRY(e->alloc_t(&e->wpart, part_max));
+    CLM_TRY(e->alloc_t(&e->wattn, (size_t)W * d.qd()));
+    CLM_TRY(e->alloc((void**)&e->wxh, P * maxcols * sizeof(__half)));
+  }
   {
     const size_t n = (size_t)e->spec.max_context * (d.hd / 2);
     CLM_TRY(e->alloc_t(&e->rope, n));
@@ -1086,6 +1183,7 @@ int llama_run_tree_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q
   }
   s->outstanding = q;
   s->tree = true;
+  s->tree_parents.clear();  // validated on the device: commit_path reads them there
   return CLM_OK;
 }
 
@@ -1128,6 +1226,54 @@ static int run_window_host(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t 
   CLM_CUDA(cudaStreamSynchronize(st));
   s->outstanding = q;
   s->tree = h_parents != nullptr;
+  if (h_parents)
+    s->tree_parents.assign(h_parents, h_parents + q);
+  else
+    s->tree_parents.clear();
+  return CLM_OK;
+}
+
+int llama_run_batch(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint64_t* bases, uint32_t q,
+                    const int32_t* h_parents, const int32_t* h_tokens, float* h_logits) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(e->spec.role == CLM_ROLE_WHOLE, CLM_FAILED_PRECONDITION, "batched windows need a whole-model engine");
+  CLM_CHECK(ids != nullptr && bases != nullptr && h_tokens != nullptr && n >= 1 && q >= 1, CLM_INVALID_ARGUMENT,
+            "batched window: null or empty argument");
+  CLM_CHECK((uint64_t)n * q <= e->spec.max_window, CLM_RESOURCE_EXHAUSTED, "batched window exceeds max_window");
+  CLM_CHECK(q <= 16, CLM_OUT_OF_RANGE, "batched window: at most 16 rows per session");
+  const uint32_t Q = n * q;
+  CLM_CHECK(Q > 16, CLM_OUT_OF_RANGE, "batched window: more than 16 rows in all (fewer: one window per session)");
+  if (h_parents != nullptr)
+    for (uint32_t i = 0; i < q; ++i)
+      CLM_CHECK(h_parents[i] >= -1 && h_parents[i] < (int32_t)i, CLM_INVALID_ARGUMENT,
+                "tree window: parent[i] must be -1 or an earlier node");
+  for (uint32_t i = 0; i < Q; ++i)
+    CLM_CHECK(h_tokens[i] >= 0 && h_tokens[i] < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+  cudaStream_t st = e->ctx->stream;
+  std::vector<LlamaEngine::WideSeg> segs;
+  for (uint32_t b = 0; b < n; ++b) {
+    for (uint32_t c = 0; c < b; ++c) CLM_CHECK(ids[c] != ids[b], CLM_INVALID_ARGUMENT, "a session appears twice");
+    Session* s = nullptr;
+    CLM_TRY(run_window_common(e, ids[b], bases[b], q, st, &s));
+    segs.push_back({s, (int)(b * q), (int)q});
+  }
+  CLM_CUDA(cudaMemcpyAsync(e->win, h_tokens, Q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  if (h_parents != nullptr)
+    CLM_CUDA(cudaMemcpyAsync(e->parents, h_parents, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  // launched directly (the session set changes from call to call; no graph is kept)
+  CLM_TRY(e->enqueue_window_wide(segs.data(), (int)n, (int)Q, e->win, h_parents ? e->parents : nullptr, st));
+  if (h_logits)
+    CLM_CUDA(cudaMemcpyAsync(h_logits, e->logits, (size_t)Q * e->d.V * sizeof(float), cudaMemcpyDeviceToHost, st));
+  CLM_CUDA(cudaStreamSynchronize(st));
+  for (auto& g : segs) {
+    g.s->outstanding = q;
+    g.s->tree = h_parents != nullptr;
+    if (h_parents)
+      g.s->tree_parents.assign(h_parents, h_parents + q);
+    else
+      g.s->tree_parents.clear();
+  }
   return CLM_OK;
 }
 
@@ -1149,7 +1295,9 @@ int llama_commit_path(LlamaEngine* e, uint64_t id, const int32_t* h_path, uint32
   CLM_CHECK(s->outstanding > 0, CLM_FAILED_PRECONDITION, "no outstanding window");
   CLM_CHECK(h_path != nullptr && n >= 1 && n <= s->outstanding, CLM_INVALID_ARGUMENT, "path must hold 1..q nodes");
   std::vector<int32_t> parents(s->outstanding, -1);
-  if (s->tree)
+  if (s->tree && s->tree_parents.size() == s->outstanding)
+    parents = s->tree_parents;
+  else if (s->tree)
     CLM_CUDA(cudaMemcpy(parents.data(), e->parents, s->outstanding * sizeof(int32_t), cudaMemcpyDeviceToHost));
   else
     for (uint32_t i = 0; i < s->outstanding; ++i) parents[i] = (int32_t)i - 1;
@@ -1177,6 +1325,7 @@ int llama_commit_path(LlamaEngine* e, uint64_t id, const int32_t* h_path, uint32
     }
     CLM_CUDA(cudaMemcpyAsync(e->parents, h_path, n * sizeof(int32_t), cudaMemcpyHostToDevice, st));
     const size_t smem = (size_t)n * 2 * e->d.hd * sizeof(__half);
+    CLM_TRY(ensure_smem(kv_compact_kernel, smem));
     kv_compact_kernel<<<dim3((unsigned)e->layers.size(), (unsigned)e->d.nkv), 256, smem, st>>>(
         e->d_kpools, e->d_vpools, s->d_pages, &s->d_state->pos, e->parents, (int)n, e->d.nkv, e->d.hd);
     CLM_LAUNCHED("kv_compact_kernel");

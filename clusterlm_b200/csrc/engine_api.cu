@@ -156,6 +156,13 @@ int clm_b200_run_tree_window_device(clm_b200_engine* e, uint64_t id, uint64_t ba
   return llama_run_tree_device(llama(e), id, base, positions, d_parents, d_tokens, d_in, d_out, d_logits, stream);
 }
 
+int clm_b200_run_batch_window(clm_b200_engine* e, uint32_t n_sessions, const uint64_t* sessions, const uint64_t* bases,
+                              uint32_t positions, const int32_t* h_parents, const int32_t* h_tokens, float* h_logits) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "batched windows are implemented for the Llama family");
+  return llama_run_batch(llama(e), n_sessions, sessions, bases, positions, h_parents, h_tokens, h_logits);
+}
+
 static int llama_only(clm_b200_engine* e) {
   CLM_TRY(enter(e));
   CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "stage pipelines are implemented for the Llama family");

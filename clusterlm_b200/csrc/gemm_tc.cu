@@ -44,9 +44,7 @@ constexpr int kTcKc = 64;                     // columns per chunk (one 128-byte
 constexpr uint32_t kATileBytes = 128 * kTcKc * 2;  // 16 KB
 
 // Byte offset of element chunk (row r, 16-byte chunk c) in a K-major SW128 tile.
-__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) { return tc_tile_off(r, c); }
 
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart (SBO), LBO unused (1).
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -389,18 +387,30 @@ TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count) {
   return p;
 }
 
+int launch_tc_xprep(const float* d_x, int q, int K, int P, uint8_t* d_xh, cudaStream_t st) {
+  CLM_CHECK(K % kTcKc == 0 && q >= 1 && q <= P && P % 16 == 0, CLM_INVALID_ARGUMENT, "activation tile shape");
+  CLM_CHECK((reinterpret_cast<uintptr_t>(d_x) & 15) == 0 && (reinterpret_cast<uintptr_t>(d_xh) & 15) == 0,
+            CLM_INTERNAL, "activation rows and tiles must be 16-byte aligned");
+  const uint64_t n = (uint64_t)(K / kTcKc) * P * 8;
+  return launch_pdl(tc_xprep_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,
+                    d_x, q, K, P, d_xh);
+}
+
 int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
                    uint8_t* d_xh, float* d_part, int* d_err, cudaStream_t st) {
-  CLM_CHECK(q > 16 && q <= 256, CLM_OUT_OF_RANGE, "tensor-core GEMM covers 17..256 window rows");
+  CLM_TRY(launch_tc_xprep(d_x, q, (int)s.cols, p.P, d_xh, st));
+  return launch_gemm_tc_tiles(s, p, d_tiles, d_xh, q, d_y, d_part, d_err, st);
+}
+
+int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const uint8_t* d_xh, int q,
+                         float* d_y, float* d_part, int* d_err, cudaStream_t st) {
+  CLM_CHECK(q > 16 && q <= 256 && p.P == ((q + 15) / 16) * 16, CLM_OUT_OF_RANGE,
+            "tensor-core GEMM covers 17..256 window rows");
   CLM_CHECK(s.cols % 256 == 0, CLM_INVALID_ARGUMENT, "columns must be a multiple of 256");
   CLM_CHECK(s.quant == CLM_QUANT_Q4_K || s.quant == CLM_QUANT_Q8_0, CLM_UNIMPLEMENTED, "tensor-core GEMM: Q4_K / Q8_0");
   CLM_CHECK(p.smem <= 227 * 1024, CLM_RESOURCE_EXHAUSTED, "tensor-core GEMM: shared memory");
   CLM_CHECK((reinterpret_cast<uintptr_t>(d_xh) & 15) == 0, CLM_INTERNAL, "activation tiles must be 16-byte aligned");
-  {
-    const uint64_t n = (uint64_t)(s.cols / kTcKc) * p.P * 8;
-    CLM_TRY(launch_pdl(tc_xprep_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,
-                       d_x, q, (int)s.cols, p.P, d_xh));
-  }
+  CLM_CHECK(p.ksplit == 1 || d_part != nullptr, CLM_INTERNAL, "split-K partials need a buffer");
   const dim3 grid(s.ng, (unsigned)p.ksplit);
   float* out = p.ksplit > 1 ? d_part : d_y;
   const uint8_t* xh = d_xh;

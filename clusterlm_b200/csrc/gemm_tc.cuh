@@ -23,4 +23,17 @@ TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count);
 int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
                    uint8_t* d_xh, float* d_part, int* d_err, cudaStream_t st);
 
+// The GEMM alone, over activation tiles already in d_xh (written by launch_tc_xprep or a fused producer).
+int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const uint8_t* d_xh, int q,
+                         float* d_y, float* d_part, int* d_err, cudaStream_t st);
+
+// Activation tiles of the GEMM: x (q x K f32, row-major) -> fp16, K-major 128-byte-swizzled tiles of 64 columns,
+// tile c at d_xh + c * P * 128 with row p's 16-byte chunk j at tc_tile_off(p, j); rows q..P-1 are zero.
+int launch_tc_xprep(const float* d_x, int q, int K, int P, uint8_t* d_xh, cudaStream_t st);
+
+// Byte offset of row r's 16-byte chunk c (8 fp16 columns) inside one 64-column activation tile.
+__host__ __device__ __forceinline__ uint32_t tc_tile_off(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
 }  // namespace clm

@@ -74,7 +74,7 @@ __device__ __forceinline__ bool visible(long long pos, long long base, int i, co
   if (pos < base) return true;
   const long long rel = pos - base;
   if (!parent) return rel <= i;
-  for (int a = i, guard = 0; a >= 0 && guard < 64; a = parent[a], ++guard)
+  for (int a = i, guard = 0; a >= 0 && guard < 256; a = parent[a], ++guard)
     if (a == rel) return true;
   return false;
 }
@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const int32_t* __restrict__ pages, const long long* __restrict__ d_pos, const int32_t* __restrict__ parent, int q,
     int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
     float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err,
-    const uint8_t* __restrict__ pf, unsigned long long pf_bytes) {
+    const uint8_t* __restrict__ pf, unsigned long long pf_bytes, float* __restrict__ out_f32) {
   static_assert(HD == 128, "head_dim 128 layout");
   static_assert(kAttnWarps == 2 * kAttnPages, "two warps per page buffer");
   constexpr int RW = kAttnRowFloats;  // one partial row: O[HD], m, l, padding (16-byte aligned rows)
@@ -377,6 +377,11 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
       }
     }
     s_out[li][c] = L > 0.0f ? a / L : 0.0f;
+    if (out_f32 != nullptr) {  // f32 rows [q][nh * HD] (the wide window's W_o input)
+      const int i = (mt * 16 + r) / group, head = kvh * group + (mt * 16 + r) % group;
+      if (live && i < q) out_f32[(size_t)i * qd + head * HD + 16 * cg + c] = s_out[li][c];
+      continue;
+    }
     __syncthreads();
     if (live && c == 0) {
       // query vector r = window row i, head kvh*group + r%group; 16 columns 16cg.. of that head
@@ -391,22 +396,24 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum, int* d_err,
-                     const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count, cudaStream_t st) {
+                     const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count, cudaStream_t st,
+                     float* d_out_f32) {
   CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
+  CLM_CHECK(d_out_f32 != nullptr || q <= 16, CLM_OUT_OF_RANGE, "W_o input fragments cover at most 16 window rows");
   const int group = d.nh / d.nkv;
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
   const size_t smem = attn_smem_bytes(128);
-  // splits per (kv head, m-tile): enough for the pages, no more CTAs than SMs (the splits wait for each other)
+  // splits per (kv head, m-tile): enough for the pages, no more CTAs than SMs (the splits wait for each other).
+  // With more (kv head, m-tile) pairs than SMs there is one split each, whose wait is on its own arrival only.
   const int heads = d.nkv * mtiles;
-  CLM_CHECK(heads <= sm_count, CLM_RESOURCE_EXHAUSTED, "attention: more (kv head, m-tile) pairs than SMs");
   int splits = (max_pages + kAttnPages - 1) / kAttnPages;
   if (splits > sm_count / heads) splits = sm_count / heads;
   if (splits < 1) splits = 1;
   CLM_TRY(ensure_smem(attention_kernel<128>, smem));
   return launch_pdl(attention_kernel<128>, dim3(d.nkv, splits, mtiles), dim3(32 * kAttnWarps), smem, st, d_q, d_k,
                     d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2, max_pages, d_part, d_counters, nt_out,
-                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes);
+                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes, d_out_f32);
 }
 
 // ---------------------------------------------------------------------------------------------------

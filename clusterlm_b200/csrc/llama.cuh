@@ -39,12 +39,14 @@ int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int 
 // writes W_o's input fragments (out_frag / out_sum, qd columns).  S is chosen so that the grid fits the SM count.
 // d_part holds mtiles*nkv*max_pages*attn_partial_floats(hd) floats; d_counters 2*mtiles*nkv zeroed ints (left zero);
 // a bounded wait that gives up stores kErrWaitTimeout in *d_err.  [d_prefetch, d_prefetch + prefetch_bytes) (the next
-// kernel's weights, or null) is prefetched into L2, split over the CTAs.
+// kernel's weights, or null) is prefetched into L2, split over the CTAs.  With d_out_f32 (wide windows, any q) the
+// outputs go to f32 rows d_out_f32[q][qd] instead of the fragments; when the (kv head, m-tile) pairs outnumber the
+// SMs each pair has one split.
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
                      int* d_err, const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count,
-                     cudaStream_t st);
+                     cudaStream_t st, float* d_out_f32 = nullptr);
 // Copies h[p][0:H] of rows into the boundary records out[p] = {S = h, P = 0, g = 1} (hc = 1).
 int launch_pack_boundary(const float* d_h, const float* d_part, int nsplit, int q, int H, float* d_out,
                          cudaStream_t st);

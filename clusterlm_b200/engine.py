@@ -194,6 +194,20 @@ class Engine:
              None if has_head else out.ctypes.data_as(_vp), out.ctypes.data_as(_vp) if has_head else None)
         return out
 
+    def run_batch_window(self, sessions, bases, tokens, parents=None, logits=True):
+        """One window over several sessions (clm_b200_run_batch_window): tokens (n, q), shared tree parents (q,) or
+        None for linear windows; returns logits (n, q, vocab), or None with logits=False (no device-to-host copy)."""
+        ids = np.ascontiguousarray(sessions, dtype=np.uint64)
+        bs = np.ascontiguousarray(bases, dtype=np.uint64)
+        tokens = _i32(tokens)
+        n, q = tokens.shape
+        out = np.zeros((n, q, self.vocab), np.float32) if logits else None
+        par = None if parents is None else _i32(parents)
+        call("clm_b200_run_batch_window", self.h, n, ids.ctypes.data_as(_vp), bs.ctypes.data_as(_vp), q,
+             None if par is None else par.ctypes.data_as(_vp), tokens.ctypes.data_as(_vp),
+             None if out is None else out.ctypes.data_as(_vp))
+        return out
+
     def run_tree_window_device(self, session: int, base: int, d_parents, d_tokens=None, d_out=None, stream=None,
                                d_records=None):
         """Device-buffer tree window (torch CUDA tensors): parents, tokens or records in; logits or records out."""

@@ -195,7 +195,8 @@ CLM_API int clm_b200_engine_info(const clm_b200_engine* e, uint64_t* weight_byte
                                  uint32_t* floats_per_position);
 CLM_API int clm_b200_session_open(clm_b200_engine* e, uint64_t session);
 CLM_API int clm_b200_session_close(clm_b200_engine* e, uint64_t session);
-/* One verification window of `positions` rows at committed position `base`.
+/* One verification window of `positions` rows (1..max_window; max_window <= 256: windows of more than 16 rows,
+ * prefill chunks and large trees, run on the tensor-core path) at committed position `base`.
  *   prefix / whole: h_tokens[positions]; middle / tail: h_in[positions][floats_per_position]
  *   prefix / middle: h_out[positions][floats_per_position]; tail / whole: h_logits[positions][vocab]
  * The window's state changes (KV rows) are tentative until clm_b200_commit. */
@@ -223,6 +224,16 @@ CLM_API int clm_b200_run_tree_window_device(clm_b200_engine* e, uint64_t session
  * rows move to slots base..base+n-1 and the committed position advances by n (commit_window's keep-prefix rule
  * for a tree). */
 CLM_API int clm_b200_commit_path(clm_b200_engine* e, uint64_t session, const int32_t* h_path, uint32_t n);
+/* One window over several sessions at once (no reference counterpart: the reference runs one window per
+ * ExecutionDomain call, reference_domain.cpp:376-445): session sessions[b] verifies `positions` (<= 16) rows at
+ * its committed position bases[b], as a tree with the shared parent array h_parents (see
+ * clm_b200_run_tree_window) or linearly when h_parents is null.  Every weight matrix is read once for all
+ * n_sessions * positions rows (17..max_window rows, the tensor-core path).  h_tokens[n_sessions][positions];
+ * h_logits[n_sessions][positions][vocab] (optional).  Whole-model engines.  Each session then commits with
+ * clm_b200_commit_path / clm_b200_commit (linear) or drops its window with clm_b200_abort. */
+CLM_API int clm_b200_run_batch_window(clm_b200_engine* e, uint32_t n_sessions, const uint64_t* sessions,
+                                      const uint64_t* bases, uint32_t positions, const int32_t* h_parents,
+                                      const int32_t* h_tokens, float* h_logits);
 /* Drops the outstanding window (abort_window, reference_domain.cpp:319-329). */
 CLM_API int clm_b200_abort(clm_b200_engine* e, uint64_t session);
 CLM_API int clm_b200_session_position(const clm_b200_engine* e, uint64_t session, uint64_t* committed);
