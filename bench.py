@@ -17,6 +17,9 @@ cpu_baseline the oracle's refmath-order CPU restatement on this host's cores, a 
              layer at context 4096 + the LM head + one MTP step, q = 4) extrapolated to a round
 wide_window  128 window rows (8 sequences x 16 tree nodes) through the tcgen05 tensor-core GEMM over one 8B layer's
              Q8_0 matrices: TFLOP/s against the measured bf16 tensor peak
+prefill      a 4096-token prompt in 256-row windows through the engine (tcgen05 path): tokens/s, GEMM TFLOP/s
+tree_window  C4: a 16-node draft tree at context 4096 in Q8_0, batch 1 (GEMV chain) and batch 8 (eight sessions'
+             trees in one 128-row window, clm_b200_run_batch_window): window time and HBM / tensor rooflines
 With N > 1 (torchrun, one process per GPU) the model is split into N pipeline stages (layer ranges balanced by
 the bytes each stage streams per round; the tail holds the LM head and the MTP drafter), joined by device links
 over NVLink, with N sequences in flight (--inflight) so that every stage is busy: weak scaling (each GPU streams
@@ -778,7 +781,24 @@ def run_micro(args):
     dev = torch.device("cuda:0")
     ctx = Context(0)
     peak, _ = load_peaks()
-    obj = wide_micro(ctx, dev) if args.micro == "wide" else acceptance_micro(ctx, dev, peak, False)
+    if args.micro == "wide":
+        obj = wide_micro(ctx, dev)
+    elif args.micro == "prefill":
+        import numpy as np
+
+        from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+
+        geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
+        eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, args.context + 64, PREFILL_CHUNK, 2)
+        eng.generate_weights(seed=SEED, stddev=0.02)
+        eng.prepare()
+        stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+        obj = prefill_micro(eng, geo, dev, stream, args.context, np.random.default_rng(5)) or {}
+        eng.close()
+    elif args.micro == "tree":
+        obj = tree_micro(ctx, dev, peak, args.context)
+    else:
+        obj = acceptance_micro(ctx, dev, peak, False)
     ctx.close()
     print(json.dumps({"micro": args.micro, **obj}), flush=True)
 
@@ -795,7 +815,7 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
     ap.add_argument("--inflight", type=int, default=0, help="sequences in flight with N > 1 (default N)")
     ap.add_argument("--plan", default="", help="stage plan BEGIN-END@gK,... with N > 1 (default: byte-balanced)")
-    ap.add_argument("--micro", default="", choices=["", "wide", "accept"],
+    ap.add_argument("--micro", default="", choices=["", "wide", "accept", "prefill", "tree"],
                     help="run one micro-benchmark alone and print its object (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
