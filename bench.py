@@ -339,8 +339,8 @@ def tree_micro(ctx, dev, peak, context):
     """C4: 16-node tree verification windows (Q8_0 8B shape, context `context` per sequence).
     batch 1: one sequence's tree through clm_b200_run_tree_window_device (the GEMV chain), event-timed on the
     engine's stream.  batch 8: eight sequences' trees in ONE window through clm_b200_run_batch_window (128 rows:
-    tcgen05 GEMMs, each weight matrix read once; per-sequence RoPE/KV and attention), timed by events on the engine
-    stream around the host call (its launches are issued directly, so the time includes their issue)."""
+    tcgen05 GEMMs, each weight matrix read once; per-sequence RoPE/KV and attention; a CUDA graph per session
+    set), timed by events on the engine stream around the host call."""
     import numpy as np
     import torch
 

@@ -268,6 +268,9 @@ struct LlamaEngine : clm_b200_engine {
   clm_b200_link* pipe_out = nullptr;
   LinkDev lin, lout;
   std::map<uint64_t, std::unique_ptr<Session>> sessions;
+  // batched windows: CUDA graphs per session set (the Session objects hold only graphs), dropped whenever a session
+  // closes (the graphs hold its position and page-table addresses)
+  std::map<std::vector<uint64_t>, std::unique_ptr<Session>> batch_graphs;
   std::vector<void*> allocations;
   uint64_t weight_bytes = 0;
 
@@ -753,9 +756,15 @@ struct LlamaEngine : clm_b200_engine {
     s.d_state = nullptr;
   }
 
+  void drop_batch_graphs() {
+    for (auto& kv : batch_graphs) release_session(*kv.second);
+    batch_graphs.clear();
+  }
+
   ~LlamaEngine() override {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
+    drop_batch_graphs();
     for (auto& kv : sessions) release_session(*kv.second);
     sessions.clear();
     auto free_m = [](Gemv& g) {
@@ -1098,6 +1107,7 @@ int llama_session_close(LlamaEngine* e, uint64_t id) {
   Session* s = find_session(e, id);
   if (!s) return CLM_OK;  // idempotent cleanup (WindowLedger::abort_session)
   CLM_CUDA(cudaStreamSynchronize(e->ctx->stream));
+  e->drop_batch_graphs();
   e->release_session(*s);
   e->sessions.erase(id);
   return CLM_OK;
@@ -1261,8 +1271,14 @@ int llama_run_batch(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint6
   CLM_CUDA(cudaMemcpyAsync(e->win, h_tokens, Q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
   if (h_parents != nullptr)
     CLM_CUDA(cudaMemcpyAsync(e->parents, h_parents, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
-  // launched directly (the session set changes from call to call; no graph is kept)
-  CLM_TRY(e->enqueue_window_wide(segs.data(), (int)n, (int)Q, e->win, h_parents ? e->parents : nullptr, st));
+  // one CUDA graph per session set (eager on first use, captured on the second, replayed after)
+  std::vector<uint64_t> key(ids, ids + n);
+  auto& holder = e->batch_graphs[key];
+  if (!holder) holder = std::make_unique<Session>();
+  const int32_t* par = h_parents ? e->parents : nullptr;
+  CLM_TRY(e->run_graph(*holder, 7, (int)Q, h_parents ? 1 : 0, st, [&](cudaStream_t cs) {
+    return e->enqueue_window_wide(segs.data(), (int)n, (int)Q, e->win, par, cs);
+  }));
   if (h_logits)
     CLM_CUDA(cudaMemcpyAsync(h_logits, e->logits, (size_t)Q * e->d.V * sizeof(float), cudaMemcpyDeviceToHost, st));
   CLM_CUDA(cudaStreamSynchronize(st));

@@ -154,7 +154,7 @@ def test_batch_tree_window_matches_per_session_trees(ctx, oracle):
     rng = np.random.default_rng(21)
     pos = []
     for b in range(4):
-        n = 5 + 7 * b
+        n = 3 + 4 * b  # at most 16: the reference engine's windows
         pre = rng.integers(0, geo.vocab, n).astype(np.int32)
         for eng in (e, ref):
             eng.open_session(b + 1)
