@@ -243,6 +243,10 @@ struct LlamaEngine : clm_b200_engine {
   float* wpart = nullptr;    // split-K partials of the tensor-core GEMMs
   size_t wpart_floats = 0;
   float* wattn = nullptr;    // attention outputs [W][qd]
+  float* wattn_part = nullptr;  // wide attention: KV-split partials and their tile counters
+  size_t wattn_part_floats = 0;
+  int* wattn_cnt = nullptr;
+  int wattn_tiles = 0;
   uint8_t* wxh = nullptr;    // fp16 activation tiles of the next GEMM
   float* logits = nullptr;
   int32_t* tokens = nullptr;
@@ -496,11 +500,19 @@ struct LlamaEngine : clm_b200_engine {
     return launch_window_mk(P, d.quant, nt, mk_grid[nt - 1], st);
   }
 
-  // ---- one tensor-core GEMM of a wide window: y[p] = W . x[p] over the tiles in wxh
-  int gemm_wide(const Gemv& g, int q, float* y, cudaStream_t st) {
+  // ---- one tensor-core GEMM of a wide window: y[p] = W . x[p] over the tiles in wxh.  `out` tells the next step
+  // where the product is: y itself, or the K-split partials it sums (no separate reduction launch).
+  int gemm_wide(const Gemv& g, int q, float* y, cudaStream_t st, WideIn* out = nullptr) {
     const TcPlan p = gemm_tc_plan(g.m->shape, q, ctx->sm_count);
     CLM_CHECK(p.ksplit == 1 || p.part_floats <= wpart_floats, CLM_INTERNAL, "wide window: split-K partials");
-    return launch_gemm_tc_tiles(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), wxh, q, y, wpart, bad, st);
+    const bool defer = out != nullptr && p.ksplit > 1;
+    if (out != nullptr) {
+      out->p = defer ? wpart : y;
+      out->nsplit = defer ? p.ksplit : 1;
+      out->stride = (unsigned long long)q * g.m->shape.rows;
+    }
+    return launch_gemm_tc_tiles(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), wxh, q, y, wpart, bad, st,
+                                !defer);
   }
 
   // ---- a wide window (17..256 rows: prefill chunks, large trees, or the windows of several sessions stacked):
@@ -519,6 +531,14 @@ struct LlamaEngine : clm_b200_engine {
                           cudaStream_t st) {
     const int P = (q + 15) / 16 * 16;
     const size_t qkv_rows = (size_t)d.qd() + 2 * d.kvd();
+    CLM_CHECK(nseg >= 1 && nseg <= kWideAttnMaxSegs, CLM_OUT_OF_RANGE, "wide window: at most 16 sessions");
+    AttnSegs attn_segs{};
+    for (int k = 0; k < nseg; ++k) {
+      CLM_CHECK(segs[k].q == segs[0].q && segs[k].row0 == k * segs[0].q, CLM_INTERNAL, "wide window: segment rows");
+      attn_segs.pos[k] = &segs[k].s->d_state->pos;
+      attn_segs.pages[k] = segs[k].s->d_pages;
+      attn_segs.row0[k] = segs[k].row0;
+    }
     if (has_tokens) {
       CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(256), 0, st, d_tok, q, (int)d.V, tokens, bad));
       CLM_TRY(launch_embed(embd, d.quant, tokens, q, d.H, h, st));
@@ -526,28 +546,31 @@ struct LlamaEngine : clm_b200_engine {
       CLM_TRY(launch_unpack_boundary(bin, q, d.H, h, st));
     }
     const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
-    CLM_TRY(launch_wide_norm_prep(nullptr, h, q, d.H, w0, d.eps, P, wxh, st));
+    CLM_TRY(launch_wide_norm_prep(WideIn{}, h, q, d.H, w0, d.eps, P, wxh, st));
     for (size_t li = 0; li < layers.size(); ++li) {
       const Layer& L = layers[li];
-      CLM_TRY(gemm_wide(L.qkv, q, wy, st));
+      WideIn y;
+      CLM_TRY(gemm_wide(L.qkv, q, wy, st, &y));
       for (int k = 0; k < nseg; ++k) {
         const WideSeg& g = segs[k];
         const long long* pos = &g.s->d_state->pos;
         __half* qs = q16 + (size_t)g.row0 * d.qd();
-        CLM_TRY(launch_wide_rope_kv(wy + (size_t)g.row0 * qkv_rows, g.q, d, rope, pos, g.s->d_pages, parent, qs,
-                                    kpool[li], vpool[li], st));
-        CLM_TRY(launch_attention(qs, kpool[li], vpool[li], g.s->d_pages, pos, parent, g.q, d, max_pages, attn_part,
-                                 acount, 2, hi_scale(), xb.frag, xb.sum, bad, nullptr, 0, ctx->sm_count, st,
-                                 wattn + (size_t)g.row0 * d.qd()));
+        WideIn ys = y;
+        ys.p += (size_t)g.row0 * qkv_rows;
+        CLM_TRY(launch_wide_rope_kv(ys, g.q, d, rope, pos, g.s->d_pages, parent, qs, kpool[li], vpool[li], st));
       }
+      // one attention launch over every segment (all segments have segs[0].q rows)
+      CLM_TRY(launch_attention_wide(q16, kpool[li], vpool[li], attn_segs, nseg, parent, segs[0].q, d, max_pages,
+                                    wattn_part, wattn_part_floats, wattn_cnt, wattn_tiles, ctx->sm_count, wattn, bad,
+                                    st));
       CLM_TRY(launch_tc_xprep(wattn, q, d.qd(), P, wxh, st));
-      CLM_TRY(gemm_wide(L.o, q, wy, st));
-      CLM_TRY(launch_wide_norm_prep(wy, h, q, d.H, L.ffn_norm, d.eps, P, wxh, st));
-      CLM_TRY(gemm_wide(L.gu, q, wy, st));
-      CLM_TRY(launch_wide_swiglu_prep(wy, q, d.F, P, wxh, st));
-      CLM_TRY(gemm_wide(L.down, q, wy, st));
+      CLM_TRY(gemm_wide(L.o, q, wy, st, &y));
+      CLM_TRY(launch_wide_norm_prep(y, h, q, d.H, L.ffn_norm, d.eps, P, wxh, st));
+      CLM_TRY(gemm_wide(L.gu, q, wy, st, &y));
+      CLM_TRY(launch_wide_swiglu_prep(y, q, d.F, P, wxh, st));
+      CLM_TRY(gemm_wide(L.down, q, wy, st, &y));
       const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
-      CLM_TRY(launch_wide_norm_prep(wy, h, q, d.H, wnext, d.eps, P, wxh, st));
+      CLM_TRY(launch_wide_norm_prep(y, h, q, d.H, wnext, d.eps, P, wxh, st));
     }
     if (has_head) return gemm_wide(head, q, logits, st);
     return launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st);
@@ -984,6 +1007,15 @@ int llama_prepare(LlamaEngine* e) {
     e->wpart_floats = part_max;
     if (part_max) CLM_TRY(e->alloc_t(&e->wpart, part_max));
     CLM_TRY(e->alloc_t(&e->wattn, (size_t)W * d.qd()));
+    {
+      // tiles of a wide attention launch: (kv head, head subgroup) x (16-row blocks, or sessions of <= 16 rows)
+      const int group = d.nh / d.nkv, hg = group < 4 ? group : 4;
+      e->wattn_tiles = d.nkv * (group / hg) * std::max((W + 15) / 16, 16);
+      e->wattn_part_floats = (size_t)e->wattn_tiles * 8 * hg * 16 * kAttnRowFloats;
+      CLM_TRY(e->alloc_t(&e->wattn_part, e->wattn_part_floats));
+      CLM_TRY(e->alloc_t(&e->wattn_cnt, (size_t)e->wattn_tiles));
+      CLM_CUDA(cudaMemset(e->wattn_cnt, 0, (size_t)e->wattn_tiles * sizeof(int)));
+    }
     CLM_TRY(e->alloc((void**)&e->wxh, P * maxcols * sizeof(__half)));
   }
   {

@@ -403,7 +403,7 @@ int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, 
 }
 
 int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const uint8_t* d_xh, int q,
-                         float* d_y, float* d_part, int* d_err, cudaStream_t st) {
+                         float* d_y, float* d_part, int* d_err, cudaStream_t st, bool sum_splits) {
   CLM_CHECK(q > 16 && q <= 256 && p.P == ((q + 15) / 16) * 16, CLM_OUT_OF_RANGE,
             "tensor-core GEMM covers 17..256 window rows");
   CLM_CHECK(s.cols % 256 == 0, CLM_INVALID_ARGUMENT, "columns must be a multiple of 256");
@@ -423,7 +423,7 @@ int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_t
     CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q8_0>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
                        s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err));
   }
-  if (p.ksplit > 1) {
+  if (p.ksplit > 1 && sum_splits) {
     const uint64_t n = (uint64_t)q * s.rows;
     CLM_TRY(launch_pdl(split_sum_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,
                        (const float*)d_part, p.ksplit, n, d_y));

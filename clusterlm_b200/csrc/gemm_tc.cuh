@@ -23,9 +23,11 @@ TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count);
 int launch_gemm_tc(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const float* d_x, int q, float* d_y,
                    uint8_t* d_xh, float* d_part, int* d_err, cudaStream_t st);
 
-// The GEMM alone, over activation tiles already in d_xh (written by launch_tc_xprep or a fused producer).
+// The GEMM alone, over activation tiles already in d_xh (written by launch_tc_xprep or a fused producer).  With
+// sum_splits false and p.ksplit > 1 the K-split partials stay in d_part ([ksplit][q][rows], summed in split order
+// by the consumer) and d_y is not written.
 int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_tiles, const uint8_t* d_xh, int q,
-                         float* d_y, float* d_part, int* d_err, cudaStream_t st);
+                         float* d_y, float* d_part, int* d_err, cudaStream_t st, bool sum_splits = true);
 
 // Activation tiles of the GEMM: x (q x K f32, row-major) -> fp16, K-major 128-byte-swizzled tiles of 64 columns,
 // tile c at d_xh + c * P * 128 with row p's 16-byte chunk j at tc_tile_off(p, j); rows q..P-1 are zero.

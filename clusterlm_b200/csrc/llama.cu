@@ -417,6 +417,310 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
 }
 
 // ---------------------------------------------------------------------------------------------------
+// wide-window attention: every KV page read once per (kv head, 16-row block, segment)
+// ---------------------------------------------------------------------------------------------------
+constexpr int kWideAttnPages = 3;        // page ring depth (K page + V^T page per slot)
+constexpr int kWideAttnMaxGroup = 8;     // query heads per kv head
+constexpr int kWideAttnHeads = 4;        // query heads per CTA (a larger group is split over group / 4 CTAs)
+constexpr int kWideAttnMaxSplits = 8;    // KV splits per (kv head, 16-row block, segment)
+
+template <int HD>
+__global__ void __launch_bounds__(32 * (2 * kWideAttnHeads + 1), 1) attention_wide_kernel(
+    const __half* __restrict__ q16, const __half* __restrict__ kpool, const __half* __restrict__ vpool,
+    const __grid_constant__ AttnSegs segs, const int32_t* __restrict__ parent, int qs, int nh, int nkv, float scale_log2,
+    int max_pages, int nsplit, float* __restrict__ gpart, int* __restrict__ counters, float* __restrict__ out,
+    int* __restrict__ err) {
+  static_assert(HD == 128, "head_dim 128 layout");
+  constexpr int RW = kAttnRowFloats;
+  constexpr uint32_t kPageBytes = (uint32_t)attn_page_bytes(HD);
+  extern __shared__ __align__(128) uint8_t wa_smem[];
+  __shared__ __align__(8) uint64_t full[kWideAttnPages], empty[kWideAttnPages];
+  const int group = nh / nkv, hg = group < kWideAttnHeads ? group : kWideAttnHeads, nsub = group / hg;
+  const int kvh = blockIdx.x / nsub, h0 = kvh * group + (blockIdx.x % nsub) * hg;  // this CTA's first query head
+  const int blk = blockIdx.y, seg = blockIdx.z / nsplit, split = blockIdx.z % nsplit;
+  const int nw = 2 * hg;  // consumer warps
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, g = lane / 4, t = lane % 4;
+  const long long* d_pos = segs.pos[seg];
+  const int32_t* pages = segs.pages[seg];
+  const int row0 = segs.row0[seg];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWideAttnPages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], nw);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // committed position and page table do not depend on the preceding kernel
+  const long long base = *d_pos;
+  const int last_row = min(16 * blk + 15, qs - 1);
+  const long long np_l = (base + last_row + 1 + kPageTokens - 1) / kPageTokens;
+  const int np_all = (int)(np_l < max_pages ? np_l : max_pages);
+  // this split's contiguous share of the visible pages
+  const int pg_begin = (int)((long long)split * np_all / nsplit), pg_end = (int)((long long)(split + 1) * np_all / nsplit);
+  auto kbuf = [&](int s) { return reinterpret_cast<__half*>(wa_smem + (size_t)s * 2 * kPageBytes); };
+  // the consumers' final states, after the page ring: [warp][16 rows][RW]
+  float* parts = reinterpret_cast<float*>(wa_smem + (size_t)kWideAttnPages * 2 * kPageBytes);
+
+  if (warp == nw) {
+    // ---------------- producer: committed pages before griddepcontrol.wait, the window's after ----------------
+    bool waited = false;
+    if (lane == 0) {
+      int slot = 0;
+      uint32_t phase = 0;
+      for (int pg = pg_begin; pg < pg_end; ++pg) {
+        if (!waited && (long long)(pg + 1) * kPageTokens > base) {
+          griddep_wait();  // this page holds rows the preceding kernel wrote
+          waited = true;
+        }
+        if (!mbar_wait(&empty[slot], phase ^ 1u, err)) break;
+        const size_t off = ((size_t)pages[pg] * nkv + kvh) * kPageTokens * HD;
+        mbar_expect_tx(&full[slot], 2 * kPageBytes);
+        bulk_g2s(kbuf(slot), kpool + off, kPageBytes, &full[slot]);
+        bulk_g2s(kbuf(slot) + kPageTokens * HD, vpool + off, kPageBytes, &full[slot]);
+        if (++slot == kWideAttnPages) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!waited) griddep_wait();
+    griddep_launch();
+  } else if (warp < nw) {
+    // ---------------- consumers: m-tile j (16 of the block's 16 x group rows), half of every page ----------------
+    griddep_wait();
+    griddep_launch();
+    const int j = warp / 2, half = warp % 2;
+    const int r0 = j * 16 + g, r1 = r0 + 8;  // rows of the block: window row 16 blk + r / hg, head h0 + r % hg
+    const int i0 = 16 * blk + r0 / hg, i1 = 16 * blk + r1 / hg;
+    const bool v0 = i0 < qs, v1 = i1 < qs;
+    float O[HD / 8][4];
+#pragma unroll
+    for (int jn = 0; jn < HD / 8; ++jn) O[jn][0] = O[jn][1] = O[jn][2] = O[jn][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    uint4 qw0[4], qw1[4];
+    {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      const uint4* a = reinterpret_cast<const uint4*>(
+          q16 + ((size_t)(row0 + (v0 ? i0 : 0)) * nh + h0 + r0 % hg) * HD + 32 * t);
+      const uint4* b = reinterpret_cast<const uint4*>(
+          q16 + ((size_t)(row0 + (v1 ? i1 : 0)) * nh + h0 + r1 % hg) * HD + 32 * t);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        qw0[u] = v0 ? a[u] : z;
+        qw1[u] = v1 ? b[u] : z;
+      }
+    }
+    int slot = 0;
+    uint32_t phase = 0;
+    for (int pg = pg_begin; pg < pg_end; ++pg) {
+      const bool ok = mbar_wait(&full[slot], phase, err);
+      const __half* ks = kbuf(slot);
+      const __half* vs = ks + kPageTokens * HD;
+      if (ok) {
+        float Sx[4][4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          Sx[jj][0] = Sx[jj][1] = Sx[jj][2] = Sx[jj][3] = 0.0f;
+          const int pos = 32 * half + 8 * (g / 2) + 2 * jj + (g % 2);
+          const uint4* kr = reinterpret_cast<const uint4*>(ks + (size_t)pos * HD);
+          uint4 kw[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) kw[u] = kr[kv_k_chunk(4 * t + u, pos)];
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16(Sx[jj], word_of(qw0, 2 * kk), word_of(qw1, 2 * kk), word_of(qw0, 2 * kk + 1),
+                    word_of(qw1, 2 * kk + 1), word_of(kw, 2 * kk), word_of(kw, 2 * kk + 1));
+        }
+        float mx0 = m0, mx1 = m1;
+        if ((long long)(pg + 1) * kPageTokens <= base) {  // every position is visible to every window row
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              Sx[jj][e] = v0 ? Sx[jj][e] * scale_log2 : -INFINITY;
+              Sx[jj][2 + e] = v1 ? Sx[jj][2 + e] * scale_log2 : -INFINITY;
+              mx0 = fmaxf(mx0, Sx[jj][e]);
+              mx1 = fmaxf(mx1, Sx[jj][2 + e]);
+            }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const long long pos = (long long)pg * kPageTokens + 32 * half + 8 * t + 2 * jj + e;
+              Sx[jj][e] = (v0 && visible(pos, base, i0, parent)) ? Sx[jj][e] * scale_log2 : -INFINITY;
+              Sx[jj][2 + e] = (v1 && visible(pos, base, i1, parent)) ? Sx[jj][2 + e] * scale_log2 : -INFINITY;
+              mx0 = fmaxf(mx0, Sx[jj][e]);
+              mx1 = fmaxf(mx1, Sx[jj][2 + e]);
+            }
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        const float c0 = mx0 == -INFINITY ? 1.0f : exp2f(m0 - mx0), c1 = mx1 == -INFINITY ? 1.0f : exp2f(m1 - mx1);
+        m0 = mx0;
+        m1 = mx1;
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int jn = 0; jn < HD / 8; ++jn) {
+          O[jn][0] *= c0;
+          O[jn][1] *= c0;
+          O[jn][2] *= c1;
+          O[jn][3] *= c1;
+        }
+        uint32_t pa[4][2];
+        float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float p00 = m0 == -INFINITY ? 0.0f : exp2f(Sx[jj][0] - m0);
+          const float p01 = m0 == -INFINITY ? 0.0f : exp2f(Sx[jj][1] - m0);
+          const float p10 = m1 == -INFINITY ? 0.0f : exp2f(Sx[jj][2] - m1);
+          const float p11 = m1 == -INFINITY ? 0.0f : exp2f(Sx[jj][3] - m1);
+          ps0 += p00 + p01;
+          ps1 += p10 + p11;
+          pa[jj][0] = pack_half2(p00, p01);
+          pa[jj][1] = pack_half2(p10, p11);
+        }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+          ps0 += __shfl_xor_sync(0xffffffffu, ps0, o);
+          ps1 += __shfl_xor_sync(0xffffffffu, ps1, o);
+        }
+        l0 += ps0;
+        l1 += ps1;
+#pragma unroll
+        for (int jn = 0; jn < HD / 8; ++jn) {
+          const int vrow = 8 * jn + g;
+          const uint4 va =
+              reinterpret_cast<const uint4*>(vs + (size_t)vrow * kPageTokens)[kv_v_chunk(4 * half + t, vrow)];
+          mma_f16(O[jn], pa[0][0], pa[0][1], pa[1][0], pa[1][1], va.x, va.y);
+          mma_f16(O[jn], pa[2][0], pa[2][1], pa[3][0], pa[3][1], va.z, va.w);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (++slot == kWideAttnPages) {
+        slot = 0;
+        phase ^= 1u;
+      }
+    }
+    float* sp = parts + (size_t)warp * 16 * RW;
+#pragma unroll
+    for (int jn = 0; jn < HD / 8; ++jn) {
+      *reinterpret_cast<float2*>(sp + g * RW + 8 * jn + 2 * t) = make_float2(O[jn][0], O[jn][1]);
+      *reinterpret_cast<float2*>(sp + (g + 8) * RW + 8 * jn + 2 * t) = make_float2(O[jn][2], O[jn][3]);
+    }
+    if (t == 0) {
+      sp[g * RW + HD] = m0;
+      sp[g * RW + HD + 1] = l0;
+      sp[(g + 8) * RW + HD] = m1;
+      sp[(g + 8) * RW + HD + 1] = l1;
+    }
+  }
+  __syncthreads();
+  const int qd = nh * HD;
+  const int rows = hg * 16;  // this CTA's rows: m-tile j = row / 16
+  if (nsplit == 1) {
+    // combine the two halves of every m-tile into f32 rows
+    for (int idx = threadIdx.x; idx < rows * HD; idx += blockDim.x) {
+      const int j = idx / (16 * HD), r = (idx / HD) % 16, c = idx % HD;
+      const int rr = j * 16 + r, i = 16 * blk + rr / hg;
+      if (i >= qs) continue;
+      const float* a = parts + (size_t)(2 * j) * 16 * RW + r * RW;
+      const float* b = a + 16 * RW;
+      const float ma = a[HD], mb = b[HD];
+      const float M = fmaxf(ma, mb);
+      const float ea = ma == -INFINITY ? 0.0f : exp2f(ma - M), eb = mb == -INFINITY ? 0.0f : exp2f(mb - M);
+      const float L = a[HD + 1] * ea + b[HD + 1] * eb;
+      out[(size_t)(row0 + i) * qd + (h0 + rr % hg) * HD + c] = L > 0.0f ? (a[c] * ea + b[c] * eb) / L : 0.0f;
+    }
+    return;
+  }
+  // split KV: the halves combined into this split's partial (unnormalised O, max, sum) in global memory; the last
+  // split of the tile to arrive (counter) combines all of them, so no CTA waits for another
+  const int tile = (blockIdx.x * gridDim.y + blk) * (gridDim.z / nsplit) + seg;
+  float* tp = gpart + (size_t)tile * nsplit * rows * RW;
+  float* mine = tp + (size_t)split * rows * RW;
+  for (int idx = threadIdx.x; idx < rows * (HD + 2); idx += blockDim.x) {
+    const int rr = idx / (HD + 2), c = idx % (HD + 2), j = rr / 16, r = rr % 16;
+    const float* a = parts + (size_t)(2 * j) * 16 * RW + r * RW;
+    const float* b = a + 16 * RW;
+    const float ma = a[HD], mb = b[HD];
+    const float M = fmaxf(ma, mb);
+    const float ea = ma == -INFINITY ? 0.0f : exp2f(ma - M), eb = mb == -INFINITY ? 0.0f : exp2f(mb - M);
+    float v;
+    if (c < HD)
+      v = a[c] * ea + b[c] * eb;
+    else if (c == HD)
+      v = M;
+    else
+      v = a[HD + 1] * ea + b[HD + 1] * eb;
+    mine[(size_t)rr * RW + c] = v;
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(&counters[tile], 1);
+    s_last = prev == nsplit - 1;
+    if (s_last) {
+      counters[tile] = 0;  // every split of this launch has arrived: ready for the next launch
+      __threadfence();
+    }
+  }
+  __syncthreads();
+  if (!s_last) return;
+  for (int idx = threadIdx.x; idx < rows * HD; idx += blockDim.x) {
+    const int rr = idx / HD, c = idx % HD, i = 16 * blk + rr / hg;
+    if (i >= qs) continue;
+    float M = -INFINITY;
+    for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(tp + ((size_t)k * rows + rr) * RW + HD));
+    float L = 0.0f, acc = 0.0f;
+    for (int k = 0; k < nsplit; ++k) {
+      const float* row = tp + ((size_t)k * rows + rr) * RW;
+      const float mk = __ldcg(row + HD);
+      const float e = mk == -INFINITY ? 0.0f : exp2f(mk - M);
+      L += __ldcg(row + HD + 1) * e;
+      acc += __ldcg(row + c) * e;
+    }
+    out[(size_t)(row0 + i) * qd + (h0 + rr % hg) * HD + c] = L > 0.0f ? acc / L : 0.0f;
+  }
+}
+
+int launch_attention_wide(const __half* d_q, const __half* d_k, const __half* d_v, const AttnSegs& segs, int nseg,
+                          const int32_t* d_parent, int qs, const LlamaDims& d, int max_pages, float* d_part,
+                          size_t part_floats, int* d_counters, int n_counters, int sm_count, float* d_out, int* d_err,
+                          cudaStream_t st) {
+  CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
+  const int group = d.nh / d.nkv;
+  const int hg = group < kWideAttnHeads ? group : kWideAttnHeads;
+  CLM_CHECK(group >= 1 && group <= kWideAttnMaxGroup && group * d.nkv == d.nh && group % hg == 0, CLM_UNIMPLEMENTED,
+            "wide attention: 1, 2, 4 or 8 query heads per kv head");
+  CLM_CHECK(nseg >= 1 && nseg <= kWideAttnMaxSegs && qs >= 1, CLM_INVALID_ARGUMENT, "wide attention: segments");
+  const size_t ring = (size_t)kWideAttnPages * 2 * attn_page_bytes(128);
+  const size_t parts = (size_t)2 * hg * 16 * kAttnRowFloats * sizeof(float);
+  const size_t smem = ring + parts;
+  CLM_TRY(ensure_smem(attention_wide_kernel<128>, smem));
+  const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
+  // KV splits only while the tiles leave SMs idle: as many as fit in one wave (a 256-row prefill window has 128
+  // tiles and runs unsplit, which measured faster than splitting it), at least four pages per split
+  const int tiles = d.nkv * (group / hg) * ((qs + 15) / 16) * nseg;
+  int nsplit = (sm_count > 0 ? sm_count : 148) / tiles;
+  if (nsplit > max_pages / 4) nsplit = max_pages / 4;
+  if (nsplit > kWideAttnMaxSplits) nsplit = kWideAttnMaxSplits;
+  if (nsplit < 1) nsplit = 1;
+  const size_t per_split = (size_t)hg * 16 * kAttnRowFloats;
+  while (nsplit > 1 && ((size_t)tiles * nsplit * per_split > part_floats || tiles > n_counters)) --nsplit;
+  return launch_pdl(attention_wide_kernel<128>, dim3(d.nkv * (group / hg), (qs + 15) / 16, nseg * nsplit),
+                    dim3(32 * (2 * hg + 1)), smem, st, d_q, d_k, d_v, segs, d_parent, qs, d.nh, d.nkv, scale_log2,
+                    max_pages, nsplit, d_part, d_counters, d_out, d_err);
+}
+
+// ---------------------------------------------------------------------------------------------------
 // stage boundary records (hc = 1): {S[H], P[H], g}
 // ---------------------------------------------------------------------------------------------------
 __global__ void pack_boundary_kernel(const float* __restrict__ h, const float* __restrict__ part, int nsplit, int q,

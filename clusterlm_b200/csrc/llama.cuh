@@ -47,6 +47,26 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
                      int* d_err, const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count,
                      cudaStream_t st, float* d_out_f32 = nullptr);
+// Wide-window attention (windows of more than 16 rows, and batched windows of several sessions): one CTA per
+// (kv head, block of 16 window rows, session segment) holds the block's rows of every query head of the kv head
+// (16 x group rows; a group of 8 is split over two CTAs of 4 heads) and streams the segment's visible KV pages once through a 3-page ring (bulk copies by a
+// producer warp); two warps per 16-row m-tile take the two halves of each page with an online softmax, and the CTA
+// combines them into f32 rows out[row0 + i][nh * hd].  Segment s: window rows row0[s] .. row0[s] + qs - 1 of
+// q16 / out, committed position *pos[s], page table pages[s]; parent (shared tree shape, or null for linear
+// windows) as in launch_attention.  group = nh / nkv <= 8, hd = 128, at most kWideAttnMaxSegs segments.
+constexpr int kWideAttnMaxSegs = 16;
+struct AttnSegs {
+  const long long* pos[kWideAttnMaxSegs];
+  const int32_t* pages[kWideAttnMaxSegs];
+  int row0[kWideAttnMaxSegs];
+};
+// With fewer (kv head, block, segment) tiles than SMs the visible pages are split over up to 8 CTAs per tile (as
+// many as fit in one wave): each writes its partial to d_part (part_floats floats) and the last to arrive on the tile's
+// counter (d_counters: n_counters zeroed ints, left zero) combines them; no CTA waits for another.
+int launch_attention_wide(const __half* d_q, const __half* d_k, const __half* d_v, const AttnSegs& segs, int nseg,
+                          const int32_t* d_parent, int qs, const LlamaDims& d, int max_pages, float* d_part,
+                          size_t part_floats, int* d_counters, int n_counters, int sm_count, float* d_out, int* d_err,
+                          cudaStream_t st);
 // Copies h[p][0:H] of rows into the boundary records out[p] = {S = h, P = 0, g = 1} (hc = 1).
 int launch_pack_boundary(const float* d_h, const float* d_part, int nsplit, int q, int H, float* d_out,
                          cudaStream_t st);

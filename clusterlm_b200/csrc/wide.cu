@@ -11,13 +11,26 @@ namespace {
 constexpr int kNormThreads = 256;
 constexpr int kNormUnits = 4;  // 8-column units per thread: H <= 8 * 256 * 4
 
+__device__ __forceinline__ float4 ld_in4(const WideIn& y, size_t i) {
+  float4 a = *reinterpret_cast<const float4*>(y.p + i);
+  for (int k = 1; k < y.nsplit; ++k) {
+    const float4 b = *reinterpret_cast<const float4*>(y.p + k * y.stride + i);
+    a = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+  }
+  return a;
+}
+__device__ __forceinline__ float ld_in(const WideIn& y, size_t i) {
+  float a = y.p[i];
+  for (int k = 1; k < y.nsplit; ++k) a += y.p[k * y.stride + i];
+  return a;
+}
+
 __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
 }
 
 // One CTA per window row: the residual update, the row's sum of squares, then its normalised fp16 tile chunks.
-__global__ void __launch_bounds__(kNormThreads) wide_norm_prep_kernel(const float* __restrict__ y,
-                                                                      float* __restrict__ h, int H,
+__global__ void __launch_bounds__(kNormThreads) wide_norm_prep_kernel(const WideIn y, float* __restrict__ h, int H,
                                                                       const float* __restrict__ w, float eps, int P,
                                                                       uint8_t* __restrict__ xh) {
   griddep_wait();
@@ -25,7 +38,7 @@ __global__ void __launch_bounds__(kNormThreads) wide_norm_prep_kernel(const floa
   __shared__ float s_red[kNormThreads / 32];
   const int p = blockIdx.x, tid = threadIdx.x, units = H / 8;
   float* hp = h + (size_t)p * H;
-  const float* yp = y ? y + (size_t)p * H : nullptr;
+  const size_t yrow = (size_t)p * H;
   float v[kNormUnits][8];
   float ss = 0.0f;
 #pragma unroll
@@ -33,8 +46,8 @@ __global__ void __launch_bounds__(kNormThreads) wide_norm_prep_kernel(const floa
     const int u = tid + kNormThreads * k;
     if (u >= units) continue;
     float4 a = *reinterpret_cast<const float4*>(hp + 8 * u), b = *reinterpret_cast<const float4*>(hp + 8 * u + 4);
-    if (yp) {
-      const float4 c = *reinterpret_cast<const float4*>(yp + 8 * u), e = *reinterpret_cast<const float4*>(yp + 8 * u + 4);
+    if (y.p) {
+      const float4 c = ld_in4(y, yrow + 8 * u), e = ld_in4(y, yrow + 8 * u + 4);
       a = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
       b = make_float4(b.x + e.x, b.y + e.y, b.z + e.z, b.w + e.w);
       *reinterpret_cast<float4*>(hp + 8 * u) = a;
@@ -73,7 +86,7 @@ __device__ __forceinline__ int node_depth(const int32_t* parent, int i) {
 }
 
 // Grid (window row, head of the QKV rows), hd / 2 threads: one RoPE pair (or two V dims) each.
-__global__ void wide_rope_kv_kernel(const float* __restrict__ y, int nh, int nkv, int hd,
+__global__ void wide_rope_kv_kernel(const WideIn y, int nh, int nkv, int hd,
                                     const float2* __restrict__ rope, const long long* __restrict__ d_pos,
                                     const int32_t* __restrict__ pages, const int32_t* __restrict__ parent,
                                     __half* __restrict__ q16, __half* __restrict__ kpool, __half* __restrict__ vpool) {
@@ -81,7 +94,7 @@ __global__ void wide_rope_kv_kernel(const float* __restrict__ y, int nh, int nkv
   griddep_launch();
   const int p = blockIdx.x, head = blockIdx.y, pr = threadIdx.x;
   const int rows = (nh + 2 * nkv) * hd;
-  const float a = y[(size_t)p * rows + head * hd + 2 * pr], b = y[(size_t)p * rows + head * hd + 2 * pr + 1];
+  const float a = ld_in(y, (size_t)p * rows + head * hd + 2 * pr), b = ld_in(y, (size_t)p * rows + head * hd + 2 * pr + 1);
   const long long base = *d_pos, slot = base + p;
   const int32_t page = pages[slot / kPageTokens];
   const int pos = (int)(slot % kPageTokens), d0 = 2 * pr;
@@ -105,17 +118,17 @@ __global__ void wide_rope_kv_kernel(const float* __restrict__ y, int nh, int nkv
 }
 
 // Grid (window row, F / 512), 64 threads: eight consecutive ffn indices each.
-__global__ void wide_swiglu_prep_kernel(const float* __restrict__ y, int F, int P, uint8_t* __restrict__ xh) {
+__global__ void wide_swiglu_prep_kernel(const WideIn y, int F, int P, uint8_t* __restrict__ xh) {
   griddep_wait();
   griddep_launch();
   const int p = blockIdx.x;
   const int j0 = (blockIdx.y * 64 + threadIdx.x) * 8;
   if (j0 >= F) return;
-  const float* g = y + (size_t)p * 2 * F + (size_t)(j0 / 64) * 128 + j0 % 64;
+  const size_t g = (size_t)p * 2 * F + (size_t)(j0 / 64) * 128 + j0 % 64;
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float gv = g[i], uv = g[64 + i];
+    const float gv = ld_in(y, g + i), uv = ld_in(y, g + 64 + i);
     o[i] = gv / (1.0f + expf(-gv)) * uv;
   }
   *reinterpret_cast<uint4*>(xh + (size_t)(j0 / 64) * P * 128 + tc_tile_off(p, (j0 % 64) / 8)) = pack8(o);
@@ -123,14 +136,14 @@ __global__ void wide_swiglu_prep_kernel(const float* __restrict__ y, int F, int 
 
 }  // namespace
 
-int launch_wide_norm_prep(const float* d_y, float* d_h, int q, int H, const float* d_w, float eps, int P,
+int launch_wide_norm_prep(WideIn d_y, float* d_h, int q, int H, const float* d_w, float eps, int P,
                           uint8_t* d_xh, cudaStream_t st) {
   CLM_CHECK(H % 64 == 0 && H <= 8 * kNormThreads * kNormUnits, CLM_UNIMPLEMENTED, "wide window: hidden size");
   CLM_CHECK(q >= 1 && q <= P && P % 16 == 0, CLM_INVALID_ARGUMENT, "wide window: row count");
   return launch_pdl(wide_norm_prep_kernel, dim3(q), dim3(kNormThreads), 0, st, d_y, d_h, H, d_w, eps, P, d_xh);
 }
 
-int launch_wide_rope_kv(const float* d_y, int q, const LlamaDims& d, const float2* d_rope, const long long* d_pos,
+int launch_wide_rope_kv(WideIn d_y, int q, const LlamaDims& d, const float2* d_rope, const long long* d_pos,
                         const int32_t* d_pages, const int32_t* d_parent, __half* d_q16, __half* d_kpool,
                         __half* d_vpool, cudaStream_t st) {
   CLM_CHECK(d.hd % 16 == 0 && d.hd <= 256, CLM_UNIMPLEMENTED, "wide window: head dim");
@@ -138,7 +151,7 @@ int launch_wide_rope_kv(const float* d_y, int q, const LlamaDims& d, const float
                     d_rope, d_pos, d_pages, d_parent, d_q16, d_kpool, d_vpool);
 }
 
-int launch_wide_swiglu_prep(const float* d_y, int q, int F, int P, uint8_t* d_xh, cudaStream_t st) {
+int launch_wide_swiglu_prep(WideIn d_y, int q, int F, int P, uint8_t* d_xh, cudaStream_t st) {
   CLM_CHECK(F % 64 == 0, CLM_UNIMPLEMENTED, "wide window: ffn size");
   return launch_pdl(wide_swiglu_prep_kernel, dim3(q, (F + 511) / 512), dim3(64), 0, st, d_y, F, P, d_xh);
 }
