@@ -624,42 +624,56 @@ __global__ void __launch_bounds__(32 * (2 * kWideAttnHeads + 1), 1) attention_wi
   __syncthreads();
   const int qd = nh * HD;
   const int rows = hg * 16;  // this CTA's rows: m-tile j = row / 16
-  if (nsplit == 1) {
-    // combine the two halves of every m-tile into f32 rows
-    for (int idx = threadIdx.x; idx < rows * HD; idx += blockDim.x) {
-      const int j = idx / (16 * HD), r = (idx / HD) % 16, c = idx % HD;
-      const int rr = j * 16 + r, i = 16 * blk + rr / hg;
-      if (i >= qs) continue;
-      const float* a = parts + (size_t)(2 * j) * 16 * RW + r * RW;
-      const float* b = a + 16 * RW;
-      const float ma = a[HD], mb = b[HD];
-      const float M = fmaxf(ma, mb);
-      const float ea = ma == -INFINITY ? 0.0f : exp2f(ma - M), eb = mb == -INFINITY ? 0.0f : exp2f(mb - M);
-      const float L = a[HD + 1] * ea + b[HD + 1] * eb;
-      out[(size_t)(row0 + i) * qd + (h0 + rr % hg) * HD + c] = L > 0.0f ? (a[c] * ea + b[c] * eb) / L : 0.0f;
-    }
-    return;
-  }
-  // split KV: the halves combined into this split's partial (unnormalised O, max, sum) in global memory; the last
-  // split of the tile to arrive (counter) combines all of them, so no CTA waits for another
-  const int tile = (blockIdx.x * gridDim.y + blk) * (gridDim.z / nsplit) + seg;
-  float* tp = gpart + (size_t)tile * nsplit * rows * RW;
-  float* mine = tp + (size_t)split * rows * RW;
-  for (int idx = threadIdx.x; idx < rows * (HD + 2); idx += blockDim.x) {
-    const int rr = idx / (HD + 2), c = idx % (HD + 2), j = rr / 16, r = rr % 16;
+  constexpr int C4 = HD / 4;
+  // per row, once: the weights of the two halves (and, for a split, the combined max and sum)
+  __shared__ float s_wa[kWideAttnHeads * 16], s_wb[kWideAttnHeads * 16], s_M[kWideAttnHeads * 16],
+      s_L[kWideAttnHeads * 16];
+  __shared__ float s_wk[kWideAttnMaxSplits][kWideAttnHeads * 16];
+  if (threadIdx.x < rows) {
+    const int rr = threadIdx.x, j = rr / 16, r = rr % 16;
     const float* a = parts + (size_t)(2 * j) * 16 * RW + r * RW;
     const float* b = a + 16 * RW;
     const float ma = a[HD], mb = b[HD];
     const float M = fmaxf(ma, mb);
     const float ea = ma == -INFINITY ? 0.0f : exp2f(ma - M), eb = mb == -INFINITY ? 0.0f : exp2f(mb - M);
-    float v;
-    if (c < HD)
-      v = a[c] * ea + b[c] * eb;
-    else if (c == HD)
-      v = M;
-    else
-      v = a[HD + 1] * ea + b[HD + 1] * eb;
-    mine[(size_t)rr * RW + c] = v;
+    const float L = a[HD + 1] * ea + b[HD + 1] * eb;
+    const bool norm = nsplit == 1;
+    s_wa[rr] = norm ? (L > 0.0f ? ea / L : 0.0f) : ea;
+    s_wb[rr] = norm ? (L > 0.0f ? eb / L : 0.0f) : eb;
+    s_M[rr] = M;
+    s_L[rr] = L;
+  }
+  __syncthreads();
+  auto half_sum = [&](int rr, int c4) {
+    const int j = rr / 16, r = rr % 16;
+    const float4 x = *reinterpret_cast<const float4*>(parts + (size_t)(2 * j) * 16 * RW + r * RW + 4 * c4);
+    const float4 y = *reinterpret_cast<const float4*>(parts + (size_t)(2 * j + 1) * 16 * RW + r * RW + 4 * c4);
+    const float wa = s_wa[rr], wb = s_wb[rr];
+    return make_float4(x.x * wa + y.x * wb, x.y * wa + y.y * wb, x.z * wa + y.z * wb, x.w * wa + y.w * wb);
+  };
+  auto out_at = [&](int rr, int c4) -> float4* {
+    const int i = 16 * blk + rr / hg;
+    return reinterpret_cast<float4*>(out + (size_t)(row0 + i) * qd + (h0 + rr % hg) * HD + 4 * c4);
+  };
+  if (nsplit == 1) {
+    for (int idx = threadIdx.x; idx < rows * C4; idx += blockDim.x) {
+      const int rr = idx / C4, c4 = idx % C4;
+      if (16 * blk + rr / hg < qs) *out_at(rr, c4) = half_sum(rr, c4);
+    }
+    return;
+  }
+  // split KV: this split's partial (unnormalised O, max, sum) to global memory; the last split of the tile to
+  // arrive (counter) combines all of them, so no CTA waits for another
+  const int tile = (blockIdx.x * gridDim.y + blk) * (gridDim.z / nsplit) + seg;
+  float* tp = gpart + (size_t)tile * nsplit * rows * RW;
+  float* mine = tp + (size_t)split * rows * RW;
+  for (int idx = threadIdx.x; idx < rows * C4; idx += blockDim.x) {
+    const int rr = idx / C4, c4 = idx % C4;
+    *reinterpret_cast<float4*>(mine + (size_t)rr * RW + 4 * c4) = half_sum(rr, c4);
+  }
+  if (threadIdx.x < rows) {
+    mine[(size_t)threadIdx.x * RW + HD] = s_M[threadIdx.x];
+    mine[(size_t)threadIdx.x * RW + HD + 1] = s_L[threadIdx.x];
   }
   __threadfence();
   __syncthreads();
@@ -674,20 +688,31 @@ __global__ void __launch_bounds__(32 * (2 * kWideAttnHeads + 1), 1) attention_wi
   }
   __syncthreads();
   if (!s_last) return;
-  for (int idx = threadIdx.x; idx < rows * HD; idx += blockDim.x) {
-    const int rr = idx / HD, c = idx % HD, i = 16 * blk + rr / hg;
-    if (i >= qs) continue;
+  if (threadIdx.x < rows) {  // per row: the splits' weights e_k / sum_k(L_k e_k)
+    const int rr = threadIdx.x;
     float M = -INFINITY;
     for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(tp + ((size_t)k * rows + rr) * RW + HD));
-    float L = 0.0f, acc = 0.0f;
+    float L = 0.0f;
     for (int k = 0; k < nsplit; ++k) {
       const float* row = tp + ((size_t)k * rows + rr) * RW;
       const float mk = __ldcg(row + HD);
       const float e = mk == -INFINITY ? 0.0f : exp2f(mk - M);
+      s_wk[k][rr] = e;
       L += __ldcg(row + HD + 1) * e;
-      acc += __ldcg(row + c) * e;
     }
-    out[(size_t)(row0 + i) * qd + (h0 + rr % hg) * HD + c] = L > 0.0f ? acc / L : 0.0f;
+    for (int k = 0; k < nsplit; ++k) s_wk[k][rr] = L > 0.0f ? s_wk[k][rr] / L : 0.0f;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rows * C4; idx += blockDim.x) {
+    const int rr = idx / C4, c4 = idx % C4;
+    if (16 * blk + rr / hg >= qs) continue;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int k = 0; k < nsplit; ++k) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(tp + ((size_t)k * rows + rr) * RW) + c4);
+      const float w = s_wk[k][rr];
+      acc = make_float4(acc.x + v.x * w, acc.y + v.y * w, acc.z + v.z * w, acc.w + v.w * w);
+    }
+    *out_at(rr, c4) = acc;
   }
 }
 
