@@ -20,6 +20,8 @@ wide_window  128 window rows (8 sequences x 16 tree nodes) through the tcgen05 t
 prefill      a 4096-token prompt in 256-row windows through the engine (tcgen05 path): tokens/s, GEMM TFLOP/s
 tree_window  C4: a 16-node draft tree at context 4096 in Q8_0, batch 1 (GEMV chain) and batch 8 (eight sessions'
              trees in one 128-row window, clm_b200_run_batch_window): window time and HBM / tensor rooflines
+c5_stage     C5 per GPU: a middle stage of 10 layers of the 70B shape (Q4_K), q = 8 windows of boundary records at
+             context 8192, four sessions: window time and HBM roofline
 With N > 1 (torchrun, one process per GPU) the model is split into N pipeline stages (layer ranges balanced by
 the bytes each stage streams per round; the tail holds the LM head and the MTP drafter), joined by device links
 over NVLink, with N sequences in flight (--inflight) so that every stage is busy: weak scaling (each GPU streams
@@ -240,7 +242,7 @@ class CpuBaseline:
 
 
 # emitted tokens per round of the device arm on the bench workload (mean over 200 seeded rounds, measured on B200)
-REF_EMITTED_PER_ROUND = 1.515
+REF_EMITTED_PER_ROUND = 1.555
 
 
 def run_reference(args, world, rank):
@@ -432,6 +434,69 @@ def tree_micro(ctx, dev, peak, context):
                                   "unit": "TFLOP/s", "frac": bflops / bsec / 1e12 / tpeak, "peak_kind": tkind}}}
 
 
+# C5: one middle stage of the 70B shape in an 8-stage plan (10 of 80 layers, Q4_K), q = 8, batch 4, context 8192
+C5_LAYERS, C5_Q, C5_BATCH, C5_CONTEXT = 10, 8, 4, 8192
+
+
+def c5_micro(ctx, dev, peak):
+    """C5 per GPU: a middle stage holding 10 layers of the 70B shape (Q4_K) with four sessions at context 8192.
+    Each verify window (q = 8 boundary records in, records out, clm_b200_run_window_device) is event-timed on the
+    engine stream and dropped; batch 4 is the four sessions' windows one after another (each streams the stage's
+    weights)."""
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.engine import LLAMA3_70B, ROLE_MIDDLE, Engine
+
+    geo = LLAMA3_70B
+    H = geo.hidden
+    fpp = 2 * H + 1
+    eng = Engine(ctx, geo, 30, 30 + C5_LAYERS, ROLE_MIDDLE, C5_CONTEXT + 64, 16, C5_BATCH)
+    eng.generate_weights(seed=SEED, stddev=0.02)
+    eng.prepare()
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    gen = torch.Generator(device=dev).manual_seed(55)
+    rec = torch.zeros((16, fpp), dtype=torch.float32, device=dev)
+    rec[:, :H] = torch.randn((16, H), generator=gen, device=dev)
+    rec[:, 2 * H] = 1.0
+    out = torch.empty((16, fpp), dtype=torch.float32, device=dev)
+    for b in range(1, C5_BATCH + 1):
+        eng.open_session(b)
+        for off in range(0, C5_CONTEXT, 16):
+            eng.run_window_device(b, off, d_out=out, stream=stream.cuda_stream, d_records=rec)
+            eng.commit(b, 16)
+    times = []
+    for i in range(6):
+        per = []
+        for b in range(1, C5_BATCH + 1):
+            torch.cuda.synchronize(dev)
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            eng.run_window_device(b, C5_CONTEXT, d_out=out[:C5_Q], stream=stream.cuda_stream, d_records=rec[:C5_Q])
+            s1.record(stream)
+            torch.cuda.synchronize(dev)
+            eng.abort(b)
+            per.append(s0.elapsed_time(s1) / 1e3)
+        if i >= 2:
+            times.extend(per)
+    del rec, out
+    torch.cuda.synchronize(dev)
+    for b in range(1, C5_BATCH + 1):
+        eng.close_session(b)
+    eng.close()
+    sec = statistics.median(times)
+    qd, kvd, F = geo.n_heads * geo.head_dim, geo.n_kv_heads * geo.head_dim, geo.ffn
+    params = C5_LAYERS * ((qd + 2 * kvd) * H + H * qd + 3 * F * H)
+    weights = params * 144 // 256
+    kv = C5_LAYERS * 2 * C5_CONTEXT * kvd * 2
+    algo = weights + kv
+    return {"config": f"70B-shape middle stage: layers 30-39 of 80 (Q4_K), q={C5_Q} boundary records in and out, "
+                      f"context {C5_CONTEXT}, {C5_BATCH} sessions",
+            "ms_per_window": sec * 1e3, "batch4_ms": C5_BATCH * sec * 1e3,
+            "roofline": {"bound": "hbm", "algorithmic_bytes": algo, "weight_bytes": weights, "kv_bytes": kv,
+                         "achieved": algo / sec / 1e9, "peak": peak, "unit": "GB/s", "frac": algo / sec / 1e9 / peak}}
+
+
 def load_tensor_peak():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -618,6 +683,7 @@ def run_b200(args, world, rank, local):
     micro = acceptance_micro(ctx, dev, peak, not args.no_cpu) if (world == 1 and not profile_case(args)) else None
     tree = tree_micro(ctx, dev, peak, context) if (world == 1 and not profile_case(args)) else None
     wide = wide_micro(ctx, dev) if (world == 1 and not profile_case(args)) else None
+    c5 = c5_micro(ctx, dev, peak) if (world == 1 and not profile_case(args)) else None
     ctx.close()
 
     if rank != 0:
@@ -659,6 +725,8 @@ def run_b200(args, world, rank, local):
         line["wide_window"] = wide
     if prefill:
         line["prefill"] = prefill
+    if c5:
+        line["c5_stage"] = c5
     print(json.dumps(line), flush=True)
 
 
@@ -804,6 +872,8 @@ def run_micro(args):
         eng.close()
     elif args.micro == "tree":
         obj = tree_micro(ctx, dev, peak, args.context)
+    elif args.micro == "c5":
+        obj = c5_micro(ctx, dev, peak)
     else:
         obj = acceptance_micro(ctx, dev, peak, False)
     ctx.close()
@@ -822,7 +892,7 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
     ap.add_argument("--inflight", type=int, default=0, help="sequences in flight with N > 1 (default N)")
     ap.add_argument("--plan", default="", help="stage plan BEGIN-END@gK,... with N > 1 (default: byte-balanced)")
-    ap.add_argument("--micro", default="", choices=["", "wide", "accept", "prefill", "tree"],
+    ap.add_argument("--micro", default="", choices=["", "wide", "accept", "prefill", "tree", "c5"],
                     help="run one micro-benchmark alone and print its object (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
