@@ -73,6 +73,7 @@ _SIGS = {
     "clm_b200_commit": (_i, [_vp, _u64, _u32]),
     "clm_b200_run_tree_window": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "clm_b200_run_batch_window": (_i, [_vp, _u32, _vp, _vp, _u32, _vp, _vp, _vp]),
+    "clm_b200_llama_load_tensors": (_i, [_vp, _vp, _u32]),
     "clm_b200_commit_path": (_i, [_vp, _u64, _vp, _u32]),
     "clm_b200_run_tree_window_device": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "clm_b200_abort": (_i, [_vp, _u64]),

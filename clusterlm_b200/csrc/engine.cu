@@ -936,6 +936,130 @@ int llama_generate_weights(LlamaEngine* e, uint64_t seed, float stddev) {
   return rc;
 }
 
+// Binds this stage's weights from named host tensors in GGUF naming and block layout (llama.cpp's tensor names:
+// token_embd, blk.L.{attn_q,attn_k,attn_v,attn_output,ffn_gate,ffn_up,ffn_down,attn_norm,ffn_norm}, output_norm,
+// output, each with the ".weight" suffix; the MTP head as mtp.{ffn_gate,ffn_up,ffn_down,ffn_norm,output_norm}).
+// Matrices are in the engine's quantisation, norms f32; the same matrices are built as by llama_generate_weights.
+int llama_load_tensors(LlamaEngine* e, const clm_b200_tensor* t, uint32_t n) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(!e->weights_ready, CLM_FAILED_PRECONDITION, "weights already bound");
+  CLM_CHECK(t != nullptr || n == 0, CLM_INVALID_ARGUMENT, "null tensor list");
+  const LlamaDims& d = e->d;
+  cudaStream_t st = e->ctx->stream;
+  std::map<std::string, const clm_b200_tensor*> by;
+  for (uint32_t i = 0; i < n; ++i) {
+    CLM_CHECK(t[i].name != nullptr && (t[i].data != nullptr || t[i].bytes == 0), CLM_INVALID_ARGUMENT,
+              "tensor without a name or data");
+    by[t[i].name] = &t[i];
+  }
+  auto tbytes = [&](uint64_t m) { return clm_b200_tensor_bytes(d.quant, m); };
+  // one required tensor of `elems` elements in the engine's quantisation (f32 when `norm`)
+  auto find = [&](const std::string& name, uint64_t elems, bool norm, const clm_b200_tensor** out) -> int {
+    auto it = by.find(name);
+    if (it == by.end()) return fail(CLM_NOT_FOUND, ("tensor missing: " + name).c_str());
+    const clm_b200_tensor* x = it->second;
+    const int want = norm ? CLM_QUANT_F32 : d.quant;
+    if (x->quant != want)
+      return fail(CLM_UNIMPLEMENTED, ("tensor " + name + " is not in the engine's quantisation (norms: f32)").c_str());
+    const uint64_t want_bytes = norm ? elems * 4 : tbytes(elems);
+    if (x->bytes != want_bytes) return fail(CLM_DATA_LOSS, ("tensor " + name + " has the wrong size").c_str());
+    *out = x;
+    return CLM_OK;
+  };
+  uint64_t biggest = std::max<uint64_t>(tbytes((uint64_t)(d.qd() + 2 * d.kvd()) * d.H), tbytes((uint64_t)2 * d.F * d.H));
+  biggest = std::max<uint64_t>(biggest, tbytes((uint64_t)d.H * d.F));
+  if (e->has_head) biggest = std::max<uint64_t>(biggest, tbytes((uint64_t)d.V * d.H));
+  uint8_t* tmp = nullptr;
+  CLM_CUDA(cudaMalloc(&tmp, biggest));
+  int rc = CLM_OK;
+  // host bytes of tensors `parts` one after another into tmp
+  auto stage = [&](std::initializer_list<const clm_b200_tensor*> parts) -> int {
+    uint64_t off = 0;
+    for (const clm_b200_tensor* x : parts) {
+      const cudaError_t err = cudaMemcpyAsync(tmp + off, x->data, x->bytes, cudaMemcpyHostToDevice, st);
+      if (err != cudaSuccess) return cuda_fail(err, "tensor upload");
+      off += x->bytes;
+    }
+    const cudaError_t err = cudaStreamSynchronize(st);
+    return err == cudaSuccess ? CLM_OK : cuda_fail(err, "tensor upload");
+  };
+  auto norm = [&](const std::string& name, float** dst) -> int {
+    const clm_b200_tensor* x = nullptr;
+    int r = find(name, (uint64_t)d.H, true, &x);
+    if (r == CLM_OK) r = e->alloc_t(dst, (size_t)d.H);
+    if (r == CLM_OK) {
+      const cudaError_t err = cudaMemcpy(*dst, x->data, (size_t)d.H * 4, cudaMemcpyHostToDevice);
+      if (err != cudaSuccess) r = cuda_fail(err, "norm upload");
+    }
+    return r;
+  };
+  do {
+    const uint64_t H = d.H, qd = d.qd(), kvd = d.kvd(), F = d.F;
+    for (uint32_t L = e->spec.layer_begin; L < e->spec.layer_end && rc == CLM_OK; ++L) {
+      LlamaEngine::Layer lay;
+      const std::string b = "blk." + std::to_string(L) + ".";
+      const clm_b200_tensor *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr, *g = nullptr, *u = nullptr,
+                            *dn = nullptr;
+      if ((rc = find(b + "attn_q.weight", qd * H, false, &q)) || (rc = find(b + "attn_k.weight", kvd * H, false, &k)) ||
+          (rc = find(b + "attn_v.weight", kvd * H, false, &v)) ||
+          (rc = find(b + "attn_output.weight", H * qd, false, &o)) ||
+          (rc = find(b + "ffn_gate.weight", F * H, false, &g)) || (rc = find(b + "ffn_up.weight", F * H, false, &u)) ||
+          (rc = find(b + "ffn_down.weight", H * F, false, &dn)))
+        break;
+      if ((rc = stage({q, k, v})) ||
+          (rc = e->make_gemv(lay.qkv, tmp, tbytes((qd + 2 * kvd) * H), (uint32_t)(qd + 2 * kvd), (uint32_t)H)))
+        break;
+      if ((rc = stage({o})) || (rc = e->make_gemv(lay.o, tmp, tbytes(H * qd), (uint32_t)H, (uint32_t)qd))) break;
+      if ((rc = stage({g, u})) ||
+          (rc = e->make_gemv(lay.gu, tmp, tbytes(2 * F * H), (uint32_t)(2 * F), (uint32_t)H, (uint32_t)F)))
+        break;
+      if ((rc = stage({dn})) || (rc = e->make_gemv(lay.down, tmp, tbytes(H * F), (uint32_t)H, (uint32_t)F))) break;
+      if ((rc = norm(b + "attn_norm.weight", &lay.attn_norm)) || (rc = norm(b + "ffn_norm.weight", &lay.ffn_norm)))
+        break;
+      e->layers.push_back(lay);
+    }
+    if (rc) break;
+    const uint64_t VH = (uint64_t)d.V * d.H;
+    if (e->has_embd) {
+      const clm_b200_tensor* x = nullptr;
+      if ((rc = find("token_embd.weight", VH, false, &x))) break;
+      e->embd_bytes = x->bytes;
+      if ((rc = e->alloc((void**)&e->embd, e->embd_bytes))) break;
+      const cudaError_t err = cudaMemcpy(e->embd, x->data, x->bytes, cudaMemcpyHostToDevice);
+      if (err != cudaSuccess) {
+        rc = cuda_fail(err, "embedding upload");
+        break;
+      }
+      e->weight_bytes += e->embd_bytes;
+    }
+    if (e->has_head) {
+      const clm_b200_tensor* x = nullptr;
+      if ((rc = find("output.weight", VH, false, &x)) || (rc = stage({x})) ||
+          (rc = e->make_gemv(e->head, tmp, tbytes(VH), (uint32_t)d.V, (uint32_t)d.H)))
+        break;
+      if ((rc = norm("output_norm.weight", &e->out_norm))) break;
+    }
+    if (e->has_mtp) {
+      const uint64_t FH = (uint64_t)d.F * d.H;
+      const clm_b200_tensor *g = nullptr, *u = nullptr, *dn = nullptr;
+      if ((rc = find("mtp.ffn_gate.weight", FH, false, &g)) || (rc = find("mtp.ffn_up.weight", FH, false, &u)) ||
+          (rc = find("mtp.ffn_down.weight", FH, false, &dn)))
+        break;
+      if ((rc = stage({g, u})) ||
+          (rc = e->make_gemv(e->mtp_gu, tmp, tbytes(2 * FH), (uint32_t)(2 * d.F), (uint32_t)d.H, (uint32_t)d.F)))
+        break;
+      if ((rc = stage({dn})) || (rc = e->make_gemv(e->mtp_down, tmp, tbytes(FH), (uint32_t)d.H, (uint32_t)d.F)))
+        break;
+      if ((rc = norm("mtp.ffn_norm.weight", &e->mtp_ffn_norm)) || (rc = norm("mtp.output_norm.weight", &e->mtp_out_norm)))
+        break;
+    }
+  } while (false);
+  cudaStreamSynchronize(st);
+  cudaFree(tmp);
+  if (rc == CLM_OK) e->weights_ready = true;
+  return rc;
+}
+
 int llama_prepare(LlamaEngine* e) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->weights_ready, CLM_FAILED_PRECONDITION, "weights are not bound");

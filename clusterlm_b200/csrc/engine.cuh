@@ -22,6 +22,7 @@ FixtureEngine* as_fixture(clm_b200_engine* e);
 int llama_create(clm_b200_ctx* ctx, const clm_b200_llama_geometry* g, const clm_b200_stage_spec* spec,
                  clm_b200_engine** out);
 int llama_generate_weights(LlamaEngine* e, uint64_t seed, float stddev);
+int llama_load_tensors(LlamaEngine* e, const clm_b200_tensor* t, uint32_t n);
 int llama_prepare(LlamaEngine* e);
 int llama_info(const LlamaEngine* e, uint64_t* weight_bytes, uint64_t* state_bytes, uint32_t* fpp);
 int llama_session_open(LlamaEngine* e, uint64_t id);

@@ -43,6 +43,12 @@ int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float st
   return llama_generate_weights(llama(e), seed, stddev);
 }
 
+int clm_b200_llama_load_tensors(clm_b200_engine* e, const clm_b200_tensor* tensors, uint32_t n) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "GGUF tensors bind to Llama-family engines");
+  return llama_load_tensors(llama(e), tensors, n);
+}
+
 int clm_b200_engine_set_object(clm_b200_engine* e, const char* name, int quant, const void* h_bytes, uint64_t nbytes) {
   CLM_TRY(enter(e));
   CLM_CHECK(e->family == CLM_FAMILY_FIXTURE, CLM_UNIMPLEMENTED, "object binding is implemented for the fixture family");

@@ -121,6 +121,12 @@ class Engine:
     def generate_weights(self, seed: int = 0, stddev: float = 0.02):
         call("clm_b200_engine_generate_weights", self.h, seed, stddev)
 
+    def load_gguf(self, path: str):
+        """Binds this stage's weights from a GGUF file (clusterlm_b200.gguf_file; llama.cpp tensor names)."""
+        from .gguf_file import GGUFFile, load_into
+
+        load_into(self, GGUFFile(path))
+
     def prepare(self):
         call("clm_b200_engine_prepare", self.h)
 

@@ -188,6 +188,22 @@ CLM_API int clm_b200_engine_destroy(clm_b200_engine* e);
  * gate/up/down), encoded in the geometry's quant; norm weights are 1.  Replaces provisioning for tests and
  * benchmarks (random-init weights of the named architecture). */
 CLM_API int clm_b200_engine_generate_weights(clm_b200_engine* e, uint64_t seed, float stddev);
+/* One named host tensor: GGUF block bytes (quant = CLM_QUANT_Q4_K / CLM_QUANT_Q8_0) or f32 (CLM_QUANT_F32). */
+typedef struct {
+  const char* name;
+  int quant;
+  const void* data;
+  uint64_t bytes;
+} clm_b200_tensor;
+/* Binds this stage's weights from tensors in llama.cpp's GGUF names and block layout (the weights of a GGUF file;
+ * ClusterLM's GGUF manifests, runtime/objects/src/gguf_manifest.cpp, name the same tensors): token_embd.weight
+ * (prefix / whole), blk.L.{attn_q,attn_k,attn_v,attn_output,ffn_gate,ffn_up,ffn_down}.weight in the geometry's
+ * quant and blk.L.{attn_norm,ffn_norm}.weight in f32 for the stage's layers, output.weight + output_norm.weight
+ * (tail / whole), and for mtp = 1 the head mtp.{ffn_gate,ffn_up,ffn_down}.weight + mtp.{ffn_norm,output_norm}.weight.
+ * The host buffers are read during the call only.  CLM_NOT_FOUND names a missing tensor, CLM_DATA_LOSS a size
+ * that does not match the geometry, CLM_UNIMPLEMENTED another quantisation (a file must be quantised uniformly,
+ * e.g. llama-quantize --pure). */
+CLM_API int clm_b200_llama_load_tensors(clm_b200_engine* e, const clm_b200_tensor* tensors, uint32_t n);
 /* Allocates sequence state and window buffers (ExecutionDomain::prepare, execution_domain.hpp:150). */
 CLM_API int clm_b200_engine_prepare(clm_b200_engine* e);
 /* Resident weight bytes, per-session state bytes and boundary floats per position (hc*H + H + hc). */
