@@ -180,96 +180,171 @@ def sum_over_ranks(world, value, device):
 
 # --------------------------------------------------------------------------- CPU side (oracle)
 
-class CpuBaseline:
-    """The oracle's refmath-order CPU restatement of the round on this host, a bounded sample: one decoder
-    layer (q = 4 at context 4096, KV filled with random values), the LM head (q = 4) and one MTP step are
-    timed; a round is extrapolated as 32 layers + head + 3 MTP steps.  Weight bytes are random valid Q4_K
-    blocks (timing does not depend on their values)."""
+@dataclasses.dataclass(frozen=True)
+class Shape:
+    """The decoder shape of the workload (the GPU arm asserts it equals clusterlm_b200.engine.LLAMA3_8B).  Kept here
+    so that the reference arm never imports clusterlm_b200, which loads the CUDA library."""
+    n_layers: int = 32
+    hidden: int = 4096
+    n_heads: int = 32
+    n_kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 14336
+    vocab: int = 128256
+    rope_theta: float = 500000.0
+    rms_eps: float = 1e-5
 
-    def __init__(self, threads: int):
+
+SHAPE_8B = Shape()
+
+
+def bench_config(n_gpus: int, context: int, inflight: int = 1) -> dict:
+    """The workload description both arms print as `config` (identical for the same N)."""
+    return {"workload": f"llama3-8b-shape q4_k spec decode q={Q} ctx={context} mtp=1-layer T={TEMPERATURE:g}",
+            "q": Q, "context": context, "temperature": TEMPERATURE, "batch": 1,
+            "weights": "random-init N(0, 0.02) quantised to Q4_K", "parallelism": "single" if n_gpus == 1 else
+            f"pp{n_gpus}", "inflight": inflight,
+            "l2": "inputs larger than L2 (4.8 GB of weights streamed per round)"}
+
+
+class CpuRounds:
+    """Speculative rounds of the workload on the host cores: the oracle's restatement of the reference's refmath
+    order (f32 dot products in ascending order over Q4_K rows decoded one at a time) for the decoder layers, the LM
+    head and the MTP head, and its restatement of distribution / sample_from / verify_speculative for the draft
+    sampling and the acceptance.  A round is what the GPU arm's round is: 3 MTP drafts (each: the MTP block, the
+    head, distribution and a Philox-drawn sample), the 4-row verify window over all 32 layers and the head,
+    distribution of the 4 target rows and rejection-sampling acceptance, then the commit (the context grows by the
+    emitted tokens).  Weights come from the same counter-based generator as the GPU engine (seed 0, N(0, 0.02),
+    Q4_K); the KV context of 4096 positions holds seeded N(0, 1) values (a CPU prefill of 4096 tokens through
+    32 layers would take hours)."""
+
+    def __init__(self, threads: int, shape: Shape = SHAPE_8B, context: int = CONTEXT, max_rounds: int = 64):
+        import concurrent.futures as cf
+
         import numpy as np
 
-        from clusterlm_b200.engine import LLAMA3_8B
         from oracle.oracle_py import LlamaDims, Oracle
 
-        self.np = np
-        self.o = Oracle()
-        self.g = g = LLAMA3_8B
-        self.threads = threads
-        rng = np.random.default_rng(0)
-
-        def q4k(rows, cols):
-            b = rng.integers(0, 256, (rows * cols // 256, 144), dtype=np.uint8)
-            b[:, 0:4] = np.frombuffer(np.array([0x1400, 0x1400], np.uint16).tobytes(), np.uint8)  # d, dmin ~ 2^-10
-            return b.reshape(-1)
-
+        self.np, self.o, self.g, self.threads = np, Oracle(), shape, threads
+        g, o = shape, self.o
         H, qd, kvd, F, V = g.hidden, g.n_heads * g.head_dim, g.n_kv_heads * g.head_dim, g.ffn, g.vocab
-        self.wqkv, self.wo, self.wgu, self.wd = q4k(qd + 2 * kvd, H), q4k(H, qd), q4k(2 * F, H), q4k(H, F)
-        self.head = q4k(V, H)
+        t0 = time.perf_counter()
+        pool = cf.ThreadPoolExecutor(max_workers=threads)
+
+        def gen(tid, n):  # generate + encode in chunks of whole superblocks on all threads (ctypes drops the GIL)
+            chunk = 1 << 22
+            parts = list(pool.map(lambda f: o.encode("q4_k", o.gen_weights(SEED, tid, f, min(chunk, n - f), 0.02)),
+                                  range(0, n, chunk)))
+            return np.concatenate(parts)
+
+        self.layers = []
+        for L in range(g.n_layers):
+            i = 16 * L
+            self.layers.append((np.concatenate([gen(i, qd * H), gen(i + 1, kvd * H), gen(i + 2, kvd * H)]),
+                                gen(i + 3, H * qd), np.concatenate([gen(i + 4, F * H), gen(i + 5, F * H)]),
+                                gen(i + 6, H * F)))
+        self.head = gen(1001, V * H)
+        self.mtp = (np.concatenate([gen(1002, F * H), gen(1003, F * H)]), gen(1004, H * F))
+        pool.shutdown()
         self.ones = np.ones(H, np.float32)
-        self.kc = rng.standard_normal((CONTEXT + Q, kvd)).astype(np.float32)
-        self.vc = rng.standard_normal((CONTEXT + Q, kvd)).astype(np.float32)
         self.dims = LlamaDims(H, g.n_heads, g.n_kv_heads, g.head_dim, F, g.rope_theta, g.rms_eps)
+        rng = np.random.default_rng(4096)
+        cap = context + (Q + 1) * max_rounds + 8
+        self.kc = [np.zeros((cap, kvd), np.float32) for _ in range(g.n_layers)]
+        self.vc = [np.zeros((cap, kvd), np.float32) for _ in range(g.n_layers)]
+        for L in range(g.n_layers):
+            self.kc[L][:context] = rng.standard_normal((context, kvd), dtype=np.float32)
+            self.vc[L][:context] = rng.standard_normal((context, kvd), dtype=np.float32)
+        self.pos, self.cap = context, cap
+        self.next_token = int(rng.integers(0, V))
+        self.round_no = 0
+        self.setup_s = time.perf_counter() - t0
         self.parts = {}
 
-    def round_s(self) -> float:
+    def embed(self, tokens):
+        o, g = self.o, self.g
+        rows = [o.decode("q4_k", o.encode("q4_k", o.gen_weights(SEED, 1000, int(t) * g.hidden, g.hidden, 0.02)),
+                         g.hidden) for t in tokens]
+        return self.np.stack(rows).astype(self.np.float32)
+
+    def head_logits(self, h):
+        o, g = self.o, self.g
+        x = self.np.stack([o.rmsnorm(r, self.ones, g.rms_eps) for r in h])
+        return o.matmul_rows_quant("q4_k", self.head, g.vocab, g.hidden, x, self.threads)
+
+    def mtp_logits(self, prev: int):
         np, o, g = self.np, self.o, self.g
-        h = np.random.default_rng(1).standard_normal((Q, g.hidden)).astype(np.float32)
-        t0 = time.perf_counter()
-        o.llama_layer(self.dims, "q4_k", self.wqkv, self.wo, self.wgu, self.wd, self.ones, self.ones, self.kc,
-                      self.vc, CONTEXT, h, None, self.threads)
-        layer = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        o.matmul_rows_quant("q4_k", self.head, g.vocab, g.hidden, h, self.threads)
-        head = time.perf_counter() - t0
-        t0 = time.perf_counter()  # one MTP step: SwiGLU block over one row + the head over one row
-        x = h[:1]
-        y = o.matmul_rows_quant("q4_k", self.wgu, 2 * g.ffn, g.hidden, x, self.threads)
+        x = self.embed([prev])
+        xn = o.rmsnorm(x[0], self.ones, g.rms_eps)[None]
+        y = o.matmul_rows_quant("q4_k", self.mtp[0], 2 * g.ffn, g.hidden, xn, self.threads)[0]
         with np.errstate(over="ignore"):
-            a = (y[:, :g.ffn] / (1.0 + np.exp(-y[:, :g.ffn])) * y[:, g.ffn:]).astype(np.float32)
-        o.matmul_rows_quant("q4_k", self.wd, g.hidden, g.ffn, a, self.threads)
-        o.matmul_rows_quant("q4_k", self.head, g.vocab, g.hidden, x, self.threads)
-        mtp = time.perf_counter() - t0
-        self.parts = {"layer_s": layer, "head_s": head, "mtp_s": mtp}
-        return g.n_layers * layer + head + (Q - 1) * mtp
+            a = (y[:g.ffn] / (np.float32(1.0) + np.exp(-y[:g.ffn])) * y[g.ffn:]).astype(np.float32)
+        d = o.matmul_rows_quant("q4_k", self.mtp[1], g.hidden, g.ffn, a[None], self.threads)[0]
+        return self.head_logits((x[0] + d)[None])[0]
 
-    def sample_text(self, emitted_per_round: float) -> str:
+    def round(self) -> int:
+        """One speculative round; returns the emitted tokens (accepted drafts + 1)."""
+        np, o, g = self.np, self.o, self.g
+        if self.pos + Q + 1 > self.cap:
+            raise RuntimeError("CpuRounds: context capacity reached")
+        r = self.round_no
+        t0 = time.perf_counter()
+        win, dprobs = [self.next_token], []
+        for j in range(Q - 1):  # MTP drafts, sampled at T = 1
+            p = o.distribution(self.mtp_logits(win[-1]), TEMPERATURE)
+            dprobs.append(p)
+            win.append(o.sample_from(p, o.philox_uniform(SEED, j, 1, r & 0xFFFFFFFF, r >> 32)))
+        t1 = time.perf_counter()
+        h = self.embed(win)
+        for L, (wqkv, wo, wgu, wd) in enumerate(self.layers):
+            o.llama_layer(self.dims, "q4_k", wqkv, wo, wgu, wd, self.ones, self.ones, self.kc[L], self.vc[L],
+                          self.pos, h, None, self.threads)
+        logits = self.head_logits(h)
+        t2 = time.perf_counter()
+        P = np.stack([o.distribution(row, TEMPERATURE) for row in logits])
+        us = np.array([o.philox_uniform(SEED, n, 0, r & 0xFFFFFFFF, r >> 32) for n in range(Q)])
+        acc, nxt, _ = o.verify(P, np.array(win[1:], np.int32), np.stack(dprobs), us)
+        t3 = time.perf_counter()
+        self.pos += acc + 1  # commit: the accepted window rows stay in the caches
+        self.next_token = int(nxt)
+        self.round_no += 1
+        self.parts = {"draft_s": t1 - t0, "window_s": t2 - t1, "accept_s": t3 - t2}
+        return acc + 1
+
+    def sample_text(self, rounds: int, emitted: int) -> str:
         p = self.parts
-        return (f"oracle (refmath-order f32 dot products over Q4_K rows decoded one at a time), {self.threads} "
-                f"threads: 1 decoder layer at context {CONTEXT} ({p['layer_s']:.3f} s), LM head q={Q} "
-                f"({p['head_s']:.3f} s), 1 MTP step ({p['mtp_s']:.3f} s) timed; round = {self.g.n_layers} layers + "
-                f"head + {Q - 1} MTP steps (extrapolated); {emitted_per_round:.3f} emitted tokens per round")
-
-
-# emitted tokens per round of the device arm on the bench workload (mean over 200 seeded rounds, measured on B200)
-REF_EMITTED_PER_ROUND = 1.555
+        return (f"oracle port (refmath-order f32 dot products over Q4_K rows decoded one at a time; double-precision "
+                f"distribution / verify_speculative), {self.threads} threads: {rounds} full speculative rounds "
+                f"(3 MTP drafts, 32-layer q={Q} window + LM head, acceptance, commit) from context {CONTEXT}, "
+                f"{emitted} tokens emitted; last round draft {p.get('draft_s', 0):.2f} s, window "
+                f"{p.get('window_s', 0):.2f} s, acceptance {p.get('accept_s', 0):.2f} s; weights generated in "
+                f"{self.setup_s:.1f} s (untimed)")
 
 
 def run_reference(args, world, rank):
-    """The reference arm: the reference has no Llama-family code (its llama path is un-vendored llama.cpp),
-    so this times the oracle port of its refmath-order CPU math on all host threads, one bounded sample
-    (one layer + head + one MTP step, extrapolated to a round) per step."""
+    """The reference arm: ClusterLM has no Llama-family CPU code of its own (its llama path is the un-vendored
+    llama.cpp), so this runs the oracle's restatement of its refmath-order math on all host threads: W untimed and
+    K timed full speculative rounds (CpuRounds), tokens counted from its own acceptance."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cpu = CpuBaseline(threads)
-    warm = 3  # untimed samples (each is seconds of CPU work)
-    for _ in range(warm):
-        cpu.round_s()
-    steps = max(1, min(args.steps, 5))
-    per_step = [cpu.round_s() for _ in range(steps)]
-    sec = statistics.median(per_step)
-    # tokens per round: the device arm's measured mean on this workload (same seeds), so that both arms count the
-    # same accepted drafts; this arm does not run the acceptance itself
-    value = REF_EMITTED_PER_ROUND / sec
+    cpu = CpuRounds(threads, max_rounds=args.warmup + args.steps + 2)
+    for _ in range(args.warmup):
+        cpu.round()
+    t0 = time.perf_counter()
+    emitted = sum(cpu.round() for _ in range(args.steps))
+    sec = time.perf_counter() - t0
+    value = emitted / sec
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": warm, "ms_per_step": sec * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec / args.steps * 1e3,
+        "ms_per_round": sec / args.steps * 1e3, "emitted_per_round": emitted / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama3-8b-shape q4_k spec decode q=4 ctx=4096 batch=1", "q": Q, "context": CONTEXT},
+        "config": bench_config(args.gpus, CONTEXT, args.inflight or args.gpus if args.gpus > 1 else 1),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": cpu.sample_text(REF_EMITTED_PER_ROUND)},
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                         "sample": cpu.sample_text(args.steps, emitted)},
+        "e2e": {"value": value, "unit": "tok/s", "ms_per_round": sec / args.steps * 1e3, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -597,6 +672,33 @@ def prefill_micro(eng, geo, dev, stream, context, rng):
                          "peak_kind": kind, "gemm_flops": flops}}
 
 
+# DRAM bytes (read + write) of one verify window (32 layers + head, q = 4, context 4096) from an ncu capture of
+# every kernel of one window, keyed by layer count; the capture and its command are summarised under profiles/
+WINDOW_TRAFFIC: dict = {}
+
+
+def c1_fixture():
+    """C1 (the reference's own fixture model, 4-stage plan, q = 4, ScriptedDrafter corruption 0.3, 32 new tokens):
+    the reference's ReferenceDomain pipeline (its own compiled CPU code, 1 thread per stage) against the b200
+    pipeline (the product's C++ backend behind the same ExecutionDomain interface), both driven in one process by
+    the drop-in parity driver built from the reference sources.  None when the driver is not built."""
+    import tempfile
+
+    exe = os.path.join(ROOT, "oracle", "_ref", "backend_parity")
+    if not os.path.exists(exe):
+        return None
+    with tempfile.TemporaryDirectory() as d:
+        r = subprocess.run([exe, d, "--bench"], capture_output=True, text=True, timeout=600)
+    for ln in r.stdout.splitlines():
+        if ln.startswith("{"):
+            o = json.loads(ln)
+            o["config"] = ("clusterlm-fixture default spec (16 layers, H 64, hc 4, 32 experts top-4, V 256), plan "
+                           "0-4|4-10|10-13|13-16 in one process, q=4, ScriptedDrafter corruption 0.3, 32 new tokens")
+            o["parity_failures"] = r.returncode
+            return o
+    return {"error": (r.stdout + r.stderr)[-300:]}
+
+
 def run_b200(args, world, rank, local):
     import numpy as np
     import torch
@@ -606,25 +708,30 @@ def run_b200(args, world, rank, local):
 
     torch.cuda.set_device(local)
     dev = torch.device(f"cuda:{local}")
+    assert all(getattr(LLAMA3_8B, f.name) == getattr(SHAPE_8B, f.name) for f in dataclasses.fields(Shape))
     geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
     context = args.context
     ctx = Context(local)
-    max_ctx = context + (args.warmup + args.steps + 8) * (Q + 1) + 64
+    n_rounds = args.warmup + args.steps
+    max_ctx = context + (n_rounds + 8) * (Q + 1) + 64
     # windows of up to 256 rows: the prompt is prefilled in 256-row windows on the tensor-core path (the profile
     # case keeps 16-row prefill windows, so its launch list matches the recorded ncu skip counts)
     wmax = 16 if profile_case(args) else PREFILL_CHUNK
-    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, wmax, 2)
+    # sessions: 1 the device-resident rounds, 3 the same rounds through the host API (same prompt and seed, so the
+    # same emitted tokens), 2 the prefill measurement
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, max_ctx, wmax, 3)
     eng.generate_weights(seed=SEED, stddev=0.02)
     eng.prepare()
-    eng.open_session(1)
     rng = np.random.default_rng(1234 + rank)
     prompt = rng.integers(0, geo.vocab, context).astype(np.int32)
     t0 = time.perf_counter()
-    eng.spec_begin(1, prompt, Q, temperature=TEMPERATURE, seed=SEED)
-    prefill_s = time.perf_counter() - t0
+    for sid in (1, 3):
+        eng.open_session(sid)
+        eng.spec_begin(sid, prompt, Q, temperature=TEMPERATURE, seed=SEED)
+    prefill_s = (time.perf_counter() - t0) / 2
     stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
-    counts = torch.zeros(args.warmup + args.steps, dtype=torch.int32, device=dev)
-    toks = torch.zeros((args.warmup + args.steps, Q + 1), dtype=torch.int32, device=dev)
+    counts = torch.zeros(n_rounds, dtype=torch.int32, device=dev)
+    toks = torch.zeros((n_rounds, Q + 1), dtype=torch.int32, device=dev)
     for i in range(args.warmup):
         eng.spec_round_device(1, Q, TEMPERATURE, SEED, toks[i], counts[i], stream.cuda_stream)
     torch.cuda.synchronize(dev)
@@ -634,7 +741,7 @@ def run_b200(args, world, rank, local):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize(dev)
     start.record(stream)
-    for i in range(args.warmup, args.warmup + args.steps):
+    for i in range(args.warmup, n_rounds):
         eng.spec_round_device(1, Q, TEMPERATURE, SEED, toks[i], counts[i], stream.cuda_stream)
     end.record(stream)
     torch.cuda.synchronize(dev)
@@ -646,17 +753,23 @@ def run_b200(args, world, rank, local):
     emitted_all = sum_over_ranks(world, emitted, dev)
     value = emitted_all / elapsed_max
 
-    # e2e: host API, parameters in / tokens out every round
+    # e2e: the same W + K rounds on session 3 through the host API (round parameters host -> device and the emitted
+    # tokens device -> host every round, synchronised); the K rounds after the warm-up are timed on the host
     barrier(world)
     torch.cuda.synchronize(dev)
-    e2e_n = max(4, args.steps // 2)
+    host_tokens = []
+    for _ in range(args.warmup):
+        host_tokens.append(eng.spec_round(3, Q, TEMPERATURE, SEED))
     t0 = time.perf_counter()
-    e_emitted = 0
-    for _ in range(e2e_n):
-        e_emitted += eng.spec_round(1, Q, TEMPERATURE, SEED).size
+    for _ in range(args.steps):
+        host_tokens.append(eng.spec_round(3, Q, TEMPERATURE, SEED))
     e2e_s = time.perf_counter() - t0
+    e_emitted = sum(t.size for t in host_tokens[args.warmup:])
+    dev_tokens = [toks[i, :int(counts[i])].cpu().numpy() for i in range(n_rounds)]
+    e2e_same = all(np.array_equal(a, b) for a, b in zip(host_tokens, dev_tokens))
     e2e_s = max_over_ranks(world, e2e_s, dev)
     e2e_value = sum_over_ranks(world, e_emitted, dev) / e2e_s
+    eng.close_session(3)
 
     # verify-window roofline: one q = 4 window through the public window call, event-timed
     total_b, weight_b, kv_b = window_bytes(geo, context)
@@ -688,35 +801,46 @@ def run_b200(args, world, rank, local):
 
     if rank != 0:
         return
-    cpu = None
     profile = profile_case(args)
+    cpu, c1 = None, None
     if world == 1 and not args.no_cpu and not profile:
-        cb = CpuBaseline(os.cpu_count() or 1)
-        r = cb.round_s()
-        cpu = {"value": (emitted / args.steps) / r, "cores": cb.threads, "sample": cb.sample_text(emitted / args.steps)}
+        cr = CpuRounds(os.cpu_count() or 1, max_rounds=4)
+        cr.round()  # untimed
+        t0 = time.perf_counter()
+        n_cpu = 2
+        cpu_emitted = sum(cr.round() for _ in range(n_cpu))
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": cpu_emitted / cpu_s, "unit": "tok/s", "cores": cr.threads, "kind": "port",
+               "ms_per_round": cpu_s / n_cpu * 1e3, "sample": cr.sample_text(n_cpu, cpu_emitted)}
+        del cr
+        c1 = c1_fixture()
+    config = bench_config(world, context)
+    if profile:
+        config["workload"] += f" PROFILE CASE ({geo.n_layers} layers)"
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3,
+        "ms_per_round": elapsed_max / args.steps * 1e3, "emitted_per_round": emitted / args.steps,
+        "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
         "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
-        "config": {"workload": (f"llama3-8b-shape q4_k spec decode q=4 ctx={context} batch=1 mtp=1-layer T=1"
-                                + (f" PROFILE CASE ({geo.n_layers} layers)" if profile else "")),
-                   "q": Q, "context": context, "temperature": TEMPERATURE,
-                   "parallelism": "single",
-                   "l2": "inputs larger than L2 (4.8 GB weights streamed per round)",
-                   "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted / args.steps},
-        "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": (Q + 1) * 4 + 4},
+        "config": config,
+        "prefill_s": round(prefill_s, 2),
+        "e2e": {"value": e2e_value, "unit": "tok/s", "ms_per_round": e2e_s / args.steps * 1e3,
+                "rounds": args.steps, "same_tokens_as_device_rounds": bool(e2e_same),
+                "h2d_bytes_per_step": 16, "d2h_bytes_per_step": (Q + 1) * 4 + 4},
         "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_kind": peak_kind,
+                     "traffic": WINDOW_TRAFFIC.get(geo.n_layers), "peak_kind": peak_kind,
                      "kernel": f"verify window q=4 ({geo.n_layers} layers + head)",
                      "algorithmic_bytes": total_b, "weight_bytes": weight_b, "kv_bytes": kv_b,
                      "window_ms": window_s * 1e3},
         "clocks": clk,
     }
     if cpu:
-        line["cpu_baseline"] = {"value": cpu["value"], "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
-                                "sample": cpu["sample"]}
+        line["cpu_baseline"] = cpu
+    if c1:
+        line["c1_fixture"] = c1
     if micro:
         line["acceptance_micro"] = micro
     if tree:
@@ -745,7 +869,7 @@ def run_pipeline(args, world, rank, local):
     context = args.context
     S = args.inflight or world
     plan = parse_plan(args.plan, geo.n_layers) if args.plan else plan_stages(geo, world, Q, context)
-    e2e_n = max(4, args.steps // 2)
+    e2e_n = args.steps  # the e2e leg runs as many rounds as the timed loop
     max_ctx = context + (args.warmup + args.steps + e2e_n + 8) * (Q + 1) + 64
     ctx = Context(local)
 
@@ -827,14 +951,12 @@ def run_pipeline(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
         "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
-        "config": {"workload": (f"llama3-8b-shape q4_k spec decode q=4 ctx={context} mtp=1-layer T=1, "
-                                f"{world}-stage pipeline, {S} sequences in flight"
-                                + (f" PROFILE CASE ({geo.n_layers} layers)" if profile_case(args) else "")),
-                   "q": Q, "context": context, "temperature": TEMPERATURE, "parallelism": f"pp{world}",
-                   "plan": format_plan(plan), "inflight": S, "step": f"one round of each of the {S} sequences",
-                   "l2": "inputs larger than L2 (each stage streams its weights every round)",
-                   "prefill_s": round(prefill_s, 2), "accepted_per_round": emitted_all / (args.steps * S)},
-        "e2e": {"value": e2e_emitted / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16 * S * world,
+        "config": bench_config(world, context, S),
+        "plan": format_plan(plan), "step": f"one round of each of the {S} sequences",
+        "ms_per_round": elapsed_max / (args.steps * S) * 1e3, "emitted_per_round": emitted_all / (args.steps * S),
+        "prefill_s": round(prefill_s, 2),
+        "e2e": {"value": e2e_emitted / e2e_s, "unit": "tok/s", "ms_per_round": e2e_s / (e2e_n * S) * 1e3,
+                "h2d_bytes_per_step": 16 * S * world,
                 "d2h_bytes_per_step": ((Q + 1) * 4 + 4) * S},
         "gpu_launches": int(launches_all),
         "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,

@@ -20,6 +20,7 @@ ERROR_NAMES = {
     19: "kHardwareUnavailable",
 }
 QUANTS = {"f32": 0, "q8_0-fixture": 1, "q8_0": 2, "q4_k": 3}
+CLM_UNIMPLEMENTED = 18
 
 
 class ClmError(RuntimeError):

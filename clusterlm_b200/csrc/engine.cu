@@ -226,6 +226,9 @@ struct LlamaEngine : clm_b200_engine {
   float* part = nullptr;     // GEMV split partials (last-CTA reduction)
   int* gcount = nullptr;     // GEMV row-group counters
   int* acount = nullptr;     // attention (m-tile, kv head) counters
+  size_t gcount_n = 0, acount_n = 0;  // their lengths (reset_counters)
+  void* samp_counters = nullptr;      // the sampling scratch's arrival counters and their bytes
+  size_t samp_counter_bytes = 0;
   XBuf xa, xb;               // activation hand-offs, alternated along the chain
   float* ones_h = nullptr;   // norm weight 1 for stage ends without a following norm
   __half* q16 = nullptr;
@@ -744,12 +747,25 @@ struct LlamaEngine : clm_b200_engine {
     return CLM_OK;
   }
 
+  // Zeroes every arrival counter of the split reductions.  A reduction resets its counter only after a wait that
+  // succeeded, so after a bounded wait gave up the counters may hold arrivals of the failed launch; without this a
+  // later window (or graph replay) would pass its waits early and sum stale partials.  The stream is idle here.
+  int reset_counters() {
+    if (gcount) CLM_CUDA(cudaMemset(gcount, 0, gcount_n * sizeof(int)));
+    if (acount) CLM_CUDA(cudaMemset(acount, 0, acount_n * sizeof(int)));
+    if (wattn_cnt) CLM_CUDA(cudaMemset(wattn_cnt, 0, (size_t)wattn_tiles * sizeof(int)));
+    if (samp_counters) CLM_CUDA(cudaMemset(samp_counters, 0, samp_counter_bytes));
+    if (mk_bar) CLM_CUDA(cudaMemset(mk_bar, 0, sizeof(unsigned)));
+    return CLM_OK;
+  }
+
   int check_bad(cudaStream_t st) {
     int b = 0;
     CLM_CUDA(cudaMemcpyAsync(&b, bad, sizeof(int), cudaMemcpyDeviceToHost, st));
     CLM_CUDA(cudaStreamSynchronize(st));
     if (b) {
       CLM_CUDA(cudaMemset(bad, 0, sizeof(int)));
+      CLM_TRY(reset_counters());
       if (b == kErrWaitTimeout) return fail(CLM_DEADLINE_EXCEEDED, "a bounded device wait gave up (copy never completed)");
       if (b == kErrPartialSlots) return fail(CLM_INTERNAL, "a split reduction needed more partial slots than planned");
       if (b == kErrLinkTimeout)
@@ -959,6 +975,10 @@ int llama_load_tensors(LlamaEngine* e, const clm_b200_tensor* t, uint32_t n) {
     if (it == by.end()) return fail(CLM_NOT_FOUND, ("tensor missing: " + name).c_str());
     const clm_b200_tensor* x = it->second;
     const int want = norm ? CLM_QUANT_F32 : d.quant;
+    if (x->quant < 0)  // a ggml type without a CLM representation (ggml type -1 - quant), e.g. Q6_K
+      return fail(CLM_UNIMPLEMENTED, ("tensor " + name + " is in ggml type " + std::to_string(-1 - x->quant) +
+                                      ", which the engine does not bind (Q4_K, Q8_0 matrices; f32 norms)")
+                                         .c_str());
     if (x->quant != want)
       return fail(CLM_UNIMPLEMENTED, ("tensor " + name + " is not in the engine's quantisation (norms: f32)").c_str());
     const uint64_t want_bytes = norm ? elems * 4 : tbytes(elems);
@@ -1034,7 +1054,10 @@ int llama_load_tensors(LlamaEngine* e, const clm_b200_tensor* t, uint32_t n) {
     }
     if (e->has_head) {
       const clm_b200_tensor* x = nullptr;
-      if ((rc = find("output.weight", VH, false, &x)) || (rc = stage({x})) ||
+      // files whose head shares the token embedding's weights have no output.weight (llama.cpp then uses
+      // token_embd.weight as the head)
+      const char* head_name = by.count("output.weight") ? "output.weight" : "token_embd.weight";
+      if ((rc = find(head_name, VH, false, &x)) || (rc = stage({x})) ||
           (rc = e->make_gemv(e->head, tmp, tbytes(VH), (uint32_t)d.V, (uint32_t)d.H)))
         break;
       if ((rc = norm("output_norm.weight", &e->out_norm))) break;
@@ -1092,8 +1115,10 @@ int llama_prepare(LlamaEngine* e) {
   CLM_TRY(e->alloc_t(&e->part, part_floats));
   CLM_TRY(e->alloc_t(&e->gcount, max_ng));
   CLM_CUDA(cudaMemset(e->gcount, 0, max_ng * sizeof(int)));
+  e->gcount_n = max_ng;
   CLM_TRY(e->alloc_t(&e->acount, (size_t)2 * mtiles * d.nkv));  // attention arrival + departure counters
   CLM_CUDA(cudaMemset(e->acount, 0, (size_t)2 * mtiles * d.nkv * sizeof(int)));
+  e->acount_n = (size_t)2 * mtiles * d.nkv;
   for (XBuf* x : {&e->xa, &e->xb}) {
     CLM_TRY(e->alloc((void**)&x->frag, xfrag_bytes(maxcols, 2)));
     CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));
@@ -1195,6 +1220,8 @@ int llama_prepare(LlamaEngine* e) {
     CLM_TRY(e->alloc(&sbase, sbytes));
     e->samp = SampleScratch::carve(sbase, 2 * W, 1, d.V);
     CLM_CUDA(cudaMemset(sbase, 0, e->samp.counter_bytes));
+    e->samp_counters = sbase;
+    e->samp_counter_bytes = e->samp.counter_bytes;
   }
   CLM_TRY(e->alloc_t(&e->acc, 1));
   CLM_TRY(e->alloc_t(&e->nxt, 1));

@@ -387,8 +387,19 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
   consumer_sync();
   int seg = 0, nseg = 1;
   group_segments((long long)grp * ppr, (long long)grp * ppr + ppr - 1, U, G, u0, &seg, &nseg);
+  // A row group that cannot be reduced (too few partial slots, or a wait that gave up) raises the error flag; a
+  // plain product (EPI_STORE) also writes its rows as NaN, so a caller without an error flag never reads stale or
+  // partial sums as a result.
+  auto fail_group = [&](int code) {
+    if (tid == 0 && epi.err && code) atomicExch(epi.err, code);
+    if (epi_kind == EPI_STORE)
+      for (int i = tid; i < q * 128; i += kG4Consumers) {
+        const int p = i / 128, r = i % 128;
+        if (grp * 128 + r < (int)rows) epi.out[(size_t)p * epi.out_ld + grp * 128 + r] = __int_as_float(0x7fc00000);
+      }
+  };
   if (nseg > maxseg) {  // partial slots too few for this launch shape: never write past them
-    if (tid == 0 && epi.err) atomicExch(epi.err, kErrPartialSlots);
+    fail_group(kErrPartialSlots);
     return;
   }
   if (nseg > 1) {
@@ -407,7 +418,10 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
       *s_last = ok;
     }
     consumer_sync();
-    if (!*s_last) return;
+    if (!*s_last) {
+      fail_group(0);  // wait_count raised the flag
+      return;
+    }
     const float* all = part + (size_t)grp * maxseg * q * 128;
     for (int i = tid; i < q * 128; i += kG4Consumers) {
       float a = y[i];

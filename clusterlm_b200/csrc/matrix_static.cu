@@ -2,12 +2,14 @@
 // scratch in one fixed device array compiled into this library, so that the call allocates no device memory.
 //
 // Scratch layout inside g_matmul_scratch (offsets 256-byte aligned):
-//   [0, kCounterBytes)   split-reduction counters, one int per 128-row group.  They MUST be zero when a call
-//                        starts: static __device__ storage is zero when the module loads, and the last CTA of
-//                        each row group writes its counter back to 0, so every completed call leaves them zero.
-//                        Nothing else in the array needs any initial value.
+//   [0, kCounterBytes)   split-reduction counters, one int per 128-row group, and after them one error word.  They
+//                        must be zero when the product starts, so every call clears them first (an asynchronous
+//                        memset of the array, no allocation): a call whose bounded wait gave up leaves arrivals
+//                        behind, and the next call must not pass its waits on them.
 //   then                 activation fragments, sub-block sums, split partials (written before they are read
 //                        within the same call).
+// A row group whose split reduction gave up is written as NaN (the call itself has already returned CLM_OK: it
+// only enqueues work).
 // One array per device: two calls whose kernels overlap on the same device (different streams, or different
 // threads without ordering) race on it and give wrong results.  Callers serialise calls per device.
 // The first call on a device resolves the array's address with cudaGetSymbolAddress (with that device current)
@@ -21,7 +23,8 @@ namespace clm {
 namespace {
 
 constexpr size_t kStaticScratchBytes = CLM_B200_STATIC_SCRATCH_BYTES;
-constexpr size_t kCounterBytes = 16 * 1024;  // 4096 row groups = 524,288 rows
+constexpr size_t kCounterBytes = 16 * 1024;
+constexpr size_t kMaxGroups = kCounterBytes / sizeof(int) - 64;  // 4032 row groups = 516,096 rows; then the error word
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_matmul_scratch[kStaticScratchBytes];
@@ -52,8 +55,8 @@ int matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float*
     return launch_gemv_f32(static_cast<const float*>(w->data), w->rows, w->cols, d_x, q, d_y, st);
   const GemvShape& s = w->shape;
   const GemvPlan p = gemv_plan(s, q, ctx->sm_count);
-  CLM_CHECK((size_t)s.ng * sizeof(int) <= kCounterBytes, CLM_OUT_OF_RANGE,
-            "matrix has more row groups than the static scratch's counters cover (rows <= 524288)");
+  CLM_CHECK((size_t)s.ng <= kMaxGroups, CLM_OUT_OF_RANGE,
+            "matrix has more row groups than the static scratch's counters cover (rows <= 516096)");
   const size_t fb = align256(xfrag_bytes((int)s.cols, p.nt)), sb = align256(xsum_bytes((int)s.cols));
   const size_t pb = align256((size_t)s.ng * p.ksplit * q * 128 * sizeof(float));
   const size_t need = kCounterBytes + fb + sb + pb;
@@ -64,6 +67,7 @@ int matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float*
   CLM_TRY(static_scratch(ctx->device, &scratch));
   uint8_t* base = static_cast<uint8_t*>(scratch);
   int* counters = reinterpret_cast<int*>(base);
+  CLM_CUDA(cudaMemsetAsync(counters, 0, (kMaxGroups + 1) * sizeof(int), st));
   XBuf in;
   in.frag = reinterpret_cast<uint2*>(base + kCounterBytes);
   in.sum = reinterpret_cast<float*>(base + kCounterBytes + fb);
@@ -74,6 +78,7 @@ int matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float*
   e.kind = EPI_STORE;
   e.out = d_y;
   e.out_ld = s.rows;
+  e.err = counters + kMaxGroups;
   return launch_gemv(s, p, static_cast<const uint8_t*>(w->data), in, q, e, part, counters, st);
 }
 

@@ -14,7 +14,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._native import QUANTS, call
+from ._native import CLM_UNIMPLEMENTED, QUANTS, ClmError, call
 from .engine import LlamaGeometry
 
 # ggml tensor types this engine binds, and their (block elements, block bytes)
@@ -124,6 +124,14 @@ def llama_geometry(f: GGUFFile) -> LlamaGeometry:
     q = f.tensors["blk.0.attn_q.weight"].ggml_type
     if q not in _QUANT_NAME:
         raise ValueError(f"{f.path}: matrices in ggml type {q}; the engine binds Q4_K or Q8_0")
+    # RoPE frequency scaling (Llama 3.1+ files carry rope_freqs.weight; others a rope.scaling.type) changes the
+    # rotation llama.cpp applies; the engine's RoPE table is the plain theta^(-2i/hd) one, so such files are refused
+    # rather than run with different logits
+    if "rope_freqs.weight" in f.tensors:
+        raise ClmError(CLM_UNIMPLEMENTED, f"{f.path}: rope_freqs.weight (RoPE frequency factors) is not supported")
+    scaling = f.kv.get(key("rope.scaling.type"), "none")
+    if scaling not in ("none", ""):
+        raise ClmError(CLM_UNIMPLEMENTED, f"{f.path}: RoPE scaling '{scaling}' is not supported")
     return LlamaGeometry(
         n_layers=int(f.kv[key("block_count")]), hidden=H, n_heads=nh, n_kv_heads=nkv, head_dim=hd,
         ffn=int(f.kv[key("feed_forward_length")]), vocab=int(f.tensors["token_embd.weight"].dims[1]),
@@ -144,6 +152,10 @@ def load_into(engine, f: GGUFFile) -> None:
     n = 0
     for name, info in f.tensors.items():
         if info.ggml_type not in _TO_CLM:
+            # passed without data and with no CLM quantisation: the engine refuses it by name (CLM_UNIMPLEMENTED)
+            # if its stage needs it, and ignores it otherwise
+            arr[n] = _Tensor(name.encode(), -1 - info.ggml_type, None, 0)
+            n += 1
             continue
         buf = np.ascontiguousarray(f.data(name))
         keep.append(buf)

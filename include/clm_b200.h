@@ -107,9 +107,10 @@ CLM_API int clm_b200_matmul_rows(clm_b200_ctx* ctx, const clm_b200_matrix* w, co
  * cudaMalloc).  No reference counterpart: the reference's CPU matmul needs no device scratch.  For callers
  * that must not allocate once admitted, e.g. a domain whose device memory is fully leased at prepare.
  * CLM_RESOURCE_EXHAUSTED when the matrix/positions need more scratch than the array holds (then use
- * clm_b200_matmul_rows); CLM_OUT_OF_RANGE for more than 524,288 rows.  One array per device: calls whose kernels
- * overlap on one device race on it, so serialise them per device.  The first call on a device resolves the
- * array's address (set-up); make it before any stream capture meant to contain later calls. */
+ * clm_b200_matmul_rows); CLM_OUT_OF_RANGE for more than 516,096 rows.  One array per device: calls whose kernels
+ * overlap on one device race on it, so serialise them per device.  Every call first clears the array's reduction
+ * counters; a row group whose bounded reduction wait gave up is written as NaN.  The first call on a device
+ * resolves the array's address (set-up); make it before any stream capture meant to contain later calls. */
 #define CLM_B200_STATIC_SCRATCH_BYTES (8u << 20)
 CLM_API int clm_b200_matmul_rows_static(clm_b200_ctx* ctx, const clm_b200_matrix* w, const float* d_x,
                                         uint32_t positions, float* d_y, void* stream);

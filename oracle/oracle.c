@@ -612,6 +612,36 @@ static void rope_inplace(float* v, uint32_t hd, uint64_t pos, float theta) {
   }
 }
 
+/* The K and V rows one layer appends to its cache for q positions at base..base+q-1 (the prefill of a context
+ * without the rest of the layer): rmsnorm(h[p]) with attn_norm, the k and v rows of the q|k|v matrix (rows qd ..
+ * qd+2kvd of wqkv), RoPE on k at position base+p -- the same steps as the first half of orc_llama_layer. */
+int orc_llama_kv_rows(const orc_llama_dims* d, int quant, const uint8_t* wqkv, const float* attn_norm,
+                      const float* h, uint64_t base, uint32_t q, float* kc, float* vc, int threads) {
+  const uint32_t H = d->hidden, nh = d->n_heads, nkv = d->n_kv_heads, hd = d->head_dim;
+  const uint32_t qd = nh * hd, kvd = nkv * hd;
+  float* xn = (float*)malloc((size_t)q * H * sizeof(float));
+  float* kv = (float*)malloc((size_t)q * 2 * kvd * sizeof(float));
+  int st = 0;
+  if (!xn || !kv) {
+    st = 6;
+    goto done;
+  }
+  for (uint32_t p = 0; p < q; ++p) orc_rmsnorm(h + (size_t)p * H, attn_norm, H, d->rms_eps, xn + (size_t)p * H);
+  if ((st = orc_matmul_rows_quant(quant, wqkv + orc_tensor_bytes(quant, (uint64_t)qd * H), 2 * kvd, H, xn, q, kv,
+                                  threads)))
+    goto done;
+  for (uint32_t p = 0; p < q; ++p) {
+    float* row = kv + (size_t)p * 2 * kvd;
+    for (uint32_t hh = 0; hh < nkv; ++hh) rope_inplace(row + hh * hd, hd, base + p, d->rope_theta);
+    memcpy(kc + (base + p) * kvd, row, kvd * sizeof(float));
+    memcpy(vc + (base + p) * kvd, row + kvd, kvd * sizeof(float));
+  }
+done:
+  free(xn);
+  free(kv);
+  return st;
+}
+
 int orc_llama_layer(const orc_llama_dims* d, int quant, const uint8_t* wqkv, const uint8_t* wo, const uint8_t* wgu,
                     const uint8_t* wd, const float* attn_norm, const float* ffn_norm, float* kc, float* vc,
                     uint64_t base, uint32_t q, const int32_t* parent, float* h, int threads) {

@@ -104,6 +104,9 @@ typedef struct {
  * kcache/vcache are [max_ctx][n_kv*head_dim] f32; positions base..base+q-1 are written.
  * Attention: row i attends slots 0..base+i (causal), or, when `parent` is non-NULL, the committed
  * prefix 0..base-1 plus its own ancestors inside the window (tree drafts: parent[i] < i or -1). */
+/* K / V cache rows of one layer for q positions (rmsnorm, k|v rows of the q|k|v matrix, RoPE on k). */
+int orc_llama_kv_rows(const orc_llama_dims* d, int quant, const uint8_t* wqkv, const float* attn_norm,
+                      const float* h, uint64_t base, uint32_t q, float* kc, float* vc, int threads);
 int orc_llama_layer(const orc_llama_dims* d, int quant, const uint8_t* wqkv, const uint8_t* wo, const uint8_t* wgu,
                     const uint8_t* wd, const float* attn_norm, const float* ffn_norm, float* kcache, float* vcache,
                     uint64_t base, uint32_t q, const int32_t* parent, float* h, int threads);

@@ -31,8 +31,8 @@ def build(reference_root: str | None = None) -> None:
     """Compile liboracle.so, and (when the reference sources are present) _ref/libclm_ref.so and the
     drop-in parity driver _ref/backend_parity (needs libclm_b200.so built first)."""
     targets = ["oracle"]
-    root = reference_root or os.environ.get("CLM_REFERENCE_ROOT", "/root/reference")
-    if os.path.isdir(os.path.join(root, "runtime", "domain")):
+    root = reference_root or os.environ.get("CLM_REFERENCE_ROOT", "")
+    if root and os.path.isdir(os.path.join(root, "runtime", "domain")):
         targets += ["ref", "parity"]
     subprocess.run(["make", "-s", "-C", HERE, f"REFERENCE_ROOT={root}", "-j8", *targets], check=True)
 
@@ -80,6 +80,8 @@ class Oracle:
         L.orc_rmsnorm.argtypes = [_fp, _fp, C.c_uint64, C.c_float, _fp]
         L.orc_silu.restype = C.c_float
         L.orc_silu.argtypes = [C.c_float]
+        L.orc_llama_kv_rows.restype = C.c_int
+        L.orc_llama_kv_rows.argtypes = [C.c_void_p, C.c_int, _u8p, _fp, _fp, C.c_uint64, C.c_uint32, _fp, _fp, C.c_int]
         L.orc_llama_layer.restype = C.c_int
         L.orc_llama_layer.argtypes = [C.c_void_p, C.c_int, _u8p, _u8p, _u8p, _u8p, _fp, _fp, _fp, _fp,
                                       C.c_uint64, C.c_uint32, C.c_void_p, _fp, C.c_int]
@@ -195,6 +197,14 @@ class Oracle:
                                     None if par is None else par.ctypes.data, h, threads)
         if st:
             raise RuntimeError(f"orc_llama_layer failed with code {st}")
+
+    def llama_kv_rows(self, dims: "LlamaDims", quant: str, wqkv, attn_norm, kcache, vcache, base: int, h,
+                      threads: int = 8) -> None:
+        """The K / V rows of positions base..base+len(h)-1 into the caches (max_ctx, kvd), in place."""
+        st = self.L.orc_llama_kv_rows(C.byref(dims), QUANTS[quant], wqkv, _c(attn_norm, F32), _c(h, F32), kcache,
+                                      vcache, base, h.shape[0], threads)
+        if st:
+            raise RuntimeError(f"orc_llama_kv_rows failed with code {st}")
 
     def gen_weights(self, seed: int, tensor_id: int, first: int, n: int, stddev: float) -> np.ndarray:
         out = np.zeros(n, F32)

@@ -494,8 +494,44 @@ int main(int argc, char** argv) {
     auto bp = Pipeline::build(m, *store, plan, {b200.get(), b200.get(), b200.get(), b200.get()}, 2048, 8);
     if (rp && bp) {
       const double wr = time_windows(*rp, 100), wb = time_windows(*bp, 400);
+      // the C1 workload end to end: speculative generation of 32 new tokens, q = 4, ScriptedDrafter with
+      // corruption 0.3, from the 16-token prompt; decode tokens per second over `reps` generations (prefill
+      // included, as the reference's clusterlm-bench reports decode tok/s of whole requests)
+      std::vector<std::int32_t> seq = prompt;
+      {
+        auto gp = Pipeline::build(m, *store, plan, {ref.get(), ref.get(), ref.get(), ref.get()}, 128, 8);
+        Trace g = gp ? generate(*gp, prompt, 32, nullptr, 1, V) : Trace{};
+        seq.insert(seq.end(), g.generated.begin(), g.generated.end());
+      }
+      auto gen_rate = [&](BackendAdapter* be, int reps, double* accepted_per_round) {
+        ScriptedDrafter::Config cfg;
+        cfg.vocab = V;
+        cfg.seed = 1;
+        cfg.corruption_rate = 0.3;
+        double secs = 0.0;
+        std::size_t tokens = 0, rounds = 0;
+        for (int r = 0; r < reps; ++r) {
+          ScriptedDrafter d(seq, cfg);
+          auto p = Pipeline::build(m, *store, plan, {be, be, be, be}, 128, 8);
+          if (!p) return 0.0;
+          const auto t0 = std::chrono::steady_clock::now();
+          Trace t = generate(*p, prompt, 32, &d, 4, V);
+          secs += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+          if (!t.ok) return 0.0;
+          tokens += t.generated.size();
+          rounds += t.accepted.size();
+        }
+        *accepted_per_round = rounds ? static_cast<double>(tokens) / rounds : 0.0;
+        return tokens / secs;
+      };
+      double apr_r = 0.0, apr_b = 0.0;
+      gen_rate(b200.get(), 2, &apr_b);  // warm-up: CUDA graphs captured on first use
+      const double tr = gen_rate(ref.get(), 5, &apr_r), tb = gen_rate(b200.get(), 20, &apr_b);
       std::printf("{\"bench\": \"fixture q=4 windows (4 stages in one process, wire encoding between stages)\", "
-                  "\"reference_windows_per_s\": %.2f, \"b200_windows_per_s\": %.2f}\n", wr, wb);
+                  "\"reference_windows_per_s\": %.2f, \"b200_windows_per_s\": %.2f, "
+                  "\"reference_decode_tok_s\": %.2f, \"b200_decode_tok_s\": %.2f, "
+                  "\"reference_tokens_per_round\": %.3f, \"b200_tokens_per_round\": %.3f}\n",
+                  wr, wb, tr, tb, apr_r, apr_b);
     }
   }
   std::printf("%d failure(s)\n", g_failures);

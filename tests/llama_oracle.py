@@ -32,17 +32,19 @@ class LlamaOracle:
         self.ones = np.ones(H, np.float32)
         self.kc = {L: np.zeros((max_ctx, kvd), np.float32) for L in self.layers}
         self.vc = {L: np.zeros((max_ctx, kvd), np.float32) for L in self.layers}
-        self._embd = None
         self._head = None
 
     def enc(self, tensor_id: int, n: int) -> np.ndarray:
-        return self.o.encode(self.q, self.o.gen_weights(self.seed, tensor_id, 0, n, self.std))
+        chunk = 1 << 22  # whole Q4_K superblocks / Q8_0 blocks; chunks are generated and encoded on all threads
+        if n <= chunk:
+            return self.o.encode(self.q, self.o.gen_weights(self.seed, tensor_id, 0, n, self.std))
+        import concurrent.futures as cf
 
-    @property
-    def embd(self):
-        if self._embd is None:
-            self._embd = self.enc(1000, self.g.vocab * self.g.hidden)
-        return self._embd
+        with cf.ThreadPoolExecutor(max_workers=self.threads) as pool:
+            parts = list(pool.map(
+                lambda f: self.o.encode(self.q, self.o.gen_weights(self.seed, tensor_id, f, min(chunk, n - f),
+                                                                   self.std)), range(0, n, chunk)))
+        return np.concatenate(parts)
 
     @property
     def head(self):
@@ -51,9 +53,19 @@ class LlamaOracle:
         return self._head
 
     def embed(self, tokens) -> np.ndarray:
+        """Embedding rows, generated and encoded row by row (a row is whole blocks, so its bytes are the full
+        table's bytes of that row)."""
         H = self.g.hidden
-        rb = self.o.tensor_bytes(self.q, H)
-        return np.stack([self.o.decode(self.q, self.embd[t * rb:(t + 1) * rb], H) for t in tokens])
+        return np.stack([self.o.decode(self.q, self.o.encode(self.q, self.o.gen_weights(
+            self.seed, 1000, int(t) * H, H, self.std)), H) for t in tokens])
+
+    def fill_context(self, tokens) -> None:
+        """K / V rows of positions 0..len(tokens)-1 in every layer, as a prefill of `tokens` writes them; only the
+        first layer's rows are exact without running the layers, so this is for single-layer models."""
+        assert len(self.layers) == 1, "fill_context computes the first layer's caches only"
+        L = self.layers[0]
+        h = self.embed(tokens)
+        self.o.llama_kv_rows(self.dims, self.q, self.w[L][0], self.ones, self.kc[L], self.vc[L], 0, h, self.threads)
 
     def run_layers(self, h: np.ndarray, base: int, parent=None) -> np.ndarray:
         h = np.ascontiguousarray(h, np.float32).copy()

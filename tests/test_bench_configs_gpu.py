@@ -1,0 +1,174 @@
+"""Parity at the benchmark configurations themselves (the sizes bench.py times), against the oracle.
+
+* C3: the 8B shape in Q4_K, one decoder layer and the full 128,256-row LM head, context filled to 4,096 by 256-row
+  prefill windows (tensor-core path), then a q = 4 window on the GEMV chain: the decode attention's split / combine
+  path over 64 KV pages and RoPE at positions >= 4,096.  Logits within 2e-2 of the oracle (max |diff| / max |ref|).
+* C4: the same in Q8_0 with the 16-node draft tree, one session through the tree window and two sessions in one
+  batched window (the wide attention's KV splits at context 4,096).
+* Greedy: a 2-layer model at the full 8B width with the real head; 100 tokens from the device's greedy speculative
+  rounds (q = 4, MTP drafts) against the oracle's argmax at every position given the same prefix: >= 99% equal, and
+  every disagreement is a near tie in the oracle's logits.
+* C2: the full acceptance micro-workload (64 sequences x q = 8 x vocab 151,936) from logits: every sequence's
+  (accepted, next) equals the oracle's distribution + verify_speculative with the same Philox uniforms.
+
+The oracle's K / V context of 4,096 positions is computed by its own restatement of the layer's first half
+(orc_llama_kv_rows) from the same generated weights, so the prefill is checked too.
+"""
+import concurrent.futures as cf
+import dataclasses
+import os
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+sys.path.insert(0, os.path.dirname(__file__))
+
+TOL = 2e-2
+CONTEXT = 4096
+THREADS = os.cpu_count() or 8
+TREE16 = np.array([-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 6, 7], np.int32)
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _prefill(eng, sid, prompt, chunk=256):
+    """Commits `prompt` into session sid in `chunk`-row windows with device buffers (no logits copied back)."""
+    import torch
+
+    dev = torch.device("cuda:0")
+    toks = torch.from_numpy(np.ascontiguousarray(prompt, np.int32)).to(dev)
+    out = torch.empty((chunk, eng.vocab), dtype=torch.float32, device=dev)
+    for off in range(0, len(prompt), chunk):
+        n = min(chunk, len(prompt) - off)
+        eng.run_window_device(sid, off, toks[off:off + n], out[:n])
+        eng.commit(sid, n)
+    torch.cuda.synchronize()
+
+
+def _one_layer(ctx, oracle, quant, sessions=1):
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+    from llama_oracle import LlamaOracle
+
+    geo = dataclasses.replace(LLAMA3_8B, n_layers=1, quant=quant)
+    eng = Engine(ctx, geo, 0, 1, ROLE_WHOLE, CONTEXT + 64, 256, sessions)
+    eng.generate_weights(seed=0, stddev=0.02)
+    eng.prepare()
+    models = [LlamaOracle(oracle, geo, max_ctx=CONTEXT + 64, threads=THREADS)]
+    for _ in range(1, sessions):  # same weights, another cache
+        m = LlamaOracle.__new__(LlamaOracle)
+        m.__dict__.update(models[0].__dict__)
+        m.kc = {L: np.zeros_like(v) for L, v in models[0].kc.items()}
+        m.vc = {L: np.zeros_like(v) for L, v in models[0].vc.items()}
+        models.append(m)
+    return geo, eng, models
+
+
+@pytest.mark.parametrize("quant", ["q4_k"])
+def test_c3_layer_and_head_at_context_4096(ctx, oracle, quant):
+    geo, eng, (m,) = _one_layer(ctx, oracle, quant)
+    rng = np.random.default_rng(30)
+    prompt = rng.integers(0, geo.vocab, CONTEXT).astype(np.int32)
+    eng.open_session(1)
+    _prefill(eng, 1, prompt)
+    m.fill_context(prompt)
+    assert eng.position(1) == CONTEXT
+    for q, keep in [(4, 2), (4, 4)]:
+        base = eng.position(1)
+        w = rng.integers(0, geo.vocab, q).astype(np.int32)
+        got = eng.run_window(1, base, tokens=w)
+        want = m.window(w, base)
+        assert got.shape == (q, geo.vocab)
+        assert rel(got, want) < TOL, (base, rel(got, want))
+        assert all(int(np.argmax(got[i])) == int(np.argmax(want[i])) or
+                   np.sort(want[i])[-1] - np.sort(want[i])[-2] < TOL * np.abs(want[i]).max() for i in range(q))
+        eng.commit(1, keep)  # the oracle's window rows past the kept ones are rewritten by the next window
+    eng.close()
+
+
+def test_c4_tree_windows_at_context_4096(ctx, oracle):
+    geo, eng, models = _one_layer(ctx, oracle, "q8_0", sessions=2)
+    rng = np.random.default_rng(40)
+    prompts = [rng.integers(0, geo.vocab, CONTEXT).astype(np.int32) for _ in models]
+    for sid, (p, m) in enumerate(zip(prompts, models), start=1):
+        eng.open_session(sid)
+        _prefill(eng, sid, p)
+        m.fill_context(p)
+    toks = [rng.integers(0, geo.vocab, 16).astype(np.int32) for _ in models]
+    want = [m.logits(m.run_layers(m.embed(t), CONTEXT, parent=TREE16)) for m, t in zip(models, toks)]
+    # one session's tree on the GEMV chain (16 rows)
+    got = eng.run_tree_window(1, CONTEXT, TREE16, tokens=toks[0])
+    assert rel(got, want[0]) < TOL, rel(got, want[0])
+    eng.abort(1)
+    # both sessions' trees in one batched window (32 rows: the tensor-core GEMMs and the wide attention)
+    got2 = eng.run_batch_window([1, 2], [CONTEXT, CONTEXT], np.stack(toks), TREE16)
+    for b in range(2):
+        assert rel(got2[b], want[b]) < TOL, (b, rel(got2[b], want[b]))
+    eng.close()
+
+
+def test_greedy_generation_agrees_with_oracle_8b_width(ctx, oracle):
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+    from llama_oracle import LlamaOracle
+
+    geo = dataclasses.replace(LLAMA3_8B, n_layers=2)
+    n_prompt, n_new = 12, 100
+    eng = Engine(ctx, geo, 0, 2, ROLE_WHOLE, 256, 16, 1)
+    eng.generate_weights(seed=0, stddev=0.02)
+    eng.prepare()
+    eng.open_session(1)
+    prompt = np.random.default_rng(50).integers(0, geo.vocab, n_prompt).astype(np.int32)
+    eng.spec_begin(1, prompt, 4)
+    out = []
+    while len(out) < n_new:
+        out += list(eng.spec_round(1, 4))
+    eng.close()
+    seq = np.concatenate([prompt, np.array(out[:n_new], np.int32)])
+    # the oracle's logits at every position of the device's sequence (teacher forcing on the device's tokens)
+    m = LlamaOracle(oracle, geo, max_ctx=256, threads=THREADS)
+    logits = m.window(seq[:-1], 0)
+    pred = logits[n_prompt - 1:].argmax(axis=1)
+    agree = pred == seq[n_prompt:]
+    srt = np.sort(logits[n_prompt - 1:], axis=1)
+    gap = srt[:, -1] - srt[:, -2]
+    scale = np.abs(logits).max()
+    assert agree.mean() >= 0.99, (agree.mean(), np.nonzero(~agree)[0])
+    assert np.all(gap[~agree] < TOL * scale), gap[~agree]
+
+
+def test_c2_acceptance_from_logits_full_size(ctx, oracle):
+    import torch
+
+    from clusterlm_b200.runtime import accept_logits, distribution
+
+    B, Qw, V = 64, 8, 151936
+    k = Qw - 1
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev).manual_seed(0)
+    tl = torch.randn((B, Qw, V), generator=g, device=dev) * 3.0
+    dl = tl[:, :k] + torch.randn((B, k, V), generator=g, device=dev) * 0.5
+    drafts = torch.multinomial(torch.softmax(dl.reshape(-1, V), dim=-1), 1, generator=g).reshape(B, k)
+    drafts = drafts.to(torch.int32).contiguous()
+    acc, nxt = accept_logits(ctx, tl, dl.contiguous(), drafts, 1.0, seed=0, counter_base=0)
+    P_dev = distribution(ctx, tl.reshape(-1, V), 1.0).cpu().numpy().reshape(B, Qw, V)
+    acc, nxt = acc.cpu().numpy(), nxt.cpu().numpy()
+    tl_h, dl_h, dr_h = tl.cpu().numpy(), dl.cpu().numpy(), drafts.cpu().numpy()
+    del tl, dl
+    with cf.ThreadPoolExecutor(max_workers=THREADS) as pool:
+        P = np.stack(list(pool.map(lambda r: oracle.distribution(r, 1.0), tl_h.reshape(-1, V)))).reshape(B, Qw, V)
+        Qp = np.stack(list(pool.map(lambda r: oracle.distribution(r, 1.0), dl_h.reshape(-1, V)))).reshape(B, k, V)
+    ulp = np.abs(P_dev.view(np.int32).astype(np.int64) - P.view(np.int32).astype(np.int64))
+    print(f"C2 distribution rows: {int((ulp == 1).sum())} of {ulp.size} entries differ by 1 ulp, "
+          f"max {int(ulp.max())} ulp")
+    assert ulp.max() <= 1
+    mism = []
+    for b in range(B):
+        us = np.array([oracle.philox_uniform(0, n, b, 0, 0) for n in range(k + 1)])
+        a, n, _ = oracle.verify(P[b], dr_h[b], Qp[b], us)
+        if (a, n) != (int(acc[b]), int(nxt[b])):
+            mism.append((b, (a, n), (int(acc[b]), int(nxt[b]))))
+    assert not mism, mism

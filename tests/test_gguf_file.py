@@ -80,3 +80,47 @@ def test_reader_refuses_broken_files(tmp_path):
     bad.write_bytes(raw[:-1000])
     with pytest.raises(ValueError, match="past the end"):
         GGUFFile(str(bad)).data("blk.0.attn_norm.weight")
+
+
+def test_geometry_refuses_rope_frequency_scaling(tmp_path):
+    """Llama 3.1+ files carry RoPE frequency factors (rope_freqs.weight) or a rope.scaling.type; the engine's RoPE is
+    the unscaled theta^(-2i/hd) rotation, so such files are refused instead of running with other logits."""
+    from clusterlm_b200 import ClmError
+
+    path = tmp_path / "freqs.gguf"
+    w = gguf.GGUFWriter(str(path), "llama")
+    w.add_block_count(1)
+    w.add_embedding_length(256)
+    w.add_head_count(2)
+    w.add_feed_forward_length(512)
+    rng = np.random.default_rng(1)
+    w.add_tensor("token_embd.weight", rng.integers(0, 256, (512, 144), dtype=np.uint8),
+                 raw_dtype=gguf.GGMLQuantizationType.Q4_K)
+    w.add_tensor("blk.0.attn_q.weight", rng.integers(0, 256, (256, 144), dtype=np.uint8),
+                 raw_dtype=gguf.GGMLQuantizationType.Q4_K)
+    w.add_tensor("rope_freqs.weight", np.ones(64, np.float32))
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pytest.raises(ClmError, match="rope_freqs") as ex:
+        llama_geometry(GGUFFile(str(path)))
+    assert ex.value.name == "kUnimplemented"
+
+    path2 = tmp_path / "scaled.gguf"
+    w = gguf.GGUFWriter(str(path2), "llama")
+    w.add_block_count(1)
+    w.add_embedding_length(256)
+    w.add_head_count(2)
+    w.add_feed_forward_length(512)
+    w.add_string("llama.rope.scaling.type", "linear")
+    w.add_tensor("token_embd.weight", rng.integers(0, 256, (512, 144), dtype=np.uint8),
+                 raw_dtype=gguf.GGMLQuantizationType.Q4_K)
+    w.add_tensor("blk.0.attn_q.weight", rng.integers(0, 256, (256, 144), dtype=np.uint8),
+                 raw_dtype=gguf.GGMLQuantizationType.Q4_K)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    with pytest.raises(ClmError, match="scaling 'linear'"):
+        llama_geometry(GGUFFile(str(path2)))

@@ -17,7 +17,9 @@ sys.path.insert(0, os.path.dirname(__file__))
 from test_llama_gpu import small_geo  # noqa: E402
 
 
-def _write_model(path, oracle, geo):
+def _write_model(path, oracle, geo, head_id=1001, tie_head=False, q6k_down0=False):
+    """tie_head: no output.weight (the head shares token_embd.weight); head_id: generator tensor of output.weight;
+    q6k_down0: blk.0.ffn_down.weight stored as (random) Q6_K blocks."""
     from llama_oracle import LlamaOracle
 
     m = LlamaOracle(oracle, geo, layers=[])
@@ -46,11 +48,16 @@ def _write_model(path, oracle, geo):
         mat(b + "attn_output.weight", 16 * L + 3, H, qd)
         mat(b + "ffn_gate.weight", 16 * L + 4, F, H)
         mat(b + "ffn_up.weight", 16 * L + 5, F, H)
-        mat(b + "ffn_down.weight", 16 * L + 6, H, F)
+        if q6k_down0 and L == 0:
+            blocks = np.random.default_rng(3).integers(0, 256, (H, F // 256 * 210), dtype=np.uint8)
+            w.add_tensor(b + "ffn_down.weight", blocks, raw_dtype=gguf.GGMLQuantizationType.Q6_K)
+        else:
+            mat(b + "ffn_down.weight", 16 * L + 6, H, F)
         w.add_tensor(b + "attn_norm.weight", ones)
         w.add_tensor(b + "ffn_norm.weight", ones)
     w.add_tensor("output_norm.weight", ones)
-    mat("output.weight", 1001, V, H)
+    if not tie_head:
+        mat("output.weight", head_id, V, H)
     mat("mtp.ffn_gate.weight", 1002, F, H)
     mat("mtp.ffn_up.weight", 1003, F, H)
     mat("mtp.ffn_down.weight", 1004, H, F)
@@ -120,4 +127,32 @@ def test_gguf_refusals(ctx, oracle, tmp_path):
     with pytest.raises(ClmError) as ex:
         e.load_gguf(str(path))
     assert ex.value.name == "kNotFound" and "blk.2." in str(ex.value)
+    e.close()
+
+
+def test_gguf_tied_head_and_unsupported_type(ctx, oracle, tmp_path):
+    """A file without output.weight uses token_embd.weight as its head (llama.cpp's tied embedding): it computes the
+    same logits as a file whose output.weight holds the embedding's bytes.  A stage matrix in a ggml type the engine
+    does not bind (Q6_K here) is refused by name with CLM_UNIMPLEMENTED."""
+    from clusterlm_b200 import ClmError
+    from clusterlm_b200.engine import ROLE_WHOLE, Engine
+
+    geo = small_geo("q4_k")
+    tied, explicit, q6k = tmp_path / "tied.gguf", tmp_path / "explicit.gguf", tmp_path / "q6k.gguf"
+    _write_model(tied, oracle, geo, tie_head=True)
+    _write_model(explicit, oracle, geo, head_id=1000)
+    _write_model(q6k, oracle, geo, q6k_down0=True)
+    outs = []
+    for path in (tied, explicit):
+        e = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, 64, 8, 1)
+        e.load_gguf(str(path))
+        e.prepare()
+        e.open_session(1)
+        outs.append(e.run_window(1, 0, tokens=np.arange(5, dtype=np.int32)))
+        e.close()
+    assert np.array_equal(outs[0], outs[1])
+    e = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, 64, 8, 1)
+    with pytest.raises(ClmError, match="blk.0.ffn_down.weight is in ggml type 14") as ex:
+        e.load_gguf(str(q6k))
+    assert ex.value.name == "kUnimplemented"
     e.close()
