@@ -18,7 +18,7 @@
 #include "bulk.cuh"
 #include "engine.cuh"
 #include "link.cuh"
-#include "window.cuh"
+#include "flow.cuh"
 #include "gemv.cuh"
 #include "gemv2.cuh"
 #include "llama.cuh"
@@ -59,7 +59,7 @@ struct Session {
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;  // (kind, q, flag) -> executable graph
   std::map<std::tuple<int, int, int>, int> seen;
   std::map<std::tuple<int, int, int>, unsigned long long> launches;  // kernels per graph
-  std::map<int, MkPhase*> mk_phases;  // window megakernel phase tables by q (device arrays)
+  std::map<int, FlowPhase*> flow_phases;  // dataflow window kernel phase tables by q (device arrays)
   int32_t* d_win = nullptr;    // pipeline tail: this session's current window tokens [W + 1]
   float* d_dprobs = nullptr;   // pipeline tail: draft distributions of the current window [W][V]
 };
@@ -234,12 +234,17 @@ struct LlamaEngine : clm_b200_engine {
   __half* q16 = nullptr;
   float* attn_part = nullptr;
   float2* rope = nullptr;    // RoPE (cos, sin) table [max_context][hd/2]
-  // verify-window megakernel (window.cu): grid / ring stages per column-tile count (index nt - 1), barrier counter,
-  // attention segment partials
-  int mk_grid[2] = {0, 0}, mk_stage_count[2] = {0, 0}, mk_stage_bytes[2] = {0, 0};
-  int mk_attn_maxseg = 0;
-  unsigned* mk_bar = nullptr;
-  float* mk_attn_part = nullptr;
+  // dataflow verify-window kernel (flow.cu): grid / ring stages per column-tile count (index nt - 1), attention
+  // segment partials, per-kind GEMV partials, readiness counters
+  int flow_grid_n[2] = {0, 0}, flow_stage_count[2] = {0, 0}, flow_stage_bytes[2] = {0, 0};
+  int flow_attn_maxseg = 0;
+  float* flow_attn_part = nullptr;
+  enum { FK_QKV = 0, FK_O, FK_GU, FK_DOWN, FK_HEAD, FK_KINDS };
+  float* flow_part[FK_KINDS] = {};  // stream-K partials per matrix kind (phases of one kind never overlap)
+  int* flow_gcount[FK_KINDS] = {};  // their row-group counters
+  size_t flow_gcount_n[FK_KINDS] = {};
+  int* flow_ctr = nullptr;          // readiness counters of one window, zeroed before every launch
+  size_t flow_ctr_n = 0;
   // wide windows (17..max_window rows when max_window > 16): tensor-core GEMMs (gemm_tc.cu) between the elementwise
   // steps of wide.cu
   float* wy = nullptr;       // GEMM outputs [W][largest row count of a layer matrix]
@@ -395,9 +400,9 @@ struct LlamaEngine : clm_b200_engine {
     return CLM_OK;
   }
 
-  // ---- the layers (+ head) of a window as megakernel phases: the same chain as enqueue_layers
-  MkGemv mk_gemv(const Gemv& g, int nt, const XBuf& in, const Epi& epi) const {
-    MkGemv m;
+  // ---- the layers (+ head) of a window as phases of the dataflow kernel: the same chain as enqueue_layers
+  FlowGemv flow_gemv(const Gemv& g, int nt, const XBuf& in, const Epi& epi, int kind) const {
+    FlowGemv m;
     m.tiles = static_cast<const uint8_t*>(g.m->data);
     m.rows = g.m->shape.rows;
     m.ng = (int)g.m->shape.ng;
@@ -406,22 +411,51 @@ struct LlamaEngine : clm_b200_engine {
     m.in = in;
     m.epi = epi;
     m.epi_kind = epi.kind;
+    m.part = flow_part[kind];
+    m.counters = flow_gcount[kind];
     return m;
   }
 
-  int enqueue_window_mk(Session& s, int q, cudaStream_t st) {
+  // Readiness counters of one window (offsets into flow_ctr): per layer the 512-column chunks of the QKV, W_o,
+  // gate|up and down inputs, the kv heads of the attention, and the finished-row-group counts of W_o and down;
+  // then the head's input chunks.
+  struct FlowCtr {
+    int per_layer = 0, qkv = 0, attn = 0, o = 0, gu = 0, down = 0, done_o = 0, done_down = 0, head = 0;
+  };
+  FlowCtr flow_ctr_layout() const {
+    FlowCtr c;
+    c.qkv = 0;
+    c.attn = c.qkv + d.H / 512;
+    c.o = c.attn + d.nkv;
+    c.gu = c.o + d.qd() / 512;
+    c.down = c.gu + d.H / 512;
+    c.done_o = c.down + d.F / 512;
+    c.done_down = c.done_o + 1;
+    c.per_layer = c.done_down + 1;
+    c.head = (int)layers.size() * c.per_layer;
+    return c;
+  }
+  bool flow_shape_ok() const {
+    return d.hd == 128 && d.H % 512 == 0 && d.F % 512 == 0 && d.qd() % 512 == 0 && !layers.empty();
+  }
+
+  int enqueue_window_flow(Session& s, int q, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
-    auto it = s.mk_phases.find(q);
-    MkPhase* d_ph = nullptr;
+    auto it = s.flow_phases.find(q);
+    FlowPhase* d_ph = nullptr;
     const int nph = (int)layers.size() * 5 + (has_head ? 1 : 0);
-    if (it != s.mk_phases.end()) {
+    if (it != s.flow_phases.end()) {
       d_ph = it->second;
     } else {
-      std::vector<MkPhase> ph;
+      const FlowCtr C = flow_ctr_layout();
+      std::vector<FlowPhase> ph;
       const long long* pos = &s.d_state->pos;
       const int group = d.nh / d.nkv;
+      const int mtiles = (q * group + 15) / 16;
+      const int ng_h = d.H / 128;  // row groups of a residual GEMV (W_o, down)
       for (size_t li = 0; li < layers.size(); ++li) {
         const Layer& L = layers[li];
+        int* lc = flow_ctr + li * C.per_layer;
         Epi ek = epi_base(EPI_ROPE_KV);
         ek.nh = d.nh;
         ek.nkv = d.nkv;
@@ -432,75 +466,107 @@ struct LlamaEngine : clm_b200_engine {
         ek.kpool = kpool[li];
         ek.vpool = vpool[li];
         ek.q16 = q16;
-        MkPhase p0;
-        p0.kind = MK_GEMV;
-        p0.g = mk_gemv(L.qkv, nt, xa, ek);
+        FlowPhase p0;
+        p0.kind = FLOW_GEMV;
+        p0.g = flow_gemv(L.qkv, nt, xa, ek, FK_QKV);
+        if (li > 0) {
+          p0.wait = lc + C.qkv;
+          p0.wait_target = 4;
+          p0.ss_done = lc - C.per_layer + C.done_down;
+          p0.ss_target = ng_h;
+        }
+        p0.sig = lc + C.attn;
+        p0.sig_qkv = 1;
         ph.push_back(p0);
-        MkPhase pa;
-        pa.kind = MK_ATTN;
+        FlowPhase pa;
+        pa.kind = FLOW_ATTN;
         pa.a.q16 = q16;
         pa.a.kpool = kpool[li];
         pa.a.vpool = vpool[li];
         pa.a.pages = s.d_pages;
         pa.a.nh = d.nh;
         pa.a.nkv = d.nkv;
-        pa.a.mtiles = (q * group + 15) / 16;
-        pa.a.maxseg = mk_attn_maxseg;
+        pa.a.mtiles = mtiles;
+        pa.a.maxseg = flow_attn_maxseg;
         pa.a.scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
-        pa.a.part = mk_attn_part;
+        pa.a.part = flow_attn_part;
         pa.a.counters = acount;
         pa.a.out = xb;
         pa.a.out.ss = nullptr;
         pa.a.hi_scale = hi_scale();
         pa.a.nt_out = nt;
+        pa.wait = lc + C.attn;
+        pa.wait_target = group + 2;
+        pa.sig = lc + C.o;
+        // a W_o unit reads 512 columns = 4 query heads: a kv head's outputs cover group / 4 chunks, or 4 / group kv
+        // heads share one chunk
+        pa.sig_span = group >= 4 ? group / 4 : 1;
+        pa.sig_kvh_div = group >= 4 ? 1 : 4 / group;
         ph.push_back(pa);
         XBuf ob = xb;
         ob.ss = nullptr;
-        MkPhase po;
-        po.kind = MK_GEMV;
-        po.g = mk_gemv(L.o, nt, ob, epi_resid(h, L.ffn_norm, xa));
+        FlowPhase po;
+        po.kind = FLOW_GEMV;
+        po.g = flow_gemv(L.o, nt, ob, epi_resid(h, L.ffn_norm, xa), FK_O);
+        po.wait = lc + C.o;
+        po.wait_target = mtiles * pa.sig_kvh_div;
+        po.sig = lc + C.gu;
+        po.sig_div = 4;
+        po.done = lc + C.done_o;
         ph.push_back(po);
         Epi es = epi_base(EPI_SWIGLU_PREP);
         es.ffn = d.F;
         es.next = xb;
-        MkPhase pg;
-        pg.kind = MK_GEMV;
-        pg.g = mk_gemv(L.gu, nt, xa, es);
+        FlowPhase pg;
+        pg.kind = FLOW_GEMV;
+        pg.g = flow_gemv(L.gu, nt, xa, es, FK_GU);
+        pg.wait = lc + C.gu;
+        pg.wait_target = 4;
+        pg.ss_done = lc + C.done_o;
+        pg.ss_target = ng_h;
+        pg.sig = lc + C.down;
+        pg.sig_div = 8;  // a gate|up row group gives 64 SwiGLU columns
         ph.push_back(pg);
         const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
         XBuf db = xb;
         db.ss = nullptr;
-        MkPhase pd;
-        pd.kind = MK_GEMV;
-        pd.g = mk_gemv(L.down, nt, db, epi_resid(h, wnext, xa));
+        FlowPhase pd;
+        pd.kind = FLOW_GEMV;
+        pd.g = flow_gemv(L.down, nt, db, epi_resid(h, wnext, xa), FK_DOWN);
+        pd.wait = lc + C.down;
+        pd.wait_target = 8;
+        pd.sig = li + 1 < layers.size() ? lc + C.per_layer + C.qkv : (has_head ? flow_ctr + C.head : nullptr);
+        pd.sig_div = 4;
+        pd.done = lc + C.done_down;
         ph.push_back(pd);
       }
       if (has_head) {
         Epi eo = epi_base(EPI_STORE);
         eo.out = logits;
         eo.out_ld = d.V;
-        MkPhase pho;
-        pho.kind = MK_GEMV;
-        pho.g = mk_gemv(head, nt, xa, eo);
+        FlowPhase pho;
+        pho.kind = FLOW_GEMV;
+        pho.g = flow_gemv(head, nt, xa, eo, FK_HEAD);
+        pho.wait = flow_ctr + C.head;
+        pho.wait_target = 4;
+        pho.ss_done = flow_ctr + (layers.size() - 1) * C.per_layer + C.done_down;
+        pho.ss_target = ng_h;
         ph.push_back(pho);
       }
-      CLM_CHECK((int)ph.size() == nph, CLM_INTERNAL, "megakernel phase count");
-      CLM_CUDA(cudaMalloc(&d_ph, ph.size() * sizeof(MkPhase)));
-      CLM_CUDA(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
-      s.mk_phases[q] = d_ph;
+      CLM_CHECK((int)ph.size() == nph, CLM_INTERNAL, "flow kernel phase count");
+      CLM_CUDA(cudaMalloc(&d_ph, ph.size() * sizeof(FlowPhase)));
+      CLM_CUDA(cudaMemcpy(d_ph, ph.data(), ph.size() * sizeof(FlowPhase), cudaMemcpyHostToDevice));
+      s.flow_phases[q] = d_ph;
     }
-    MkParams P;
+    FlowParams P;
     P.phases = d_ph;
     P.nphases = nph;
     P.q = q;
     P.pos = &s.d_state->pos;
-    P.part = part;
-    P.counters = gcount;
-    P.barrier = mk_bar;
     P.err = bad;
-    P.stages = mk_stage_count[nt - 1];
-    P.stage_bytes = mk_stage_bytes[nt - 1];
-    return launch_window_mk(P, d.quant, nt, mk_grid[nt - 1], st);
+    P.stages = flow_stage_count[nt - 1];
+    P.stage_bytes = flow_stage_bytes[nt - 1];
+    return launch_flow(P, d.quant, nt, flow_grid_n[nt - 1], flow_ctr, flow_ctr_n * sizeof(int), st);
   }
 
   // ---- one tensor-core GEMM of a wide window: y[p] = W . x[p] over the tiles in wxh.  `out` tells the next step
@@ -591,9 +657,9 @@ struct LlamaEngine : clm_b200_engine {
     }
     const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
     CLM_TRY(launch_prep_rows(h, d.H, q, d.H, w0, nt, hi_scale(), xa, true, st));
-    if (mk_grid[nt - 1] > 0 && !layers.empty() && parent == nullptr) {
+    if (flow_grid_n[nt - 1] > 0 && parent == nullptr) {
       // layers (and the head) in one cooperative launch
-      CLM_TRY(enqueue_window_mk(s, q, st));
+      CLM_TRY(enqueue_window_flow(s, q, st));
       if (!has_head) CLM_TRY(launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st));
       return CLM_OK;
     }
@@ -755,7 +821,8 @@ struct LlamaEngine : clm_b200_engine {
     if (acount) CLM_CUDA(cudaMemset(acount, 0, acount_n * sizeof(int)));
     if (wattn_cnt) CLM_CUDA(cudaMemset(wattn_cnt, 0, (size_t)wattn_tiles * sizeof(int)));
     if (samp_counters) CLM_CUDA(cudaMemset(samp_counters, 0, samp_counter_bytes));
-    if (mk_bar) CLM_CUDA(cudaMemset(mk_bar, 0, sizeof(unsigned)));
+    for (int k = 0; k < FK_KINDS; ++k)
+      if (flow_gcount[k]) CLM_CUDA(cudaMemset(flow_gcount[k], 0, flow_gcount_n[k] * sizeof(int)));
     return CLM_OK;
   }
 
@@ -781,8 +848,8 @@ struct LlamaEngine : clm_b200_engine {
   void release_session(Session& s) {
     for (auto& kv : s.graphs) cudaGraphExecDestroy(kv.second);
     s.graphs.clear();
-    for (auto& kv : s.mk_phases) cudaFree(kv.second);
-    s.mk_phases.clear();
+    for (auto& kv : s.flow_phases) cudaFree(kv.second);
+    s.flow_phases.clear();
     if (s.d_pages) cudaFree(s.d_pages);
     if (s.d_state) cudaFree(s.d_state);
     if (s.d_win) cudaFree(s.d_win);
@@ -1174,26 +1241,49 @@ int llama_prepare(LlamaEngine* e) {
                                                                                d.theta);
     CLM_LAUNCHED("rope_table_kernel");
   }
-  // window megakernel: one cooperative grid per column-tile count, opt-in with CLM_B200_WINDOW_MK=1 (the
-  // per-kernel chain with programmatic dependent launch is faster on the measured shapes: it overlaps each
-  // kernel's tail with the next kernel's start, which the megakernel's grid barriers cannot)
+  // dataflow window kernel (windows of <= 16 rows without a tree): one cooperative grid per column-tile count; on
+  // by default, CLM_B200_FLOW=0 keeps every window on the per-kernel chain
   {
-    const char* env = getenv("CLM_B200_WINDOW_MK");
-    const bool want = env && env[0] == '1' && d.hd == 128;
+    const char* env = getenv("CLM_B200_FLOW");
+    const bool want = !(env && env[0] == '0') && e->flow_shape_ok();
     const int G = e->ctx->sm_count;
-    e->mk_attn_maxseg = (G + d.nkv - 1) / d.nkv + 1;  // bound for one m-tile (more m-tiles: fewer segments)
-    if (want && !e->layers.empty() && e->mk_attn_maxseg <= 64) {
+    e->flow_attn_maxseg = (G + d.nkv - 1) / d.nkv + 1;  // bound for one m-tile (more m-tiles: fewer segments)
+    if (want && e->flow_attn_maxseg <= 64) {
       for (int nt = 1; nt <= 2; ++nt) {
         const GemvShape sh = e->layers[0].qkv.m->shape;
         const int sbytes = g4_geom(sh, nt).stage_bytes;
-        const int stages = mk_stages(sbytes);
-        e->mk_stage_bytes[nt - 1] = sbytes;
-        e->mk_stage_count[nt - 1] = stages;
-        e->mk_grid[nt - 1] = stages ? mk_grid(e->ctx->device, stages, sbytes, d.quant, nt) : 0;
-        if (e->mk_grid[nt - 1] != G) e->mk_grid[nt - 1] = 0;  // the stream-K bounds assume one CTA per SM
+        const int stages = flow_stages(sbytes);
+        e->flow_stage_bytes[nt - 1] = sbytes;
+        e->flow_stage_count[nt - 1] = stages;
+        e->flow_grid_n[nt - 1] = stages ? flow_grid(e->ctx->device, stages, sbytes, d.quant, nt) : 0;
+        if (e->flow_grid_n[nt - 1] != G) e->flow_grid_n[nt - 1] = 0;  // the stream-K bounds assume one CTA per SM
       }
-      CLM_TRY(e->alloc_t(&e->mk_bar, 1));
-      CLM_TRY(e->alloc_t(&e->mk_attn_part, (size_t)mtiles * d.nkv * e->mk_attn_maxseg * 16 * kMkAttnRowFloats));
+      const int wq = std::min(W, 16);
+      auto region = [&](int kind, std::initializer_list<const Gemv*> gs) -> int {
+        uint64_t floats = 1, ng = 1;
+        for (const Gemv* g : gs) {
+          if (!g->m) continue;
+          for (int i = 0; i < 2; ++i)
+            floats = std::max<uint64_t>(floats, (uint64_t)g->m->shape.ng * g->plan[i].ksplit * wq * 128);
+          ng = std::max<uint64_t>(ng, g->m->shape.ng);
+        }
+        CLM_TRY(e->alloc_t(&e->flow_part[kind], floats));
+        CLM_TRY(e->alloc_t(&e->flow_gcount[kind], ng));
+        CLM_CUDA(cudaMemset(e->flow_gcount[kind], 0, ng * sizeof(int)));
+        e->flow_gcount_n[kind] = ng;
+        return CLM_OK;
+      };
+      const auto& L0 = e->layers[0];  // every layer's matrices have the same shapes
+      CLM_TRY(region(LlamaEngine::FK_QKV, {&L0.qkv}));
+      CLM_TRY(region(LlamaEngine::FK_O, {&L0.o}));
+      CLM_TRY(region(LlamaEngine::FK_GU, {&L0.gu}));
+      CLM_TRY(region(LlamaEngine::FK_DOWN, {&L0.down}));
+      CLM_TRY(region(LlamaEngine::FK_HEAD, {&e->head}));
+      CLM_TRY(e->alloc_t(&e->flow_attn_part,
+                         (size_t)mtiles_q16 * d.nkv * e->flow_attn_maxseg * 16 * kFlowAttnRowFloats));
+      const auto C = e->flow_ctr_layout();
+      e->flow_ctr_n = (size_t)C.head + d.H / 512;
+      CLM_TRY(e->alloc_t(&e->flow_ctr, e->flow_ctr_n));
     }
   }
   CLM_TRY(e->alloc_t(&e->tokens, (size_t)W));

@@ -1,5 +1,5 @@
 // gemv_core.cuh — building blocks of the persistent q-row GEMV shared by the single-matrix kernel (gemv4.cu)
-// and the verify-window megakernel (window.cu): consumer warp roles, the per-unit tensor-core step, row-group
+// and the verify-window dataflow kernel (flow.cu): consumer warp roles, the per-unit tensor-core step, row-group
 // flush (segment partials reduced by the group's first segment) and the fused epilogues.
 #pragma once
 #include "bulk.cuh"
@@ -45,7 +45,7 @@ __device__ __forceinline__ void group_segments(long long x, long long y, long lo
 
 struct G4Geom {
   int sb;          // superblocks per row
-  int usb;         // superblocks per unit (1: the single-matrix GEMV, 2: the window megakernel)
+  int usb;         // superblocks per unit (2 in both the single-matrix GEMV and the dataflow kernel)
   int ppr;         // units per row group
   int tile_bytes;  // one 16-row x 256-column tile
   int sb_bytes;    // 8 tiles of one superblock
@@ -89,7 +89,7 @@ __device__ __forceinline__ void epi_preload(EpiPre& pre, int grp, uint32_t rows,
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
-      pre.h[k] = (i < q * 128 && row0 + r < (int)rows) ? epi.h[(size_t)p * epi.H + row0 + r] : 0.0f;
+      pre.h[k] = (i < q * 128 && row0 + r < (int)rows) ? __ldcg(epi.h + (size_t)p * epi.H + row0 + r) : 0.0f;
     }
     pre.w = (tid < 128 && row0 + tid < (int)rows) ? epi.wnext[row0 + tid] : 0.0f;
   } else if (EPI == EPI_ROPE_KV) {
@@ -222,7 +222,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
 }
 
 
-// Epilogue kind chosen at run time (the megakernel's phases).
+// Epilogue kind chosen at run time (the dataflow kernel's phases).
 __device__ __forceinline__ void g4_epilogue_rt(int kind, float* y, const float* s_scale, int grp, uint32_t rows,
                                                int q, const Epi& epi, float* s_aux, const EpiPre* pre) {
   switch (kind) {
@@ -245,8 +245,8 @@ __device__ __forceinline__ G4SsPre g4_ss_load(const XBuf& in) {
   const int tid = threadIdx.x, p = tid % 16, c = tid / 16;
   constexpr int kStride = kG4Consumers / 16;
   if (in.ss) {
-    if (c < in.nss) r.a = in.ss[(size_t)c * 16 + p];
-    if (c + kStride < in.nss) r.b = in.ss[(size_t)(c + kStride) * 16 + p];
+    if (c < in.nss) r.a = __ldcg(in.ss + (size_t)c * 16 + p);
+    if (c + kStride < in.nss) r.b = __ldcg(in.ss + (size_t)(c + kStride) * 16 + p);
   }
   return r;
 }
@@ -369,9 +369,9 @@ __device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom&
 // counter by one thread after the consumer barrier) and continues without waiting, and the group's first segment
 // waits (bounded acquire spin) for the other nseg-1 partials, sums them in segment order, resets the counter and
 // runs the epilogue.  Every CTA of the grid is resident (one per SM), so the wait always ends.  Consumer threads
-// only.
+// only.  Returns true in the CTA that ran the group's epilogue.
 template <int NT>
-__device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
+__device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
                          long long U, int G, long long u0, int ppr, int q, uint32_t rows, int epi_kind, const Epi& epi,
                          float* s_scale, int* s_last, const G4SsPre& ss_pre, const XBuf& in, bool& scale_ready,
                          float* s_red, const EpiPre* pre = nullptr) {
@@ -400,7 +400,7 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
   };
   if (nseg > maxseg) {  // partial slots too few for this launch shape: never write past them
     fail_group(kErrPartialSlots);
-    return;
+    return false;
   }
   if (nseg > 1) {
     if (seg > 0) {
@@ -410,7 +410,7 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
       for (int i = tid; i < q * 128; i += kG4Consumers) mine[i] = y[i];
       consumer_sync();
       if (tid == 0) red_release_add(&counters[grp], 1);
-      return;
+      return false;
     }
     if (tid == 0) {
       const bool ok = wait_count(&counters[grp], nseg - 1, epi.err);
@@ -420,7 +420,7 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     consumer_sync();
     if (!*s_last) {
       fail_group(0);  // wait_count raised the flag
-      return;
+      return false;
     }
     const float* all = part + (size_t)grp * maxseg * q * 128;
     for (int i = tid; i < q * 128; i += kG4Consumers) {
@@ -440,6 +440,7 @@ __device__ void g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     consumer_sync();
   }
   g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);
+  return true;
 }
 
 // Geometry of a tiled matrix in the persistent GEMV for `nt` column tiles and units of `usb` superblocks.

@@ -222,36 +222,47 @@ def test_llama8b_first_layer_matches_oracle(ctx, oracle):
     e.close()
 
 
-def test_window_megakernel_matches_chain_and_oracle(ctx, oracle, monkeypatch):
-    """The cooperative window megakernel (CLM_B200_WINDOW_MK=1) computes the same windows as the per-kernel
-    chain: multi-page contexts split over several CTAs per kv head, so every combine path runs."""
+def test_flow_window_matches_chain_and_oracle(ctx, oracle, monkeypatch):
+    """The dataflow window kernel (one cooperative launch per window, the default for windows of <= 16 rows) computes
+    the same windows as the per-kernel chain (CLM_B200_FLOW=0): multi-page contexts split over several CTAs per kv
+    head, so every combine path runs, at q = 1..16 (one and two column tiles)."""
     from llama_oracle import LlamaOracle
 
-    geo = small_geo(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=4, ffn=2048, vocab=1024)
-    monkeypatch.setenv("CLM_B200_WINDOW_MK", "1")
-    mk = make_engine(ctx, geo, max_context=512, max_window=16)
-    monkeypatch.setenv("CLM_B200_WINDOW_MK", "0")
+    geo = small_geo(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=2, ffn=2048, vocab=1024)
+    monkeypatch.setenv("CLM_B200_FLOW", "1")
+    fl = make_engine(ctx, geo, max_context=512, max_window=16)
+    monkeypatch.setenv("CLM_B200_FLOW", "0")
     ch = make_engine(ctx, geo, max_context=512, max_window=16)
     m = LlamaOracle(oracle, geo, max_ctx=512)
     rng = np.random.default_rng(5)
     toks = rng.integers(0, geo.vocab, 400).astype(np.int32)
-    for e in (mk, ch):
+    for e in (fl, ch):
         e.open_session(1)
     pos = 0
-    plan = [(16, 16)] * 20 + [(4, 2), (4, 4), (3, 1), (12, 5)]
+    plan = [(16, 16)] * 20 + [(4, 2), (4, 4), (3, 1), (12, 5), (1, 1), (8, 3)]
     for q, keep in plan:
         w = toks[pos:pos + q]
-        a = mk.run_window(1, pos, tokens=w)
-        n_mk = mk.last_launches()
+        a = fl.run_window(1, pos, tokens=w)
+        n_fl = fl.last_launches()
         b = ch.run_window(1, pos, tokens=w)
         n_ch = ch.last_launches()
-        assert n_mk < n_ch, (n_mk, n_ch)  # the megakernel really ran
+        assert n_fl < n_ch, (n_fl, n_ch)  # the dataflow kernel really ran
         # the two attention schedules round the fp16 probabilities against different running maxima
         assert rel(a, b) < 5e-3, (q, pos, rel(a, b))
         assert rel(a, m.window(w, pos)) < 2e-2
-        mk.commit(1, keep)
+        fl.commit(1, keep)
         ch.commit(1, keep)
         pos += keep
+    # repeated windows (CUDA graph replays) give identical logits
+    w = toks[pos:pos + 4]
+    first = fl.run_window(1, pos, tokens=w)
+    fl.abort(1)
+    for _ in range(3):
+        again = fl.run_window(1, pos, tokens=w)
+        fl.abort(1)
+        assert np.array_equal(first, again)
+    fl.close()
+    ch.close()
 
 
 def _tree16():
