@@ -1663,6 +1663,8 @@ int llama_session_position(const LlamaEngine* e, uint64_t id, uint64_t* committe
   CLM_CHECK(e != nullptr && committed != nullptr, CLM_INVALID_ARGUMENT, "null argument");
   auto it = e->sessions.find(id);
   CLM_CHECK(it != e->sessions.end(), CLM_NOT_FOUND, "session not open");
+  // device-resident rounds advance the position on the device: read it back (waits for the engine's stream)
+  CLM_TRY(sync_pos(const_cast<LlamaEngine*>(e), it->second.get()));
   *committed = (uint64_t)it->second->pos;
   return CLM_OK;
 }

@@ -130,7 +130,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
       const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
       if (i >= q * 128 || row0 + r >= (int)rows) continue;
       float* hp = epi.h + (size_t)p * epi.H + row0 + r;
-      const float hn = (pre ? pre->h[k] : *hp) + y[i] * s_scale[p];
+      const float hn = (pre ? pre->h[k] : __ldcg(hp)) + y[i] * s_scale[p];  // h is written by other CTAs
       *hp = hn;
       y[i] = hn;
     }

@@ -201,8 +201,8 @@ class Oracle:
     def llama_kv_rows(self, dims: "LlamaDims", quant: str, wqkv, attn_norm, kcache, vcache, base: int, h,
                       threads: int = 8) -> None:
         """The K / V rows of positions base..base+len(h)-1 into the caches (max_ctx, kvd), in place."""
-        st = self.L.orc_llama_kv_rows(C.byref(dims), QUANTS[quant], wqkv, _c(attn_norm, F32), _c(h, F32), kcache,
-                                      vcache, base, h.shape[0], threads)
+        st = self.L.orc_llama_kv_rows(C.byref(dims), QUANTS[quant], wqkv, _c(attn_norm, F32), _c(h, F32), base,
+                                      h.shape[0], kcache, vcache, threads)
         if st:
             raise RuntimeError(f"orc_llama_kv_rows failed with code {st}")
 

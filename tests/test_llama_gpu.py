@@ -222,13 +222,15 @@ def test_llama8b_first_layer_matches_oracle(ctx, oracle):
     e.close()
 
 
-def test_flow_window_matches_chain_and_oracle(ctx, oracle, monkeypatch):
+@pytest.mark.parametrize("heads", [(8, 4), (16, 4)])
+def test_flow_window_matches_chain_and_oracle(ctx, oracle, monkeypatch, heads):
     """The dataflow window kernel (one cooperative launch per window, the default for windows of <= 16 rows) computes
     the same windows as the per-kernel chain (CLM_B200_FLOW=0): multi-page contexts split over several CTAs per kv
-    head, so every combine path runs, at q = 1..16 (one and two column tiles)."""
+    head, so every combine path runs, at q = 1..16 (one and two column tiles); GQA groups of 2 (two kv heads share
+    a W_o input chunk) and 4 (one chunk per kv head)."""
     from llama_oracle import LlamaOracle
 
-    geo = small_geo(n_layers=2, hidden=1024, n_heads=8, n_kv_heads=2, ffn=2048, vocab=1024)
+    geo = small_geo(n_layers=2, hidden=1024, n_heads=heads[0], n_kv_heads=heads[1], ffn=2048, vocab=1024)
     monkeypatch.setenv("CLM_B200_FLOW", "1")
     fl = make_engine(ctx, geo, max_context=512, max_window=16)
     monkeypatch.setenv("CLM_B200_FLOW", "0")
