@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -18,6 +19,7 @@
 
 #include "../../include/clm_b200.h"
 #include "clusterlm/domain/drafter.hpp"
+#include "clusterlm/objects/gguf.hpp"
 #include "clusterlm/windows/window_ledger.hpp"
 
 namespace clusterlm::backends {
@@ -38,6 +40,22 @@ using objects::ModelGeometry;
 using objects::ModelManifest;
 
 constexpr std::string_view kFixtureFamily = "clusterlm-fixture";
+// Manifests built from llama.cpp GGUF files name their family "llama.cpp:<architecture>"
+// (runtime/backends/llama/src/llama_manifest.cpp:77); the b200 engine runs the dense "llama" architecture.
+constexpr std::string_view kLlamaFamilyPrefix = "llama.cpp:";
+
+bool is_llama_family(const ModelGeometry& g) { return g.family.rfind(kLlamaFamilyPrefix, 0) == 0; }
+
+// ggml tensor type -> clm_b200 quant id (GGML_TYPE_F32 = 0, Q8_0 = 8, Q4_K = 12); other types pass as -1 - type,
+// which clm_b200_llama_load_tensors refuses by name when the stage needs the tensor.
+int quant_of_ggml(objects::GgmlType t) {
+  switch (static_cast<int>(t)) {
+    case 0: return CLM_QUANT_F32;
+    case 8: return CLM_QUANT_Q8_0;
+    case 12: return CLM_QUANT_Q4_K;
+    default: return -1 - static_cast<int>(t);
+  }
+}
 
 // clm_b200 status codes are ErrorCode values (include/clm_b200.h); the message is the library's thread-local text.
 Status from_clm(int rc, std::string_view what) {
@@ -103,17 +121,18 @@ clm_b200_fixture_geometry fixture_geometry(const ModelGeometry& g, std::vector<s
 
 class B200Domain final : public domain::ExecutionDomain {
  public:
-  B200Domain(ModelManifest manifest, DomainSpec spec, int device)
+  B200Domain(ModelManifest manifest, DomainSpec spec, int device, std::filesystem::path model_dir)
       : manifest_(std::move(manifest)), g_(manifest_.geometry), spec_(spec), device_(device),
-        layout_(domain::BoundaryLayout::for_geometry(g_)) {}
+        layout_(domain::BoundaryLayout::for_geometry(g_)), model_dir_(std::move(model_dir)) {}
   ~B200Domain() override { destroy_engine(); }
 
   Status init() {
     CLM_RETURN_IF_ERROR(manifest_.validate());
-    if (g_.family != kFixtureFamily)
-      return make_error(ErrorCode::kUnimplemented,
-                        "b200 backend serves the clusterlm-fixture family through ExecutionDomain; family '" +
-                            g_.family + "' is not bound to manifests yet");
+    llama_ = is_llama_family(g_);
+    if (g_.family != kFixtureFamily && !llama_)
+      return make_error(ErrorCode::kUnimplemented, "b200 backend serves the clusterlm-fixture and llama.cpp:llama "
+                                                   "families; family '" + g_.family + "' is not implemented");
+    if (llama_) CLM_RETURN_IF_ERROR(init_llama());
     if (spec_.max_context == 0 || spec_.max_window == 0 || spec_.max_sessions == 0 || spec_.max_window > spec_.max_context)
       return invalid("domain spec needs max_context >= max_window >= 1 and max_sessions >= 1");
     if (spec_.layers.end > g_.n_layers || spec_.layers.end < spec_.layers.begin)
@@ -127,6 +146,7 @@ class B200Domain final : public domain::ExecutionDomain {
   domain::BoundaryLayout boundary() const override { return layout_; }
 
   Result<DomainRequirements> describe_requirements() const override {
+    if (llama_) return llama_requirements();
     DomainRequirements r;
     r.required_objects = required_object_names();
     std::uint64_t largest = 0;
@@ -244,6 +264,9 @@ class B200Domain final : public domain::ExecutionDomain {
 
   // The engine and the draft width of a prepared tail that holds the MTP drafter objects (nullptr otherwise).
   clm_b200_engine* drafter_engine() const { return prepared_ && drafter_ready_ ? engine_ : nullptr; }
+  // Drafts per device call: the fixture engine drafts up to max_window tokens, the llama engine max_window - 1.
+  std::uint32_t max_draft() const { return llama_ ? std::max<std::uint32_t>(spec_.max_window, 2) - 1 : spec_.max_window; }
+  std::uint32_t vocab() const { return g_.vocab_size; }
 
   DomainMetrics read_metrics() const override {
     DomainMetrics m = metrics_;
@@ -261,6 +284,7 @@ class B200Domain final : public domain::ExecutionDomain {
   bool has_head() const { return spec_.role == StageRole::kTail; }
 
   std::vector<std::string> required_object_names() const {
+    if (llama_) return llama_object_names();
     std::vector<std::string> names;
     if (spec_.role == StageRole::kPrefix) {
       names.emplace_back(objects::kEmbeddingObjectName);
@@ -276,6 +300,7 @@ class B200Domain final : public domain::ExecutionDomain {
   }
 
   std::uint64_t window_bytes_per_session() const {
+    if (llama_) return 0;  // no per-window state beyond the KV rows the window writes into its pages
     std::uint64_t rec = 0;
     for (std::uint32_t L = spec_.layers.begin; L < spec_.layers.end; ++L)
       rec += g_.layer_kinds[L] == LayerKind::kRecurrent ? 1 : 0;
@@ -283,8 +308,6 @@ class B200Domain final : public domain::ExecutionDomain {
   }
 
   Status create_engine() {
-    std::vector<std::uint8_t> kinds;
-    const clm_b200_fixture_geometry cg = fixture_geometry(g_, kinds);
     clm_b200_stage_spec cs{};
     cs.layer_begin = spec_.layers.begin;
     cs.layer_end = spec_.layers.end;
@@ -292,6 +315,9 @@ class B200Domain final : public domain::ExecutionDomain {
     cs.max_context = spec_.max_context;
     cs.max_window = spec_.max_window;
     cs.max_sessions = spec_.max_sessions;
+    if (llama_) return from_clm(clm_b200_llama_create(ctx_.get(), &lgeo_, &cs, &engine_), "clm_b200_llama_create");
+    std::vector<std::uint8_t> kinds;
+    const clm_b200_fixture_geometry cg = fixture_geometry(g_, kinds);
     return from_clm(clm_b200_fixture_create(ctx_.get(), &cg, &cs, &engine_), "clm_b200_fixture_create");
   }
 
@@ -313,6 +339,7 @@ class B200Domain final : public domain::ExecutionDomain {
   }
 
   Status bind_and_prepare(const objects::ObjectResolver& resolver) {
+    if (llama_) return llama_bind_and_prepare(resolver);
     for (const std::string& name : required_object_names()) CLM_RETURN_IF_ERROR(bind(resolver, name));
     // A Father tail also binds the MTP drafter and the embedding when they are provisioned to it, so that a
     // drafter bound to this domain (make_b200_mtp_drafter(tail)) runs on the same GPU as the head.
@@ -324,6 +351,129 @@ class B200Domain final : public domain::ExecutionDomain {
       CLM_RETURN_IF_ERROR(bind(resolver, std::string(objects::kEmbeddingObjectName)));
       drafter_ready_ = true;
     }
+    return from_clm(clm_b200_engine_prepare(engine_), "clm_b200_engine_prepare");
+  }
+
+  // ---- the llama.cpp family (dense "llama" architecture)
+  // Reads the GGUF tensor directory and metadata of the manifest's shards (model_dir / ShardInfo::file_name) to name
+  // the byte ranges of each object and to complete the engine geometry (RoPE base, RMS epsilon, quantisation).
+  Status init_llama() {
+    if (model_dir_.empty())
+      return precondition("b200 backend: a llama.cpp manifest needs B200BackendOptions::model_dir (the GGUF directory)");
+    std::vector<std::filesystem::path> paths;
+    for (const auto& sh : manifest_.shards) paths.push_back(model_dir_ / sh.file_name);
+    auto files = objects::open_gguf_model(paths);
+    if (!files.is_ok()) return files.status();
+    gguf_ = std::make_unique<objects::GgufModelFiles>(std::move(files).value());
+    const objects::GgufFile& meta = gguf_->meta();
+    auto meta_str = [&](const std::string& k) {
+      const objects::GgufValue* v = meta.find(k);
+      return v != nullptr && v->is_string() ? v->s : std::string{};
+    };
+    auto meta_num = [&](const std::string& k, double dflt) {
+      const objects::GgufValue* v = meta.find(k);
+      if (v == nullptr) return dflt;
+      auto d = v->as_double();
+      return d ? *d : dflt;
+    };
+    const std::string arch = meta_str("general.architecture");
+    if (arch != "llama" || g_.n_experts != 1 || g_.shared_expert_ff != 0)
+      return make_error(ErrorCode::kUnimplemented,
+                        "b200 backend: llama.cpp architecture '" + arch + "' (dense llama only)");
+    for (auto k : g_.layer_kinds)
+      if (k != LayerKind::kFullAttention) return make_error(ErrorCode::kUnimplemented, "b200 backend: recurrent layers");
+    if (gguf_->find_tensor("rope_freqs.weight"))
+      return make_error(ErrorCode::kUnimplemented, "b200 backend: rope_freqs.weight (RoPE frequency factors)");
+    const std::string scaling = meta_str(arch + ".rope.scaling.type");
+    if (!scaling.empty() && scaling != "none")
+      return make_error(ErrorCode::kUnimplemented, "b200 backend: RoPE scaling '" + scaling + "'");
+    auto q = gguf_->find_tensor("blk.0.attn_q.weight");
+    if (!q) return make_error(ErrorCode::kNotFound, "b200 backend: blk.0.attn_q.weight missing");
+    lgeo_.quant = quant_of_ggml(q->info->type);
+    if (lgeo_.quant != CLM_QUANT_Q4_K && lgeo_.quant != CLM_QUANT_Q8_0)
+      return make_error(ErrorCode::kUnimplemented, "b200 backend: matrices must be Q4_K or Q8_0 (llama-quantize --pure)");
+    lgeo_.n_layers = g_.n_layers;
+    lgeo_.hidden = g_.hidden_size;
+    lgeo_.n_heads = g_.n_heads;
+    lgeo_.n_kv_heads = g_.n_kv_heads;
+    lgeo_.head_dim = g_.head_dim;
+    lgeo_.ffn = g_.expert_ff;
+    lgeo_.vocab = g_.vocab_size;
+    lgeo_.rope_theta = static_cast<float>(meta_num(arch + ".rope.freq_base", 10000.0));
+    lgeo_.rms_eps = static_cast<float>(meta_num(arch + ".attention.layer_norm_rms_epsilon", 1e-5));
+    lgeo_.mtp = gguf_->find_tensor("mtp.ffn_gate.weight") ? 1u : 0u;
+    for (std::uint32_t sh = 0; sh < gguf_->shards.size(); ++sh)
+      for (const auto& t : gguf_->shards[sh].tensors) by_offset_[{sh, t.file_offset}] = &t;
+    return Status::ok();
+  }
+
+  // token_embd on the prefix (and on a tail whose head shares it, or whose MTP head needs it), blk.L.dense per
+  // layer, output_head on the tail (llama_manifest.hpp:9-11).
+  std::vector<std::string> llama_object_names() const {
+    std::vector<std::string> names;
+    const bool tail = spec_.role == StageRole::kTail;
+    const bool tied = !gguf_->find_tensor("output.weight");
+    if (spec_.role == StageRole::kPrefix || (tail && (tied || lgeo_.mtp)))
+      names.emplace_back(objects::kEmbeddingObjectName);
+    for (std::uint32_t L = spec_.layers.begin; L < spec_.layers.end; ++L) names.push_back(objects::dense_object_name(L));
+    if (tail) names.emplace_back(objects::kHeadObjectName);
+    return names;
+  }
+
+  Result<DomainRequirements> llama_requirements() const {
+    DomainRequirements r;
+    r.required_objects = llama_object_names();
+    std::uint64_t largest = 0;
+    for (const auto& name : r.required_objects) {
+      const objects::ManifestObject* o = manifest_.find(name);
+      if (o == nullptr) return make_error(ErrorCode::kNotFound, "manifest has no object '" + name + "'");
+      r.gpu_weight_bytes += o->byte_size;  // Q4_K / Q8_0 blocks are repacked losslessly: the same bytes resident
+      largest = std::max(largest, o->byte_size);
+    }
+    // paged fp16 KV cache: every layer of the stage, K and V, max_context positions in 64-position pages
+    const std::uint64_t kvd = std::uint64_t{g_.n_kv_heads} * g_.head_dim;
+    const std::uint64_t ctx_pages = (std::uint64_t{spec_.max_context} + 63) / 64;
+    r.state_bytes = std::uint64_t{spec_.layers.end - spec_.layers.begin} * 2 * ctx_pages * 64 * kvd * 2 *
+                    spec_.max_sessions;
+    r.window_bytes = 0;
+    // window buffers: residual rows, records in and out, the widest activation hand-off, logits and draft rows
+    const std::uint64_t W = spec_.max_window, H = g_.hidden_size, V = g_.vocab_size;
+    const std::uint64_t wide = std::max<std::uint64_t>({H, std::uint64_t{g_.expert_ff}, std::uint64_t{g_.n_heads} * g_.head_dim});
+    r.scratch_bytes = W * (H + 2 * layout_.floats_per_position() + 4 * wide) * 4 +
+                      (spec_.role == StageRole::kTail ? 3 * W * V * 4 : 0);
+    r.staging_bytes = largest;
+    return r;
+  }
+
+  // Binds the stage's tensors from the resolver's object bytes: each source range of an object is one GGUF tensor,
+  // named from the tensor directory by (shard, file offset); the engine repacks them on the device.
+  Status llama_bind_and_prepare(const objects::ObjectResolver& resolver) {
+    std::vector<objects::ProvisionedObject> held;
+    std::vector<clm_b200_tensor> tensors;
+    std::vector<std::string> names;
+    names.reserve(4096);
+    for (const std::string& name : llama_object_names()) {
+      CLM_ASSIGN_OR_RETURN(objects::ProvisionedObject obj, resolver.resolve(name));
+      if (obj.entry == nullptr) return make_error(ErrorCode::kInternal, "resolver returned no manifest entry");
+      if (obj.bytes.size() != obj.entry->byte_size)
+        return make_error(ErrorCode::kDataLoss, "object '" + name + "' has " + std::to_string(obj.bytes.size()) +
+                                                    " bytes, the manifest says " + std::to_string(obj.entry->byte_size));
+      std::uint64_t off = 0;
+      for (const auto& r : obj.entry->source_ranges) {
+        auto it = by_offset_.find({r.shard, r.offset});
+        if (it == by_offset_.end() || it->second->n_bytes != r.length)
+          return make_error(ErrorCode::kVersionMismatch,
+                            "object '" + name + "': a source range is not a tensor of the model directory's GGUF files");
+        names.push_back(it->second->name);
+        tensors.push_back(clm_b200_tensor{nullptr, quant_of_ggml(it->second->type), obj.bytes.data() + off, r.length});
+        off += r.length;
+      }
+      held.push_back(obj);
+    }
+    for (std::size_t i = 0; i < tensors.size(); ++i) tensors[i].name = names[i].c_str();
+    CLM_RETURN_IF_ERROR(from_clm(clm_b200_llama_load_tensors(engine_, tensors.data(), static_cast<std::uint32_t>(tensors.size())),
+                                 "clm_b200_llama_load_tensors"));
+    drafter_ready_ = spec_.role == StageRole::kTail && lgeo_.mtp != 0;
     return from_clm(clm_b200_engine_prepare(engine_), "clm_b200_engine_prepare");
   }
 
@@ -382,6 +532,11 @@ class B200Domain final : public domain::ExecutionDomain {
   DomainSpec spec_;
   int device_;
   domain::BoundaryLayout layout_;
+  std::filesystem::path model_dir_;
+  bool llama_ = false;
+  std::unique_ptr<objects::GgufModelFiles> gguf_;  // llama family: tensor directory of the model's GGUF files
+  std::map<std::pair<std::uint32_t, std::uint64_t>, const objects::GgufTensorInfo*> by_offset_;
+  clm_b200_llama_geometry lgeo_{};
   std::shared_ptr<clm_b200_ctx> ctx_;
   clm_b200_engine* engine_ = nullptr;
   bool prepared_ = false;
@@ -410,7 +565,7 @@ class B200Backend final : public domain::BackendAdapter {
                                                                  const DomainSpec& spec) override {
     const std::uint32_t s = spec.stage.value;
     const int device = s < options_.stage_devices.size() ? options_.stage_devices[s] : options_.default_device;
-    auto d = std::make_unique<B200Domain>(manifest, spec, device);
+    auto d = std::make_unique<B200Domain>(manifest, spec, device, options_.model_dir);
     CLM_RETURN_IF_ERROR(d->init());
     return std::unique_ptr<domain::ExecutionDomain>(std::move(d));
   }
@@ -420,10 +575,13 @@ class B200Backend final : public domain::BackendAdapter {
 };
 
 // MTP drafter on the GPU (MtpFixtureDrafter's step chained count times, drafter.cpp:39-89).  Either bound to a
-// prepared b200 tail domain that holds the drafter objects (it then borrows the tail's engine, so the tail must
-// outlive it), or standalone over a zero-layer tail engine of its own that holds token_embd, output_head and
-// mtp_drafter.  draft() is greedy (argmax, lowest index on ties); propose() keeps the Drafter default (the
-// deterministic draft with one-hot Q, which keeps speculative sampling exact).
+// prepared b200 tail domain that holds the drafter (the fixture's mtp_drafter + token_embd objects, or a llama
+// file's mtp.* tensors; it then borrows the tail's engine, so the tail must outlive it), or standalone over a
+// zero-layer fixture tail engine of its own that holds token_embd, output_head and mtp_drafter.  draft() is greedy
+// (argmax, lowest index on ties).  propose() is MtpFixtureDrafter::propose (drafter.cpp:72-86): with sampling
+// parameters each draft is sampled from distribution(step logits, params) on the device with one uniform of the
+// caller's Rng, drawn in the reference's order, and the proposal carries every draft's distribution (the Q rows
+// of stochastic verification); greedy parameters give the greedy draft without rows.
 class B200MtpDrafter final : public domain::Drafter {
  public:
   static Result<std::unique_ptr<domain::Drafter>> bound(domain::ExecutionDomain& tail) {
@@ -434,7 +592,8 @@ class B200MtpDrafter final : public domain::Drafter {
       return precondition("the b200 tail holds no MTP drafter (mtp_drafter and token_embd not provisioned, or not prepared)");
     auto out = std::unique_ptr<B200MtpDrafter>(new B200MtpDrafter());
     out->engine_ = d->drafter_engine();
-    out->max_draft_ = d->spec().max_window;
+    out->max_draft_ = d->max_draft();
+    out->vocab_ = d->vocab();
     return std::unique_ptr<domain::Drafter>(std::move(out));
   }
 
@@ -467,6 +626,7 @@ class B200MtpDrafter final : public domain::Drafter {
     }
     CLM_RETURN_IF_ERROR(from_clm(clm_b200_engine_prepare(d->owned_), "clm_b200_engine_prepare"));
     d->max_draft_ = cs.max_window;
+    d->vocab_ = g.vocab_size;
     return std::unique_ptr<domain::Drafter>(std::move(d));
   }
 
@@ -489,12 +649,37 @@ class B200MtpDrafter final : public domain::Drafter {
     return out;
   }
 
+  // Drafter::propose has no error channel either: a failed device call yields an empty proposal.
+  domain::DraftProposal propose(std::span<const std::int32_t> committed, std::int32_t next_token, std::uint32_t count,
+                                const domain::SamplingParams& params, domain::Rng& rng) override {
+    if (params.greedy()) return domain::DraftProposal{draft(committed, next_token, count), {}};
+    domain::DraftProposal out;
+    std::int32_t prev = next_token;
+    while (out.tokens.size() < count) {
+      const std::uint32_t n = std::min<std::uint32_t>(count - static_cast<std::uint32_t>(out.tokens.size()), max_draft_);
+      std::vector<double> u(n);
+      for (double& x : u) x = rng.uniform();  // one uniform per draft, as sample_from draws them
+      std::vector<std::int32_t> toks(n, 0);
+      std::vector<float> probs(std::size_t{n} * vocab_);
+      if (clm_b200_mtp_propose(engine_, prev, n, params.temperature, params.top_k, params.top_p, u.data(), toks.data(),
+                               probs.data()) != CLM_OK)
+        return {};
+      for (std::uint32_t j = 0; j < n; ++j) {
+        out.tokens.push_back(toks[j]);
+        out.probs.emplace_back(probs.begin() + std::size_t{j} * vocab_, probs.begin() + std::size_t{j + 1} * vocab_);
+      }
+      prev = out.tokens.back();
+    }
+    return out;
+  }
+
  private:
   B200MtpDrafter() = default;
   std::shared_ptr<clm_b200_ctx> ctx_;
   clm_b200_engine* owned_ = nullptr;   // standalone drafters own their engine
   clm_b200_engine* engine_ = nullptr;  // the engine drafted on (owned_ or a tail domain's)
   std::uint32_t max_draft_ = 1;
+  std::uint32_t vocab_ = 0;
 };
 
 }  // namespace

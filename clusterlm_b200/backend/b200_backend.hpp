@@ -9,6 +9,7 @@
 //
 // This translation unit is compiled against the reference's headers and links its runtime (ledger, status,
 // boundary codec); it is the code a maintainer adds as runtime/backends/b200 (see the integration notes).
+#include <filesystem>
 #include <memory>
 #include <vector>
 
@@ -21,6 +22,10 @@ struct B200BackendOptions {
   // CUDA device of each domain, by StageId (stage index); stages beyond the list use `default_device`.
   std::vector<int> stage_devices;
   int default_device = 0;
+  // Directory of the GGUF files a llama.cpp manifest names (ModelManifest::shards), as LlamaBackendOptions'
+  // model_dir (runtime/backends/llama/src/llama_backend.cpp:307).  Read for the tensor directory and metadata
+  // only: the tensor bytes come from the domain's ObjectResolver at prepare.  Unused for the fixture family.
+  std::filesystem::path model_dir;
 };
 
 // Build hash shared by Father and Nodes (PreparePlan admission).

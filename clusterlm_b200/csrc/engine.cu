@@ -275,6 +275,7 @@ struct LlamaEngine : clm_b200_engine {
   int* bad = nullptr;
   unsigned long long* zero_counter = nullptr;
   RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
+  double* propose_u = nullptr;           // clm_b200_mtp_propose's uniforms [max_window]
   // stage pipeline (link.cuh): input and output links and their device views
   clm_b200_link* pipe_in = nullptr;
   clm_b200_link* pipe_out = nullptr;
@@ -1693,6 +1694,39 @@ int llama_mtp_draft(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint6
   CLM_CUDA(cudaMemcpyAsync(e->zero_counter, &ctr, sizeof(ctr), cudaMemcpyHostToDevice, st));
   CLM_CUDA(cudaStreamSynchronize(st));
   return CLM_OK;
+}
+
+// Stochastic MTP proposal (clm_b200_mtp_propose): each draft sampled from distribution(step logits, T, top-k,
+// top-p) with the caller's uniform, its distribution row returned.
+int llama_mtp_propose(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint32_t top_k, float top_p,
+                      const double* h_uniforms, int32_t* h_tokens, float* h_probs) {
+  if (T <= 0.0f) {  // greedy drafts (argmax chain), one-hot rows
+    const int rc = llama_mtp_draft(e, prev, count, 0.0f, 0, 0, h_tokens, nullptr);
+    if (rc == CLM_OK && h_probs != nullptr) {
+      const size_t V = (size_t)e->d.V;
+      std::memset(h_probs, 0, count * V * sizeof(float));
+      for (uint32_t j = 0; j < count; ++j) h_probs[j * V + (uint32_t)h_tokens[j]] = 1.0f;
+    }
+    return rc;
+  }
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared && e->has_mtp, CLM_FAILED_PRECONDITION, "engine has no MTP head");
+  CLM_CHECK(count >= 1 && count < e->spec.max_window, CLM_OUT_OF_RANGE, "count must be in [1, max_window)");
+  CLM_CHECK(prev >= 0 && prev < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+  CLM_CHECK(h_tokens != nullptr && h_uniforms != nullptr, CLM_INVALID_ARGUMENT, "null argument");
+  cudaStream_t st = e->ctx->stream;
+  if (e->propose_u == nullptr) CLM_TRY(e->alloc_t(&e->propose_u, (size_t)e->wmax()));
+  CLM_CUDA(cudaMemcpyAsync(e->propose_u, h_uniforms, count * sizeof(double), cudaMemcpyHostToDevice, st));
+  CLM_CUDA(cudaMemcpyAsync(e->win, &prev, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+  const size_t V = (size_t)e->d.V;
+  for (uint32_t j = 0; j < count; ++j) {
+    CLM_TRY(e->enqueue_mtp_step(e->win + j, e->draft_logits + j * V, st));
+    CLM_TRY(launch_draft_sample(e->ctx, e->draft_logits + j * V, (uint32_t)V, T, top_k, top_p, e->propose_u + j,
+                                e->dprobs + j * V, e->win + j + 1, e->samp, st));
+  }
+  CLM_CUDA(cudaMemcpyAsync(h_tokens, e->win + 1, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  if (h_probs) CLM_CUDA(cudaMemcpyAsync(h_probs, e->dprobs, count * V * sizeof(float), cudaMemcpyDeviceToHost, st));
+  return e->check_bad(st);
 }
 
 int llama_spec_begin(LlamaEngine* e, uint64_t id, const int32_t* h_prompt, uint32_t n,

@@ -43,6 +43,8 @@ int llama_abort(LlamaEngine* e, uint64_t id);
 int llama_session_position(const LlamaEngine* e, uint64_t id, uint64_t* committed);
 int llama_mtp_draft(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,
                     int32_t* h_tokens, float* h_logits);
+int llama_mtp_propose(LlamaEngine* e, int32_t prev, uint32_t count, float T, uint32_t top_k, float top_p,
+                      const double* h_uniforms, int32_t* h_tokens, float* h_probs);
 int llama_spec_begin(LlamaEngine* e, uint64_t id, const int32_t* h_prompt, uint32_t n, const clm_b200_spec_params* p);
 int llama_spec_round_device(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens,
                             uint32_t* d_count, void* stream);
@@ -68,4 +70,6 @@ int fixture_abort(FixtureEngine* e, uint64_t id);
 int fixture_session_position(const FixtureEngine* e, uint64_t id, uint64_t* committed);
 int fixture_mtp_draft(FixtureEngine* e, int32_t prev, uint32_t count, float T, uint64_t seed, uint64_t counter,
                       int32_t* h_tokens, float* h_logits);
+int fixture_mtp_propose(FixtureEngine* e, int32_t prev, uint32_t count, float T, uint32_t top_k, float top_p,
+                        const double* h_uniforms, int32_t* h_tokens, float* h_probs);
 }  // namespace clm

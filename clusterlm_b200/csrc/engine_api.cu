@@ -133,6 +133,14 @@ int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float T
   return fixture_mtp_draft(fixture(e), prev, count, T, seed, counter, h_tokens, h_logits);
 }
 
+int clm_b200_mtp_propose(clm_b200_engine* e, int32_t prev, uint32_t count, float temperature, uint32_t top_k,
+                         float top_p, const double* h_uniforms, int32_t* h_tokens, float* h_probs) {
+  CLM_TRY(enter(e));
+  if (e->family == CLM_FAMILY_LLAMA)
+    return llama_mtp_propose(llama(e), prev, count, temperature, top_k, top_p, h_uniforms, h_tokens, h_probs);
+  return fixture_mtp_propose(fixture(e), prev, count, temperature, top_k, top_p, h_uniforms, h_tokens, h_probs);
+}
+
 int clm_b200_spec_begin(clm_b200_engine* e, uint64_t id, const int32_t* h_prompt, uint32_t n,
                         const clm_b200_spec_params* p) {
   CLM_TRY(enter(e));

@@ -631,7 +631,7 @@ int fixture_prepare(FixtureEngine* e) {
   if (e->has_head()) CLM_TRY(e->alloc((void**)&e->logits, (size_t)W * P.V * sizeof(float)));
   if (e->obj("mtp_drafter")) {
     CLM_TRY(e->alloc((void**)&e->mtp_logits, (size_t)W * P.V * sizeof(float)));
-    CLM_TRY(e->alloc((void**)&e->mtp_probs, (size_t)P.V * sizeof(float)));
+    CLM_TRY(e->alloc((void**)&e->mtp_probs, (size_t)W * P.V * sizeof(float)));  // one row per draft step
     void* sbase = nullptr;
     CLM_TRY(e->alloc(&sbase, SampleScratch::bytes(1, 1, (uint32_t)P.V)));
     e->samp = SampleScratch::carve(sbase, 1, 1, (uint32_t)P.V);
@@ -831,6 +831,51 @@ int fixture_mtp_draft(FixtureEngine* e, int32_t prev, uint32_t count, float T, u
   }
   cudaStreamSynchronize(st);
   cudaFree(ctr);
+  return rc;
+}
+
+// Stochastic MTP proposal (clm_b200_mtp_propose; MtpFixtureDrafter::propose, drafter.cpp:72-86): each draft is
+// sampled from distribution(step logits, T, top-k, top-p) with the caller's uniform; the rows are returned.
+int fixture_mtp_propose(FixtureEngine* e, int32_t prev, uint32_t count, float T, uint32_t top_k, float top_p,
+                        const double* h_uniforms, int32_t* h_tokens, float* h_probs) {
+  if (T <= 0.0f) {  // greedy drafts (argmax chain), one-hot rows
+    const int rc = fixture_mtp_draft(e, prev, count, 0.0f, 0, 0, h_tokens, nullptr);
+    if (rc == CLM_OK && h_probs != nullptr) {
+      const size_t V = (size_t)e->P.V;
+      std::memset(h_probs, 0, count * V * sizeof(float));
+      for (uint32_t j = 0; j < count; ++j) h_probs[j * V + (uint32_t)h_tokens[j]] = 1.0f;
+    }
+    return rc;
+  }
+  CLM_TRY(ctx_enter(e->ctx));
+  CLM_CHECK(e->prepared && e->obj("mtp_drafter") && e->obj("token_embd"), CLM_FAILED_PRECONDITION,
+            "the MTP drafter needs the mtp_drafter and token_embd objects");
+  CLM_CHECK(count >= 1 && count <= e->spec.max_window, CLM_OUT_OF_RANGE, "count must be in [1, max_window]");
+  CLM_CHECK(h_tokens != nullptr && h_uniforms != nullptr, CLM_INVALID_ARGUMENT, "null argument");
+  const FixParams& P = e->P;
+  CLM_CHECK(prev >= 0 && prev < P.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
+  cudaStream_t st = e->ctx->stream;
+  double* du = nullptr;
+  CLM_CUDA(cudaMalloc(&du, count * sizeof(double)));
+  int rc = CLM_OK;
+  if (cudaMemcpyAsync(du, h_uniforms, count * sizeof(double), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(e->tokens, &prev, sizeof(int32_t), cudaMemcpyHostToDevice, st) != cudaSuccess)
+    rc = fail(CLM_INTERNAL, "uniform / token upload failed");
+  const float* mtp = e->obj("mtp_drafter");
+  for (uint32_t j = 0; j < count && rc == CLM_OK; ++j) {
+    rc = launch_pdl(fixture_mtp_kernel, dim3(1), dim3(256), 0, st, (const float*)e->obj("token_embd"), mtp, mtp + P.H,
+                    P.H, P.V, (const int32_t*)(e->tokens + j), e->mtp_logits + (size_t)j * P.V);
+    if (rc == CLM_OK)
+      rc = launch_draft_sample(e->ctx, e->mtp_logits + (size_t)j * P.V, (uint32_t)P.V, T, top_k, top_p, du + j,
+                               e->mtp_probs + (size_t)j * P.V, e->tokens + j + 1, e->samp, st);
+  }
+  if (rc == CLM_OK) {
+    cudaMemcpyAsync(h_tokens, e->tokens + 1, count * sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+    if (h_probs) cudaMemcpyAsync(h_probs, e->mtp_probs, (size_t)count * P.V * sizeof(float), cudaMemcpyDeviceToHost, st);
+  }
+  const cudaError_t se = cudaStreamSynchronize(st);
+  cudaFree(du);
+  if (rc == CLM_OK && se != cudaSuccess) rc = cuda_fail(se, "mtp propose");
   return rc;
 }
 

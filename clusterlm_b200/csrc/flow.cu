@@ -145,10 +145,14 @@ struct Cursor {
   int slot = 0;
   uint32_t parity = 0;
   PhaseRange R;
+  int rp = -1;  // phase whose range R holds
   __device__ __forceinline__ void settle(const FlowParams& P, int npages) {
-    // skip phases in which this CTA owns no unit
+    // skip phases in which this CTA owns no unit (the range is computed once per phase)
     while (p < P.nphases) {
-      R = phase_range(P.phases[p], npages);
+      if (rp != p) {
+        R = phase_range(P.phases[p], npages);
+        rp = p;
+      }
       if (i < R.n) break;
       ++p;
       i = 0;
@@ -252,12 +256,26 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
         }
       }
     };
-    // whether the produced part of unit c is complete (acquire), and its copies
+    // whether the produced part of unit c is complete: a chunk (GEMV) or kv head (attention) seen complete once is
+    // remembered for the rest of the phase, so the counter is acquired once per chunk, not once per unit; a newly
+    // acquired counter asks for an async-proxy fence before the next copy
+    uint64_t seen = 0;
+    int seen_phase = -1;
+    bool need_fence = false;
     auto late_ready = [&](const Cursor& c) {
       const FlowPhase& ph = P.phases[c.p];
       if (ph.wait == nullptr) return true;
-      if (ph.kind == FLOW_GEMV) return ld_acquire(ph.wait + c.pr) >= ph.wait_target;
-      return committed(c.pr) || ld_acquire(ph.wait + c.grp % ph.a.nkv) >= ph.wait_target;
+      if (ph.kind != FLOW_GEMV && committed(c.pr)) return true;
+      if (seen_phase != c.p) {
+        seen = 0;
+        seen_phase = c.p;
+      }
+      const int chunk = ph.kind == FLOW_GEMV ? c.pr : c.grp % ph.a.nkv;
+      if (chunk < 64 && ((seen >> chunk) & 1ull)) return true;
+      if (ld_acquire(ph.wait + chunk) < ph.wait_target) return false;
+      if (chunk < 64) seen |= 1ull << chunk;
+      need_fence = true;
+      return true;
     };
     auto late = [&](const Cursor& c) {
       const FlowPhase& ph = P.phases[c.p];
@@ -308,7 +326,10 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
         progress = true;
       }
       if (na < nw && late_ready(A)) {
-        fence_proxy_async_global();
+        if (need_fence) {
+          fence_proxy_async_global();
+          need_fence = false;
+        }
         late(A);
         A.next(P, npages);
         ++na;

@@ -1053,6 +1053,29 @@ int launch_accept(const AcceptRows& rows, const int32_t* d_drafts, uint32_t batc
   return launch_sample_job(job, batch, V, s.u, d_next, s, st);
 }
 
+
+// One stochastic draft step: probs = distribution(logits, T, top_k, top_p) for T > 0 (with top-k / top-p the exact
+// reference truncation order, scratch from the context), then out = sample_from(probs, *d_u).
+int launch_draft_sample(clm_b200_ctx* ctx, const float* d_logits, uint32_t V, float T, uint32_t top_k, float top_p,
+                        const double* d_u, float* d_probs, int32_t* d_out, const SampleScratch& s, cudaStream_t st) {
+  if (top_k > 0 || top_p < 1.0f) {
+    void* scr = nullptr;
+    const size_t n = V;
+    CLM_TRY(ctx_scratch(ctx, n * (8 + 8 + 8 + 4 + 4) + 1024, &scr));
+    double* e = static_cast<double*>(scr);
+    unsigned long long* ka = reinterpret_cast<unsigned long long*>(e + n);
+    unsigned long long* kb = ka + n;
+    uint32_t* ia = reinterpret_cast<uint32_t*>(kb + n);
+    uint32_t* ib = ia + n;
+    truncated_distribution_kernel<<<1, kTruncThreads, 0, st>>>(d_logits, V, T, top_k, top_p, e, ka, kb, ia, ib,
+                                                               d_probs);
+    CLM_LAUNCHED("truncated_distribution_kernel");
+  } else {
+    CLM_TRY(launch_probs(d_logits, 1, V, T, nullptr, d_probs, s, st));
+  }
+  return launch_sample_rows(d_probs, 1, V, V, d_u, 0, 0, 0, nullptr, nullptr, d_out, s, st);
+}
+
 }  // namespace clm
 
 using namespace clm;

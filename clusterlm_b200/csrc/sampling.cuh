@@ -52,6 +52,10 @@ int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, cons
 int launch_sample_rows(const float* d_probs, uint32_t rows, uint64_t row_stride, uint32_t V, const double* d_uniforms,
                        uint64_t seed, uint32_t draw, uint32_t stream_id, const unsigned long long* d_counter,
                        const RoundCtl* ctl, int32_t* d_out, const SampleScratch& s, cudaStream_t st);
+// One stochastic draft step: d_probs = distribution(d_logits, T, top_k, top_p) (T > 0; top-k / top-p truncation in
+// the reference's exact order with scratch from the context), then *d_out = sample_from(d_probs, *d_u).
+int launch_draft_sample(clm_b200_ctx* ctx, const float* d_logits, uint32_t V, float T, uint32_t top_k, float top_p,
+                        const double* d_u, float* d_probs, int32_t* d_out, const SampleScratch& s, cudaStream_t st);
 // The rows verify_speculative reads: target P [batch][k+1][V] and draft Q [batch][k][V] as probabilities, or as
 // logits (LP / LQ) whose launch_row_stats statistics are at scratch rows 0.. (target) and q_stats_off.. (draft);
 // the probabilities are then evaluated where they are used, bit-identical to launch_probs' output.  No Q and

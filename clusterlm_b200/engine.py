@@ -236,6 +236,16 @@ class Engine:
     def abort(self, session: int):
         call("clm_b200_abort", self.h, session)
 
+    def mtp_propose(self, prev: int, uniforms, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0):
+        """len(uniforms) drafts after prev, each sampled with its uniform; returns (tokens, probs (count, vocab))."""
+        u = np.ascontiguousarray(uniforms, dtype=np.float64)
+        count = u.size
+        toks = np.zeros(count, np.int32)
+        probs = np.zeros((count, self.vocab), np.float32)
+        call("clm_b200_mtp_propose", self.h, prev, count, temperature, top_k, top_p, u.ctypes.data_as(_vp),
+             toks.ctypes.data_as(_vp), probs.ctypes.data_as(_vp))
+        return toks, probs
+
     def mtp_draft(self, prev: int, count: int, temperature: float = 0.0, seed: int = 0, counter: int = 0,
                   want_logits: bool = False):
         toks = np.zeros(count, np.int32)

@@ -264,6 +264,14 @@ CLM_API int clm_b200_engine_last_launches(const clm_b200_engine* e, uint64_t* la
 CLM_API int clm_b200_mtp_draft(clm_b200_engine* e, int32_t prev, uint32_t count, float temperature, uint64_t seed,
                                uint64_t counter, int32_t* h_tokens, float* h_logits);
 
+/* Stochastic MTP proposal (MtpFixtureDrafter::propose, runtime/domain/src/drafter.cpp:72-86): `count` chained drafts
+ * after `prev`, draft j sampled from distribution(step logits, temperature, top_k, top_p) with the caller's uniform
+ * h_uniforms[j] (the reference's sample_from draws one Rng uniform per draft, in this order).  h_probs (optional)
+ * receives the [count][vocab] draft distributions, the Q rows of verify_speculative.  temperature <= 0: the greedy
+ * draft with one-hot rows (h_uniforms unused). */
+CLM_API int clm_b200_mtp_propose(clm_b200_engine* e, int32_t prev, uint32_t count, float temperature, uint32_t top_k,
+                                 float top_p, const double* h_uniforms, int32_t* h_tokens, float* h_probs);
+
 /* Device-resident speculative decoding on a WHOLE engine: one round = MTP draft of q-1 tokens, the q-row
  * verify window, acceptance (greedy prefix match, coordinator.cpp:1295-1298, or stochastic
  * verify_speculative with Philox draws keyed by (seed, session round)) and commit of accepted + 1

@@ -3,6 +3,7 @@
 // interfaces (runtime/domain/include/clusterlm/domain/backend_adapter.hpp:14-27, execution_domain.hpp:143-174).
 //
 //   backend_parity <scratch dir> [--bench]
+//   backend_parity <scratch dir> --llama <model.gguf>
 //
 // Checks (each prints PASS/FAIL; the exit status is the number of failures):
 //   * greedy speculative generation (ScriptedDrafter, corruption 0.3, q = 4, 32 new tokens; plan 0-4|4-10|10-13|13-16)
@@ -12,12 +13,18 @@
 //   * admission, commit and abort rules (ledger errors, idempotent commit replay, abort then re-run);
 //   * the GPU MTP drafter drafts the same tokens as MtpFixtureDrafter.
 // With --bench it also times windows per second of both pipelines (q = 4 windows, 1 thread each).
+// With --llama, a llama GGUF file's ModelManifest (the reference's build_llama_manifest) drives a 3-stage pipeline of
+// b200 domains (prefix, middle, tail; tensors named from the file's directory, bytes from an ObjectResolver over the
+// file) whose logits must equal, bit for bit, a whole-model engine loaded from the same file through the C ABI; plus
+// the domains' requirements and the stochastic MTP proposal when the file has an MTP head.
 // Activations cross every stage boundary through the wire encoding (StageActivations::encode / decode).
 #include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <filesystem>
+#include <fstream>
+#include <map>
 #include <functional>
 #include <memory>
 #include <string>
@@ -27,8 +34,11 @@
 #include "clusterlm/domain/backend_adapter.hpp"
 #include "clusterlm/domain/drafter.hpp"
 #include "clusterlm/domain/sampling.hpp"
+#include "clusterlm/backends/llama_manifest.hpp"
 #include "clusterlm/objects/canonical_store.hpp"
 #include "clusterlm/objects/fixture_model.hpp"
+#include "clusterlm/objects/gguf.hpp"
+#include "../../include/clm_b200.h"
 #include "../../clusterlm_b200/backend/b200_backend.hpp"
 
 using namespace clusterlm;
@@ -384,6 +394,171 @@ double time_windows(Pipeline& p, int n) {
   return n / std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 
+// ObjectResolver over a model's GGUF files: each object is its source ranges read and concatenated (what a
+// Node's lease store provisions for the manifest).
+class GgufResolver final : public objects::ObjectResolver {
+ public:
+  GgufResolver(const objects::ModelManifest& m, const std::filesystem::path& dir) : m_(m), dir_(dir) {}
+  Result<objects::ProvisionedObject> resolve(std::string_view name) const override {
+    const objects::ManifestObject* o = m_.find(name);
+    if (o == nullptr) return make_error(ErrorCode::kNotFound, "no object " + std::string(name));
+    auto& buf = cache_[std::string(name)];
+    if (buf.empty()) {
+      for (const auto& r : o->source_ranges) {
+        std::ifstream f(dir_ / m_.shards[r.shard].file_name, std::ios::binary);
+        f.seekg(static_cast<std::streamoff>(r.offset));
+        const std::size_t at = buf.size();
+        buf.resize(at + r.length);
+        f.read(reinterpret_cast<char*>(buf.data() + at), static_cast<std::streamsize>(r.length));
+        if (!f) return make_error(ErrorCode::kDataLoss, "short read of " + std::string(name));
+      }
+    }
+    objects::ProvisionedObject p;
+    p.entry = o;
+    p.bytes = std::span<const std::uint8_t>(buf.data(), buf.size());
+    return p;
+  }
+
+ private:
+  const objects::ModelManifest& m_;
+  std::filesystem::path dir_;
+  mutable std::map<std::string, std::vector<std::uint8_t>> cache_;
+};
+
+int llama_mode(const std::filesystem::path& gguf) {
+  auto mm = backends::build_llama_manifest({gguf});
+  if (!mm.is_ok()) {
+    std::fprintf(stderr, "manifest: %s\n", mm.status().to_string().c_str());
+    return 2;
+  }
+  const objects::ModelManifest m = std::move(mm).value();
+  const auto& g = m.geometry;
+  const std::uint32_t V = g.vocab_size, L = g.n_layers;
+  check(g.family == "llama.cpp:llama" && g.residual_streams == 1 && L >= 3, "llama manifest geometry",
+        g.family + " layers " + std::to_string(L));
+  GgufResolver store(m, gguf.parent_path());
+  backends::B200BackendOptions opt;
+  opt.model_dir = gguf.parent_path();
+  auto b200 = backends::make_b200_backend(opt);
+  // the same domains without model_dir are refused at create_domain
+  {
+    auto plain = backends::make_b200_backend();
+    DomainSpec spec;
+    spec.role = StageRole::kPrefix;
+    spec.layers = {0, 1};
+    spec.max_context = 64;
+    spec.max_window = 8;
+    auto d = plain->create_domain(m, spec);
+    check(!d.is_ok() && d.status().code() == ErrorCode::kFailedPrecondition, "llama domain without model_dir refused");
+  }
+  const std::vector<std::uint32_t> plan{0, 1, L - 1, L};
+  auto bp = Pipeline::build(m, store, plan, {b200.get(), b200.get(), b200.get()}, 128, 8);
+  if (!bp) return g_failures;
+  {  // requirements of the middle stage: its layers' objects, the KV pages of its layers
+    const auto req = bp->stages[1]->describe_requirements();
+    std::uint64_t want = 0;
+    for (std::uint32_t l = 1; l + 1 < L; ++l) want += m.find(objects::dense_object_name(l))->byte_size;
+    const std::uint64_t kv = std::uint64_t{L - 2} * 2 * 128 * g.n_kv_heads * g.head_dim * 2 * 4;
+    check(req.is_ok() && req->gpu_weight_bytes == want && req->state_bytes == kv &&
+              req->required_objects.size() == L - 2,
+          "llama middle-stage requirements (weights, KV pages, objects)");
+  }
+  // the whole model through the C ABI from the same file
+  auto files = objects::open_gguf_model({gguf});
+  if (!files.is_ok()) return 2;
+  std::vector<std::vector<std::uint8_t>> data;
+  std::vector<clm_b200_tensor> tensors;
+  std::ifstream f(gguf, std::ios::binary);
+  for (const auto& t : files->shards[0].tensors) {
+    data.emplace_back(t.n_bytes);
+    f.seekg(static_cast<std::streamoff>(t.file_offset));
+    f.read(reinterpret_cast<char*>(data.back().data()), static_cast<std::streamsize>(t.n_bytes));
+    const int ty = static_cast<int>(t.type);
+    tensors.push_back(clm_b200_tensor{t.name.c_str(), ty == 0 ? CLM_QUANT_F32 : ty == 8 ? CLM_QUANT_Q8_0 : ty == 12 ? CLM_QUANT_Q4_K : -1 - ty,
+                                      nullptr, t.n_bytes});
+  }
+  for (std::size_t i = 0; i < tensors.size(); ++i) tensors[i].data = data[i].data();
+  clm_b200_ctx* cx = nullptr;
+  clm_b200_engine* whole = nullptr;
+  clm_b200_llama_geometry lg{};
+  lg.n_layers = L;
+  lg.hidden = g.hidden_size;
+  lg.n_heads = g.n_heads;
+  lg.n_kv_heads = g.n_kv_heads;
+  lg.head_dim = g.head_dim;
+  lg.ffn = g.expert_ff;
+  lg.vocab = V;
+  const objects::GgufValue* th = files->meta().find("llama.rope.freq_base");
+  lg.rope_theta = th ? static_cast<float>(*th->as_double()) : 10000.0f;
+  const objects::GgufValue* ep = files->meta().find("llama.attention.layer_norm_rms_epsilon");
+  lg.rms_eps = ep ? static_cast<float>(*ep->as_double()) : 1e-5f;
+  const auto qt = files->find_tensor("blk.0.attn_q.weight");
+  lg.quant = qt && static_cast<int>(qt->info->type) == 8 ? CLM_QUANT_Q8_0 : CLM_QUANT_Q4_K;
+  lg.mtp = files->find_tensor("mtp.ffn_gate.weight") ? 1 : 0;
+  clm_b200_stage_spec ws{0, L, CLM_ROLE_WHOLE, 128, 8, 1};
+  bool ok = clm_b200_ctx_create(0, &cx) == CLM_OK && clm_b200_llama_create(cx, &lg, &ws, &whole) == CLM_OK &&
+            clm_b200_llama_load_tensors(whole, tensors.data(), static_cast<std::uint32_t>(tensors.size())) == CLM_OK &&
+            clm_b200_engine_prepare(whole) == CLM_OK && clm_b200_session_open(whole, 1) == CLM_OK;
+  check(ok, "whole-model engine from the GGUF file", ok ? "" : clm_b200_last_error());
+  if (!ok) return g_failures;
+  // windows through the pipeline and the whole engine: prefill 8, then q = 4 windows keeping 4, 2, 1, 3
+  check(bp->open().is_ok(), "open llama pipeline sessions");
+  Rng rng(7);
+  std::uint64_t base = 0, state = 0, wid = 0;
+  bool same = true;
+  std::size_t windows = 0;
+  const std::vector<std::pair<std::uint32_t, std::uint32_t>> steps{{8, 8}, {4, 4}, {4, 2}, {4, 1}, {4, 3}};
+  for (auto [q, keep] : steps) {
+    std::vector<std::int32_t> toks(q);
+    for (auto& t : toks) t = static_cast<std::int32_t>(rng.uniform() * V);
+    auto l = bp->run(request(++wid, base, state, q), toks);
+    std::vector<float> want(std::size_t{q} * V);
+    const int rc = clm_b200_run_window(whole, 1, base, q, toks.data(), nullptr, nullptr, want.data());
+    if (!l.is_ok() || rc != CLM_OK) {
+      check(false, "llama window", l.is_ok() ? clm_b200_last_error() : l.status().to_string());
+      return g_failures;
+    }
+    same &= l->data == want;
+    ++windows;
+    CommitRequest c;
+    c.epoch = bp->epoch;
+    c.session = bp->session;
+    c.window = WindowId{wid};
+    c.accepted = keep;
+    c.expected_state = StateVersion{state};
+    auto ack = bp->commit(c);
+    if (!ack.is_ok() || clm_b200_commit(whole, 1, keep) != CLM_OK) {
+      check(false, "llama commit", ack.is_ok() ? clm_b200_last_error() : ack.status().to_string());
+      return g_failures;
+    }
+    state = ack->state.value;
+    base += keep;
+  }
+  check(same, "3-stage llama pipeline (b200 ExecutionDomain over the GGUF manifest) == whole-model engine, bitwise",
+        std::to_string(windows) + " windows");
+  if (lg.mtp) {  // the drafter bound to the llama tail: greedy draft and stochastic proposal rows
+    auto drafter = backends::make_b200_mtp_drafter(*bp->stages.back());
+    check(drafter.is_ok(), "MTP drafter bound to the llama tail", drafter.is_ok() ? "" : drafter.status().to_string());
+    if (drafter.is_ok()) {
+      SamplingParams sp;
+      sp.temperature = 1.0f;
+      Rng r1(11);
+      auto prop = (*drafter)->propose({}, 5, 3, sp, r1);
+      bool rows = prop.tokens.size() == 3 && prop.probs.size() == 3;
+      for (std::size_t j = 0; rows && j < 3; ++j) {
+        double tot = 0.0;
+        for (float v : prop.probs[j]) tot += v;
+        rows &= prop.probs[j].size() == V && std::fabs(tot - 1.0) < 1e-3 && prop.probs[j][prop.tokens[j]] > 0.0f;
+      }
+      check(rows, "llama MTP proposal: 3 drafts with their distributions");
+    }
+  }
+  clm_b200_engine_destroy(whole);
+  clm_b200_ctx_destroy(cx);
+  std::printf("%d failure(s)\n", g_failures);
+  return g_failures;
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -391,6 +566,7 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "usage: backend_parity <scratch dir> [--bench]\n");
     return 2;
   }
+  if (argc > 3 && std::strcmp(argv[2], "--llama") == 0) return llama_mode(argv[3]);
   const std::filesystem::path dir = std::filesystem::path(argv[1]) / "fixture";
   const bool bench = argc > 2 && std::strcmp(argv[2], "--bench") == 0;
   std::filesystem::create_directories(dir);
@@ -467,6 +643,36 @@ int main(int argc, char** argv) {
         same &= a == b && a.size() == 11;
       }
       check(same, "standalone GPU MTP drafter drafts the reference's tokens (16 starts x 11 steps)");
+      // stochastic proposals (MtpFixtureDrafter::propose, drafter.cpp:72-86) from the same Rng: the same tokens, and
+      // distribution rows within one ulp (the double exp and kept-sum order of the device's distribution)
+      bool same_tokens = true;
+      std::size_t entries = 0, off_by_one = 0, worse = 0;
+      for (int variant = 0; variant < 2; ++variant) {
+        SamplingParams sp;
+        sp.temperature = variant == 0 ? 1.0f : 0.8f;
+        sp.top_k = variant == 0 ? 0 : 40;
+        sp.top_p = variant == 0 ? 1.0f : 0.9f;
+        for (std::int32_t start = 0; start < 8; ++start) {
+          Rng ra(100 + start), rb(100 + start);
+          auto a = (*md)->propose({}, start * 29 % static_cast<std::int32_t>(V), 7, sp, ra);
+          auto b = (*bd)->propose({}, start * 29 % static_cast<std::int32_t>(V), 7, sp, rb);
+          same_tokens &= a.tokens == b.tokens && a.probs.size() == b.probs.size();
+          for (std::size_t j = 0; j < std::min(a.probs.size(), b.probs.size()); ++j)
+            for (std::size_t i = 0; i < a.probs[j].size() && i < b.probs[j].size(); ++i) {
+              std::int32_t x, y;
+              std::memcpy(&x, &a.probs[j][i], 4);
+              std::memcpy(&y, &b.probs[j][i], 4);
+              const std::int64_t d = std::llabs(static_cast<std::int64_t>(x) - y);
+              ++entries;
+              off_by_one += d == 1;
+              worse += d > 1;
+            }
+        }
+      }
+      char pb[160];
+      std::snprintf(pb, sizeof pb, "%zu entries, %zu off by 1 ulp, %zu by more", entries, off_by_one, worse);
+      check(same_tokens && worse == 0, "GPU MTP proposal == MtpFixtureDrafter::propose (T=1; T=0.8 top-k 40 top-p 0.9)",
+            pb);
 
       // speculative generation with MTP drafts: reference pipeline + MtpFixtureDrafter against the b200 pipeline +
       // the drafter bound to its tail

@@ -51,3 +51,27 @@ def test_dropin_pipelines_match_reference(tmp_path):
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "0 failure(s)" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("quant", ["q4_k", "q8_0"])
+def test_llama_manifest_pipeline_through_execution_domain(tmp_path, oracle, quant):
+    """The Llama family behind ExecutionDomain: a llama GGUF file (written by gguf-py in llama.cpp's tensor names) is
+    turned into a ModelManifest by the reference's own build_llama_manifest; a prefix / middle / tail pipeline of b200
+    domains binds its tensors from an ObjectResolver over the file and must give the logits of a whole-model engine
+    loaded from the same file, bit for bit; the domains' requirements and the MTP proposal are checked too."""
+    import sys
+
+    _need_driver()
+    pytest.importorskip("gguf")
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_gguf_gpu import _write_model
+    from test_llama_gpu import small_geo
+
+    geo = small_geo(quant, n_layers=4)
+    path = tmp_path / "llama.gguf"
+    _write_model(path, oracle, geo)
+    r = subprocess.run([DRIVER, str(tmp_path), "--llama", str(path)], capture_output=True, text=True, timeout=600)
+    print(r.stdout)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "0 failure(s)" in r.stdout

@@ -117,13 +117,17 @@ def test_greedy_generation_agrees_with_oracle_8b_width(ctx, oracle):
 
     geo = dataclasses.replace(LLAMA3_8B, n_layers=2)
     n_prompt, n_new = 12, 100
-    eng = Engine(ctx, geo, 0, 2, ROLE_WHOLE, 256, 16, 1)
+    eng = Engine(ctx, geo, 0, 2, ROLE_WHOLE, 256, 16, 2)
     eng.generate_weights(seed=0, stddev=0.02)
     eng.prepare()
     eng.open_session(1)
     prompt = np.random.default_rng(50).integers(0, geo.vocab, n_prompt).astype(np.int32)
     eng.spec_begin(1, prompt, 4)
-    out = []
+    # the first generated token is the prefill's argmax (spec_begin keeps it as the next window's first token and
+    # the rounds emit what follows it): the same prompt through a plain window on a second session gives it
+    eng.open_session(2)
+    first = int(np.argmax(eng.run_window(2, 0, tokens=prompt)[-1]))
+    out = [first]
     while len(out) < n_new:
         out += list(eng.spec_round(1, 4))
     eng.close()
