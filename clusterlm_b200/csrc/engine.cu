@@ -1242,11 +1242,11 @@ int llama_prepare(LlamaEngine* e) {
                                                                                d.theta);
     CLM_LAUNCHED("rope_table_kernel");
   }
-  // dataflow window kernel (windows of <= 16 rows without a tree): one cooperative grid per column-tile count; on
-  // by default, CLM_B200_FLOW=0 keeps every window on the per-kernel chain
+  // dataflow window kernel (windows of <= 16 rows without a tree): one cooperative grid per column-tile count;
+  // opt-in with CLM_B200_FLOW=1 (the per-kernel chain is faster on the measured shapes)
   {
     const char* env = getenv("CLM_B200_FLOW");
-    const bool want = !(env && env[0] == '0') && e->flow_shape_ok();
+    const bool want = env && env[0] == '1' && e->flow_shape_ok();
     const int G = e->ctx->sm_count;
     e->flow_attn_maxseg = (G + d.nkv - 1) / d.nkv + 1;  // bound for one m-tile (more m-tiles: fewer segments)
     if (want && e->flow_attn_maxseg <= 64) {
