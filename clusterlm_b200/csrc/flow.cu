@@ -78,6 +78,18 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// One potentially blocking test of a barrier phase (mbarrier.try_wait: the thread may be suspended until the phase
+// completes or a hardware time limit passes); true if the phase completed.
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // mbarrier wait of a consumer: bounded, and returns false at once once the error flag is raised.
 __device__ bool flow_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   const uint32_t a = smem_addr(bar);
@@ -100,6 +112,11 @@ __device__ bool flow_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
       }
     }
   }
+}
+
+// Arrival with a count (a warp that stands for several of the barrier's expected arrivals).
+__device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
 }
 
 // Removes `bytes` of expected transactions from the current phase of a barrier (copies that will not be issued).
@@ -302,10 +319,29 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
       return committed(c.pr) ? 0u : 2 * kPageBytes;
     };
 
-    Cursor W, A;
+    // L2 lookahead: the immutable parts of the next kLookahead units beyond the ring are prefetched into L2 (no
+    // shared memory, nothing to wait for), so HBM keeps streaming weights while the ring waits on a dependency
+    auto prefetch = [&](const Cursor& c) {
+      const FlowPhase& ph = P.phases[c.p];
+      if (ph.kind == FLOW_GEMV) {
+        const FlowGemv& m = ph.g;
+        const int nsb = min(2, m.geo.sb - 2 * c.pr);
+        const uint8_t* src = m.tiles + ((size_t)c.grp * m.geo.sb + 2 * c.pr) * m.geo.sb_bytes;
+        const uint32_t bytes = (uint32_t)(nsb * m.geo.sb_bytes);
+        for (uint32_t o = 0; o < bytes; o += 32768u) bulk_prefetch_l2(src + o, min(32768u, bytes - o));
+      } else if (committed(c.pr)) {
+        const FlowAttn& a = ph.a;
+        const size_t off = ((size_t)a.pages[c.pr] * a.nkv + c.grp % a.nkv) * 64 * kHd;
+        bulk_prefetch_l2(a.kpool + off, kPageBytes);
+        bulk_prefetch_l2(a.vpool + off, kPageBytes);
+      }
+    };
+    constexpr long long kLookahead = 4;
+    Cursor W, A, F;
     W.settle(P, npages);
     A.settle(P, npages);
-    long long nw = 0, na = 0;  // units whose immutable / produced parts are requested
+    F.settle(P, npages);
+    long long nw = 0, na = 0, nf = 0;  // units whose immutable / produced parts are requested, units prefetched
     // the first stages' weights stream in while the previous kernel finishes; the stage input (phase 0's
     // activations) and every write are ordered after griddepcontrol.wait
     while (!W.done(P) && nw < P.stages && (P.phases[W.p].kind == FLOW_GEMV || committed(W.pr))) {
@@ -313,10 +349,15 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
       W.next(P, npages);
       ++nw;
     }
+    while (nf < nw) {  // the lookahead cursor starts where the ring stops
+      F.next(P, npages);
+      ++nf;
+    }
     griddep_wait();
     griddep_launch();
     bool ok = true;
     unsigned long long idle_since = 0;
+    uint32_t idle = 0;  // consecutive turns without progress
     while (ok && !A.done(P)) {
       bool progress = false;
       if (!W.done(P) && mbar_test(&empty[W.slot], W.parity ^ 1u)) {
@@ -335,23 +376,43 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
         ++na;
         progress = true;
       }
+      if (nf < nw) {  // units the ring requested itself need no prefetch
+        F = W;
+        nf = nw;
+      }
+      if (!F.done(P) && nf < nw + kLookahead) {
+        prefetch(F);
+        F.next(P, npages);
+        ++nf;
+        progress = true;
+      }
       if (progress) {
-        idle_since = 0;
+        idle = 0;
         continue;
       }
-      if (failed(err)) {
-        ok = false;
-        break;
+      // idle: with every produced part requested the only thing to wait for is a free ring slot, so the producer
+      // blocks on that slot's barrier (mbarrier.try_wait suspends until the slot is released or a short hardware
+      // limit); while a produced part is outstanding it polls its counter.  The error flag and the clock are read
+      // every 64th idle turn only (each is a global-memory round trip).
+      if (na == nw && !W.done(P)) {
+        mbar_try(&empty[W.slot], W.parity ^ 1u);
+      } else {
+        __nanosleep(32);
       }
-      const unsigned long long now = globaltimer();
-      if (idle_since == 0) {
-        idle_since = now;
-      } else if (now - idle_since > kWaitNs) {
-        raise(err);
-        ok = false;
-        break;
+      if ((++idle & 63) == 0) {
+        if (failed(err)) {
+          ok = false;
+          break;
+        }
+        const unsigned long long now = globaltimer();
+        if (idle_since == 0 || idle == 64) {
+          idle_since = now;
+        } else if (now - idle_since > kWaitNs) {
+          raise(err);
+          ok = false;
+          break;
+        }
       }
-      __nanosleep(32);
     }
     if (!ok) {
       // requested immutable parts whose produced part will not come: balance their barriers so the copies already
@@ -406,6 +467,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
       G4Acc<NT> acc;
       acc.zero();
       int cur = grp;
+      const int my_group = warp / kGemvWarps, rt = warp % kGemvWarps;
       auto flush = [&](int gi) {
         if (!scale_ready) {
           // the row scale needs every row group of the previous residual phase
@@ -415,8 +477,14 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
           g4_ss_finish(ss_pre, m.in, m.epi, q, s_red, s_scale);
           scale_ready = true;
         }
+        // the residual epilogue's operands (residual rows, next norm weights): every unit of the group is consumed,
+        // so the rows other CTAs wrote before this phase are final; their loads overlap the segment reduction
+        EpiPre pre;
+        const bool resid = m.epi_kind == EPI_RESID_PREP;
+        if (resid) epi_preload<EPI_RESID_PREP>(pre, gi, m.rows, q, m.epi);
         const bool ran = g4_flush<NT>(gi, acc, y, m.part, m.counters, m.maxseg, R.U, G, R.u0, R.per, q, m.rows,
-                                      m.epi_kind, m.epi, s_scale, &s_last, G4SsPre{}, m.in, scale_ready, s_red);
+                                      m.epi_kind, m.epi, s_scale, &s_last, G4SsPre{}, m.in, scale_ready, s_red,
+                                      resid ? &pre : nullptr);
         if (ran) {
           if (ph.sig != nullptr) {
             int c = gi / ph.sig_div;
@@ -435,11 +503,15 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
           cur = grp;
           acc.zero();
         }
-        const int nsb = min(2, m.geo.sb - 2 * pr);
-        if (flow_mbar_wait(&full[rs_slot], rs_parity, err))
-          g4_consume_unit<Raw, NT>(ring + (size_t)rs_slot * P.stage_bytes, m.geo, nsb, warp, lane, acc);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[rs_slot]);
+        // the two groups of 8 warps take alternate units (warp: row tile rt of both superblocks), so their
+        // dequantisation bursts interleave; each warp's release stands for two of the slot's 16 arrivals
+        if ((i & 1) == my_group) {
+          const int nsb = min(2, m.geo.sb - 2 * pr);
+          if (flow_mbar_wait(&full[rs_slot], rs_parity, err))
+            g4_consume_pair<Raw, NT>(ring + (size_t)rs_slot * P.stage_bytes, m.geo, nsb, rt, lane, acc);
+          __syncwarp();
+          if (lane == 0) mbar_arrive_n(&empty[rs_slot], 2);
+        }
         ring_next();
         if (++pr == R.per) {
           pr = 0;
@@ -538,16 +610,24 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
           for (int s = 0; s < nseg; ++s) cw[s * 16 + tid] *= inv;
         }
         consumer_sync();
-        {  // thread -> (row r, 4 columns)
+        {  // thread -> (row r, 4 columns); eight partials' loads in flight at a time, summed in segment order
           const int r = tid / 32, c4 = (tid % 32) * 4;
           float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          for (int s = 0; s < nseg; ++s) {
-            const float w = cw[s * 16 + r];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(allp + ((size_t)s * 16 + r) * kRW + c4));
-            acc4[0] += v.x * w;
-            acc4[1] += v.y * w;
-            acc4[2] += v.z * w;
-            acc4[3] += v.w * w;
+          const float4* src = reinterpret_cast<const float4*>(allp + (size_t)r * kRW + c4);
+          const size_t seg_stride = (size_t)16 * kRW / 4;  // float4 units between segments
+          for (int s0 = 0; s0 < nseg; s0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = s0 + k < nseg ? __ldcg(src + (s0 + k) * seg_stride) : make_float4(0, 0, 0, 0);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              if (s0 + k >= nseg) break;
+              const float w = cw[(s0 + k) * 16 + r];
+              acc4[0] += v[k].x * w;
+              acc4[1] += v[k].y * w;
+              acc4[2] += v[k].z * w;
+              acc4[3] += v[k].w * w;
+            }
           }
           o_s[r * kHd + c4] = acc4[0];
           o_s[r * kHd + c4 + 1] = acc4[1];
