@@ -291,6 +291,20 @@ struct LlamaEngine : clm_b200_engine {
   float hi_scale() const { return d.quant == CLM_QUANT_Q4_K ? 0.0625f : 1.0f; }
   int wmax() const { return (int)spec.max_window; }
 
+  // pinned host staging of the host-buffer window calls (grown on demand, freed with the engine)
+  void* pin_in = nullptr;
+  void* pin_out = nullptr;
+  size_t pin_in_bytes = 0, pin_out_bytes = 0;
+  int pinned(void** buf, size_t* cap, size_t bytes) {
+    if (bytes <= *cap) return CLM_OK;
+    if (*buf) CLM_CUDA(cudaFreeHost(*buf));
+    *buf = nullptr;
+    *cap = 0;
+    CLM_CUDA(cudaHostAlloc(buf, bytes, cudaHostAllocDefault));
+    *cap = bytes;
+    return CLM_OK;
+  }
+
   int alloc(void** p, size_t bytes) {
     CLM_CUDA(cudaMalloc(p, bytes));
     allocations.push_back(*p);
@@ -888,6 +902,8 @@ struct LlamaEngine : clm_b200_engine {
     free_m(mtp_gu);
     free_m(mtp_down);
     for (void* p : allocations) cudaFree(p);
+    if (pin_in) cudaFreeHost(pin_in);
+    if (pin_out) cudaFreeHost(pin_out);
   }
 };
 
@@ -1484,14 +1500,21 @@ static int run_window_host(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t 
   }
   CLM_TRY(run_window_common(e, id, base, q, st, &s));
   const size_t rec = (size_t)q * e->floats_per_position() * sizeof(float);
+  const size_t out_bytes = e->has_head ? (size_t)q * e->d.V * sizeof(float) : rec;
+  // the caller's buffers are pageable (records arriving from another host, logits for the acceptance): they pass
+  // through pinned staging buffers of the engine, so both copies are DMA transfers at full link speed
+  CLM_TRY(e->pinned(&e->pin_in, &e->pin_in_bytes, std::max(rec, (size_t)q * sizeof(int32_t))));
+  CLM_TRY(e->pinned(&e->pin_out, &e->pin_out_bytes, out_bytes));
   if (e->has_tokens) {
     CLM_CHECK(h_tokens != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes tokens");
     for (uint32_t i = 0; i < q; ++i)
       CLM_CHECK(h_tokens[i] >= 0 && h_tokens[i] < e->d.V, CLM_INVALID_ARGUMENT, "token outside the vocabulary");
-    CLM_CUDA(cudaMemcpyAsync(e->win, h_tokens, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    std::memcpy(e->pin_in, h_tokens, q * sizeof(int32_t));
+    CLM_CUDA(cudaMemcpyAsync(e->win, e->pin_in, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
   } else {
     CLM_CHECK(h_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
-    CLM_CUDA(cudaMemcpyAsync(e->bin, h_in, rec, cudaMemcpyHostToDevice, st));
+    std::memcpy(e->pin_in, h_in, rec);
+    CLM_CUDA(cudaMemcpyAsync(e->bin, e->pin_in, rec, cudaMemcpyHostToDevice, st));
   }
   if (h_parents != nullptr) {
     CLM_CUDA(cudaMemcpyAsync(e->parents, h_parents, q * sizeof(int32_t), cudaMemcpyHostToDevice, st));
@@ -1501,13 +1524,11 @@ static int run_window_host(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t 
     CLM_TRY(e->run_graph(*s, 0, (int)q, 0, st,
                          [&](cudaStream_t cs) { return e->enqueue_window(*s, (int)q, e->win, cs); }));
   }
-  if (e->has_head) {
-    if (h_logits)
-      CLM_CUDA(cudaMemcpyAsync(h_logits, e->logits, (size_t)q * e->d.V * sizeof(float), cudaMemcpyDeviceToHost, st));
-  } else if (h_out) {
-    CLM_CUDA(cudaMemcpyAsync(h_out, e->bout, rec, cudaMemcpyDeviceToHost, st));
-  }
+  float* h_dst = e->has_head ? h_logits : h_out;
+  if (h_dst)
+    CLM_CUDA(cudaMemcpyAsync(e->pin_out, e->has_head ? e->logits : e->bout, out_bytes, cudaMemcpyDeviceToHost, st));
   CLM_CUDA(cudaStreamSynchronize(st));
+  if (h_dst) std::memcpy(h_dst, e->pin_out, out_bytes);
   s->outstanding = q;
   s->tree = h_parents != nullptr;
   if (h_parents)
