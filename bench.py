@@ -854,6 +854,67 @@ def run_b200(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def sharded_head_micro(ctx, dev, world, rank, steps=20):
+    """The vocab-sharded LM head on the N GPUs of the pipeline job (NCCL): the 8B head (128,256 x 4,096, Q4_K)
+    split by vocabulary, one q = 4 verify window per step: the shard logits, the global statistics of the target
+    and draft rows and the speculative acceptance over the shards.  Event-timed on each rank, max over ranks;
+    rank 0 also times the unsharded head and clm_b200_accept_logits on its own GPU."""
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.engine import LLAMA3_8B
+    from clusterlm_b200.runtime import Matrix, accept_logits, encode, generate_weights
+    from clusterlm_b200.sharded_head import ShardedHead, shard_bounds
+
+    V, H = LLAMA3_8B.vocab, LLAMA3_8B.hidden
+    v0, v1 = shard_bounds(V, world)[rank]
+    head = ShardedHead(ctx, "q4_k", encode(ctx, "q4_k", generate_weights(ctx, SEED, 1001, v0 * H, (v1 - v0) * H, 0.02)),
+                       V, H)
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn((2 * Q - 1, H), generator=g)).to(dev)
+    drafts = [int(d) for d in np.random.default_rng(4).integers(0, V, Q - 1)]
+
+    def step(i):
+        L = head.logits(x)
+        return head.accept(L[:Q].contiguous(), L[Q:].contiguous(), drafts, TEMPERATURE, seed=SEED, counter_base=i)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for i in range(steps):
+        step(i)
+    s1.record()
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(world, s0.elapsed_time(s1) / steps, dev)
+    head.close()
+    out = {"config": f"8B head {V} x {H} Q4_K split by vocabulary over {world} GPUs ({v1 - v0} columns on rank "
+                     f"{rank}), q={Q} window, T={TEMPERATURE:g}, stochastic drafts; logits + global max / kept "
+                     "(NCCL all-gathers in column order) + acceptance", "ms_per_window": ms}
+    if rank == 0:
+        whole = Matrix(ctx, "q4_k", encode(ctx, "q4_k", generate_weights(ctx, SEED, 1001, 0, V * H, 0.02)), V, H)
+        dd = torch.tensor([drafts], dtype=torch.int32, device=dev)
+
+        def one(i):
+            L = whole.matmul_rows(x)
+            return accept_logits(ctx, L[:Q].reshape(1, Q, V), L[Q:].reshape(1, Q - 1, V), dd, TEMPERATURE, seed=SEED,
+                                 counter_base=i)
+
+        for i in range(3):
+            one(i)
+        torch.cuda.synchronize(dev)
+        s0.record()
+        for i in range(steps):
+            one(i)
+        s1.record()
+        torch.cuda.synchronize(dev)
+        out["unsharded_ms_per_window"] = s0.elapsed_time(s1) / steps
+        whole.close()
+    return out
+
+
 def run_pipeline(args, world, rank, local):
     """N > 1: the stage pipeline (clusterlm_b200.pipeline) with `inflight` sequences."""
     import numpy as np
@@ -884,11 +945,15 @@ def run_pipeline(args, world, rank, local):
                          weight_seed=SEED)
     stream = torch.cuda.ExternalStream(pipe.engine.stream(), device=dev)
     t0 = time.perf_counter()
+    rows = []
     for s in range(2 * S):
         prompt = np.random.default_rng(1234 + s % S).integers(0, geo.vocab, context).astype(np.int32)
         pipe.open_session(s + 1)
-        row = pipe.prefill(s + 1, prompt)
-        pipe.begin(s + 1, row, Q, TEMPERATURE, SEED)
+        rows.append(pipe.prefill(s + 1, prompt))
+    # a stage's inbound link is one FIFO for all sessions: a session's first window is sent only when its rounds
+    # are next, so that the messages stay in the order the rounds are issued
+    for s in range(S):
+        pipe.begin(s + 1, rows[s], Q, TEMPERATURE, SEED)
     pipe.status()
     barrier(world)
     prefill_s = max_over_ranks(world, time.perf_counter() - t0, dev) / 2
@@ -936,6 +1001,8 @@ def run_pipeline(args, world, rank, local):
                         hcnt[k, s].copy_(e_cnt[s], non_blocking=True)
         stream.synchronize()
 
+    for s in range(S, 2 * S):
+        pipe.begin(s + 1, rows[s], Q, TEMPERATURE, SEED)
     host_rounds(0, args.warmup)
     torch.cuda.synchronize(dev)
     barrier(world)
@@ -946,7 +1013,7 @@ def run_pipeline(args, world, rank, local):
     same = 0
     if pipe.is_tail:
         dc, dt = cnt.cpu().numpy(), toks.cpu().numpy()
-        hc, ht = hcnt.numpy(), host.numpy()
+        hc, ht = hcnt.numpy().copy(), host.numpy().copy()  # copies: a view would keep the pinned buffers alive
         same = int(np.array_equal(dc, hc) and all(np.array_equal(dt[k, s_, :dc[k, s_]], ht[k, s_, :hc[k, s_]])
                                                   for k in range(n_rounds) for s_ in range(S)))
     same_all = max_over_ranks(world, same, dev) if world > 1 else same
@@ -956,6 +1023,7 @@ def run_pipeline(args, world, rank, local):
     del host, hcnt, e_toks, e_cnt, toks, cnt
     torch.cuda.synchronize(dev)
     pipe.close(lambda: barrier(world))
+    sharded = sharded_head_micro(ctx, dev, world, rank) if not profile_case(args) else None
     ctx.close()
     if rank != 0:
         return
@@ -981,6 +1049,8 @@ def run_pipeline(args, world, rank, local):
                      "algorithmic_bytes_per_round": round_bytes(geo, context)},
         "clocks": clk,
     }
+    if sharded:
+        line["sharded_head"] = sharded
     print(json.dumps(line), flush=True)
 
 

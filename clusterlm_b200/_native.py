@@ -82,6 +82,8 @@ _SIGS = {
     "clm_b200_engine_last_launches": (_i, [_vp, C.POINTER(_u64)]),
     "clm_b200_mtp_draft": (_i, [_vp, C.c_int32, _u32, _f, _u64, _u64, _vp, _vp]),
     "clm_b200_mtp_propose": (_i, [_vp, C.c_int32, _u32, _f, _u32, _f, _vp, _vp, _vp]),
+    "clm_b200_shard_stats": (_i, [_vp, _vp, _u32, _u32, _u64, _f, _vp, _vp, _vp]),
+    "clm_b200_shard_probs": (_i, [_vp, _vp, _u32, _u32, _f, _vp, _vp, _vp, _vp]),
     "clm_b200_spec_begin": (_i, [_vp, _u64, _vp, _u32, _vp]),
     "clm_b200_spec_round": (_i, [_vp, _u64, _vp, _vp, _vp]),
     "clm_b200_spec_round_device": (_i, [_vp, _u64, _vp, _vp, _vp, _vp]),

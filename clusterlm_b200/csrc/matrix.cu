@@ -67,7 +67,14 @@ int matrix_create(clm_b200_ctx* ctx, int quant, const void* bytes, bool device_s
   int status = CLM_OK;
   do {
     const void* src = bytes;
-    if (!device_src) {
+    if (device_src) {
+      // the bytes may still be in flight on another stream of the caller (an encode, a copy): wait for the device
+      cudaError_t e = cudaDeviceSynchronize();
+      if (e != cudaSuccess) {
+        status = cuda_fail(e, "cudaDeviceSynchronize(matrix upload)");
+        break;
+      }
+    } else {
       cudaError_t e = cudaMalloc(&staging, nbytes);
       if (e != cudaSuccess) {
         status = cuda_fail(e, "cudaMalloc(matrix staging)");

@@ -483,19 +483,11 @@ __global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* 
   }
 }
 
-__global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* __restrict__ logits, uint32_t V,
-                                                                   uint32_t off, float T,
-                                                                   const RoundCtl* __restrict__ ctl,
-                                                                   const float* __restrict__ mx,
-                                                                   double* __restrict__ csum, double* __restrict__ kept,
-                                                                   int* __restrict__ cnt) {
-  griddep_wait();
-  griddep_launch();
-  T = read_temperature(T, ctl);
-  const uint32_t c = blockIdx.x, C = gridDim.x;
-  const float* l = logits + (size_t)blockIdx.y * V;
-  const uint32_t r = blockIdx.y + off;
-  const float m = mx[r];
+// The double sum of the softmax terms of chunk c (entries [c * kStatsChunk, ..) of the row l of V entries) against
+// the row maximum m, in one fixed order (thread-strided float4 lanes, four accumulators, block reduction); the
+// block's threads all return the chunk's sum.  Shared by the whole-row statistics and the vocab-shard statistics,
+// so a shard that starts at a chunk boundary reproduces the whole row's chunk sums bit for bit.
+__device__ __forceinline__ double chunk_soft_sum(const float* __restrict__ l, uint32_t V, uint32_t c, float m, float T) {
   const uint32_t lo = c * kStatsChunk, hi = min(V, lo + kStatsChunk);
   double acc = 0.0;
   if ((V & 3u) == 0) {
@@ -512,7 +504,22 @@ __global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* 
   } else {
     for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) acc += soft_term(l[i], m, T);
   }
-  acc = block_sum_d(acc);
+  return block_sum_d(acc);
+}
+
+__global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* __restrict__ logits, uint32_t V,
+                                                                   uint32_t off, float T,
+                                                                   const RoundCtl* __restrict__ ctl,
+                                                                   const float* __restrict__ mx,
+                                                                   double* __restrict__ csum, double* __restrict__ kept,
+                                                                   int* __restrict__ cnt) {
+  griddep_wait();
+  griddep_launch();
+  T = read_temperature(T, ctl);
+  const uint32_t c = blockIdx.x, C = gridDim.x;
+  const float* l = logits + (size_t)blockIdx.y * V;
+  const uint32_t r = blockIdx.y + off;
+  const double acc = chunk_soft_sum(l, V, c, mx[r], T);
   if (threadIdx.x == 0) csum[(size_t)r * C + c] = acc;
   if (!last_of(&cnt[r], (int)C)) return;
   if (threadIdx.x == 0) {
@@ -520,6 +527,16 @@ __global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* 
     for (uint32_t k = 0; k < C; ++k) a += __ldcg(csum + (size_t)r * C + k);
     kept[r] = a;
   }
+}
+
+// Vocab shard statistics: the chunk sums of rows of a shard (entries [first, first + Vs) of each row, first a
+// multiple of kStatsChunk) against the rows' global maxima, without the combine: out[r][c] for the shard's chunks.
+__global__ void __launch_bounds__(kSampleThreads) shard_chunk_sums_kernel(const float* __restrict__ logits, uint32_t Vs,
+                                                                          float T, const float* __restrict__ gmax,
+                                                                          double* __restrict__ out) {
+  const uint32_t c = blockIdx.x, C = gridDim.x;
+  const double acc = chunk_soft_sum(logits + (size_t)blockIdx.y * Vs, Vs, c, gmax[blockIdx.y], T);
+  if (threadIdx.x == 0) out[(size_t)blockIdx.y * C + c] = acc;
 }
 
 __global__ void __launch_bounds__(kSampleThreads) probs_kernel(const float* __restrict__ logits, uint32_t V, float T,
@@ -670,16 +687,24 @@ __global__ void __launch_bounds__(kSampleThreads) sample_chunks_kernel(SampleJob
   if (tid == 0) s_flags = 0;
   __syncthreads();
   const uint32_t lo = min(chi, clo + tid * kPerThread), hi = min(chi, lo + kPerThread);
-  for (int variant = 0; variant < (two ? 2 : 1); ++variant) {
+  // the main pass sums the main row only; the fallback P[b][j] of a residual is needed only when no entry of the
+  // whole residual is positive, which the last CTA alone learns, so that CTA sums the fallback's chunks itself
+  {
+    const int variant = 0;
     const RowFx fx = job_fx(job, b, V, variant, T);
     U192 sum;
     int32_t last;
     bool bad;
     thread_sums(fx, lo, hi, sum, last, bad);
+    // residual mass test of sampling.cpp:121-123 (some double residual > 0).  A residual is the difference of two
+    // floats (or of a float and 1), so when positive it is at least 2^-149 and its float is positive too: with every
+    // entry finite the test is "a positive entry was summed".  Non-finite entries take the double test itself.
     bool anypos = false;
-    if (variant == 0 && two)
-      for (uint32_t i = lo; i < hi; ++i)  // residual mass test in double (sampling.cpp:121-123)
-        anypos |= ((double)fx.P(i) - fx.q_at(i)) > 0.0;
+    if (variant == 0 && two) {
+      anypos = last >= 0;
+      if (bad && !anypos)
+        for (uint32_t i = lo; i < hi; ++i) anypos |= ((double)fx.P(i) - fx.q_at(i)) > 0.0;
+    }
     U192 total;
     (void)block_exclusive_scan(sum, &total);
     int32_t lmax;
@@ -699,15 +724,43 @@ __global__ void __launch_bounds__(kSampleThreads) sample_chunks_kernel(SampleJob
   if (!last_of(&cnt[b], (int)C)) return;
 
   // ---- last CTA of sequence b: pick the row variant, locate the chunk, then the entry ----
-  __shared__ int s_variant, s_state, s_chunk;
+  __shared__ int s_variant, s_state, s_chunk, s_fl;
   __shared__ int32_t s_result, s_prev_nz;
   __shared__ U192 s_th_true, s_th_false, s_prefix;
   if (tid == 0) {
     int fl = 0;
     for (uint32_t k = 0; k < C; ++k) fl |= __ldcg(cflag + (size_t)b * C + k);
+    s_fl = fl;
     s_variant = (two && !(fl & 2)) ? 1 : 0;
-    s_state = (fl & (s_variant == 0 ? 1 : 4)) ? 2 : 0;  // a non-finite or huge value: serial walk
   }
+  __syncthreads();
+  if (s_variant == 1) {
+    // the residual has no positive entry: the chunk sums of the fallback row, chunk after chunk
+    const RowFx fx1 = job_fx(job, b, V, 1, T);
+    for (uint32_t k = 0; k < C; ++k) {
+      const uint32_t klo = k * kSampleChunk, khi = min(V, klo + kSampleChunk);
+      const uint32_t lo1 = min(khi, klo + tid * kPerThread), hi1 = min(khi, lo1 + kPerThread);
+      U192 sum;
+      int32_t last;
+      bool bad;
+      thread_sums(fx1, lo1, hi1, sum, last, bad);
+      U192 total;
+      (void)block_exclusive_scan(sum, &total);
+      int32_t lmax;
+      (void)block_exclusive_max(last, &lmax);
+      if (bad) atomicOr(&s_fl, 4);
+      if (tid == 0) {
+        unsigned long long* o = c192 + (((size_t)b * 2 + 1) * C + k) * 3;
+        o[0] = total.w[0];
+        o[1] = total.w[1];
+        o[2] = total.w[2];
+        clast[((size_t)b * 2 + 1) * C + k] = lmax;
+        __threadfence();  // read back below through L2 (__ldcg) by other threads of the CTA
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) s_state = (s_fl & (s_variant == 0 ? 1 : 4)) ? 2 : 0;  // a non-finite or huge value: serial walk
   __syncthreads();
   const int variant = s_variant;
   const RowFx fx = job_fx(job, b, V, variant, T);
@@ -1199,6 +1252,42 @@ int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_
   src.T = temperature;
   return launch_accept(src, d_drafts, batch, k, vocab, d_uniforms, seed, counter_base, nullptr, nullptr, d_accepted,
                        d_next, s, st);
+}
+
+int clm_b200_shard_stats(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
+                         uint64_t first_col, float temperature, const float* d_global_max, void* d_out, void* stream) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(vocab_shard > 0 && temperature > 0.0f, CLM_INVALID_ARGUMENT, "empty shard or temperature <= 0");
+  CLM_CHECK(first_col % kStatsChunk == 0, CLM_INVALID_ARGUMENT,
+            "a vocab shard must start at a multiple of 16384 columns (the statistics chunk)");
+  if (rows == 0) return CLM_OK;
+  CLM_CHECK(d_logits && d_out, CLM_INVALID_ARGUMENT, "null buffer");
+  cudaStream_t st = pick_stream(ctx, stream);
+  if (d_global_max == nullptr) {
+    SampleScratch s;
+    CLM_TRY(abi_scratch(ctx, rows, 0, vocab_shard, 0, st, &s, nullptr));
+    const dim3 grid(stats_chunks(vocab_shard), rows);
+    CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, vocab_shard, 0u, s.cmax,
+                       static_cast<float*>(d_out), s.rcnt));
+    return CLM_OK;
+  }
+  shard_chunk_sums_kernel<<<dim3(stats_chunks(vocab_shard), rows), kSampleThreads, 0, st>>>(
+      d_logits, vocab_shard, temperature, d_global_max, static_cast<double*>(d_out));
+  CLM_LAUNCHED("shard_chunk_sums_kernel");
+  return CLM_OK;
+}
+
+int clm_b200_shard_probs(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
+                         float temperature, const float* d_global_max, const double* d_kept, float* d_probs,
+                         void* stream) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(vocab_shard > 0 && temperature > 0.0f, CLM_INVALID_ARGUMENT, "empty shard or temperature <= 0");
+  if (rows == 0) return CLM_OK;
+  CLM_CHECK(d_logits && d_global_max && d_kept && d_probs, CLM_INVALID_ARGUMENT, "null buffer");
+  cudaStream_t st = pick_stream(ctx, stream);
+  const dim3 grid(sample_chunks(vocab_shard), rows);
+  return launch_pdl(probs_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, vocab_shard, temperature,
+                    (const RoundCtl*)nullptr, d_global_max, d_kept, d_probs);
 }
 
 int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,

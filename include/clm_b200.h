@@ -89,7 +89,8 @@ typedef struct clm_b200_matrix clm_b200_matrix;
 /* Upload a rows x cols row-major tensor in its stored representation and repack it for the tiled
  * kernels (lossless byte permutation for Q4_K / Q8_0; f32 / q8_0-fixture are decoded exactly to f32, as
  * the reference does at prepare, reference_domain.cpp:222-231).  Q4_K and Q8_0 need rows % 16 == 0 and
- * cols % 256 == 0.  `h_bytes` is host memory; `d_bytes` (the _device variant) is device memory. */
+ * cols % 256 == 0.  `h_bytes` is host memory; `d_bytes` (the _device variant) is device memory, read after a
+ * device synchronisation (so work of any stream that writes it completes first). */
 CLM_API int clm_b200_matrix_upload(clm_b200_ctx* ctx, int quant, const void* h_bytes, uint64_t nbytes, uint32_t rows,
                            uint32_t cols, clm_b200_matrix** out);
 CLM_API int clm_b200_matrix_upload_device(clm_b200_ctx* ctx, int quant, const void* d_bytes, uint64_t nbytes, uint32_t rows,
@@ -150,6 +151,22 @@ CLM_API int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_target_logi
                            const int32_t* d_drafts, uint32_t batch, uint32_t k, uint32_t vocab, float temperature,
                            const double* d_uniforms, uint64_t seed, uint64_t counter_base, uint32_t* d_accepted,
                            int32_t* d_next, void* stream);
+/* Vocab-sharded distribution rows (the LM head split by vocabulary over GPUs; no reference counterpart: the
+ * reference computes distribution(), sampling.cpp:51-86, over whole rows).  A rank holds the logits of columns
+ * [first_col, first_col + vocab_shard) of `rows` rows (first_col a multiple of 16384, the statistics chunk).
+ *   d_global_max == NULL: d_out = float[rows], each row's maximum over the shard;
+ *   otherwise (the rows' maxima over the whole vocabulary): d_out = double[rows][ceil(vocab_shard / 16384)], the
+ *   sums of exp(double(l - max) / T) of each 16384-column chunk in the shard, bit-identical to the chunk sums of
+ *   the whole-row statistics, so that summing every rank's chunks in column order gives the whole row's kept sum
+ *   exactly. */
+CLM_API int clm_b200_shard_stats(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
+                                 uint64_t first_col, float temperature, const float* d_global_max, void* d_out,
+                                 void* stream);
+/* The shard's probabilities float(exp(double(l - max) / T) / kept) from the rows' global max and kept sum: the same
+ * values clm_b200_distribution_rows writes for those columns of the whole rows. */
+CLM_API int clm_b200_shard_probs(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
+                                 float temperature, const float* d_global_max, const double* d_kept, float* d_probs,
+                                 void* stream);
 /* Philox4x32-10 uniforms: out[i] = top 53 bits of (o0:o1) * 2^-53 for counter (first+i lo, hi, c2, c3). */
 CLM_API int clm_b200_philox_uniforms(clm_b200_ctx* ctx, uint64_t seed, uint64_t first, uint32_t c2, uint32_t c3, uint64_t n,
                              double* d_out, void* stream);
@@ -329,7 +346,9 @@ CLM_API int clm_b200_pipe_begin(clm_b200_engine* e, uint64_t session, uint32_t r
 /* One speculative round of `session` on this stage, device-resident: wait for the input, commit the previous
  * round, run the window, forward.  The tail also accepts (as clm_b200_spec_round_device), commits, drafts the
  * next window and sends it to the prefix; its emitted tokens / count go to d_tokens / d_count (optional).
- * Every stage runs the same rounds of the same sessions in the same order. */
+ * Every stage runs the same rounds of the same sessions in the same order.  A link delivers its messages in the
+ * order they were sent, whatever their session: the prefix's rounds must come in the order of the tail's
+ * clm_b200_pipe_begin / round calls that sent their windows. */
 CLM_API int clm_b200_pipe_round(clm_b200_engine* e, uint64_t session, const clm_b200_spec_params* params,
                                 int32_t* d_tokens, uint32_t* d_count, void* stream);
 /* Synchronises the engine's stream; CLM_DEADLINE_EXCEEDED if a link wait gave up (a peer stage stopped). */

@@ -296,6 +296,30 @@ def test_accept_logits_philox_matches_oracle(ctx, oracle):
         assert (a, n) == (acc[b], nxt[b]), b
 
 
+def test_verify_residual_without_mass_falls_back_to_target_row(ctx, oracle):
+    """A draft with q(d) = 0 is rejected without a uniform; when Q equals P the residual max(P - Q, 0) has no
+    positive entry and the sample comes from P[j] itself (sampling.cpp:113-126), over a multi-chunk vocabulary."""
+    from clusterlm_b200.runtime import distribution, verify_speculative
+
+    B, k, V = 3, 3, 151936
+    rng = np.random.default_rng(21)
+    tl = (rng.standard_normal((B, k + 1, V)) * 3).astype(np.float32)
+    tl[:, :, 5] = -np.inf  # column 5 has probability 0 in every row
+    P = host(distribution(ctx, dev(tl.reshape(-1, V)), 1.0)).reshape(B, k + 1, V)
+    Q = P[:, :k].copy()
+    Q[1] = host(distribution(ctx, dev((tl[1, :k] + rng.standard_normal((k, V)) * 0.5).astype(np.float32)), 1.0))
+    drafts = np.stack([[int(np.argmax(Q[b, j])) for j in range(k)] for b in range(B)]).astype(np.int32)
+    drafts[0, 0] = 5  # rejected at once: residual of P[0][0] - Q[0][0] = 0 everywhere
+    drafts[2, 1] = 5  # draft 0 accepted (p = q), draft 1 rejected with an empty residual
+    us = rng.random((B, k + 1))
+    acc, nxt = verify_speculative(ctx, dev(P), dev(drafts), dev(Q), uniforms=dev(us))
+    acc, nxt = host(acc), host(nxt)
+    for b in range(B):
+        a, n, _ = oracle.verify(P[b], drafts[b], Q[b], us[b])
+        assert (a, n) == (acc[b], nxt[b]), b
+    assert acc[0] == 0 and acc[2] == 1
+
+
 def test_accept_logits_equals_materialised_at_acceptance_micro_size(ctx):
     """The acceptance micro-workload at full size (64 sequences x q = 8 x vocab 151,936): acceptance evaluated from
     logits gives the same accepted counts and tokens as verify_speculative over the materialised distributions
