@@ -132,4 +132,50 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, int* err)
   return false;
 }
 
+// ---- dataflow between CTAs (and between the overlapping launches of a window chain)
+
+constexpr unsigned long long kDepWaitNs = 1000000000ull;  // a cross-CTA wait gives up after 1 s without progress
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool dep_failed(const int* err) { return *reinterpret_cast<const volatile int*>(err) != 0; }
+
+__device__ __forceinline__ void dep_raise(int* err) { atomicCAS(err, 0, kErrWaitTimeout); }
+
+// Waits until *ctr >= target (acquire, gpu scope); false when the error flag is (or gets) raised, or after
+// kDepWaitNs without reaching the target (then it raises the flag itself), so every wait ends.
+__device__ inline bool dep_wait(const int* ctr, int target, int* err) {
+  if (ld_acquire(ctr) >= target) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (ld_acquire(ctr) >= target) return true;
+    if ((i & 63) == 63) {
+      if (dep_failed(err)) return false;
+      if (globaltimer() - t0 > kDepWaitNs) {
+        dep_raise(err);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
+// Removes `bytes` of expected transactions from the current phase of a barrier (copies that will not be issued).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+
+// Bulk copies issued after this read global memory written by other CTAs' ordinary stores.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
 }  // namespace clm

@@ -17,6 +17,7 @@
 #include "codec.cuh"
 #include "bulk.cuh"
 #include "engine.cuh"
+#include "gemv_strip.cuh"
 #include "link.cuh"
 #include "flow.cuh"
 #include "gemv.cuh"
@@ -63,6 +64,13 @@ struct Session {
   int32_t* d_win = nullptr;    // pipeline tail: this session's current window tokens [W + 1]
   float* d_dprobs = nullptr;   // pipeline tail: draft distributions of the current window [W][V]
 };
+
+// Zeroes the dataflow counters of a window chain before its first linked launch (after the previous window ended).
+__global__ void zero_ints_kernel(int* __restrict__ p, int n) {
+  griddep_wait();
+  griddep_launch();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0;
+}
 
 __global__ void fill_kernel(float* p, float v, uint64_t n) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
@@ -225,6 +233,18 @@ struct LlamaEngine : clm_b200_engine {
   float* h = nullptr;
   float* part = nullptr;     // GEMV split partials (last-CTA reduction)
   int* gcount = nullptr;     // GEMV row-group counters
+  // the second partial region of the linked chain: consecutive GEMVs alternate between the two (a GEMV's partials
+  // may still be read by its first segments while the next GEMV's later segments write theirs)
+  float* part2 = nullptr;
+  int* gcount2 = nullptr;
+  // dataflow counters of a linked window chain (LinkLayout per layer), zeroed at the start of every window
+  int* link_ctr = nullptr;
+  int link_n = 0;
+  bool link_ok = false;  // the linked chain is on (CLM_B200_LINK=1) and the geometry fits it
+  // the strip GEMV (gemv_strip.cu) for the layers' QKV (1), W_o (2), gate|up (4) (CLM_B200_STRIP): measured faster
+  // for QKV and W_o, whose stream-K reductions dominate their time, slower for the longer gate|up stream
+  int strip_mask = 3;
+  unsigned long long pf_cap = 64 * 1024;  // L2 lookahead bytes per CTA of the next GEMV (CLM_B200_PF_KB)
   int* acount = nullptr;     // attention (m-tile, kv head) counters
   size_t gcount_n = 0, acount_n = 0;  // their lengths (reset_counters)
   void* samp_counters = nullptr;      // the sampling scratch's arrival counters and their bytes
@@ -334,9 +354,42 @@ struct LlamaEngine : clm_b200_engine {
   }
 
   // ---- one fused GEMV of the chain
-  int gemv(const Gemv& g, int q, const XBuf& in, const Epi& epi, cudaStream_t st) {
+  int gemv_strip(const Gemv& g, int q, const XBuf& in, const Epi& epi, cudaStream_t st) {
+    return launch_gemv_strip(g.m->shape, static_cast<const uint8_t*>(g.m->data), in, q, epi, ctx->sm_count, st);
+  }
+  // Whether matrix `bit` of a layer (1 QKV, 2 W_o, 4 gate|up) runs on the strip GEMV for q rows.
+  bool strip_for(const Gemv& g, int bit, int q, int kind) const {
+    return (strip_mask & bit) && gemv_strip_ok(g.m->shape, q, kind);
+  }
+  int gemv(const Gemv& g, int q, const XBuf& in, const Epi& epi, cudaStream_t st, bool alt = false) {
     const GemvPlan& p = g.for_q(q);
-    return launch_gemv(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), in, q, epi, part, gcount, st);
+    return launch_gemv(g.m->shape, p, static_cast<const uint8_t*>(g.m->data), in, q, epi, alt ? part2 : part,
+                       alt ? gcount2 : gcount, st);
+  }
+
+  // Counters of one layer of a linked chain (ints at link_ctr + layer * per_layer): the attention's wait per kv
+  // head, W_o's input chunks, gate|up's input chunks + W_o's finished groups, down's input chunks, the next QKV's
+  // (or the head's) input chunks + down's finished groups.
+  struct LinkLayout {
+    int attn, o, gu, o_done, down, next, down_done, per_layer;
+  };
+  LinkLayout link_layout() const {
+    LinkLayout L;
+    const int ch_h = d.H / 512, ch_q = d.qd() / 512, ch_f = d.F / 512;
+    L.attn = 0;
+    L.o = L.attn + d.nkv;
+    L.gu = L.o + ch_q;
+    L.o_done = L.gu + ch_h;
+    L.down = L.o_done + 1;
+    L.next = L.down + ch_f;
+    L.down_done = L.next + ch_h;
+    L.per_layer = L.down_done + 1;
+    return L;
+  }
+  bool link_shape_ok() const {
+    const int group = d.nh / d.nkv;
+    return d.hd == 128 && d.H % 512 == 0 && d.qd() % 512 == 0 && d.F % 512 == 0 &&
+           (group % 4 == 0 || 4 % group == 0);
   }
   Epi epi_base(int kind) const {
     Epi e;
@@ -358,18 +411,29 @@ struct LlamaEngine : clm_b200_engine {
 
   // L2 lookahead of the next GEMV of the chain: each CTA prefetches the first bytes of the matching CTA range of
   // `next` (its first units) once its own copies are issued
-  static void lookahead(Epi& e, const Gemv& next) {
+  void lookahead(Epi& e, const Gemv& next) const {
     e.pf = static_cast<const uint8_t*>(next.m->data);
     e.pf_bytes = next.m->shape.bytes();
-    e.pf_cap = 64 * 1024;
+    e.pf_cap = pf_cap;
   }
 
   // ---- the layer range over q rows; h holds the stage input and xa its first norm's preparation
   int enqueue_layers(Session& s, int q, const int32_t* parent, cudaStream_t st) {
     const int nt = q <= 8 ? 1 : 2;
     const long long* pos = &s.d_state->pos;
+    // linked chain: every launch after the first waits on per-chunk readiness counters instead of on its
+    // predecessor's completion (gemv4.cu, llama.cu); the partial regions alternate between consecutive GEMVs
+    const bool linked = link_ok;
+    const LinkLayout LL = link_layout();
+    const int group = d.nh / d.nkv;
+    const int mtiles = (q * group + 15) / 16;
+    const int splits = attention_splits(q, d, max_pages, ctx->sm_count);
+    auto ctr = [&](size_t li, int off) { return link_ctr + li * LL.per_layer + off; };
     for (size_t li = 0; li < layers.size(); ++li) {
       Layer& L = layers[li];
+      const bool sq = strip_for(L.qkv, 1, q, EPI_ROPE_KV), so = strip_for(L.o, 2, q, EPI_RESID_PREP),
+                 sg = strip_for(L.gu, 4, q, EPI_SWIGLU_PREP);
+      const int strips_per_head = d.hd / 16;
       // q, k, v with RoPE and the paged KV append fused into the epilogue (input: xa = h * attn_norm)
       Epi ek = epi_base(EPI_ROPE_KV);
       ek.nh = d.nh;
@@ -384,23 +448,65 @@ struct LlamaEngine : clm_b200_engine {
       ek.parent = parent;
       ek.pf_kv = true;  // the attention's KV pages into L2 while the QKV GEMV drains
       ek.pf_max_pages = max_pages;
-      CLM_TRY(gemv(L.qkv, q, xa, ek, st));
+      AttnLink al;
+      if (linked) {
+        if (li > 0) link_in(ek, li - 1, LL.next, 4, LL.down_done, d.H / 128);
+        ek.sig = ctr(li, LL.attn);
+        ek.sig_qkv = 1;
+        al.wait = ctr(li, LL.attn);
+        // the kv head's query heads, its k head and its v head (each in 8 strips on the strip GEMV)
+        al.target = (group + 2) * (sq ? strips_per_head : 1);
+        al.sig = ctr(li, LL.o);
+        if (group >= 4) {
+          al.span = group / 4;
+        } else {
+          al.kvh_div = 4 / group;
+        }
+      }
+      if (sq) {
+        CLM_TRY(gemv_strip(L.qkv, q, xa, ek, st));
+      } else {
+        CLM_TRY(gemv(L.qkv, q, xa, ek, st));
+      }
       // attention -> xb (W_o input); W_o into L2 meanwhile
       CLM_TRY(launch_attention(q16, kpool[li], vpool[li], s.d_pages, pos, parent, q, d, max_pages, attn_part, acount,
                                nt, hi_scale(), xb.frag, xb.sum, bad, static_cast<const uint8_t*>(L.o.m->data),
-                               L.o.m->shape.bytes(), ctx->sm_count, st));
+                               L.o.m->shape.bytes(), ctx->sm_count, st, nullptr, al));
       XBuf ob = xb;
       ob.ss = nullptr;
       // h += W_o o ; xa = h * ffn_norm (+ sum of squares)
       Epi eo = epi_resid(h, L.ffn_norm, xa);
       lookahead(eo, L.gu);
-      CLM_TRY(gemv(L.o, q, ob, eo, st));
+      if (linked) {
+        eo.wait = ctr(li, LL.o);
+        eo.wait_target = splits * mtiles * (group >= 4 ? 1 : 4 / group);
+        eo.sig = ctr(li, LL.gu);
+        eo.sig_div = 4;
+        eo.done = ctr(li, LL.o_done);
+      }
+      if (so) {
+        CLM_TRY(gemv_strip(L.o, q, ob, eo, st));
+      } else {
+        CLM_TRY(gemv(L.o, q, ob, eo, st, linked));
+      }
       // SwiGLU of the gate/up rows -> xb (W_down input)
       Epi es = epi_base(EPI_SWIGLU_PREP);
       es.ffn = d.F;
       es.next = xb;
       lookahead(es, L.down);
-      CLM_TRY(gemv(L.gu, q, xa, es, st));
+      XBuf gin = xa;
+      if (so) gin.nss = d.H / 16;  // W_o's strips wrote sum-of-squares partials per 16 columns
+      if (linked) {
+        // a chunk of gate|up's input: 4 row groups of W_o, or 32 of its strips
+        link_in(es, li, LL.gu, so ? 32 : 4, LL.o_done, so ? d.H / 16 : d.H / 128);
+        es.sig = ctr(li, LL.down);
+        es.sig_div = 8;  // 64 SwiGLU outputs per row group, 512 per chunk of down's input
+      }
+      if (sg) {
+        CLM_TRY(gemv_strip(L.gu, q, gin, es, st));
+      } else {
+        CLM_TRY(gemv(L.gu, q, gin, es, st));
+      }
       // h += W_down a ; xa = h * (next layer's attn_norm | output norm | 1)
       const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
       XBuf db = xb;
@@ -410,9 +516,24 @@ struct LlamaEngine : clm_b200_engine {
         lookahead(ed, layers[li + 1].qkv);
       else if (has_head)
         lookahead(ed, head);
-      CLM_TRY(gemv(L.down, q, db, ed, st));
+      if (linked) {
+        ed.wait = ctr(li, LL.down);
+        ed.wait_target = sg ? 32 : 8;  // gate|up units (16 outputs) or row groups (64 outputs) per chunk
+        ed.sig = ctr(li, LL.next);
+        ed.sig_div = 4;
+        ed.done = ctr(li, LL.down_done);
+      }
+      CLM_TRY(gemv(L.down, q, db, ed, st, linked));
     }
     return CLM_OK;
+  }
+  // A linked GEMV whose input is a residual phase's preparation (4 row groups per chunk) with the folded rmsnorm:
+  // chunk counters at layer li's offset `chunks`, the phase's finished groups at `done`.
+  void link_in(Epi& e, size_t li, int chunks, int per_chunk, int done, int done_target) const {
+    e.wait = link_ctr + li * link_layout().per_layer + chunks;
+    e.wait_target = per_chunk;
+    e.ss_done = link_ctr + li * link_layout().per_layer + done;
+    e.ss_target = done_target;
   }
 
   // ---- the layers (+ head) of a window as phases of the dataflow kernel: the same chain as enqueue_layers
@@ -671,6 +792,8 @@ struct LlamaEngine : clm_b200_engine {
       CLM_TRY(launch_unpack_boundary(bin, q, d.H, h, st));
     }
     const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
+    if (link_ok && !layers.empty())
+      CLM_TRY(launch_pdl(zero_ints_kernel, dim3((unsigned)ceil_div(link_n, 256)), dim3(256), 0, st, link_ctr, link_n));
     CLM_TRY(launch_prep_rows(h, d.H, q, d.H, w0, nt, hi_scale(), xa, true, st));
     if (flow_grid_n[nt - 1] > 0 && parent == nullptr) {
       // layers (and the head) in one cooperative launch
@@ -683,6 +806,8 @@ struct LlamaEngine : clm_b200_engine {
       Epi eo = epi_base(EPI_STORE);
       eo.out = logits;
       eo.out_ld = d.V;
+      if (link_ok && !layers.empty())
+        link_in(eo, layers.size() - 1, link_layout().next, 4, link_layout().down_done, d.H / 128);
       CLM_TRY(gemv(head, q, xa, eo, st));
     } else {
       CLM_TRY(launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st));
@@ -833,6 +958,8 @@ struct LlamaEngine : clm_b200_engine {
   // later window (or graph replay) would pass its waits early and sum stale partials.  The stream is idle here.
   int reset_counters() {
     if (gcount) CLM_CUDA(cudaMemset(gcount, 0, gcount_n * sizeof(int)));
+    if (gcount2) CLM_CUDA(cudaMemset(gcount2, 0, gcount_n * sizeof(int)));
+    if (link_ctr) CLM_CUDA(cudaMemset(link_ctr, 0, (size_t)link_n * sizeof(int)));
     if (acount) CLM_CUDA(cudaMemset(acount, 0, acount_n * sizeof(int)));
     if (wattn_cnt) CLM_CUDA(cudaMemset(wattn_cnt, 0, (size_t)wattn_tiles * sizeof(int)));
     if (samp_counters) CLM_CUDA(cudaMemset(samp_counters, 0, samp_counter_bytes));
@@ -1200,6 +1327,22 @@ int llama_prepare(LlamaEngine* e) {
   CLM_TRY(e->alloc_t(&e->gcount, max_ng));
   CLM_CUDA(cudaMemset(e->gcount, 0, max_ng * sizeof(int)));
   e->gcount_n = max_ng;
+  {
+    const char* env = getenv("CLM_B200_LINK");
+    e->link_ok = env && env[0] == '1' && e->link_shape_ok() && !e->layers.empty();
+    const char* senv = getenv("CLM_B200_STRIP");
+    if (senv) e->strip_mask = atoi(senv);
+    const char* penv = getenv("CLM_B200_PF_KB");
+    if (penv && atoi(penv) > 0) e->pf_cap = (unsigned long long)atoi(penv) * 1024;
+  }
+  if (e->link_ok) {
+    CLM_TRY(e->alloc_t(&e->part2, part_floats));
+    CLM_TRY(e->alloc_t(&e->gcount2, max_ng));
+    CLM_CUDA(cudaMemset(e->gcount2, 0, max_ng * sizeof(int)));
+    e->link_n = (int)(e->layers.size() * e->link_layout().per_layer);
+    CLM_TRY(e->alloc_t(&e->link_ctr, (size_t)e->link_n));
+    CLM_CUDA(cudaMemset(e->link_ctr, 0, (size_t)e->link_n * sizeof(int)));
+  }
   CLM_TRY(e->alloc_t(&e->acount, (size_t)2 * mtiles * d.nkv));  // attention arrival + departure counters
   CLM_CUDA(cudaMemset(e->acount, 0, (size_t)2 * mtiles * d.nkv * sizeof(int)));
   e->acount_n = (size_t)2 * mtiles * d.nkv;
@@ -1208,7 +1351,7 @@ int llama_prepare(LlamaEngine* e) {
     CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));
     CLM_TRY(e->alloc((void**)&x->sum, xsum_bytes(maxcols)));
     CLM_CUDA(cudaMemset(x->sum, 0, xsum_bytes(maxcols)));
-    CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 128) * 16));
+    CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 16) * 16));  // partials per 128 columns, or per 16 (strip GEMV)
     x->nss = d.H / 128;
   }
   CLM_TRY(e->ones(&e->ones_h, d.H));

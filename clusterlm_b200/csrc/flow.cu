@@ -30,43 +30,10 @@ constexpr int kHd = 128;
 constexpr int kRW = kFlowAttnRowFloats;
 constexpr uint32_t kPageBytes = 64u * kHd * 2u;  // one K or V^T page of one kv head (16 KB)
 constexpr int kMaxAttnSeg = 64;                  // attention segments per head combined in shared memory
-constexpr unsigned long long kWaitNs = 1000000000ull;  // a cross-CTA wait gives up after 1 s without progress
 // fixed shared memory after the ring: y / o [16][128] f32, S [16][64] f32, P [16][64] fp16, m/l/alpha [3][16],
 // combine weights and sums [2][kMaxAttnSeg][16]
 constexpr size_t kFixedBytes = 16 * 128 * 4 + 16 * 64 * 4 + 16 * 64 * 2 + 3 * 16 * 4 + 2 * kMaxAttnSeg * 16 * 4;
 
-__device__ __forceinline__ unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool failed(const int* err) { return *reinterpret_cast<const volatile int*>(err) != 0; }
-
-__device__ __forceinline__ void raise(int* err) { atomicCAS(err, 0, kErrWaitTimeout); }
-
-// Waits until *ctr >= target (acquire); false when the error flag is (or gets) raised or the wait gives up.
-__device__ bool flow_wait_count(const int* ctr, int target, int* err) {
-  if (ld_acquire(ctr) >= target) return true;
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t i = 0;; ++i) {
-    if (ld_acquire(ctr) >= target) return true;
-    if ((i & 63) == 63) {
-      if (failed(err)) return false;
-      if (globaltimer() - t0 > kWaitNs) {
-        raise(err);
-        return false;
-      }
-    }
-    __nanosleep(64);
-  }
-}
 
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   uint32_t done;
@@ -103,11 +70,11 @@ __device__ bool flow_mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
         : "memory");
     if (done) return true;
     if ((i & 255) == 255) {
-      if (failed(err)) return false;
+      if (dep_failed(err)) return false;
       if (t0 == 0) {
         t0 = globaltimer();
-      } else if (globaltimer() - t0 > kWaitNs) {
-        raise(err);
+      } else if (globaltimer() - t0 > kDepWaitNs) {
+        dep_raise(err);
         return false;
       }
     }
@@ -119,18 +86,12 @@ __device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t n) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
 }
 
-// Removes `bytes` of expected transactions from the current phase of a barrier (copies that will not be issued).
-__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
 
 __device__ __forceinline__ uint32_t word_of4(const uint4 (&v)[4], int w) {
   const uint4& u = v[w / 4];
   return (w % 4 == 0) ? u.x : (w % 4 == 1) ? u.y : (w % 4 == 2) ? u.z : u.w;
 }
 
-// Bulk copies issued after this read global memory written by other CTAs' ordinary stores.
-__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Units and this CTA's range of a phase.
 struct PhaseRange {
@@ -400,15 +361,15 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
         __nanosleep(32);
       }
       if ((++idle & 63) == 0) {
-        if (failed(err)) {
+        if (dep_failed(err)) {
           ok = false;
           break;
         }
         const unsigned long long now = globaltimer();
         if (idle_since == 0 || idle == 64) {
           idle_since = now;
-        } else if (now - idle_since > kWaitNs) {
-          raise(err);
+        } else if (now - idle_since > kDepWaitNs) {
+          dep_raise(err);
           ok = false;
           break;
         }
@@ -441,7 +402,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
   };
   // one thread waits for a counter; the result is shared with the consumer threads
   auto cta_wait = [&](const int* ctr, int target) -> bool {
-    if (tid == 0) s_ok = flow_wait_count(ctr, target, err);
+    if (tid == 0) s_ok = dep_wait(ctr, target, err);
     consumer_sync();
     const bool r = s_ok;
     consumer_sync();

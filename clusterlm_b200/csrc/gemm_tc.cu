@@ -27,6 +27,8 @@
 //
 // Weights are dequantised as GGUF decodes them (Q4_K: q * (d*sc) - dmin*m, Q8_0: q * d), rounded to fp16 once
 // (d*sc and dmin*m are themselves fp16); the activations are rounded to fp16; products accumulate in f32.
+#include <cstdlib>
+
 #include "bulk.cuh"
 #include "gemm_tc.cuh"
 #include "gemv_tile.cuh"
@@ -186,7 +188,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
                                                                  int tile_bytes, const uint8_t* __restrict__ xh, int q,
                                                                  int K, int P, int ksplit, int stages,
                                                                  float* __restrict__ part, uint32_t rows_total,
-                                                                 int* __restrict__ err) {
+                                                                 int* __restrict__ err, int ahead) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   __shared__ __align__(8) uint64_t full[kTcMaxStages], freeb[kTcMaxStages], raw_full[kTcRawSlots],
       raw_free[kTcRawSlots], done;
@@ -233,10 +235,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
       int rslot = 0, slot = 0;
       uint32_t rphase = 0, phase = 0;
       bool waited = false;
+      // L2 lookahead: the raw ring holds two superblocks, so the superblocks after them are prefetched into L2
+      // (`ahead` of them), which keeps more of the weight stream in flight than the ring's shared memory holds
+      const int sb_end = (c1 + 3) / 4;
+      int l2sb = c0 / 4 + kTcRawSlots;
+      auto l2_until = [&](int upto) {
+        for (; l2sb < sb_end && l2sb < upto; ++l2sb)
+          l2_prefetch_share(tiles + ((size_t)grp * sb_count + l2sb) * (size_t)raw_bytes, raw_bytes, 0, 1, raw_bytes);
+      };
+      l2_until(c0 / 4 + kTcRawSlots + ahead);
       for (int c = c0; c < c1; ++c) {
         if (c == c0 || c % 4 == 0) {
           if (!mbar_wait_backoff(&raw_free[rslot], rphase ^ 1u, err, 64)) break;
           const int sb = c / 4;
+          l2_until(sb + 1 + kTcRawSlots + ahead);
           mbar_expect_tx(&raw_full[rslot], raw_bytes);
           bulk_g2s_stream(raw_base + (size_t)rslot * raw_bytes,
                           tiles + ((size_t)grp * sb_count + sb) * (size_t)raw_bytes, raw_bytes, &raw_full[rslot],
@@ -365,6 +377,16 @@ __global__ void split_sum_kernel(const float* __restrict__ part, int ksplit, uin
   }
 }
 
+// Raw superblocks prefetched into L2 beyond the ring (CLM_B200_TC_AHEAD).  Off by default: at 128 and 256 rows
+// the GEMM is bound by the per-chunk hand-offs between its warps, and 4 or 8 superblocks ahead measured slower.
+int tc_l2_ahead() {
+  static const int v = [] {
+    const char* e = getenv("CLM_B200_TC_AHEAD");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
 }  // namespace
 
 TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count) {
@@ -417,11 +439,11 @@ int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_t
   if (s.quant == CLM_QUANT_Q4_K) {
     CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q4_K>, p.smem));
     CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q4_K>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err));
+                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err, tc_l2_ahead()));
   } else {
     CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q8_0>, p.smem));
     CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q8_0>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err));
+                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err, tc_l2_ahead()));
   }
   if (p.ksplit > 1 && sum_splits) {
     const uint64_t n = (uint64_t)q * s.rows;

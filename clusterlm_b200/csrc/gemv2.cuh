@@ -60,12 +60,31 @@ struct Epi {
   unsigned long long pf_bytes = 0, pf_cap = 0;
   bool pf_kv = false;
   int pf_max_pages = 0;
+  // Dataflow inside a window chain (gemv4.cu, gemv_strip.cu).  wait == null: the kernel reads what its predecessor
+  // wrote after griddepcontrol.wait.  Otherwise input chunk c (the 512 columns of the units' superblock pair c) is
+  // ready once wait[c] >= wait_target and the row scale's sums of squares once *ss_done >= ss_target, and the kernel
+  // never waits for its predecessor's completion: everything it reads is published by release-adds that it acquires,
+  // and no CTA of a linked launch touches memory after its last signal, so a plain launch that waits for the chain's
+  // last kernel sees all of the chain's results.  A finished row group g adds 1 to sig[g / sig_div] (sig_qkv: to its
+  // kv head's counter) and to *done (either may be null).
+  const int* wait = nullptr;
+  int wait_target = 0;
+  const int* ss_done = nullptr;
+  int ss_target = 0;
+  int* sig = nullptr;
+  int sig_div = 1;
+  int sig_qkv = 0;
+  int* done = nullptr;
 };
 
 // The fused GEMV (gemv4.cu) over the group-major tile layout of gemv.cuh.  `part` holds ng*p.ksplit*q*128 f32
 // segment partials and `counters` ng zero-initialised ints (left zero after every launch).
 int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q, const Epi& epi,
                 float* part, int* counters, cudaStream_t st);
+// Units (or strip stages) that the GEMVs prefetch into L2 beyond their shared-memory ring (CLM_B200_L2AHEAD).  Off
+// by default: the stream is bound by the consumers' dequantisation, and prefetching ahead measured slower.
+constexpr int kL2Ahead = 0;
+int gemv_l2_ahead();
 
 // Producer helpers.
 // x[q][cols] fp32 (row stride ld) times optional w[cols] -> fragments + sums (+ ss partials over 16-column

@@ -23,6 +23,8 @@
 //    on, and the group's first segment, which reaches the group at the end of its range, waits for them (bounded
 //    acquire spin), sums the segments in index order (deterministic) and runs the epilogue.
 //  * Every mbarrier wait is bounded (bulk.cuh); a timeout raises the epilogue's error flag.
+#include <cstdlib>
+
 #include "gemv_core.cuh"
 #include "pdl.cuh"
 
@@ -32,7 +34,7 @@ template <typename Raw, int NT, int EPI>
 __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __restrict__ tiles, uint32_t rows,
                                                              int ng, G4Geom geo, int stages, XBuf in, int q, Epi epi,
                                                              float* __restrict__ part, int* __restrict__ counters,
-                                                             int maxseg) {
+                                                             int maxseg, int ahead) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kG4MaxStages], empty[kG4MaxStages];
   __shared__ float s_scale[16];
@@ -41,6 +43,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
   float* y = reinterpret_cast<float*>(smem + (size_t)stages * geo.stage_bytes);  // [16][128]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const bool linked = epi.wait != nullptr;
   const long long U = (long long)ng * geo.ppr;
   const int G = gridDim.x;
   const long long u0 = (long long)blockIdx.x * U / G, u1 = (long long)(blockIdx.x + 1) * U / G;
@@ -78,17 +81,45 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         bulk_g2s(st + geo.sum_off, reinterpret_cast<const uint8_t*>(in.sum) + (size_t)2 * c.pr * 1024,
                  (uint32_t)(nsb * 1024), &full[c.slot]);
       };
+      // dataflow: a unit's activation copies wait for its input chunk (a failed wait drops them from the stage's
+      // barrier instead, so the consumers never wait for copies that will not come; the error flag is raised)
+      auto acts_when_ready = [&](const UnitCursor& c) {
+        if (linked) {
+          if (!dep_wait(epi.wait + c.pr, epi.wait_target, epi.err)) {
+            const int nsb = min(2, geo.sb - 2 * c.pr);
+            mbar_complete_tx(&full[c.slot], (uint32_t)(nsb * NT * kXfragSbBytes + 2 * nsb * kG4SbSumBytes));
+            return;
+          }
+          fence_proxy_async_global();  // the copies read what other CTAs' epilogues stored
+        }
+        issue_acts(c);
+      };
+      // L2 lookahead cursor: unit i + `ahead` is prefetched into L2 when unit i's copies are issued, so the ring's
+      // copies find their bytes in L2 and the DRAM stream keeps more bytes in flight than the ring can hold
+      UnitCursor l2 = start;
+      int l2i = 0;
+      auto l2_until = [&](int upto) {
+        for (; l2i < n && l2i < upto; ++l2i, l2.next(geo.ppr, stages)) {
+          const int nsb = min(2, geo.sb - 2 * l2.pr);
+          const unsigned long long bytes = (unsigned long long)nsb * geo.sb_bytes;
+          l2_prefetch_share(tiles + ((size_t)l2.grp * geo.sb + 2 * l2.pr) * geo.sb_bytes, bytes, 0, 1, bytes);
+        }
+      };
       const int pre = min(n, stages);
+      l2i = pre;
+      for (int i = 0; i < pre; ++i) l2.next(geo.ppr, stages);
+      l2_until(pre + ahead);
       UnitCursor w = start, a = start;
       for (int i = 0; i < pre; ++i, w.next(geo.ppr, stages)) issue_weights(w);
-      griddep_wait();
+      if (!linked) griddep_wait();
       griddep_launch();
-      for (int i = 0; i < pre; ++i, a.next(geo.ppr, stages)) issue_acts(a);
+      for (int i = 0; i < pre; ++i, a.next(geo.ppr, stages)) acts_when_ready(a);
       for (int i = pre; i < n; ++i, w.next(geo.ppr, stages)) {
         // the slot's previous use is consumed (sleeping between polls leaves the issue slots to the consumers)
         if (!mbar_wait_backoff(&empty[w.slot], w.phase ^ 1u, epi.err, 128)) break;
         issue_weights(w);
-        issue_acts(w);
+        acts_when_ready(w);
+        l2_until(i + 1 + ahead);
       }
       // every copy of this CTA is issued: prefetch the next kernel's first bytes into L2 while this one drains
       if (EPI == EPI_ROPE_KV && epi.pf_kv) {
@@ -104,32 +135,37 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
       } else {
         l2_prefetch_share(epi.pf, epi.pf_bytes, blockIdx.x, G, epi.pf_cap);
       }
-    } else {
-      griddep_wait();
-      griddep_launch();
     }
+    griddep_launch();
     return;
   }
 
   // ---------------- consumers ----------------
-  griddep_wait();
-  griddep_launch();
+  // linked: nothing this launch reads from its predecessor is touched before the unit data has arrived (the
+  // producer waited for it), the row scale's partials are read after their own wait, and the epilogue's operands
+  // are loaded by a group's first segment while it waits for the other segments, not at the group's start
+  if (!linked) {
+    griddep_wait();
+    griddep_launch();
+  }
   const int grp_of_warp = warp / kGemvWarps, rt = warp % kGemvWarps;
-  const G4SsPre ss_pre = g4_ss_load(in);
+  const G4SsPre ss_pre = linked ? G4SsPre{} : g4_ss_load(in);
   bool scale_ready = false;
   G4Acc<NT> acc;
   acc.zero();
   int cur = n > 0 ? start.grp : -1;
   EpiPre pre;
-  if (cur >= 0) epi_preload<EPI>(pre, cur, rows, q, epi);
+  const EpiPre* prep = linked ? nullptr : &pre;
+  EpiPre* lazy = linked ? &pre : nullptr;
+  if (cur >= 0 && !linked) epi_preload<EPI>(pre, cur, rows, q, epi);
   UnitCursor c = start;
   // both groups walk every unit of the range, so they flush the same row groups at the same points
   for (int i = 0; i < n; ++i, c.next(geo.ppr, stages)) {
     if (c.grp != cur) {
       g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
-                   in, scale_ready, s_red, &pre);
+                   in, scale_ready, s_red, prep, lazy);
       cur = c.grp;
-      epi_preload<EPI>(pre, cur, rows, q, epi);
+      if (!linked) epi_preload<EPI>(pre, cur, rows, q, epi);
       acc.zero();
     }
     if ((i & 1) != grp_of_warp) continue;
@@ -139,7 +175,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
     if (lane == 0) mbar_arrive(&empty[c.slot]);
   }
   if (cur >= 0) g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
-                   in, scale_ready, s_red, &pre);
+                   in, scale_ready, s_red, prep, lazy);
 }
 
 // x[p][0:cols] (row stride ld) * w -> fragments / sums (+ sum-of-squares partials per 128 columns); one warp per
@@ -185,6 +221,15 @@ int launch_prep_rows(const float* d_x, long long ld, int q, int cols, const floa
                     out.frag, out.sum, with_ss ? out.ss : nullptr);
 }
 
+// Units of L2 lookahead beyond the ring (CLM_B200_L2AHEAD, default kL2Ahead).
+int gemv_l2_ahead() {
+  static const int v = [] {
+    const char* e = getenv("CLM_B200_L2AHEAD");
+    return e ? atoi(e) : kL2Ahead;
+  }();
+  return v;
+}
+
 template <typename Raw, int NT, int EPI>
 static int launch4(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q,
                    const Epi& epi, float* part, int* counters, cudaStream_t st) {
@@ -192,7 +237,7 @@ static int launch4(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles
   CLM_TRY(ensure_smem(kern, p.smem));
   const G4Geom geo = g4_geom(s, NT, 2);
   return launch_pdl(kern, dim3((unsigned)p.grid), dim3(kG4Threads), p.smem, st, d_tiles, s.rows, (int)s.ng, geo,
-                    p.stages, in, q, epi, part, counters, p.ksplit);
+                    p.stages, in, q, epi, part, counters, p.ksplit, gemv_l2_ahead());
 }
 
 template <typename Raw, int NT>

@@ -233,10 +233,17 @@ __device__ __forceinline__ void g4_epilogue_rt(int kind, float* y, const float* 
   }
 }
 
+// epi_preload with the kind chosen at run time.
+__device__ __forceinline__ void epi_preload_rt(int kind, EpiPre& pre, int grp, uint32_t rows, int q, const Epi& epi) {
+  if (kind == EPI_RESID_PREP) epi_preload<EPI_RESID_PREP>(pre, grp, rows, q, epi);
+  if (kind == EPI_ROPE_KV) epi_preload<EPI_ROPE_KV>(pre, grp, rows, q, epi);
+}
+
 // Row scale (folded rmsnorm) 1/sqrt(sum(ss)/ss_n + eps) per window row from the input's sum-of-squares partials
 // (1 without partials), in two steps so that the partials' load latency overlaps the first units: g4_ss_load at
 // the start of a GEMV (registers only), g4_ss_finish before the first flush.  Consumer threads only; s_red holds
-// kG4Consumers floats; at most 2 * kG4Consumers / 16 partials per row.
+// kG4Consumers floats.  Thread tid adds partials c = tid / 16 + 32 k (k ascending) of row tid % 16; the first two
+// are loaded ahead, any further ones (partials per 16 columns of the strip GEMV) in g4_ss_finish.
 struct G4SsPre {
   float a = 0.0f, b = 0.0f;
 };
@@ -253,7 +260,13 @@ __device__ __forceinline__ G4SsPre g4_ss_load(const XBuf& in) {
 __device__ __forceinline__ void g4_ss_finish(const G4SsPre& pre, const XBuf& in, const Epi& epi, int q, float* s_red,
                                              float* s_scale) {
   const int tid = threadIdx.x;
-  s_red[tid] = pre.a + pre.b;
+  {
+    constexpr int kStride = kG4Consumers / 16;
+    float a = pre.a + pre.b;
+    if (in.ss)
+      for (int c = tid / 16 + 2 * kStride; c < in.nss; c += kStride) a += __ldcg(in.ss + (size_t)c * 16 + tid % 16);
+    s_red[tid] = a;
+  }
   consumer_sync();
   if (tid < 16) {
     float sc = 1.0f;
@@ -364,6 +377,21 @@ __device__ __forceinline__ void g4_consume_unit(const uint8_t* st, const G4Geom&
   g4_consume_tile<Raw, NT>(st, geo, hh, nsb, rt, lane, acc);
 }
 
+// Dataflow signal of a finished row group (one thread, after the consumer barrier that ends the epilogue, so the
+// release covers every consumer's stores): its chunk counter (a QKV head signals its kv head) and the phase's
+// finished-group count.
+__device__ __forceinline__ void g4_signal(const Epi& epi, int grp) {
+  if (epi.sig != nullptr) {
+    int c = grp / epi.sig_div;
+    if (epi.sig_qkv) {
+      const int group = epi.nh / epi.nkv;
+      c = grp < epi.nh ? grp / group : (grp < epi.nh + epi.nkv ? grp - epi.nh : grp - epi.nh - epi.nkv);
+    }
+    red_release_add(epi.sig + c, 1);
+  }
+  if (epi.done != nullptr) red_release_add(epi.done, 1);
+}
+
 // Flush row group `grp` of a stream-K range: fold the two superblock warps into y (fixed order); a group owned by
 // this CTA alone goes to the epilogue.  Otherwise a later segment publishes its partial (release-add on the group's
 // counter by one thread after the consumer barrier) and continues without waiting, and the group's first segment
@@ -374,10 +402,17 @@ template <int NT>
 __device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, int* counters, int maxseg,
                          long long U, int G, long long u0, int ppr, int q, uint32_t rows, int epi_kind, const Epi& epi,
                          float* s_scale, int* s_last, const G4SsPre& ss_pre, const XBuf& in, bool& scale_ready,
-                         float* s_red, const EpiPre* pre = nullptr) {
+                         float* s_red, const EpiPre* pre = nullptr, EpiPre* lazy = nullptr) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, tid = threadIdx.x;
   if (!scale_ready) {
-    g4_ss_finish(ss_pre, in, epi, q, s_red, s_scale);
+    G4SsPre sp = ss_pre;
+    if (epi.ss_done != nullptr) {
+      // dataflow: the row scale needs every sum-of-squares partial of the residual phase that wrote the input
+      if (tid == 0) (void)dep_wait(epi.ss_done, epi.ss_target, epi.err);
+      consumer_sync();
+      sp = g4_ss_load(in);
+    }
+    g4_ss_finish(sp, in, epi, q, s_red, s_scale);
     scale_ready = true;
   }
   const int rt = warp % kGemvWarps, hh = warp / kGemvWarps;
@@ -412,6 +447,10 @@ __device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
       if (tid == 0) red_release_add(&counters[grp], 1);
       return false;
     }
+    if (lazy != nullptr) {  // the epilogue's operands load while the other segments' partials arrive
+      epi_preload_rt(epi_kind, *lazy, grp, rows, q, epi);
+      pre = lazy;
+    }
     if (tid == 0) {
       const bool ok = wait_count(&counters[grp], nseg - 1, epi.err);
       if (ok) counters[grp] = 0;  // every arrival of this launch is in: ready for the next launch
@@ -439,7 +478,8 @@ __device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     }
     consumer_sync();
   }
-  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);
+  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);  // ends with a consumer barrier
+  if (tid == 0) g4_signal(epi, grp);
   return true;
 }
 

@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const int32_t* __restrict__ pages, const long long* __restrict__ d_pos, const int32_t* __restrict__ parent, int q,
     int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
     float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err,
-    const uint8_t* __restrict__ pf, unsigned long long pf_bytes, float* __restrict__ out_f32) {
+    const uint8_t* __restrict__ pf, unsigned long long pf_bytes, float* __restrict__ out_f32, AttnLink link) {
   static_assert(HD == 128, "head_dim 128 layout");
   static_assert(kAttnWarps == 2 * kAttnPages, "two warps per page buffer");
   constexpr int RW = kAttnRowFloats;  // one partial row: O[HD], m, l, padding (16-byte aligned rows)
@@ -152,8 +152,17 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
   if (threadIdx.x == 32 * (kAttnWarps - 1))
     l2_prefetch_share(pf, pf_bytes, (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z)),
                       (int)(gridDim.x * gridDim.y * gridDim.z), ~0ull);
-  griddep_wait();
+  const bool linked = link.wait != nullptr;
+  if (!linked) griddep_wait();
   griddep_launch();
+  if (linked) {
+    // dataflow: this kv head's query, key and value rows are written
+    __shared__ int s_dep;
+    if (threadIdx.x == 0) s_dep = dep_wait(link.wait + kvh, link.target, err);
+    __syncthreads();
+    (void)s_dep;                 // on failure the flag is raised; the window's outputs are not used
+    fence_proxy_async_global();  // the window's page is bulk-copied after other CTAs' stores into it
+  }
   if (owner && first < p_end && !first_committed) request(first);
 
   const int group = nh / nkv;
@@ -167,9 +176,9 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const uint4* a = reinterpret_cast<const uint4*>(q16 + ((size_t)i0 * nh + kvh * group + r0 % group) * HD + 32 * t);
     const uint4* b = reinterpret_cast<const uint4*>(q16 + ((size_t)i1 * nh + kvh * group + r1 % group) * HD + 32 * t);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      qw0[j] = v0 ? a[j] : z;
-      qw1[j] = v1 ? b[j] : z;
+    for (int j = 0; j < 4; ++j) {  // L2 reads: the rows may have been written by other SMs during this launch
+      qw0[j] = v0 ? __ldcg(a + j) : z;
+      qw1[j] = v1 ? __ldcg(b + j) : z;
     }
   }
   float O[HD / 8][4];
@@ -391,13 +400,23 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     }
     __syncthreads();
   }
+  if (link.sig != nullptr) {
+    __syncthreads();  // every thread's fragments are stored before the release
+    if (threadIdx.x == 0) {
+      if (link.span > 1) {
+        for (int c = 0; c < link.span; ++c) red_release_add(link.sig + kvh * link.span + c, 1);
+      } else {
+        red_release_add(link.sig + kvh / link.kvh_div, 1);
+      }
+    }
+  }
 }
 
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum, int* d_err,
                      const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count, cudaStream_t st,
-                     float* d_out_f32) {
+                     float* d_out_f32, const AttnLink& link) {
   CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
   CLM_CHECK(d_out_f32 != nullptr || q <= 16, CLM_OUT_OF_RANGE, "W_o input fragments cover at most 16 window rows");
   const int group = d.nh / d.nkv;
@@ -406,14 +425,20 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
   const size_t smem = attn_smem_bytes(128);
   // splits per (kv head, m-tile): enough for the pages, no more CTAs than SMs (the splits wait for each other).
   // With more (kv head, m-tile) pairs than SMs there is one split each, whose wait is on its own arrival only.
+  const int splits = attention_splits(q, d, max_pages, sm_count);
+  CLM_TRY(ensure_smem(attention_kernel<128>, smem));
+  return launch_pdl(attention_kernel<128>, dim3(d.nkv, splits, mtiles), dim3(32 * kAttnWarps), smem, st, d_q, d_k,
+                    d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2, max_pages, d_part, d_counters, nt_out,
+                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes, d_out_f32, link);
+}
+
+int attention_splits(int q, const LlamaDims& d, int max_pages, int sm_count) {
+  const int mtiles = (q * (d.nh / d.nkv) + 15) / 16;
   const int heads = d.nkv * mtiles;
   int splits = (max_pages + kAttnPages - 1) / kAttnPages;
   if (splits > sm_count / heads) splits = sm_count / heads;
   if (splits < 1) splits = 1;
-  CLM_TRY(ensure_smem(attention_kernel<128>, smem));
-  return launch_pdl(attention_kernel<128>, dim3(d.nkv, splits, mtiles), dim3(32 * kAttnWarps), smem, st, d_q, d_k,
-                    d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2, max_pages, d_part, d_counters, nt_out,
-                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes, d_out_f32);
+  return splits;
 }
 
 // ---------------------------------------------------------------------------------------------------

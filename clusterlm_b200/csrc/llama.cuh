@@ -42,11 +42,24 @@ int launch_embed(const uint8_t* d_embd, int quant, const int32_t* d_tokens, int 
 // kernel's weights, or null) is prefetched into L2, split over the CTAs.  With d_out_f32 (wide windows, any q) the
 // outputs go to f32 rows d_out_f32[q][qd] instead of the fragments; when the (kv head, m-tile) pairs outnumber the
 // SMs each pair has one split.
+//
+// Dataflow inside a window chain (link.wait non-null): kv head h's inputs (its query heads, k and v rows from the
+// QKV GEMV) are ready once link.wait[h] >= link.target; the kernel does not wait for its predecessor's completion.
+// Every CTA adds 1, once its share of the W_o fragments is written, to link.sig[h * span + i] for i < span (a kv
+// head's query heads cover `span` 512-column chunks) or to link.sig[h / kvh_div] (kv heads sharing a chunk).
+struct AttnLink {
+  const int* wait = nullptr;
+  int target = 0;
+  int* sig = nullptr;
+  int span = 1, kvh_div = 1;
+};
 int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, const int32_t* d_pages,
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
                      int* d_err, const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count,
-                     cudaStream_t st, float* d_out_f32 = nullptr);
+                     cudaStream_t st, float* d_out_f32 = nullptr, const AttnLink& link = AttnLink{});
+// Splits per (kv head, m-tile) that launch_attention uses for these arguments (its grid is nkv x splits x mtiles).
+int attention_splits(int q, const LlamaDims& d, int max_pages, int sm_count);
 // Wide-window attention (windows of more than 16 rows, and batched windows of several sessions): one CTA per
 // (kv head, block of 16 window rows, session segment) holds the block's rows of every query head of the kv head
 // (16 x group rows; a group of 8 is split over two CTAs of 4 heads) and streams the segment's visible KV pages once through a 3-page ring (bulk copies by a
