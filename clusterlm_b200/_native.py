@@ -74,6 +74,7 @@ _SIGS = {
     "clm_b200_commit": (_i, [_vp, _u64, _u32]),
     "clm_b200_run_tree_window": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp]),
     "clm_b200_run_batch_window": (_i, [_vp, _u32, _vp, _vp, _u32, _vp, _vp, _vp]),
+    "clm_b200_run_batch_window_device": (_i, [_vp, _u32, _vp, _vp, _u32, _vp, _vp, _vp, _vp, _vp]),
     "clm_b200_llama_load_tensors": (_i, [_vp, _vp, _u32]),
     "clm_b200_commit_path": (_i, [_vp, _u64, _vp, _u32]),
     "clm_b200_run_tree_window_device": (_i, [_vp, _u64, _u64, _u32, _vp, _vp, _vp, _vp, _vp, _vp]),
@@ -83,6 +84,7 @@ _SIGS = {
     "clm_b200_mtp_draft": (_i, [_vp, C.c_int32, _u32, _f, _u64, _u64, _vp, _vp]),
     "clm_b200_mtp_propose": (_i, [_vp, C.c_int32, _u32, _f, _u32, _f, _vp, _vp, _vp]),
     "clm_b200_shard_stats": (_i, [_vp, _vp, _u32, _u32, _u64, _f, _vp, _vp, _vp]),
+    "clm_b200_shard_combine": (_i, [_vp, _vp, _vp, _u32, _vp, _u32, _u32, _f, _vp, _vp, _vp]),
     "clm_b200_shard_probs": (_i, [_vp, _vp, _u32, _u32, _f, _vp, _vp, _vp, _vp]),
     "clm_b200_spec_begin": (_i, [_vp, _u64, _vp, _u32, _vp]),
     "clm_b200_spec_round": (_i, [_vp, _u64, _vp, _vp, _vp]),

@@ -42,8 +42,8 @@ struct SessionState {  // device-resident, one per session
 
 struct Gemv {
   clm_b200_matrix* m = nullptr;
-  GemvPlan plan[2];  // nt = 1, 2
-  const GemvPlan& for_q(int q) const { return plan[q <= 8 ? 0 : 1]; }
+  GemvPlan plan[3];  // nt = 1, 2, 4
+  const GemvPlan& for_q(int q) const { return plan[q <= 8 ? 0 : (q <= 16 ? 1 : 2)]; }
 };
 
 struct Session {
@@ -342,6 +342,7 @@ struct LlamaEngine : clm_b200_engine {
     CLM_TRY(matrix_create(ctx, d.quant, d_src, true, nbytes, rows, cols, &g.m, half_rows));
     g.plan[0] = gemv_plan(g.m->shape, 8, ctx->sm_count);
     g.plan[1] = gemv_plan(g.m->shape, 16, ctx->sm_count);
+    g.plan[2] = gemv_plan(g.m->shape, 32, ctx->sm_count);
     weight_bytes += g.m->bytes;
     return CLM_OK;
   }
@@ -779,6 +780,72 @@ struct LlamaEngine : clm_b200_engine {
     }
     if (has_head) return gemm_wide(head, q, logits, st);
     return launch_pack_boundary(h, nullptr, 0, q, d.H, bout, st);
+  }
+
+  // ---- one window over several sessions on the q-row GEMV chain (n sessions x qs <= 32 rows, linear windows): every
+  // matrix streams once for all rows (the 4-n-tile GEMV), the QKV epilogue places each row's K / V at its own
+  // session's position, and the attention runs once per session into that session's rows of W_o's input
+  int enqueue_batch_chain(const WideSeg* segs, int nseg, int Q, const int32_t* d_tok, cudaStream_t st) {
+    const int qs = segs[0].q;
+    CLM_CHECK(nseg >= 1 && nseg <= 4 && Q == nseg * qs && Q <= 32, CLM_OUT_OF_RANGE,
+              "batched GEMV window: at most 4 sessions and 32 rows");
+    const int nt = Q <= 8 ? 1 : (Q <= 16 ? 2 : 4);
+    if (has_tokens) {
+      CLM_TRY(launch_pdl(embed_guard_kernel, dim3(1), dim3(64), 0, st, d_tok, Q, (int)d.V, tokens, bad));
+      CLM_TRY(launch_embed(embd, d.quant, tokens, Q, d.H, h, st));
+    } else {
+      CLM_TRY(launch_unpack_boundary(bin, Q, d.H, h, st));
+    }
+    const float* w0 = layers.empty() ? (has_head ? out_norm : ones_h) : layers[0].attn_norm;
+    CLM_TRY(launch_prep_rows(h, d.H, Q, d.H, w0, nt, hi_scale(), xa, true, st));
+    for (size_t li = 0; li < layers.size(); ++li) {
+      Layer& L = layers[li];
+      Epi ek = epi_base(EPI_ROPE_KV);
+      ek.nh = d.nh;
+      ek.nkv = d.nkv;
+      ek.hd = d.hd;
+      ek.rope = rope;
+      ek.kpool = kpool[li];
+      ek.vpool = vpool[li];
+      ek.q16 = q16;
+      ek.seg_q = qs;
+      for (int k = 0; k < nseg; ++k) {
+        ek.seg_pos[k] = &segs[k].s->d_state->pos;
+        ek.seg_pages[k] = segs[k].s->d_pages;
+      }
+      CLM_TRY(gemv(L.qkv, Q, xa, ek, st));
+      for (int k = 0; k < nseg; ++k)
+        CLM_TRY(launch_attention(q16 + (size_t)segs[k].row0 * d.qd(), kpool[li], vpool[li], segs[k].s->d_pages,
+                                 &segs[k].s->d_state->pos, nullptr, qs, d, max_pages, attn_part, acount, nt, hi_scale(),
+                                 xb.frag, xb.sum, bad, k + 1 == nseg ? static_cast<const uint8_t*>(L.o.m->data) : nullptr,
+                                 L.o.m->shape.bytes(), ctx->sm_count, st, nullptr, AttnLink{}, segs[k].row0, Q));
+      XBuf ob = xb;
+      ob.ss = nullptr;
+      Epi eo = epi_resid(h, L.ffn_norm, xa);
+      lookahead(eo, L.gu);
+      CLM_TRY(gemv(L.o, Q, ob, eo, st));
+      Epi es = epi_base(EPI_SWIGLU_PREP);
+      es.ffn = d.F;
+      es.next = xb;
+      lookahead(es, L.down);
+      CLM_TRY(gemv(L.gu, Q, xa, es, st));
+      const float* wnext = li + 1 < layers.size() ? layers[li + 1].attn_norm : (has_head ? out_norm : ones_h);
+      XBuf db = xb;
+      db.ss = nullptr;
+      Epi ed = epi_resid(h, wnext, xa);
+      if (li + 1 < layers.size())
+        lookahead(ed, layers[li + 1].qkv);
+      else if (has_head)
+        lookahead(ed, head);
+      CLM_TRY(gemv(L.down, Q, db, ed, st));
+    }
+    if (has_head) {
+      Epi eo = epi_base(EPI_STORE);
+      eo.out = logits;
+      eo.out_ld = d.V;
+      return gemv(head, Q, xa, eo, st);
+    }
+    return launch_pack_boundary(h, nullptr, 0, Q, d.H, bout, st);
   }
 
   // ---- a full window: input (tokens or records) -> layers -> logits or records
@@ -1304,7 +1371,7 @@ int llama_prepare(LlamaEngine* e) {
   uint64_t part_floats = 1, max_ng = 1;
   auto account = [&](const Gemv& g) {
     if (!g.m) return;
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < 3; ++i)
       part_floats = std::max<uint64_t>(part_floats, (uint64_t)g.m->shape.ng * g.plan[i].ksplit * W * 128);
     max_ng = std::max<uint64_t>(max_ng, g.m->shape.ng);
   };
@@ -1347,10 +1414,11 @@ int llama_prepare(LlamaEngine* e) {
   CLM_CUDA(cudaMemset(e->acount, 0, (size_t)2 * mtiles * d.nkv * sizeof(int)));
   e->acount_n = (size_t)2 * mtiles * d.nkv;
   for (XBuf* x : {&e->xa, &e->xb}) {
-    CLM_TRY(e->alloc((void**)&x->frag, xfrag_bytes(maxcols, 2)));
-    CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 2)));
-    CLM_TRY(e->alloc((void**)&x->sum, xsum_bytes(maxcols)));
-    CLM_CUDA(cudaMemset(x->sum, 0, xsum_bytes(maxcols)));
+    // fragments and sums for up to 32 window rows (the batched GEMV chain's 4 n-tiles)
+    CLM_TRY(e->alloc((void**)&x->frag, xfrag_bytes(maxcols, 4)));
+    CLM_CUDA(cudaMemset(x->frag, 0, xfrag_bytes(maxcols, 4)));
+    CLM_TRY(e->alloc((void**)&x->sum, xsum_bytes(maxcols, 4)));
+    CLM_CUDA(cudaMemset(x->sum, 0, xsum_bytes(maxcols, 4)));
     CLM_TRY(e->alloc_t(&x->ss, (size_t)(d.H / 16) * 16));  // partials per 128 columns, or per 16 (strip GEMV)
     x->nss = d.H / 128;
   }
@@ -1727,6 +1795,51 @@ int llama_run_batch(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint6
       g.s->tree_parents.assign(h_parents, h_parents + q);
     else
       g.s->tree_parents.clear();
+  }
+  return CLM_OK;
+}
+
+int llama_run_batch_device(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint64_t* bases, uint32_t q,
+                           const int32_t* d_tokens, const float* d_in, float* d_out, float* d_logits, void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(ids != nullptr && bases != nullptr && n >= 1 && n <= 4 && q >= 1 && q <= 8, CLM_INVALID_ARGUMENT,
+            "batched GEMV window: 1..4 sessions of 1..8 rows");
+  const uint32_t Q = n * q;
+  CLM_CHECK(Q <= e->spec.max_window, CLM_RESOURCE_EXHAUSTED, "batched window exceeds max_window");
+  if (e->has_tokens)
+    CLM_CHECK(d_tokens != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes tokens");
+  else
+    CLM_CHECK(d_in != nullptr, CLM_INVALID_ARGUMENT, "this stage consumes activations");
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  std::vector<LlamaEngine::WideSeg> segs;
+  for (uint32_t b = 0; b < n; ++b) {
+    for (uint32_t c = 0; c < b; ++c) CLM_CHECK(ids[c] != ids[b], CLM_INVALID_ARGUMENT, "a session appears twice");
+    Session* s = nullptr;
+    CLM_TRY(run_window_common(e, ids[b], bases[b], q, st, &s));
+    segs.push_back({s, (int)(b * q), (int)q});
+  }
+  const size_t rec = (size_t)Q * e->floats_per_position() * sizeof(float);
+  if (e->has_tokens)
+    CLM_CUDA(cudaMemcpyAsync(e->win, d_tokens, Q * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  else
+    CLM_CUDA(cudaMemcpyAsync(e->bin, d_in, rec, cudaMemcpyDeviceToDevice, st));
+  std::vector<uint64_t> key(ids, ids + n);
+  auto& holder = e->batch_graphs[key];
+  if (!holder) holder = std::make_unique<Session>();
+  CLM_TRY(e->run_graph(*holder, 8, (int)Q, 0, st, [&](cudaStream_t cs) {
+    return e->enqueue_batch_chain(segs.data(), (int)n, (int)Q, e->win, cs);
+  }));
+  if (e->has_head) {
+    if (d_logits)
+      CLM_CUDA(cudaMemcpyAsync(d_logits, e->logits, (size_t)Q * e->d.V * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  } else if (d_out) {
+    CLM_CUDA(cudaMemcpyAsync(d_out, e->bout, rec, cudaMemcpyDeviceToDevice, st));
+  }
+  for (auto& g : segs) {
+    g.s->outstanding = q;
+    g.s->tree = false;
+    g.s->tree_parents.clear();
   }
   return CLM_OK;
 }

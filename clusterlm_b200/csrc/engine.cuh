@@ -37,6 +37,8 @@ int llama_run_tree(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const
 int llama_commit_path(LlamaEngine* e, uint64_t id, const int32_t* h_path, uint32_t n);
 int llama_run_tree_device(LlamaEngine* e, uint64_t id, uint64_t base, uint32_t q, const int32_t* d_parents,
                           const int32_t* d_tokens, const float* d_in, float* d_out, float* d_logits, void* stream);
+int llama_run_batch_device(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint64_t* bases, uint32_t q,
+                           const int32_t* d_tokens, const float* d_in, float* d_out, float* d_logits, void* stream);
 int llama_run_batch(LlamaEngine* e, uint32_t n, const uint64_t* ids, const uint64_t* bases, uint32_t q,
                     const int32_t* h_parents, const int32_t* h_tokens, float* h_logits);
 int llama_abort(LlamaEngine* e, uint64_t id);

@@ -177,6 +177,15 @@ int clm_b200_run_batch_window(clm_b200_engine* e, uint32_t n_sessions, const uin
   return llama_run_batch(llama(e), n_sessions, sessions, bases, positions, h_parents, h_tokens, h_logits);
 }
 
+int clm_b200_run_batch_window_device(clm_b200_engine* e, uint32_t n_sessions, const uint64_t* sessions,
+                                     const uint64_t* bases, uint32_t positions, const int32_t* d_tokens,
+                                     const float* d_in, float* d_out, float* d_logits, void* stream) {
+  CLM_TRY(enter(e));
+  CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "batched windows are implemented for the Llama family");
+  return llama_run_batch_device(llama(e), n_sessions, sessions, bases, positions, d_tokens, d_in, d_out, d_logits,
+                                stream);
+}
+
 static int llama_only(clm_b200_engine* e) {
   CLM_TRY(enter(e));
   CLM_CHECK(e->family == CLM_FAMILY_LLAMA, CLM_UNIMPLEMENTED, "stage pipelines are implemented for the Llama family");

@@ -172,7 +172,7 @@ template <typename Raw, int NT>
 __global__ void __launch_bounds__(kG4Threads, 1) flow_kernel(FlowParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kG4MaxStages], empty[kG4MaxStages];
-  __shared__ float s_scale[16];
+  __shared__ float s_scale[kSsRows];
   __shared__ float s_red[kG4Consumers];
   __shared__ int s_last, s_ok;
   uint8_t* ring = smem;

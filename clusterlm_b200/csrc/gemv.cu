@@ -134,18 +134,21 @@ GemvShape gemv_shape(int quant, uint32_t rows, uint32_t cols) {
 
 GemvPlan gemv_plan(const GemvShape& s, int q, int sm_count) {
   // The persistent GEMV (gemv4.cu): one CTA per SM over a ring of `stages` superblock-pair stages, each holding
-  // the pair's weights (2 x 8 tiles), activation fragments (2 x nt x 4 KB) and sub-block sums (2 x 1 KB).
+  // the pair's weights (2 x 8 tiles), activation fragments (2 x nt x 4 KB) and sub-block sums (2 x sum tiles x
+  // 512 B); nt = 1, 2 or 4 n-tiles of 8 window rows.
   GemvPlan p;
-  p.nt = q <= 8 ? 1 : 2;
-  const long long units = (long long)s.ng * ((s.sb + 1) / 2);
+  p.nt = q <= 8 ? 1 : (q <= 16 ? 2 : 4);
+  const int usb = gemv_unit_sb(p.nt);
+  const long long units = (long long)s.ng * ((s.sb + usb - 1) / usb);
   p.grid = (int)std::min<long long>(units, sm_count > 0 ? sm_count : 148);
-  const size_t stage = (size_t)2 * kGemvWarps * s.tile_bytes + (size_t)2 * p.nt * kXfragSbBytes + 2 * 1024;
-  const size_t y_bytes = (size_t)16 * 128 * sizeof(float);
-  p.stages = 4;
+  const size_t stage = (size_t)usb * kGemvWarps * s.tile_bytes + (size_t)usb * p.nt * kXfragSbBytes +
+                       (size_t)usb * 512 * sum_tiles(p.nt);
+  const size_t y_bytes = (size_t)(p.nt >= 4 ? 32 : 16) * 128 * sizeof(float);
+  p.stages = usb == 1 ? 8 : 4;
   while (p.stages > 2 && p.stages * stage + y_bytes > kGemvSmemBudget) --p.stages;
   p.smem = p.stages * stage + y_bytes;
   // row-group segments: a group of ppr units spans at most ceil(ppr * grid / units) + 1 CTA ranges
-  const long long ppr = (s.sb + 1) / 2;
+  const long long ppr = (s.sb + usb - 1) / usb;
   p.ksplit = (int)((ppr * p.grid + units - 1) / units + 1);
   p.xfrag_bytes = (uint64_t)p.nt * s.sb * kXfragSbBytes;
   p.xs_bytes = 0;

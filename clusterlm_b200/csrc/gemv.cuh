@@ -28,6 +28,16 @@ constexpr int kGemvWarps = 8;        // row tiles per row group / warps per CTA
 constexpr int kXfragSbBytes = 16 * 32 * 8;  // one superblock of B fragments for one n8 column tile
 constexpr size_t kGemvSmemBudget = 210 * 1024;  // dynamic shared memory of one persistent GEMV CTA
 
+// n-tiles of the min / bias B fragments per superblock in an activation hand-off (two for up to 16 window rows,
+// four for up to 32)
+__host__ __device__ constexpr int sum_tiles(int nt) { return nt < 2 ? 2 : nt; }
+// window rows per group of sum-of-squares partials (XBuf::ss is [nss][kSsRows])
+constexpr int kSsRows = 32;
+
+// Superblocks per unit of the stream-K GEMV: pairs, or single superblocks for 4 n-tiles (whose activation fragments
+// would otherwise leave room for only two ring stages).
+__host__ __device__ constexpr int gemv_unit_sb(int nt) { return nt >= 4 ? 1 : 2; }
+
 struct GemvShape {
   int quant = 0;
   uint32_t rows = 0, cols = 0;

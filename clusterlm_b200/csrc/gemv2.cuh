@@ -22,8 +22,8 @@ enum { EPI_STORE = 0, EPI_RESID_PREP = 1, EPI_ROPE_KV = 2, EPI_SWIGLU_PREP = 3 }
 // Activation hand-off between a producer and a consuming GEMV.
 struct XBuf {
   uint2* frag = nullptr;   // [SB][nt][16 s][32 lanes]
-  float* sum = nullptr;    // [SB][2 n-tiles][32 lanes][4 words] min / bias mma B fragments (1 KB per superblock)
-  float* ss = nullptr;     // [nss][16 p] sum-of-squares partials, one per 128 columns (row scale), or null
+  float* sum = nullptr;    // [SB][sum_tiles(nt) n-tiles][32 lanes][4 words] min / bias mma B fragments (512 B each)
+  float* ss = nullptr;     // [nss][kSsRows p] sum-of-squares partials, one per 128 (or 16) columns, or null
   int nss = 0;
 };
 
@@ -49,6 +49,11 @@ struct Epi {
   __half* kpool = nullptr;
   __half* vpool = nullptr;
   __half* q16 = nullptr;
+  // EPI_ROPE_KV over a window of several sessions (seg_q > 0): rows [s * seg_q, (s + 1) * seg_q) belong to session
+  // s, at its committed position *seg_pos[s] with its page table seg_pages[s] (linear windows; pos / pages unused)
+  int seg_q = 0;
+  const long long* seg_pos[4] = {};
+  const int32_t* seg_pages[4] = {};
   // EPI_SWIGLU_PREP: rows of the CTA's first tile are gate rows, second tile the matching up rows
   int ffn = 0;
   int* err = nullptr;  // set to 1 if a bounded wait gave up
@@ -93,7 +98,7 @@ int launch_prep_rows(const float* d_x, long long ld, int q, int cols, const floa
                      const XBuf& out, bool with_ss, cudaStream_t st);
 // Bytes of the fragment / sum buffers for `cols` columns.
 inline size_t xfrag_bytes(int cols, int nt) { return (size_t)(cols / 256) * nt * 32 * 16 * sizeof(uint2); }
-inline size_t xsum_bytes(int cols) { return (size_t)(cols / 256) * 1024; }
+inline size_t xsum_bytes(int cols, int nt = 2) { return (size_t)(cols / 256) * 512 * sum_tiles(nt); }
 
 // Device helper shared by producers: writes the fragments / half sums of one 16-column group [16c, 16c+16)
 // of activation row p from `vals` (16 floats, already multiplied by the next norm's weight if any) and, when
@@ -118,15 +123,16 @@ __device__ __forceinline__ void prep16(const float* vals, const float* raw, int 
         (uint32_t)__half_as_ushort(__float2half_rn(sa)) | ((uint32_t)__half_as_ushort(__float2half_rn(sbv)) << 16);
   }
   const int j = o / 32, half = (o % 32) / 16;
-  if (p < 16) {
+  const int ns = sum_tiles(nt);
+  if (p < 8 * ns) {
     // B fragment words of the min / bias mma (k = half * 8 + sub-block): lane (p % 8, j / 2), element j % 2
     const __half hi = __float2half_rn(sum);
     const __half lo = __float2half_rn(sum - __half2float(hi));
-    __half* wq = reinterpret_cast<__half*>(xsum) + ((((size_t)sb * 2 + ntile) * 32 + g * 4 + (j >> 1)) * 4) * 2;
+    __half* wq = reinterpret_cast<__half*>(xsum) + ((((size_t)sb * ns + ntile) * 32 + g * 4 + (j >> 1)) * 4) * 2;
     wq[half * 2 + (j & 1)] = hi;
     wq[(2 + half) * 2 + (j & 1)] = lo;
   }
-  if (ss_out && p < 16) ss_out[(size_t)c * 16 + p] = ss;
+  if (ss_out && p < kSsRows) ss_out[(size_t)c * kSsRows + p] = ss;
   (void)total_cols;
 }
 

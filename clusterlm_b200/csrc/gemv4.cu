@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
                                                              int maxseg, int ahead) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kG4MaxStages], empty[kG4MaxStages];
-  __shared__ float s_scale[16];
+  __shared__ float s_scale[kSsRows];
   __shared__ float s_red[kG4Consumers];
   __shared__ int s_last;
   float* y = reinterpret_cast<float*>(smem + (size_t)stages * geo.stage_bytes);  // [16][128]
@@ -66,28 +66,28 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
     if (lane == 0) {
       const uint64_t policy = evict_first_policy();
       auto issue_weights = [&](const UnitCursor& c) {
-        const int nsb = min(2, geo.sb - 2 * c.pr);
+        const int nsb = min(geo.usb, geo.sb - geo.usb * c.pr);
         uint8_t* st = smem + (size_t)c.slot * geo.stage_bytes;
         const uint32_t wb = (uint32_t)(nsb * geo.sb_bytes);
-        const uint32_t ab = (uint32_t)(nsb * NT * kXfragSbBytes + 2 * nsb * kG4SbSumBytes);
+        const uint32_t ab = (uint32_t)(nsb * NT * kXfragSbBytes + nsb * 512 * sum_tiles(NT));
         mbar_expect_tx(&full[c.slot], wb + ab);
-        bulk_g2s_stream(st, tiles + ((size_t)c.grp * geo.sb + 2 * c.pr) * geo.sb_bytes, wb, &full[c.slot], policy);
+        bulk_g2s_stream(st, tiles + ((size_t)c.grp * geo.sb + geo.usb * c.pr) * geo.sb_bytes, wb, &full[c.slot], policy);
       };
       auto issue_acts = [&](const UnitCursor& c) {
-        const int nsb = min(2, geo.sb - 2 * c.pr);
+        const int nsb = min(geo.usb, geo.sb - geo.usb * c.pr);
         uint8_t* st = smem + (size_t)c.slot * geo.stage_bytes;
-        bulk_g2s(st + geo.frag_off, in.frag + (size_t)2 * c.pr * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
+        bulk_g2s(st + geo.frag_off, in.frag + (size_t)geo.usb * c.pr * NT * 512, (uint32_t)(nsb * NT * kXfragSbBytes),
                  &full[c.slot]);
-        bulk_g2s(st + geo.sum_off, reinterpret_cast<const uint8_t*>(in.sum) + (size_t)2 * c.pr * 1024,
-                 (uint32_t)(nsb * 1024), &full[c.slot]);
+        bulk_g2s(st + geo.sum_off, reinterpret_cast<const uint8_t*>(in.sum) + (size_t)geo.usb * c.pr * 512 * sum_tiles(NT),
+                 (uint32_t)(nsb * 512 * sum_tiles(NT)), &full[c.slot]);
       };
       // dataflow: a unit's activation copies wait for its input chunk (a failed wait drops them from the stage's
       // barrier instead, so the consumers never wait for copies that will not come; the error flag is raised)
       auto acts_when_ready = [&](const UnitCursor& c) {
         if (linked) {
           if (!dep_wait(epi.wait + c.pr, epi.wait_target, epi.err)) {
-            const int nsb = min(2, geo.sb - 2 * c.pr);
-            mbar_complete_tx(&full[c.slot], (uint32_t)(nsb * NT * kXfragSbBytes + 2 * nsb * kG4SbSumBytes));
+            const int nsb = min(geo.usb, geo.sb - geo.usb * c.pr);
+            mbar_complete_tx(&full[c.slot], (uint32_t)(nsb * NT * kXfragSbBytes + nsb * 512 * sum_tiles(NT)));
             return;
           }
           fence_proxy_async_global();  // the copies read what other CTAs' epilogues stored
@@ -100,9 +100,9 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
       int l2i = 0;
       auto l2_until = [&](int upto) {
         for (; l2i < n && l2i < upto; ++l2i, l2.next(geo.ppr, stages)) {
-          const int nsb = min(2, geo.sb - 2 * l2.pr);
+          const int nsb = min(geo.usb, geo.sb - geo.usb * l2.pr);
           const unsigned long long bytes = (unsigned long long)nsb * geo.sb_bytes;
-          l2_prefetch_share(tiles + ((size_t)l2.grp * geo.sb + 2 * l2.pr) * geo.sb_bytes, bytes, 0, 1, bytes);
+          l2_prefetch_share(tiles + ((size_t)l2.grp * geo.sb + geo.usb * l2.pr) * geo.sb_bytes, bytes, 0, 1, bytes);
         }
       };
       const int pre = min(n, stages);
@@ -155,9 +155,12 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
   acc.zero();
   int cur = n > 0 ? start.grp : -1;
   EpiPre pre;
-  const EpiPre* prep = linked ? nullptr : &pre;
-  EpiPre* lazy = linked ? &pre : nullptr;
-  if (cur >= 0 && !linked) epi_preload<EPI>(pre, cur, rows, q, epi);
+  // 32-row launches keep no operands across the units (their accumulators already fill the register budget)
+  const bool preload = !linked && NT < 4;
+  const EpiPre* prep = preload ? &pre : nullptr;
+  EpiPre* lazy = linked && NT < 4 ? &pre : nullptr;
+  constexpr int kQm = NT >= 4 ? 32 : 16;
+  if (cur >= 0 && preload) epi_preload<EPI, kQm>(pre, cur, rows, q, epi);
   UnitCursor c = start;
   // both groups walk every unit of the range, so they flush the same row groups at the same points
   for (int i = 0; i < n; ++i, c.next(geo.ppr, stages)) {
@@ -165,12 +168,12 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
       g4_flush<NT>(cur, acc, y, part, counters, maxseg, U, G, u0, geo.ppr, q, rows, EPI, epi, s_scale, &s_last, ss_pre,
                    in, scale_ready, s_red, prep, lazy);
       cur = c.grp;
-      if (!linked) epi_preload<EPI>(pre, cur, rows, q, epi);
+      if (preload) epi_preload<EPI, kQm>(pre, cur, rows, q, epi);
       acc.zero();
     }
     if ((i & 1) != grp_of_warp) continue;
     mbar_wait(&full[c.slot], c.phase, epi.err);
-    g4_consume_pair<Raw, NT>(smem + (size_t)c.slot * geo.stage_bytes, geo, min(2, geo.sb - 2 * c.pr), rt, lane, acc);
+    g4_consume_pair<Raw, NT>(smem + (size_t)c.slot * geo.stage_bytes, geo, min(geo.usb, geo.sb - geo.usb * c.pr), rt, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[c.slot]);
   }
@@ -210,7 +213,7 @@ __global__ void prep_rows_kernel(const float* __restrict__ x, long long ld, int 
     }
   }
   for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  if (ss && ln == 0 && p < 16) ss[(size_t)c * 16 + p] = a;
+  if (ss && ln == 0 && p < kSsRows) ss[(size_t)c * kSsRows + p] = a;
 }
 
 int launch_prep_rows(const float* d_x, long long ld, int q, int cols, const float* d_w, int nt, float hi_scale,
@@ -235,7 +238,7 @@ static int launch4(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles
                    const Epi& epi, float* part, int* counters, cudaStream_t st) {
   auto kern = gemv4_kernel<Raw, NT, EPI>;
   CLM_TRY(ensure_smem(kern, p.smem));
-  const G4Geom geo = g4_geom(s, NT, 2);
+  const G4Geom geo = g4_geom(s, NT, gemv_unit_sb(NT));
   return launch_pdl(kern, dim3((unsigned)p.grid), dim3(kG4Threads), p.smem, st, d_tiles, s.rows, (int)s.ng, geo,
                     p.stages, in, q, epi, part, counters, p.ksplit, gemv_l2_ahead());
 }
@@ -255,11 +258,14 @@ static int launch4_epi(const GemvShape& s, const GemvPlan& p, const uint8_t* d_t
 int launch_gemv(const GemvShape& s, const GemvPlan& p, const uint8_t* d_tiles, const XBuf& in, int q, const Epi& epi,
                 float* part, int* counters, cudaStream_t st) {
   CLM_CHECK(q >= 1 && q <= 8 * p.nt, CLM_INTERNAL, "GEMV plan does not cover the window width");
-  if (s.quant == CLM_QUANT_Q4_K)
-    return p.nt == 1 ? launch4_epi<RawQ4k, 1>(s, p, d_tiles, in, q, epi, part, counters, st)
-                     : launch4_epi<RawQ4k, 2>(s, p, d_tiles, in, q, epi, part, counters, st);
-  return p.nt == 1 ? launch4_epi<RawQ80, 1>(s, p, d_tiles, in, q, epi, part, counters, st)
-                   : launch4_epi<RawQ80, 2>(s, p, d_tiles, in, q, epi, part, counters, st);
+  if (s.quant == CLM_QUANT_Q4_K) {
+    if (p.nt == 1) return launch4_epi<RawQ4k, 1>(s, p, d_tiles, in, q, epi, part, counters, st);
+    if (p.nt == 2) return launch4_epi<RawQ4k, 2>(s, p, d_tiles, in, q, epi, part, counters, st);
+    return launch4_epi<RawQ4k, 4>(s, p, d_tiles, in, q, epi, part, counters, st);
+  }
+  if (p.nt == 1) return launch4_epi<RawQ80, 1>(s, p, d_tiles, in, q, epi, part, counters, st);
+  if (p.nt == 2) return launch4_epi<RawQ80, 2>(s, p, d_tiles, in, q, epi, part, counters, st);
+  return launch4_epi<RawQ80, 4>(s, p, d_tiles, in, q, epi, part, counters, st);
 }
 
 }  // namespace clm

@@ -74,29 +74,32 @@ struct UnitCursor {
 // Epilogue operands that do not depend on this kernel's products (the residual rows and the next norm's weights,
 // or the position, page and RoPE factors), loaded when a CTA starts a row group so that their latency overlaps the
 // group's tensor-core work and the segment exchange.  Element i = tid + kG4Consumers * k of the epilogue's loops.
+// QM: the most window rows the launch serves (16, or 32 for the 4-n-tile GEMV); the loops below run QM / 4 (residual)
+// and QM / 8 (RoPE) elements per thread.
 struct EpiPre {
-  float h[4];       // EPI_RESID_PREP: h[p][row0 + r], i = p * 128 + r
+  float h[8];       // EPI_RESID_PREP: h[p][row0 + r], i = p * 128 + r
   float w;          // EPI_RESID_PREP: wnext[row0 + tid] (tid < 128)
   long long base;   // EPI_ROPE_KV: committed position
-  float2 cs[2];     // EPI_ROPE_KV: RoPE (cos, sin) of element i = p * (hd / 2) + pair
-  int32_t page[2];  // EPI_ROPE_KV: KV page of window row p
+  float2 cs[4];     // EPI_ROPE_KV: RoPE (cos, sin) of element i = p * (hd / 2) + pair
+  int32_t page[4];  // EPI_ROPE_KV: KV page of window row p
 };
 
-template <int EPI>
+template <int EPI, int QM = 16>
 __device__ __forceinline__ void epi_preload(EpiPre& pre, int grp, uint32_t rows, int q, const Epi& epi) {
   const int tid = threadIdx.x, row0 = grp * 128;
   if (EPI == EPI_RESID_PREP) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < QM / 4; ++k) {
       const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
       pre.h[k] = (i < q * 128 && row0 + r < (int)rows) ? __ldcg(epi.h + (size_t)p * epi.H + row0 + r) : 0.0f;
     }
     pre.w = (tid < 128 && row0 + tid < (int)rows) ? epi.wnext[row0 + tid] : 0.0f;
   } else if (EPI == EPI_ROPE_KV) {
+    if (epi.seg_q > 0) return;  // several sessions: the epilogue reads its operands itself
     const int hd = epi.hd, head = grp;
     pre.base = *epi.pos;
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < QM / 8; ++k) {
       const int i = tid + kG4Consumers * k, p = i / (hd / 2), pr = i % (hd / 2);
       pre.cs[k] = make_float2(0.0f, 0.0f);
       pre.page[k] = 0;
@@ -114,7 +117,7 @@ __device__ __forceinline__ void epi_preload(EpiPre& pre, int grp, uint32_t rows,
 
 // Epilogue over y[p][r] (128 rows of group grp) in shared memory; consumer threads only.  `pre` holds the operands
 // preloaded by epi_preload (or null: they are read here); s_aux is shared scratch of at least 128 floats.
-template <int EPI>
+template <int EPI, int QM = 16>
 __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t rows, int q, const Epi& epi,
                             float* s_aux, const EpiPre* pre) {
   const int tid = threadIdx.x;
@@ -126,7 +129,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
     }
   } else if (EPI == EPI_RESID_PREP) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < QM / 4; ++k) {
       const int i = tid + kG4Consumers * k, p = i / 128, r = i % 128;
       if (i >= q * 128 || row0 + r >= (int)rows) continue;
       float* hp = epi.h + (size_t)p * epi.H + row0 + r;
@@ -136,7 +139,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
     }
     if (tid < 128) s_aux[tid] = pre ? pre->w : (row0 + tid < (int)rows ? epi.wnext[row0 + tid] : 0.0f);
     consumer_sync();
-    const int nt_out = q <= 8 ? 1 : 2;
+    const int nt_out = (q + 7) / 8 == 3 ? 4 : (q + 7) / 8;
     for (int i = tid; i < 8 * 8 * nt_out; i += kG4Consumers) {
       const int gg = i % 8, p = i / 8;
       float vals[16];
@@ -150,35 +153,42 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
     }
     // the next consumer's row scale: sum of squares of this group's 128 new residual values, per row
     if (epi.next.ss) {
-      const int p = tid / 32, ln = tid % 32;  // 16 rows, one warp each
-      float a = 0.0f;
-      if (p < q && row0 + ln < (int)rows) {
+      const int ln = tid % 32;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float v = y[p * 128 + ln + 32 * k];
-          a += v * v;
+      for (int p = tid / 32; p < QM; p += kG4Consumers / 32) {  // one warp per row
+        float a = 0.0f;
+        if (p < q && row0 + ln < (int)rows) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float v = y[p * 128 + ln + 32 * k];
+            a += v * v;
+          }
         }
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (ln == 0) epi.next.ss[(size_t)grp * kSsRows + p] = a;
       }
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (ln == 0) epi.next.ss[(size_t)grp * 16 + p] = a;
     }
   } else if (EPI == EPI_ROPE_KV) {
     const int head = grp, hd = epi.hd;
-    const long long base = pre ? pre->base : *epi.pos;
+    const bool seg = epi.seg_q > 0;
+    if (seg) pre = nullptr;
+    const long long base = seg ? 0 : (pre ? pre->base : *epi.pos);
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < QM / 8; ++k) {
       const int i = tid + kG4Consumers * k;
       if (i >= q * (hd / 2)) continue;
       const int p = i / (hd / 2), pr = i % (hd / 2);
       const float a = y[p * 128 + 2 * pr] * s_scale[p], b = y[p * 128 + 2 * pr + 1] * s_scale[p];
-      const long long slot = base + p;
-      const int32_t page = pre ? pre->page[k] : epi.pages[slot / 64];
+      // several sessions: row p is row p % seg_q of session p / seg_q
+      const int sg = seg ? p / epi.seg_q : 0;
+      const long long slot = seg ? *epi.seg_pos[sg] + (p - sg * epi.seg_q) : base + p;
+      const int32_t page = pre ? pre->page[k] : (seg ? epi.seg_pages[sg] : epi.pages)[slot / 64];
       if (head < epi.nh + epi.nkv) {
         float2 cs;
         if (pre) {
           cs = pre->cs[k];
         } else {
-          const long long rope_pos = epi.parent ? base + tree_depth4(epi.parent, p) : slot;
+          const long long rope_pos = (!seg && epi.parent) ? base + tree_depth4(epi.parent, p) : slot;
           cs = epi.rope[(size_t)rope_pos * (hd / 2) + pr];
         }
         const float c = cs.x, s = cs.y;
@@ -208,7 +218,7 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
       y[p * 128 + k] = gv / (1.0f + expf(-gv)) * uv;
     }
     consumer_sync();
-    const int nt_out = q <= 8 ? 1 : 2;
+    const int nt_out = (q + 7) / 8 == 3 ? 4 : (q + 7) / 8;
     for (int i = tid; i < 4 * 8 * nt_out; i += kG4Consumers) {
       const int gg = i % 4, p = i / 4;
       float vals[16];
@@ -222,57 +232,60 @@ __device__ void g4_epilogue(float* y, const float* s_scale, int grp, uint32_t ro
 }
 
 
-// Epilogue kind chosen at run time (the dataflow kernel's phases).
+// Epilogue kind chosen at run time (the dataflow kernel's phases, the flush of a row group).
+template <int QM = 16>
 __device__ __forceinline__ void g4_epilogue_rt(int kind, float* y, const float* s_scale, int grp, uint32_t rows,
                                                int q, const Epi& epi, float* s_aux, const EpiPre* pre) {
   switch (kind) {
-    case EPI_STORE: g4_epilogue<EPI_STORE>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
-    case EPI_RESID_PREP: g4_epilogue<EPI_RESID_PREP>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
-    case EPI_ROPE_KV: g4_epilogue<EPI_ROPE_KV>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
-    default: g4_epilogue<EPI_SWIGLU_PREP>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    case EPI_STORE: g4_epilogue<EPI_STORE, QM>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    case EPI_RESID_PREP: g4_epilogue<EPI_RESID_PREP, QM>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    case EPI_ROPE_KV: g4_epilogue<EPI_ROPE_KV, QM>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
+    default: g4_epilogue<EPI_SWIGLU_PREP, QM>(y, s_scale, grp, rows, q, epi, s_aux, pre); break;
   }
 }
 
 // epi_preload with the kind chosen at run time.
+template <int QM = 16>
 __device__ __forceinline__ void epi_preload_rt(int kind, EpiPre& pre, int grp, uint32_t rows, int q, const Epi& epi) {
-  if (kind == EPI_RESID_PREP) epi_preload<EPI_RESID_PREP>(pre, grp, rows, q, epi);
-  if (kind == EPI_ROPE_KV) epi_preload<EPI_ROPE_KV>(pre, grp, rows, q, epi);
+  if (kind == EPI_RESID_PREP) epi_preload<EPI_RESID_PREP, QM>(pre, grp, rows, q, epi);
+  if (kind == EPI_ROPE_KV) epi_preload<EPI_ROPE_KV, QM>(pre, grp, rows, q, epi);
 }
 
 // Row scale (folded rmsnorm) 1/sqrt(sum(ss)/ss_n + eps) per window row from the input's sum-of-squares partials
 // (1 without partials), in two steps so that the partials' load latency overlaps the first units: g4_ss_load at
 // the start of a GEMV (registers only), g4_ss_finish before the first flush.  Consumer threads only; s_red holds
-// kG4Consumers floats.  Thread tid adds partials c = tid / 16 + 32 k (k ascending) of row tid % 16; the first two
-// are loaded ahead, any further ones (partials per 16 columns of the strip GEMV) in g4_ss_finish.
+// kG4Consumers floats, s_scale kSsRows.  Thread tid adds partials c = tid / 32 + 16 k (k ascending) of row tid % 32;
+// the first two are loaded ahead, any further ones (partials per 16 columns of the strip GEMV) in g4_ss_finish.
 struct G4SsPre {
   float a = 0.0f, b = 0.0f;
 };
 __device__ __forceinline__ G4SsPre g4_ss_load(const XBuf& in) {
   G4SsPre r;
-  const int tid = threadIdx.x, p = tid % 16, c = tid / 16;
-  constexpr int kStride = kG4Consumers / 16;
+  const int tid = threadIdx.x, p = tid % kSsRows, c = tid / kSsRows;
+  constexpr int kStride = kG4Consumers / kSsRows;
   if (in.ss) {
-    if (c < in.nss) r.a = __ldcg(in.ss + (size_t)c * 16 + p);
-    if (c + kStride < in.nss) r.b = __ldcg(in.ss + (size_t)(c + kStride) * 16 + p);
+    if (c < in.nss) r.a = __ldcg(in.ss + (size_t)c * kSsRows + p);
+    if (c + kStride < in.nss) r.b = __ldcg(in.ss + (size_t)(c + kStride) * kSsRows + p);
   }
   return r;
 }
 __device__ __forceinline__ void g4_ss_finish(const G4SsPre& pre, const XBuf& in, const Epi& epi, int q, float* s_red,
                                              float* s_scale) {
   const int tid = threadIdx.x;
+  constexpr int kStride = kG4Consumers / kSsRows;
   {
-    constexpr int kStride = kG4Consumers / 16;
     float a = pre.a + pre.b;
     if (in.ss)
-      for (int c = tid / 16 + 2 * kStride; c < in.nss; c += kStride) a += __ldcg(in.ss + (size_t)c * 16 + tid % 16);
+      for (int c = tid / kSsRows + 2 * kStride; c < in.nss; c += kStride)
+        a += __ldcg(in.ss + (size_t)c * kSsRows + tid % kSsRows);
     s_red[tid] = a;
   }
   consumer_sync();
-  if (tid < 16) {
+  if (tid < kSsRows) {
     float sc = 1.0f;
     if (in.ss && tid < q) {
       float tot = 0.0f;
-      for (int c = 0; c < kG4Consumers / 16; ++c) tot += s_red[c * 16 + tid];
+      for (int c = 0; c < kStride; ++c) tot += s_red[c * kSsRows + tid];
       sc = 1.0f / sqrtf(tot / epi.ss_n + epi.eps);
     }
     s_scale[tid] = sc;
@@ -326,7 +339,7 @@ __device__ __forceinline__ void g4_consume_tile(const uint8_t* st, const G4Geom&
   tile_mmas<NT>(r, t, xf, lane, acc.v, mg, mg8);
   // min / bias term of this superblock: A = -m per (row, sub-block) for both 16-column halves, B = the staged
   // fp16 hi / lo half sums (prep16's fragment layout)
-  const uint4* sf = reinterpret_cast<const uint4*>(st + geo.sum_off) + hh * 64;
+  const uint4* sf = reinterpret_cast<const uint4*>(st + geo.sum_off) + hh * 32 * sum_tiles(NT);
   (void)nsb;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -361,9 +374,9 @@ __device__ __forceinline__ void g4_consume_pair(const uint8_t* st, const G4Geom&
     const uint32_t a = hh ? m1 : m0, a8 = hh ? m18 : m08;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const uint4 b = sf[hh * 64 + nt * 32 + lane];
+      const uint4 b = sf[hh * 32 * sum_tiles(NT) + nt * 32 + lane];
       mma16816(acc.v[0][nt], a, a8, a, a8, b.x, b.y);
-      mma16816(acc.v[1][nt], a, a8, a, a8, b.z, b.w);
+      mma16816(acc.v[NT >= 4 ? 0 : 1][nt], a, a8, a, a8, b.z, b.w);
     }
   }
 }
@@ -448,7 +461,7 @@ __device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
       return false;
     }
     if (lazy != nullptr) {  // the epilogue's operands load while the other segments' partials arrive
-      epi_preload_rt(epi_kind, *lazy, grp, rows, q, epi);
+      epi_preload_rt<NT >= 4 ? 32 : 16>(epi_kind, *lazy, grp, rows, q, epi);
       pre = lazy;
     }
     if (tid == 0) {
@@ -478,7 +491,7 @@ __device__ bool g4_flush(int grp, const G4Acc<NT>& acc, float* y, float* part, i
     }
     consumer_sync();
   }
-  g4_epilogue_rt(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);  // ends with a consumer barrier
+  g4_epilogue_rt<NT >= 4 ? 32 : 16>(epi_kind, y, s_scale, grp, rows, q, epi, s_red, pre);  // ends with a barrier
   if (tid == 0) g4_signal(epi, grp);
   return true;
 }
@@ -491,7 +504,7 @@ inline G4Geom g4_geom(const GemvShape& s, int nt, int usb = 2) {
   geo.ppr = (int)(s.sb + usb - 1) / usb;
   geo.tile_bytes = s.tile_bytes;
   geo.sb_bytes = kGemvWarps * s.tile_bytes;
-  geo.sum_half = usb * kG4SbSumBytes;  // the stage's sum region is 2 * sum_half = usb x 1 KB
+  geo.sum_half = usb * 256 * sum_tiles(nt);  // the stage's sum region is 2 * sum_half = usb x 512 B x sum tiles
   geo.frag_off = usb * geo.sb_bytes;
   geo.sum_off = geo.frag_off + usb * nt * kXfragSbBytes;
   geo.stage_bytes = geo.sum_off + 2 * geo.sum_half;

@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
         float sc = 1.0f;
         if (in.ss && tg < q) {
           float tot = 0.0f;
-          for (int c = 0; c < in.nss; ++c) tot += __ldcg(in.ss + (size_t)c * 16 + tg);
+          for (int c = 0; c < in.nss; ++c) tot += __ldcg(in.ss + (size_t)c * kSsRows + tg);
           sc = 1.0f / sqrtf(tot / epi.ss_n + epi.eps);
         }
         s_scale[grp_of_warp][tg] = sc;
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
         if (p < q)
 #pragma unroll
           for (int k = 0; k < 16; ++k) a += y[k * 8 + p] * y[k * 8 + p];
-        epi.next.ss[(size_t)(row0 / 16) * 16 + p] = a;
+        epi.next.ss[(size_t)(row0 / 16) * kSsRows + p] = a;
       }
     } else if (EPI == EPI_ROPE_KV) {
       // rows row0 .. row0 + 15: dims d0 .. d0 + 15 of head row0 / hd (pairs d0 / 2 + i)

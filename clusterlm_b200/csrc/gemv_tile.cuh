@@ -153,7 +153,8 @@ static __device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const u
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
+      // with 4 n-tiles the chains are already independent: one accumulator set (registers for the 32-row GEMV)
+      mma16816(acc[NT >= 4 ? 0 : (s & 1)][nt], a0, a1, a2, a3, b.x, b.y);
     }
   }
 }
@@ -176,7 +177,7 @@ static __device__ __forceinline__ void tile_mmas(const RawQ80& r, int t, const u
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
+      mma16816(acc[NT >= 4 ? 0 : (s & 1)][nt], a0, a1, a2, a3, b.x, b.y);
     }
   }
 }

@@ -110,7 +110,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
     const int32_t* __restrict__ pages, const long long* __restrict__ d_pos, const int32_t* __restrict__ parent, int q,
     int nh, int nkv, float scale_log2, int max_pages, float* __restrict__ part, int* __restrict__ counters, int nt_out,
     float hi_scale, uint2* __restrict__ out_frag, float* __restrict__ out_sum, int* __restrict__ err,
-    const uint8_t* __restrict__ pf, unsigned long long pf_bytes, float* __restrict__ out_f32, AttnLink link) {
+    const uint8_t* __restrict__ pf, unsigned long long pf_bytes, float* __restrict__ out_f32, AttnLink link,
+    int row_off, int q_frag) {
   static_assert(HD == 128, "head_dim 128 layout");
   static_assert(kAttnWarps == 2 * kAttnPages, "two warps per page buffer");
   constexpr int RW = kAttnRowFloats;  // one partial row: O[HD], m, l, padding (16-byte aligned rows)
@@ -396,7 +397,8 @@ __global__ void __launch_bounds__(32 * kAttnWarps) attention_kernel(
       // query vector r = window row i, head kvh*group + r%group; 16 columns 16cg.. of that head
       const int i = (mt * 16 + r) / group, head = kvh * group + (mt * 16 + r) % group;
       if (i < q)
-        prep16(s_out[li], nullptr, i, q, (head * HD + 16 * cg) / 16, nt_out, hi_scale, out_frag, out_sum, nullptr, qd);
+        prep16(s_out[li], nullptr, row_off + i, q_frag, (head * HD + 16 * cg) / 16, nt_out, hi_scale, out_frag, out_sum,
+               nullptr, qd);
     }
     __syncthreads();
   }
@@ -416,9 +418,11 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum, int* d_err,
                      const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count, cudaStream_t st,
-                     float* d_out_f32, const AttnLink& link) {
+                     float* d_out_f32, const AttnLink& link, int row_off, int q_frag) {
   CLM_CHECK(d.hd == 128, CLM_UNIMPLEMENTED, "attention kernel supports head_dim 128");
-  CLM_CHECK(d_out_f32 != nullptr || q <= 16, CLM_OUT_OF_RANGE, "W_o input fragments cover at most 16 window rows");
+  if (q_frag <= 0) q_frag = q;
+  CLM_CHECK(d_out_f32 != nullptr || (row_off >= 0 && row_off + q <= q_frag && q_frag <= 8 * nt_out && nt_out <= 4),
+            CLM_OUT_OF_RANGE, "W_o input fragments: rows outside the window's n-tiles");
   const int group = d.nh / d.nkv;
   const int mtiles = (q * group + 15) / 16;
   const float scale_log2 = (float)(1.4426950408889634 / sqrt((double)d.hd));
@@ -429,7 +433,8 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
   CLM_TRY(ensure_smem(attention_kernel<128>, smem));
   return launch_pdl(attention_kernel<128>, dim3(d.nkv, splits, mtiles), dim3(32 * kAttnWarps), smem, st, d_q, d_k,
                     d_v, d_pages, d_pos, d_parent, q, d.nh, d.nkv, scale_log2, max_pages, d_part, d_counters, nt_out,
-                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes, d_out_f32, link);
+                    hi_scale, static_cast<uint2*>(d_frag), d_sum, d_err, d_prefetch, prefetch_bytes, d_out_f32, link,
+                    row_off, q_frag);
 }
 
 int attention_splits(int q, const LlamaDims& d, int max_pages, int sm_count) {

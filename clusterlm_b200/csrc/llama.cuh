@@ -57,7 +57,10 @@ int launch_attention(const __half* d_q, const __half* d_k, const __half* d_v, co
                      const long long* d_pos, const int32_t* d_parent, int q, const LlamaDims& d, int max_pages,
                      float* d_part, int* d_counters, int nt_out, float hi_scale, void* d_frag, float* d_sum,
                      int* d_err, const uint8_t* d_prefetch, unsigned long long prefetch_bytes, int sm_count,
-                     cudaStream_t st, float* d_out_f32 = nullptr, const AttnLink& link = AttnLink{});
+                     cudaStream_t st, float* d_out_f32 = nullptr, const AttnLink& link = AttnLink{},
+                     int row_off = 0, int q_frag = 0);
+// row_off / q_frag: the window's rows are rows row_off .. row_off + q - 1 of a batched window of q_frag rows (the W_o
+// fragments of every session of the batch; q_frag 0 = q).
 // Splits per (kv head, m-tile) that launch_attention uses for these arguments (its grid is nkv x splits x mtiles).
 int attention_splits(int q, const LlamaDims& d, int max_pages, int sm_count);
 // Wide-window attention (windows of more than 16 rows, and batched windows of several sessions): one CTA per

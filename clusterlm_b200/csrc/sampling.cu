@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "pdl.cuh"
 #include "sampling.cuh"
+#include "exp2_table.cuh"
 
 namespace clm {
 
@@ -316,94 +317,27 @@ __device__ bool last_of(int* cnt, int total) {
 
 __device__ __forceinline__ float read_temperature(float T, const RoundCtl* ctl) { return ctl ? ctl->temperature : T; }
 
-// 2^(j/256), j = 0..255, correctly rounded to double (table of the table-driven exponential below).
-__device__ const double kExp2Tab[256] = {
-    0x1.0000000000000p+0, 0x1.00b1afa5abcbfp+0, 0x1.0163da9fb3335p+0, 0x1.02168143b0281p+0,
-    0x1.02c9a3e778061p+0, 0x1.037d42e11bbccp+0, 0x1.04315e86e7f85p+0, 0x1.04e5f72f654b1p+0,
-    0x1.059b0d3158574p+0, 0x1.0650a0e3c1f89p+0, 0x1.0706b29ddf6dep+0, 0x1.07bd42b72a836p+0,
-    0x1.0874518759bc8p+0, 0x1.092bdf66607e0p+0, 0x1.09e3ecac6f383p+0, 0x1.0a9c79b1f3919p+0,
-    0x1.0b5586cf9890fp+0, 0x1.0c0f145e46c85p+0, 0x1.0cc922b7247f7p+0, 0x1.0d83b23395decp+0,
-    0x1.0e3ec32d3d1a2p+0, 0x1.0efa55fdfa9c5p+0, 0x1.0fb66affed31bp+0, 0x1.1073028d7233ep+0,
-    0x1.11301d0125b51p+0, 0x1.11edbab5e2ab6p+0, 0x1.12abdc06c31ccp+0, 0x1.136a814f204abp+0,
-    0x1.1429aaea92de0p+0, 0x1.14e95934f312ep+0, 0x1.15a98c8a58e51p+0, 0x1.166a45471c3c2p+0,
-    0x1.172b83c7d517bp+0, 0x1.17ed48695bbc0p+0, 0x1.18af9388c8deap+0, 0x1.1972658375d2fp+0,
-    0x1.1a35beb6fcb75p+0, 0x1.1af99f8138a1cp+0, 0x1.1bbe084045cd4p+0, 0x1.1c82f95281c6bp+0,
-    0x1.1d4873168b9aap+0, 0x1.1e0e75eb44027p+0, 0x1.1ed5022fcd91dp+0, 0x1.1f9c18438ce4dp+0,
-    0x1.2063b88628cd6p+0, 0x1.212be3578a819p+0, 0x1.21f49917ddc96p+0, 0x1.22bdda27912d1p+0,
-    0x1.2387a6e756238p+0, 0x1.2451ffb82140ap+0, 0x1.251ce4fb2a63fp+0, 0x1.25e85711ece75p+0,
-    0x1.26b4565e27cddp+0, 0x1.2780e341ddf29p+0, 0x1.284dfe1f56381p+0, 0x1.291ba7591bb70p+0,
-    0x1.29e9df51fdee1p+0, 0x1.2ab8a66d10f13p+0, 0x1.2b87fd0dad990p+0, 0x1.2c57e39771b2fp+0,
-    0x1.2d285a6e4030bp+0, 0x1.2df961f641589p+0, 0x1.2ecafa93e2f56p+0, 0x1.2f9d24abd886bp+0,
-    0x1.306fe0a31b715p+0, 0x1.31432edeeb2fdp+0, 0x1.32170fc4cd831p+0, 0x1.32eb83ba8ea32p+0,
-    0x1.33c08b26416ffp+0, 0x1.3496266e3fa2dp+0, 0x1.356c55f929ff1p+0, 0x1.36431a2de883bp+0,
-    0x1.371a7373aa9cbp+0, 0x1.37f26231e754ap+0, 0x1.38cae6d05d866p+0, 0x1.39a401b7140efp+0,
-    0x1.3a7db34e59ff7p+0, 0x1.3b57fbfec6cf4p+0, 0x1.3c32dc313a8e5p+0, 0x1.3d0e544ede173p+0,
-    0x1.3dea64c123422p+0, 0x1.3ec70df1c5175p+0, 0x1.3fa4504ac801cp+0, 0x1.40822c367a024p+0,
-    0x1.4160a21f72e2ap+0, 0x1.423fb2709468ap+0, 0x1.431f5d950a897p+0, 0x1.43ffa3f84b9d4p+0,
-    0x1.44e086061892dp+0, 0x1.45c2042a7d232p+0, 0x1.46a41ed1d0057p+0, 0x1.4786d668b3237p+0,
-    0x1.486a2b5c13cd0p+0, 0x1.494e1e192aed2p+0, 0x1.4a32af0d7d3dep+0, 0x1.4b17dea6db7d7p+0,
-    0x1.4bfdad5362a27p+0, 0x1.4ce41b817c114p+0, 0x1.4dcb299fddd0dp+0, 0x1.4eb2d81d8abffp+0,
-    0x1.4f9b2769d2ca7p+0, 0x1.508417f4531eep+0, 0x1.516daa2cf6642p+0, 0x1.5257de83f4eefp+0,
-    0x1.5342b569d4f82p+0, 0x1.542e2f4f6ad27p+0, 0x1.551a4ca5d920fp+0, 0x1.56070dde910d2p+0,
-    0x1.56f4736b527dap+0, 0x1.57e27dbe2c4cfp+0, 0x1.58d12d497c7fdp+0, 0x1.59c0827ff07ccp+0,
-    0x1.5ab07dd485429p+0, 0x1.5ba11fba87a03p+0, 0x1.5c9268a5946b7p+0, 0x1.5d84590998b93p+0,
-    0x1.5e76f15ad2148p+0, 0x1.5f6a320dceb71p+0, 0x1.605e1b976dc09p+0, 0x1.6152ae6cdf6f4p+0,
-    0x1.6247eb03a5585p+0, 0x1.633dd1d1929fdp+0, 0x1.6434634ccc320p+0, 0x1.652b9febc8fb7p+0,
-    0x1.6623882552225p+0, 0x1.671c1c70833f6p+0, 0x1.68155d44ca973p+0, 0x1.690f4b19e9538p+0,
-    0x1.6a09e667f3bcdp+0, 0x1.6b052fa75173ep+0, 0x1.6c012750bdabfp+0, 0x1.6cfdcddd47645p+0,
-    0x1.6dfb23c651a2fp+0, 0x1.6ef9298593ae5p+0, 0x1.6ff7df9519484p+0, 0x1.70f7466f42e87p+0,
-    0x1.71f75e8ec5f74p+0, 0x1.72f8286ead08ap+0, 0x1.73f9a48a58174p+0, 0x1.74fbd35d7cbfdp+0,
-    0x1.75feb564267c9p+0, 0x1.77024b1ab6e09p+0, 0x1.780694fde5d3fp+0, 0x1.790b938ac1cf6p+0,
-    0x1.7a11473eb0187p+0, 0x1.7b17b0976cfdbp+0, 0x1.7c1ed0130c132p+0, 0x1.7d26a62ff86f0p+0,
-    0x1.7e2f336cf4e62p+0, 0x1.7f3878491c491p+0, 0x1.80427543e1a12p+0, 0x1.814d2add106d9p+0,
-    0x1.82589994cce13p+0, 0x1.8364c1eb941f7p+0, 0x1.8471a4623c7adp+0, 0x1.857f4179f5b21p+0,
-    0x1.868d99b4492edp+0, 0x1.879cad931a436p+0, 0x1.88ac7d98a6699p+0, 0x1.89bd0a478580fp+0,
-    0x1.8ace5422aa0dbp+0, 0x1.8be05bad61778p+0, 0x1.8cf3216b5448cp+0, 0x1.8e06a5e0866d9p+0,
-    0x1.8f1ae99157736p+0, 0x1.902fed0282c8ap+0, 0x1.9145b0b91ffc6p+0, 0x1.925c353aa2fe2p+0,
-    0x1.93737b0cdc5e5p+0, 0x1.948b82b5f98e5p+0, 0x1.95a44cbc8520fp+0, 0x1.96bdd9a7670b3p+0,
-    0x1.97d829fde4e50p+0, 0x1.98f33e47a22a2p+0, 0x1.9a0f170ca07bap+0, 0x1.9b2bb4d53fe0dp+0,
-    0x1.9c49182a3f090p+0, 0x1.9d674194bb8d5p+0, 0x1.9e86319e32323p+0, 0x1.9fa5e8d07f29ep+0,
-    0x1.a0c667b5de565p+0, 0x1.a1e7aed8eb8bbp+0, 0x1.a309bec4a2d33p+0, 0x1.a42c980460ad8p+0,
-    0x1.a5503b23e255dp+0, 0x1.a674a8af46052p+0, 0x1.a799e1330b358p+0, 0x1.a8bfe53c12e59p+0,
-    0x1.a9e6b5579fdbfp+0, 0x1.ab0e521356ebap+0, 0x1.ac36bbfd3f37ap+0, 0x1.ad5ff3a3c2774p+0,
-    0x1.ae89f995ad3adp+0, 0x1.afb4ce622f2ffp+0, 0x1.b0e07298db666p+0, 0x1.b20ce6c9a8952p+0,
-    0x1.b33a2b84f15fbp+0, 0x1.b468415b749b1p+0, 0x1.b59728de5593ap+0, 0x1.b6c6e29f1c52ap+0,
-    0x1.b7f76f2fb5e47p+0, 0x1.b928cf22749e4p+0, 0x1.ba5b030a1064ap+0, 0x1.bb8e0b79a6f1fp+0,
-    0x1.bcc1e904bc1d2p+0, 0x1.bdf69c3f3a207p+0, 0x1.bf2c25bd71e09p+0, 0x1.c06286141b33dp+0,
-    0x1.c199bdd85529cp+0, 0x1.c2d1cd9fa652cp+0, 0x1.c40ab5fffd07ap+0, 0x1.c544778fafb22p+0,
-    0x1.c67f12e57d14bp+0, 0x1.c7ba88988c933p+0, 0x1.c8f6d9406e7b5p+0, 0x1.ca3405751c4dbp+0,
-    0x1.cb720dcef9069p+0, 0x1.ccb0f2e6d1675p+0, 0x1.cdf0b555dc3fap+0, 0x1.cf3155b5bab74p+0,
-    0x1.d072d4a07897cp+0, 0x1.d1b532b08c968p+0, 0x1.d2f87080d89f2p+0, 0x1.d43c8eacaa1d6p+0,
-    0x1.d5818dcfba487p+0, 0x1.d6c76e862e6d3p+0, 0x1.d80e316c98398p+0, 0x1.d955d71ff6075p+0,
-    0x1.da9e603db3285p+0, 0x1.dbe7cd63a8315p+0, 0x1.dd321f301b460p+0, 0x1.de7d5641c0658p+0,
-    0x1.dfc97337b9b5fp+0, 0x1.e11676b197d17p+0, 0x1.e264614f5a129p+0, 0x1.e3b333b16ee12p+0,
-    0x1.e502ee78b3ff6p+0, 0x1.e653924676d76p+0, 0x1.e7a51fbc74c83p+0, 0x1.e8f7977cdb740p+0,
-    0x1.ea4afa2a490dap+0, 0x1.eb9f4867cca6ep+0, 0x1.ecf482d8e67f1p+0, 0x1.ee4aaa2188510p+0,
-    0x1.efa1bee615a27p+0, 0x1.f0f9c1cb6412ap+0, 0x1.f252b376bba97p+0, 0x1.f3ac948dd7274p+0,
-    0x1.f50765b6e4540p+0, 0x1.f6632798844f8p+0, 0x1.f7bfdad9cbe14p+0, 0x1.f91d802243c89p+0,
-    0x1.fa7c1819e90d8p+0, 0x1.fbdba3692d514p+0, 0x1.fd3c22b8f71f1p+0, 0x1.fe9d96b2a23d9p+0,
-};
-
 // exp(x) for x <= 0 in double precision by Tang's table-driven method (P. T. P. Tang, "Table-driven
-// implementation of the exponential function in IEEE floating-point arithmetic", ACM TOMS 15(2), 1989):
-// x = (k + r') ln2 / 256 with k = rint(x * 256 / ln2) and |r| <= ln2 / 512 (ln2 / 256 split into a 34-bit head, so
-// that k * head is exact, and a tail); exp(x) = 2^(k >> 8) * T[k & 255] * (1 + p(r)) with p the degree-5 Taylor
-// polynomial of exp(r) - 1 (truncation below 1e-20 relative).  About 1 ulp, like a library exp; results that
-// would be subnormal, -inf and NaN take the library exp.
+// implementation of the exponential function in IEEE floating-point arithmetic", ACM TOMS 15(2), 1989), with a
+// 2048-entry table (exp2_table.cuh): x = (k + r') ln2 / 2048 with k = round(x * 2048 / ln2), taken from the low bits
+// of x * 2048 / ln2 + 1.5 * 2^52 (no conversion instructions), and |r| <= ln2 / 4096 (ln2 / 2048 split into a
+// 29-bit head, so that k * head is exact, and a tail); exp(x) = 2^(k >> 11) * T[k & 2047] * (1 + p(r)) with p the
+// degree-4 Taylor polynomial of exp(r) - 1 (truncation below 1e-20 relative).  Within 1 ulp of exp, like a library
+// exp; results that would be subnormal, -inf and NaN take the library exp.
 __device__ __forceinline__ double exp_nonpos(double x) {
   if (!(x > -707.0)) return exp(x);
-  const double kd = rint(x * 0x1.71547652b82fep+8);
-  const int k = (int)kd;
-  double r = fma(kd, -0x1.62e42fef80000p-9, x);
-  r = fma(kd, -0x1.1cf79abc9e3b4p-44, r);
-  double p = fma(r, 1.0 / 120.0, 1.0 / 24.0);
-  p = fma(p, r, 1.0 / 6.0);
-  p = fma(p, r, 0.5);
-  p = fma(p, r, 1.0);
-  p *= r;
-  const double t = __ldg(&kExp2Tab[k & 255]);
-  const double y = fma(t, p, t);
-  return __longlong_as_double(__double_as_longlong(y) + ((long long)(k >> 8) << 52));
+  constexpr double kShift = 0x1.8p52;
+  double kd = fma(x, k2048ByLn2, kShift);
+  const int k = (int)(unsigned)__double_as_longlong(kd);  // the rounded integer sits in the low bits
+  kd -= kShift;
+  double r = fma(kd, -kLn2By2048Head, x);
+  r = fma(kd, -kLn2By2048Tail, r);
+  double t = fma(r, 1.0 / 24.0, 1.0 / 6.0);
+  t = fma(r, t, 0.5);
+  const double p = fma(r * r, t, r);
+  const double tab = __ldg(&kExp2Tab2048[k & 2047]);
+  const double y = fma(tab, p, tab);
+  return __longlong_as_double(__double_as_longlong(y) + ((long long)(k >> 11) << 52));
 }
 
 // e = exp(double(l - m) / T), the reference's softmax term (sampling.cpp:64); at T = 1 the division is the
@@ -411,6 +345,19 @@ __device__ __forceinline__ double exp_nonpos(double x) {
 __device__ __forceinline__ double soft_term(float l, float m, float T) {
   const double x = (double)__fsub_rn(l, m);
   return exp_nonpos(T == 1.0f ? x : x / (double)T);
+}
+
+// float(e / kept), the reference's probability of a softmax term (sampling.cpp:64-83: a double quotient rounded to
+// float), through a multiplication by inv = 1 / kept: the double product differs from the correctly rounded quotient
+// by at most 2 ulps, so it rounds to the same float unless it lies within a few ulps of a float rounding boundary
+// (a double whose 29 bits below the float mantissa are 1 << 28); there, and outside the normal float range of a
+// probability, the quotient itself is computed.  Same float as (float)(e / kept) for every input.
+__device__ __forceinline__ float prob_of(double e, double kept, double inv) {
+  const double q = e * inv;
+  if (!(q > 0x1p-125 && q < 1.0)) return (float)(e / kept);
+  const long long d = (long long)(__double_as_longlong(q) & 0x1FFFFFFFll) - (1ll << 28);
+  if (d > -16 && d < 16) return (float)(e / kept);
+  return (float)q;
 }
 
 // ---------------------------------------------------------------------------------------------------
@@ -451,18 +398,22 @@ __global__ void __launch_bounds__(kSampleThreads) argmax_chunks_kernel(const flo
 constexpr uint32_t kStatsChunk = 16384;
 inline uint32_t stats_chunks(uint32_t V) { return (V + kStatsChunk - 1) / kStatsChunk; }
 
-__global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* __restrict__ logits, uint32_t V,
-                                                                   uint32_t off, float* __restrict__ cmax,
-                                                                   float* __restrict__ mx, int* __restrict__ cnt) {
-  griddep_wait();
-  griddep_launch();
-  const uint32_t c = blockIdx.x, C = gridDim.x;
-  const float* l = logits + (size_t)blockIdx.y * V;
-  const uint32_t r = blockIdx.y + off;  // statistics row
+// One chunk's statistics in one launch: the chunk maximum m_c (from -FLT_MAX, like the row maximum of the
+// reference's scan) and the double sum s_c of exp(double(l - m_c) / T) in one fixed order (thread-strided float4
+// lanes, four accumulators, block reduction).  The CTA reads its 64 KB chunk twice; the second pass finds it in
+// L1 / L2, so DRAM sees the logits once.  Every thread of the block returns both.  The whole-row statistics and the
+// vocab-shard statistics share it, so a shard that starts at a chunk boundary reproduces the whole row's chunk
+// statistics bit for bit.
+struct ChunkStats {
+  float m;
+  double s;
+};
+__device__ __forceinline__ ChunkStats chunk_stats(const float* __restrict__ l, uint32_t V, uint32_t c, float T) {
   const uint32_t lo = c * kStatsChunk, hi = min(V, lo + kStatsChunk);
-  float m0 = -FLT_MAX, m1 = -FLT_MAX, m2 = -FLT_MAX, m3 = -FLT_MAX;
+  ChunkStats r;
   if ((V & 3u) == 0) {  // rows start 16-byte aligned: float4 loads
     const float4* l4 = reinterpret_cast<const float4*>(l);
+    float m0 = -FLT_MAX, m1 = -FLT_MAX, m2 = -FLT_MAX, m3 = -FLT_MAX;
     for (uint32_t i = lo / 4 + threadIdx.x; i < hi / 4; i += kSampleThreads) {
       const float4 v = l4[i];
       m0 = fmaxf(m0, v.x);
@@ -470,73 +421,98 @@ __global__ void __launch_bounds__(kSampleThreads) stats_max_kernel(const float* 
       m2 = fmaxf(m2, v.z);
       m3 = fmaxf(m3, v.w);
     }
-  } else {
-    for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) m0 = fmaxf(m0, l[i]);
-  }
-  float m = block_max(fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
-  if (threadIdx.x == 0) cmax[(size_t)r * C + c] = m;
-  if (!last_of(&cnt[r], (int)C)) return;
-  if (threadIdx.x == 0) {
-    float a = -FLT_MAX;
-    for (uint32_t k = 0; k < C; ++k) a = fmaxf(a, __ldcg(cmax + (size_t)r * C + k));
-    mx[r] = a;
-  }
-}
-
-// The double sum of the softmax terms of chunk c (entries [c * kStatsChunk, ..) of the row l of V entries) against
-// the row maximum m, in one fixed order (thread-strided float4 lanes, four accumulators, block reduction); the
-// block's threads all return the chunk's sum.  Shared by the whole-row statistics and the vocab-shard statistics,
-// so a shard that starts at a chunk boundary reproduces the whole row's chunk sums bit for bit.
-__device__ __forceinline__ double chunk_soft_sum(const float* __restrict__ l, uint32_t V, uint32_t c, float m, float T) {
-  const uint32_t lo = c * kStatsChunk, hi = min(V, lo + kStatsChunk);
-  double acc = 0.0;
-  if ((V & 3u) == 0) {
-    const float4* l4 = reinterpret_cast<const float4*>(l);
-    double a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    r.m = block_max(fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
     for (uint32_t i = lo / 4 + threadIdx.x; i < hi / 4; i += kSampleThreads) {
       const float4 v = l4[i];
-      acc += soft_term(v.x, m, T);
-      a1 += soft_term(v.y, m, T);
-      a2 += soft_term(v.z, m, T);
-      a3 += soft_term(v.w, m, T);
+      a0 += soft_term(v.x, r.m, T);
+      a1 += soft_term(v.y, r.m, T);
+      a2 += soft_term(v.z, r.m, T);
+      a3 += soft_term(v.w, r.m, T);
     }
-    acc = (acc + a1) + (a2 + a3);
+    r.s = block_sum_d((a0 + a1) + (a2 + a3));
   } else {
-    for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) acc += soft_term(l[i], m, T);
+    float m0 = -FLT_MAX;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) m0 = fmaxf(m0, l[i]);
+    r.m = block_max(m0);
+    double a0 = 0.0;
+    for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) a0 += soft_term(l[i], r.m, T);
+    r.s = block_sum_d(a0);
   }
-  return block_sum_d(acc);
+  return r;
 }
 
-__global__ void __launch_bounds__(kSampleThreads) stats_sum_kernel(const float* __restrict__ logits, uint32_t V,
-                                                                   uint32_t off, float T,
-                                                                   const RoundCtl* __restrict__ ctl,
-                                                                   const float* __restrict__ mx,
-                                                                   double* __restrict__ csum, double* __restrict__ kept,
-                                                                   int* __restrict__ cnt) {
+// Row maximum M (the chunk maxima in chunk order) and kept = sum over chunks of s_c * exp(double(m_c - M) / T), in
+// chunk order: exp((l - M) / T) = exp((l - m_c) / T) * exp((m_c - M) / T), so kept is the whole row's softmax
+// denominator with one extra rounding per chunk.  n chunks at cm / cs (stride 1).
+__device__ __forceinline__ void combine_chunks(const float* cm, const double* cs, uint32_t n, float T, float* M_out,
+                                               double* kept_out) {
+  float M = -FLT_MAX;
+  for (uint32_t k = 0; k < n; ++k) M = fmaxf(M, __ldcg(cm + k));
+  double kept = 0.0;
+  for (uint32_t k = 0; k < n; ++k) kept += __ldcg(cs + k) * soft_term(__ldcg(cm + k), M, T);
+  *M_out = M;
+  *kept_out = kept;
+}
+
+// Row statistics in one pass over the logits: per chunk (m_c, s_c), then the row's last CTA combines them.
+__global__ void __launch_bounds__(kSampleThreads) stats_kernel(const float* __restrict__ logits, uint32_t V,
+                                                               uint32_t off, float T, const RoundCtl* __restrict__ ctl,
+                                                               float* __restrict__ cmax, double* __restrict__ csum,
+                                                               float* __restrict__ mx, double* __restrict__ kept,
+                                                               int* __restrict__ cnt) {
   griddep_wait();
   griddep_launch();
   T = read_temperature(T, ctl);
   const uint32_t c = blockIdx.x, C = gridDim.x;
-  const float* l = logits + (size_t)blockIdx.y * V;
-  const uint32_t r = blockIdx.y + off;
-  const double acc = chunk_soft_sum(l, V, c, mx[r], T);
-  if (threadIdx.x == 0) csum[(size_t)r * C + c] = acc;
-  if (!last_of(&cnt[r], (int)C)) return;
+  const uint32_t r = blockIdx.y + off;  // statistics row
+  const ChunkStats cs = chunk_stats(logits + (size_t)blockIdx.y * V, V, c, T);
   if (threadIdx.x == 0) {
-    double a = 0.0;
-    for (uint32_t k = 0; k < C; ++k) a += __ldcg(csum + (size_t)r * C + k);
-    kept[r] = a;
+    cmax[(size_t)r * C + c] = cs.m;
+    csum[(size_t)r * C + c] = cs.s;
+  }
+  if (!last_of(&cnt[r], (int)C)) return;
+  if (threadIdx.x == 0) combine_chunks(cmax + (size_t)r * C, csum + (size_t)r * C, C, T, &mx[r], &kept[r]);
+}
+
+// Vocab shard statistics: the chunk statistics of the rows of a shard (entries [first, first + Vs) of each row, first
+// a multiple of kStatsChunk), without the combine: om[r][c], os[r][c] for the shard's chunks.
+__global__ void __launch_bounds__(kSampleThreads) shard_chunk_stats_kernel(const float* __restrict__ logits,
+                                                                           uint32_t Vs, float T, float* __restrict__ om,
+                                                                           double* __restrict__ os) {
+  griddep_wait();
+  griddep_launch();
+  const uint32_t c = blockIdx.x, C = gridDim.x;
+  const ChunkStats cs = chunk_stats(logits + (size_t)blockIdx.y * Vs, Vs, c, T);
+  if (threadIdx.x == 0) {
+    om[(size_t)blockIdx.y * C + c] = cs.m;
+    os[(size_t)blockIdx.y * C + c] = cs.s;
   }
 }
 
-// Vocab shard statistics: the chunk sums of rows of a shard (entries [first, first + Vs) of each row, first a
-// multiple of kStatsChunk) against the rows' global maxima, without the combine: out[r][c] for the shard's chunks.
-__global__ void __launch_bounds__(kSampleThreads) shard_chunk_sums_kernel(const float* __restrict__ logits, uint32_t Vs,
-                                                                          float T, const float* __restrict__ gmax,
-                                                                          double* __restrict__ out) {
-  const uint32_t c = blockIdx.x, C = gridDim.x;
-  const double acc = chunk_soft_sum(logits + (size_t)blockIdx.y * Vs, Vs, c, gmax[blockIdx.y], T);
-  if (threadIdx.x == 0) out[(size_t)blockIdx.y * C + c] = acc;
+// The whole rows' (max, kept) from the ranks' gathered chunk statistics gm / gs [world][rows][cmax] (rank w holds
+// counts.n[w] chunks of each row), combined in column order exactly as combine_chunks does for a whole row.
+struct ShardCounts {
+  uint32_t n[64];
+};
+__global__ void shard_combine_kernel(const float* __restrict__ gm, const double* __restrict__ gs, ShardCounts counts,
+                                     uint32_t world, uint32_t rows, uint32_t cmax, float T, float* __restrict__ mx,
+                                     double* __restrict__ kept) {
+  griddep_wait();
+  griddep_launch();
+  const uint32_t r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float M = -FLT_MAX;
+  for (uint32_t w = 0; w < world; ++w)
+    for (uint32_t k = 0; k < counts.n[w]; ++k) M = fmaxf(M, gm[((size_t)w * rows + r) * cmax + k]);
+  double a = 0.0;
+  for (uint32_t w = 0; w < world; ++w)
+    for (uint32_t k = 0; k < counts.n[w]; ++k) {
+      const size_t i = ((size_t)w * rows + r) * cmax + k;
+      a += gs[i] * soft_term(gm[i], M, T);
+    }
+  mx[r] = M;
+  kept[r] = a;
 }
 
 __global__ void __launch_bounds__(kSampleThreads) probs_kernel(const float* __restrict__ logits, uint32_t V, float T,
@@ -551,10 +527,9 @@ __global__ void __launch_bounds__(kSampleThreads) probs_kernel(const float* __re
   const float* l = logits + (size_t)r * V;
   float* o = probs + (size_t)r * V;
   const float m = mx[r];
-  const double k = kept[r];
+  const double k = kept[r], inv = 1.0 / k;
   const uint32_t lo = c * kSampleChunk, hi = min(V, lo + kSampleChunk);
-  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads)
-    o[i] = (float)(soft_term(l[i], m, T) / k);
+  for (uint32_t i = lo + threadIdx.x; i < hi; i += kSampleThreads) o[i] = prob_of(soft_term(l[i], m, T), k, inv);
 }
 
 __global__ void onehot_kernel(const int32_t* __restrict__ idx, uint32_t vocab, float* __restrict__ probs) {
@@ -601,8 +576,9 @@ struct ProbRow {
   float m = 0.0f;
   double kept = 1.0;
   float T = 1.0f;
+  double inv = 1.0;  // 1 / kept
   __device__ __forceinline__ float operator()(uint32_t i) const {
-    return p ? p[i] : (float)(soft_term(l[i], m, T) / kept);
+    return p ? p[i] : prob_of(soft_term(l[i], m, T), kept, inv);
   }
 };
 
@@ -625,11 +601,14 @@ __device__ __forceinline__ float job_temperature(const SampleJob& job) { return 
 // Target row `row` ([seq][k+1] numbering) and draft row `row` ([seq][k]) of an acceptance job.
 __device__ __forceinline__ ProbRow target_row(const SampleJob& job, size_t row, uint32_t V, float T) {
   if (job.P) return ProbRow{job.P + row * V};
-  return ProbRow{nullptr, job.LP + row * V, job.mx[row], job.kept[row], T};
+  return ProbRow{nullptr, job.LP + row * V, job.mx[row], job.kept[row], T, 1.0 / job.kept[row]};
 }
 __device__ __forceinline__ ProbRow draft_row(const SampleJob& job, size_t row, uint32_t V, float T) {
   if (job.Q) return ProbRow{job.Q + row * V};
-  if (job.LQ) return ProbRow{nullptr, job.LQ + row * V, job.mx[job.qoff + row], job.kept[job.qoff + row], T};
+  if (job.LQ) {
+    const double kq = job.kept[job.qoff + row];
+    return ProbRow{nullptr, job.LQ + row * V, job.mx[job.qoff + row], kq, T, 1.0 / kq};
+  }
   return ProbRow{};
 }
 
@@ -1040,9 +1019,8 @@ int launch_row_stats(const float* d_logits, uint32_t rows, uint32_t V, float T, 
   if (rows == 0) return CLM_OK;
   CLM_CHECK(off + rows <= s.rows, CLM_INTERNAL, "sampling scratch too small");
   const dim3 grid(stats_chunks(V), rows);
-  CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, off, s.cmax, s.mx, s.rcnt));
-  return launch_pdl(stats_sum_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, off, T, ctl,
-                    (const float*)s.mx, s.csum, s.kept, s.rcnt);
+  return launch_pdl(stats_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, V, off, T, ctl, s.cmax, s.csum, s.mx,
+                    s.kept, s.rcnt);
 }
 
 int launch_probs(const float* d_logits, uint32_t rows, uint32_t V, float T, const RoundCtl* ctl, float* d_probs,
@@ -1255,26 +1233,32 @@ int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_tl, const float* d_
 }
 
 int clm_b200_shard_stats(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
-                         uint64_t first_col, float temperature, const float* d_global_max, void* d_out, void* stream) {
+                         uint64_t first_col, float temperature, float* d_chunk_max, double* d_chunk_sum, void* stream) {
   CLM_TRY(ctx_enter(ctx));
   CLM_CHECK(vocab_shard > 0 && temperature > 0.0f, CLM_INVALID_ARGUMENT, "empty shard or temperature <= 0");
   CLM_CHECK(first_col % kStatsChunk == 0, CLM_INVALID_ARGUMENT,
             "a vocab shard must start at a multiple of 16384 columns (the statistics chunk)");
   if (rows == 0) return CLM_OK;
-  CLM_CHECK(d_logits && d_out, CLM_INVALID_ARGUMENT, "null buffer");
-  cudaStream_t st = pick_stream(ctx, stream);
-  if (d_global_max == nullptr) {
-    SampleScratch s;
-    CLM_TRY(abi_scratch(ctx, rows, 0, vocab_shard, 0, st, &s, nullptr));
-    const dim3 grid(stats_chunks(vocab_shard), rows);
-    CLM_TRY(launch_pdl(stats_max_kernel, grid, dim3(kSampleThreads), 0, st, d_logits, vocab_shard, 0u, s.cmax,
-                       static_cast<float*>(d_out), s.rcnt));
-    return CLM_OK;
+  CLM_CHECK(d_logits && d_chunk_max && d_chunk_sum, CLM_INVALID_ARGUMENT, "null buffer");
+  return launch_pdl(shard_chunk_stats_kernel, dim3(stats_chunks(vocab_shard), rows), dim3(kSampleThreads), 0,
+                    pick_stream(ctx, stream), d_logits, vocab_shard, temperature, d_chunk_max, d_chunk_sum);
+}
+
+int clm_b200_shard_combine(clm_b200_ctx* ctx, const float* d_chunk_max, const double* d_chunk_sum, uint32_t world,
+                           const uint32_t* h_counts, uint32_t rows, uint32_t max_chunks, float temperature,
+                           float* d_max, double* d_kept, void* stream) {
+  CLM_TRY(ctx_enter(ctx));
+  CLM_CHECK(world >= 1 && world <= 64 && h_counts != nullptr && temperature > 0.0f, CLM_INVALID_ARGUMENT,
+            "1..64 shards with their chunk counts, temperature > 0");
+  if (rows == 0) return CLM_OK;
+  CLM_CHECK(d_chunk_max && d_chunk_sum && d_max && d_kept, CLM_INVALID_ARGUMENT, "null buffer");
+  ShardCounts c{};
+  for (uint32_t w = 0; w < world; ++w) {
+    CLM_CHECK(h_counts[w] <= max_chunks, CLM_INVALID_ARGUMENT, "a shard's chunk count exceeds max_chunks");
+    c.n[w] = h_counts[w];
   }
-  shard_chunk_sums_kernel<<<dim3(stats_chunks(vocab_shard), rows), kSampleThreads, 0, st>>>(
-      d_logits, vocab_shard, temperature, d_global_max, static_cast<double*>(d_out));
-  CLM_LAUNCHED("shard_chunk_sums_kernel");
-  return CLM_OK;
+  return launch_pdl(shard_combine_kernel, dim3((unsigned)ceil_div(rows, 128)), dim3(128), 0, pick_stream(ctx, stream),
+                    d_chunk_max, d_chunk_sum, c, world, rows, max_chunks, temperature, d_max, d_kept);
 }
 
 int clm_b200_shard_probs(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,

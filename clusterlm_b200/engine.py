@@ -214,6 +214,20 @@ class Engine:
              None if out is None else out.ctypes.data_as(_vp))
         return out
 
+    def run_batch_window_device(self, sessions, bases, positions: int, d_tokens=None, d_records=None, d_out=None,
+                                stream=None):
+        """One linear window over up to 4 sessions on the q-row GEMV chain (clm_b200_run_batch_window_device): device
+        tokens (n * positions,) or records (n * positions, floats per position) in, session-major; logits or records
+        out (d_out)."""
+        ids = np.ascontiguousarray(sessions, dtype=np.uint64)
+        bs = np.ascontiguousarray(bases, dtype=np.uint64)
+        has_head = self.role in (ROLE_TAIL, ROLE_WHOLE)
+        call("clm_b200_run_batch_window_device", self.h, ids.size, ids.ctypes.data_as(_vp), bs.ctypes.data_as(_vp),
+             positions, None if d_tokens is None else _vp(d_tokens.data_ptr()),
+             None if d_records is None else _vp(d_records.data_ptr()),
+             None if has_head else _vp(d_out.data_ptr()), _vp(d_out.data_ptr()) if has_head else None,
+             None if stream is None else _vp(stream))
+
     def run_tree_window_device(self, session: int, base: int, d_parents, d_tokens=None, d_out=None, stream=None,
                                d_records=None):
         """Device-buffer tree window (torch CUDA tensors): parents, tokens or records in; logits or records out."""

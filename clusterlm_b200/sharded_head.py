@@ -6,10 +6,12 @@ The reference computes the head and distribution() over whole rows on one proces
 head rows [v0_r, v1_r) (shard boundaries at multiples of the 16,384-column statistics chunk) and:
 
   * computes its columns of the logits (clm_b200_matmul_rows over its shard of the head);
-  * reduces the row maxima with an all-gather (the maximum is exact in any order);
-  * computes the double sums of exp(double(l - max) / T) of its 16,384-column chunks (clm_b200_shard_stats, the
-    same device code as the whole-row statistics) and all-gathers them, and every rank adds all chunks of the row
-    in column order, one after another from 0.0: the kept sum of the whole row, bit for bit;
+  * computes, in one pass over its logits, each 16,384-column chunk's maximum and the double sum of
+    exp(double(l - chunk max) / T) (clm_b200_shard_stats, the same device code as the whole-row statistics);
+  * all-gathers these chunk statistics, and every rank combines them in column order (clm_b200_shard_combine): the
+    row maximum, and the kept sum as the chunk sums times exp(double(chunk max - max) / T) added one after another
+    from 0.0, exactly as the whole-row statistics combine their chunks, so max and kept equal the whole row's bit
+    for bit;
   * evaluates any probability it owns as float(exp(double(l - max) / T) / kept), the whole-row value;
   * runs verify_speculative (sampling.cpp:103-131) with p(d) / q(d) at the draft tokens taken from their owning
     ranks (an all-reduce of a k-vector), the accept decisions in IEEE double exactly as the reference's walk, and
@@ -23,6 +25,8 @@ and one for the final sample, in the reference's order.  Collectives go through 
 GPUs); every rank makes the same calls in the same order.
 """
 from __future__ import annotations
+
+import ctypes as C
 
 import torch
 import torch.distributed as dist
@@ -51,28 +55,20 @@ def combine_max(gathered: torch.Tensor) -> torch.Tensor:
     return gathered.max(dim=0).values
 
 
-def combine_kept(gathered, counts) -> list[float]:
-    """The whole rows' kept sums from the ranks' chunk sums (gathered[r][row][c], counts[r] chunks of rank r): one
-    sequential double addition per chunk in column order, the order of the whole-row statistics."""
-    rows = len(gathered[0])
-    kept = []
+def combine_kept(chunk_max, chunk_sum, counts, factor):
+    """The whole rows' (max, kept) from the ranks' chunk statistics (chunk_max[r][row][c], chunk_sum[r][row][c],
+    counts[r] chunks of rank r) in column order: max over every chunk, then kept = sum of chunk_sum * factor(chunk
+    max, max) added one after another from 0.0 (factor: exp(double(m_c - max) / T) in the device code)."""
+    rows = len(chunk_max[0])
+    out = []
     for i in range(rows):
+        M = max(chunk_max[r][i][c] for r, n in enumerate(counts) for c in range(n))
         a = 0.0
         for r, n in enumerate(counts):
             for c in range(n):
-                a += float(gathered[r][i][c])
-        kept.append(a)
-    return kept
-
-
-def combine_kept_t(gathered: torch.Tensor, counts) -> torch.Tensor:
-    """combine_kept on a [world][rows][max chunks] float64 tensor, where it lies (no host copy): the same
-    sequential additions, one elementwise add per chunk, starting from 0.0 as the whole-row statistics do."""
-    kept = torch.zeros(gathered.shape[1], dtype=torch.float64, device=gathered.device)
-    for r, n in enumerate(counts):
-        for c in range(n):
-            kept = kept + gathered[r, :, c]
-    return kept
+                a += chunk_sum[r][i][c] * factor(chunk_max[r][i][c], M)
+        out.append((M, a))
+    return out
 
 
 def merge_argmax(values, indices):
@@ -144,20 +140,25 @@ class ShardedHead:
     def stats(self, L: torch.Tensor, temperature: float):
         """(max, kept) of the whole rows: float32 and float64 device tensors of len(L) rows."""
         rows = L.shape[0]
-        local = torch.empty(rows, dtype=torch.float32, device=self.dev)
-        call("clm_b200_shard_stats", self.ctx.h, _ptr(L), rows, self.n, self.v0, temperature, None, _ptr(local),
-             _stream())
-        maxima = torch.empty((self.world, rows), dtype=torch.float32, device=self.dev)
-        dist.all_gather_into_tensor(maxima, local, group=self.group)
-        gmax = combine_max(maxima)
-        part = torch.empty((rows, self.counts[self.rank]), dtype=torch.float64, device=self.dev)
-        call("clm_b200_shard_stats", self.ctx.h, _ptr(L), rows, self.n, self.v0, temperature, _ptr(gmax),
-             _ptr(part), _stream())
-        sums = torch.zeros((rows, max(self.counts)), dtype=torch.float64, device=self.dev)
-        sums[:, :part.shape[1]] = part
-        gathered = torch.empty((self.world, rows, sums.shape[1]), dtype=torch.float64, device=self.dev)
-        dist.all_gather_into_tensor(gathered, sums, group=self.group)
-        return gmax, combine_kept_t(gathered, self.counts)
+        cmax = max(self.counts)
+        cm = torch.full((rows, cmax), -3.0e38, dtype=torch.float32, device=self.dev)
+        cs = torch.zeros((rows, cmax), dtype=torch.float64, device=self.dev)
+        mine_m = torch.empty((rows, self.counts[self.rank]), dtype=torch.float32, device=self.dev)
+        mine_s = torch.empty((rows, self.counts[self.rank]), dtype=torch.float64, device=self.dev)
+        call("clm_b200_shard_stats", self.ctx.h, _ptr(L), rows, self.n, self.v0, temperature, _ptr(mine_m),
+             _ptr(mine_s), _stream())
+        cm[:, :mine_m.shape[1]] = mine_m
+        cs[:, :mine_s.shape[1]] = mine_s
+        gm = torch.empty((self.world, rows, cmax), dtype=torch.float32, device=self.dev)
+        gs = torch.empty((self.world, rows, cmax), dtype=torch.float64, device=self.dev)
+        dist.all_gather_into_tensor(gm, cm, group=self.group)
+        dist.all_gather_into_tensor(gs, cs, group=self.group)
+        gmax = torch.empty(rows, dtype=torch.float32, device=self.dev)
+        kept = torch.empty(rows, dtype=torch.float64, device=self.dev)
+        counts = (C.c_uint32 * self.world)(*self.counts)
+        call("clm_b200_shard_combine", self.ctx.h, _ptr(gm), _ptr(gs), self.world, counts, rows, cmax, temperature,
+             _ptr(gmax), _ptr(kept), _stream())
+        return gmax, kept
 
     def probs(self, L: torch.Tensor, gmax: torch.Tensor, kept: torch.Tensor, temperature: float) -> torch.Tensor:
         out = torch.empty_like(L)

@@ -154,14 +154,19 @@ CLM_API int clm_b200_accept_logits(clm_b200_ctx* ctx, const float* d_target_logi
 /* Vocab-sharded distribution rows (the LM head split by vocabulary over GPUs; no reference counterpart: the
  * reference computes distribution(), sampling.cpp:51-86, over whole rows).  A rank holds the logits of columns
  * [first_col, first_col + vocab_shard) of `rows` rows (first_col a multiple of 16384, the statistics chunk).
- *   d_global_max == NULL: d_out = float[rows], each row's maximum over the shard;
- *   otherwise (the rows' maxima over the whole vocabulary): d_out = double[rows][ceil(vocab_shard / 16384)], the
- *   sums of exp(double(l - max) / T) of each 16384-column chunk in the shard, bit-identical to the chunk sums of
- *   the whole-row statistics, so that summing every rank's chunks in column order gives the whole row's kept sum
- *   exactly. */
+ * clm_b200_shard_stats writes, per row and 16384-column chunk of the shard (C = ceil(vocab_shard / 16384) per row),
+ * the chunk's maximum (d_chunk_max, float[rows][C]) and the double sum of exp(double(l - chunk max) / T)
+ * (d_chunk_sum, double[rows][C]): the same values as the whole-row statistics compute for those chunks. */
 CLM_API int clm_b200_shard_stats(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
-                                 uint64_t first_col, float temperature, const float* d_global_max, void* d_out,
+                                 uint64_t first_col, float temperature, float* d_chunk_max, double* d_chunk_sum,
                                  void* stream);
+/* The whole rows' maximum (d_max, float[rows]) and kept sum (d_kept, double[rows]) from every rank's chunk
+ * statistics gathered as d_chunk_max / d_chunk_sum [world][rows][max_chunks] (rank w's first h_counts[w] chunks of
+ * each row valid), combined in column order exactly as the whole-row statistics combine their chunks, so the
+ * results equal those of clm_b200_distribution_rows over the gathered rows bit for bit.  world <= 64. */
+CLM_API int clm_b200_shard_combine(clm_b200_ctx* ctx, const float* d_chunk_max, const double* d_chunk_sum,
+                                   uint32_t world, const uint32_t* h_counts, uint32_t rows, uint32_t max_chunks,
+                                   float temperature, float* d_max, double* d_kept, void* stream);
 /* The shard's probabilities float(exp(double(l - max) / T) / kept) from the rows' global max and kept sum: the same
  * values clm_b200_distribution_rows writes for those columns of the whole rows. */
 CLM_API int clm_b200_shard_probs(clm_b200_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t vocab_shard,
@@ -268,6 +273,17 @@ CLM_API int clm_b200_commit_path(clm_b200_engine* e, uint64_t session, const int
 CLM_API int clm_b200_run_batch_window(clm_b200_engine* e, uint32_t n_sessions, const uint64_t* sessions,
                                       const uint64_t* bases, uint32_t positions, const int32_t* h_parents,
                                       const int32_t* h_tokens, float* h_logits);
+/* A batched window on the q-row GEMV chain, for stages of any role: sessions[b] (n_sessions <= 4) verifies
+ * `positions` (<= 8) linear rows at its committed position bases[b]; every weight matrix of the stage streams once for
+ * all n_sessions * positions rows (<= 32, and <= max_window), with each session's KV rows and attention its own.
+ * Device buffers on the engine's GPU, rows session-major:
+ *   prefix / whole: d_tokens[n][positions]; middle / tail: d_in[n][positions][floats_per_position]
+ *   prefix / middle: d_out[n][positions][floats_per_position]; tail / whole: d_logits[n][positions][vocab]
+ * (no reference counterpart: the reference runs one window per ExecutionDomain call).  Each session then commits or
+ * aborts on its own. */
+CLM_API int clm_b200_run_batch_window_device(clm_b200_engine* e, uint32_t n_sessions, const uint64_t* sessions,
+                                             const uint64_t* bases, uint32_t positions, const int32_t* d_tokens,
+                                             const float* d_in, float* d_out, float* d_logits, void* stream);
 /* Drops the outstanding window (abort_window, reference_domain.cpp:319-329). */
 CLM_API int clm_b200_abort(clm_b200_engine* e, uint64_t session);
 CLM_API int clm_b200_session_position(const clm_b200_engine* e, uint64_t session, uint64_t* committed);

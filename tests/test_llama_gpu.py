@@ -355,3 +355,65 @@ def test_tree_window_device_equals_host_and_guards_parents(ctx):
         e.commit_path(1, [0])
     assert e.position(1) == 18
     e.close()
+
+
+@pytest.mark.parametrize("role", [1, 3])  # middle stage (records in and out), whole model (tokens in, logits out)
+def test_batched_gemv_window_equals_separate_windows(ctx, role):
+    """clm_b200_run_batch_window_device: four sessions' 8-row windows in one 32-row window on the q-row GEMV chain
+    (every matrix streamed once) give each session the outputs of its own window, at different committed positions,
+    and the KV rows each session commits are the ones its later windows read."""
+    import torch
+
+    from clusterlm_b200.engine import ROLE_MIDDLE, ROLE_WHOLE
+
+    geo = small_geo(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, ffn=1024)
+    role = ROLE_MIDDLE if role == 1 else ROLE_WHOLE
+    e = make_engine(ctx, geo, role, 0, 2, max_context=256, max_window=32, sessions=4)
+    dev = torch.device("cuda:0")
+    fpp = 2 * geo.hidden + 1
+    gen = torch.Generator(device=dev).manual_seed(9)
+    rng = np.random.default_rng(9)
+    n, q = 4, 8
+    ids = [11, 12, 13, 14]
+
+    def inputs(rows):
+        if role == ROLE_WHOLE:
+            return dict(d_tokens=torch.from_numpy(rng.integers(0, geo.vocab, rows).astype(np.int32)).to(dev))
+        rec = torch.zeros((rows, fpp), dtype=torch.float32, device=dev)
+        rec[:, :geo.hidden] = torch.randn((rows, geo.hidden), generator=gen, device=dev)
+        rec[:, 2 * geo.hidden] = 1.0
+        return dict(d_records=rec)
+
+    width = geo.vocab if role == ROLE_WHOLE else fpp
+    pos = {}
+    for b, s in enumerate(ids):  # different context lengths
+        e.open_session(s)
+        L = [9, 16, 23, 5][b]
+        out = torch.empty((L, width), device=dev)
+        e.run_window_device(s, 0, d_out=out, **inputs(L))
+        e.commit(s, L)
+        pos[s] = L
+    for rnd in range(2):
+        inp = inputs(n * q)
+        key = "d_tokens" if role == ROLE_WHOLE else "d_records"
+        want = []
+        for b, s in enumerate(ids):
+            o = torch.empty((q, width), device=dev)
+            e.run_window_device(s, pos[s], d_out=o, **{key: inp[key][b * q:(b + 1) * q].contiguous()})
+            torch.cuda.synchronize()
+            e.abort(s)
+            want.append(o)
+        got = torch.empty((n * q, width), device=dev)
+        e.run_batch_window_device(ids, [pos[s] for s in ids], q, d_out=got, **inp)
+        torch.cuda.synchronize()
+        for b in range(n):
+            # the 32-row GEMV adds each row's products in another order than the 8-row one (single-superblock units,
+            # other split-K segments), and the fp16 rounding of every layer's inputs turns such last-bit differences
+            # into ~1e-3 of the scale by the logits: a quarter of the oracle bound of these tests (2e-2)
+            w, g = want[b].cpu().numpy(), got[b * q:(b + 1) * q].cpu().numpy()
+            assert rel(g, w) < 5e-3, (rnd, b, rel(g, w))
+        for b, s in enumerate(ids):
+            keep = [8, 3, 5, 1][(b + rnd) % 4]
+            e.commit(s, keep)
+            pos[s] += keep
+    e.close()

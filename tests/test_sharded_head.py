@@ -10,8 +10,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from clusterlm_b200.sharded_head import (CHUNK, combine_kept, combine_kept_t, combine_max, merge_argmax, shard_bounds,
-                                         verify_decisions, verify_decisions_t)
+from clusterlm_b200.sharded_head import (CHUNK, combine_kept, combine_max, merge_argmax, shard_bounds, verify_decisions,
+                                         verify_decisions_t)
 
 
 def test_shard_bounds_cover_the_vocabulary_at_chunk_boundaries():
@@ -54,9 +54,19 @@ def test_tensor_decisions_equal_the_walk():
         assert (int(a), int(n)) == verify_decisions(p.tolist(), q.tolist(), u.tolist()), (p, q, u)
 
 
-def _chunk_sums(row, m):
-    """Chunk sums of exp(l - m) in double, one fixed order per chunk (a stand-in for the device chunk kernel)."""
-    return [float(np.sum(np.exp(row[c:c + CHUNK].astype(np.float64) - m))) for c in range(0, row.size, CHUNK)]
+def _chunk_stats(row):
+    """(max, double sum of exp(l - max)) of each chunk, in one fixed order per chunk (a stand-in for the device
+    chunk kernel)."""
+    out = []
+    for c in range(0, row.size, CHUNK):
+        ch = row[c:c + CHUNK]
+        m = float(max(ch.max(), np.float32(-3.4028235e38)))
+        out.append((m, float(np.sum(np.exp(ch.astype(np.float64) - m)))))
+    return out
+
+
+def _factor(m, M):
+    return float(np.exp(np.float64(np.float32(m) - np.float32(M))))
 
 
 def _rank(rank, world, port, V, rows, q):
@@ -68,27 +78,29 @@ def _rank(rank, world, port, V, rows, q):
         v0, v1 = shard_bounds(V, world)[rank]
         mine = logits[:, v0:v1]
         counts = [(b1 - b0 + CHUNK - 1) // CHUNK for b0, b1 in shard_bounds(V, world)]
-        # the maxima
+        # the maxima of the shards combine exactly in any order
         local = torch.from_numpy(mine.max(axis=1).copy())
         out = [torch.empty_like(local) for _ in range(world)]
         dist.all_gather(out, local)
-        gmax = combine_max(torch.stack(out)).numpy()
-        assert np.array_equal(gmax, logits.max(axis=1))
-        # the kept sums: chunk sums padded to the widest rank, gathered, added in column order
-        sums = np.zeros((rows, max(counts)))
+        assert np.array_equal(combine_max(torch.stack(out)).numpy(), logits.max(axis=1))
+        # the chunk statistics, padded to the widest rank, gathered, combined in column order
+        cm = np.full((rows, max(counts)), -3.0e38)
+        cs = np.zeros((rows, max(counts)))
         for i in range(rows):
-            cs = _chunk_sums(mine[i], gmax[i])
-            sums[i, :len(cs)] = cs
-        t = torch.from_numpy(sums)
-        out = [torch.empty_like(t) for _ in range(world)]
-        dist.all_gather(out, t)
-        kept = combine_kept([o.tolist() for o in out], counts)
-        assert combine_kept_t(torch.stack(out), counts).tolist() == kept
+            for c, (m, sm) in enumerate(_chunk_stats(mine[i])):
+                cm[i, c], cs[i, c] = m, sm
+        gm = [torch.empty((rows, max(counts)), dtype=torch.float64) for _ in range(world)]
+        gs = [torch.empty((rows, max(counts)), dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(gm, torch.from_numpy(cm))
+        dist.all_gather(gs, torch.from_numpy(cs))
+        got = combine_kept([g.tolist() for g in gm], [g.tolist() for g in gs], counts, _factor)
         for i in range(rows):
-            whole = 0.0
-            for c in _chunk_sums(logits[i], gmax[i]):
-                whole += c
-            assert kept[i] == whole
+            whole = _chunk_stats(logits[i])
+            M = max(m for m, _ in whole)
+            a = 0.0
+            for m, sm in whole:
+                a += sm * _factor(m, M)
+            assert got[i] == (M, a)
         q.put((rank, "ok"))
     except Exception as e:  # noqa: BLE001
         q.put((rank, repr(e)))
