@@ -109,8 +109,17 @@ __device__ __forceinline__ void prep16(const float* vals, const float* raw, int 
                                        float* ss_out, int total_cols) {
   const int k = 16 * c, sb = k / 256, o = k % 256, t = o / 64, part = (o % 64) / 32, s0 = (o % 32) / 2;
   const int ntile = p / 8, g = p % 8;
-  // fragment layout [sb][nt][s][lane] (gemv.cuh): word (s, lane) at ((sb*nt + ntile)*16 + s)*32 + lane
-  uint32_t* w = reinterpret_cast<uint32_t*>(frag + ((size_t)sb * nt + ntile) * 512 + g * 4 + t);
+  // fragment layout [sb][nt][s][lane] (gemv.cuh): word (s, lane) at ((sb*nt + ntile)*16 + s)*32 + lane; with 4 n-tiles
+  // the n-tiles are interleaved in pairs, [sb][nt / 2][s][lane][2], so that one 16-byte load reads two n-tiles
+  uint32_t* w;
+  int sstride;  // u32 words between consecutive k-steps s
+  if (nt == 4) {
+    w = reinterpret_cast<uint32_t*>(frag + (((size_t)sb * 2 + ntile / 2) * 16 * 32 + g * 4 + t) * 2 + (ntile & 1));
+    sstride = 128;
+  } else {
+    w = reinterpret_cast<uint32_t*>(frag + ((size_t)sb * nt + ntile) * 512 + g * 4 + t);
+    sstride = 64;
+  }
   float sum = 0.0f, ss = 0.0f;
   const bool live = p < q;
 #pragma unroll
@@ -119,7 +128,7 @@ __device__ __forceinline__ void prep16(const float* vals, const float* raw, int 
     sum += a + b;
     if (raw && live) ss += raw[2 * i] * raw[2 * i] + raw[2 * i + 1] * raw[2 * i + 1];
     const float sa = part ? a * hi_scale : a, sbv = part ? b * hi_scale : b;
-    w[(s0 + i) * 64 + part] =
+    w[(s0 + i) * sstride + part] =
         (uint32_t)__half_as_ushort(__float2half_rn(sa)) | ((uint32_t)__half_as_ushort(__float2half_rn(sbv)) << 16);
   }
   const int j = o / 32, half = (o % 32) / 16;

@@ -150,11 +150,22 @@ static __device__ __forceinline__ void tile_mmas(const RawQ4k& r, int t, const u
     const uint32_t a1 = hfma2u(and_or<0x000F000Fu>(w8, magic), dg8.sA, dg8.nA);
     const uint32_t a2 = hfma2u(and_or<0x00F000F0u>(w, magic), dg.sB, dg.nB);
     const uint32_t a3 = hfma2u(and_or<0x00F000F0u>(w8, magic), dg8.sB, dg8.nB);
+    if (NT >= 4) {
+      // 4 n-tiles, interleaved in pairs: one 16-byte load per pair; the chains are already independent, so one
+      // accumulator set (registers for the 32-row GEMV)
+      const uint4* xf4 = reinterpret_cast<const uint4*>(xf);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      // with 4 n-tiles the chains are already independent: one accumulator set (registers for the 32-row GEMV)
-      mma16816(acc[NT >= 4 ? 0 : (s & 1)][nt], a0, a1, a2, a3, b.x, b.y);
+      for (int pr = 0; pr < NT / 2; ++pr) {
+        const uint4 b = xf4[(pr * 16 + s) * 32 + lane];
+        mma16816(acc[0][2 * pr], a0, a1, a2, a3, b.x, b.y);
+        mma16816(acc[0][2 * pr + 1], a0, a1, a2, a3, b.z, b.w);
+      }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 b = xf[(nt * 16 + s) * 32 + lane];
+        mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
+      }
     }
   }
 }
@@ -174,10 +185,20 @@ static __device__ __forceinline__ void tile_mmas(const RawQ80& r, int t, const u
     const uint32_t a1 = hfma2u(__byte_perm(w0, 0x64646464u, 0x4342), dg8.sA, dg8.nA);
     const uint32_t a2 = hfma2u(__byte_perm(w1, 0x64646464u, 0x4140), dg.sB, dg.nB);
     const uint32_t a3 = hfma2u(__byte_perm(w1, 0x64646464u, 0x4342), dg8.sB, dg8.nB);
+    if (NT >= 4) {
+      const uint4* xf4 = reinterpret_cast<const uint4*>(xf);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 b = xf[(nt * 16 + s) * 32 + lane];
-      mma16816(acc[NT >= 4 ? 0 : (s & 1)][nt], a0, a1, a2, a3, b.x, b.y);
+      for (int pr = 0; pr < NT / 2; ++pr) {
+        const uint4 b = xf4[(pr * 16 + s) * 32 + lane];
+        mma16816(acc[0][2 * pr], a0, a1, a2, a3, b.x, b.y);
+        mma16816(acc[0][2 * pr + 1], a0, a1, a2, a3, b.z, b.w);
+      }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 b = xf[(nt * 16 + s) * 32 + lane];
+        mma16816(acc[s & 1][nt], a0, a1, a2, a3, b.x, b.y);
+      }
     }
   }
 }

@@ -414,6 +414,7 @@ __device__ __forceinline__ ChunkStats chunk_stats(const float* __restrict__ l, u
   if ((V & 3u) == 0) {  // rows start 16-byte aligned: float4 loads
     const float4* l4 = reinterpret_cast<const float4*>(l);
     float m0 = -FLT_MAX, m1 = -FLT_MAX, m2 = -FLT_MAX, m3 = -FLT_MAX;
+#pragma unroll 4
     for (uint32_t i = lo / 4 + threadIdx.x; i < hi / 4; i += kSampleThreads) {
       const float4 v = l4[i];
       m0 = fmaxf(m0, v.x);
@@ -423,6 +424,8 @@ __device__ __forceinline__ ChunkStats chunk_stats(const float* __restrict__ l, u
     }
     r.m = block_max(fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)));
     double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    // unrolled so that several iterations' loads and exps are in flight (the additions keep their order)
+#pragma unroll 4
     for (uint32_t i = lo / 4 + threadIdx.x; i < hi / 4; i += kSampleThreads) {
       const float4 v = l4[i];
       a0 += soft_term(v.x, r.m, T);
