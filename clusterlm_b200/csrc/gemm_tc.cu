@@ -8,14 +8,17 @@
 //  * A first kernel converts the window's activations (f32) to fp16 tiles already in the MMA's layout (K-major,
 //    128-byte swizzle: 8-row atoms of 1024 B, 16-byte chunk c of row r stored at chunk c ^ (r % 8)), one
 //    P x 64 tile per 64-column chunk.
-//  * Grid (row group of 128 weight rows, K split).  A CTA walks its K range in chunks of 64 columns.  Warp 9
-//    bulk-copies (cp.async.bulk, no multicast) the group's raw superblocks (8 repacked tiles, issued before
-//    griddepcontrol.wait) into a 2-slot ring and each chunk's activation tile into the chunk's stage.  For every
-//    chunk eight warps dequantise the group's 128 x 64 weights (row tile w of warp w) from the staged superblock
-//    into the stage's fp16 A tile, in the same swizzled layout.  Up to four stages keep the copies and the
-//    dequantisation ahead of the MMAs.
+//  * Grid (row group of 128 weight rows, K split).  A CTA walks its K range in chunks of KC = 128 columns (64 when
+//    two 128-column stages do not fit next to the raw ring, i.e. above 128 window rows): every stage hands the MMA
+//    warp KC / 64 swizzled 64-column A and B tiles at once, which halves the per-stage hand-offs that bound this
+//    kernel (a dequantising warp spends a fixed ~0.25 us between stages).  Warp 9 bulk-copies (cp.async.bulk, no
+//    multicast) the group's raw superblocks (8 repacked tiles, issued before griddepcontrol.wait) into a 2-slot
+//    ring and each chunk's activation tiles (contiguous in xh) into the chunk's stage.  For every chunk eight warps
+//    dequantise the group's 128 x KC weights (row tile w of warp w) from the staged superblock into the stage's fp16
+//    A tiles, in the same swizzled layout.  Up to four stages keep the copies and the dequantisation ahead of the
+//    MMAs.
 //  * Warp 8 owns the accumulator: it allocates P (rounded up to a power of two, >= 32) TMEM columns, and one of
-//    its lanes issues the four K = 16 tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = P window
+//    its lanes issues the KC / 16 K = 16 tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = P window
 //    rows, f32 accumulate in TMEM) per chunk once the stage's "full" mbarrier has the eight warps' arrivals and
 //    the activation tile's bytes, then
 //    tcgen05.commit releases the stage ("free" mbarrier) when those MMAs have read it.
@@ -183,7 +186,7 @@ __global__ void tc_xprep_kernel(const float* __restrict__ x, int q, int K, int P
   }
 }
 
-template <int QUANT>
+template <int QUANT, int KC>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* __restrict__ tiles, int sb_count,
                                                                  int tile_bytes, const uint8_t* __restrict__ xh, int q,
                                                                  int K, int P, int ksplit, int stages,
@@ -195,13 +198,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
   __shared__ uint32_t s_tmem;
   // 1024-byte aligned area (the dynamic allocation carries 1 KB of slack): [stages x (A tile, B tile)][raw slots]
   uint8_t* tc_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~(uintptr_t)1023);
-  const uint32_t btile = (uint32_t)P * 128u;
-  const uint32_t stage_bytes = kATileBytes + btile;
+  constexpr int SUB = KC / kTcKc;  // 64-column tiles per stage
+  constexpr int CPS = 256 / KC;    // stages per raw superblock
+  const uint32_t btile = (uint32_t)P * 128u * SUB;
+  const uint32_t atile = kATileBytes * SUB;
+  const uint32_t stage_bytes = atile + btile;
   const uint32_t raw_bytes = (uint32_t)kGemvWarps * (uint32_t)tile_bytes;
   uint8_t* raw_base = tc_smem + (size_t)stages * stage_bytes;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int grp = blockIdx.x, split = blockIdx.y;
-  const int chunks = K / kTcKc;
+  const int chunks = K / KC;
   const int c0 = split * chunks / ksplit, c1 = (split + 1) * chunks / ksplit;
   const int ncols = P <= 32 ? 32 : (P <= 64 ? 64 : (P <= 128 ? 128 : 256));
 
@@ -237,17 +243,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
       bool waited = false;
       // L2 lookahead: the raw ring holds two superblocks, so the superblocks after them are prefetched into L2
       // (`ahead` of them), which keeps more of the weight stream in flight than the ring's shared memory holds
-      const int sb_end = (c1 + 3) / 4;
-      int l2sb = c0 / 4 + kTcRawSlots;
+      const int sb_end = (c1 + CPS - 1) / CPS;
+      int l2sb = c0 / CPS + kTcRawSlots;
       auto l2_until = [&](int upto) {
         for (; l2sb < sb_end && l2sb < upto; ++l2sb)
           l2_prefetch_share(tiles + ((size_t)grp * sb_count + l2sb) * (size_t)raw_bytes, raw_bytes, 0, 1, raw_bytes);
       };
-      l2_until(c0 / 4 + kTcRawSlots + ahead);
+      l2_until(c0 / CPS + kTcRawSlots + ahead);
       for (int c = c0; c < c1; ++c) {
-        if (c == c0 || c % 4 == 0) {
+        if (c == c0 || c % CPS == 0) {
           if (!mbar_wait_backoff(&raw_free[rslot], rphase ^ 1u, err, 64)) break;
-          const int sb = c / 4;
+          const int sb = c / CPS;
           l2_until(sb + 1 + kTcRawSlots + ahead);
           mbar_expect_tx(&raw_full[rslot], raw_bytes);
           bulk_g2s_stream(raw_base + (size_t)rslot * raw_bytes,
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
         }
         if (!mbar_wait_backoff(&freeb[slot], phase ^ 1u, err, 64)) break;
         mbar_expect_tx(&full[slot], btile);
-        bulk_g2s(tc_smem + (size_t)slot * stage_bytes + kATileBytes, xh + (size_t)c * btile, btile, &full[slot]);
+        bulk_g2s(tc_smem + (size_t)slot * stage_bytes + atile, xh + (size_t)c * btile, btile, &full[slot]);
         if (++slot == stages) {
           slot = 0;
           phase ^= 1u;
@@ -291,11 +297,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
       for (int c = c0; c < c1; ++c) {
         mbar_wait(&full[slot], phase, err);
         tc_fence_after();
-        const uint32_t a = sbase + (uint32_t)slot * stage_bytes, b = a + kATileBytes;
+        const uint32_t a = sbase + (uint32_t)slot * stage_bytes, b = a + atile;
 #pragma unroll
-        for (int kk = 0; kk < kTcKc / 16; ++kk)
-          umma_f16(tmem, umma_desc_sw128(a + 32 * kk), umma_desc_sw128(b + 32 * kk), idesc,
-                   (c > c0 || kk > 0) ? 1u : 0u);
+        for (int sub = 0; sub < SUB; ++sub)
+#pragma unroll
+          for (int kk = 0; kk < kTcKc / 16; ++kk)
+            umma_f16(tmem, umma_desc_sw128(a + sub * kATileBytes + 32 * kk),
+                     umma_desc_sw128(b + sub * (uint32_t)P * 128u + 32 * kk), idesc,
+                     (c > c0 || sub > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&freeb[slot]);  // the stage is free once these MMAs have read it
         if (++slot == stages) {
           slot = 0;
@@ -313,25 +322,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const uint8_t* _
     int slot = 0, rslot = 0;
     uint32_t phase = 0, rphase = 0;
     for (int c = c0; c < c1; ++c) {
-      if (c == c0 || c % 4 == 0) mbar_wait(&raw_full[rslot], rphase, err);
+      if (c == c0 || c % CPS == 0) mbar_wait(&raw_full[rslot], rphase, err);
       // the slot's previous MMAs have read it (a fresh barrier passes the parity-1 wait at once)
       mbar_wait(&freeb[slot], phase ^ 1u, err);
       uint8_t* A = tc_smem + (size_t)slot * stage_bytes;
       const uint8_t* tile = raw_base + (size_t)rslot * raw_bytes + (size_t)rt * tile_bytes;
-      Dq8 r0, r8;
-      if (QUANT == CLM_QUANT_Q4_K)
-        dq_q4k(tile, c % 4, g, qq, r0, r8);
-      else
-        dq_q80(tile, c % 4, g, qq, r0, r8);
-      const int row = rt * 16 + g;
-      *reinterpret_cast<uint4*>(A + sw128_off(row, qq)) = r0.lo;
-      *reinterpret_cast<uint4*>(A + sw128_off(row, 4 + qq)) = r0.hi;
-      *reinterpret_cast<uint4*>(A + sw128_off(row + 8, qq)) = r8.lo;
-      *reinterpret_cast<uint4*>(A + sw128_off(row + 8, 4 + qq)) = r8.hi;
+#pragma unroll
+      for (int sub = 0; sub < SUB; ++sub) {  // quarter j of the superblock -> 64-column A tile `sub`
+        const int j = (c % CPS) * SUB + sub;
+        Dq8 r0, r8;
+        if (QUANT == CLM_QUANT_Q4_K)
+          dq_q4k(tile, j, g, qq, r0, r8);
+        else
+          dq_q80(tile, j, g, qq, r0, r8);
+        const int row = rt * 16 + g;
+        uint8_t* As = A + sub * kATileBytes;
+        *reinterpret_cast<uint4*>(As + sw128_off(row, qq)) = r0.lo;
+        *reinterpret_cast<uint4*>(As + sw128_off(row, 4 + qq)) = r0.hi;
+        *reinterpret_cast<uint4*>(As + sw128_off(row + 8, qq)) = r8.lo;
+        *reinterpret_cast<uint4*>(As + sw128_off(row + 8, 4 + qq)) = r8.hi;
+      }
       fence_async_smem();  // generic-proxy writes -> visible to the tensor core's async reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[slot]);
-      if (c % 4 == 3 || c == c1 - 1) {  // done with this raw superblock
+      if (c % CPS == CPS - 1 || c == c1 - 1) {  // done with this raw superblock
         if (lane == 0) mbar_arrive(&raw_free[rslot]);
         if (++rslot == kTcRawSlots) {
           rslot = 0;
@@ -392,17 +406,22 @@ int tc_l2_ahead() {
 TcPlan gemm_tc_plan(const GemvShape& s, int q, int sm_count) {
   TcPlan p;
   p.P = ((q + 15) / 16) * 16;
-  const int chunks = (int)s.cols / kTcKc;
-  // K splits: as many as keep the grid within one wave of CTAs (one per SM), at least two chunks per CTA
+  const size_t raw = (size_t)kTcRawSlots * kGemvWarps * s.tile_bytes;
+  const size_t stage64 = kATileBytes + (size_t)p.P * 128;
+  constexpr size_t kSmemMax = 227 * 1024;
+  // 128-column stages when two of them fit next to the raw ring (up to 128 window rows)
+  p.kc = 1024 + 2 * 2 * stage64 + raw <= kSmemMax ? 128 : 64;
+  const size_t stage = stage64 * (p.kc / kTcKc);
+  const int chunks = (int)s.cols / p.kc;
+  // K splits: as many as keep the grid within one wave of CTAs (one per SM), at least two chunks per CTA.  (Splits
+  // that balance a second wave, e.g. 3 for 224 row groups, measured slower: their partials cost more than the wave.)
   const int sms = sm_count > 0 ? sm_count : 148;
   int ks = (int)(s.ng < (uint32_t)sms ? sms / s.ng : 1);
   if (ks > chunks / 2) ks = chunks / 2;
   if (ks < 1) ks = 1;
   p.ksplit = ks;
-  const size_t raw = (size_t)kTcRawSlots * kGemvWarps * s.tile_bytes;
-  const size_t stage = kATileBytes + (size_t)p.P * 128;
   p.stages = kTcMaxStages;
-  while (p.stages > 2 && 1024 + p.stages * stage + raw > 227 * 1024) --p.stages;
+  while (p.stages > 2 && 1024 + p.stages * stage + raw > kSmemMax) --p.stages;
   p.smem = 1024 + (size_t)p.stages * stage + raw;
   p.part_floats = (size_t)ks * q * s.rows;
   p.xh_bytes = (size_t)p.P * s.cols * 2;
@@ -433,18 +452,18 @@ int launch_gemm_tc_tiles(const GemvShape& s, const TcPlan& p, const uint8_t* d_t
   CLM_CHECK(p.smem <= 227 * 1024, CLM_RESOURCE_EXHAUSTED, "tensor-core GEMM: shared memory");
   CLM_CHECK((reinterpret_cast<uintptr_t>(d_xh) & 15) == 0, CLM_INTERNAL, "activation tiles must be 16-byte aligned");
   CLM_CHECK(p.ksplit == 1 || d_part != nullptr, CLM_INTERNAL, "split-K partials need a buffer");
+  CLM_CHECK(p.kc == 64 || p.kc == 128, CLM_INTERNAL, "tensor-core GEMM: stage width");
   const dim3 grid(s.ng, (unsigned)p.ksplit);
   float* out = p.ksplit > 1 ? d_part : d_y;
-  const uint8_t* xh = d_xh;
-  if (s.quant == CLM_QUANT_Q4_K) {
-    CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q4_K>, p.smem));
-    CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q4_K>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err, tc_l2_ahead()));
-  } else {
-    CLM_TRY(ensure_smem(gemm_tc_kernel<CLM_QUANT_Q8_0>, p.smem));
-    CLM_TRY(launch_pdl(gemm_tc_kernel<CLM_QUANT_Q8_0>, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb,
-                       s.tile_bytes, xh, q, (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err, tc_l2_ahead()));
-  }
+  auto go = [&](auto kern) -> int {
+    CLM_TRY(ensure_smem(kern, p.smem));
+    return launch_pdl(kern, grid, dim3(kTcThreads), p.smem, st, d_tiles, (int)s.sb, s.tile_bytes, d_xh, q,
+                      (int)s.cols, p.P, p.ksplit, p.stages, out, s.rows, d_err, tc_l2_ahead());
+  };
+  if (s.quant == CLM_QUANT_Q4_K)
+    CLM_TRY(p.kc == 128 ? go(gemm_tc_kernel<CLM_QUANT_Q4_K, 128>) : go(gemm_tc_kernel<CLM_QUANT_Q4_K, 64>));
+  else
+    CLM_TRY(p.kc == 128 ? go(gemm_tc_kernel<CLM_QUANT_Q8_0, 128>) : go(gemm_tc_kernel<CLM_QUANT_Q8_0, 64>));
   if (p.ksplit > 1 && sum_splits) {
     const uint64_t n = (uint64_t)q * s.rows;
     CLM_TRY(launch_pdl(split_sum_kernel, dim3((unsigned)std::min<uint64_t>((n + 255) / 256, 4096)), dim3(256), 0, st,

@@ -9,6 +9,7 @@ struct TcPlan {
   int P = 0;              // window rows rounded up to a multiple of 16 (the MMA's N)
   int ksplit = 1;         // K splits (grid y); > 1 sums f32 partials in split order
   int stages = 0;         // (A tile, B tile) stages in shared memory
+  int kc = 64;            // columns per stage (64, or 128 when two such stages fit next to the raw ring)
   size_t smem = 0;        // dynamic shared memory of one CTA
   size_t part_floats = 0; // f32 partials needed when ksplit > 1
   size_t xh_bytes = 0;    // fp16 activation tiles (P x cols)
