@@ -1062,6 +1062,53 @@ def run_pipeline(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def window_micro(ctx, dev, args):
+    """The C3 verify window alone: an 8B-shape Q4_K engine with `--layers` decoder layers, the `--context` prompt
+    prefilled in 256-row windows, then `--warmup` untimed and `--steps` (at most 50) event-timed q = 4 windows on
+    the engine stream, each aborted after it runs.  A small command for launch lists and DRAM-traffic captures of
+    one window's kernels (the prefill's launches come first)."""
+    import numpy as np
+    import torch
+
+    from clusterlm_b200.engine import LLAMA3_8B, ROLE_WHOLE, Engine
+
+    geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
+    context = args.context
+    eng = Engine(ctx, geo, 0, geo.n_layers, ROLE_WHOLE, context + 64, PREFILL_CHUNK, 1)
+    eng.generate_weights(seed=SEED, stddev=0.02)
+    eng.prepare()
+    eng.open_session(1)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    rng = np.random.default_rng(1)
+    prompt = torch.from_numpy(rng.integers(0, geo.vocab, context).astype(np.int32)).to(dev)
+    out = torch.empty((PREFILL_CHUNK, geo.vocab), dtype=torch.float32, device=dev)
+    for off in range(0, context, PREFILL_CHUNK):
+        n = min(PREFILL_CHUNK, context - off)
+        eng.run_window_device(1, off, prompt[off:off + n], out[:n], stream.cuda_stream)
+        eng.commit(1, n)
+    toks = torch.from_numpy(rng.integers(0, geo.vocab, Q).astype(np.int32)).to(dev)
+    logits = torch.empty((Q, geo.vocab), dtype=torch.float32, device=dev)
+    times = []
+    for i in range(args.warmup + min(args.steps, 50)):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        eng.run_window_device(1, context, toks, logits, stream.cuda_stream)
+        s1.record(stream)
+        torch.cuda.synchronize(dev)
+        eng.abort(1)
+        if i >= args.warmup:
+            times.append(s0.elapsed_time(s1) / 1e3)
+    eng.close()
+    sec = statistics.median(times)
+    total_b, weight_b, kv_b = window_bytes(geo, context)
+    peak, kind = load_peaks()
+    return {"config": f"8B-shape Q4_K verify window, q={Q}, {geo.n_layers} layers + head, context {context}",
+            "ms_per_window": sec * 1e3, "windows": len(times),
+            "roofline": {"bound": "hbm", "algorithmic_bytes": total_b, "weight_bytes": weight_b, "kv_bytes": kv_b,
+                         "achieved": total_b / sec / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": total_b / sec / 1e9 / peak, "peak_kind": kind}}
+
+
 def run_micro(args):
     """One micro-benchmark alone on cuda:0 (a small command for profiler captures); prints its JSON object."""
     import torch
@@ -1088,6 +1135,8 @@ def run_micro(args):
         eng.close()
     elif args.micro == "tree":
         obj = tree_micro(ctx, dev, peak, args.context)
+    elif args.micro == "window":
+        obj = window_micro(ctx, dev, args)
     elif args.micro == "c5":
         obj = c5_micro(ctx, dev, peak)
     else:
@@ -1108,7 +1157,7 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="decoder layers of the 8B shape (profiling)")
     ap.add_argument("--inflight", type=int, default=0, help="sequences in flight with N > 1 (default N)")
     ap.add_argument("--plan", default="", help="stage plan BEGIN-END@gK,... with N > 1 (default: byte-balanced)")
-    ap.add_argument("--micro", default="", choices=["", "wide", "accept", "prefill", "tree", "c5"],
+    ap.add_argument("--micro", default="", choices=["", "wide", "accept", "prefill", "tree", "c5", "window"],
                     help="run one micro-benchmark alone and print its object (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
