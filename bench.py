@@ -691,9 +691,11 @@ def prefill_micro(eng, geo, dev, stream, context, rng):
                          "peak_kind": kind, "gemm_flops": flops}}
 
 
-# DRAM bytes (read + write) of one verify window (32 layers + head, q = 4, context 4096) from an ncu capture of
-# every kernel of one window, keyed by layer count; the capture and its command are summarised under profiles/
-WINDOW_TRAFFIC: dict = {}
+# DRAM bytes (read + write) of one verify window (q = 4, context 4096), keyed by layer count: an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum, caches not flushed between kernels) of every kernel of one window
+# of `bench.py --micro window --layers 8`; 32 layers = the head and embedding kernels + 4 x the 8 layers' kernels.
+# The capture and its command are summarised under profiles/.
+WINDOW_TRAFFIC: dict = {8: 1530851840, 32: 5100370688}
 
 
 def c1_fixture():
