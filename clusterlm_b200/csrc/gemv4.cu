@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv4_kernel(const uint8_t* __r
         if (!mbar_wait_backoff(&empty[w.slot], w.phase ^ 1u, epi.err, 128)) break;
         issue_weights(w);
         acts_when_ready(w);
-        l2_until(i + 1 + ahead);
+        if (ahead > 0) l2_until(i + 1 + ahead);  // (at 0 the cursor would prefetch the unit just issued)
       }
       // every copy of this CTA is issued: prefetch the next kernel's first bytes into L2 while this one drains
       if (EPI == EPI_ROPE_KV && epi.pf_kv) {

@@ -276,8 +276,17 @@ __device__ __forceinline__ void g4_ss_finish(const G4SsPre& pre, const XBuf& in,
   {
     float a = pre.a + pre.b;
     if (in.ss)
-      for (int c = tid / kSsRows + 2 * kStride; c < in.nss; c += kStride)
-        a += __ldcg(in.ss + (size_t)c * kSsRows + tid % kSsRows);
+      for (int c0 = tid / kSsRows + 2 * kStride; c0 < in.nss; c0 += 8 * kStride) {
+        // eight loads in flight, added in partial order
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int c = c0 + k * kStride;
+          v[k] = c < in.nss ? __ldcg(in.ss + (size_t)c * kSsRows + tid % kSsRows) : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) a += v[k];
+      }
     s_red[tid] = a;
   }
   consumer_sync();

@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kStripMaxStages], empty[kStripMaxStages], xbar[kStripSb / 2];
   __shared__ float s_scale[2][8];
+  __shared__ float s_ssp[2][256];  // row-scale partial sums: [group][thread]
   constexpr bool kSwiglu = EPI == EPI_SWIGLU_PREP;
   constexpr int kSpu = kSwiglu ? 4 : 2;  // stages per unit
   uint8_t* xfrag = smem;
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
         const int slot = j % stages;
         if (!mbar_wait_backoff(&empty[slot], ((j / stages) & 1) ^ 1u, epi.err, 128)) break;
         issue_stage(j);
-        l2_until(j + 1 + ahead);
+        if (ahead > 0) l2_until(j + 1 + ahead);  // (at 0 the cursor would prefetch the stage just issued)
       }
       // every copy of this CTA is issued: the next kernel's first bytes into L2 while this one drains
       if (EPI == EPI_ROPE_KV && epi.pf_kv) {
@@ -166,6 +167,17 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
   const int grp_of_warp = warp / kGemvWarps, w = warp % kGemvWarps, tg = threadIdx.x % 256;
   const int t = lane % 4;
   float* y = ybuf + grp_of_warp * 2 * 128;  // [16 rows][8 columns], then the up rows (SwiGLU)
+  // Row scale (folded rmsnorm) from the input's sum-of-squares partials: thread tg adds partials tg / 8 + 32 k
+  // (k ascending) of row tg % 8, all of them independent loads; the first epilogue adds the 32 threads of a row in
+  // order (for up to 32 partials the serial partial order).  Issued here, so the loads overlap the first strip,
+  // unless the partials are still being written (dataflow mode, after the epilogue's readiness wait).
+  auto ss_part = [&]() -> float {
+    float a = 0.0f;
+    if (in.ss && tg % 8 < q)
+      for (int c = tg / 8; c < in.nss; c += 32) a += __ldcg(in.ss + (size_t)c * kSsRows + tg % 8);
+    return a;
+  };
+  const float ss_pre = linked ? 0.0f : ss_part();
   bool scale_ready = false;
   uint32_t xready = 0;  // chunks of this warp's superblocks already waited for
   for (int i = grp_of_warp; i < n; i += 2) {
@@ -210,11 +222,13 @@ __global__ void __launch_bounds__(kG4Threads, 1) gemv_strip_kernel(const uint8_t
       // row scale (folded rmsnorm) from the input's sum-of-squares partials, summed in partial order
       if (epi.ss_done != nullptr && tg == 0) (void)dep_wait(epi.ss_done, epi.ss_target, epi.err);
       group_sync(grp_of_warp);
+      s_ssp[grp_of_warp][tg] = linked ? ss_part() : ss_pre;
+      group_sync(grp_of_warp);
       if (tg < 8) {
         float sc = 1.0f;
         if (in.ss && tg < q) {
           float tot = 0.0f;
-          for (int c = 0; c < in.nss; ++c) tot += __ldcg(in.ss + (size_t)c * kSsRows + tg);
+          for (int c = 0; c < 32; ++c) tot += s_ssp[grp_of_warp][tg + 8 * c];
           sc = 1.0f / sqrtf(tot / epi.ss_n + epi.eps);
         }
         s_scale[grp_of_warp][tg] = sc;
