@@ -22,8 +22,19 @@ __global__ void embed_kernel(const uint8_t* __restrict__ embd, int quant, const 
   const int p = blockIdx.x;
   const int32_t tok = tokens[p];
   float* out = h + (size_t)p * H;
+  // the token's row is staged in shared memory with 16-byte loads (one round trip), then decoded from there
+  constexpr int kRowMax = 9216;  // a Q4_K row of H <= 16384 or a Q8_0 row of H <= 8448
+  __shared__ __align__(16) uint8_t srow[kRowMax];
+  const size_t row_bytes = quant == CLM_QUANT_Q4_K ? (size_t)(H / 256) * 144 : (size_t)(H / 32) * 34;
+  const uint8_t* grow = embd + (size_t)tok * row_bytes;
+  const bool staged = row_bytes <= kRowMax && row_bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(grow) & 15) == 0;
+  if (staged) {
+    for (int i = threadIdx.x; i < (int)(row_bytes / 16); i += blockDim.x)
+      reinterpret_cast<uint4*>(srow)[i] = __ldg(reinterpret_cast<const uint4*>(grow) + i);
+    __syncthreads();
+  }
+  const uint8_t* row = staged ? srow : grow;
   if (quant == CLM_QUANT_Q4_K) {
-    const uint8_t* row = embd + (size_t)tok * (H / 256) * 144;
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
       const uint8_t* b = row + (i / 256) * 144;
       const int e = i % 256, j = e / 32, l = e % 32;
@@ -41,7 +52,6 @@ __global__ void embed_kernel(const uint8_t* __restrict__ embd, int quant, const 
       out[i] = __fsub_rn(__fmul_rn(ds, (float)qv), dm);
     }
   } else {
-    const uint8_t* row = embd + (size_t)tok * (H / 32) * 34;
     for (int i = threadIdx.x; i < H; i += blockDim.x) {
       const uint8_t* b = row + (i / 32) * 34;
       out[i] = __fmul_rn(ld_half_le(b), (float)(int8_t)b[2 + i % 32]);
