@@ -950,7 +950,7 @@ def run_pipeline(args, world, rank, local):
     geo = LLAMA3_8B if args.layers == LLAMA3_8B.n_layers else dataclasses.replace(LLAMA3_8B, n_layers=args.layers)
     context = args.context
     S = args.inflight or world
-    plan = parse_plan(args.plan, geo.n_layers) if args.plan else plan_stages(geo, world, Q, context)
+    plan = parse_plan(args.plan, geo.n_layers) if args.plan else plan_stages(geo, world, Q, context, sessions=S)
     e2e_n = args.steps  # the e2e leg runs as many rounds as the timed loop
     max_ctx = context + (args.warmup + args.steps + 8) * (Q + 1) + 64
     ctx = Context(local)

@@ -292,6 +292,7 @@ struct LlamaEngine : clm_b200_engine {
   int32_t* nxt = nullptr;
   int32_t* emitted = nullptr;
   uint32_t* count = nullptr;
+  uint32_t* relay_commit = nullptr;      // commit count of the message a tail replica relays (clm_b200_pipe_relay)
   int* bad = nullptr;
   unsigned long long* zero_counter = nullptr;
   RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
@@ -1545,6 +1546,7 @@ int llama_prepare(LlamaEngine* e) {
   CLM_TRY(e->alloc_t(&e->nxt, 1));
   CLM_TRY(e->alloc_t(&e->emitted, (size_t)W + 1));
   CLM_TRY(e->alloc_t(&e->count, 1));
+  CLM_TRY(e->alloc_t(&e->relay_commit, 1));
   CLM_TRY(e->alloc_t(&e->zero_counter, 1));
   CLM_TRY(e->alloc_t(&e->ctl, 1));
   CLM_CUDA(cudaMemset(e->ctl, 0, sizeof(RoundCtl)));
@@ -2156,6 +2158,29 @@ int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p,
 int llama_pipe_status(LlamaEngine* e, void* stream) {
   CLM_TRY(engine_enter(e));
   return e->check_bad(pick_stream(e->ctx, stream));
+}
+
+// A tail replica passes on a message of a session that another replica owns: the next inbound message goes out
+// unchanged (payload, window width, commit count, kind) on the outbound link.  Boundary records go on towards the
+// owning replica further down the chain; window tokens from a replica before this one go on towards the prefix.
+int llama_pipe_relay(LlamaEngine* e, uint32_t what, uint32_t q, void* stream) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
+  CLM_CHECK(e->pipe_in != nullptr, CLM_FAILED_PRECONDITION, "engine is not attached to a pipeline");
+  CLM_CHECK(e->spec.role == CLM_ROLE_TAIL, CLM_FAILED_PRECONDITION, "only a pipeline tail replica relays messages");
+  CLM_CHECK(q >= 1 && q <= e->spec.max_window, CLM_OUT_OF_RANGE, "window must be in [1, max_window]");
+  uint32_t bytes = 0, kind = LINK_MSG_WINDOW;
+  switch (what) {
+    case CLM_RELAY_WINDOW: bytes = e->record_bytes((int)q); break;
+    case CLM_RELAY_PREFILL: bytes = e->record_bytes((int)q); kind = LINK_MSG_PREFILL; break;
+    case CLM_RELAY_TOKENS: bytes = LlamaEngine::token_bytes((int)q); break;
+    default: return fail(CLM_INVALID_ARGUMENT, "unknown relay message");
+  }
+  CLM_CHECK(e->lout.slot_bytes >= bytes + kLinkHeaderBytes, CLM_RESOURCE_EXHAUSTED,
+            "outbound link slots are smaller than the relayed message");
+  cudaStream_t st = pick_stream(e->ctx, stream);
+  CLM_TRY(launch_link_recv(e->lin, e->bin, e->record_bytes(e->wmax()), q, nullptr, e->relay_commit, e->bad, st));
+  return launch_link_send(e->lout, e->bin, bytes, e->relay_commit, q, kind, e->bad, st);
 }
 
 int llama_spec_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,

@@ -16,6 +16,7 @@ from ._native import LINK_HANDLE_BYTES, QUANTS, call
 _vp = C.c_void_p
 
 ROLE_PREFIX, ROLE_MIDDLE, ROLE_TAIL, ROLE_WHOLE = 0, 1, 2, 3
+RELAY_WINDOW, RELAY_PREFILL, RELAY_TOKENS = 0, 1, 2  # clm_b200_pipe_relay's message kinds
 
 
 class _Geometry(C.Structure):
@@ -312,6 +313,11 @@ class Engine:
 
     def pipe_status(self, stream=None):
         call("clm_b200_pipe_status", self.h, None if stream is None else _vp(stream))
+
+    def pipe_relay(self, what: int, q: int, stream=None):
+        """Tail replica: pass the next inbound message (RELAY_WINDOW / RELAY_PREFILL records, RELAY_TOKENS) on
+        unchanged to the next stage."""
+        call("clm_b200_pipe_relay", self.h, what, q, None if stream is None else _vp(stream))
 
 
 LINK_SEND, LINK_RECV = 0, 1

@@ -10,14 +10,19 @@ round, so no stage needs a host round trip.  Several sequences are in flight so 
 
 Plans use the reference's text form (ClusterPlan::parse, coordinator.cpp:54-95): "BEGIN-END@OWNER,...", in pipeline
 order, contiguous, ending at the last layer, only the tail may be empty; an owner here is a GPU of the node
-("g3" or "3") rather than a Node index or "father".
+("g3" or "3") rather than a Node index or "father".  One extension: the plan may end in k > 1 items with the same
+range (e.g. "...,27-32@g5,32-32@g6,32-32@g7"), k tail replicas.  They are chained in the ring (... -> tail 0 ->
+tail 1 -> ... -> prefix); tail j runs the sessions s with s % k == j, and passes the other sessions' messages on
+unchanged (clm_b200_pipe_relay): boundary records towards their owner, window tokens towards the prefix.  The
+tail's LM head and MTP draft steps, which no layer split can shrink, are then shared by k GPUs.
 """
 from __future__ import annotations
 
 import dataclasses
 from typing import Callable, Sequence
 
-from .engine import LINK_RECV, LINK_SEND, ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL, Engine, LlamaGeometry, Link
+from .engine import (LINK_RECV, LINK_SEND, RELAY_PREFILL, RELAY_TOKENS, RELAY_WINDOW, ROLE_MIDDLE, ROLE_PREFIX,
+                     ROLE_TAIL, Engine, LlamaGeometry, Link)
 
 BYTES_PER_WEIGHT = {"q4_k": 144 / 256, "q8_0": 34 / 32}
 
@@ -53,14 +58,25 @@ def parse_plan(text: str, n_layers: int) -> list[StagePlan]:
         raise ValueError("a plan needs at least a prefix and a tail")
     if stages[-1].end != n_layers:
         raise ValueError(f"plan must end at layer {n_layers}")
+    k = tail_replicas(stages)
+    if k == len(stages):
+        raise ValueError("a plan needs a prefix before its tail replicas")
     expect = 0
-    for i, s in enumerate(stages):
-        if s.begin != expect or (s.end <= s.begin and i + 1 != len(stages)):
+    for i, s in enumerate(stages[:len(stages) - k + 1]):
+        if s.begin != expect or (s.end <= s.begin and i != len(stages) - k):
             raise ValueError("stage ranges must be contiguous and non-empty")
         expect = s.end
     if len({s.gpu for s in stages}) != len(stages):
         raise ValueError("every stage needs its own GPU")
     return stages
+
+
+def tail_replicas(stages: Sequence[StagePlan]) -> int:
+    """Number k of tail replicas: the trailing plan items with the last item's layer range."""
+    k = 1
+    while k < len(stages) and (stages[-1 - k].begin, stages[-1 - k].end) == (stages[-1].begin, stages[-1].end):
+        k += 1
+    return k
 
 
 def format_plan(stages: Sequence[StagePlan]) -> str:
@@ -80,15 +96,22 @@ def stage_costs(geo: LlamaGeometry, q: int, context: int) -> tuple[float, float]
     return layer, tail
 
 
-def plan_stages(geo: LlamaGeometry, world: int, q: int, context: int) -> list[StagePlan]:
-    """Contiguous layer ranges for `world` GPUs minimising the largest per-round byte stream of a stage (every
-    stage but the tail holds at least one layer)."""
+def plan_stages(geo: LlamaGeometry, world: int, q: int, context: int, tails: int | None = None,
+                sessions: int | None = None) -> list[StagePlan]:
+    """Contiguous layer ranges for `world` GPUs minimising the largest byte stream of a stage while each of
+    `sessions` sequences in flight (default `world`) runs one round (every stage but the tail holds at least one
+    layer).  The last `tails` GPUs are tail replicas with one range; the busiest runs ceil(sessions / tails) of the
+    sessions.  By default the replica count (1 .. world-1) with the smallest largest stream, the fewest on ties."""
     L = geo.n_layers
     if world < 2:
         raise ValueError("a pipeline needs at least two stages")
     if world - 1 > L:
         raise ValueError("more stages than layers")
+    if tails is not None and not 1 <= tails <= world - 1:
+        raise ValueError("tail replicas must leave at least the prefix")
+    S = sessions or world
     layer, tail = stage_costs(geo, q, context)
+    layer *= S
     INF = float("inf")
     # best[i][k]: smallest max cost placing layers [0, k) on stages [0, i) (all non-empty)
     best = [[INF] * (L + 1) for _ in range(world)]
@@ -100,21 +123,27 @@ def plan_stages(geo: LlamaGeometry, world: int, q: int, context: int) -> list[St
                 c = max(best[i - 1][j], (k - j) * layer)
                 if c < best[i][k]:
                     best[i][k], cut[i][k] = c, j
-    # the tail takes the rest (possibly nothing)
-    end, top = None, INF
-    for k in range(world - 1, L + 1):
-        c = max(best[world - 1][k], (L - k) * layer + tail)
-        if c < top:
-            top, end = c, k
+    # the tail replicas take the rest (possibly nothing); the busiest runs ceil(S / r) sessions
+    choice, top = None, INF
+    for r in ([tails] if tails else range(1, world)):
+        n = world - r  # stages before the tail replicas
+        busiest = -(-S // r)
+        for k in range(n, L + 1):
+            c = max(best[n][k], busiest * ((L - k) * layer / S + tail))
+            if choice is None or c < top - 1e-9 * top:
+                top, choice = c, (r, k)
+    r, end = choice
+    n = world - r
     bounds = [end]
-    for i in range(world - 1, 0, -1):
+    for i in range(n, 0, -1):
         bounds.append(cut[i][bounds[-1]])
-    bounds = bounds[::-1] + [L]
-    return [StagePlan(bounds[i], bounds[i + 1], i) for i in range(world)]
+    bounds = bounds[::-1]
+    return ([StagePlan(bounds[i], bounds[i + 1], i) for i in range(n)] +
+            [StagePlan(end, L, n + j) for j in range(r)])
 
 
-def role_of(rank: int, world: int) -> int:
-    return ROLE_PREFIX if rank == 0 else ROLE_TAIL if rank == world - 1 else ROLE_MIDDLE
+def role_of(rank: int, world: int, tails: int = 1) -> int:
+    return ROLE_PREFIX if rank == 0 else ROLE_TAIL if rank >= world - tails else ROLE_MIDDLE
 
 
 def link_peers(rank: int, world: int) -> tuple[int, int]:
@@ -134,14 +163,18 @@ class StagePipeline:
 
     Every rank must make the same calls (prefill chunks, rounds) for the same sessions in the same order.
     `all_gather` exchanges one picklable object per rank (torch.distributed.all_gather_object in practice);
-    `engine_factory` / `link_factory` default to the device classes (host-logic tests pass stand-ins)."""
+    `engine_factory` / `link_factory` default to the device classes (host-logic tests pass stand-ins).
+    With tail replicas (see the module docstring) a tail rank runs its own sessions and relays the others'."""
 
     def __init__(self, ctx, geo: LlamaGeometry, plan: Sequence[StagePlan], rank: int, max_context: int,
                  sessions: int, all_gather: Callable[[object], list], max_window: int = 16, slots: int = 0,
                  timeout_s: float = 30.0, weight_seed: int = 0, stddev: float = 0.02,
                  engine_factory=Engine, link_factory=Link):
         self.rank, self.world = rank, len(plan)
-        self.role = role_of(rank, self.world)
+        self.tails = tail_replicas(plan)
+        self.role = role_of(rank, self.world, self.tails)
+        # this rank's place among the tail replicas (0 .. tails-1), or None
+        self.tail_index = rank - (self.world - self.tails) if self.role == ROLE_TAIL else None
         self.max_window = max_window
         self.ctx = ctx
         st = plan[rank]
@@ -153,8 +186,10 @@ class StagePipeline:
         tok = (max_window + 1) * 4
         # a slot per sequence in flight (plus one), so no sender ever waits on a credit in steady state
         slots = slots or sessions + 1
+        # only the last stage sends window tokens alone; a tail replica before it also relays records
+        last = rank == self.world - 1
         self.link_in = link_factory(ctx, LINK_RECV, slots, tok if self.role == ROLE_PREFIX else rec, timeout_s)
-        self.link_out = link_factory(ctx, LINK_SEND, slots, tok if self.role == ROLE_TAIL else rec, timeout_s)
+        self.link_out = link_factory(ctx, LINK_SEND, slots, tok if last else rec, timeout_s)
         gathered = all_gather((self.link_in.export(), self.link_out.export()))
         peer_in, peer_out = wire(rank, self.world, gathered)
         self.link_in.connect(peer_in)
@@ -165,26 +200,51 @@ class StagePipeline:
     def is_tail(self) -> bool:
         return self.role == ROLE_TAIL
 
+    def owner(self, session: int) -> int:
+        """The tail replica (0 .. tails-1) that runs `session`'s head, acceptance and drafts."""
+        return session % self.tails
+
+    def _place(self, session: int) -> int:
+        """-1: a tail replica before the session's owner, 0: its owner, 1: after it (not a tail: 0)."""
+        if self.tail_index is None:
+            return 0
+        o = self.owner(session)
+        return (self.tail_index > o) - (self.tail_index < o)
+
     def open_session(self, session: int):
         self.engine.open_session(session)
 
     def prefill(self, session: int, prompt: Sequence[int], stream=None) -> int:
         """Runs the prompt through this stage in chunks of max_window; returns the last chunk's final row."""
         n = len(prompt)
+        place = self._place(session)
         off = 0
         while off < n:
             q = min(self.max_window, n - off)
-            self.engine.pipe_prefill(session, q, prompt[off:off + q] if self.role == ROLE_PREFIX else None, stream)
+            if place < 0:
+                self.engine.pipe_relay(RELAY_PREFILL, q, stream)
+            elif place == 0:
+                self.engine.pipe_prefill(session, q, prompt[off:off + q] if self.role == ROLE_PREFIX else None,
+                                         stream)
             off += q
         return (n - 1) % self.max_window
 
     def begin(self, session: int, row: int, q: int, temperature: float = 0.0, seed: int = 0, stream=None):
         if self.is_tail:
-            self.engine.pipe_begin(session, row, q, temperature, seed, stream)
+            place = self._place(session)
+            if place == 0:
+                self.engine.pipe_begin(session, row, q, temperature, seed, stream)
+            elif place > 0:
+                self.engine.pipe_relay(RELAY_TOKENS, q, stream)
 
     def round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None, d_count=None,
               stream=None):
-        self.engine.pipe_round(session, q, temperature, seed, d_tokens, d_count, stream)
+        """One round of `session` on this stage; only the owning tail writes d_tokens / d_count."""
+        place = self._place(session)
+        if place == 0:
+            self.engine.pipe_round(session, q, temperature, seed, d_tokens, d_count, stream)
+        else:
+            self.engine.pipe_relay(RELAY_WINDOW if place < 0 else RELAY_TOKENS, q, stream)
 
     def status(self, stream=None):
         self.engine.pipe_status(stream)

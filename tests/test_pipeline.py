@@ -6,9 +6,10 @@ import socket
 
 import pytest
 
-from clusterlm_b200.engine import LLAMA3_8B, LLAMA3_70B, ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL, LlamaGeometry
+from clusterlm_b200.engine import (LLAMA3_8B, LLAMA3_70B, RELAY_PREFILL, RELAY_TOKENS, RELAY_WINDOW, ROLE_MIDDLE,
+                                   ROLE_PREFIX, ROLE_TAIL, LlamaGeometry)
 from clusterlm_b200.pipeline import (StagePipeline, StagePlan, format_plan, link_peers, parse_plan, plan_stages,
-                                     role_of, stage_costs, wire)
+                                     role_of, stage_costs, tail_replicas, wire)
 
 
 def test_parse_plan_accepts_reference_form():
@@ -17,6 +18,10 @@ def test_parse_plan_accepts_reference_form():
     assert format_plan(st) == "0-10@g0,10-20@g1,20-32@g2"
     # only the tail may be empty (ClusterPlan::validate)
     assert parse_plan("0-32@g0,32-32@g1", 32)[1] == StagePlan(32, 32, 1)
+    # tail replicas: trailing items with one range
+    st = parse_plan("0-8@g0,8-20@g1,20-32@g2,20-32@g3,20-32@g4", 32)
+    assert tail_replicas(st) == 3 and tail_replicas(parse_plan("0-8@g0,8-32@g1", 32)) == 1
+    assert tail_replicas(parse_plan("0-32@g0,32-32@g1,32-32@g2", 32)) == 2
 
 
 @pytest.mark.parametrize("text, msg", [
@@ -28,44 +33,75 @@ def test_parse_plan_accepts_reference_form():
     ("0-x@g0,10-32@g1", "bad layer range"),
     ("0-10@father,10-32@g1", "bad owner"),
     ("0-10@g1,10-32@g1", "own GPU"),
+    ("32-32@g0,32-32@g1", "prefix before its tail replicas"),
+    ("0-10@g0,10-20@g1,32-32@g2,32-32@g3", "contiguous"),
+    ("0-10@g0,10-10@g1,10-32@g2,10-32@g3", "contiguous"),
 ])
 def test_parse_plan_rejects(text, msg):
     with pytest.raises(ValueError, match=msg):
         parse_plan(text, 32)
 
 
-@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def _stage_loads(plan, geo, q, ctx, sessions):
+    """Bytes each stage streams while every session runs one round (replicas: their busiest share)."""
+    layer, tail = stage_costs(geo, q, ctx)
+    r = tail_replicas(plan)
+    n = len(plan) - r
+    loads = [sessions * (s.end - s.begin) * layer for s in plan[:n]]
+    return loads + [-(-sessions // r) * ((s.end - s.begin) * layer + tail) for s in plan[n:]]
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 5, 8])
 def test_plan_stages_balances_bytes(world):
     geo, q, ctx = LLAMA3_8B, 4, 4096
     plan = plan_stages(geo, world, q, ctx)
-    assert len(plan) == world
+    assert len(plan) == world and [s.gpu for s in plan] == list(range(world))
+    r = tail_replicas(plan)
+    n = world - r
     assert plan[0].begin == 0 and plan[-1].end == geo.n_layers
-    assert all(a.end == b.begin for a, b in zip(plan, plan[1:]))
-    assert all(s.end > s.begin for s in plan[:-1])
-    layer, tail = stage_costs(geo, q, ctx)
-    costs = [(s.end - s.begin) * layer + (tail if i == world - 1 else 0) for i, s in enumerate(plan)]
-    # optimal: no single-layer move between neighbours lowers the maximum
+    assert all(a.end == b.begin for a, b in zip(plan[:n], plan[1:n + 1]))
+    assert all(s.end > s.begin for s in plan[:n])
+    assert all((s.begin, s.end) == (plan[-1].begin, plan[-1].end) for s in plan[n:])
+    layer, _ = stage_costs(geo, q, ctx)
+    costs = _stage_loads(plan, geo, q, ctx, world)
     top = max(costs)
-    for i in range(world - 1):
+    # no other replica count does better (each count's own split is optimal among contiguous splits)
+    for rr in range(1, world):
+        assert max(_stage_loads(plan_stages(geo, world, q, ctx, tails=rr), geo, q, ctx, world)) >= top - 1e-3
+    # optimal for its replica count: no single-layer move between neighbouring stages lowers the maximum
+    sizes = [s.end - s.begin for s in plan[:n]] + [plan[-1].end - plan[-1].begin]
+    for i in range(n):
         for d in (-1, 1):
-            c = list(costs)
-            c[i] += d * layer
-            c[i + 1] -= d * layer
-            n_i = plan[i].end - plan[i].begin + d
-            if n_i >= 1 and (plan[i + 1].end - plan[i + 1].begin - d) >= (0 if i + 1 == world - 1 else 1):
-                assert max(c) >= top - 1e-6
-    # the tail carries the head and the MTP drafts, so it gets fewer layers than the prefix
-    assert plan[-1].end - plan[-1].begin < plan[0].end - plan[0].begin
+            sz = list(sizes)
+            sz[i] += d
+            sz[i + 1] -= d
+            if min(sz[:n]) < 1 or sz[n] < 0:
+                continue
+            bounds = [0]
+            for x in sz[:n]:
+                bounds.append(bounds[-1] + x)
+            moved = [StagePlan(bounds[j], bounds[j + 1], j) for j in range(n)]
+            moved += [StagePlan(bounds[n], geo.n_layers, j) for j in range(n, world)]
+            assert max(_stage_loads(moved, geo, q, ctx, world)) >= top - 1e-3
+    if r == 1:
+        # the tail carries the head and the MTP drafts, so it gets fewer layers than the prefix
+        assert plan[-1].end - plan[-1].begin < plan[0].end - plan[0].begin
+    # 2 and 4 GPUs keep a single tail; 8 GPUs share the tail's head and drafts among replicas
+    assert (r == 1) if world in (2, 4) else True
+    if world == 8:
+        assert r > 1 and top < 0.6 * max(_stage_loads(plan_stages(geo, 8, q, ctx, tails=1), geo, q, ctx, 8))
 
 
 def test_plan_stages_70b_eight_gpus():
     plan = plan_stages(LLAMA3_70B, 8, 8, 8192)
     assert [s.gpu for s in plan] == list(range(8))
-    assert sum(s.end - s.begin for s in plan) == 80
+    n = len(plan) - tail_replicas(plan)
+    assert sum(s.end - s.begin for s in plan[:n]) + plan[-1].end - plan[-1].begin == 80
 
 
 def test_roles_and_ring():
     assert [role_of(r, 4) for r in range(4)] == [ROLE_PREFIX, ROLE_MIDDLE, ROLE_MIDDLE, ROLE_TAIL]
+    assert [role_of(r, 4, 2) for r in range(4)] == [ROLE_PREFIX, ROLE_MIDDLE, ROLE_TAIL, ROLE_TAIL]
     assert [link_peers(r, 3) for r in range(3)] == [(2, 1), (0, 2), (1, 0)]
     g = [(b"in0", b"out0"), (b"in1", b"out1"), (b"in2", b"out2")]
     # rank r's receiving end maps the sender's output end; its sending end maps the receiver's input end
@@ -117,6 +153,9 @@ class FakeEngine:
     def pipe_round(self, s, q, T, seed, d_tokens, d_count, stream):
         self.log.append(("round", s, q))
 
+    def pipe_relay(self, what, q, stream):
+        self.log.append(("relay", what, q))
+
     def pipe_status(self, stream):
         self.log.append(("status",))
 
@@ -138,14 +177,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, plan_text, out):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         geo = LlamaGeometry(6, 256, 4, 2, 128, 512, 512)
-        plan = plan_stages(geo, world, 4, 64)
+        plan = parse_plan(plan_text, geo.n_layers) if plan_text else plan_stages(geo, world, 4, 64)
 
         def gather(obj):
             res = [None] * world
@@ -165,21 +204,74 @@ def _worker(rank, world, port, out):
                 p.round(s, 4)
         p.close(dist.barrier)
         out[rank] = (ctx.log, p.link_in.peer, p.link_out.peer, p.link_in.closed and p.link_out.closed, row,
-                     p.link_in.export(), p.link_out.export())
+                     p.link_in.export(), p.link_out.export(), p.tail_index)
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_pipeline_ranks_gloo(world):
+def _replay(logs, world):
+    """Replays every rank's calls over FIFO links (rank r sends to rank r+1, the last to the prefix) and returns the
+    largest number of messages any link held.  A message is (kind, session); every call consumes what its role
+    receives and produces what it sends; a relay passes the message on unchanged.  Fails on a message of the wrong
+    kind or session, on a call that could never run (deadlock) or on messages left over beyond the next windows
+    of sessions 1 and 2."""
+    relay_kind = {RELAY_WINDOW: "rec", RELAY_PREFILL: "pre", RELAY_TOKENS: "tok"}
+    ops = []
+    for r in range(world):
+        role = logs[r][0][0][3]
+        seq = []
+        for e in logs[r][0]:
+            if e[0] == "prefill":
+                seq.append(("pre" if role != ROLE_PREFIX else None, ("pre", e[1]) if role != ROLE_TAIL else None, e[1]))
+            elif e[0] == "begin":
+                seq.append((None, ("tok", e[1]), e[1]))
+            elif e[0] == "round":
+                want = "tok" if role == ROLE_PREFIX else "rec"
+                seq.append((want, ("tok", e[1]) if role == ROLE_TAIL else ("rec", e[1]), e[1]))
+            elif e[0] == "relay":
+                seq.append((relay_kind[e[1]], "pass", None))
+        ops.append(seq)
+    inbox = [[] for _ in range(world)]
+    at = [0] * world
+    peak = 0
+    while any(at[r] < len(ops[r]) for r in range(world)):
+        moved = False
+        for r in range(world):
+            if at[r] == len(ops[r]):
+                continue
+            want, send, sess = ops[r][at[r]]
+            msg = None
+            if want is not None:
+                if not inbox[r]:
+                    continue
+                msg = inbox[r].pop(0)
+                assert msg[0] == want, f"rank {r} call {at[r]} wanted {want}, got {msg}"
+                assert sess is None or msg[1] == sess, f"rank {r} call {at[r]}: session {sess}, message {msg}"
+            if send == "pass":
+                send = msg
+            if send is not None:
+                inbox[(r + 1) % world].append(send)
+                peak = max(peak, len(inbox[(r + 1) % world]))
+            at[r] += 1
+            moved = True
+        assert moved, f"deadlock: calls done {at} of {[len(o) for o in ops]}, inboxes {inbox}"
+    # only the next windows the last rounds drafted wait at the prefix, one per session in round order
+    assert inbox[0] == [("tok", 1), ("tok", 2)] and all(not b for b in inbox[1:]), f"messages left over: {inbox}"
+    return peak
+
+
+@pytest.mark.parametrize("world, plan_text", [(2, None), (3, None), (4, "0-3@g0,3-5@g1,5-6@g2,5-6@g3"),
+                                              (4, "0-4@g0,4-6@g1,6-6@g2,6-6@g3"), (3, "0-6@g0,6-6@g1,6-6@g2")])
+def test_pipeline_ranks_gloo(world, plan_text):
     import torch.multiprocessing as mp
 
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), plan_text, out), nprocs=world, join=True)
     logs = {r: out[r] for r in range(world)}
+    tails = 1 if plan_text is None else tail_replicas(parse_plan(plan_text, 6))
     for r in range(world):
-        log, peer_in, peer_out, closed, row, own_in, own_out = logs[r]
+        log, peer_in, peer_out, closed, row, own_in, own_out, tail_index = logs[r]
         src, dst = (r - 1) % world, (r + 1) % world
         # ring wiring: input from the previous stage's sending end, output to the next stage's receiving end
         assert peer_in.startswith(f"r{src}-send".encode()) and peer_out.startswith(f"r{dst}-recv".encode())
@@ -189,23 +281,35 @@ def test_pipeline_ranks_gloo(world):
         assert closed
         assert row == (37 - 1) % 16
         kinds = [e[0] for e in log]
-        role = role_of(r, world)
+        role = role_of(r, world, tails)
         assert kinds[:4] == ["create", "weights", "prepare", "attach"]
         assert log[0][3] == role
+        assert tail_index == (r - (world - tails) if role == ROLE_TAIL else None)
+        # a tail replica runs the sessions s with s % tails == its index and relays the others'
+        own = {1, 2} if role != ROLE_TAIL else {s for s in (1, 2) if s % tails == tail_index}
         prefills = [e for e in log if e[0] == "prefill"]
         # chunks of max_window: 16, 16, 5 per session; only the prefix passes tokens
-        assert [e[2] for e in prefills] == [16, 16, 5, 16, 16, 5]
+        assert [e[2] for e in prefills] == [16, 16, 5] * len(own)
+        assert {e[1] for e in prefills} == own
         assert all((e[3] is not None) == (role == ROLE_PREFIX) for e in prefills)
         if role == ROLE_PREFIX:
             assert prefills[0][3] == list(range(16)) and prefills[2][3] == list(range(32, 37))
         begins = [e for e in log if e[0] == "begin"]
-        assert len(begins) == (2 if role == ROLE_TAIL else 0)
-        assert [e[1] for e in log if e[0] == "round"] == [1, 2] * 3
+        assert [e[1] for e in begins] == (sorted(own) if role == ROLE_TAIL else [])
+        assert [e[1] for e in log if e[0] == "round"] == [s for s in [1, 2] * 3 if s in own]
+        relays = [e for e in log if e[0] == "relay"]
+        if role != ROLE_TAIL:
+            assert not relays
         # close protocol: drain this stage, wait for every rank, then release
         assert kinds[-2:] == ["sync", "close"]
-    # the same prefill / round sequence on every rank
-    seqs = [[(e[0], e[1], e[2]) for e in logs[r][0] if e[0] in ("prefill", "round")] for r in range(world)]
+    # the same prefill / round sequence on every rank that is not a tail replica
+    seqs = [[(e[0], e[1], e[2]) for e in logs[r][0] if e[0] in ("prefill", "round")]
+            for r in range(world - tails)]
     assert all(s == seqs[0] for s in seqs)
-    # the tail -> prefix link carries window tokens, the others boundary records
+    # every message reaches the stage that expects it, in order, within the link's slots (sessions + 1)
+    assert _replay(logs, world) <= 3
+    # the last stage -> prefix link carries window tokens, a tail replica before it also relays records
     assert int(logs[world - 1][6].split(b"-")[3]) == (16 + 1) * 4
     assert int(logs[0][6].split(b"-")[3]) == 16 * (2 * 256 + 1) * 4
+    for r in range(world - tails, world - 1):
+        assert int(logs[r][6].split(b"-")[3]) == 16 * (2 * 256 + 1) * 4

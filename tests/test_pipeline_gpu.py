@@ -93,8 +93,10 @@ def _pipe_worker(rank, world, port, plan_text, temperature, seed, out):
                 p.round(s + 1, Q, temperature, seed, toks[r, s], cnt[r, s])
         p.status()
         if p.is_tail:
+            # a tail replica writes the tokens of its own sessions only
             t, c = toks.cpu().numpy(), cnt.cpu().numpy()
-            out["tail"] = {s + 1: [list(t[r, s, :c[r, s]]) for r in range(ROUNDS)] for s in range(SESSIONS)}
+            out[f"tail{rank}"] = {s + 1: [list(t[r, s, :c[r, s]]) for r in range(ROUNDS)] for s in range(SESSIONS)
+                                  if p.owner(s + 1) == p.tail_index}
         p.close(dist.barrier)
         ctx.close()
         out[rank] = "ok"
@@ -112,11 +114,39 @@ def test_two_stage_pipeline_equals_whole_model(ctx, temperature, seed):
     out = mgr.dict()
     mp.spawn(_pipe_worker, args=(2, _free_port(), "0-3@g0,3-4@g1", temperature, seed, out), nprocs=2, join=True)
     assert out[0] == "ok" and out[1] == "ok"
-    got = out["tail"]
+    got = out["tail1"]
     for s in want:
         assert got[s] == want[s], f"session {s}"
     # every round emits 1..q tokens
     assert all(1 <= len(r) <= Q for s in got for r in got[s])
+
+
+@pytest.mark.parametrize("plan_text, temperature, seed", [("0-2@g0,2-3@g1,3-4@g2,3-4@g3", 1.0, 5),
+                                                          ("0-4@g0,4-4@g1,4-4@g2", 0.0, 0)])
+def test_tail_replicas_equal_whole_model(ctx, plan_text, temperature, seed):
+    """Tail replicas (clm_b200_pipe_relay): each tail GPU runs the sessions s with s % replicas == its index and
+    passes the others' records and tokens on; every session's tokens equal the whole model's."""
+    import torch
+
+    from clusterlm_b200.pipeline import parse_plan, tail_replicas
+
+    world = len(plan_text.split(","))
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    want = _whole_model_tokens(ctx, temperature, seed)
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_pipe_worker, args=(world, _free_port(), plan_text, temperature, seed, out), nprocs=world, join=True)
+    assert all(out[r] == "ok" for r in range(world))
+    k = tail_replicas(parse_plan(plan_text, GEO["n_layers"]))
+    got = {}
+    for r in range(world - k, world):
+        mine = out[f"tail{r}"]
+        assert set(mine) == {s for s in want if s % k == r - (world - k)}
+        got.update(mine)
+    assert got == want
 
 
 def _timeout_worker(rank, world, port, out):
