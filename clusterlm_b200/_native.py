@@ -98,7 +98,7 @@ _SIGS = {
     "clm_b200_pipe_begin": (_i, [_vp, _u64, _u32, _vp, _vp]),
     "clm_b200_pipe_round": (_i, [_vp, _u64, _vp, _vp, _vp, _vp]),
     "clm_b200_pipe_status": (_i, [_vp, _vp]),
-    "clm_b200_pipe_relay": (_i, [_vp, _u32, _u32, _vp]),
+    "clm_b200_pipe_attach_session": (_i, [_vp, _u64, _vp, _vp]),
 }
 LINK_HANDLE_BYTES = 128  # CLM_B200_LINK_HANDLE_BYTES
 

@@ -63,6 +63,8 @@ struct Session {
   std::map<int, FlowPhase*> flow_phases;  // dataflow window kernel phase tables by q (device arrays)
   int32_t* d_win = nullptr;    // pipeline tail: this session's current window tokens [W + 1]
   float* d_dprobs = nullptr;   // pipeline tail: draft distributions of the current window [W][V]
+  bool own_links = false;      // pipeline: the session's messages use lin / lout below (clm_b200_pipe_attach_session)
+  LinkDev lin, lout;
 };
 
 // Zeroes the dataflow counters of a window chain before its first linked launch (after the previous window ended).
@@ -292,7 +294,6 @@ struct LlamaEngine : clm_b200_engine {
   int32_t* nxt = nullptr;
   int32_t* emitted = nullptr;
   uint32_t* count = nullptr;
-  uint32_t* relay_commit = nullptr;      // commit count of the message a tail replica relays (clm_b200_pipe_relay)
   int* bad = nullptr;
   unsigned long long* zero_counter = nullptr;
   RoundCtl* ctl = nullptr;               // temperature / seed of the current round (device)
@@ -944,34 +945,39 @@ struct LlamaEngine : clm_b200_engine {
   uint32_t record_bytes(int q) const { return (uint32_t)(((size_t)q * floats_per_position() * 4 + 15) / 16 * 16); }
   static uint32_t token_bytes(int q) { return (uint32_t)((q * 4 + 15) / 16 * 16); }
 
+  // The links of session s's messages: its own (clm_b200_pipe_attach_session) or the engine's.
+  const LinkDev& link_in(const Session& s) const { return s.own_links ? s.lin : lin; }
+  const LinkDev& link_out(const Session& s) const { return s.own_links ? s.lout : lout; }
+
   // One round of session s on this stage (see clm_b200_pipe_round).
   int enqueue_pipe_round(Session& s, int q, bool stochastic, cudaStream_t st) {
     long long* pos = &s.d_state->pos;
     unsigned* cin = &s.d_state->commit_in;
+    const LinkDev &li = link_in(s), &lo = link_out(s);
     if (spec.role == CLM_ROLE_PREFIX) {
-      CLM_TRY(launch_link_recv(lin, win, (uint32_t)((wmax() + 1) * 4), (uint32_t)q, pos, cin, bad, st));
+      CLM_TRY(launch_link_recv(li, win, (uint32_t)((wmax() + 1) * 4), (uint32_t)q, pos, cin, bad, st));
     } else {
       // the tail committed its own previous round at acceptance
-      CLM_TRY(launch_link_recv(lin, bin, record_bytes(wmax()), (uint32_t)q,
+      CLM_TRY(launch_link_recv(li, bin, record_bytes(wmax()), (uint32_t)q,
                                spec.role == CLM_ROLE_TAIL ? nullptr : pos, cin, bad, st));
     }
     if (spec.role != CLM_ROLE_TAIL) {
       CLM_TRY(enqueue_window(s, q, win, st));
-      return launch_link_send(lout, bout, record_bytes(q), cin, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
+      return launch_link_send(lo, bout, record_bytes(q), cin, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
     }
     CLM_TRY(enqueue_window(s, q, s.d_win, st));
     CLM_TRY(enqueue_accept(s, q, stochastic, s.d_win, s.d_dprobs, st));
     CLM_TRY(enqueue_drafts(s, q, stochastic, s.d_win, s.d_dprobs, st));
-    return launch_link_send(lout, s.d_win, token_bytes(q), count, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
+    return launch_link_send(lo, s.d_win, token_bytes(q), count, (uint32_t)q, LINK_MSG_WINDOW, bad, st);
   }
 
   // One prompt chunk of session s on this stage, committed at once (the prefix's tokens are already in win).
   int enqueue_pipe_prefill(Session& s, int q, cudaStream_t st) {
     if (spec.role != CLM_ROLE_PREFIX)
-      CLM_TRY(launch_link_recv(lin, bin, record_bytes(wmax()), (uint32_t)q, nullptr, nullptr, bad, st));
+      CLM_TRY(launch_link_recv(link_in(s), bin, record_bytes(wmax()), (uint32_t)q, nullptr, nullptr, bad, st));
     CLM_TRY(enqueue_window(s, q, win, st));
     if (spec.role != CLM_ROLE_TAIL)
-      CLM_TRY(launch_link_send(lout, bout, record_bytes(q), nullptr, (uint32_t)q, LINK_MSG_PREFILL, bad, st));
+      CLM_TRY(launch_link_send(link_out(s), bout, record_bytes(q), nullptr, (uint32_t)q, LINK_MSG_PREFILL, bad, st));
     return launch_pdl(pos_advance_kernel, dim3(1), dim3(32), 0, st, s.d_state, q);
   }
 
@@ -1546,7 +1552,6 @@ int llama_prepare(LlamaEngine* e) {
   CLM_TRY(e->alloc_t(&e->nxt, 1));
   CLM_TRY(e->alloc_t(&e->emitted, (size_t)W + 1));
   CLM_TRY(e->alloc_t(&e->count, 1));
-  CLM_TRY(e->alloc_t(&e->relay_commit, 1));
   CLM_TRY(e->alloc_t(&e->zero_counter, 1));
   CLM_TRY(e->alloc_t(&e->ctl, 1));
   CLM_CUDA(cudaMemset(e->ctl, 0, sizeof(RoundCtl)));
@@ -2062,6 +2067,17 @@ int llama_spec_round_device(LlamaEngine* e, uint64_t id, const clm_b200_spec_par
 
 // ---- stage pipeline ------------------------------------------------------------------------------
 
+// Device views of a stage's input and output links, checked against the largest message this stage exchanges.
+static int pipe_links(const LlamaEngine* e, clm_b200_link* in, clm_b200_link* out, LinkDev* li, LinkDev* lo) {
+  CLM_TRY(link_dev(in, false, li));
+  CLM_TRY(link_dev(out, true, lo));
+  const uint32_t need_in = e->spec.role == CLM_ROLE_PREFIX ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
+  const uint32_t need_out = e->spec.role == CLM_ROLE_TAIL ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
+  CLM_CHECK(li->slot_bytes >= need_in + kLinkHeaderBytes && lo->slot_bytes >= need_out + kLinkHeaderBytes,
+            CLM_RESOURCE_EXHAUSTED, "link slots are smaller than a max_window message");
+  return CLM_OK;
+}
+
 int llama_pipe_attach(LlamaEngine* e, clm_b200_link* in, clm_b200_link* out) {
   CLM_TRY(engine_enter(e));
   CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
@@ -2069,16 +2085,30 @@ int llama_pipe_attach(LlamaEngine* e, clm_b200_link* in, clm_b200_link* out) {
   CLM_CHECK(e->spec.role != CLM_ROLE_TAIL || e->has_mtp, CLM_FAILED_PRECONDITION,
             "a pipeline tail drafts the next window: it needs an MTP head");
   LinkDev li, lo;
-  CLM_TRY(link_dev(in, false, &li));
-  CLM_TRY(link_dev(out, true, &lo));
-  const uint32_t need_in = e->spec.role == CLM_ROLE_PREFIX ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
-  const uint32_t need_out = e->spec.role == CLM_ROLE_TAIL ? LlamaEngine::token_bytes(e->wmax()) : e->record_bytes(e->wmax());
-  CLM_CHECK(li.slot_bytes >= need_in + kLinkHeaderBytes && lo.slot_bytes >= need_out + kLinkHeaderBytes,
-            CLM_RESOURCE_EXHAUSTED, "link slots are smaller than a max_window message");
+  CLM_TRY(pipe_links(e, in, out, &li, &lo));
   e->pipe_in = in;
   e->pipe_out = out;
   e->lin = li;
   e->lout = lo;
+  return CLM_OK;
+}
+
+int llama_pipe_attach_session(LlamaEngine* e, uint64_t id, clm_b200_link* in, clm_b200_link* out) {
+  CLM_TRY(engine_enter(e));
+  CLM_CHECK(e->pipe_in != nullptr, CLM_FAILED_PRECONDITION, "engine is not attached to a pipeline");
+  Session* s = find_session(e, id);
+  CLM_CHECK(s != nullptr, CLM_NOT_FOUND, "session not open");
+  CLM_CHECK(s->outstanding == 0, CLM_FAILED_PRECONDITION, "a window is outstanding");
+  LinkDev li, lo;
+  CLM_TRY(pipe_links(e, in ? in : e->pipe_in, out ? out : e->pipe_out, &li, &lo));
+  // the session's captured rounds hold the links they were captured with
+  for (auto& kv : s->graphs) cudaGraphExecDestroy(kv.second);
+  s->graphs.clear();
+  s->seen.clear();
+  s->launches.clear();
+  s->lin = li;
+  s->lout = lo;
+  s->own_links = true;
   return CLM_OK;
 }
 
@@ -2127,8 +2157,8 @@ int llama_pipe_begin(LlamaEngine* e, uint64_t id, uint32_t row, const clm_b200_s
                           e->zero_counter, nullptr, e->tprobs, e->nxt, st));
   CLM_TRY(launch_pdl(set_next_kernel, dim3(1), dim3(32), 0, st, s->d_state, (const int32_t*)e->nxt));
   CLM_TRY(e->enqueue_drafts(*s, (int)p->q, stochastic, s->d_win, s->d_dprobs, st));
-  return launch_link_send(e->lout, s->d_win, LlamaEngine::token_bytes((int)p->q), nullptr, p->q, LINK_MSG_WINDOW,
-                          e->bad, st);
+  return launch_link_send(e->link_out(*s), s->d_win, LlamaEngine::token_bytes((int)p->q), nullptr, p->q,
+                          LINK_MSG_WINDOW, e->bad, st);
 }
 
 int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens, uint32_t* d_count,
@@ -2158,29 +2188,6 @@ int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p,
 int llama_pipe_status(LlamaEngine* e, void* stream) {
   CLM_TRY(engine_enter(e));
   return e->check_bad(pick_stream(e->ctx, stream));
-}
-
-// A tail replica passes on a message of a session that another replica owns: the next inbound message goes out
-// unchanged (payload, window width, commit count, kind) on the outbound link.  Boundary records go on towards the
-// owning replica further down the chain; window tokens from a replica before this one go on towards the prefix.
-int llama_pipe_relay(LlamaEngine* e, uint32_t what, uint32_t q, void* stream) {
-  CLM_TRY(engine_enter(e));
-  CLM_CHECK(e->prepared, CLM_FAILED_PRECONDITION, "engine not prepared");
-  CLM_CHECK(e->pipe_in != nullptr, CLM_FAILED_PRECONDITION, "engine is not attached to a pipeline");
-  CLM_CHECK(e->spec.role == CLM_ROLE_TAIL, CLM_FAILED_PRECONDITION, "only a pipeline tail replica relays messages");
-  CLM_CHECK(q >= 1 && q <= e->spec.max_window, CLM_OUT_OF_RANGE, "window must be in [1, max_window]");
-  uint32_t bytes = 0, kind = LINK_MSG_WINDOW;
-  switch (what) {
-    case CLM_RELAY_WINDOW: bytes = e->record_bytes((int)q); break;
-    case CLM_RELAY_PREFILL: bytes = e->record_bytes((int)q); kind = LINK_MSG_PREFILL; break;
-    case CLM_RELAY_TOKENS: bytes = LlamaEngine::token_bytes((int)q); break;
-    default: return fail(CLM_INVALID_ARGUMENT, "unknown relay message");
-  }
-  CLM_CHECK(e->lout.slot_bytes >= bytes + kLinkHeaderBytes, CLM_RESOURCE_EXHAUSTED,
-            "outbound link slots are smaller than the relayed message");
-  cudaStream_t st = pick_stream(e->ctx, stream);
-  CLM_TRY(launch_link_recv(e->lin, e->bin, e->record_bytes(e->wmax()), q, nullptr, e->relay_commit, e->bad, st));
-  return launch_link_send(e->lout, e->bin, bytes, e->relay_commit, q, kind, e->bad, st);
 }
 
 int llama_spec_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* h_tokens,

@@ -57,7 +57,7 @@ int llama_pipe_begin(LlamaEngine* e, uint64_t id, uint32_t row, const clm_b200_s
 int llama_pipe_round(LlamaEngine* e, uint64_t id, const clm_b200_spec_params* p, int32_t* d_tokens, uint32_t* d_count,
                      void* stream);
 int llama_pipe_status(LlamaEngine* e, void* stream);
-int llama_pipe_relay(LlamaEngine* e, uint32_t what, uint32_t q, void* stream);
+int llama_pipe_attach_session(LlamaEngine* e, uint64_t id, clm_b200_link* in, clm_b200_link* out);
 // fixture family (fixture.cu)
 int fixture_create(clm_b200_ctx* ctx, const clm_b200_fixture_geometry* g, const clm_b200_stage_spec* spec,
                    clm_b200_engine** out);

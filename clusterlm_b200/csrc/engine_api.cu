@@ -218,9 +218,9 @@ int clm_b200_pipe_status(clm_b200_engine* e, void* stream) {
   return llama_pipe_status(llama(e), stream);
 }
 
-int clm_b200_pipe_relay(clm_b200_engine* e, uint32_t what, uint32_t positions, void* stream) {
+int clm_b200_pipe_attach_session(clm_b200_engine* e, uint64_t id, clm_b200_link* in, clm_b200_link* out) {
   CLM_TRY(llama_only(e));
-  return llama_pipe_relay(llama(e), what, positions, stream);
+  return llama_pipe_attach_session(llama(e), id, in, out);
 }
 
 }  // extern "C"

@@ -16,7 +16,6 @@ from ._native import LINK_HANDLE_BYTES, QUANTS, call
 _vp = C.c_void_p
 
 ROLE_PREFIX, ROLE_MIDDLE, ROLE_TAIL, ROLE_WHOLE = 0, 1, 2, 3
-RELAY_WINDOW, RELAY_PREFILL, RELAY_TOKENS = 0, 1, 2  # clm_b200_pipe_relay's message kinds
 
 
 class _Geometry(C.Structure):
@@ -314,10 +313,10 @@ class Engine:
     def pipe_status(self, stream=None):
         call("clm_b200_pipe_status", self.h, None if stream is None else _vp(stream))
 
-    def pipe_relay(self, what: int, q: int, stream=None):
-        """Tail replica: pass the next inbound message (RELAY_WINDOW / RELAY_PREFILL records, RELAY_TOKENS) on
-        unchanged to the next stage."""
-        call("clm_b200_pipe_relay", self.h, what, q, None if stream is None else _vp(stream))
+    def pipe_attach_session(self, session: int, link_in=None, link_out=None):
+        """Binds `session`'s messages to their own links (None: the engine's)."""
+        call("clm_b200_pipe_attach_session", self.h, session, None if link_in is None else link_in.h,
+             None if link_out is None else link_out.h)
 
 
 LINK_SEND, LINK_RECV = 0, 1

@@ -11,18 +11,17 @@ round, so no stage needs a host round trip.  Several sequences are in flight so 
 Plans use the reference's text form (ClusterPlan::parse, coordinator.cpp:54-95): "BEGIN-END@OWNER,...", in pipeline
 order, contiguous, ending at the last layer, only the tail may be empty; an owner here is a GPU of the node
 ("g3" or "3") rather than a Node index or "father".  One extension: the plan may end in k > 1 items with the same
-range (e.g. "...,27-32@g5,32-32@g6,32-32@g7"), k tail replicas.  They are chained in the ring (... -> tail 0 ->
-tail 1 -> ... -> prefix); tail j runs the sessions s with s % k == j, and passes the other sessions' messages on
-unchanged (clm_b200_pipe_relay): boundary records towards their owner, window tokens towards the prefix.  The
-tail's LM head and MTP draft steps, which no layer split can shrink, are then shared by k GPUs.
+range (e.g. "...,27-32@g5,32-32@g6,32-32@g7"), k tail replicas.  Replica j runs the sessions s with s % k == j:
+the stage before the replicas has a link to each and sends every session's records to its replica, and the prefix
+has a link from each and takes every session's window tokens from its replica (clm_b200_pipe_attach_session).
+The tail's LM head and MTP draft steps, which no layer split can shrink, are then shared by k GPUs.
 """
 from __future__ import annotations
 
 import dataclasses
 from typing import Callable, Sequence
 
-from .engine import (LINK_RECV, LINK_SEND, RELAY_PREFILL, RELAY_TOKENS, RELAY_WINDOW, ROLE_MIDDLE, ROLE_PREFIX,
-                     ROLE_TAIL, Engine, LlamaGeometry, Link)
+from .engine import LINK_RECV, LINK_SEND, ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL, Engine, LlamaGeometry, Link
 
 BYTES_PER_WEIGHT = {"q4_k": 144 / 256, "q8_0": 34 / 32}
 
@@ -146,25 +145,31 @@ def role_of(rank: int, world: int, tails: int = 1) -> int:
     return ROLE_PREFIX if rank == 0 else ROLE_TAIL if rank >= world - tails else ROLE_MIDDLE
 
 
-def link_peers(rank: int, world: int) -> tuple[int, int]:
-    """(rank whose output this rank receives, rank this rank sends to): the ring prefix -> ... -> tail -> prefix."""
-    return (rank - 1) % world, (rank + 1) % world
+def link_peers(rank: int, world: int, tails: int = 1) -> tuple[list[int], list[int]]:
+    """(ranks this rank receives from, ranks it sends to).  Stages pass records forward; the stage before the
+    tail replicas sends to every replica, and every replica sends window tokens back to the prefix (with one tail:
+    the ring prefix -> ... -> tail -> prefix)."""
+    first = world - tails  # the first tail replica
+    last = first - 1       # the stage before the replicas
+    ins = list(range(first, world)) if rank == 0 else [last] if rank >= first else [rank - 1]
+    outs = [0] if rank >= first else list(range(first, world)) if rank == last else [rank + 1]
+    return ins, outs
 
 
-def wire(rank: int, world: int, gathered: Sequence[tuple[bytes, bytes]]) -> tuple[bytes, bytes]:
-    """Given every rank's (input-link handle, output-link handle), the handles this rank's input and output links
-    connect to: the input (receiving end) maps its sender's output end and vice versa."""
-    src, dst = link_peers(rank, world)
-    return gathered[src][1], gathered[dst][0]
+def wire(rank: int, world: int, gathered: Sequence[dict], tails: int = 1) -> tuple[dict, dict]:
+    """Given every rank's exported link ends ({("in", src): handle, ("out", dst): handle}), the handles this rank's
+    links connect to: {src: the sender's output end} and {dst: the receiver's input end}."""
+    ins, outs = link_peers(rank, world, tails)
+    return ({src: gathered[src][("out", rank)] for src in ins}, {dst: gathered[dst][("in", rank)] for dst in outs})
 
 
 class StagePipeline:
     """This rank's stage of a speculative pipeline: engine, links and the per-round calls.
 
-    Every rank must make the same calls (prefill chunks, rounds) for the same sessions in the same order.
-    `all_gather` exchanges one picklable object per rank (torch.distributed.all_gather_object in practice);
-    `engine_factory` / `link_factory` default to the device classes (host-logic tests pass stand-ins).
-    With tail replicas (see the module docstring) a tail rank runs its own sessions and relays the others'."""
+    Every rank must make the same calls (prefill chunks, rounds) for the same sessions in the same order; a tail
+    replica makes them only for its own sessions (`owner`).  `all_gather` exchanges one picklable object per rank
+    (torch.distributed.all_gather_object in practice); `engine_factory` / `link_factory` default to the device
+    classes (host-logic tests pass stand-ins)."""
 
     def __init__(self, ctx, geo: LlamaGeometry, plan: Sequence[StagePlan], rank: int, max_context: int,
                  sessions: int, all_gather: Callable[[object], list], max_window: int = 16, slots: int = 0,
@@ -173,8 +178,9 @@ class StagePipeline:
         self.rank, self.world = rank, len(plan)
         self.tails = tail_replicas(plan)
         self.role = role_of(rank, self.world, self.tails)
+        self.first_tail = self.world - self.tails
         # this rank's place among the tail replicas (0 .. tails-1), or None
-        self.tail_index = rank - (self.world - self.tails) if self.role == ROLE_TAIL else None
+        self.tail_index = rank - self.first_tail if self.role == ROLE_TAIL else None
         self.max_window = max_window
         self.ctx = ctx
         st = plan[rank]
@@ -186,14 +192,20 @@ class StagePipeline:
         tok = (max_window + 1) * 4
         # a slot per sequence in flight (plus one), so no sender ever waits on a credit in steady state
         slots = slots or sessions + 1
-        # only the last stage sends window tokens alone; a tail replica before it also relays records
-        last = rank == self.world - 1
-        self.link_in = link_factory(ctx, LINK_RECV, slots, tok if self.role == ROLE_PREFIX else rec, timeout_s)
-        self.link_out = link_factory(ctx, LINK_SEND, slots, tok if last else rec, timeout_s)
-        gathered = all_gather((self.link_in.export(), self.link_out.export()))
-        peer_in, peer_out = wire(rank, self.world, gathered)
-        self.link_in.connect(peer_in)
-        self.link_out.connect(peer_out)
+        ins, outs = link_peers(rank, self.world, self.tails)
+        # replicas send window tokens, every other stage boundary records
+        self.links_in = {src: link_factory(ctx, LINK_RECV, slots, tok if src >= self.first_tail else rec, timeout_s)
+                         for src in ins}
+        self.links_out = {dst: link_factory(ctx, LINK_SEND, slots, tok if self.role == ROLE_TAIL else rec, timeout_s)
+                          for dst in outs}
+        mine = {("in", src): l.export() for src, l in self.links_in.items()}
+        mine.update({("out", dst): l.export() for dst, l in self.links_out.items()})
+        peer_in, peer_out = wire(rank, self.world, all_gather(mine), self.tails)
+        for src, l in self.links_in.items():
+            l.connect(peer_in[src])
+        for dst, l in self.links_out.items():
+            l.connect(peer_out[dst])
+        self.link_in, self.link_out = self.links_in[ins[0]], self.links_out[outs[0]]
         self.engine.pipe_attach(self.link_in, self.link_out)
 
     @property
@@ -204,47 +216,39 @@ class StagePipeline:
         """The tail replica (0 .. tails-1) that runs `session`'s head, acceptance and drafts."""
         return session % self.tails
 
-    def _place(self, session: int) -> int:
-        """-1: a tail replica before the session's owner, 0: its owner, 1: after it (not a tail: 0)."""
-        if self.tail_index is None:
-            return 0
-        o = self.owner(session)
-        return (self.tail_index > o) - (self.tail_index < o)
+    def _runs(self, session: int) -> bool:
+        return self.tail_index is None or self.owner(session) == self.tail_index
 
     def open_session(self, session: int):
+        if not self._runs(session):
+            return
         self.engine.open_session(session)
+        if len(self.links_in) > 1 or len(self.links_out) > 1:
+            replica = self.first_tail + self.owner(session)
+            self.engine.pipe_attach_session(session, self.links_in.get(replica), self.links_out.get(replica))
 
     def prefill(self, session: int, prompt: Sequence[int], stream=None) -> int:
         """Runs the prompt through this stage in chunks of max_window; returns the last chunk's final row."""
         n = len(prompt)
-        place = self._place(session)
         off = 0
         while off < n:
             q = min(self.max_window, n - off)
-            if place < 0:
-                self.engine.pipe_relay(RELAY_PREFILL, q, stream)
-            elif place == 0:
+            if self._runs(session):
                 self.engine.pipe_prefill(session, q, prompt[off:off + q] if self.role == ROLE_PREFIX else None,
                                          stream)
             off += q
         return (n - 1) % self.max_window
 
     def begin(self, session: int, row: int, q: int, temperature: float = 0.0, seed: int = 0, stream=None):
-        if self.is_tail:
-            place = self._place(session)
-            if place == 0:
-                self.engine.pipe_begin(session, row, q, temperature, seed, stream)
-            elif place > 0:
-                self.engine.pipe_relay(RELAY_TOKENS, q, stream)
+        if self.is_tail and self._runs(session):
+            self.engine.pipe_begin(session, row, q, temperature, seed, stream)
 
     def round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None, d_count=None,
               stream=None):
-        """One round of `session` on this stage; only the owning tail writes d_tokens / d_count."""
-        place = self._place(session)
-        if place == 0:
+        """One round of `session` on this stage (a tail replica: its own sessions only, which alone write
+        d_tokens / d_count)."""
+        if self._runs(session):
             self.engine.pipe_round(session, q, temperature, seed, d_tokens, d_count, stream)
-        else:
-            self.engine.pipe_relay(RELAY_WINDOW if place < 0 else RELAY_TOKENS, q, stream)
 
     def status(self, stream=None):
         self.engine.pipe_status(stream)
@@ -255,6 +259,6 @@ class StagePipeline:
         self.ctx.synchronize()
         barrier()
         self.engine.close()
-        self.link_in.close()
-        self.link_out.close()
+        for l in list(self.links_in.values()) + list(self.links_out.values()):
+            l.close()
         barrier()

@@ -369,17 +369,14 @@ CLM_API int clm_b200_pipe_round(clm_b200_engine* e, uint64_t session, const clm_
                                 int32_t* d_tokens, uint32_t* d_count, void* stream);
 /* Synchronises the engine's stream; CLM_DEADLINE_EXCEEDED if a link wait gave up (a peer stage stopped). */
 CLM_API int clm_b200_pipe_status(clm_b200_engine* e, void* stream);
-/* Tail replicas: a plan may end in k tail stages with the same layer range on k GPUs, chained in the ring
- * (... -> tail 0 -> tail 1 -> ... -> tail k-1 -> prefix); tail j runs the sessions s with s % k == j.  For a
- * session of another replica a tail passes the next inbound message on unchanged (payload, window width, commit
- * count, kind): `what` CLM_RELAY_WINDOW / CLM_RELAY_PREFILL for the boundary records of a round / a prompt chunk
- * (replicas before the owner), CLM_RELAY_TOKENS for the window tokens the owner sent (replicas after it).  The
- * reference has one tail per plan (its Father's tail domain, coordinator.cpp:736-892); the replicas share the
- * tail's LM head and MTP draft steps, the stage no layer split can make smaller.  Tail engines only. */
-#define CLM_RELAY_WINDOW 0u
-#define CLM_RELAY_PREFILL 1u
-#define CLM_RELAY_TOKENS 2u
-CLM_API int clm_b200_pipe_relay(clm_b200_engine* e, uint32_t what, uint32_t positions, void* stream);
+/* Binds one session's messages to their own input / output links (NULL: the engine's, from
+ * clm_b200_pipe_attach); the session's captured rounds are dropped.  Used by tail replicas: a plan may end in k
+ * tail stages with the same layer range on k GPUs, replica j running the sessions s with s % k == j; the stage
+ * before the replicas sends each session's records on the link to its replica and the prefix receives each
+ * session's window tokens on the link from its replica.  The reference has one tail per plan (its Father's tail
+ * domain, coordinator.cpp:736-892); replicas share the tail's LM head and MTP draft steps, the stage that no layer
+ * split can make smaller. */
+CLM_API int clm_b200_pipe_attach_session(clm_b200_engine* e, uint64_t session, clm_b200_link* in, clm_b200_link* out);
 
 /* ---- clusterlm-fixture family: the reference's own model (hc gated residual streams, 3:1 recurrent /
  * attention layers without RoPE, top-K MoE with a shared SwiGLU expert, PLE n-gram lookup, injection gates;

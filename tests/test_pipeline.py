@@ -6,8 +6,7 @@ import socket
 
 import pytest
 
-from clusterlm_b200.engine import (LLAMA3_8B, LLAMA3_70B, RELAY_PREFILL, RELAY_TOKENS, RELAY_WINDOW, ROLE_MIDDLE,
-                                   ROLE_PREFIX, ROLE_TAIL, LlamaGeometry)
+from clusterlm_b200.engine import LLAMA3_8B, LLAMA3_70B, ROLE_MIDDLE, ROLE_PREFIX, ROLE_TAIL, LlamaGeometry
 from clusterlm_b200.pipeline import (StagePipeline, StagePlan, format_plan, link_peers, parse_plan, plan_stages,
                                      role_of, stage_costs, tail_replicas, wire)
 
@@ -102,12 +101,19 @@ def test_plan_stages_70b_eight_gpus():
 def test_roles_and_ring():
     assert [role_of(r, 4) for r in range(4)] == [ROLE_PREFIX, ROLE_MIDDLE, ROLE_MIDDLE, ROLE_TAIL]
     assert [role_of(r, 4, 2) for r in range(4)] == [ROLE_PREFIX, ROLE_MIDDLE, ROLE_TAIL, ROLE_TAIL]
-    assert [link_peers(r, 3) for r in range(3)] == [(2, 1), (0, 2), (1, 0)]
-    g = [(b"in0", b"out0"), (b"in1", b"out1"), (b"in2", b"out2")]
+    # one tail: the ring prefix -> ... -> tail -> prefix
+    assert [link_peers(r, 3) for r in range(3)] == [([2], [1]), ([0], [2]), ([1], [0])]
+    # replicas 3 and 4: the stage before them feeds both, both feed the prefix
+    assert [link_peers(r, 5, 2) for r in range(5)] == [([3, 4], [1]), ([0], [2]), ([1], [3, 4]), ([2], [0]),
+                                                       ([2], [0])]
+    # the prefix itself before the replicas
+    assert [link_peers(r, 3, 2) for r in range(3)] == [([1, 2], [1, 2]), ([0], [0]), ([0], [0])]
+    g = [{("in", 2): b"in0", ("out", 1): b"out0"}, {("in", 0): b"in1", ("out", 2): b"out1"},
+         {("in", 1): b"in2", ("out", 0): b"out2"}]
     # rank r's receiving end maps the sender's output end; its sending end maps the receiver's input end
-    assert wire(0, 3, g) == (b"out2", b"in1")
-    assert wire(1, 3, g) == (b"out0", b"in2")
-    assert wire(2, 3, g) == (b"out1", b"in0")
+    assert wire(0, 3, g) == ({2: b"out2"}, {1: b"in1"})
+    assert wire(1, 3, g) == ({0: b"out0"}, {2: b"in2"})
+    assert wire(2, 3, g) == ({1: b"out1"}, {0: b"in0"})
 
 
 # ---- gloo: every rank's StagePipeline with stand-in engines and links ----
@@ -153,8 +159,8 @@ class FakeEngine:
     def pipe_round(self, s, q, T, seed, d_tokens, d_count, stream):
         self.log.append(("round", s, q))
 
-    def pipe_relay(self, what, q, stream):
-        self.log.append(("relay", what, q))
+    def pipe_attach_session(self, s, a, b):
+        self.log.append(("attach_session", s, None if a is None else a.peer, None if b is None else b.peer))
 
     def pipe_status(self, stream):
         self.log.append(("status",))
@@ -203,35 +209,41 @@ def _worker(rank, world, port, plan_text, out):
             for s in (1, 2):
                 p.round(s, 4)
         p.close(dist.barrier)
-        out[rank] = (ctx.log, p.link_in.peer, p.link_out.peer, p.link_in.closed and p.link_out.closed, row,
-                     p.link_in.export(), p.link_out.export(), p.tail_index)
+        links = {("in", k): (l.export(), l.peer, l.closed) for k, l in p.links_in.items()}
+        links.update({("out", k): (l.export(), l.peer, l.closed) for k, l in p.links_out.items()})
+        out[rank] = (ctx.log, links, row, p.tail_index)
     finally:
         dist.destroy_process_group()
 
 
-def _replay(logs, world):
-    """Replays every rank's calls over FIFO links (rank r sends to rank r+1, the last to the prefix) and returns the
-    largest number of messages any link held.  A message is (kind, session); every call consumes what its role
-    receives and produces what it sends; a relay passes the message on unchanged.  Fails on a message of the wrong
-    kind or session, on a call that could never run (deadlock) or on messages left over beyond the next windows
-    of sessions 1 and 2."""
-    relay_kind = {RELAY_WINDOW: "rec", RELAY_PREFILL: "pre", RELAY_TOKENS: "tok"}
+def _replay(logs, world, tails):
+    """Replays every rank's calls over FIFO links and returns the largest number of messages any link held.  A
+    message is (kind, session); a call receives on the link its role and session name (the prefix from the
+    session's replica, a replica from the stage before the replicas, others from the previous stage) and sends on
+    the matching one.  Fails on a message of the wrong kind or session, on a call that could never run (deadlock)
+    or on messages left over beyond the next windows of sessions 1 and 2."""
+    first = world - tails
+
+    def src(r, s):
+        return first + s % tails if r == 0 else first - 1 if r >= first else r - 1
+
+    def dst(r, s):
+        return 0 if r >= first else first + s % tails if r == first - 1 else r + 1
+
     ops = []
     for r in range(world):
         role = logs[r][0][0][3]
         seq = []
         for e in logs[r][0]:
+            s = e[1] if e[0] in ("prefill", "begin", "round") else None
             if e[0] == "prefill":
-                seq.append(("pre" if role != ROLE_PREFIX else None, ("pre", e[1]) if role != ROLE_TAIL else None, e[1]))
+                seq.append(("pre" if role != ROLE_PREFIX else None, ("pre", s) if role != ROLE_TAIL else None, s))
             elif e[0] == "begin":
-                seq.append((None, ("tok", e[1]), e[1]))
+                seq.append((None, ("tok", s), s))
             elif e[0] == "round":
-                want = "tok" if role == ROLE_PREFIX else "rec"
-                seq.append((want, ("tok", e[1]) if role == ROLE_TAIL else ("rec", e[1]), e[1]))
-            elif e[0] == "relay":
-                seq.append((relay_kind[e[1]], "pass", None))
+                seq.append(("tok" if role == ROLE_PREFIX else "rec", ("tok", s) if role == ROLE_TAIL else ("rec", s), s))
         ops.append(seq)
-    inbox = [[] for _ in range(world)]
+    inbox = {}
     at = [0] * world
     peak = 0
     while any(at[r] < len(ops[r]) for r in range(world)):
@@ -239,24 +251,24 @@ def _replay(logs, world):
         for r in range(world):
             if at[r] == len(ops[r]):
                 continue
-            want, send, sess = ops[r][at[r]]
-            msg = None
+            want, send, s = ops[r][at[r]]
             if want is not None:
-                if not inbox[r]:
+                box = inbox.setdefault((src(r, s), r), [])
+                if not box:
                     continue
-                msg = inbox[r].pop(0)
-                assert msg[0] == want, f"rank {r} call {at[r]} wanted {want}, got {msg}"
-                assert sess is None or msg[1] == sess, f"rank {r} call {at[r]}: session {sess}, message {msg}"
-            if send == "pass":
-                send = msg
+                msg = box.pop(0)
+                assert msg == (want, s), f"rank {r} call {at[r]} wanted {(want, s)}, got {msg}"
             if send is not None:
-                inbox[(r + 1) % world].append(send)
-                peak = max(peak, len(inbox[(r + 1) % world]))
+                box = inbox.setdefault((r, dst(r, s)), [])
+                box.append(send)
+                peak = max(peak, len(box))
             at[r] += 1
             moved = True
         assert moved, f"deadlock: calls done {at} of {[len(o) for o in ops]}, inboxes {inbox}"
-    # only the next windows the last rounds drafted wait at the prefix, one per session in round order
-    assert inbox[0] == [("tok", 1), ("tok", 2)] and all(not b for b in inbox[1:]), f"messages left over: {inbox}"
+    left = sorted(m for b in inbox.values() for m in b)
+    # only the next windows the last rounds drafted wait at the prefix, one per session
+    assert left == [("tok", 1), ("tok", 2)], f"messages left over: {inbox}"
+    assert all(k[1] == 0 for k, b in inbox.items() if b)
     return peak
 
 
@@ -271,35 +283,47 @@ def test_pipeline_ranks_gloo(world, plan_text):
     logs = {r: out[r] for r in range(world)}
     tails = 1 if plan_text is None else tail_replicas(parse_plan(plan_text, 6))
     for r in range(world):
-        log, peer_in, peer_out, closed, row, own_in, own_out, tail_index = logs[r]
-        src, dst = (r - 1) % world, (r + 1) % world
-        # ring wiring: input from the previous stage's sending end, output to the next stage's receiving end
-        assert peer_in.startswith(f"r{src}-send".encode()) and peer_out.startswith(f"r{dst}-recv".encode())
-        # both ends of a link agree on slots and payload size
-        assert own_out.split(b"-")[2:] == logs[dst][5].split(b"-")[2:]
-        assert own_in.split(b"-")[2:] == logs[src][6].split(b"-")[2:]
-        assert closed
+        log, links, row, tail_index = logs[r]
+        ins, outs = link_peers(r, world, tails)
+        assert sorted(k for k in links if k[0] == "in") == [("in", x) for x in ins]
+        assert sorted(k for k in links if k[0] == "out") == [("out", x) for x in outs]
+        for (end, peer), (own, connected, closed) in links.items():
+            # a receiving end maps the sender's output end and vice versa; both ends agree on slots and payload
+            other = logs[peer][1][("out" if end == "in" else "in", r)][0]
+            assert connected == other and closed
+            assert own.split(b"-")[2:] == other.split(b"-")[2:]
+            # replicas send window tokens, every other stage boundary records
+            sender = peer if end == "in" else r
+            assert int(own.split(b"-")[3]) == ((16 + 1) * 4 if sender >= world - tails else 16 * (2 * 256 + 1) * 4)
         assert row == (37 - 1) % 16
         kinds = [e[0] for e in log]
         role = role_of(r, world, tails)
         assert kinds[:4] == ["create", "weights", "prepare", "attach"]
         assert log[0][3] == role
         assert tail_index == (r - (world - tails) if role == ROLE_TAIL else None)
-        # a tail replica runs the sessions s with s % tails == its index and relays the others'
-        own = {1, 2} if role != ROLE_TAIL else {s for s in (1, 2) if s % tails == tail_index}
+        # a tail replica runs the sessions s with s % tails == its index, and no other
+        own = [1, 2] if role != ROLE_TAIL else [s for s in (1, 2) if s % tails == tail_index]
+        assert [e[1] for e in log if e[0] == "open"] == own
+        # stages with several links bind every session to its replica's link
+        binds = [e for e in log if e[0] == "attach_session"]
+        if len(ins) > 1 or len(outs) > 1:
+            for s in own:
+                replica = world - tails + s % tails
+                want_in = links[("in", replica)][1] if ("in", replica) in links else None
+                want_out = links[("out", replica)][1] if ("out", replica) in links else None
+                assert ("attach_session", s, want_in, want_out) in binds
+        else:
+            assert not binds
         prefills = [e for e in log if e[0] == "prefill"]
         # chunks of max_window: 16, 16, 5 per session; only the prefix passes tokens
         assert [e[2] for e in prefills] == [16, 16, 5] * len(own)
-        assert {e[1] for e in prefills} == own
+        assert [e[1] for e in prefills] == [s for s in own for _ in range(3)]
         assert all((e[3] is not None) == (role == ROLE_PREFIX) for e in prefills)
         if role == ROLE_PREFIX:
             assert prefills[0][3] == list(range(16)) and prefills[2][3] == list(range(32, 37))
         begins = [e for e in log if e[0] == "begin"]
-        assert [e[1] for e in begins] == (sorted(own) if role == ROLE_TAIL else [])
+        assert [e[1] for e in begins] == (own if role == ROLE_TAIL else [])
         assert [e[1] for e in log if e[0] == "round"] == [s for s in [1, 2] * 3 if s in own]
-        relays = [e for e in log if e[0] == "relay"]
-        if role != ROLE_TAIL:
-            assert not relays
         # close protocol: drain this stage, wait for every rank, then release
         assert kinds[-2:] == ["sync", "close"]
     # the same prefill / round sequence on every rank that is not a tail replica
@@ -307,9 +331,4 @@ def test_pipeline_ranks_gloo(world, plan_text):
             for r in range(world - tails)]
     assert all(s == seqs[0] for s in seqs)
     # every message reaches the stage that expects it, in order, within the link's slots (sessions + 1)
-    assert _replay(logs, world) <= 3
-    # the last stage -> prefix link carries window tokens, a tail replica before it also relays records
-    assert int(logs[world - 1][6].split(b"-")[3]) == (16 + 1) * 4
-    assert int(logs[0][6].split(b"-")[3]) == 16 * (2 * 256 + 1) * 4
-    for r in range(world - tails, world - 1):
-        assert int(logs[r][6].split(b"-")[3]) == 16 * (2 * 256 + 1) * 4
+    assert _replay(logs, world, tails) <= 3
