@@ -993,7 +993,7 @@ def run_pipeline(args, world, rank, local):
     end.record(stream)
     pipe.status()
     clk = clocks.stop()
-    launches = pipe.engine.last_launches() * args.steps * S
+    launches = pipe.engine.last_launches() * args.steps * sum(pipe.runs(s + 1) for s in range(S))
     elapsed = start.elapsed_time(end) / 1e3
     emitted = int(cnt[args.warmup:].sum().item()) if pipe.is_tail else 0
     elapsed_max = max_over_ranks(world, elapsed, dev)

@@ -216,11 +216,12 @@ class StagePipeline:
         """The tail replica (0 .. tails-1) that runs `session`'s head, acceptance and drafts."""
         return session % self.tails
 
-    def _runs(self, session: int) -> bool:
+    def runs(self, session: int) -> bool:
+        """Whether this rank runs `session` (every stage does; a tail replica only its own sessions)."""
         return self.tail_index is None or self.owner(session) == self.tail_index
 
     def open_session(self, session: int):
-        if not self._runs(session):
+        if not self.runs(session):
             return
         self.engine.open_session(session)
         if len(self.links_in) > 1 or len(self.links_out) > 1:
@@ -233,21 +234,21 @@ class StagePipeline:
         off = 0
         while off < n:
             q = min(self.max_window, n - off)
-            if self._runs(session):
+            if self.runs(session):
                 self.engine.pipe_prefill(session, q, prompt[off:off + q] if self.role == ROLE_PREFIX else None,
                                          stream)
             off += q
         return (n - 1) % self.max_window
 
     def begin(self, session: int, row: int, q: int, temperature: float = 0.0, seed: int = 0, stream=None):
-        if self.is_tail and self._runs(session):
+        if self.is_tail and self.runs(session):
             self.engine.pipe_begin(session, row, q, temperature, seed, stream)
 
     def round(self, session: int, q: int, temperature: float = 0.0, seed: int = 0, d_tokens=None, d_count=None,
               stream=None):
         """One round of `session` on this stage (a tail replica: its own sessions only, which alone write
         d_tokens / d_count)."""
-        if self._runs(session):
+        if self.runs(session):
             self.engine.pipe_round(session, q, temperature, seed, d_tokens, d_count, stream)
 
     def status(self, stream=None):
