@@ -1044,7 +1044,7 @@ def run_pipeline(args, world, rank, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_k weights, fp16 operands, f32 accumulate",
         "data": "synthetic (random-init N(0,0.02) weights, seeded random context tokens)",
         "config": bench_config(world, context, S),
-        "plan": format_plan(plan), "step": f"one round of each of the {S} sequences",
+        "plan": format_plan(plan), "tail_replicas": pipe.tails, "step": f"one round of each of the {S} sequences",
         "ms_per_round": elapsed_max / (args.steps * S) * 1e3, "emitted_per_round": emitted_all / (args.steps * S),
         "prefill_s": round(prefill_s, 2),
         "e2e": {"value": e2e_emitted / e2e_s, "unit": "tok/s", "ms_per_round": e2e_s / (e2e_n * S) * 1e3,
